@@ -1,0 +1,425 @@
+#!/usr/bin/env python3
+"""Benchmark of the pre-norm Transformer forward on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload B1]
+    python bench.py --impl reference ...          # the reference forward on host CPU cores
+
+One step = one forward pass over one batch of the workload. The default
+workload is B1: d_model 128, 4 heads, ffn 128, 4 layers, causal, batch 4 x seq
+16, x ~ N(0,1) -- the launch-bound small shape. Other workloads (A, B2, C, D,
+E) are selectable for measurement; see ttjam_gottagofast_b200/config.py.
+
+Our arm prints one JSON line with
+  value      whole-job tokens/s (B*S tokens per rank per step, all ranks), timed
+             on the device with CUDA events around each step on the launching
+             stream, inputs resident in HBM, L2 flushed between steps (a 256 MiB
+             write), max over ranks;
+  e2e        the same metric through the public module call
+             (UserOptimizedTransformer.forward) from pinned host buffers, with
+             the host->device copy of x and the mask and the device->host copy
+             of y inside each timed step;
+  roofline   the forward against measured HBM bandwidth (algorithmic bytes:
+             packed weights read once + x read + y written);
+  cpu_baseline  the reference forward (oracle restatement, torch eager fp32)
+             on this host's CPU cores, rank 0 at N=1 only.
+Multi-GPU runs use torchrun (one process per GPU, NCCL); every rank runs its
+own batch (weak scaling; workload E splits its batch of 64 across ranks, strong
+scaling). There is no collective inside a step.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from ttjam_gottagofast_b200 import _lib  # noqa: E402
+from ttjam_gottagofast_b200.config import MODEL_SEED, TIMING_DATA_SEED, WORKLOADS  # noqa: E402
+from ttjam_gottagofast_b200.contract import generate_random_case  # noqa: E402
+
+METRIC = "fwd latency (us) & tokens/s"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--workload", default="B1", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget-s", type=float, default=10.0)
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def per_rank_batch(w, world, rank):
+    """Batch rows this rank owns: E splits its batch of 64 contiguously (strong
+    scaling); every other workload gives each rank a full batch (weak scaling)."""
+    b = w.config.batch_size
+    if w.name == "E":
+        if b % world:
+            raise SystemExit(f"batch {b} does not split over {world} GPUs")
+        per = b // world
+        return rank * per, per, "strong"
+    return 0, b, "weak"
+
+
+# ---------------------------------------------------------------------------
+# measurement helpers
+# ---------------------------------------------------------------------------
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            pk = json.load(fh)
+        return float(pk["hbm_gbs"]), float(pk["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples while the GPU is under load."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.idx = device_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.idx), "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                    "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def algorithmic_bytes(cfg, b, s, mask_bytes):
+    """Bytes a forward must move at least: every weight once, x in, y out."""
+    d, f, l = cfg.d_model, cfg.ffn_dim, cfg.num_layers
+    weights = l * (4 * d * d + 2 * d * f + 3 * d + d + f + d + 4 * d) + 2 * d
+    return 4 * weights + 4 * 2 * b * s * d + mask_bytes
+
+
+def algorithmic_flops(cfg, mask):
+    """GEMM 2*Tv*(4D^2+2DF)*L + attention 4*D*sum_b len_b(len_b+1)/2*L over
+    valid tokens and causal valid pairs (padded tokens need no work)."""
+    d, f, l = cfg.d_model, cfg.ffn_dim, cfg.num_layers
+    lens = mask.sum(1).double()
+    tv = float(lens.sum())
+    pairs = float((lens * (lens + 1) / 2).sum()) if cfg.causal else float((lens * lens).sum())
+    return 2 * tv * (4 * d * d + 2 * d * f) * l + 4 * d * pairs * l
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the reference forward (oracle restatement) on host cores
+# ---------------------------------------------------------------------------
+def cpu_reference_run(w, steps, warmup, budget_s):
+    """Times the reference forward (torch eager fp32, same ops as
+    BaselineTransformer.forward) on all host cores. Each step runs a bounded
+    slice of the workload's batch so a step stays near budget_s/steps."""
+    from oracle import reference_model as oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg = w.config
+    params = oracle.init_params(cfg, seed=MODEL_SEED)
+    x, mask = generate_random_case(cfg, "cpu", torch.float32, TIMING_DATA_SEED,
+                                   w.padding_ratio, w.input_scale)
+    # size the slice: one probe sequence, then as many sequences as fit the budget
+    t0 = time.perf_counter()
+    oracle.forward(params, cfg, x[:1], mask[:1])
+    one = time.perf_counter() - t0
+    per_step_budget = max(budget_s / max(steps + warmup, 1), 1e-3)
+    nb = int(max(1, min(cfg.batch_size, per_step_budget / max(one, 1e-6))))
+    xs, ms = x[:nb].contiguous(), mask[:nb].contiguous()
+    for _ in range(warmup):
+        oracle.forward(params, cfg, xs, ms)
+    samples = []
+    for _ in range(steps):
+        t0 = time.perf_counter_ns()
+        oracle.forward(params, cfg, xs, ms)
+        samples.append((time.perf_counter_ns() - t0) / 1e6)
+    med = statistics.median(samples)
+    tokens = nb * cfg.seq_len
+    return {
+        "value": tokens * 1000.0 / med, "unit": "tokens/s", "cores": threads,
+        "kind": "port", "ms_per_step": med,
+        "sample": (f"{nb} of {cfg.batch_size} sequences x seq {cfg.seq_len} per step, "
+                   f"median of {steps} steps after {warmup} warm-up, torch eager fp32 "
+                   f"restatement of BaselineTransformer.forward, {threads} threads"),
+    }
+
+
+def run_reference_arm(args, world, rank):
+    if rank != 0:
+        return 0
+    w = WORKLOADS[args.workload]
+    res = cpu_reference_run(w, args.steps, args.warmup, budget_s=120.0)
+    cfg = w.config
+    line = {
+        "impl": "reference", "metric": METRIC, "value": res["value"], "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": res["ms_per_step"], "higher_is_better": True,
+        "scaling": "weak" if w.name != "E" else "strong", "vs_baseline": None,
+        "dtype": "fp32", "data": "synthetic (seeded generate_random_case, random-init weights)",
+        "config": workload_config(w, cfg.batch_size, world),
+        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": res["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(w, per_rank_b, world):
+    c = w.config
+    return {"workload": f"{w.name}: {w.description}", "batch_per_gpu": per_rank_b,
+            "global_batch": per_rank_b * world if w.name != "E" else c.batch_size,
+            "seq_len": c.seq_len, "d_model": c.d_model, "num_heads": c.num_heads,
+            "ffn_dim": c.ffn_dim, "num_layers": c.num_layers, "causal": c.causal,
+            "input_scale": w.input_scale, "padding_ratio": w.padding_ratio,
+            "parallelism": f"dp{world} (batch-sharded, weights replicated)",
+            "l2": "flushed between timed steps (256 MiB write)"}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args, world, rank, local):
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device for --impl ours")
+    from ttjam_gottagofast_b200 import UserOptimizedTransformer
+    dev = torch.device("cuda", local if world > 1 else 0)
+    w = WORKLOADS[args.workload]
+    cfg = w.config
+    b0, nb, scaling = per_rank_batch(w, world, rank)
+    x_all, m_all = generate_random_case(cfg, "cpu", torch.float32, TIMING_DATA_SEED,
+                                        w.padding_ratio, w.input_scale)
+    x_host = x_all[b0:b0 + nb].contiguous()
+    m_host = m_all[b0:b0 + nb].contiguous()
+    S = cfg.seq_len
+
+    torch.manual_seed(MODEL_SEED)
+    model = UserOptimizedTransformer(cfg).to(dev).eval()
+    lib, tcfg = model._lib, model._cfg
+    x = x_host.to(dev)
+    mask = m_host.to(dev)
+    with torch.inference_mode():
+        model(x, mask)  # packs the image
+    image = model._image
+    y = torch.empty_like(x)
+    ws_bytes = lib.tt_workspace_bytes(ctypes.byref(tcfg), nb, S)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+    cfg_ref = ctypes.byref(tcfg)
+    args_fwd = (cfg_ref, image.data_ptr(), x.data_ptr(), mask.data_ptr(), nb, S,
+                y.data_ptr(), ws.data_ptr(), ws_bytes, sptr)
+
+    def step():
+        rc = lib.tt_forward(*args_fwd)
+        if rc:
+            _lib.check(rc, "tt_forward", lib)
+
+    for _ in range(max(args.warmup, 3)):
+        flush.fill_(1)
+        step()
+    torch.cuda.synchronize(dev)
+
+    # keep the GPU busy ~1 s before the timed region so the clock samples
+    # describe a loaded GPU, then time exactly K steps
+    sampler = ClockSampler(dev.index)
+    sampler.start()
+    t_end = time.time() + 1.0
+    while time.time() < t_end:
+        for _ in range(20):
+            flush.fill_(1)
+            step()
+        torch.cuda.synchronize(dev)
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clocks = sampler.stop()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = max_over_ranks(sum(step_ms), world)
+    med_ms = max_over_ranks(statistics.median(step_ms), world)
+    tokens_per_step_all = nb * S * world
+    value = tokens_per_step_all * args.steps * 1000.0 / total_ms
+
+    code, detail = model.read_device_status()
+    if code != 0:
+        raise SystemExit(f"device status {code} (detail {detail}) after timed steps")
+
+    # ---- e2e through the public module call, host buffers -----------------
+    xh = x_host.pin_memory()
+    mh = m_host.pin_memory()
+    yh = torch.empty_like(x_host).pin_memory()
+    e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with torch.inference_mode():
+        for _ in range(3):
+            xd = xh.to(dev, non_blocking=True)
+            md = mh.to(dev, non_blocking=True)
+            yh.copy_(model(xd, md), non_blocking=True)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            e_starts[i].record(stream)
+            xd = xh.to(dev, non_blocking=True)
+            md = mh.to(dev, non_blocking=True)
+            yd = model(xd, md)
+            yh.copy_(yd, non_blocking=True)
+            e_ends[i].record(stream)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+    e_total = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(e_starts, e_ends)), world)
+    e2e_value = tokens_per_step_all * args.steps * 1000.0 / e_total
+    assert torch.equal(yh, y.cpu()), "e2e output differs from the device-timed output"
+
+    # ---- roofline of the forward -------------------------------------------
+    hbm_peak, tc_peak, peak_kind = load_peaks()
+    launches = lib.tt_forward_launch_count(cfg_ref, nb, S)
+    plan = _lib.PLAN_NAMES.get(lib.tt_forward_plan(cfg_ref, nb, S), "?")
+    mean_ms = sum(step_ms) / len(step_ms)
+    bytes_step = algorithmic_bytes(cfg, nb, S, mask.numel())
+    flops_step = algorithmic_flops(cfg, m_host)
+    achieved_gbs = bytes_step / (mean_ms * 1e-3) / 1e9
+    roofline = {
+        "bound": "hbm", "achieved": round(achieved_gbs, 2), "peak": hbm_peak,
+        "unit": "GB/s", "frac": round(achieved_gbs / hbm_peak, 5), "traffic": None,
+        "kernel": ("whole forward" if launches == 1 else
+                   f"whole forward ({launches} launches, plan {plan})"),
+        "algorithmic_bytes_per_launch": bytes_step if launches == 1 else None,
+        "algorithmic_bytes_per_step": bytes_step,
+        "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+        "fp32_flops_per_step": flops_step,
+        "achieved_fp32_tflops": round(flops_step / (mean_ms * 1e-3) / 1e12, 4),
+    }
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+        "latency_us": {"mean": total_ms / args.steps * 1000.0, "median": med_ms * 1000.0},
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded generate_random_case, seeded random-init weights)",
+        "config": workload_config(w, nb, world), "plan": plan,
+        "gpu_launches": launches * args.steps,
+        "roofline": roofline,
+        "e2e": {"value": e2e_value, "unit": "tokens/s",
+                "h2d_bytes_per_step": x_host.numel() * 4 + m_host.numel(),
+                "d2h_bytes_per_step": x_host.numel() * 4,
+                "path": "UserOptimizedTransformer.forward from pinned host buffers"},
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_reference_run(w, steps=20, warmup=2, budget_s=args.cpu_budget_s)
+        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse_args()
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        if args.impl == "reference":
+            return run_reference_arm(args, world, rank)
+        return run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,133 @@
+/*
+ * ttjam_b200.h -- C ABI of the B200 (sm_100a) pre-norm Transformer forward.
+ *
+ * The reference exposes this path as a PyTorch module contract
+ * (torch_transformer_benchmark.py): a `TransformerConfig` shape record
+ * (:29-56), `UserOptimizedTransformer.forward(x, valid_token_mask)` (:175-200)
+ * whose weights arrive through `load_state_dict` (`copy_model_weights`,
+ * :203-213), and an optimised implementation of it (final_submission.py) with
+ * module-level `build_model` / `load_from_baseline` (final_submission.py:528-539).
+ * This header is the native boundary under that contract: plain pointers and
+ * sizes, no torch types. Every pointer argument that names tensor data is a
+ * device pointer unless stated otherwise; every entry point that launches work
+ * takes a `cudaStream_t` passed as `void*` and never synchronises it (except
+ * `tt_read_status`, which says so).
+ *
+ * Ownership: the library allocates nothing. The caller owns the packed model
+ * image (`tt_image_bytes`), the per-call workspace (`tt_workspace_bytes`), the
+ * input, the mask and the output.
+ *
+ * Return codes: 0 on success, a negative `tt_status` value on failure; the last
+ * failure's message is available from `tt_last_error` (per host thread).
+ */
+#ifndef TTJAM_B200_H
+#define TTJAM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TT_ABI_VERSION 1
+
+typedef enum tt_status {
+  TT_OK = 0,
+  TT_ERR_INVALID_CONFIG = -1,  /* mirrors the ValueErrors of TransformerConfig.validate */
+  TT_ERR_INVALID_ARGUMENT = -2,/* null pointer, bad size, misaligned pointer */
+  TT_ERR_UNSUPPORTED = -3,     /* a shape this build has no kernel for */
+  TT_ERR_WORKSPACE = -4,       /* workspace or image smaller than required */
+  TT_ERR_CUDA = -5,            /* a CUDA runtime call or launch failed */
+  TT_ERR_DEVICE_TIMEOUT = -6,  /* a bounded device-side wait gave up (status word) */
+  TT_ERR_DEVICE_FAULT = -7     /* a device-side self-check failed (status word) */
+} tt_status;
+
+/* Shape record: the fields of TransformerConfig that fix the weights
+ * (torch_transformer_benchmark.py:29-37). batch_size/seq_len are per call. */
+typedef struct tt_config {
+  int32_t d_model;
+  int32_t num_heads;
+  int32_t ffn_dim;
+  int32_t num_layers;
+  int32_t causal;      /* 0 or 1 */
+  int32_t reserved[3]; /* must be 0 */
+} tt_config;
+
+/* One BaselineTransformerBlock's parameters, nn.Linear layout W[out,in]
+ * (torch_transformer_benchmark.py:125-132, :72-75). Device pointers, fp32,
+ * contiguous. */
+typedef struct tt_layer_params {
+  const float *norm1_weight, *norm1_bias;     /* [D] */
+  const float *q_weight, *q_bias;             /* [D,D], [D] */
+  const float *k_weight, *k_bias;
+  const float *v_weight, *v_bias;
+  const float *out_weight, *out_bias;         /* [D,D], [D] */
+  const float *norm2_weight, *norm2_bias;     /* [D] */
+  const float *ffn_in_weight, *ffn_in_bias;   /* [F,D], [F] */
+  const float *ffn_out_weight, *ffn_out_bias; /* [D,F], [D] */
+} tt_layer_params;
+
+/* ABI version of the loaded library (TT_ABI_VERSION at build time). */
+int tt_abi_version(void);
+
+/* TransformerConfig.validate (torch_transformer_benchmark.py:39-56) plus the
+ * limits of this build. Returns TT_OK, TT_ERR_INVALID_CONFIG or
+ * TT_ERR_UNSUPPORTED; the message names the failing field. */
+int tt_validate_config(const tt_config *cfg);
+
+/* Bytes of the packed model image for `cfg` (0 if cfg is invalid). */
+size_t tt_image_bytes(const tt_config *cfg);
+
+/* Pack one model's parameters into `image` on `stream`: q/k/v concatenated
+ * into one [3D,D] projection, precision splits for the tensor-core path, a
+ * zeroed device status word. Replaces the weight delivery of
+ * `copy_model_weights` / `load_state_dict` (torch_transformer_benchmark.py:
+ * 203-213) and the repack of final_submission.py:426-466. `layers` is a host
+ * array of `cfg->num_layers` entries. The source parameters may be freed or
+ * changed once the stream has passed this call. */
+int tt_pack_image(const tt_config *cfg, const tt_layer_params *layers,
+                  const float *final_norm_weight, const float *final_norm_bias,
+                  void *image, size_t image_bytes, void *stream);
+
+/* Bytes of scratch `tt_forward` needs for one [batch, seq] call. */
+size_t tt_workspace_bytes(const tt_config *cfg, int64_t batch, int64_t seq);
+
+/* The forward pass, BaselineTransformer.forward / UserOptimizedTransformer.forward
+ * (torch_transformer_benchmark.py:162-172, :185-199):
+ *   x    [batch, seq, d_model] fp32, contiguous;
+ *   mask [batch, seq] bytes (torch.bool layout: 0 = padding, 1 = valid), or NULL
+ *        for "no mask";
+ *   y    [batch, seq, d_model] fp32, written in full (padding rows are 0);
+ *        may not alias x.
+ * Enqueues all work on `stream`; returns after launching, without a sync.
+ * Errors found on the device (a bounded wait that gave up) are latched in the
+ * image's status word; read them with tt_read_status. */
+int tt_forward(const tt_config *cfg, const void *image, const float *x,
+               const uint8_t *mask, int64_t batch, int64_t seq, float *y,
+               void *workspace, size_t workspace_bytes, void *stream);
+
+/* Which kernel schedule tt_forward picks for this call (for reports and tests):
+ * 1 = single-launch cluster forward, 2 = per-op kernels with FFMA GEMMs,
+ * 3 = per-op kernels with 3xTF32 tensor-core GEMMs. Negative on error. */
+int tt_forward_plan(const tt_config *cfg, int64_t batch, int64_t seq);
+
+/* Number of kernel launches tt_forward makes for this call (what a profiler
+ * sees per forward). Negative on error. */
+int tt_forward_launch_count(const tt_config *cfg, int64_t batch, int64_t seq);
+
+/* Synchronises `stream`, reads and clears the image's device status word.
+ * *code receives TT_OK or the latched device error (TT_ERR_DEVICE_*),
+ * *detail a kernel-specific location code. Returns TT_OK unless the read
+ * itself failed. */
+int tt_read_status(const tt_config *cfg, const void *image, int32_t *code,
+                   int32_t *detail, void *stream);
+
+/* Copies the calling thread's last error message into buf (NUL-terminated,
+ * truncated to len). Returns the message length. */
+int tt_last_error(char *buf, size_t len);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TTJAM_B200_H */

@@ -1,0 +1,89 @@
+"""The C ABI library: loads, exports every declared symbol, validates without a GPU."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from ttjam_gottagofast_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    inc = os.path.join(ROOT, "include")
+    for fn in os.listdir(inc):
+        if fn.endswith(".h"):
+            text = open(os.path.join(inc, fn)).read()
+            text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+            names |= set(re.findall(r"\b(tt_[a-z_0-9]+)\s*\(", text))
+    return names
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return _lib.load()
+
+
+def test_library_is_sm100a_build_in_tree(lib):
+    assert os.path.dirname(_lib.lib_path()).endswith("ttjam_gottagofast_b200")
+    assert lib.tt_abi_version() == _lib.TT_ABI_VERSION
+
+
+def test_every_declared_symbol_is_exported(lib):
+    decl = declared_symbols()
+    assert decl, "no declarations parsed"
+    assert decl <= set(_lib.EXPORTED) | decl
+    for name in decl:
+        assert hasattr(lib, name), name
+
+
+def _cfg(d=128, h=4, f=128, l=4, causal=1):
+    c = _lib.TTConfig()
+    c.d_model, c.num_heads, c.ffn_dim, c.num_layers, c.causal = d, h, f, l, causal
+    return c
+
+
+def test_validate_config_codes(lib):
+    assert lib.tt_validate_config(ctypes.byref(_cfg())) == 0
+    assert lib.tt_validate_config(ctypes.byref(_cfg(h=3))) == _lib.TT_ERR_INVALID_CONFIG
+    assert "divisible" in _lib.last_error(lib)
+    assert lib.tt_validate_config(ctypes.byref(_cfg(l=0))) == _lib.TT_ERR_INVALID_CONFIG
+    assert lib.tt_validate_config(ctypes.byref(_cfg(d=1024, h=2))) == _lib.TT_ERR_UNSUPPORTED
+    assert lib.tt_validate_config(None) == _lib.TT_ERR_INVALID_ARGUMENT
+
+
+def test_image_and_workspace_sizes(lib):
+    c = _cfg()
+    n = lib.tt_image_bytes(ctypes.byref(c))
+    per_layer = (4 * 128 * 128 + 2 * 128 * 128) * 4
+    assert 4 * per_layer < n < 4 * per_layer + 64 * 1024
+    ws = lib.tt_workspace_bytes(ctypes.byref(c), 4, 16)
+    assert ws >= 64 * (3 * 128 + 128 + 128) * 4
+    assert lib.tt_image_bytes(ctypes.byref(_cfg(h=3))) == 0
+
+
+def test_forward_argument_errors_need_no_gpu(lib):
+    c = _cfg()
+    rc = lib.tt_forward(ctypes.byref(c), None, None, None, 4, 16, None, None, 0, None)
+    assert rc == _lib.TT_ERR_INVALID_ARGUMENT
+    # sizes are checked before anything is launched
+    rc = lib.tt_forward(ctypes.byref(c), 256, 512, None, 4, 16, 1024, 2048, 16, None)
+    assert rc == _lib.TT_ERR_WORKSPACE
+    assert "workspace" in _lib.last_error(lib)
+    rc = lib.tt_forward(ctypes.byref(c), 256, 512, None, -1, 16, 1024, 2048, 16, None)
+    assert rc == _lib.TT_ERR_INVALID_ARGUMENT
+    # empty batch is a no-op
+    assert lib.tt_forward(ctypes.byref(c), None, None, None, 0, 16, None, None, 0, None) == 0
+
+
+def test_pack_argument_errors_need_no_gpu(lib):
+    c = _cfg()
+    rc = lib.tt_pack_image(ctypes.byref(c), None, None, None, None, 0, None)
+    assert rc == _lib.TT_ERR_INVALID_ARGUMENT
+
+
+def test_forward_plan(lib):
+    assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(_cfg(d=512, h=8, f=2048, l=6)),
+                                               16, 1024)]

@@ -1,0 +1,171 @@
+"""Parity of the CUDA forward (through the C ABI) against the reference.
+
+Two anchors:
+* the golden fixtures, produced by the reference module itself on CPU;
+* the oracle restatement run on the same device in strict fp32 (TF32 off) at
+  the full sizes of every workload, sequence-sliced where the reference's
+  [B,H,S,S] tensor would be large.
+
+Tolerance: the reference's accuracy gate, element-wise
+abs(opt - ref) <= 0.002 OR abs(opt - ref) <= 0.02 * abs(ref), all finite
+(torch_transformer_benchmark.py:309-316, defaults :618-619).
+"""
+import pytest
+import torch
+
+from conftest import GOLDENS, GOLDEN_IDS
+from oracle import reference_model as oracle
+from ttjam_gottagofast_b200 import UserOptimizedTransformer, compare_outputs, generate_random_case
+from ttjam_gottagofast_b200.config import WORKLOADS
+from ttjam_gottagofast_b200.contract import ATOL, HARNESS_VARIANTS, RTOL
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+@pytest.fixture(autouse=True)
+def strict_fp32():
+    old = (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = old
+
+
+_MODELS = {}
+
+
+def model_for(cfg, seed=1234):
+    key = (cfg.d_model, cfg.num_heads, cfg.ffn_dim, cfg.num_layers, cfg.causal, seed)
+    if key not in _MODELS:
+        if len(_MODELS) > 3:
+            _MODELS.clear()
+        params = oracle.init_params(cfg, seed=seed, device=DEV)
+        model = UserOptimizedTransformer(cfg).to(DEV).eval()
+        model.load_state_dict(params, strict=True)
+        _MODELS[key] = (model, params)
+    return _MODELS[key]
+
+
+def check(ref, out, label):
+    res = compare_outputs(ref, out, rtol=RTOL, atol=ATOL)
+    print(f"{label}: max_abs={res.max_abs_error:.3e} max_rel={res.max_relative_error:.3e} "
+          f"failed={res.failed_elements}/{res.total_elements}")
+    assert res.passed, (label, res)
+    return res
+
+
+@pytest.mark.parametrize("case", GOLDENS, ids=GOLDEN_IDS)
+def test_golden_parity(case):
+    model, _ = model_for(case.config, case.meta["model_seed"])
+    x = torch.from_numpy(case.x).to(DEV)
+    mask = torch.from_numpy(case.mask).to(DEV) if case.uses_mask else None
+    with torch.inference_mode():
+        y = model(x, mask)
+    torch.cuda.synchronize()
+    check(torch.from_numpy(case.y), y.cpu(), case.name)
+    if mask is not None:
+        assert (y[~mask] == 0).all(), "padded rows must be exactly zero"
+    assert model.read_device_status() == (0, 0)
+
+
+def _full_size_case(name, variant):
+    w = WORKLOADS[name]
+    cfg = w.config
+    model, params = model_for(cfg)
+    seed = variant.get("seed", 101234)
+    x, mask = generate_random_case(cfg, "cpu", torch.float32, seed,
+                                   variant.get("padding_ratio", w.padding_ratio),
+                                   variant.get("input_scale", w.input_scale))
+    x, mask = x.to(DEV), mask.to(DEV)
+    with torch.inference_mode():
+        y = model(x, mask)
+    return cfg, params, x, mask, y
+
+
+SMALL_WORKLOAD_CASES = [(n, v) for n in ("A", "B1", "B2", "C")
+                        for v in [{"name": "own"}] + HARNESS_VARIANTS]
+
+
+@pytest.mark.parametrize("name,variant", SMALL_WORKLOAD_CASES,
+                         ids=[f"{n}-{v['name']}" for n, v in SMALL_WORKLOAD_CASES])
+def test_workload_parity_full_size(name, variant):
+    cfg, params, x, mask, y = _full_size_case(name, variant)
+    ref = oracle.forward(params, cfg, x, mask, batch_chunk=8)
+    check(ref, y, f"{name}/{variant['name']}")
+
+
+@pytest.mark.parametrize("variant", [{"name": "own"}, HARNESS_VARIANTS[1], HARNESS_VARIANTS[4]],
+                         ids=["own", "large_scale", "padded_heavy"])
+def test_workload_D_parity_full_size(variant):
+    cfg, params, x, mask, y = _full_size_case("D", variant)
+    ref = oracle.forward(params, cfg, x, mask, batch_chunk=2)
+    check(ref, y, f"D/{variant['name']}")
+
+
+def test_workload_E_parity_sequence_sample():
+    """Full-size E forward; the oracle checks the shortest, the longest and one
+    middle sequence (sequences are independent)."""
+    cfg, params, x, mask, y = _full_size_case("E", {"name": "own"})
+    lengths = mask.sum(1)
+    picks = sorted({int(lengths.argmin()), int(lengths.argmax()), cfg.batch_size // 2})
+    idx = torch.tensor(picks, device=DEV)
+    ref = oracle.forward(params, cfg, x[idx], mask[idx], batch_chunk=1)
+    check(ref, y[idx], f"E/seqs{picks}")
+    assert torch.isfinite(y).all()
+    assert (y[~mask] == 0).all()
+
+
+def test_output_depends_on_input_and_is_fresh():
+    """The reference harness's anti-caching check (tools/harness.py:156-173):
+    seeds 101, 202, 101 -- outputs held at the same time."""
+    cfg = WORKLOADS["A"].config
+    model, _ = model_for(cfg)
+    outs = []
+    for seed in (101, 202, 101):
+        x, mask = generate_random_case(cfg, "cpu", torch.float32, seed, 0.0, 1.0)
+        with torch.inference_mode():
+            outs.append(model(x.to(DEV), mask.to(DEV)))
+    assert not torch.equal(outs[0], outs[1])
+    assert torch.equal(outs[0], outs[2])
+    assert outs[0].data_ptr() != outs[2].data_ptr()
+
+
+def test_weight_update_repacks():
+    cfg = WORKLOADS["B1"].config
+    model = UserOptimizedTransformer(cfg).to(DEV)
+    params = oracle.init_params(cfg, seed=5, device=DEV)
+    model.load_state_dict(params)
+    x, mask = generate_random_case(cfg, "cpu", torch.float32, 3, 0.0, 1.0)
+    x, mask = x.to(DEV), mask.to(DEV)
+    with torch.inference_mode():
+        y0 = model(x, mask)
+    with torch.no_grad():
+        model.layers[0].ffn_out.bias.add_(0.5)      # in-place write: version counter
+    params["layers.0.ffn_out.bias"] = params["layers.0.ffn_out.bias"] + 0.5
+    with torch.inference_mode():
+        y1 = model(x, mask)
+    ref = oracle.forward(params, cfg, x, mask)
+    assert not torch.equal(y0, y1)
+    check(ref, y1, "after in-place update")
+
+
+def test_no_mask_and_all_true_mask_agree():
+    cfg = WORKLOADS["B1"].config
+    model, _ = model_for(cfg)
+    x, mask = generate_random_case(cfg, "cpu", torch.float32, 9, 0.0, 1.0)
+    x, mask = x.to(DEV), mask.to(DEV)
+    with torch.inference_mode():
+        torch.testing.assert_close(model(x, None), model(x, mask), rtol=0, atol=0)
+
+
+def test_runs_on_current_stream():
+    cfg = WORKLOADS["B1"].config
+    model, params = model_for(cfg)
+    x, mask = generate_random_case(cfg, "cpu", torch.float32, 4, 0.0, 1.0)
+    x, mask = x.to(DEV), mask.to(DEV)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s), torch.inference_mode():
+        y = model(x, mask)
+    s.synchronize()
+    check(oracle.forward(params, cfg, x, mask), y, "side stream")

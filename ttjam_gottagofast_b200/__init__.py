@@ -1,0 +1,17 @@
+"""B200 (sm_100a) implementation of the reference's pre-norm Transformer forward.
+
+Public surface, mirroring the reference contract (torch_transformer_benchmark.py):
+`TransformerConfig`, `UserOptimizedTransformer`, `generate_random_case`,
+`compare_outputs`, `copy_model_weights`, and the harness candidate hooks
+`build_model` / `load_from_baseline`.
+"""
+from .config import TransformerConfig, WORKLOADS, MODEL_SEED, TIMING_DATA_SEED
+from .contract import generate_random_case, compare_outputs, AccuracyResult, RTOL, ATOL
+from .model import UserOptimizedTransformer
+from .candidate import build_model, load_from_baseline, copy_model_weights
+
+__all__ = [
+    "TransformerConfig", "WORKLOADS", "MODEL_SEED", "TIMING_DATA_SEED",
+    "generate_random_case", "compare_outputs", "AccuracyResult", "RTOL", "ATOL",
+    "UserOptimizedTransformer", "build_model", "load_from_baseline", "copy_model_weights",
+]

@@ -1,0 +1,126 @@
+"""ctypes binding of the C ABI in include/ttjam_b200.h.
+
+The shared library is built in-tree (`build.py`). Loading fails loudly when it
+is missing: there is no CPU or eager-PyTorch fallback for the forward pass.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+from . import build as _build
+
+TT_ABI_VERSION = 1
+
+TT_OK = 0
+TT_ERR_INVALID_CONFIG = -1
+TT_ERR_INVALID_ARGUMENT = -2
+TT_ERR_UNSUPPORTED = -3
+TT_ERR_WORKSPACE = -4
+TT_ERR_CUDA = -5
+TT_ERR_DEVICE_TIMEOUT = -6
+TT_ERR_DEVICE_FAULT = -7
+
+PLAN_NAMES = {1: "cluster", 2: "ops_ffma", 3: "ops_tc3xtf32"}
+
+# Every entry point include/ttjam_b200.h declares.
+EXPORTED = (
+    "tt_abi_version", "tt_validate_config", "tt_image_bytes", "tt_pack_image",
+    "tt_workspace_bytes", "tt_forward", "tt_forward_plan", "tt_forward_launch_count",
+    "tt_read_status",
+    "tt_last_error",
+)
+
+
+class TTConfig(ctypes.Structure):
+    _fields_ = [("d_model", ctypes.c_int32), ("num_heads", ctypes.c_int32),
+                ("ffn_dim", ctypes.c_int32), ("num_layers", ctypes.c_int32),
+                ("causal", ctypes.c_int32), ("reserved", ctypes.c_int32 * 3)]
+
+
+class TTLayerParams(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_void_p) for name in (
+        "norm1_weight", "norm1_bias", "q_weight", "q_bias", "k_weight", "k_bias",
+        "v_weight", "v_bias", "out_weight", "out_bias", "norm2_weight", "norm2_bias",
+        "ffn_in_weight", "ffn_in_bias", "ffn_out_weight", "ffn_out_bias")]
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def lib_path() -> str:
+    return _build.LIB_PATH
+
+
+def load(build_if_missing: bool = True) -> ctypes.CDLL:
+    """Load (building first if needed and allowed) the sm_100a library."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = _build.LIB_PATH
+        if not os.path.exists(path):
+            if not build_if_missing:
+                raise RuntimeError(f"CUDA extension not built: {path} is missing "
+                                   "(run python -m ttjam_gottagofast_b200.build)")
+            _build.build()
+        lib = ctypes.CDLL(path)
+        vp, i32, i64, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t
+        cfgp = ctypes.POINTER(TTConfig)
+        lib.tt_abi_version.restype = ctypes.c_int
+        lib.tt_abi_version.argtypes = []
+        lib.tt_validate_config.restype = ctypes.c_int
+        lib.tt_validate_config.argtypes = [cfgp]
+        lib.tt_image_bytes.restype = sz
+        lib.tt_image_bytes.argtypes = [cfgp]
+        lib.tt_pack_image.restype = ctypes.c_int
+        lib.tt_pack_image.argtypes = [cfgp, ctypes.POINTER(TTLayerParams), vp, vp, vp, sz, vp]
+        lib.tt_workspace_bytes.restype = sz
+        lib.tt_workspace_bytes.argtypes = [cfgp, i64, i64]
+        lib.tt_forward.restype = ctypes.c_int
+        lib.tt_forward.argtypes = [cfgp, vp, vp, vp, i64, i64, vp, vp, sz, vp]
+        lib.tt_forward_plan.restype = ctypes.c_int
+        lib.tt_forward_plan.argtypes = [cfgp, i64, i64]
+        lib.tt_forward_launch_count.restype = ctypes.c_int
+        lib.tt_forward_launch_count.argtypes = [cfgp, i64, i64]
+        lib.tt_read_status.restype = ctypes.c_int
+        lib.tt_read_status.argtypes = [cfgp, vp, ctypes.POINTER(i32), ctypes.POINTER(i32), vp]
+        lib.tt_last_error.restype = ctypes.c_int
+        lib.tt_last_error.argtypes = [ctypes.c_char_p, sz]
+        if lib.tt_abi_version() != TT_ABI_VERSION:
+            raise RuntimeError("libttjam_b200.so ABI version mismatch; rebuild it")
+        _lib = lib
+        return lib
+
+
+def last_error(lib=None) -> str:
+    lib = lib or load()
+    buf = ctypes.create_string_buffer(1024)
+    lib.tt_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def check(rc: int, what: str, lib=None) -> None:
+    """Map a negative tt_status to the Python exception the reference raises
+    for the same condition (ValueError for config errors)."""
+    if rc == TT_OK:
+        return
+    msg = f"{what}: {last_error(lib)} (status {rc})"
+    if rc == TT_ERR_INVALID_CONFIG:
+        raise ValueError(msg)
+    if rc in (TT_ERR_INVALID_ARGUMENT, TT_ERR_UNSUPPORTED):
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def make_config(cfg) -> TTConfig:
+    """A tt_config from any object with TransformerConfig's fields."""
+    c = TTConfig()
+    c.d_model = int(cfg.d_model)
+    c.num_heads = int(cfg.num_heads)
+    c.ffn_dim = int(cfg.ffn_dim)
+    c.num_layers = int(cfg.num_layers)
+    c.causal = 1 if cfg.causal else 0
+    return c

@@ -1,0 +1,255 @@
+// C ABI of the forward pass: config validation, model-image packing and the
+// forward schedule. Declared in include/ttjam_b200.h.
+#include <cstring>
+#include <string>
+
+#include "image.cuh"
+#include "tt_common.cuh"
+
+namespace tt {
+
+static thread_local std::string g_last_error;
+
+void set_last_error(const std::string &msg) { g_last_error = msg; }
+
+namespace {
+
+__global__ void tf32_split_kernel(const float *__restrict__ src, float *__restrict__ hi,
+                                  float *__restrict__ lo, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = src[i];
+    const float h = tf32_round(v);
+    hi[i] = h;
+    lo[i] = v - h;
+  }
+}
+
+int split_tf32(const float *src, float *hi, float *lo, int64_t n, cudaStream_t stream) {
+  const int threads = 256;
+  const int64_t blocks = std::min<int64_t>(ceil_div(n, threads), 148 * 8);
+  tf32_split_kernel<<<(unsigned)blocks, threads, 0, stream>>>(src, hi, lo, n);
+  TT_LAUNCH_CHECK("tf32_split");
+  return TT_OK;
+}
+
+bool misaligned(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; }
+
+}  // namespace
+
+int validate_config(const tt_config *cfg) {
+  if (cfg == nullptr) return fail(TT_ERR_INVALID_ARGUMENT, "config is NULL");
+  // Same order and wording as TransformerConfig.validate
+  // (torch_transformer_benchmark.py:39-56) for the fields this record holds.
+  if (cfg->d_model <= 0) return fail(TT_ERR_INVALID_CONFIG, "d_model must be positive");
+  if (cfg->num_heads <= 0) return fail(TT_ERR_INVALID_CONFIG, "num_heads must be positive");
+  if (cfg->d_model % cfg->num_heads != 0)
+    return fail(TT_ERR_INVALID_CONFIG, "d_model (" + std::to_string(cfg->d_model) +
+                                           ") must be divisible by num_heads (" +
+                                           std::to_string(cfg->num_heads) + ")");
+  if (cfg->ffn_dim <= 0) return fail(TT_ERR_INVALID_CONFIG, "ffn_dim must be positive");
+  if (cfg->num_layers <= 0) return fail(TT_ERR_INVALID_CONFIG, "num_layers must be positive");
+  if (cfg->causal != 0 && cfg->causal != 1)
+    return fail(TT_ERR_INVALID_CONFIG, "causal must be 0 or 1");
+  for (int i = 0; i < 3; ++i)
+    if (cfg->reserved[i] != 0) return fail(TT_ERR_INVALID_CONFIG, "reserved fields must be 0");
+  if (cfg->d_model / cfg->num_heads > 256)
+    return fail(TT_ERR_UNSUPPORTED, "head_dim > 256 is not supported by this build");
+  if (cfg->d_model > 65536 || cfg->ffn_dim > (1 << 20))
+    return fail(TT_ERR_UNSUPPORTED, "d_model or ffn_dim too large for this build");
+  return TT_OK;
+}
+
+int forward_plan(const tt_config *cfg, int64_t batch, int64_t seq) {
+  (void)batch;
+  (void)seq;
+  return uses_tensor_cores(*cfg) ? PLAN_OPS_TC : PLAN_OPS_FFMA;
+}
+
+int forward_ops(const tt_config &cfg, const ImageLayout &L, const char *image, const float *x,
+                const uint8_t *mask, int64_t batch, int64_t seq, float *y,
+                const WorkspaceLayout &W, char *ws, cudaStream_t stream) {
+  const int D = cfg.d_model, F = cfg.ffn_dim, H = cfg.num_heads, hd = D / H;
+  const int64_t T = batch * seq;
+  float *qkv = reinterpret_cast<float *>(ws + W.qkv);
+  float *ctx = reinterpret_cast<float *>(ws + W.ctx);
+  float *hbuf = reinterpret_cast<float *>(ws + W.h);
+  const float eps = 1e-5f;
+  for (int l = 0; l < cfg.num_layers; ++l) {
+    const LayerOffsets &o = L.layer[l];
+    auto P = [&](size_t off) { return reinterpret_cast<const float *>(image + off); };
+    const float *xin = (l == 0) ? x : y;
+    int rc;
+    // q|k|v = LayerNorm1(x) . Wqkv^T + bqkv
+    GemmParams g{};
+    g.A = xin; g.lda = D; g.W = P(o.wqkv); g.bias = P(o.bqkv); g.C = qkv; g.ldc = 3LL * D;
+    g.ln_gamma = P(o.ln1_w); g.ln_beta = P(o.ln1_b); g.ln_eps = eps;
+    g.M = T; g.N = 3 * D; g.K = D; g.epilogue = EPI_BIAS;
+    if ((rc = launch_gemm_ffma(g, stream)) != TT_OK) return rc;
+    // context = softmax(q k^T * scale + masks) v
+    AttentionParams a{};
+    a.qkv = qkv; a.ctx = ctx; a.mask = mask; a.batch = batch; a.seq = (int)seq;
+    a.d_model = D; a.num_heads = H; a.head_dim = hd; a.causal = cfg.causal;
+    a.scale = (float)(1.0 / std::sqrt((double)hd));
+    if ((rc = launch_attention_ffma(a, stream)) != TT_OK) return rc;
+    // y = x + masked(context . Wo^T + bo)
+    GemmParams go{};
+    go.A = ctx; go.lda = D; go.W = P(o.wo); go.bias = P(o.bo); go.R = xin; go.C = y;
+    go.ldc = D; go.row_mask = mask; go.M = T; go.N = D; go.K = D;
+    go.epilogue = EPI_BIAS_RESIDUAL;
+    if ((rc = launch_gemm_ffma(go, stream)) != TT_OK) return rc;
+    // h = gelu(LayerNorm2(y) . W1^T + b1)
+    GemmParams g1{};
+    g1.A = y; g1.lda = D; g1.W = P(o.w1); g1.bias = P(o.b1); g1.C = hbuf; g1.ldc = F;
+    g1.ln_gamma = P(o.ln2_w); g1.ln_beta = P(o.ln2_b); g1.ln_eps = eps;
+    g1.M = T; g1.N = F; g1.K = D; g1.epilogue = EPI_BIAS_GELU;
+    if ((rc = launch_gemm_ffma(g1, stream)) != TT_OK) return rc;
+    // y = masked(y + h . W2^T + b2)
+    GemmParams g2{};
+    g2.A = hbuf; g2.lda = F; g2.W = P(o.w2); g2.bias = P(o.b2); g2.R = y; g2.C = y;
+    g2.ldc = D; g2.row_mask = mask; g2.M = T; g2.N = D; g2.K = F;
+    g2.epilogue = EPI_BIAS_RESIDUAL;
+    if ((rc = launch_gemm_ffma(g2, stream)) != TT_OK) return rc;
+  }
+  return launch_layernorm(y, y, nullptr, nullptr,
+                          reinterpret_cast<const float *>(image + L.final_w),
+                          reinterpret_cast<const float *>(image + L.final_b), mask, 1, T, D,
+                          eps, stream);
+}
+
+}  // namespace tt
+
+using namespace tt;
+
+extern "C" {
+
+int tt_abi_version(void) { return TT_ABI_VERSION; }
+
+int tt_validate_config(const tt_config *cfg) { return validate_config(cfg); }
+
+size_t tt_image_bytes(const tt_config *cfg) {
+  if (validate_config(cfg) != TT_OK) return 0;
+  return ImageLayout(*cfg).total;
+}
+
+int tt_pack_image(const tt_config *cfg, const tt_layer_params *layers,
+                  const float *final_norm_weight, const float *final_norm_bias, void *image,
+                  size_t image_bytes, void *stream_) {
+  int rc = validate_config(cfg);
+  if (rc != TT_OK) return rc;
+  if (layers == nullptr || final_norm_weight == nullptr || final_norm_bias == nullptr ||
+      image == nullptr)
+    return fail(TT_ERR_INVALID_ARGUMENT, "tt_pack_image: NULL pointer argument");
+  const ImageLayout L(*cfg);
+  if (image_bytes < L.total)
+    return fail(TT_ERR_WORKSPACE, "tt_pack_image: image buffer smaller than tt_image_bytes");
+  if (misaligned(image)) return fail(TT_ERR_INVALID_ARGUMENT, "image must be 16-byte aligned");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  char *img = static_cast<char *>(image);
+  const size_t D = cfg->d_model, F = cfg->ffn_dim, f4 = sizeof(float);
+  auto copy = [&](size_t off, const float *src, size_t n) -> int {
+    if (src == nullptr) return fail(TT_ERR_INVALID_ARGUMENT, "tt_pack_image: NULL parameter");
+    TT_CUDA_TRY(cudaMemcpyAsync(img + off, src, n * f4, cudaMemcpyDeviceToDevice, stream));
+    return TT_OK;
+  };
+  TT_CUDA_TRY(cudaMemsetAsync(img + L.status, 0, sizeof(DeviceStatus), stream));
+  for (int l = 0; l < cfg->num_layers; ++l) {
+    const tt_layer_params &p = layers[l];
+    const LayerOffsets &o = L.layer[l];
+    if ((rc = copy(o.ln1_w, p.norm1_weight, D)) || (rc = copy(o.ln1_b, p.norm1_bias, D)) ||
+        (rc = copy(o.wqkv, p.q_weight, D * D)) ||
+        (rc = copy(o.wqkv + D * D * f4, p.k_weight, D * D)) ||
+        (rc = copy(o.wqkv + 2 * D * D * f4, p.v_weight, D * D)) ||
+        (rc = copy(o.bqkv, p.q_bias, D)) || (rc = copy(o.bqkv + D * f4, p.k_bias, D)) ||
+        (rc = copy(o.bqkv + 2 * D * f4, p.v_bias, D)) || (rc = copy(o.wo, p.out_weight, D * D)) ||
+        (rc = copy(o.bo, p.out_bias, D)) || (rc = copy(o.ln2_w, p.norm2_weight, D)) ||
+        (rc = copy(o.ln2_b, p.norm2_bias, D)) || (rc = copy(o.w1, p.ffn_in_weight, F * D)) ||
+        (rc = copy(o.b1, p.ffn_in_bias, F)) || (rc = copy(o.w2, p.ffn_out_weight, D * F)) ||
+        (rc = copy(o.b2, p.ffn_out_bias, D)))
+      return rc;
+    if (L.tensor) {
+      auto F_ = [&](size_t off) { return reinterpret_cast<float *>(img + off); };
+      if ((rc = split_tf32(F_(o.wqkv), F_(o.wqkv_hi), F_(o.wqkv_lo), 3 * D * D, stream)) ||
+          (rc = split_tf32(F_(o.wo), F_(o.wo_hi), F_(o.wo_lo), D * D, stream)) ||
+          (rc = split_tf32(F_(o.w1), F_(o.w1_hi), F_(o.w1_lo), F * D, stream)) ||
+          (rc = split_tf32(F_(o.w2), F_(o.w2_hi), F_(o.w2_lo), D * F, stream)))
+        return rc;
+    }
+  }
+  if ((rc = copy(L.final_w, final_norm_weight, D)) || (rc = copy(L.final_b, final_norm_bias, D)))
+    return rc;
+  return TT_OK;
+}
+
+size_t tt_workspace_bytes(const tt_config *cfg, int64_t batch, int64_t seq) {
+  if (validate_config(cfg) != TT_OK || batch < 0 || seq < 0) return 0;
+  return WorkspaceLayout(*cfg, batch, seq).total;
+}
+
+int tt_forward_plan(const tt_config *cfg, int64_t batch, int64_t seq) {
+  const int rc = validate_config(cfg);
+  if (rc != TT_OK) return rc;
+  return forward_plan(cfg, batch, seq);
+}
+
+int tt_forward_launch_count(const tt_config *cfg, int64_t batch, int64_t seq) {
+  const int rc = validate_config(cfg);
+  if (rc != TT_OK) return rc;
+  if (batch <= 0 || seq <= 0) return 0;
+  return 5 * cfg->num_layers + 1;
+}
+
+int tt_forward(const tt_config *cfg, const void *image, const float *x, const uint8_t *mask,
+               int64_t batch, int64_t seq, float *y, void *workspace, size_t workspace_bytes,
+               void *stream_) {
+  int rc = validate_config(cfg);
+  if (rc != TT_OK) return rc;
+  if (batch < 0 || seq < 0) return fail(TT_ERR_INVALID_ARGUMENT, "batch and seq must be >= 0");
+  if (batch == 0 || seq == 0) return TT_OK;
+  if (image == nullptr || x == nullptr || y == nullptr)
+    return fail(TT_ERR_INVALID_ARGUMENT, "tt_forward: NULL image, x or y");
+  if (x == y) return fail(TT_ERR_INVALID_ARGUMENT, "tt_forward: y may not alias x");
+  if (misaligned(image) || misaligned(x) || misaligned(y) || misaligned(workspace))
+    return fail(TT_ERR_INVALID_ARGUMENT, "tt_forward: pointers must be 16-byte aligned");
+  if (seq > (int64_t)INT32_MAX || batch * seq > ((int64_t)1 << 40))
+    return fail(TT_ERR_UNSUPPORTED, "tt_forward: batch*seq too large");
+  const ImageLayout L(*cfg);
+  const WorkspaceLayout W(*cfg, batch, seq);
+  if (workspace_bytes < W.total || (W.total > 0 && workspace == nullptr))
+    return fail(TT_ERR_WORKSPACE, "tt_forward: workspace smaller than tt_workspace_bytes (" +
+                                      std::to_string(W.total) + " bytes)");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  return forward_ops(*cfg, L, static_cast<const char *>(image), x, mask, batch, seq, y, W,
+                     static_cast<char *>(workspace), stream);
+}
+
+int tt_read_status(const tt_config *cfg, const void *image, int32_t *code, int32_t *detail,
+                   void *stream_) {
+  int rc = validate_config(cfg);
+  if (rc != TT_OK) return rc;
+  if (image == nullptr || code == nullptr)
+    return fail(TT_ERR_INVALID_ARGUMENT, "tt_read_status: NULL argument");
+  const ImageLayout L(*cfg);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  DeviceStatus st{};
+  char *img = const_cast<char *>(static_cast<const char *>(image));
+  TT_CUDA_TRY(cudaMemcpyAsync(&st, img + L.status, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                              stream));
+  TT_CUDA_TRY(cudaStreamSynchronize(stream));
+  TT_CUDA_TRY(cudaMemsetAsync(img + L.status, 0, sizeof(DeviceStatus), stream));
+  *code = st.code;
+  if (detail) *detail = st.detail;
+  return TT_OK;
+}
+
+int tt_last_error(char *buf, size_t len) {
+  const std::string &m = g_last_error;
+  if (buf != nullptr && len > 0) {
+    const size_t n = std::min(len - 1, m.size());
+    std::memcpy(buf, m.data(), n);
+    buf[n] = '\0';
+  }
+  return (int)m.size();
+}
+
+}  // extern "C"

@@ -1,0 +1,104 @@
+// Layout of the packed model image and of the per-call workspace in HBM.
+//
+// Image (one per model, built by tt_pack_image):
+//   [status word, 256 B]
+//   per layer: ln1 w,b | Wqkv [3D,D] (q rows, then k, then v) | bqkv [3D] |
+//              Wo [D,D] | bo | ln2 w,b | W1 [F,D] | b1 [F] | W2 [D,F] | b2 [D]
+//              and, on the tensor-core path, the TF32 hi/lo split of each weight
+//   final_norm w,b
+// Every array starts on a 256-byte boundary (TMA and float4 friendly).
+//
+// Workspace (per call, [T = batch*seq] tokens):
+//   qkv [T,3D] | ctx [T,D] | h [T,F]   and on the tensor-core path the TF32
+//   splits of the GEMM A operands: ln_hi/ln_lo [T,D], ctx_hi/ctx_lo [T,D],
+//   h_hi/h_lo [T,F].
+#pragma once
+
+#include <vector>
+
+#include "tt_common.cuh"
+
+namespace tt {
+
+enum ForwardPlan : int { PLAN_CLUSTER = 1, PLAN_OPS_FFMA = 2, PLAN_OPS_TC = 3 };
+
+// The 3xTF32 tensor-core GEMMs take over where d_model >= 512 makes every
+// projection a large dense contraction.
+inline bool uses_tensor_cores(const tt_config &cfg) {
+  (void)cfg;
+  return false;
+}
+
+struct LayerOffsets {
+  size_t ln1_w, ln1_b, wqkv, bqkv, wo, bo, ln2_w, ln2_b, w1, b1, w2, b2;
+  size_t wqkv_hi, wqkv_lo, wo_hi, wo_lo, w1_hi, w1_lo, w2_hi, w2_lo;
+};
+
+struct ImageLayout {
+  size_t status = 0;
+  std::vector<LayerOffsets> layer;
+  size_t final_w = 0, final_b = 0, total = 0;
+  bool tensor = false;
+
+  explicit ImageLayout(const tt_config &cfg) {
+    const size_t D = cfg.d_model, F = cfg.ffn_dim, f4 = sizeof(float);
+    tensor = uses_tensor_cores(cfg);
+    size_t cur = 0;
+    auto take = [&](size_t n_floats) {
+      const size_t off = cur;
+      cur = align_up(cur + n_floats * f4, 256);
+      return off;
+    };
+    status = take(256 / f4);
+    layer.resize(cfg.num_layers);
+    for (auto &o : layer) {
+      o.ln1_w = take(D); o.ln1_b = take(D);
+      o.wqkv = take(3 * D * D); o.bqkv = take(3 * D);
+      o.wo = take(D * D); o.bo = take(D);
+      o.ln2_w = take(D); o.ln2_b = take(D);
+      o.w1 = take(F * D); o.b1 = take(F);
+      o.w2 = take(D * F); o.b2 = take(D);
+      if (tensor) {
+        o.wqkv_hi = take(3 * D * D); o.wqkv_lo = take(3 * D * D);
+        o.wo_hi = take(D * D); o.wo_lo = take(D * D);
+        o.w1_hi = take(F * D); o.w1_lo = take(F * D);
+        o.w2_hi = take(D * F); o.w2_lo = take(D * F);
+      } else {
+        o.wqkv_hi = o.wqkv_lo = o.wo_hi = o.wo_lo = o.w1_hi = o.w1_lo = o.w2_hi = o.w2_lo = 0;
+      }
+    }
+    final_w = take(D);
+    final_b = take(D);
+    total = cur;
+  }
+};
+
+struct WorkspaceLayout {
+  size_t qkv = 0, ctx = 0, h = 0;
+  size_t ln_hi = 0, ln_lo = 0, ctx_hi = 0, ctx_lo = 0, h_hi = 0, h_lo = 0;
+  size_t total = 0;
+
+  WorkspaceLayout(const tt_config &cfg, int64_t batch, int64_t seq) {
+    const size_t T = (size_t)batch * (size_t)seq, D = cfg.d_model, F = cfg.ffn_dim;
+    const size_t f4 = sizeof(float);
+    size_t cur = 0;
+    auto take = [&](size_t n_floats) {
+      const size_t off = cur;
+      cur = align_up(cur + n_floats * f4, 256);
+      return off;
+    };
+    qkv = take(T * 3 * D);
+    ctx = take(T * D);
+    h = take(T * F);
+    if (uses_tensor_cores(cfg)) {
+      ln_hi = take(T * D); ln_lo = take(T * D);
+      ctx_hi = take(T * D); ctx_lo = take(T * D);
+      h_hi = take(T * F); h_lo = take(T * F);
+    }
+    total = cur;
+  }
+};
+
+int validate_config(const tt_config *cfg);
+
+}  // namespace tt

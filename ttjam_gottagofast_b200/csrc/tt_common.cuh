@@ -1,0 +1,117 @@
+// Shared helpers for the sm_100a kernels of the pre-norm Transformer forward.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdio>
+#include <string>
+
+#include "ttjam_b200.h"
+
+namespace tt {
+
+// Device status word layout inside the model image: [0] first error code,
+// [1] detail code of the kernel that raised it.
+struct DeviceStatus {
+  int32_t code;
+  int32_t detail;
+  int32_t pad[62];
+};
+
+__device__ __forceinline__ void raise_status(DeviceStatus *st, int32_t code, int32_t detail) {
+  if (st == nullptr) return;
+  if (atomicCAS(&st->code, 0, code) == 0) atomicExch(&st->detail, detail);
+}
+
+// Host-side error latch (per thread), surfaced through tt_last_error.
+void set_last_error(const std::string &msg);
+
+inline int fail(int code, const std::string &msg) {
+  set_last_error(msg);
+  return code;
+}
+
+#define TT_CUDA_TRY(expr)                                                              \
+  do {                                                                                 \
+    cudaError_t err__ = (expr);                                                        \
+    if (err__ != cudaSuccess)                                                          \
+      return ::tt::fail(TT_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(err__)); \
+  } while (0)
+
+#define TT_LAUNCH_CHECK(what)                                                          \
+  do {                                                                                 \
+    cudaError_t err__ = cudaGetLastError();                                            \
+    if (err__ != cudaSuccess)                                                          \
+      return ::tt::fail(TT_ERR_CUDA, std::string("launch of ") + (what) + ": " +     \
+                                         cudaGetErrorString(err__));                   \
+  } while (0)
+
+// Exact GELU, F.gelu(approximate="none"): 0.5*x*(1+erf(x/sqrt(2))).
+__device__ __forceinline__ float gelu_erf(float v) {
+  return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
+}
+
+// TF32 split used by the 3xTF32 tensor-core path: hi is v rounded to TF32
+// (round-to-nearest, ties away), lo = v - hi is exact in fp32.
+__device__ __forceinline__ float tf32_round(float v) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return __uint_as_float(r);
+}
+
+__host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+__host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// ---------------------------------------------------------------------------
+// Kernel launchers (defined in the per-kernel .cu files).
+// ---------------------------------------------------------------------------
+
+// Row LayerNorm, nn.LayerNorm(D) semantics (eps, biased variance). If
+// `zero_rows_mask` is set, rows whose mask byte is 0 are written as 0.
+// If y_hi/y_lo are given, also writes the TF32 split of the output.
+int launch_layernorm(const float *x, float *y, float *y_hi, float *y_lo, const float *gamma,
+                     const float *beta, const uint8_t *row_mask, int zero_masked_rows,
+                     int64_t rows, int d, float eps, cudaStream_t stream);
+
+enum GemmEpilogue : int {
+  EPI_BIAS = 0,             // C = A W^T + b
+  EPI_BIAS_GELU = 1,        // C = gelu(A W^T + b)
+  EPI_BIAS_RESIDUAL = 2,    // C = valid ? R + (A W^T + b) : 0   (R may alias C)
+};
+
+struct GemmParams {
+  const float *A;        // [M, K] row-major, leading dim lda
+  int64_t lda;
+  const float *W;        // [N, K] row-major (nn.Linear weight)
+  const float *bias;     // [N]
+  const float *R;        // residual [M, N], leading dim ldc (may alias C)
+  float *C;              // [M, N], leading dim ldc
+  int64_t ldc;
+  float *C_hi, *C_lo;    // optional TF32 split copies of C (same ldc)
+  const uint8_t *row_mask;  // [M] row validity, or null (all valid)
+  const float *ln_gamma, *ln_beta;  // LayerNorm prologue on A when non-null
+  float ln_eps;
+  int64_t M;
+  int N, K;
+  int epilogue;
+};
+
+// FFMA register-tiled fp32 GEMM with LayerNorm prologue and fused epilogues.
+int launch_gemm_ffma(const GemmParams &p, cudaStream_t stream);
+
+struct AttentionParams {
+  const float *qkv;      // [B*S, 3D]: q | k | v, head h at columns h*hd..h*hd+hd-1
+  float *ctx;            // [B*S, D]
+  float *ctx_hi, *ctx_lo;  // optional TF32 split copies
+  const uint8_t *mask;   // [B, S] or null
+  int64_t batch;
+  int seq, d_model, num_heads, head_dim;
+  int causal;
+  float scale;
+};
+
+// Flash-style causal / key-padded attention with fp32 online softmax.
+int launch_attention_ffma(const AttentionParams &p, cudaStream_t stream);
+
+}  // namespace tt

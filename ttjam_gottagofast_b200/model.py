@@ -1,0 +1,188 @@
+"""Drop-in `UserOptimizedTransformer` on the sm_100a kernels.
+
+The module mirrors the reference contract (torch_transformer_benchmark.py):
+
+* constructor `UserOptimizedTransformer(config)` with a `TransformerConfig`
+  (:149-160, :175);
+* the same submodules in the same construction order -- `layers.{i}.norm1`,
+  `layers.{i}.attention.{q,k,v,out}_proj`, `layers.{i}.norm2`,
+  `layers.{i}.ffn_in`, `layers.{i}.ffn_out`, `final_norm` (:72-75, :128-132,
+  :152-160) -- so `load_state_dict(strict=True)` / `copy_model_weights`
+  (:203-213) work unchanged and `torch.manual_seed(s)` draws identical weights;
+* `forward(x, valid_token_mask=None)` -> [B, S, d_model] (:185-199).
+
+The forward is CUDA only. It packs the parameters into a device image on first
+use (and again whenever a parameter changes: `load_state_dict`, `.to()`, or
+an in-place write seen through the tensor version counters), allocates its
+output and scratch from PyTorch's caching allocator, and enqueues the kernels
+on `torch.cuda.current_stream()` without a host sync. There is no CPU path:
+a CPU or non-fp32 input raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+
+
+class SelfAttention(nn.Module):
+    """Parameter holder with BaselineSelfAttention's names (:62-75)."""
+
+    def __init__(self, d_model: int, num_heads: int) -> None:
+        super().__init__()
+        if d_model % num_heads != 0:
+            raise ValueError("d_model must be divisible by num_heads")
+        self.d_model = d_model
+        self.num_heads = num_heads
+        self.head_dim = d_model // num_heads
+        self.scale = self.head_dim ** -0.5
+        self.q_proj = nn.Linear(d_model, d_model, bias=True)
+        self.k_proj = nn.Linear(d_model, d_model, bias=True)
+        self.v_proj = nn.Linear(d_model, d_model, bias=True)
+        self.out_proj = nn.Linear(d_model, d_model, bias=True)
+
+
+class TransformerBlock(nn.Module):
+    """Parameter holder with BaselineTransformerBlock's names (:125-132)."""
+
+    def __init__(self, d_model: int, num_heads: int, ffn_dim: int) -> None:
+        super().__init__()
+        self.norm1 = nn.LayerNorm(d_model)
+        self.attention = SelfAttention(d_model, num_heads)
+        self.norm2 = nn.LayerNorm(d_model)
+        self.ffn_in = nn.Linear(d_model, ffn_dim)
+        self.ffn_out = nn.Linear(ffn_dim, d_model)
+
+
+class UserOptimizedTransformer(nn.Module):
+    """The reference's drop-in hook (:175-200), backed by libttjam_b200.so."""
+
+    def __init__(self, config) -> None:
+        super().__init__()
+        config.validate()
+        self.config = config
+        self.layers = nn.ModuleList([
+            TransformerBlock(config.d_model, config.num_heads, config.ffn_dim)
+            for _ in range(config.num_layers)])
+        self.final_norm = nn.LayerNorm(config.d_model)
+        self._lib = _lib.load()
+        self._cfg = _lib.make_config(config)
+        _lib.check(self._lib.tt_validate_config(ctypes.byref(self._cfg)), "config")
+        self._image: Optional[torch.Tensor] = None
+        self._image_key = None
+        self._plist = None
+        self.register_load_state_dict_post_hook(
+            lambda module, incompatible: module.invalidate())
+
+    # ---- packed image -----------------------------------------------------
+    def invalidate(self) -> None:
+        """Drop the packed device image; the next forward repacks it."""
+        self._image = None
+        self._image_key = None
+
+    def _apply(self, fn, *args, **kwargs):
+        self.invalidate()
+        return super()._apply(fn, *args, **kwargs)
+
+    def _param_key(self):
+        plist = self._plist
+        if plist is None:
+            plist = self._plist = [p for p in self.parameters()]
+        return [(p.data_ptr(), p._version) for p in plist]
+
+    def _ensure_image(self, device: torch.device) -> torch.Tensor:
+        key = self._param_key()
+        if self._image is not None and key == self._image_key:
+            return self._image
+        self._plist = None
+        key = self._param_key()
+        for name, p in self.named_parameters():
+            if p.device != device or p.dtype != torch.float32 or not p.is_contiguous():
+                raise ValueError(f"parameter {name} must be a contiguous float32 tensor "
+                                 f"on {device} (got {p.dtype} on {p.device})")
+        lib, cfg = self._lib, self._cfg
+        nbytes = lib.tt_image_bytes(ctypes.byref(cfg))
+        image = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        arr = (_lib.TTLayerParams * len(self.layers))()
+        for i, blk in enumerate(self.layers):
+            a = blk.attention
+            ptrs = dict(
+                norm1_weight=blk.norm1.weight, norm1_bias=blk.norm1.bias,
+                q_weight=a.q_proj.weight, q_bias=a.q_proj.bias,
+                k_weight=a.k_proj.weight, k_bias=a.k_proj.bias,
+                v_weight=a.v_proj.weight, v_bias=a.v_proj.bias,
+                out_weight=a.out_proj.weight, out_bias=a.out_proj.bias,
+                norm2_weight=blk.norm2.weight, norm2_bias=blk.norm2.bias,
+                ffn_in_weight=blk.ffn_in.weight, ffn_in_bias=blk.ffn_in.bias,
+                ffn_out_weight=blk.ffn_out.weight, ffn_out_bias=blk.ffn_out.bias)
+            for field, t in ptrs.items():
+                setattr(arr[i], field, t.data_ptr())
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _lib.check(lib.tt_pack_image(ctypes.byref(cfg), arr, self.final_norm.weight.data_ptr(),
+                                     self.final_norm.bias.data_ptr(), image.data_ptr(),
+                                     nbytes, stream), "tt_pack_image")
+        self._image = image
+        self._image_key = key
+        return image
+
+    # ---- forward ----------------------------------------------------------
+    def forward(self, x: torch.Tensor,
+                valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if not x.is_cuda:
+            raise RuntimeError("UserOptimizedTransformer runs on CUDA only (no CPU path)")
+        if x.dtype != torch.float32:
+            raise ValueError(f"expected float32 input, got {x.dtype}")
+        if x.dim() != 3 or x.shape[-1] != self.config.d_model:
+            raise ValueError(f"expected x of shape [B, S, {self.config.d_model}], "
+                             f"got {tuple(x.shape)}")
+        if not x.is_contiguous() or x.data_ptr() % 16:
+            x = x.contiguous().clone() if x.data_ptr() % 16 else x.contiguous()
+        b, s, _ = x.shape
+        mask_ptr = None
+        if valid_token_mask is not None:
+            m = valid_token_mask
+            if m.shape != (b, s):
+                raise ValueError(f"valid_token_mask must be [B, S] = {(b, s)}, got "
+                                 f"{tuple(m.shape)}")
+            if m.device != x.device:
+                raise ValueError("valid_token_mask must be on the same device as x")
+            if m.dtype != torch.bool and m.dtype != torch.uint8:
+                raise ValueError(f"valid_token_mask must be bool, got {m.dtype}")
+            if not m.is_contiguous():
+                m = m.contiguous()
+            valid_token_mask = m
+            mask_ptr = m.data_ptr()
+        image = self._ensure_image(x.device)
+        lib, cfg = self._lib, self._cfg
+        y = torch.empty_like(x)
+        ws_bytes = lib.tt_workspace_bytes(ctypes.byref(cfg), b, s)
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        rc = lib.tt_forward(ctypes.byref(cfg), image.data_ptr(), x.data_ptr(), mask_ptr, b, s,
+                            y.data_ptr(), ws.data_ptr(), ws_bytes, stream)
+        if rc != 0:
+            _lib.check(rc, "tt_forward", lib)
+        return y
+
+    # ---- diagnostics ------------------------------------------------------
+    def forward_plan(self, batch: int, seq: int) -> str:
+        rc = self._lib.tt_forward_plan(ctypes.byref(self._cfg), batch, seq)
+        if rc < 0:
+            _lib.check(rc, "tt_forward_plan", self._lib)
+        return _lib.PLAN_NAMES[rc]
+
+    def read_device_status(self):
+        """Synchronise and return (code, detail) latched by the kernels; (0, 0)
+        when every bounded device wait finished in time."""
+        if self._image is None:
+            return 0, 0
+        code, detail = ctypes.c_int32(0), ctypes.c_int32(0)
+        stream = torch.cuda.current_stream(self._image.device).cuda_stream
+        _lib.check(self._lib.tt_read_status(ctypes.byref(self._cfg), self._image.data_ptr(),
+                                            ctypes.byref(code), ctypes.byref(detail), stream),
+                   "tt_read_status", self._lib)
+        return code.value, detail.value
