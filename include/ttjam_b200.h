@@ -51,8 +51,17 @@ typedef struct tt_config {
   int32_t ffn_dim;
   int32_t num_layers;
   int32_t causal;      /* 0 or 1 */
-  int32_t reserved[3]; /* must be 0 */
+  int32_t plan;        /* 0 = pick automatically; else force one TT_PLAN_* schedule
+                          (tests and benchmarks); an inapplicable plan is
+                          TT_ERR_UNSUPPORTED */
+  int32_t reserved[2]; /* must be 0 */
 } tt_config;
+
+/* Kernel schedules of tt_forward. */
+#define TT_PLAN_AUTO 0
+#define TT_PLAN_CLUSTER 1   /* one launch: thread-block clusters run all layers */
+#define TT_PLAN_OPS_FFMA 2  /* per-op kernels, fp32 FFMA GEMMs */
+#define TT_PLAN_OPS_TC 3    /* per-op kernels, 3xTF32 tcgen05 GEMMs */
 
 /* One BaselineTransformerBlock's parameters, nn.Linear layout W[out,in]
  * (torch_transformer_benchmark.py:125-132, :72-75). Device pointers, fp32,
@@ -107,9 +116,9 @@ int tt_forward(const tt_config *cfg, const void *image, const float *x,
                const uint8_t *mask, int64_t batch, int64_t seq, float *y,
                void *workspace, size_t workspace_bytes, void *stream);
 
-/* Which kernel schedule tt_forward picks for this call (for reports and tests):
- * 1 = single-launch cluster forward, 2 = per-op kernels with FFMA GEMMs,
- * 3 = per-op kernels with 3xTF32 tensor-core GEMMs. Negative on error. */
+/* Which kernel schedule (TT_PLAN_*) tt_forward runs for this call on the
+ * current device. Negative on error (TT_ERR_UNSUPPORTED when cfg->plan forces
+ * a schedule that cannot run this shape). */
 int tt_forward_plan(const tt_config *cfg, int64_t batch, int64_t seq);
 
 /* Number of kernel launches tt_forward makes for this call (what a profiler

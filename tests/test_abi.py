@@ -52,6 +52,12 @@ def test_validate_config_codes(lib):
     assert lib.tt_validate_config(ctypes.byref(_cfg(l=0))) == _lib.TT_ERR_INVALID_CONFIG
     assert lib.tt_validate_config(ctypes.byref(_cfg(d=1024, h=2))) == _lib.TT_ERR_UNSUPPORTED
     assert lib.tt_validate_config(None) == _lib.TT_ERR_INVALID_ARGUMENT
+    bad = _cfg()
+    bad.plan = 9
+    assert lib.tt_validate_config(ctypes.byref(bad)) == _lib.TT_ERR_INVALID_CONFIG
+    bad = _cfg()
+    bad.reserved[1] = 1
+    assert lib.tt_validate_config(ctypes.byref(bad)) == _lib.TT_ERR_INVALID_CONFIG
 
 
 def test_image_and_workspace_sizes(lib):
@@ -87,3 +93,11 @@ def test_pack_argument_errors_need_no_gpu(lib):
 def test_forward_plan(lib):
     assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(_cfg(d=512, h=8, f=2048, l=6)),
                                                16, 1024)]
+    forced = _cfg()
+    forced.plan = _lib.PLAN_IDS["ops_ffma"]
+    assert lib.tt_forward_plan(ctypes.byref(forced), 4, 16) == 2
+    assert lib.tt_forward_launch_count(ctypes.byref(forced), 4, 16) == 5 * 4 + 1
+    # the cluster schedule never applies at d_model 512
+    big = _cfg(d=512, h=8, f=2048, l=6)
+    big.plan = _lib.PLAN_IDS["cluster"]
+    assert lib.tt_forward_plan(ctypes.byref(big), 4, 16) == _lib.TT_ERR_UNSUPPORTED

@@ -47,6 +47,32 @@ def model_for(cfg, seed=1234):
     return _MODELS[key]
 
 
+def applicable_plans(model, b, s):
+    """Every kernel schedule that can run [b, s] for this model."""
+    import ctypes
+    from ttjam_gottagofast_b200 import _lib
+    out = []
+    for name in ("cluster", "ops_ffma", "ops_tc3xtf32"):
+        cfg = _lib.make_config(model.config, name)
+        if model._lib.tt_forward_plan(ctypes.byref(cfg), b, s) > 0:
+            out.append(name)
+    return out
+
+
+def run_plans(model, x, mask):
+    """{plan: output} for every applicable schedule, then back to "auto"."""
+    outs = {}
+    try:
+        for plan in applicable_plans(model, x.shape[0], x.shape[1]):
+            model.set_plan(plan)
+            with torch.inference_mode():
+                outs[plan] = model(x, mask)
+    finally:
+        model.set_plan("auto")
+    assert outs
+    return outs
+
+
 def check(ref, out, label):
     res = compare_outputs(ref, out, rtol=RTOL, atol=ATOL)
     print(f"{label}: max_abs={res.max_abs_error:.3e} max_rel={res.max_relative_error:.3e} "
@@ -60,12 +86,11 @@ def test_golden_parity(case):
     model, _ = model_for(case.config, case.meta["model_seed"])
     x = torch.from_numpy(case.x).to(DEV)
     mask = torch.from_numpy(case.mask).to(DEV) if case.uses_mask else None
-    with torch.inference_mode():
-        y = model(x, mask)
-    torch.cuda.synchronize()
-    check(torch.from_numpy(case.y), y.cpu(), case.name)
-    if mask is not None:
-        assert (y[~mask] == 0).all(), "padded rows must be exactly zero"
+    for plan, y in run_plans(model, x, mask).items():
+        torch.cuda.synchronize()
+        check(torch.from_numpy(case.y), y.cpu(), f"{case.name}[{plan}]")
+        if mask is not None:
+            assert (y[~mask] == 0).all(), "padded rows must be exactly zero"
     assert model.read_device_status() == (0, 0)
 
 
@@ -83,6 +108,17 @@ def _full_size_case(name, variant):
     return cfg, params, x, mask, y
 
 
+def test_small_shapes_run_in_one_launch():
+    """The launch-bound workloads take the single-launch cluster schedule."""
+    import ctypes
+    for name in ("B1", "B2"):
+        cfg = WORKLOADS[name].config
+        model, _ = model_for(cfg)
+        assert model.forward_plan(cfg.batch_size, cfg.seq_len) == "cluster"
+        assert model._lib.tt_forward_launch_count(ctypes.byref(model._cfg), cfg.batch_size,
+                                                  cfg.seq_len) == 1
+
+
 SMALL_WORKLOAD_CASES = [(n, v) for n in ("A", "B1", "B2", "C")
                         for v in [{"name": "own"}] + HARNESS_VARIANTS]
 
@@ -92,7 +128,9 @@ SMALL_WORKLOAD_CASES = [(n, v) for n in ("A", "B1", "B2", "C")
 def test_workload_parity_full_size(name, variant):
     cfg, params, x, mask, y = _full_size_case(name, variant)
     ref = oracle.forward(params, cfg, x, mask, batch_chunk=8)
-    check(ref, y, f"{name}/{variant['name']}")
+    model, _ = model_for(cfg)
+    for plan, out in run_plans(model, x, mask).items():
+        check(ref, out, f"{name}/{variant['name']}[{plan}]")
 
 
 @pytest.mark.parametrize("variant", [{"name": "own"}, HARNESS_VARIANTS[1], HARNESS_VARIANTS[4]],

@@ -23,6 +23,7 @@ TT_ERR_DEVICE_TIMEOUT = -6
 TT_ERR_DEVICE_FAULT = -7
 
 PLAN_NAMES = {1: "cluster", 2: "ops_ffma", 3: "ops_tc3xtf32"}
+PLAN_IDS = {"auto": 0, **{v: k for k, v in PLAN_NAMES.items()}}
 
 # Every entry point include/ttjam_b200.h declares.
 EXPORTED = (
@@ -36,7 +37,8 @@ EXPORTED = (
 class TTConfig(ctypes.Structure):
     _fields_ = [("d_model", ctypes.c_int32), ("num_heads", ctypes.c_int32),
                 ("ffn_dim", ctypes.c_int32), ("num_layers", ctypes.c_int32),
-                ("causal", ctypes.c_int32), ("reserved", ctypes.c_int32 * 3)]
+                ("causal", ctypes.c_int32), ("plan", ctypes.c_int32),
+                ("reserved", ctypes.c_int32 * 2)]
 
 
 class TTLayerParams(ctypes.Structure):
@@ -115,9 +117,10 @@ def check(rc: int, what: str, lib=None) -> None:
     raise RuntimeError(msg)
 
 
-def make_config(cfg) -> TTConfig:
+def make_config(cfg, plan: str = "auto") -> TTConfig:
     """A tt_config from any object with TransformerConfig's fields."""
     c = TTConfig()
+    c.plan = PLAN_IDS[plan]
     c.d_model = int(cfg.d_model)
     c.num_heads = int(cfg.num_heads)
     c.ffn_dim = int(cfg.ffn_dim)

@@ -3,6 +3,7 @@
 #include <cstring>
 #include <string>
 
+#include "cluster_forward.cuh"
 #include "image.cuh"
 #include "tt_common.cuh"
 
@@ -51,7 +52,9 @@ int validate_config(const tt_config *cfg) {
   if (cfg->num_layers <= 0) return fail(TT_ERR_INVALID_CONFIG, "num_layers must be positive");
   if (cfg->causal != 0 && cfg->causal != 1)
     return fail(TT_ERR_INVALID_CONFIG, "causal must be 0 or 1");
-  for (int i = 0; i < 3; ++i)
+  if (cfg->plan < TT_PLAN_AUTO || cfg->plan > TT_PLAN_OPS_TC)
+    return fail(TT_ERR_INVALID_CONFIG, "plan must be one of TT_PLAN_*");
+  for (int i = 0; i < 2; ++i)
     if (cfg->reserved[i] != 0) return fail(TT_ERR_INVALID_CONFIG, "reserved fields must be 0");
   if (cfg->d_model / cfg->num_heads > 256)
     return fail(TT_ERR_UNSUPPORTED, "head_dim > 256 is not supported by this build");
@@ -61,9 +64,43 @@ int validate_config(const tt_config *cfg) {
 }
 
 int forward_plan(const tt_config *cfg, int64_t batch, int64_t seq) {
-  (void)batch;
-  (void)seq;
-  return uses_tensor_cores(*cfg) ? PLAN_OPS_TC : PLAN_OPS_FFMA;
+  const int ops = uses_tensor_cores(*cfg) ? PLAN_OPS_TC : PLAN_OPS_FFMA;
+  switch (cfg->plan) {
+    case TT_PLAN_AUTO:
+      return choose_cluster(*cfg, batch, seq).cluster > 0 ? PLAN_CLUSTER : ops;
+    case TT_PLAN_CLUSTER:
+      if (choose_cluster(*cfg, batch, seq).cluster > 0) return PLAN_CLUSTER;
+      return fail(TT_ERR_UNSUPPORTED, "cluster schedule needs d_model = ffn_dim = 128, "
+                                      "num_heads in {1,2,4,8,16} and a short sequence");
+    case TT_PLAN_OPS_FFMA:
+      return PLAN_OPS_FFMA;
+    default:
+      if (ops == PLAN_OPS_TC) return PLAN_OPS_TC;
+      return fail(TT_ERR_UNSUPPORTED, "tensor-core schedule is not available for this shape");
+  }
+}
+
+int forward_cluster(const tt_config &cfg, const ClusterChoice &cc, const ImageLayout &L,
+                    const char *image, const float *x, const uint8_t *mask, int64_t batch,
+                    int64_t seq, float *y, cudaStream_t stream) {
+  ClusterArgs a{};
+  a.image = image;
+  a.layer_stride = L.layer.size() > 1 ? L.layer[1].ln1_w - L.layer[0].ln1_w : 0;
+  a.off = L.layer[0];
+  a.final_w = reinterpret_cast<const float *>(image + L.final_w);
+  a.final_b = reinterpret_cast<const float *>(image + L.final_b);
+  a.x = x;
+  a.mask = mask;
+  a.y = y;
+  a.status = reinterpret_cast<DeviceStatus *>(const_cast<char *>(image) + L.status);
+  a.seq = (int)seq;
+  a.nseq = (int)batch;
+  a.seq_per_cluster = cc.seq_per_cluster;
+  a.num_layers = cfg.num_layers;
+  a.causal = cfg.causal;
+  a.scale = (float)(1.0 / std::sqrt((double)(cfg.d_model / cfg.num_heads)));
+  a.eps = 1e-5f;
+  return launch_cluster_forward(cc, a, cfg.num_heads, stream);
 }
 
 int forward_ops(const tt_config &cfg, const ImageLayout &L, const char *image, const float *x,
@@ -183,6 +220,8 @@ int tt_pack_image(const tt_config *cfg, const tt_layer_params *layers,
 
 size_t tt_workspace_bytes(const tt_config *cfg, int64_t batch, int64_t seq) {
   if (validate_config(cfg) != TT_OK || batch < 0 || seq < 0) return 0;
+  const int plan = forward_plan(cfg, batch, seq);
+  if (plan < 0 || plan == PLAN_CLUSTER) return 0;
   return WorkspaceLayout(*cfg, batch, seq).total;
 }
 
@@ -196,6 +235,9 @@ int tt_forward_launch_count(const tt_config *cfg, int64_t batch, int64_t seq) {
   const int rc = validate_config(cfg);
   if (rc != TT_OK) return rc;
   if (batch <= 0 || seq <= 0) return 0;
+  const int plan = forward_plan(cfg, batch, seq);
+  if (plan < 0) return plan;
+  if (plan == PLAN_CLUSTER) return 1;
   return 5 * cfg->num_layers + 1;
 }
 
@@ -214,11 +256,16 @@ int tt_forward(const tt_config *cfg, const void *image, const float *x, const ui
   if (seq > (int64_t)INT32_MAX || batch * seq > ((int64_t)1 << 40))
     return fail(TT_ERR_UNSUPPORTED, "tt_forward: batch*seq too large");
   const ImageLayout L(*cfg);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const int plan = forward_plan(cfg, batch, seq);
+  if (plan < 0) return plan;
+  if (plan == PLAN_CLUSTER)
+    return forward_cluster(*cfg, choose_cluster(*cfg, batch, seq), L,
+                           static_cast<const char *>(image), x, mask, batch, seq, y, stream);
   const WorkspaceLayout W(*cfg, batch, seq);
   if (workspace_bytes < W.total || (W.total > 0 && workspace == nullptr))
     return fail(TT_ERR_WORKSPACE, "tt_forward: workspace smaller than tt_workspace_bytes (" +
                                       std::to_string(W.total) + " bytes)");
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   return forward_ops(*cfg, L, static_cast<const char *>(image), x, mask, batch, seq, y, W,
                      static_cast<char *>(workspace), stream);
 }

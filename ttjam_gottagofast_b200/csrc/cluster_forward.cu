@@ -1,0 +1,572 @@
+// Whole forward pass in ONE kernel launch for short sequences at d_model = 128,
+// ffn_dim = 128 (the launch-bound shapes).
+//
+// Schedule. Each thread-block cluster (CL = 8 or 16 CTAs) owns a group of whole
+// sequences (R <= RMAX token rows) and runs all L layers and the final
+// LayerNorm for them; clusters never wait on each other, so there is no
+// grid-wide barrier and clusters need not be co-resident. Inside a cluster:
+//   * weights are column-partitioned: CTA r owns 128/CL output columns of each
+//     of q, k, v, out_proj, ffn_in and ffn_out. Its slice of a layer (48 rows
+//     of 128 floats at CL = 16) is streamed global -> shared with bulk async
+//     copies completing on an mbarrier, double-buffered so layer l+1 loads
+//     while layer l computes;
+//   * activations are replicated: every CTA holds the full residual stream
+//     X[R,128] in shared memory and computes LayerNorms locally; each projection
+//     writes its columns into every CTA's copy through distributed shared
+//     memory (st.shared::cluster), followed by one cluster barrier;
+//   * attention: CTA r serves head r / (CL/H) for every (CL/H)-th query row,
+//     one warp per query row, from the q/k/v head slices its head group wrote.
+// Per layer: 5 cluster barriers (after q/k/v, context, out_proj, ffn_in,
+// ffn_out). Padded rows are zeroed exactly where the reference zeroes them.
+//
+// Semantics follow BaselineTransformer.forward (torch_transformer_benchmark.py:
+// 59-172): pre-norm block :140-144, attention :93-121, final norm :169-171.
+// Every wait on an mbarrier is bounded; a wait that gives up latches
+// TT_ERR_DEVICE_TIMEOUT in the status word and the kernel still reaches every
+// cluster barrier, so no CTA is left waiting.
+#include <math_constants.h>
+
+#include "cluster_forward.cuh"
+
+namespace tt {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kD = 128;
+constexpr int kF = 128;
+constexpr int kST = kD + 4;  // padded smem row stride (floats): conflict-free float4 rows
+
+// Shared-memory floats of one CTA for cluster size CL, H heads, R rows.
+constexpr int cluster_smem_floats(int CL, int H, int R) {
+  return 2 * 6 * (kD / CL) * kST + 3 * R * kST + 3 * R * (kD / H + 1) + R + 8;
+}
+// Largest row count per cluster (a multiple of 16, at most 64) that fits the
+// 227 KB of shared memory a CTA may use.
+constexpr int cluster_rmax(int CL, int H) {
+  int r = 64;
+  while (r > 16 && cluster_smem_floats(CL, H, r) * 4 > 227 * 1024) r -= 16;
+  return r;
+}
+
+template <int CL, int H>
+struct CS {
+  static constexpr int RMAX = cluster_rmax(CL, H);
+  static constexpr int HD = kD / H;          // head dim
+  static constexpr int G = CL / H;           // CTAs per head
+  static constexpr int NC = kD / CL;         // columns per CTA per projection
+  static constexpr int WR = 6 * NC;          // weight rows per CTA per layer (q,k,v,o,ffn_in,ffn_out)
+  static constexpr int HDP = HD + 1;         // padded head row stride
+  static constexpr int OFF_W = 0;                          // [2][WR][kST]
+  static constexpr int OFF_X = OFF_W + 2 * WR * kST;       // [RMAX][kST] residual stream
+  static constexpr int OFF_N = OFF_X + RMAX * kST;         // [RMAX][kST] LayerNorm output
+  static constexpr int OFF_CB = OFF_N + RMAX * kST;        // [RMAX][kST] context / ffn hidden
+  static constexpr int OFF_Q = OFF_CB + RMAX * kST;        // [RMAX][HDP]
+  static constexpr int OFF_K = OFF_Q + RMAX * HDP;
+  static constexpr int OFF_V = OFF_K + RMAX * HDP;
+  static constexpr int OFF_VALID = OFF_V + RMAX * HDP;     // [RMAX]
+  static constexpr int OFF_BAR = (OFF_VALID + RMAX + 3) / 4 * 4;  // 2 mbarriers (16 B)
+  static constexpr int FLOATS = OFF_BAR + 4;
+  static_assert(FLOATS <= cluster_smem_floats(CL, H, RMAX), "layout");
+  static constexpr size_t BYTES = (size_t)FLOATS * sizeof(float);
+  static_assert(H <= CL && CL % H == 0, "heads must divide the cluster");
+  static_assert(HD % G == 0, "head split");
+  static_assert(BYTES <= 227 * 1024, "shared memory budget");
+};
+
+// ---- PTX helpers -----------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint32_t cluster_map(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster4(uint32_t addr, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x),
+               "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes,
+                                         uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Bounded wait for the weight slice of one layer. Gives up after ~2^31 cycles
+// (about a second) and latches a timeout; the caller carries on so that every
+// CTA still reaches every cluster barrier.
+__device__ __forceinline__ void wait_weights(uint32_t bar, uint32_t parity, DeviceStatus *st,
+                                             int layer) {
+  if (mbar_try_wait(bar, parity)) return;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > (1LL << 31)) {
+      raise_status(st, TT_ERR_DEVICE_TIMEOUT, 0x100 + layer);
+      return;
+    }
+  }
+}
+
+// Issue the bulk copies of one layer's weight slice (6 blocks of NC rows, one
+// copy per row so rows land at the padded stride). Called by one warp.
+template <int CL, int H>
+__device__ void load_layer_weights(const ClusterArgs &a, int layer, float *wbuf, uint32_t bar,
+                                   int rank, int lane) {
+  using C = CS<CL, H>;
+  const char *base = a.image + (size_t)layer * a.layer_stride;
+  const float *wqkv = reinterpret_cast<const float *>(base + a.off.wqkv);
+  const float *wo = reinterpret_cast<const float *>(base + a.off.wo);
+  const float *w1 = reinterpret_cast<const float *>(base + a.off.w1);
+  const float *w2 = reinterpret_cast<const float *>(base + a.off.w2);
+  const int h = rank / C::G, sub = rank % C::G;
+  const int qcol = h * C::HD + sub * (C::HD / C::G);  // first q/k/v column of this CTA
+  if (lane == 0) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_expect_tx(bar, (uint32_t)(C::WR * kD * sizeof(float)));
+  }
+  __syncwarp();
+  for (int r = lane; r < C::WR; r += 32) {
+    const int blk = r / C::NC, i = r % C::NC;
+    const float *src;
+    if (blk < 3) src = wqkv + (size_t)(blk * kD + qcol + i) * kD;      // q, k, v rows
+    else if (blk == 3) src = wo + (size_t)(rank * C::NC + i) * kD;     // out_proj rows
+    else if (blk == 4) src = w1 + (size_t)(rank * C::NC + i) * kD;     // ffn_in rows
+    else src = w2 + (size_t)(rank * C::NC + i) * kF;                   // ffn_out rows
+    bulk_g2s(smem_u32(wbuf + r * kST), src, kD * sizeof(float), bar);
+  }
+}
+
+// Row LayerNorm of R rows of `src` (stride kST) into `dst`, one warp per row.
+__device__ void ln_rows(const float *src, float *dst, int R, const float *gamma,
+                        const float *beta, float eps, int warp, int lane) {
+  const float4 g = reinterpret_cast<const float4 *>(gamma)[lane];
+  const float4 b = reinterpret_cast<const float4 *>(beta)[lane];
+  for (int r = warp; r < R; r += kThreads / 32) {
+    const float4 v = reinterpret_cast<const float4 *>(src + r * kST)[lane];
+    const float mean = warp_sum((v.x + v.y) + (v.z + v.w)) * (1.0f / kD);
+    const float a0 = v.x - mean, a1 = v.y - mean, a2 = v.z - mean, a3 = v.w - mean;
+    const float rstd = rsqrtf(warp_sum((a0 * a0 + a1 * a1) + (a2 * a2 + a3 * a3)) * (1.0f / kD) + eps);
+    float4 o;
+    o.x = a0 * rstd * g.x + b.x;
+    o.y = a1 * rstd * g.y + b.y;
+    o.z = a2 * rstd * g.z + b.z;
+    o.w = a3 * rstd * g.w + b.w;
+    reinterpret_cast<float4 *>(dst + r * kST)[lane] = o;
+  }
+}
+
+// out[r][c] = sum_k A[r][k] * W[c][k] for r < R, c < NCOL, K = 128, both
+// operands in shared memory at stride kST. Work split: 2x4 output micro-tiles,
+// each shared by KS consecutive lanes that split K and reduce by shuffles.
+// epi(r, c, acc) runs on the lane with kq == 0.
+template <int NCOL, typename Epi>
+__device__ __forceinline__ void smem_gemm(const float *A, const float *W, int R, Epi epi) {
+  constexpr int TI = 2, TJ = 4;
+  static_assert(NCOL % TJ == 0, "columns");
+  constexpr int CT = NCOL / TJ;
+  const int tiles = ((R + TI - 1) / TI) * CT;
+  int ks = 1;
+  while (ks < 16 && tiles * ks * 2 <= kThreads) ks <<= 1;
+  const int tid = threadIdx.x;
+  const int kq = tid % ks;
+  // every thread runs the same number of iterations (shuffles below need the
+  // whole warp); lanes past the last tile compute on tile 0 and store nothing
+  for (int base = 0; base < tiles; base += kThreads / ks) {
+    const int t_raw = base + tid / ks;
+    const bool active = t_raw < tiles;
+    const int t = active ? t_raw : 0;
+    const int r0 = (t / CT) * TI, c0 = (t % CT) * TJ;
+    const int r1 = min(r0 + 1, R - 1);
+    float acc[TI][TJ] = {};
+    const float *a0p = A + r0 * kST, *a1p = A + r1 * kST;
+    for (int k = kq * 4; k < kD; k += ks * 4) {
+      const float4 a0 = *reinterpret_cast<const float4 *>(a0p + k);
+      const float4 a1 = *reinterpret_cast<const float4 *>(a1p + k);
+#pragma unroll
+      for (int j = 0; j < TJ; ++j) {
+        const float4 w = *reinterpret_cast<const float4 *>(W + (c0 + j) * kST + k);
+        acc[0][j] = fmaf(a0.x, w.x, acc[0][j]);
+        acc[0][j] = fmaf(a0.y, w.y, acc[0][j]);
+        acc[0][j] = fmaf(a0.z, w.z, acc[0][j]);
+        acc[0][j] = fmaf(a0.w, w.w, acc[0][j]);
+        acc[1][j] = fmaf(a1.x, w.x, acc[1][j]);
+        acc[1][j] = fmaf(a1.y, w.y, acc[1][j]);
+        acc[1][j] = fmaf(a1.z, w.z, acc[1][j]);
+        acc[1][j] = fmaf(a1.w, w.w, acc[1][j]);
+      }
+    }
+    // reduce the K split across the ks consecutive lanes of this tile
+    for (int off = 1; off < ks; off <<= 1) {
+#pragma unroll
+      for (int i = 0; i < TI; ++i)
+#pragma unroll
+        for (int j = 0; j < TJ; ++j) acc[i][j] += __shfl_xor_sync(0xffffffffu, acc[i][j], off);
+    }
+    if (active && kq == 0) {
+#pragma unroll
+      for (int i = 0; i < TI; ++i) {
+        if (r0 + i >= R) break;
+#pragma unroll
+        for (int j = 0; j < TJ; ++j) epi(r0 + i, c0 + j, acc[i][j]);
+      }
+    }
+  }
+}
+
+template <int CL, int H>
+__global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const ClusterArgs a) {
+  using C = CS<CL, H>;
+  extern __shared__ __align__(128) float sm[];
+  float *sW = sm + C::OFF_W;
+  float *sX = sm + C::OFF_X;
+  float *sN = sm + C::OFF_N;
+  float *sCB = sm + C::OFF_CB;
+  float *sQ = sm + C::OFF_Q;
+  float *sK = sm + C::OFF_K;
+  float *sV = sm + C::OFF_V;
+  float *sValid = sm + C::OFF_VALID;
+  const uint32_t bar0 = smem_u32(sm + C::OFF_BAR);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int rank = blockIdx.x % CL;
+  const int cid = blockIdx.x / CL;
+  const int S = a.seq;
+  const int seq0 = cid * a.seq_per_cluster;
+  const int nsq = min(a.seq_per_cluster, a.nseq - seq0);
+  const int R = nsq * S;               // token rows owned by this cluster (<= RMAX)
+  const int64_t row0 = (int64_t)seq0 * S;
+  const int h = rank / C::G, sub = rank % C::G;
+
+  if (tid == 0) {
+    mbar_init(bar0, 1);
+    mbar_init(bar0 + 8, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (warp == 0) {
+    load_layer_weights<CL, H>(a, 0, sW, bar0, rank, lane);
+    if (a.num_layers > 1)
+      load_layer_weights<CL, H>(a, 1, sW + C::WR * kST, bar0 + 8, rank, lane);
+  }
+  // residual stream and row validity for this cluster's sequences
+  for (int i = tid; i < R * (kD / 4); i += kThreads) {
+    const int r = i / (kD / 4), c4 = i % (kD / 4);
+    reinterpret_cast<float4 *>(sX + r * kST)[c4] =
+        reinterpret_cast<const float4 *>(a.x + (row0 + r) * kD)[c4];
+  }
+  for (int r = tid; r < R; r += kThreads)
+    sValid[r] = (a.mask == nullptr || a.mask[row0 + r] != 0) ? 1.f : 0.f;
+  cluster_sync();  // every CTA of the cluster is running before any remote store
+
+  const uint32_t xs_l = smem_u32(sX), cb_l = smem_u32(sCB);
+  const uint32_t q_l = smem_u32(sQ), k_l = smem_u32(sK), v_l = smem_u32(sV);
+  constexpr int NC = C::NC;
+
+  for (int l = 0; l < a.num_layers; ++l) {
+    const char *lb = a.image + (size_t)l * a.layer_stride;
+    auto P = [&](size_t off) { return reinterpret_cast<const float *>(lb + off); };
+    float *wb = sW + (l & 1) * C::WR * kST;
+    const uint32_t bar = bar0 + 8 * (l & 1);
+    if (l >= 1 && l + 1 < a.num_layers && warp == 0)
+      load_layer_weights<CL, H>(a, l + 1, sW + ((l + 1) & 1) * C::WR * kST,
+                                      bar0 + 8 * ((l + 1) & 1), rank, lane);
+
+    // ---- LayerNorm1 (local, all rows) and this CTA's q/k/v columns --------
+    ln_rows(sX, sN, R, P(a.off.ln1_w), P(a.off.ln1_b), a.eps, warp, lane);
+    __syncthreads();
+    wait_weights(bar, (l >> 1) & 1, a.status, l);
+    {
+      const float *bqkv = P(a.off.bqkv);
+      const int qcol = h * C::HD + sub * (C::HD / C::G);
+      smem_gemm<3 * NC>(sN, wb, R, [&](int r, int c, float acc) {
+        const int blk = c / NC, i = c % NC;       // 0 = q, 1 = k, 2 = v
+        const float v = acc + bqkv[blk * kD + qcol + i];
+        const uint32_t base = blk == 0 ? q_l : (blk == 1 ? k_l : v_l);
+        const uint32_t off = (uint32_t)((r * C::HDP + sub * (C::HD / C::G) + i) * 4);
+#pragma unroll
+        for (int g = 0; g < C::G; ++g) st_cluster(cluster_map(base + off, h * C::G + g), v);
+      });
+    }
+    cluster_sync();
+
+    // ---- attention: warp per query row, head h, rows r = sub (mod G) -------
+    for (int r = sub + C::G * warp; r < R; r += C::G * (kThreads / 32)) {
+      if (sValid[r] == 0.f) continue;  // padded query: its output row is zeroed later
+      const int sq = r / S, i = r % S;
+      const int kbase = sq * S;
+      const int kend = a.causal ? i + 1 : S;
+      const float *qr = sQ + r * C::HDP;
+      float m = -CUDART_INF_F, lsum = 0.f;
+      float o[(C::HD + 31) / 32];
+#pragma unroll
+      for (int t = 0; t < (C::HD + 31) / 32; ++t) o[t] = 0.f;
+      for (int jb = 0; jb < kend; jb += 32) {
+        const int j = jb + lane;
+        float s = -CUDART_INF_F;
+        if (j < kend && sValid[kbase + j] != 0.f) {
+          const float *kr = sK + (kbase + j) * C::HDP;
+          float dot = 0.f;
+#pragma unroll 8
+          for (int d = 0; d < C::HD; ++d) dot = fmaf(qr[d], kr[d], dot);
+          s = dot * a.scale;
+        }
+        const float mn = fmaxf(m, warp_max(s));
+        if (mn == -CUDART_INF_F) continue;  // no allowed key yet (uniform across the warp)
+        const float alpha = __expf(m - mn);
+        const float p = __expf(s - mn);
+        lsum = lsum * alpha + warp_sum(p);
+#pragma unroll
+        for (int t = 0; t < (C::HD + 31) / 32; ++t) o[t] *= alpha;
+        const int nj = min(32, kend - jb);
+        for (int jj = 0; jj < nj; ++jj) {
+          const float pj = __shfl_sync(0xffffffffu, p, jj);
+          const float *vr = sV + (kbase + jb + jj) * C::HDP;
+#pragma unroll
+          for (int t = 0; t < (C::HD + 31) / 32; ++t) {
+            const int d = lane + 32 * t;
+            if (d < C::HD) o[t] = fmaf(pj, vr[d], o[t]);
+          }
+        }
+        m = mn;
+      }
+      const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+#pragma unroll
+      for (int t = 0; t < (C::HD + 31) / 32; ++t) {
+        const int d = lane + 32 * t;
+        if (d < C::HD) {
+          const uint32_t off = (uint32_t)((r * kST + h * C::HD + d) * 4);
+          const float v = o[t] * inv;
+          for (int g = 0; g < CL; ++g) st_cluster(cluster_map(cb_l + off, g), v);
+        }
+      }
+    }
+    cluster_sync();
+
+    // ---- out_proj + padded-row zeroing + residual: X[:, own cols] ---------
+    {
+      const float *bo = P(a.off.bo);
+      smem_gemm<NC>(sCB, wb + 3 * NC * kST, R, [&](int r, int c, float acc) {
+        const int col = rank * NC + c;
+        const float v = sValid[r] != 0.f ? sX[r * kST + col] + (acc + bo[col]) : 0.f;
+        const uint32_t off = (uint32_t)((r * kST + col) * 4);
+        for (int g = 0; g < CL; ++g) st_cluster(cluster_map(xs_l + off, g), v);
+      });
+    }
+    cluster_sync();
+
+    // ---- LayerNorm2 (local) and ffn_in + exact GELU: CB[:, own cols] -------
+    ln_rows(sX, sN, R, P(a.off.ln2_w), P(a.off.ln2_b), a.eps, warp, lane);
+    __syncthreads();
+    {
+      const float *b1 = P(a.off.b1);
+      smem_gemm<NC>(sN, wb + 4 * NC * kST, R, [&](int r, int c, float acc) {
+        const int col = rank * NC + c;
+        const float v = gelu_erf(acc + b1[col]);
+        const uint32_t off = (uint32_t)((r * kST + col) * 4);
+        for (int g = 0; g < CL; ++g) st_cluster(cluster_map(cb_l + off, g), v);
+      });
+    }
+    cluster_sync();
+
+    // ---- ffn_out + residual + block-end padded-row zeroing -----------------
+    {
+      const float *b2 = P(a.off.b2);
+      smem_gemm<NC>(sCB, wb + 5 * NC * kST, R, [&](int r, int c, float acc) {
+        const int col = rank * NC + c;
+        const float v = sValid[r] != 0.f ? sX[r * kST + col] + (acc + b2[col]) : 0.f;
+        const uint32_t off = (uint32_t)((r * kST + col) * 4);
+        for (int g = 0; g < CL; ++g) st_cluster(cluster_map(xs_l + off, g), v);
+      });
+    }
+    cluster_sync();
+  }
+
+  // ---- final LayerNorm of this CTA's share of rows, padded rows -> 0 --------
+  {
+    const float4 g = reinterpret_cast<const float4 *>(a.final_w)[lane];
+    const float4 b = reinterpret_cast<const float4 *>(a.final_b)[lane];
+    for (int r = rank + CL * warp; r < R; r += CL * (kThreads / 32)) {
+      const float4 v = reinterpret_cast<const float4 *>(sX + r * kST)[lane];
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (sValid[r] != 0.f) {
+        const float mean = warp_sum((v.x + v.y) + (v.z + v.w)) * (1.0f / kD);
+        const float a0 = v.x - mean, a1 = v.y - mean, a2 = v.z - mean, a3 = v.w - mean;
+        const float rstd =
+            rsqrtf(warp_sum((a0 * a0 + a1 * a1) + (a2 * a2 + a3 * a3)) * (1.0f / kD) + a.eps);
+        o.x = a0 * rstd * g.x + b.x;
+        o.y = a1 * rstd * g.y + b.y;
+        o.z = a2 * rstd * g.z + b.z;
+        o.w = a3 * rstd * g.w + b.w;
+      }
+      reinterpret_cast<float4 *>(a.y + (row0 + r) * kD)[lane] = o;
+    }
+  }
+}
+
+template <int CL, int H>
+int launch_cl(const ClusterArgs &a, int nclusters, cudaStream_t stream) {
+  using C = CS<CL, H>;
+  auto fn = cluster_forward_kernel<CL, H>;
+  TT_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::BYTES));
+  if (CL > 8) TT_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(nclusters * CL));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CL;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  TT_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, a));
+  return TT_OK;
+}
+
+template <int CL, int H>
+int max_clusters_cl() {
+  using C = CS<CL, H>;
+  auto fn = cluster_forward_kernel<CL, H>;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::BYTES) != cudaSuccess)
+    return 0;
+  if (CL > 8 &&
+      cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+    return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(CL);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::BYTES;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CL;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+template <int CL>
+int dispatch_h(int heads, const ClusterArgs *a, int nclusters, cudaStream_t stream,
+               int *max_clusters) {
+#define TT_CL_CASE(HH)                                                           \
+  if (heads == HH) {                                                             \
+    if (max_clusters) *max_clusters = max_clusters_cl<CL, HH>();           \
+    return a ? launch_cl<CL, HH>(*a, nclusters, stream) : TT_OK;           \
+  }
+  TT_CL_CASE(1)
+  TT_CL_CASE(2)
+  TT_CL_CASE(4)
+  TT_CL_CASE(8)
+  if constexpr (CL >= 16) { TT_CL_CASE(16) }
+#undef TT_CL_CASE
+  return fail(TT_ERR_UNSUPPORTED, "cluster forward: unsupported head count");
+}
+
+}  // namespace
+
+ClusterChoice choose_cluster(const tt_config &cfg, int64_t batch, int64_t seq) {
+  ClusterChoice c{};
+  if (cfg.d_model != kD || cfg.ffn_dim != kF || batch <= 0 || seq <= 0) return c;
+  const int H = cfg.num_heads;
+  if (H != 1 && H != 2 && H != 4 && H != 8 && H != 16) return c;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return c;
+  }
+  // per-device cache of the co-residency query: [device][cluster size 8/16][head idx]
+  static int cache[16][2][5];
+  static bool init[16][2][5];
+  const int hidx = H == 1 ? 0 : H == 2 ? 1 : H == 4 ? 2 : H == 8 ? 3 : 4;
+  auto query = [&](int which) {
+    if (dev >= 16) return 0;
+    if (!init[dev][which][hidx]) {
+      int n = 0;
+      if (which == 1) dispatch_h<16>(H, nullptr, 0, nullptr, &n);
+      else if (H <= 8) dispatch_h<8>(H, nullptr, 0, nullptr, &n);
+      cache[dev][which][hidx] = n;
+      init[dev][which][hidx] = true;
+    }
+    return cache[dev][which][hidx];
+  };
+  int cl = 0, rmax = 0, maxc = 0;
+  if (seq <= cluster_rmax(16, H) && (maxc = query(1)) > 0) {
+    cl = 16; rmax = cluster_rmax(16, H);
+  } else if (H <= 8 && seq <= cluster_rmax(8, H) && (maxc = query(0)) > 0) {
+    cl = 8; rmax = cluster_rmax(8, H);
+  } else {
+    return c;
+  }
+  // spread sequences over as many clusters as can run at once, never more
+  // rows per cluster than fit in shared memory
+  int64_t ncl = std::min<int64_t>(batch, (int64_t)maxc);
+  int64_t spc = (batch + ncl - 1) / ncl;
+  spc = std::min<int64_t>(spc, rmax / seq);
+  ncl = (batch + spc - 1) / spc;
+  if (ncl * cl > INT32_MAX / 2) return c;
+  c.cluster = cl;
+  c.rmax = rmax;
+  c.seq_per_cluster = (int)spc;
+  c.nclusters = (int)ncl;
+  return c;
+}
+
+int launch_cluster_forward(const ClusterChoice &c, const ClusterArgs &a, int heads,
+                           cudaStream_t stream) {
+  int rc;
+  if (c.cluster == 16) rc = dispatch_h<16>(heads, &a, c.nclusters, stream, nullptr);
+  else rc = dispatch_h<8>(heads, &a, c.nclusters, stream, nullptr);
+  if (rc != TT_OK) return rc;
+  TT_LAUNCH_CHECK("cluster_forward");
+  return TT_OK;
+}
+
+}  // namespace tt

@@ -79,6 +79,13 @@ class UserOptimizedTransformer(nn.Module):
             lambda module, incompatible: module.invalidate())
 
     # ---- packed image -----------------------------------------------------
+    def set_plan(self, plan: str = "auto") -> None:
+        """Force a kernel schedule ("auto", "cluster", "ops_ffma", "ops_tc3xtf32")
+        for tests and measurements; "auto" picks the fastest applicable one."""
+        cfg = _lib.make_config(self.config, plan)
+        _lib.check(self._lib.tt_validate_config(ctypes.byref(cfg)), "plan")
+        self._cfg = cfg
+
     def invalidate(self) -> None:
         """Drop the packed device image; the next forward repacks it."""
         self._image = None
