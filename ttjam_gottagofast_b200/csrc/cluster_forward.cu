@@ -36,9 +36,14 @@ constexpr int kD = 128;
 constexpr int kF = 128;
 constexpr int kST = kD + 4;  // padded smem row stride (floats): conflict-free float4 rows
 
+// Per-layer parameters that ride with the weight slice: ln1 w|b, ln2 w|b (128
+// each) and this CTA's NC-wide slices of bq, bk, bv, bo, b1, b2.
+constexpr int aux_floats(int CL) { return 4 * kD + 6 * (kD / CL); }
+// Floats of one weight buffer: 6*NC rows at stride kST, then the aux block.
+constexpr int wbuf_floats(int CL) { return 6 * (kD / CL) * kST + aux_floats(CL); }
 // Shared-memory floats of one CTA for cluster size CL, H heads, R rows.
 constexpr int cluster_smem_floats(int CL, int H, int R) {
-  return 2 * 6 * (kD / CL) * kST + 3 * R * kST + 3 * R * (kD / H + 1) + R + 8;
+  return 2 * wbuf_floats(CL) + 3 * R * kST + 3 * R * (kD / H + 4) + R + 8;
 }
 // Largest row count per cluster (a multiple of 16, at most 64) that fits the
 // 227 KB of shared memory a CTA may use.
@@ -55,9 +60,11 @@ struct CS {
   static constexpr int G = CL / H;           // CTAs per head
   static constexpr int NC = kD / CL;         // columns per CTA per projection
   static constexpr int WR = 6 * NC;          // weight rows per CTA per layer (q,k,v,o,ffn_in,ffn_out)
-  static constexpr int HDP = HD + 1;         // padded head row stride
-  static constexpr int OFF_W = 0;                          // [2][WR][kST]
-  static constexpr int OFF_X = OFF_W + 2 * WR * kST;       // [RMAX][kST] residual stream
+  static constexpr int WB = wbuf_floats(CL); // floats per weight buffer
+  static constexpr int AUX = WR * kST;       // offset of the aux block inside a buffer
+  static constexpr int HDP = HD + 4;         // head row stride: 16-byte rows, float4 reads conflict-free
+  static constexpr int OFF_W = 0;                          // [2][WB]
+  static constexpr int OFF_X = OFF_W + 2 * WB;             // [RMAX][kST] residual stream
   static constexpr int OFF_N = OFF_X + RMAX * kST;         // [RMAX][kST] LayerNorm output
   static constexpr int OFF_CB = OFF_N + RMAX * kST;        // [RMAX][kST] context / ffn hidden
   static constexpr int OFF_Q = OFF_CB + RMAX * kST;        // [RMAX][HDP]
@@ -67,9 +74,10 @@ struct CS {
   static constexpr int OFF_BAR = (OFF_VALID + RMAX + 3) / 4 * 4;  // 2 mbarriers (16 B)
   static constexpr int FLOATS = OFF_BAR + 4;
   static_assert(FLOATS <= cluster_smem_floats(CL, H, RMAX), "layout");
+  static_assert(WB % 4 == 0 && AUX % 4 == 0, "16-byte buffers");
   static constexpr size_t BYTES = (size_t)FLOATS * sizeof(float);
   static_assert(H <= CL && CL % H == 0, "heads must divide the cluster");
-  static_assert(HD % G == 0, "head split");
+  static_assert(HD % G == 0 && NC % 4 == 0, "head split");
   static_assert(BYTES <= 227 * 1024, "shared memory budget");
 };
 
@@ -147,32 +155,53 @@ __device__ __forceinline__ void wait_weights(uint32_t bar, uint32_t parity, Devi
   }
 }
 
-// Issue the bulk copies of one layer's weight slice (6 blocks of NC rows, one
-// copy per row so rows land at the padded stride). Called by one warp.
+// Issue the bulk copies of one layer's slice: 6 blocks of NC weight rows (one
+// copy per row, so rows land at the padded stride) and the aux block (LayerNorm
+// parameters and bias slices). Called by one whole warp.
 template <int CL, int H>
 __device__ void load_layer_weights(const ClusterArgs &a, int layer, float *wbuf, uint32_t bar,
                                    int rank, int lane) {
   using C = CS<CL, H>;
+  constexpr int NC = C::NC;
   const char *base = a.image + (size_t)layer * a.layer_stride;
-  const float *wqkv = reinterpret_cast<const float *>(base + a.off.wqkv);
-  const float *wo = reinterpret_cast<const float *>(base + a.off.wo);
-  const float *w1 = reinterpret_cast<const float *>(base + a.off.w1);
-  const float *w2 = reinterpret_cast<const float *>(base + a.off.w2);
+  auto F = [&](size_t off) { return reinterpret_cast<const float *>(base + off); };
   const int h = rank / C::G, sub = rank % C::G;
-  const int qcol = h * C::HD + sub * (C::HD / C::G);  // first q/k/v column of this CTA
+  const int qcol = h * C::HD + sub * NC;  // first q/k/v column of this CTA
+  constexpr uint32_t bytes = (uint32_t)((C::WR * kD + aux_floats(CL)) * sizeof(float));
   if (lane == 0) {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    mbar_expect_tx(bar, (uint32_t)(C::WR * kD * sizeof(float)));
+    mbar_expect_tx(bar, bytes);
   }
   __syncwarp();
-  for (int r = lane; r < C::WR; r += 32) {
-    const int blk = r / C::NC, i = r % C::NC;
+  for (int r = lane; r < C::WR + 10; r += 32) {
     const float *src;
-    if (blk < 3) src = wqkv + (size_t)(blk * kD + qcol + i) * kD;      // q, k, v rows
-    else if (blk == 3) src = wo + (size_t)(rank * C::NC + i) * kD;     // out_proj rows
-    else if (blk == 4) src = w1 + (size_t)(rank * C::NC + i) * kD;     // ffn_in rows
-    else src = w2 + (size_t)(rank * C::NC + i) * kF;                   // ffn_out rows
-    bulk_g2s(smem_u32(wbuf + r * kST), src, kD * sizeof(float), bar);
+    uint32_t dst, n;
+    if (r < C::WR) {
+      const int blk = r / NC, i = r % NC;
+      if (blk < 3) src = F(a.off.wqkv) + (size_t)(blk * kD + qcol + i) * kD;   // q, k, v rows
+      else if (blk == 3) src = F(a.off.wo) + (size_t)(rank * NC + i) * kD;   // out_proj rows
+      else if (blk == 4) src = F(a.off.w1) + (size_t)(rank * NC + i) * kD;   // ffn_in rows
+      else src = F(a.off.w2) + (size_t)(rank * NC + i) * kF;                 // ffn_out rows
+      dst = smem_u32(wbuf + r * kST);
+      n = kD * sizeof(float);
+    } else {
+      const int j = r - C::WR;  // aux pieces
+      float *aux = wbuf + C::AUX;
+      if (j < 4) {
+        src = F(j == 0 ? a.off.ln1_w : j == 1 ? a.off.ln1_b : j == 2 ? a.off.ln2_w : a.off.ln2_b);
+        dst = smem_u32(aux + j * kD);
+        n = kD * sizeof(float);
+      } else {
+        const int b = j - 4;  // bq, bk, bv, bo, b1, b2
+        if (b < 3) src = F(a.off.bqkv) + b * kD + qcol;
+        else if (b == 3) src = F(a.off.bo) + rank * NC;
+        else if (b == 4) src = F(a.off.b1) + rank * NC;
+        else src = F(a.off.b2) + rank * NC;
+        dst = smem_u32(aux + 4 * kD + b * NC);
+        n = NC * sizeof(float);
+      }
+    }
+    bulk_g2s(dst, src, n, bar);
   }
 }
 
@@ -197,8 +226,10 @@ __device__ void ln_rows(const float *src, float *dst, int R, const float *gamma,
 
 // out[r][c] = sum_k A[r][k] * W[c][k] for r < R, c < NCOL, K = 128, both
 // operands in shared memory at stride kST. Work split: 2x4 output micro-tiles,
-// each shared by KS consecutive lanes that split K and reduce by shuffles.
-// epi(r, c, acc) runs on the lane with kq == 0.
+// each shared by KS consecutive lanes that split K and butterfly-reduce, so all
+// KS lanes end with the tile's sums. epi(r0, c0, acc, kq, ks, active) runs on
+// every lane (warp-uniform, so it may __syncwarp); lanes of an active tile
+// spread the tile's stores over the ks lanes by kq, inactive lanes store nothing.
 template <int NCOL, typename Epi>
 __device__ __forceinline__ void smem_gemm(const float *A, const float *W, int R, Epi epi) {
   constexpr int TI = 2, TJ = 4;
@@ -209,7 +240,7 @@ __device__ __forceinline__ void smem_gemm(const float *A, const float *W, int R,
   while (ks < 16 && tiles * ks * 2 <= kThreads) ks <<= 1;
   const int tid = threadIdx.x;
   const int kq = tid % ks;
-  // every thread runs the same number of iterations (shuffles below need the
+  // every thread runs the same number of iterations (the shuffles need the
   // whole warp); lanes past the last tile compute on tile 0 and store nothing
   for (int base = 0; base < tiles; base += kThreads / ks) {
     const int t_raw = base + tid / ks;
@@ -235,27 +266,20 @@ __device__ __forceinline__ void smem_gemm(const float *A, const float *W, int R,
         acc[1][j] = fmaf(a1.w, w.w, acc[1][j]);
       }
     }
-    // reduce the K split across the ks consecutive lanes of this tile
     for (int off = 1; off < ks; off <<= 1) {
 #pragma unroll
       for (int i = 0; i < TI; ++i)
 #pragma unroll
         for (int j = 0; j < TJ; ++j) acc[i][j] += __shfl_xor_sync(0xffffffffu, acc[i][j], off);
     }
-    if (active && kq == 0) {
-#pragma unroll
-      for (int i = 0; i < TI; ++i) {
-        if (r0 + i >= R) break;
-#pragma unroll
-        for (int j = 0; j < TJ; ++j) epi(r0 + i, c0 + j, acc[i][j]);
-      }
-    }
+    epi(r0, c0, acc, kq, ks, active);
   }
 }
 
 template <int CL, int H>
 __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const ClusterArgs a) {
   using C = CS<CL, H>;
+  constexpr int NC = C::NC, HD = C::HD, G = C::G, HDP = C::HDP;
   extern __shared__ __align__(128) float sm[];
   float *sW = sm + C::OFF_W;
   float *sX = sm + C::OFF_X;
@@ -275,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
   const int nsq = min(a.seq_per_cluster, a.nseq - seq0);
   const int R = nsq * S;               // token rows owned by this cluster (<= RMAX)
   const int64_t row0 = (int64_t)seq0 * S;
-  const int h = rank / C::G, sub = rank % C::G;
+  const int h = rank / G, sub = rank % G;
 
   if (tid == 0) {
     mbar_init(bar0, 1);
@@ -285,8 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
   __syncthreads();
   if (warp == 0) {
     load_layer_weights<CL, H>(a, 0, sW, bar0, rank, lane);
-    if (a.num_layers > 1)
-      load_layer_weights<CL, H>(a, 1, sW + C::WR * kST, bar0 + 8, rank, lane);
+    if (a.num_layers > 1) load_layer_weights<CL, H>(a, 1, sW + C::WB, bar0 + 8, rank, lane);
   }
   // residual stream and row validity for this cluster's sequences
   for (int i = tid; i < R * (kD / 4); i += kThreads) {
@@ -300,124 +323,191 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
 
   const uint32_t xs_l = smem_u32(sX), cb_l = smem_u32(sCB);
   const uint32_t q_l = smem_u32(sQ), k_l = smem_u32(sK), v_l = smem_u32(sV);
-  constexpr int NC = C::NC;
 
   for (int l = 0; l < a.num_layers; ++l) {
-    const char *lb = a.image + (size_t)l * a.layer_stride;
-    auto P = [&](size_t off) { return reinterpret_cast<const float *>(lb + off); };
-    float *wb = sW + (l & 1) * C::WR * kST;
+    const float *wb = sW + (l & 1) * C::WB;
+    const float *aux = wb + C::AUX;  // ln1 w|b, ln2 w|b, bq, bk, bv, bo, b1, b2
     const uint32_t bar = bar0 + 8 * (l & 1);
     if (l >= 1 && l + 1 < a.num_layers && warp == 0)
-      load_layer_weights<CL, H>(a, l + 1, sW + ((l + 1) & 1) * C::WR * kST,
-                                      bar0 + 8 * ((l + 1) & 1), rank, lane);
-
-    // ---- LayerNorm1 (local, all rows) and this CTA's q/k/v columns --------
-    ln_rows(sX, sN, R, P(a.off.ln1_w), P(a.off.ln1_b), a.eps, warp, lane);
-    __syncthreads();
+      load_layer_weights<CL, H>(a, l + 1, sW + ((l + 1) & 1) * C::WB, bar0 + 8 * ((l + 1) & 1),
+                                rank, lane);
     wait_weights(bar, (l >> 1) & 1, a.status, l);
-    {
-      const float *bqkv = P(a.off.bqkv);
-      const int qcol = h * C::HD + sub * (C::HD / C::G);
-      smem_gemm<3 * NC>(sN, wb, R, [&](int r, int c, float acc) {
-        const int blk = c / NC, i = c % NC;       // 0 = q, 1 = k, 2 = v
-        const float v = acc + bqkv[blk * kD + qcol + i];
-        const uint32_t base = blk == 0 ? q_l : (blk == 1 ? k_l : v_l);
-        const uint32_t off = (uint32_t)((r * C::HDP + sub * (C::HD / C::G) + i) * 4);
+
+    // ---- LayerNorm1 (local, all rows); q/k/v columns -> head group ---------
+    ln_rows(sX, sN, R, aux, aux + kD, a.eps, warp, lane);
+    __syncthreads();
+    smem_gemm<3 * NC>(sN, wb, R, [&](int r0, int c0, float (&acc)[2][4], int kq, int ks, bool act) {
+      const int blk = c0 / NC, i0 = c0 % NC;  // 0 = q, 1 = k, 2 = v
+      const float *bias = aux + 4 * kD + blk * NC + i0;
+      float4 v[2];
 #pragma unroll
-        for (int g = 0; g < C::G; ++g) st_cluster(cluster_map(base + off, h * C::G + g), v);
-      });
-    }
+      for (int i = 0; i < 2; ++i)
+        v[i] = make_float4(acc[i][0] + bias[0], acc[i][1] + bias[1], acc[i][2] + bias[2],
+                           acc[i][3] + bias[3]);
+      for (int g = kq; act && g < G; g += ks) {
+        const uint32_t dst = cluster_map(blk == 0 ? q_l : (blk == 1 ? k_l : v_l), h * G + g);
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+          if (r0 + i < R) st_cluster4(dst + (uint32_t)(((r0 + i) * HDP + sub * NC + i0) * 4), v[i]);
+      }
+    });
     cluster_sync();
 
-    // ---- attention: warp per query row, head h, rows r = sub (mod G) -------
-    for (int r = sub + C::G * warp; r < R; r += C::G * (kThreads / 32)) {
-      if (sValid[r] == 0.f) continue;  // padded query: its output row is zeroed later
-      const int sq = r / S, i = r % S;
-      const int kbase = sq * S;
-      const int kend = a.causal ? i + 1 : S;
-      const float *qr = sQ + r * C::HDP;
-      float m = -CUDART_INF_F, lsum = 0.f;
-      float o[(C::HD + 31) / 32];
+    // ---- attention for head h, query rows r = sub (mod G), a warp per row --
+    {
+      // lane roles: scores use lane = key; P.V uses lane = (key group, 4-dim slot)
+      constexpr int SLOTS = HD / 4;                   // float4 slots of a head row
+      constexpr int KG = SLOTS >= 32 ? 1 : 32 / SLOTS;  // key groups sharing P.V
+      constexpr int NSL = (SLOTS + 31) / 32;          // slots per lane (HD = 128: 1)
+      const int kg = lane / (32 / KG) % KG;           // this lane's key group
+      const int slot0 = lane % (32 / KG);             // first slot of this lane
+      for (int r = sub + G * warp; r < R; r += G * (kThreads / 32)) {
+        if (sValid[r] == 0.f) continue;  // padded query: its output row is zeroed later
+        const int sq = r / S, i = r % S;
+        const int kbase = sq * S;
+        const int kend = a.causal ? i + 1 : S;
+        const float *qr = sQ + r * HDP;
+        float m = -CUDART_INF_F, lsum = 0.f;
+        float4 o[NSL];
 #pragma unroll
-      for (int t = 0; t < (C::HD + 31) / 32; ++t) o[t] = 0.f;
-      for (int jb = 0; jb < kend; jb += 32) {
-        const int j = jb + lane;
-        float s = -CUDART_INF_F;
-        if (j < kend && sValid[kbase + j] != 0.f) {
-          const float *kr = sK + (kbase + j) * C::HDP;
-          float dot = 0.f;
-#pragma unroll 8
-          for (int d = 0; d < C::HD; ++d) dot = fmaf(qr[d], kr[d], dot);
-          s = dot * a.scale;
+        for (int t = 0; t < NSL; ++t) o[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int jb = 0; jb < kend; jb += 32) {
+          const int j = jb + lane;
+          float s = -CUDART_INF_F;
+          if (j < kend && sValid[kbase + j] != 0.f) {
+            const float *kr = sK + (kbase + j) * HDP;
+            float dot = 0.f;
+#pragma unroll
+            for (int d = 0; d < HD; d += 4) {
+              const float4 q4 = *reinterpret_cast<const float4 *>(qr + d);
+              const float4 k4 = *reinterpret_cast<const float4 *>(kr + d);
+              dot = fmaf(q4.x, k4.x, dot);
+              dot = fmaf(q4.y, k4.y, dot);
+              dot = fmaf(q4.z, k4.z, dot);
+              dot = fmaf(q4.w, k4.w, dot);
+            }
+            s = dot * a.scale;
+          }
+          const float mn = fmaxf(m, warp_max(s));
+          if (mn == -CUDART_INF_F) continue;  // no allowed key yet (uniform across the warp)
+          const float alpha = __expf(m - mn);
+          const float p = __expf(s - mn);
+          lsum = lsum * alpha + warp_sum(p);
+#pragma unroll
+          for (int t = 0; t < NSL; ++t) {
+            o[t].x *= alpha; o[t].y *= alpha; o[t].z *= alpha; o[t].w *= alpha;
+          }
+          const int nj = min(32, kend - jb);
+          for (int jj = 0; jj < nj; jj += KG) {
+            const int jk = jj + kg;
+            const float pj = __shfl_sync(0xffffffffu, p, jk < 32 ? jk : 0);
+            if (jk < nj) {
+              const float *vr = sV + (kbase + jb + jk) * HDP;
+#pragma unroll
+              for (int t = 0; t < NSL; ++t) {
+                const int slot = slot0 + 32 * t;
+                if (slot < SLOTS) {
+                  const float4 v4 = *reinterpret_cast<const float4 *>(vr + 4 * slot);
+                  o[t].x = fmaf(pj, v4.x, o[t].x);
+                  o[t].y = fmaf(pj, v4.y, o[t].y);
+                  o[t].z = fmaf(pj, v4.z, o[t].z);
+                  o[t].w = fmaf(pj, v4.w, o[t].w);
+                }
+              }
+            }
+          }
+          m = mn;
         }
-        const float mn = fmaxf(m, warp_max(s));
-        if (mn == -CUDART_INF_F) continue;  // no allowed key yet (uniform across the warp)
-        const float alpha = __expf(m - mn);
-        const float p = __expf(s - mn);
-        lsum = lsum * alpha + warp_sum(p);
+        // combine the key groups: lanes with the same slot differ in the high bits
+        for (int off = 32 / KG; off < 32; off <<= 1) {
 #pragma unroll
-        for (int t = 0; t < (C::HD + 31) / 32; ++t) o[t] *= alpha;
-        const int nj = min(32, kend - jb);
-        for (int jj = 0; jj < nj; ++jj) {
-          const float pj = __shfl_sync(0xffffffffu, p, jj);
-          const float *vr = sV + (kbase + jb + jj) * C::HDP;
-#pragma unroll
-          for (int t = 0; t < (C::HD + 31) / 32; ++t) {
-            const int d = lane + 32 * t;
-            if (d < C::HD) o[t] = fmaf(pj, vr[d], o[t]);
+          for (int t = 0; t < NSL; ++t) {
+            o[t].x += __shfl_xor_sync(0xffffffffu, o[t].x, off);
+            o[t].y += __shfl_xor_sync(0xffffffffu, o[t].y, off);
+            o[t].z += __shfl_xor_sync(0xffffffffu, o[t].z, off);
+            o[t].w += __shfl_xor_sync(0xffffffffu, o[t].w, off);
           }
         }
-        m = mn;
-      }
-      const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+        const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
 #pragma unroll
-      for (int t = 0; t < (C::HD + 31) / 32; ++t) {
-        const int d = lane + 32 * t;
-        if (d < C::HD) {
-          const uint32_t off = (uint32_t)((r * kST + h * C::HD + d) * 4);
-          const float v = o[t] * inv;
-          for (int g = 0; g < CL; ++g) st_cluster(cluster_map(cb_l + off, g), v);
+        for (int t = 0; t < NSL; ++t) {
+          const int slot = slot0 + 32 * t;
+          if (slot < SLOTS) {
+            const float4 v4 = make_float4(o[t].x * inv, o[t].y * inv, o[t].z * inv, o[t].w * inv);
+            const uint32_t off = (uint32_t)((r * kST + h * HD + 4 * slot) * 4);
+            for (int g = kg; g < CL; g += KG) st_cluster4(cluster_map(cb_l, g) + off, v4);
+          }
         }
       }
     }
     cluster_sync();
 
     // ---- out_proj + padded-row zeroing + residual: X[:, own cols] ---------
-    {
-      const float *bo = P(a.off.bo);
-      smem_gemm<NC>(sCB, wb + 3 * NC * kST, R, [&](int r, int c, float acc) {
-        const int col = rank * NC + c;
-        const float v = sValid[r] != 0.f ? sX[r * kST + col] + (acc + bo[col]) : 0.f;
-        const uint32_t off = (uint32_t)((r * kST + col) * 4);
-        for (int g = 0; g < CL; ++g) st_cluster(cluster_map(xs_l + off, g), v);
-      });
-    }
+    smem_gemm<NC>(sCB, wb + 3 * NC * kST, R, [&](int r0, int c0, float (&acc)[2][4], int kq, int ks, bool act) {
+      const int col = rank * NC + c0;
+      const float *bias = aux + 4 * kD + 3 * NC + c0;
+      float4 v[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int r = min(r0 + i, R - 1);
+        const float4 x4 = *reinterpret_cast<const float4 *>(sX + r * kST + col);
+        v[i] = sValid[r] != 0.f
+                   ? make_float4(x4.x + (acc[i][0] + bias[0]), x4.y + (acc[i][1] + bias[1]),
+                                 x4.z + (acc[i][2] + bias[2]), x4.w + (acc[i][3] + bias[3]))
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      __syncwarp();  // every lane has read X before any lane overwrites it
+      for (int g = kq; act && g < CL; g += ks) {
+        const uint32_t dst = cluster_map(xs_l, g);
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+          if (r0 + i < R) st_cluster4(dst + (uint32_t)(((r0 + i) * kST + col) * 4), v[i]);
+      }
+    });
     cluster_sync();
 
     // ---- LayerNorm2 (local) and ffn_in + exact GELU: CB[:, own cols] -------
-    ln_rows(sX, sN, R, P(a.off.ln2_w), P(a.off.ln2_b), a.eps, warp, lane);
+    ln_rows(sX, sN, R, aux + 2 * kD, aux + 3 * kD, a.eps, warp, lane);
     __syncthreads();
-    {
-      const float *b1 = P(a.off.b1);
-      smem_gemm<NC>(sN, wb + 4 * NC * kST, R, [&](int r, int c, float acc) {
-        const int col = rank * NC + c;
-        const float v = gelu_erf(acc + b1[col]);
-        const uint32_t off = (uint32_t)((r * kST + col) * 4);
-        for (int g = 0; g < CL; ++g) st_cluster(cluster_map(cb_l + off, g), v);
-      });
-    }
+    smem_gemm<NC>(sN, wb + 4 * NC * kST, R, [&](int r0, int c0, float (&acc)[2][4], int kq, int ks, bool act) {
+      const int col = rank * NC + c0;
+      const float *bias = aux + 4 * kD + 4 * NC + c0;
+      float4 v[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+        v[i] = make_float4(gelu_erf(acc[i][0] + bias[0]), gelu_erf(acc[i][1] + bias[1]),
+                           gelu_erf(acc[i][2] + bias[2]), gelu_erf(acc[i][3] + bias[3]));
+      for (int g = kq; act && g < CL; g += ks) {
+        const uint32_t dst = cluster_map(cb_l, g);
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+          if (r0 + i < R) st_cluster4(dst + (uint32_t)(((r0 + i) * kST + col) * 4), v[i]);
+      }
+    });
     cluster_sync();
 
     // ---- ffn_out + residual + block-end padded-row zeroing -----------------
-    {
-      const float *b2 = P(a.off.b2);
-      smem_gemm<NC>(sCB, wb + 5 * NC * kST, R, [&](int r, int c, float acc) {
-        const int col = rank * NC + c;
-        const float v = sValid[r] != 0.f ? sX[r * kST + col] + (acc + b2[col]) : 0.f;
-        const uint32_t off = (uint32_t)((r * kST + col) * 4);
-        for (int g = 0; g < CL; ++g) st_cluster(cluster_map(xs_l + off, g), v);
-      });
-    }
+    smem_gemm<NC>(sCB, wb + 5 * NC * kST, R, [&](int r0, int c0, float (&acc)[2][4], int kq, int ks, bool act) {
+      const int col = rank * NC + c0;
+      const float *bias = aux + 4 * kD + 5 * NC + c0;
+      float4 v[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int r = min(r0 + i, R - 1);
+        const float4 x4 = *reinterpret_cast<const float4 *>(sX + r * kST + col);
+        v[i] = sValid[r] != 0.f
+                   ? make_float4(x4.x + (acc[i][0] + bias[0]), x4.y + (acc[i][1] + bias[1]),
+                                 x4.z + (acc[i][2] + bias[2]), x4.w + (acc[i][3] + bias[3]))
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      __syncwarp();
+      for (int g = kq; act && g < CL; g += ks) {
+        const uint32_t dst = cluster_map(xs_l, g);
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+          if (r0 + i < R) st_cluster4(dst + (uint32_t)(((r0 + i) * kST + col) * 4), v[i]);
+      }
+    });
     cluster_sync();
   }
 
