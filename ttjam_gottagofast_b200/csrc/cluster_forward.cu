@@ -7,23 +7,26 @@
 // grid-wide barrier and clusters need not be co-resident. Inside a cluster:
 //   * weights are column-partitioned: CTA r owns 128/CL output columns of each
 //     of q, k, v, out_proj, ffn_in and ffn_out. Its slice of a layer (48 rows
-//     of 128 floats at CL = 16) is streamed global -> shared with bulk async
-//     copies completing on an mbarrier, double-buffered so layer l+1 loads
-//     while layer l computes;
+//     of 128 floats at CL = 16, plus its bias slices and the LayerNorm
+//     parameters) is copied global -> shared with 16-byte cp.async by all
+//     threads, double-buffered so layer l+1 loads while layer l computes;
 //   * activations are replicated: every CTA holds the full residual stream
 //     X[R,128] in shared memory and computes LayerNorms locally; each projection
-//     writes its columns into every CTA's copy through distributed shared
-//     memory (st.shared::cluster), followed by one cluster barrier;
+//     pushes its output columns into every consumer CTA's copy with st.async
+//     (distributed shared memory), each store completing its bytes on the
+//     consumer's mbarrier for that phase. A consumer arms the mbarrier with the
+//     bytes it expects and waits for them: one-way transfers, no cluster
+//     barrier inside the layer loop. The all-to-all data dependencies order
+//     buffer reuse (a CTA can only produce phase p+1 data after it has received
+//     phase p data from every producer, so every consumer is done reading);
 //   * attention: CTA r serves head r / (CL/H) for every (CL/H)-th query row,
-//     one warp per query row, from the q/k/v head slices its head group wrote.
-// Per layer: 5 cluster barriers (after q/k/v, context, out_proj, ffn_in,
-// ffn_out). Padded rows are zeroed exactly where the reference zeroes them.
+//     one warp per query row, from the q/k/v head slices its head group pushed.
 //
 // Semantics follow BaselineTransformer.forward (torch_transformer_benchmark.py:
 // 59-172): pre-norm block :140-144, attention :93-121, final norm :169-171.
-// Every wait on an mbarrier is bounded; a wait that gives up latches
-// TT_ERR_DEVICE_TIMEOUT in the status word and the kernel still reaches every
-// cluster barrier, so no CTA is left waiting.
+// Every mbarrier wait is bounded; a wait that gives up latches
+// TT_ERR_DEVICE_TIMEOUT in the status word and the kernel carries on to the
+// closing cluster barrier, so no CTA is left waiting.
 #include <math_constants.h>
 
 #include "cluster_forward.cuh"
@@ -43,7 +46,7 @@ constexpr int aux_floats(int CL) { return 4 * kD + 6 * (kD / CL); }
 constexpr int wbuf_floats(int CL) { return 6 * (kD / CL) * kST + aux_floats(CL); }
 // Shared-memory floats of one CTA for cluster size CL, H heads, R rows.
 constexpr int cluster_smem_floats(int CL, int H, int R) {
-  return 2 * wbuf_floats(CL) + 3 * R * kST + 3 * R * (kD / H + 4) + R + 8;
+  return 2 * wbuf_floats(CL) + 3 * R * kST + 3 * R * (kD / H + 4) + R + 16;
 }
 // Largest row count per cluster (a multiple of 16, at most 64) that fits the
 // 227 KB of shared memory a CTA may use.
@@ -71,8 +74,8 @@ struct CS {
   static constexpr int OFF_K = OFF_Q + RMAX * HDP;
   static constexpr int OFF_V = OFF_K + RMAX * HDP;
   static constexpr int OFF_VALID = OFF_V + RMAX * HDP;     // [RMAX]
-  static constexpr int OFF_BAR = (OFF_VALID + RMAX + 3) / 4 * 4;  // 2 mbarriers (16 B)
-  static constexpr int FLOATS = OFF_BAR + 4;
+  static constexpr int OFF_BAR = (OFF_VALID + RMAX + 3) / 4 * 4;  // 5 phase mbarriers
+  static constexpr int FLOATS = OFF_BAR + 10;
   static_assert(FLOATS <= cluster_smem_floats(CL, H, RMAX), "layout");
   static_assert(WB % 4 == 0 && AUX % 4 == 0, "16-byte buffers");
   static constexpr size_t BYTES = (size_t)FLOATS * sizeof(float);
@@ -89,14 +92,6 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t local, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
   return r;
-}
-__device__ __forceinline__ void st_cluster(uint32_t addr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-__device__ __forceinline__ void st_cluster4(uint32_t addr, float4 v) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x),
-               "f"(v.y), "f"(v.z), "f"(v.w)
-               : "memory");
 }
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
@@ -120,13 +115,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return done != 0;
 }
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes,
-                                         uint32_t bar) {
+// 16 bytes to another CTA's shared memory; the bytes complete on that CTA's
+// mbarrier `rbar` (a shared::cluster address).
+__device__ __forceinline__ void st_async4(uint32_t raddr, float4 v, uint32_t rbar) {
   asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-          "r"(dst),
-      "l"(src), "r"(bytes), "r"(bar)
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::
+          "r"(raddr),
+      "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(rbar)
       : "memory");
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -140,87 +146,101 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// Bounded wait for the weight slice of one layer. Gives up after ~2^31 cycles
-// (about a second) and latches a timeout; the caller carries on so that every
-// CTA still reaches every cluster barrier.
-__device__ __forceinline__ void wait_weights(uint32_t bar, uint32_t parity, DeviceStatus *st,
-                                             int layer) {
+// Bounded wait for one exchange phase. Gives up after ~2^31 cycles (about a
+// second) and latches a timeout; the caller carries on so that every CTA still
+// reaches the closing cluster barrier.
+__device__ __forceinline__ void wait_phase(uint32_t bar, uint32_t parity, DeviceStatus *st,
+                                           int code) {
   if (mbar_try_wait(bar, parity)) return;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
     if (clock64() - t0 > (1LL << 31)) {
-      raise_status(st, TT_ERR_DEVICE_TIMEOUT, 0x100 + layer);
+      raise_status(st, TT_ERR_DEVICE_TIMEOUT, code);
       return;
     }
   }
 }
 
-// Issue the bulk copies of one layer's slice: 6 blocks of NC weight rows (one
-// copy per row, so rows land at the padded stride) and the aux block (LayerNorm
-// parameters and bias slices). Called by one whole warp.
+// Copy one layer's slice into a weight buffer with 16-byte cp.async spread over
+// all threads: 6 blocks of NC weight rows at the padded stride, then the aux
+// block (LayerNorm parameters and bias slices). Commits one async group.
 template <int CL, int H>
-__device__ void load_layer_weights(const ClusterArgs &a, int layer, float *wbuf, uint32_t bar,
-                                   int rank, int lane) {
+__device__ void load_layer_weights(const ClusterArgs &a, int layer, float *wbuf, int rank) {
   using C = CS<CL, H>;
   constexpr int NC = C::NC;
+  constexpr int ROW16 = kD / 4;                       // 16-byte chunks per weight row
+  constexpr int NROW = C::WR * ROW16;                 // chunks of the weight rows
+  constexpr int NLN = 4 * ROW16;                      // chunks of ln1 w|b, ln2 w|b
+  constexpr int NB = 6 * (NC / 4);                    // chunks of the bias slices
   const char *base = a.image + (size_t)layer * a.layer_stride;
   auto F = [&](size_t off) { return reinterpret_cast<const float *>(base + off); };
   const int h = rank / C::G, sub = rank % C::G;
   const int qcol = h * C::HD + sub * NC;  // first q/k/v column of this CTA
-  constexpr uint32_t bytes = (uint32_t)((C::WR * kD + aux_floats(CL)) * sizeof(float));
-  if (lane == 0) {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    mbar_expect_tx(bar, bytes);
-  }
-  __syncwarp();
-  for (int r = lane; r < C::WR + 10; r += 32) {
+  for (int c = threadIdx.x; c < NROW + NLN + NB; c += kThreads) {
     const float *src;
-    uint32_t dst, n;
-    if (r < C::WR) {
+    float *dst;
+    if (c < NROW) {
+      const int r = c / ROW16, k4 = (c % ROW16) * 4;
       const int blk = r / NC, i = r % NC;
       if (blk < 3) src = F(a.off.wqkv) + (size_t)(blk * kD + qcol + i) * kD;   // q, k, v rows
       else if (blk == 3) src = F(a.off.wo) + (size_t)(rank * NC + i) * kD;   // out_proj rows
       else if (blk == 4) src = F(a.off.w1) + (size_t)(rank * NC + i) * kD;   // ffn_in rows
       else src = F(a.off.w2) + (size_t)(rank * NC + i) * kF;                 // ffn_out rows
-      dst = smem_u32(wbuf + r * kST);
-      n = kD * sizeof(float);
+      src += k4;
+      dst = wbuf + r * kST + k4;
+    } else if (c < NROW + NLN) {
+      const int j = (c - NROW) / ROW16, k4 = ((c - NROW) % ROW16) * 4;
+      src = F(j == 0 ? a.off.ln1_w : j == 1 ? a.off.ln1_b : j == 2 ? a.off.ln2_w : a.off.ln2_b) + k4;
+      dst = wbuf + C::AUX + j * kD + k4;
     } else {
-      const int j = r - C::WR;  // aux pieces
-      float *aux = wbuf + C::AUX;
-      if (j < 4) {
-        src = F(j == 0 ? a.off.ln1_w : j == 1 ? a.off.ln1_b : j == 2 ? a.off.ln2_w : a.off.ln2_b);
-        dst = smem_u32(aux + j * kD);
-        n = kD * sizeof(float);
-      } else {
-        const int b = j - 4;  // bq, bk, bv, bo, b1, b2
-        if (b < 3) src = F(a.off.bqkv) + b * kD + qcol;
-        else if (b == 3) src = F(a.off.bo) + rank * NC;
-        else if (b == 4) src = F(a.off.b1) + rank * NC;
-        else src = F(a.off.b2) + rank * NC;
-        dst = smem_u32(aux + 4 * kD + b * NC);
-        n = NC * sizeof(float);
-      }
+      const int b = (c - NROW - NLN) / (NC / 4), k4 = ((c - NROW - NLN) % (NC / 4)) * 4;
+      if (b < 3) src = F(a.off.bqkv) + b * kD + qcol;   // bq, bk, bv
+      else if (b == 3) src = F(a.off.bo) + rank * NC;
+      else if (b == 4) src = F(a.off.b1) + rank * NC;
+      else src = F(a.off.b2) + rank * NC;
+      src += k4;
+      dst = wbuf + C::AUX + 4 * kD + b * NC + k4;
     }
-    bulk_g2s(dst, src, n, bar);
+    cp_async16(smem_u32(dst), src);
   }
+  cp_async_commit();
 }
 
-// Row LayerNorm of R rows of `src` (stride kST) into `dst`, one warp per row.
+// Row LayerNorm of R rows of `src` (stride kST) into `dst`, one warp per row,
+// two rows in flight per warp so their shuffle chains overlap.
 __device__ void ln_rows(const float *src, float *dst, int R, const float *gamma,
                         const float *beta, float eps, int warp, int lane) {
   const float4 g = reinterpret_cast<const float4 *>(gamma)[lane];
   const float4 b = reinterpret_cast<const float4 *>(beta)[lane];
-  for (int r = warp; r < R; r += kThreads / 32) {
-    const float4 v = reinterpret_cast<const float4 *>(src + r * kST)[lane];
-    const float mean = warp_sum((v.x + v.y) + (v.z + v.w)) * (1.0f / kD);
-    const float a0 = v.x - mean, a1 = v.y - mean, a2 = v.z - mean, a3 = v.w - mean;
-    const float rstd = rsqrtf(warp_sum((a0 * a0 + a1 * a1) + (a2 * a2 + a3 * a3)) * (1.0f / kD) + eps);
-    float4 o;
-    o.x = a0 * rstd * g.x + b.x;
-    o.y = a1 * rstd * g.y + b.y;
-    o.z = a2 * rstd * g.z + b.z;
-    o.w = a3 * rstd * g.w + b.w;
-    reinterpret_cast<float4 *>(dst + r * kST)[lane] = o;
+  constexpr int NW = kThreads / 32;
+  for (int r0 = warp; r0 < R; r0 += 2 * NW) {
+    const int r1 = r0 + NW < R ? r0 + NW : r0;
+    const float4 v0 = reinterpret_cast<const float4 *>(src + r0 * kST)[lane];
+    const float4 v1 = reinterpret_cast<const float4 *>(src + r1 * kST)[lane];
+    float s0 = (v0.x + v0.y) + (v0.z + v0.w), s1 = (v1.x + v1.y) + (v1.z + v1.w);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    }
+    const float m0 = s0 * (1.0f / kD), m1 = s1 * (1.0f / kD);
+    const float a0 = v0.x - m0, a1 = v0.y - m0, a2 = v0.z - m0, a3 = v0.w - m0;
+    const float c0 = v1.x - m1, c1 = v1.y - m1, c2 = v1.z - m1, c3 = v1.w - m1;
+    float q0 = (a0 * a0 + a1 * a1) + (a2 * a2 + a3 * a3);
+    float q1 = (c0 * c0 + c1 * c1) + (c2 * c2 + c3 * c3);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      q0 += __shfl_xor_sync(0xffffffffu, q0, o);
+      q1 += __shfl_xor_sync(0xffffffffu, q1, o);
+    }
+    const float rs0 = rsqrtf(q0 * (1.0f / kD) + eps), rs1 = rsqrtf(q1 * (1.0f / kD) + eps);
+    reinterpret_cast<float4 *>(dst + r0 * kST)[lane] =
+        make_float4(a0 * rs0 * g.x + b.x, a1 * rs0 * g.y + b.y, a2 * rs0 * g.z + b.z,
+                    a3 * rs0 * g.w + b.w);
+    if (r1 != r0)
+      reinterpret_cast<float4 *>(dst + r1 * kST)[lane] =
+          make_float4(c0 * rs1 * g.x + b.x, c1 * rs1 * g.y + b.y, c2 * rs1 * g.z + b.z,
+                      c3 * rs1 * g.w + b.w);
   }
 }
 
@@ -250,6 +270,7 @@ __device__ __forceinline__ void smem_gemm(const float *A, const float *W, int R,
     const int r1 = min(r0 + 1, R - 1);
     float acc[TI][TJ] = {};
     const float *a0p = A + r0 * kST, *a1p = A + r1 * kST;
+#pragma unroll 4
     for (int k = kq * 4; k < kD; k += ks * 4) {
       const float4 a0 = *reinterpret_cast<const float4 *>(a0p + k);
       const float4 a1 = *reinterpret_cast<const float4 *>(a1p + k);
@@ -280,6 +301,7 @@ template <int CL, int H>
 __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const ClusterArgs a) {
   using C = CS<CL, H>;
   constexpr int NC = C::NC, HD = C::HD, G = C::G, HDP = C::HDP;
+  enum { PH_QKV = 0, PH_CTX, PH_X1, PH_H, PH_X2, NPH };
   extern __shared__ __align__(128) float sm[];
   float *sW = sm + C::OFF_W;
   float *sX = sm + C::OFF_X;
@@ -289,12 +311,13 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
   float *sK = sm + C::OFF_K;
   float *sV = sm + C::OFF_V;
   float *sValid = sm + C::OFF_VALID;
-  const uint32_t bar0 = smem_u32(sm + C::OFF_BAR);
+  const uint32_t bar0 = smem_u32(sm + C::OFF_BAR);  // phase p's mbarrier at bar0 + 8p
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int rank = blockIdx.x % CL;
   const int cid = blockIdx.x / CL;
   const int S = a.seq;
+  const int L = a.num_layers;
   const int seq0 = cid * a.seq_per_cluster;
   const int nsq = min(a.seq_per_cluster, a.nseq - seq0);
   const int R = nsq * S;               // token rows owned by this cluster (<= RMAX)
@@ -302,36 +325,44 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
   const int h = rank / G, sub = rank % G;
 
   if (tid == 0) {
-    mbar_init(bar0, 1);
-    mbar_init(bar0 + 8, 1);
+    for (int p = 0; p < NPH; ++p) mbar_init(bar0 + 8 * p, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  __syncthreads();
-  if (warp == 0) {
-    load_layer_weights<CL, H>(a, 0, sW, bar0, rank, lane);
-    if (a.num_layers > 1) load_layer_weights<CL, H>(a, 1, sW + C::WB, bar0 + 8, rank, lane);
-  }
+  load_layer_weights<CL, H>(a, 0, sW, rank);
+  if (L > 1) load_layer_weights<CL, H>(a, 1, sW + C::WB, rank);
   // residual stream and row validity for this cluster's sequences
   for (int i = tid; i < R * (kD / 4); i += kThreads) {
     const int r = i / (kD / 4), c4 = i % (kD / 4);
     reinterpret_cast<float4 *>(sX + r * kST)[c4] =
         reinterpret_cast<const float4 *>(a.x + (row0 + r) * kD)[c4];
   }
-  for (int r = tid; r < R; r += kThreads)
-    sValid[r] = (a.mask == nullptr || a.mask[row0 + r] != 0) ? 1.f : 0.f;
-  cluster_sync();  // every CTA of the cluster is running before any remote store
+  const bool my_valid = tid < R && (a.mask == nullptr || a.mask[row0 + tid] != 0);
+  if (tid < R) sValid[tid] = my_valid ? 1.f : 0.f;
+  const int nvalid = __syncthreads_count(my_valid);
+  // bytes each phase delivers to this CTA per layer
+  const uint32_t e_qkv = (uint32_t)(R * 3 * HD * 4);
+  const uint32_t e_ctx = (uint32_t)(nvalid * kD * 4);
+  const uint32_t e_row = (uint32_t)(R * kD * 4);
+  cluster_sync();  // every CTA is running with initialised mbarriers before any remote store
 
   const uint32_t xs_l = smem_u32(sX), cb_l = smem_u32(sCB);
   const uint32_t q_l = smem_u32(sQ), k_l = smem_u32(sK), v_l = smem_u32(sV);
 
-  for (int l = 0; l < a.num_layers; ++l) {
+  for (int l = 0; l < L; ++l) {
     const float *wb = sW + (l & 1) * C::WB;
     const float *aux = wb + C::AUX;  // ln1 w|b, ln2 w|b, bq, bk, bv, bo, b1, b2
-    const uint32_t bar = bar0 + 8 * (l & 1);
-    if (l >= 1 && l + 1 < a.num_layers && warp == 0)
-      load_layer_weights<CL, H>(a, l + 1, sW + ((l + 1) & 1) * C::WB, bar0 + 8 * ((l + 1) & 1),
-                                rank, lane);
-    wait_weights(bar, (l >> 1) & 1, a.status, l);
+    const uint32_t par = l & 1;
+    __syncthreads();  // the whole CTA is done with layer l-1 (weight buffer reuse)
+    if (tid == 0) {
+      mbar_expect_tx(bar0 + 8 * PH_QKV, e_qkv);
+      mbar_expect_tx(bar0 + 8 * PH_CTX, e_ctx);
+      mbar_expect_tx(bar0 + 8 * PH_X1, e_row);
+      mbar_expect_tx(bar0 + 8 * PH_H, e_row);
+      mbar_expect_tx(bar0 + 8 * PH_X2, e_row);
+    }
+    if (l >= 1 && l + 1 < L) load_layer_weights<CL, H>(a, l + 1, sW + ((l + 1) & 1) * C::WB, rank);
+    if (l + 1 < L) cp_async_wait<1>(); else cp_async_wait<0>();
+    __syncthreads();  // layer l's weights are visible to every thread
 
     // ---- LayerNorm1 (local, all rows); q/k/v columns -> head group ---------
     ln_rows(sX, sN, R, aux, aux + kD, a.eps, warp, lane);
@@ -344,23 +375,24 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
       for (int i = 0; i < 2; ++i)
         v[i] = make_float4(acc[i][0] + bias[0], acc[i][1] + bias[1], acc[i][2] + bias[2],
                            acc[i][3] + bias[3]);
+      const uint32_t base = blk == 0 ? q_l : (blk == 1 ? k_l : v_l);
       for (int g = kq; act && g < G; g += ks) {
-        const uint32_t dst = cluster_map(blk == 0 ? q_l : (blk == 1 ? k_l : v_l), h * G + g);
+        const uint32_t dst = cluster_map(base, h * G + g);
+        const uint32_t rb = cluster_map(bar0 + 8 * PH_QKV, h * G + g);
 #pragma unroll
         for (int i = 0; i < 2; ++i)
-          if (r0 + i < R) st_cluster4(dst + (uint32_t)(((r0 + i) * HDP + sub * NC + i0) * 4), v[i]);
+          if (r0 + i < R) st_async4(dst + (uint32_t)(((r0 + i) * HDP + sub * NC + i0) * 4), v[i], rb);
       }
     });
-    cluster_sync();
+    wait_phase(bar0 + 8 * PH_QKV, par, a.status, 0x100 + l);
 
     // ---- attention for head h, query rows r = sub (mod G), a warp per row --
     {
       // lane roles: scores use lane = key; P.V uses lane = (key group, 4-dim slot)
-      constexpr int SLOTS = HD / 4;                   // float4 slots of a head row
+      constexpr int SLOTS = HD / 4;                     // float4 slots of a head row
       constexpr int KG = SLOTS >= 32 ? 1 : 32 / SLOTS;  // key groups sharing P.V
-      constexpr int NSL = (SLOTS + 31) / 32;          // slots per lane (HD = 128: 1)
-      const int kg = lane / (32 / KG) % KG;           // this lane's key group
-      const int slot0 = lane % (32 / KG);             // first slot of this lane
+      const int kg = lane / (32 / KG);                  // this lane's key group
+      const int slot = lane % (32 / KG);                // this lane's float4 slot
       for (int r = sub + G * warp; r < R; r += G * (kThreads / 32)) {
         if (sValid[r] == 0.f) continue;  // padded query: its output row is zeroed later
         const int sq = r / S, i = r % S;
@@ -368,9 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
         const int kend = a.causal ? i + 1 : S;
         const float *qr = sQ + r * HDP;
         float m = -CUDART_INF_F, lsum = 0.f;
-        float4 o[NSL];
-#pragma unroll
-        for (int t = 0; t < NSL; ++t) o[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int jb = 0; jb < kend; jb += 32) {
           const int j = jb + lane;
           float s = -CUDART_INF_F;
@@ -393,54 +423,36 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
           const float alpha = __expf(m - mn);
           const float p = __expf(s - mn);
           lsum = lsum * alpha + warp_sum(p);
-#pragma unroll
-          for (int t = 0; t < NSL; ++t) {
-            o[t].x *= alpha; o[t].y *= alpha; o[t].z *= alpha; o[t].w *= alpha;
-          }
+          o.x *= alpha; o.y *= alpha; o.z *= alpha; o.w *= alpha;
           const int nj = min(32, kend - jb);
           for (int jj = 0; jj < nj; jj += KG) {
             const int jk = jj + kg;
             const float pj = __shfl_sync(0xffffffffu, p, jk < 32 ? jk : 0);
             if (jk < nj) {
-              const float *vr = sV + (kbase + jb + jk) * HDP;
-#pragma unroll
-              for (int t = 0; t < NSL; ++t) {
-                const int slot = slot0 + 32 * t;
-                if (slot < SLOTS) {
-                  const float4 v4 = *reinterpret_cast<const float4 *>(vr + 4 * slot);
-                  o[t].x = fmaf(pj, v4.x, o[t].x);
-                  o[t].y = fmaf(pj, v4.y, o[t].y);
-                  o[t].z = fmaf(pj, v4.z, o[t].z);
-                  o[t].w = fmaf(pj, v4.w, o[t].w);
-                }
-              }
+              const float4 v4 = *reinterpret_cast<const float4 *>(sV + (kbase + jb + jk) * HDP + 4 * slot);
+              o.x = fmaf(pj, v4.x, o.x);
+              o.y = fmaf(pj, v4.y, o.y);
+              o.z = fmaf(pj, v4.z, o.z);
+              o.w = fmaf(pj, v4.w, o.w);
             }
           }
           m = mn;
         }
         // combine the key groups: lanes with the same slot differ in the high bits
         for (int off = 32 / KG; off < 32; off <<= 1) {
-#pragma unroll
-          for (int t = 0; t < NSL; ++t) {
-            o[t].x += __shfl_xor_sync(0xffffffffu, o[t].x, off);
-            o[t].y += __shfl_xor_sync(0xffffffffu, o[t].y, off);
-            o[t].z += __shfl_xor_sync(0xffffffffu, o[t].z, off);
-            o[t].w += __shfl_xor_sync(0xffffffffu, o[t].w, off);
-          }
+          o.x += __shfl_xor_sync(0xffffffffu, o.x, off);
+          o.y += __shfl_xor_sync(0xffffffffu, o.y, off);
+          o.z += __shfl_xor_sync(0xffffffffu, o.z, off);
+          o.w += __shfl_xor_sync(0xffffffffu, o.w, off);
         }
         const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-#pragma unroll
-        for (int t = 0; t < NSL; ++t) {
-          const int slot = slot0 + 32 * t;
-          if (slot < SLOTS) {
-            const float4 v4 = make_float4(o[t].x * inv, o[t].y * inv, o[t].z * inv, o[t].w * inv);
-            const uint32_t off = (uint32_t)((r * kST + h * HD + 4 * slot) * 4);
-            for (int g = kg; g < CL; g += KG) st_cluster4(cluster_map(cb_l, g) + off, v4);
-          }
-        }
+        const float4 v4 = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
+        const uint32_t off = (uint32_t)((r * kST + h * HD + 4 * slot) * 4);
+        for (int g = kg; g < CL; g += KG)
+          st_async4(cluster_map(cb_l, g) + off, v4, cluster_map(bar0 + 8 * PH_CTX, g));
       }
     }
-    cluster_sync();
+    wait_phase(bar0 + 8 * PH_CTX, par, a.status, 0x200 + l);
 
     // ---- out_proj + padded-row zeroing + residual: X[:, own cols] ---------
     smem_gemm<NC>(sCB, wb + 3 * NC * kST, R, [&](int r0, int c0, float (&acc)[2][4], int kq, int ks, bool act) {
@@ -459,12 +471,13 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
       __syncwarp();  // every lane has read X before any lane overwrites it
       for (int g = kq; act && g < CL; g += ks) {
         const uint32_t dst = cluster_map(xs_l, g);
+        const uint32_t rb = cluster_map(bar0 + 8 * PH_X1, g);
 #pragma unroll
         for (int i = 0; i < 2; ++i)
-          if (r0 + i < R) st_cluster4(dst + (uint32_t)(((r0 + i) * kST + col) * 4), v[i]);
+          if (r0 + i < R) st_async4(dst + (uint32_t)(((r0 + i) * kST + col) * 4), v[i], rb);
       }
     });
-    cluster_sync();
+    wait_phase(bar0 + 8 * PH_X1, par, a.status, 0x300 + l);
 
     // ---- LayerNorm2 (local) and ffn_in + exact GELU: CB[:, own cols] -------
     ln_rows(sX, sN, R, aux + 2 * kD, aux + 3 * kD, a.eps, warp, lane);
@@ -479,12 +492,13 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
                            gelu_erf(acc[i][2] + bias[2]), gelu_erf(acc[i][3] + bias[3]));
       for (int g = kq; act && g < CL; g += ks) {
         const uint32_t dst = cluster_map(cb_l, g);
+        const uint32_t rb = cluster_map(bar0 + 8 * PH_H, g);
 #pragma unroll
         for (int i = 0; i < 2; ++i)
-          if (r0 + i < R) st_cluster4(dst + (uint32_t)(((r0 + i) * kST + col) * 4), v[i]);
+          if (r0 + i < R) st_async4(dst + (uint32_t)(((r0 + i) * kST + col) * 4), v[i], rb);
       }
     });
-    cluster_sync();
+    wait_phase(bar0 + 8 * PH_H, par, a.status, 0x400 + l);
 
     // ---- ffn_out + residual + block-end padded-row zeroing -----------------
     smem_gemm<NC>(sCB, wb + 5 * NC * kST, R, [&](int r0, int c0, float (&acc)[2][4], int kq, int ks, bool act) {
@@ -503,12 +517,13 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
       __syncwarp();
       for (int g = kq; act && g < CL; g += ks) {
         const uint32_t dst = cluster_map(xs_l, g);
+        const uint32_t rb = cluster_map(bar0 + 8 * PH_X2, g);
 #pragma unroll
         for (int i = 0; i < 2; ++i)
-          if (r0 + i < R) st_cluster4(dst + (uint32_t)(((r0 + i) * kST + col) * 4), v[i]);
+          if (r0 + i < R) st_async4(dst + (uint32_t)(((r0 + i) * kST + col) * 4), v[i], rb);
       }
     });
-    cluster_sync();
+    wait_phase(bar0 + 8 * PH_X2, par, a.status, 0x500 + l);
   }
 
   // ---- final LayerNorm of this CTA's share of rows, padded rows -> 0 --------
@@ -531,6 +546,8 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
       reinterpret_cast<float4 *>(a.y + (row0 + r) * kD)[lane] = o;
     }
   }
+  // no CTA leaves while a peer could still address its shared memory
+  cluster_sync();
 }
 
 template <int CL, int H>
