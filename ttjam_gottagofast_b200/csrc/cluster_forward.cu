@@ -46,7 +46,7 @@ constexpr int aux_floats(int CL) { return 4 * kD + 6 * (kD / CL); }
 constexpr int wbuf_floats(int CL) { return 6 * (kD / CL) * kST + aux_floats(CL); }
 // Shared-memory floats of one CTA for cluster size CL, H heads, R rows.
 constexpr int cluster_smem_floats(int CL, int H, int R) {
-  return 2 * wbuf_floats(CL) + 3 * R * kST + 3 * R * (kD / H + 4) + R + 16;
+  return 2 * wbuf_floats(CL) + 2 * R * kST + 3 * R * (kD / H + 4) + R + 16;
 }
 // Largest row count per cluster (a multiple of 16, at most 64) that fits the
 // 227 KB of shared memory a CTA may use.
@@ -68,8 +68,7 @@ struct CS {
   static constexpr int HDP = HD + 4;         // head row stride: 16-byte rows, float4 reads conflict-free
   static constexpr int OFF_W = 0;                          // [2][WB]
   static constexpr int OFF_X = OFF_W + 2 * WB;             // [RMAX][kST] residual stream
-  static constexpr int OFF_N = OFF_X + RMAX * kST;         // [RMAX][kST] LayerNorm output
-  static constexpr int OFF_CB = OFF_N + RMAX * kST;        // [RMAX][kST] context / ffn hidden
+  static constexpr int OFF_CB = OFF_X + RMAX * kST;        // [RMAX][kST] context / ffn hidden
   static constexpr int OFF_Q = OFF_CB + RMAX * kST;        // [RMAX][HDP]
   static constexpr int OFF_K = OFF_Q + RMAX * HDP;
   static constexpr int OFF_V = OFF_K + RMAX * HDP;
@@ -206,94 +205,102 @@ __device__ void load_layer_weights(const ClusterArgs &a, int layer, float *wbuf,
   cp_async_commit();
 }
 
-// Row LayerNorm of R rows of `src` (stride kST) into `dst`, one warp per row,
-// two rows in flight per warp so their shuffle chains overlap.
-__device__ void ln_rows(const float *src, float *dst, int R, const float *gamma,
-                        const float *beta, float eps, int warp, int lane) {
-  const float4 g = reinterpret_cast<const float4 *>(gamma)[lane];
-  const float4 b = reinterpret_cast<const float4 *>(beta)[lane];
-  constexpr int NW = kThreads / 32;
-  for (int r0 = warp; r0 < R; r0 += 2 * NW) {
-    const int r1 = r0 + NW < R ? r0 + NW : r0;
-    const float4 v0 = reinterpret_cast<const float4 *>(src + r0 * kST)[lane];
-    const float4 v1 = reinterpret_cast<const float4 *>(src + r1 * kST)[lane];
-    float s0 = (v0.x + v0.y) + (v0.z + v0.w), s1 = (v1.x + v1.y) + (v1.z + v1.w);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-    }
-    const float m0 = s0 * (1.0f / kD), m1 = s1 * (1.0f / kD);
-    const float a0 = v0.x - m0, a1 = v0.y - m0, a2 = v0.z - m0, a3 = v0.w - m0;
-    const float c0 = v1.x - m1, c1 = v1.y - m1, c2 = v1.z - m1, c3 = v1.w - m1;
-    float q0 = (a0 * a0 + a1 * a1) + (a2 * a2 + a3 * a3);
-    float q1 = (c0 * c0 + c1 * c1) + (c2 * c2 + c3 * c3);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      q0 += __shfl_xor_sync(0xffffffffu, q0, o);
-      q1 += __shfl_xor_sync(0xffffffffu, q1, o);
-    }
-    const float rs0 = rsqrtf(q0 * (1.0f / kD) + eps), rs1 = rsqrtf(q1 * (1.0f / kD) + eps);
-    reinterpret_cast<float4 *>(dst + r0 * kST)[lane] =
-        make_float4(a0 * rs0 * g.x + b.x, a1 * rs0 * g.y + b.y, a2 * rs0 * g.z + b.z,
-                    a3 * rs0 * g.w + b.w);
-    if (r1 != r0)
-      reinterpret_cast<float4 *>(dst + r1 * kST)[lane] =
-          make_float4(c0 * rs1 * g.x + b.x, c1 * rs1 * g.y + b.y, c2 * rs1 * g.z + b.z,
-                      c3 * rs1 * g.w + b.w);
+// Y[r][c] = sum_k A'[r][k] * W[c][k] for r < R, c < 8*NBLK, K = 128, where A'
+// is A, or LayerNorm(A) when LN (gamma/beta in shared memory). Both operands in
+// shared memory at stride kST.
+//
+// Warp w handles row pairs (2w, 2w+1) + 16i; lane l owns the K slice
+// [4l, 4l+4), so A' is formed in registers (LayerNorm included) and each W row
+// is one conflict-free 512-byte read per warp. Per block of 8 columns a lane
+// holds 16 partial dot products (2 rows x 8 columns); a butterfly
+// reduce-scatter (16 shuffles) leaves output (row lane>>4, column (lane>>1)&7)
+// on lanes l and l^1, and a 4-shuffle gather gives each group of 8 lanes
+// (same row, same 4-column quad) the quad as a float4.
+// epi(r, c0, v, ls, ok) runs on every lane (warp-uniform, so it may
+// __syncwarp): the float4 v holds columns c0..c0+3 of row r, ls in [0, 8)
+// tells the 8 lanes sharing the quad apart so they can split its
+// destinations, and ok is false for the padding row of an odd row count.
+template <int NBLK, bool LN, typename Epi>
+__device__ __forceinline__ void warp_gemm(const float *A, const float *W, int R,
+                                          const float *gamma, const float *beta, float eps,
+                                          Epi epi) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float4 g4 = make_float4(1.f, 1.f, 1.f, 1.f), b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (LN) {
+    g4 = reinterpret_cast<const float4 *>(gamma)[lane];
+    b4 = reinterpret_cast<const float4 *>(beta)[lane];
   }
-}
-
-// out[r][c] = sum_k A[r][k] * W[c][k] for r < R, c < NCOL, K = 128, both
-// operands in shared memory at stride kST. Work split: 2x4 output micro-tiles,
-// each shared by KS consecutive lanes that split K and butterfly-reduce, so all
-// KS lanes end with the tile's sums. epi(r0, c0, acc, kq, ks, active) runs on
-// every lane (warp-uniform, so it may __syncwarp); lanes of an active tile
-// spread the tile's stores over the ks lanes by kq, inactive lanes store nothing.
-template <int NCOL, typename Epi>
-__device__ __forceinline__ void smem_gemm(const float *A, const float *W, int R, Epi epi) {
-  constexpr int TI = 2, TJ = 4;
-  static_assert(NCOL % TJ == 0, "columns");
-  constexpr int CT = NCOL / TJ;
-  const int tiles = ((R + TI - 1) / TI) * CT;
-  int ks = 1;
-  while (ks < 16 && tiles * ks * 2 <= kThreads) ks <<= 1;
-  const int tid = threadIdx.x;
-  const int kq = tid % ks;
-  // every thread runs the same number of iterations (the shuffles need the
-  // whole warp); lanes past the last tile compute on tile 0 and store nothing
-  for (int base = 0; base < tiles; base += kThreads / ks) {
-    const int t_raw = base + tid / ks;
-    const bool active = t_raw < tiles;
-    const int t = active ? t_raw : 0;
-    const int r0 = (t / CT) * TI, c0 = (t % CT) * TJ;
-    const int r1 = min(r0 + 1, R - 1);
-    float acc[TI][TJ] = {};
-    const float *a0p = A + r0 * kST, *a1p = A + r1 * kST;
-#pragma unroll 4
-    for (int k = kq * 4; k < kD; k += ks * 4) {
-      const float4 a0 = *reinterpret_cast<const float4 *>(a0p + k);
-      const float4 a1 = *reinterpret_cast<const float4 *>(a1p + k);
+  for (int r0 = 2 * warp; r0 < R; r0 += 2 * (kThreads / 32)) {
+    const int r1 = r0 + 1 < R ? r0 + 1 : r0;
+    float4 a0 = reinterpret_cast<const float4 *>(A + r0 * kST)[lane];
+    float4 a1 = reinterpret_cast<const float4 *>(A + r1 * kST)[lane];
+    if (LN) {
+      float s0 = (a0.x + a0.y) + (a0.z + a0.w), s1 = (a1.x + a1.y) + (a1.z + a1.w);
 #pragma unroll
-      for (int j = 0; j < TJ; ++j) {
-        const float4 w = *reinterpret_cast<const float4 *>(W + (c0 + j) * kST + k);
-        acc[0][j] = fmaf(a0.x, w.x, acc[0][j]);
-        acc[0][j] = fmaf(a0.y, w.y, acc[0][j]);
-        acc[0][j] = fmaf(a0.z, w.z, acc[0][j]);
-        acc[0][j] = fmaf(a0.w, w.w, acc[0][j]);
-        acc[1][j] = fmaf(a1.x, w.x, acc[1][j]);
-        acc[1][j] = fmaf(a1.y, w.y, acc[1][j]);
-        acc[1][j] = fmaf(a1.z, w.z, acc[1][j]);
-        acc[1][j] = fmaf(a1.w, w.w, acc[1][j]);
+      for (int o = 16; o > 0; o >>= 1) {
+        s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
       }
-    }
-    for (int off = 1; off < ks; off <<= 1) {
+      const float m0 = s0 * (1.0f / kD), m1 = s1 * (1.0f / kD);
+      a0.x -= m0; a0.y -= m0; a0.z -= m0; a0.w -= m0;
+      a1.x -= m1; a1.y -= m1; a1.z -= m1; a1.w -= m1;
+      float q0 = (a0.x * a0.x + a0.y * a0.y) + (a0.z * a0.z + a0.w * a0.w);
+      float q1 = (a1.x * a1.x + a1.y * a1.y) + (a1.z * a1.z + a1.w * a1.w);
 #pragma unroll
-      for (int i = 0; i < TI; ++i)
-#pragma unroll
-        for (int j = 0; j < TJ; ++j) acc[i][j] += __shfl_xor_sync(0xffffffffu, acc[i][j], off);
+      for (int o = 16; o > 0; o >>= 1) {
+        q0 += __shfl_xor_sync(0xffffffffu, q0, o);
+        q1 += __shfl_xor_sync(0xffffffffu, q1, o);
+      }
+      const float rs0 = rsqrtf(q0 * (1.0f / kD) + eps), rs1 = rsqrtf(q1 * (1.0f / kD) + eps);
+      a0 = make_float4(a0.x * rs0 * g4.x + b4.x, a0.y * rs0 * g4.y + b4.y,
+                       a0.z * rs0 * g4.z + b4.z, a0.w * rs0 * g4.w + b4.w);
+      a1 = make_float4(a1.x * rs1 * g4.x + b4.x, a1.y * rs1 * g4.y + b4.y,
+                       a1.z * rs1 * g4.z + b4.z, a1.w * rs1 * g4.w + b4.w);
     }
-    epi(r0, c0, acc, kq, ks, active);
+#pragma unroll 1
+    for (int cb = 0; cb < NBLK; ++cb) {
+      float p[16];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 w = reinterpret_cast<const float4 *>(W + (cb * 8 + j) * kST)[lane];
+        p[j] = fmaf(a0.x, w.x, fmaf(a0.y, w.y, fmaf(a0.z, w.z, a0.w * w.w)));
+        p[8 + j] = fmaf(a1.x, w.x, fmaf(a1.y, w.y, fmaf(a1.z, w.z, a1.w * w.w)));
+      }
+      // butterfly reduce-scatter of 16 values over 32 lanes
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const bool up = lane & 16;
+        const float send = up ? p[i] : p[i + 8];
+        p[i] = (up ? p[i + 8] : p[i]) + __shfl_xor_sync(0xffffffffu, send, 16);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const bool up = lane & 8;
+        const float send = up ? p[i] : p[i + 4];
+        p[i] = (up ? p[i + 4] : p[i]) + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const bool up = lane & 4;
+        const float send = up ? p[i] : p[i + 2];
+        p[i] = (up ? p[i + 2] : p[i]) + __shfl_xor_sync(0xffffffffu, send, 4);
+      }
+      {
+        const bool up = lane & 2;
+        const float send = up ? p[0] : p[1];
+        p[0] = (up ? p[1] : p[0]) + __shfl_xor_sync(0xffffffffu, send, 2);
+      }
+      p[0] += __shfl_xor_sync(0xffffffffu, p[0], 1);
+      // gather the quad: lanes base, base+2, base+4, base+6 hold its 4 columns
+      const int base = lane & 0x18;
+      float4 v;
+      v.x = __shfl_sync(0xffffffffu, p[0], base + 0);
+      v.y = __shfl_sync(0xffffffffu, p[0], base + 2);
+      v.z = __shfl_sync(0xffffffffu, p[0], base + 4);
+      v.w = __shfl_sync(0xffffffffu, p[0], base + 6);
+      const int r = (lane & 16) ? r0 + 1 : r0;
+      epi(r < R ? r : r0, cb * 8 + ((lane >> 3) & 1) * 4, v, lane & 7, r < R);
+    }
   }
 }
 
@@ -305,7 +312,6 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
   extern __shared__ __align__(128) float sm[];
   float *sW = sm + C::OFF_W;
   float *sX = sm + C::OFF_X;
-  float *sN = sm + C::OFF_N;
   float *sCB = sm + C::OFF_CB;
   float *sQ = sm + C::OFF_Q;
   float *sK = sm + C::OFF_K;
@@ -364,25 +370,16 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
     if (l + 1 < L) cp_async_wait<1>(); else cp_async_wait<0>();
     __syncthreads();  // layer l's weights are visible to every thread
 
-    // ---- LayerNorm1 (local, all rows); q/k/v columns -> head group ---------
-    ln_rows(sX, sN, R, aux, aux + kD, a.eps, warp, lane);
-    __syncthreads();
-    smem_gemm<3 * NC>(sN, wb, R, [&](int r0, int c0, float (&acc)[2][4], int kq, int ks, bool act) {
+    // ---- q/k/v columns of LayerNorm1(X) -> this CTA's head group ----------
+    warp_gemm<3 * NC / 8, true>(sX, wb, R, aux, aux + kD, a.eps,
+                               [&](int r, int c0, float4 v, int ls, bool ok) {
       const int blk = c0 / NC, i0 = c0 % NC;  // 0 = q, 1 = k, 2 = v
       const float *bias = aux + 4 * kD + blk * NC + i0;
-      float4 v[2];
-#pragma unroll
-      for (int i = 0; i < 2; ++i)
-        v[i] = make_float4(acc[i][0] + bias[0], acc[i][1] + bias[1], acc[i][2] + bias[2],
-                           acc[i][3] + bias[3]);
+      v.x += bias[0]; v.y += bias[1]; v.z += bias[2]; v.w += bias[3];
       const uint32_t base = blk == 0 ? q_l : (blk == 1 ? k_l : v_l);
-      for (int g = kq; act && g < G; g += ks) {
-        const uint32_t dst = cluster_map(base, h * G + g);
-        const uint32_t rb = cluster_map(bar0 + 8 * PH_QKV, h * G + g);
-#pragma unroll
-        for (int i = 0; i < 2; ++i)
-          if (r0 + i < R) st_async4(dst + (uint32_t)(((r0 + i) * HDP + sub * NC + i0) * 4), v[i], rb);
-      }
+      const uint32_t off = (uint32_t)((r * HDP + sub * NC + i0) * 4);
+      for (int g = ls; ok && g < G; g += 8)
+        st_async4(cluster_map(base, h * G + g) + off, v, cluster_map(bar0 + 8 * PH_QKV, h * G + g));
     });
     wait_phase(bar0 + 8 * PH_QKV, par, a.status, 0x100 + l);
 
@@ -455,73 +452,49 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
     wait_phase(bar0 + 8 * PH_CTX, par, a.status, 0x200 + l);
 
     // ---- out_proj + padded-row zeroing + residual: X[:, own cols] ---------
-    smem_gemm<NC>(sCB, wb + 3 * NC * kST, R, [&](int r0, int c0, float (&acc)[2][4], int kq, int ks, bool act) {
+    warp_gemm<NC / 8, false>(sCB, wb + 3 * NC * kST, R, nullptr, nullptr, 0.f,
+                             [&](int r, int c0, float4 v, int ls, bool ok) {
       const int col = rank * NC + c0;
       const float *bias = aux + 4 * kD + 3 * NC + c0;
-      float4 v[2];
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int r = min(r0 + i, R - 1);
-        const float4 x4 = *reinterpret_cast<const float4 *>(sX + r * kST + col);
-        v[i] = sValid[r] != 0.f
-                   ? make_float4(x4.x + (acc[i][0] + bias[0]), x4.y + (acc[i][1] + bias[1]),
-                                 x4.z + (acc[i][2] + bias[2]), x4.w + (acc[i][3] + bias[3]))
-                   : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
+      const float4 x4 = *reinterpret_cast<const float4 *>(sX + r * kST + col);
+      const float4 o = sValid[r] != 0.f
+                           ? make_float4(x4.x + (v.x + bias[0]), x4.y + (v.y + bias[1]),
+                                         x4.z + (v.z + bias[2]), x4.w + (v.w + bias[3]))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
       __syncwarp();  // every lane has read X before any lane overwrites it
-      for (int g = kq; act && g < CL; g += ks) {
-        const uint32_t dst = cluster_map(xs_l, g);
-        const uint32_t rb = cluster_map(bar0 + 8 * PH_X1, g);
-#pragma unroll
-        for (int i = 0; i < 2; ++i)
-          if (r0 + i < R) st_async4(dst + (uint32_t)(((r0 + i) * kST + col) * 4), v[i], rb);
-      }
+      const uint32_t off = (uint32_t)((r * kST + col) * 4);
+      for (int g = ls; ok && g < CL; g += 8)
+        st_async4(cluster_map(xs_l, g) + off, o, cluster_map(bar0 + 8 * PH_X1, g));
     });
     wait_phase(bar0 + 8 * PH_X1, par, a.status, 0x300 + l);
 
-    // ---- LayerNorm2 (local) and ffn_in + exact GELU: CB[:, own cols] -------
-    ln_rows(sX, sN, R, aux + 2 * kD, aux + 3 * kD, a.eps, warp, lane);
-    __syncthreads();
-    smem_gemm<NC>(sN, wb + 4 * NC * kST, R, [&](int r0, int c0, float (&acc)[2][4], int kq, int ks, bool act) {
+    // ---- ffn_in + exact GELU on LayerNorm2(X): CB[:, own cols] -------------
+    warp_gemm<NC / 8, true>(sX, wb + 4 * NC * kST, R, aux + 2 * kD, aux + 3 * kD, a.eps,
+                            [&](int r, int c0, float4 v, int ls, bool ok) {
       const int col = rank * NC + c0;
       const float *bias = aux + 4 * kD + 4 * NC + c0;
-      float4 v[2];
-#pragma unroll
-      for (int i = 0; i < 2; ++i)
-        v[i] = make_float4(gelu_erf(acc[i][0] + bias[0]), gelu_erf(acc[i][1] + bias[1]),
-                           gelu_erf(acc[i][2] + bias[2]), gelu_erf(acc[i][3] + bias[3]));
-      for (int g = kq; act && g < CL; g += ks) {
-        const uint32_t dst = cluster_map(cb_l, g);
-        const uint32_t rb = cluster_map(bar0 + 8 * PH_H, g);
-#pragma unroll
-        for (int i = 0; i < 2; ++i)
-          if (r0 + i < R) st_async4(dst + (uint32_t)(((r0 + i) * kST + col) * 4), v[i], rb);
-      }
+      const float4 o = make_float4(gelu_erf(v.x + bias[0]), gelu_erf(v.y + bias[1]),
+                                   gelu_erf(v.z + bias[2]), gelu_erf(v.w + bias[3]));
+      const uint32_t off = (uint32_t)((r * kST + col) * 4);
+      for (int g = ls; ok && g < CL; g += 8)
+        st_async4(cluster_map(cb_l, g) + off, o, cluster_map(bar0 + 8 * PH_H, g));
     });
     wait_phase(bar0 + 8 * PH_H, par, a.status, 0x400 + l);
 
     // ---- ffn_out + residual + block-end padded-row zeroing -----------------
-    smem_gemm<NC>(sCB, wb + 5 * NC * kST, R, [&](int r0, int c0, float (&acc)[2][4], int kq, int ks, bool act) {
+    warp_gemm<NC / 8, false>(sCB, wb + 5 * NC * kST, R, nullptr, nullptr, 0.f,
+                             [&](int r, int c0, float4 v, int ls, bool ok) {
       const int col = rank * NC + c0;
       const float *bias = aux + 4 * kD + 5 * NC + c0;
-      float4 v[2];
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int r = min(r0 + i, R - 1);
-        const float4 x4 = *reinterpret_cast<const float4 *>(sX + r * kST + col);
-        v[i] = sValid[r] != 0.f
-                   ? make_float4(x4.x + (acc[i][0] + bias[0]), x4.y + (acc[i][1] + bias[1]),
-                                 x4.z + (acc[i][2] + bias[2]), x4.w + (acc[i][3] + bias[3]))
-                   : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
+      const float4 x4 = *reinterpret_cast<const float4 *>(sX + r * kST + col);
+      const float4 o = sValid[r] != 0.f
+                           ? make_float4(x4.x + (v.x + bias[0]), x4.y + (v.y + bias[1]),
+                                         x4.z + (v.z + bias[2]), x4.w + (v.w + bias[3]))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
       __syncwarp();
-      for (int g = kq; act && g < CL; g += ks) {
-        const uint32_t dst = cluster_map(xs_l, g);
-        const uint32_t rb = cluster_map(bar0 + 8 * PH_X2, g);
-#pragma unroll
-        for (int i = 0; i < 2; ++i)
-          if (r0 + i < R) st_async4(dst + (uint32_t)(((r0 + i) * kST + col) * 4), v[i], rb);
-      }
+      const uint32_t off = (uint32_t)((r * kST + col) * 4);
+      for (int g = ls; ok && g < CL; g += 8)
+        st_async4(cluster_map(xs_l, g) + off, o, cluster_map(bar0 + 8 * PH_X2, g));
     });
     wait_phase(bar0 + 8 * PH_X2, par, a.status, 0x500 + l);
   }
