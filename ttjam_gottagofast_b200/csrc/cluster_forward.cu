@@ -366,8 +366,9 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
       mbar_expect_tx(bar0 + 8 * PH_H, e_row);
       mbar_expect_tx(bar0 + 8 * PH_X2, e_row);
     }
-    if (l >= 1 && l + 1 < L) load_layer_weights<CL, H>(a, l + 1, sW + ((l + 1) & 1) * C::WB, rank);
-    if (l + 1 < L) cp_async_wait<1>(); else cp_async_wait<0>();
+    // layer l's weights: copied since kernel start (l <= 1) or since layer
+    // l-1's q/k/v step; at l = 0 layer 1's group may stay in flight
+    if (l == 0 && L > 1) cp_async_wait<1>(); else cp_async_wait<0>();
     __syncthreads();  // layer l's weights are visible to every thread
 
     // ---- q/k/v columns of LayerNorm1(X) -> this CTA's head group ----------
@@ -381,6 +382,10 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
       for (int g = ls; ok && g < G; g += 8)
         st_async4(cluster_map(base, h * G + g) + off, v, cluster_map(bar0 + 8 * PH_QKV, h * G + g));
     });
+    // start copying layer l+1's weights into the buffer layer l-1 used (free
+    // since the layer-start barrier) while the q/k/v exchange is in flight;
+    // layers 0 and 1 were issued at kernel start
+    if (l >= 1 && l + 1 < L) load_layer_weights<CL, H>(a, l + 1, sW + ((l + 1) & 1) * C::WB, rank);
     wait_phase(bar0 + 8 * PH_QKV, par, a.status, 0x100 + l);
 
     // ---- attention for head h, query rows r = sub (mod G), a warp per row --
@@ -403,17 +408,17 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
           float s = -CUDART_INF_F;
           if (j < kend && sValid[kbase + j] != 0.f) {
             const float *kr = sK + (kbase + j) * HDP;
-            float dot = 0.f;
+            float d0 = 0.f, d1 = 0.f;  // two chains halve the FMA latency path
 #pragma unroll
             for (int d = 0; d < HD; d += 4) {
               const float4 q4 = *reinterpret_cast<const float4 *>(qr + d);
               const float4 k4 = *reinterpret_cast<const float4 *>(kr + d);
-              dot = fmaf(q4.x, k4.x, dot);
-              dot = fmaf(q4.y, k4.y, dot);
-              dot = fmaf(q4.z, k4.z, dot);
-              dot = fmaf(q4.w, k4.w, dot);
+              d0 = fmaf(q4.x, k4.x, d0);
+              d1 = fmaf(q4.y, k4.y, d1);
+              d0 = fmaf(q4.z, k4.z, d0);
+              d1 = fmaf(q4.w, k4.w, d1);
             }
-            s = dot * a.scale;
+            s = (d0 + d1) * a.scale;
           }
           const float mn = fmaxf(m, warp_max(s));
           if (mn == -CUDART_INF_F) continue;  // no allowed key yet (uniform across the warp)
