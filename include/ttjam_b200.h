@@ -125,6 +125,33 @@ int tt_forward_plan(const tt_config *cfg, int64_t batch, int64_t seq);
  * sees per forward). Negative on error. */
 int tt_forward_launch_count(const tt_config *cfg, int64_t batch, int64_t seq);
 
+/* Bytes of the device scratch array behind tt_forward_noalloc. */
+#define TT_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+
+/* tt_forward for callers that cannot allocate device memory when they run the
+ * forward pass: a plugin whose host owns the whole device-memory budget, a
+ * serving loop that may not call cudaMalloc (it can synchronise the device),
+ * or a process whose device memory already belongs to its own pool. It takes
+ * no workspace: its per-call scratch is a TT_NOALLOC_SCRATCH_BYTES (16 MiB)
+ * array of static device memory inside the library, which every GPU that
+ * loads the library holds until the process exits. It calls no allocator.
+ *
+ * It runs the per-op schedule (TT_PLAN_OPS_*; TT_PLAN_AUTO picks the one
+ * tt_forward uses when it does not take the single-launch path, and
+ * TT_PLAN_CLUSTER, which needs no scratch, is TT_ERR_UNSUPPORTED). A call
+ * whose scratch (tt_workspace_bytes of that schedule) exceeds the array is
+ * rejected with TT_ERR_WORKSPACE and a message giving both sizes.
+ *
+ * The first call on each device looks up the array's device address (with
+ * that device current) and caches it; make that first call before any stream
+ * capture. All calls share the one array: calls whose GPU work overlaps
+ * (unordered streams, concurrent host threads) race on it. Nothing in it needs
+ * to start at zero. Arguments as for tt_forward. This entry point has no
+ * counterpart in the reference. */
+int tt_forward_noalloc(const tt_config *cfg, const void *image, const float *x,
+                       const uint8_t *mask, int64_t batch, int64_t seq, float *y,
+                       void *stream);
+
 /* Synchronises `stream`, reads and clears the image's device status word.
  * *code receives TT_OK or the latched device error (TT_ERR_DEVICE_*),
  * *detail a kernel-specific location code. Returns TT_OK unless the read

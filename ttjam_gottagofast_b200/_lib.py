@@ -22,6 +22,9 @@ TT_ERR_CUDA = -5
 TT_ERR_DEVICE_TIMEOUT = -6
 TT_ERR_DEVICE_FAULT = -7
 
+# Size of the library's fixed scratch array behind tt_forward_noalloc.
+TT_NOALLOC_SCRATCH_BYTES = 16 << 20
+
 PLAN_NAMES = {1: "cluster", 2: "ops_ffma", 3: "ops_tc3xtf32"}
 PLAN_IDS = {"auto": 0, **{v: k for k, v in PLAN_NAMES.items()}}
 
@@ -29,8 +32,7 @@ PLAN_IDS = {"auto": 0, **{v: k for k, v in PLAN_NAMES.items()}}
 EXPORTED = (
     "tt_abi_version", "tt_validate_config", "tt_image_bytes", "tt_pack_image",
     "tt_workspace_bytes", "tt_forward", "tt_forward_plan", "tt_forward_launch_count",
-    "tt_read_status",
-    "tt_last_error",
+    "tt_read_status", "tt_last_error", "tt_forward_noalloc",
 )
 
 
@@ -87,6 +89,8 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         lib.tt_forward_plan.argtypes = [cfgp, i64, i64]
         lib.tt_forward_launch_count.restype = ctypes.c_int
         lib.tt_forward_launch_count.argtypes = [cfgp, i64, i64]
+        lib.tt_forward_noalloc.restype = ctypes.c_int
+        lib.tt_forward_noalloc.argtypes = [cfgp, vp, vp, vp, i64, i64, vp, vp]
         lib.tt_read_status.restype = ctypes.c_int
         lib.tt_read_status.argtypes = [cfgp, vp, ctypes.POINTER(i32), ctypes.POINTER(i32), vp]
         lib.tt_last_error.restype = ctypes.c_int

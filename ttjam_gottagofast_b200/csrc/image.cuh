@@ -100,5 +100,9 @@ struct WorkspaceLayout {
 };
 
 int validate_config(const tt_config *cfg);
+int forward_plan(const tt_config *cfg, int64_t batch, int64_t seq);
+int forward_ops(const tt_config &cfg, const ImageLayout &L, const char *image, const float *x,
+                const uint8_t *mask, int64_t batch, int64_t seq, float *y,
+                const WorkspaceLayout &W, char *ws, cudaStream_t stream);
 
 }  // namespace tt
