@@ -21,7 +21,7 @@ LIB_NAME = "libttjam_b200.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
 
 SOURCES = ["api.cu", "layernorm.cu", "gemm_ffma.cu", "attention_ffma.cu", "cluster_forward.cu",
-           "noalloc.cu"]
+           "gemm_tc.cu", "noalloc.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -62,7 +62,7 @@ def build(force: bool = False, verbose: bool = False, extra_flags=None) -> str:
     tmp = LIB_PATH + ".tmp"
     cmd = [nvcc_path(), *NVCC_FLAGS, *(extra_flags or []),
            "-I", os.path.join(ROOT, "include"), "-I", CSRC,
-           "-o", tmp, *_sources(), "-lcuda"]
+           "-o", tmp, *_sources()]
     if verbose:
         print(" ".join(cmd), flush=True)
     res = subprocess.run(cmd, capture_output=True, text=True)

@@ -4,6 +4,7 @@
 #include <string>
 
 #include "cluster_forward.cuh"
+#include "gemm_tc.cuh"
 #include "image.cuh"
 #include "tt_common.cuh"
 
@@ -154,6 +155,66 @@ int forward_ops(const tt_config &cfg, const ImageLayout &L, const char *image, c
                           eps, stream);
 }
 
+// Per-op schedule with 3xTF32 tensor-core GEMMs (d_model >= 512): per layer
+// LN1 -> TF32 split, q|k|v GEMM, attention (writes the split context),
+// out_proj GEMM + residual, LN2 -> split, ffn_in GEMM + GELU (writes the split
+// hidden), ffn_out GEMM + residual; then the final LayerNorm.
+int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image, const float *x,
+                   const uint8_t *mask, int64_t batch, int64_t seq, float *y,
+                   const WorkspaceLayout &W, char *ws, cudaStream_t stream) {
+  const int D = cfg.d_model, F = cfg.ffn_dim, H = cfg.num_heads, hd = D / H;
+  const int64_t T = batch * seq;
+  if (T > INT32_MAX) return fail(TT_ERR_UNSUPPORTED, "tensor-core schedule: too many tokens");
+  auto WS = [&](size_t off) { return reinterpret_cast<float *>(ws + off); };
+  float *qkv = WS(W.qkv);
+  float *ln_hi = WS(W.ln_hi), *ln_lo = WS(W.ln_lo);
+  float *ctx_hi = WS(W.ctx_hi), *ctx_lo = WS(W.ctx_lo);
+  float *h_hi = WS(W.h_hi), *h_lo = WS(W.h_lo);
+  DeviceStatus *status = reinterpret_cast<DeviceStatus *>(const_cast<char *>(image) + L.status);
+  const float eps = 1e-5f;
+  for (int l = 0; l < cfg.num_layers; ++l) {
+    const LayerOffsets &o = L.layer[l];
+    auto P = [&](size_t off) { return reinterpret_cast<const float *>(image + off); };
+    const float *xin = (l == 0) ? x : y;
+    int rc;
+    if ((rc = launch_layernorm(xin, nullptr, ln_hi, ln_lo, P(o.ln1_w), P(o.ln1_b), nullptr, 0, T,
+                               D, eps, stream)) != TT_OK)
+      return rc;
+    TcGemmParams g{};
+    g.A_hi = ln_hi; g.A_lo = ln_lo; g.lda = D; g.W_hi = P(o.wqkv_hi); g.W_lo = P(o.wqkv_lo);
+    g.bias = P(o.bqkv); g.C = qkv; g.ldc = 3LL * D; g.status = status;
+    g.M = (int)T; g.N = 3 * D; g.K = D; g.epilogue = EPI_BIAS;
+    if ((rc = launch_gemm_tc3(g, stream)) != TT_OK) return rc;
+    AttentionParams a{};
+    a.qkv = qkv; a.ctx = nullptr; a.ctx_hi = ctx_hi; a.ctx_lo = ctx_lo; a.mask = mask;
+    a.batch = batch; a.seq = (int)seq; a.d_model = D; a.num_heads = H; a.head_dim = hd;
+    a.causal = cfg.causal; a.scale = (float)(1.0 / std::sqrt((double)hd));
+    if ((rc = launch_attention_ffma(a, stream)) != TT_OK) return rc;
+    TcGemmParams go{};
+    go.A_hi = ctx_hi; go.A_lo = ctx_lo; go.lda = D; go.W_hi = P(o.wo_hi); go.W_lo = P(o.wo_lo);
+    go.bias = P(o.bo); go.R = xin; go.C = y; go.ldc = D; go.row_mask = mask; go.status = status;
+    go.M = (int)T; go.N = D; go.K = D; go.epilogue = EPI_BIAS_RESIDUAL;
+    if ((rc = launch_gemm_tc3(go, stream)) != TT_OK) return rc;
+    if ((rc = launch_layernorm(y, nullptr, ln_hi, ln_lo, P(o.ln2_w), P(o.ln2_b), nullptr, 0, T, D,
+                               eps, stream)) != TT_OK)
+      return rc;
+    TcGemmParams g1{};
+    g1.A_hi = ln_hi; g1.A_lo = ln_lo; g1.lda = D; g1.W_hi = P(o.w1_hi); g1.W_lo = P(o.w1_lo);
+    g1.bias = P(o.b1); g1.C_hi = h_hi; g1.C_lo = h_lo; g1.ldc = F; g1.status = status;
+    g1.M = (int)T; g1.N = F; g1.K = D; g1.epilogue = EPI_BIAS_GELU;
+    if ((rc = launch_gemm_tc3(g1, stream)) != TT_OK) return rc;
+    TcGemmParams g2{};
+    g2.A_hi = h_hi; g2.A_lo = h_lo; g2.lda = F; g2.W_hi = P(o.w2_hi); g2.W_lo = P(o.w2_lo);
+    g2.bias = P(o.b2); g2.R = y; g2.C = y; g2.ldc = D; g2.row_mask = mask; g2.status = status;
+    g2.M = (int)T; g2.N = D; g2.K = F; g2.epilogue = EPI_BIAS_RESIDUAL;
+    if ((rc = launch_gemm_tc3(g2, stream)) != TT_OK) return rc;
+  }
+  return launch_layernorm(y, y, nullptr, nullptr,
+                          reinterpret_cast<const float *>(image + L.final_w),
+                          reinterpret_cast<const float *>(image + L.final_b), mask, 1, T, D,
+                          eps, stream);
+}
+
 }  // namespace tt
 
 using namespace tt;
@@ -238,6 +299,7 @@ int tt_forward_launch_count(const tt_config *cfg, int64_t batch, int64_t seq) {
   const int plan = forward_plan(cfg, batch, seq);
   if (plan < 0) return plan;
   if (plan == PLAN_CLUSTER) return 1;
+  if (plan == PLAN_OPS_TC) return 7 * cfg->num_layers + 1;
   return 5 * cfg->num_layers + 1;
 }
 
@@ -266,6 +328,9 @@ int tt_forward(const tt_config *cfg, const void *image, const float *x, const ui
   if (workspace_bytes < W.total || (W.total > 0 && workspace == nullptr))
     return fail(TT_ERR_WORKSPACE, "tt_forward: workspace smaller than tt_workspace_bytes (" +
                                       std::to_string(W.total) + " bytes)");
+  if (plan == PLAN_OPS_TC)
+    return forward_ops_tc(*cfg, L, static_cast<const char *>(image), x, mask, batch, seq, y, W,
+                          static_cast<char *>(workspace), stream);
   return forward_ops(*cfg, L, static_cast<const char *>(image), x, mask, batch, seq, y, W,
                      static_cast<char *>(workspace), stream);
 }

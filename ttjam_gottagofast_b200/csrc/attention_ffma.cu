@@ -161,12 +161,11 @@ __global__ void __launch_bounds__(kThreads) attention_ffma_kernel(AttentionParam
 
   if (!row_in) return;
   const float inv = l > 0.f ? 1.f / l : 0.f;
-  float *dst = p.ctx + tok * D + (int64_t)h * hd + part * P;
 #pragma unroll
   for (int d = 0; d < P; ++d) {
     if (part * P + d < hd) {
       const float v = o[d] * inv;
-      dst[d] = v;
+      if (p.ctx != nullptr) p.ctx[tok * D + (int64_t)h * hd + part * P + d] = v;
       if (p.ctx_hi != nullptr) {
         const float hv = tf32_round(v);
         p.ctx_hi[tok * D + (int64_t)h * hd + part * P + d] = hv;

@@ -145,15 +145,17 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// Bounded wait for one exchange phase. Gives up after ~2^31 cycles (about a
-// second) and latches a timeout; the caller carries on so that every CTA still
-// reaches the closing cluster barrier.
+// Bounded wait for one exchange phase. Gives up after ~2^28 cycles (~0.14 s),
+// or at once when a wait anywhere in the launch already gave up, and latches a
+// timeout; the caller carries on so that every CTA still reaches the closing
+// cluster barrier.
 __device__ __forceinline__ void wait_phase(uint32_t bar, uint32_t parity, DeviceStatus *st,
                                            int code) {
   if (mbar_try_wait(bar, parity)) return;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > (1LL << 31)) {
+    if (st != nullptr && *reinterpret_cast<volatile int32_t *>(&st->code) != 0) return;
+    if (clock64() - t0 > (1LL << 28)) {
       raise_status(st, TT_ERR_DEVICE_TIMEOUT, code);
       return;
     }

@@ -1,0 +1,342 @@
+// 3xTF32 tensor-core GEMM on sm_100a (tcgen05 + TMA + TMEM):
+//   C[M,N] = epilogue(A[M,K] . W[N,K]^T) in fp32 accuracy.
+//
+// Split-precision product (Ootomo & Yokota 2022, "Recovering single precision
+// accuracy from Tensor Cores while surpassing the FP32 theoretical peak
+// performance"): every operand arrives as a TF32 pair x = x_hi + x_lo (x_hi =
+// x rounded to TF32, x_lo = x - x_hi, exact in fp32), and
+//   A.W^T ~= A_hi.W_hi^T + A_hi.W_lo^T + A_lo.W_hi^T
+// accumulated in fp32 in tensor memory; the dropped A_lo.W_lo^T term is about
+// 2^-22 of the product. Plain TF32 fails the reference's accuracy gate
+// (max abs error 2e-3..9e-3 on the reference's own TF32 kernels); this keeps
+// fp32-level error.
+//
+// Used for the per-token projections when d_model >= 512: q|k|v
+// (torch_transformer_benchmark.py:93-95), out_proj + residual (:118-121, :140),
+// ffn_in + GELU and ffn_out + residual (:141-144).
+//
+// CTA = one 128x128 output tile, 256 threads, warp-specialised:
+//   warp 0  TMA producer: 4 tiles per k-block (A_hi, A_lo, W_hi, W_lo; 128 rows
+//           x 32 fp32 = one 128-byte swizzle row each) into a 3-stage ring;
+//   warp 1  MMA issuer (one thread): per k-block 4 k-steps x 3 products of
+//           tcgen05.mma.cta_group::1.kind::tf32 M128 N128 K8, then
+//           tcgen05.commit frees the stage; a final commit signals the epilogue;
+//   warp 2  allocates / frees the 128 TMEM columns of the accumulator;
+//   warps 4-7 epilogue: tcgen05.ld 32x32b (TMEM lane = tile row), bias,
+//           GELU / residual / padded-row zeroing, fp32 and/or TF32-split stores.
+// Every mbarrier wait is bounded; a wait that gives up latches
+// TT_ERR_DEVICE_TIMEOUT and the kernel still frees its TMEM and returns.
+// No TMA load here uses cluster multicast.
+#include <cuda.h>
+
+#include "gemm_tc.cuh"
+
+namespace tt {
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
+constexpr int kThreads = 256;
+constexpr uint32_t TILE_A = BM * BK * 4;               // 16 KB
+constexpr uint32_t TILE_W = BN * BK * 4;               // 16 KB
+constexpr uint32_t STAGE_BYTES = 2 * TILE_A + 2 * TILE_W;
+constexpr uint32_t TMEM_COLS = BN;                      // fp32 accumulator, 128 lanes x BN
+constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+
+// ---- PTX helpers ------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// Bounded wait: false (and a latched timeout) after ~2^28 cycles (~0.14 s),
+// or at once when an earlier wait anywhere in the launch already gave up, so
+// a broken pipeline costs one timeout, not one per CTA and k-block.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, DeviceStatus *st,
+                                          int detail) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (st != nullptr && *reinterpret_cast<volatile int32_t *>(&st->code) != 0) return false;
+    if (clock64() - t0 > (1LL << 28)) {
+      raise_status(st, TT_ERR_DEVICE_TIMEOUT, detail);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *tm, int c0, int c1,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+// UMMA shared-memory descriptor, K-major, 128-byte swizzle: rows of 128 bytes,
+// 8-row groups 1024 bytes apart (SBO), LBO unused (1), version 1 (sm_100).
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;                 // LBO (16-byte units)
+  d |= (uint64_t)(1024 >> 4) << 32;       // SBO (16-byte units)
+  d |= (uint64_t)1 << 46;                 // descriptor version
+  d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
+  return d;
+}
+// Instruction descriptor: D fp32, A/B tf32, both K-major, N = BN, M = BM.
+constexpr uint32_t kIdescTF32 = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(kIdescTF32), "r"(accum)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
+                    const __grid_constant__ CUtensorMap tm_a_lo,
+                    const __grid_constant__ CUtensorMap tm_w_hi,
+                    const __grid_constant__ CUtensorMap tm_w_lo, const TcGemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  // SW128 tiles need 1024-byte alignment
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t bars = base + STAGES * STAGE_BYTES;   // full[S] | empty[S] | acc | tmem addr
+  auto full_bar = [&](int s) { return bars + 8u * s; };
+  auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
+  const uint32_t acc_bar = bars + 8u * (2 * STAGES);
+  const uint32_t tmem_slot = acc_bar + 8u;
+  uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const int KB = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    mbar_init(acc_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot_ptr;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer --------------------------------------------------------
+    for (int kb = 0; kb < KB; ++kb) {
+      const int s = kb % STAGES, n = kb / STAGES;
+      if (kb >= STAGES) mbar_wait(empty_bar(s), (n - 1) & 1, p.status, 0x1000 + kb);
+      const uint32_t st = base + s * STAGE_BYTES;
+      mbar_expect_tx(full_bar(s), STAGE_BYTES);
+      tma_load_2d(st, &tm_a_hi, kb * BK, m0, full_bar(s));
+      tma_load_2d(st + TILE_A, &tm_a_lo, kb * BK, m0, full_bar(s));
+      tma_load_2d(st + 2 * TILE_A, &tm_w_hi, kb * BK, n0, full_bar(s));
+      tma_load_2d(st + 2 * TILE_A + TILE_W, &tm_w_lo, kb * BK, n0, full_bar(s));
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----------------------------------------------------------
+    for (int kb = 0; kb < KB; ++kb) {
+      const int s = kb % STAGES, n = kb / STAGES;
+      mbar_wait(full_bar(s), n & 1, p.status, 0x2000 + kb);
+      tc_fence_after();
+      const uint32_t st = base + s * STAGE_BYTES;
+#pragma unroll
+      for (int k = 0; k < BK / 8; ++k) {  // K = 8 tf32 = 32 bytes per MMA
+        const uint64_t a_hi = umma_desc_sw128(st + k * 32);
+        const uint64_t a_lo = umma_desc_sw128(st + TILE_A + k * 32);
+        const uint64_t w_hi = umma_desc_sw128(st + 2 * TILE_A + k * 32);
+        const uint64_t w_lo = umma_desc_sw128(st + 2 * TILE_A + TILE_W + k * 32);
+        umma_tf32(tmem_base, a_hi, w_hi, (kb | k) != 0);
+        umma_tf32(tmem_base, a_hi, w_lo, 1);
+        umma_tf32(tmem_base, a_lo, w_hi, 1);
+      }
+      umma_commit(empty_bar(s));  // stage s is free once these MMAs have read it
+    }
+    umma_commit(acc_bar);  // accumulator complete
+  } else if (warp >= 4) {
+    // ---- epilogue: TMEM -> registers -> global -------------------------------
+    const int q = warp & 3;                    // TMEM lane quarter of this warp
+    const int row = m0 + q * 32 + lane;        // TMEM lane = tile row
+    bool ok = mbar_wait(acc_bar, 0, p.status, 0x3000);
+    if (!ok) ok = mbar_wait(acc_bar, 0, p.status, 0x3001);  // one more bounded wait for MMAs in flight
+    tc_fence_after();
+    const bool row_in = row < p.M;
+    const bool valid = row_in && (p.row_mask == nullptr || p.row_mask[row] != 0);
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      float v[16];
+      tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+      const int col0 = n0 + c0;
+      if (!row_in || col0 >= p.N) continue;
+      const bool full = col0 + 16 <= p.N;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int col = col0 + j;
+        float x = (full || col < p.N) ? v[j] + p.bias[col] : 0.f;
+        if (p.epilogue == EPI_BIAS_GELU) x = gelu_erf(x);
+        v[j] = x;
+      }
+      const int64_t off = (int64_t)row * p.ldc + col0;
+      if (p.epilogue == EPI_BIAS_RESIDUAL) {
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+          if (!full && col0 + j >= p.N) break;
+          const float4 r4 = *reinterpret_cast<const float4 *>(p.R + off + j);
+          v[j + 0] = valid ? r4.x + v[j + 0] : 0.f;
+          v[j + 1] = valid ? r4.y + v[j + 1] : 0.f;
+          v[j + 2] = valid ? r4.z + v[j + 2] : 0.f;
+          v[j + 3] = valid ? r4.w + v[j + 3] : 0.f;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 16; j += 4) {
+        if (!full && col0 + j >= p.N) break;
+        const float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        if (p.C != nullptr) *reinterpret_cast<float4 *>(p.C + off + j) = o;
+        if (p.C_hi != nullptr) {
+          float4 h, l;
+          h.x = tf32_round(o.x); l.x = o.x - h.x;
+          h.y = tf32_round(o.y); l.y = o.y - h.y;
+          h.z = tf32_round(o.z); l.z = o.z - h.z;
+          h.w = tf32_round(o.w); l.w = o.w - h.w;
+          *reinterpret_cast<float4 *>(p.C_hi + off + j) = h;
+          *reinterpret_cast<float4 *>(p.C_lo + off + j) = l;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// cuTensorMapEncodeTiled, resolved at run time through the runtime's driver
+// entry-point query so the library has no link-time dependency on libcuda.
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int encode_fn(EncodeTiledFn *out) {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    TT_CUDA_TRY(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    if (p == nullptr || q != cudaDriverEntryPointSuccess)
+      return fail(TT_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  *out = fn;
+  return TT_OK;
+}
+
+// 2-D fp32 tensor map over a row-major [rows, cols] matrix (leading dimension
+// ld floats), box = 32 columns (128 bytes) x box_rows rows, 128-byte swizzle,
+// zero fill outside the matrix.
+int make_tmap(CUtensorMap *tm, const float *ptr, int64_t rows, int64_t cols, int64_t ld,
+              int box_rows) {
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0 || (ld * 4) % 16 != 0)
+    return fail(TT_ERR_INVALID_ARGUMENT, "gemm_tc: operands must be 16-byte aligned with ld % 4 == 0");
+  EncodeTiledFn encode;
+  int rc = encode_fn(&encode);
+  if (rc != TT_OK) return rc;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(ptr), dims,
+                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(TT_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string((int)r));
+  return TT_OK;
+}
+
+}  // namespace
+
+int launch_gemm_tc3(const TcGemmParams &p, cudaStream_t stream) {
+  if (p.M <= 0 || p.N <= 0) return TT_OK;
+  if (p.K <= 0 || p.K % 4 != 0 || p.N % 4 != 0 || p.ldc % 4 != 0)
+    return fail(TT_ERR_UNSUPPORTED, "gemm_tc: K, N and ldc must be multiples of 4");
+  if (p.M > INT32_MAX - BM || (int64_t)(p.M + BM - 1) / BM > 65535)
+    return fail(TT_ERR_UNSUPPORTED, "gemm_tc: too many rows");
+  CUtensorMap ta_hi, ta_lo, tw_hi, tw_lo;
+  int rc;
+  if ((rc = make_tmap(&ta_hi, p.A_hi, p.M, p.K, p.lda, BM)) ||
+      (rc = make_tmap(&ta_lo, p.A_lo, p.M, p.K, p.lda, BM)) ||
+      (rc = make_tmap(&tw_hi, p.W_hi, p.N, p.K, p.K, BN)) ||
+      (rc = make_tmap(&tw_lo, p.W_lo, p.N, p.K, p.K, BN)))
+    return rc;
+  static bool attr_set = false;
+  if (!attr_set) {
+    TT_CUDA_TRY(cudaFuncSetAttribute(gemm_tc3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)SMEM_BYTES));
+    attr_set = true;
+  }
+  dim3 grid((unsigned)((p.N + BN - 1) / BN), (unsigned)((p.M + BM - 1) / BM));
+  gemm_tc3_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(ta_hi, ta_lo, tw_hi, tw_lo, p);
+  TT_LAUNCH_CHECK("gemm_tc3");
+  return TT_OK;
+}
+
+}  // namespace tt

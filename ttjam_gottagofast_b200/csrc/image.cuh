@@ -24,10 +24,7 @@ enum ForwardPlan : int { PLAN_CLUSTER = 1, PLAN_OPS_FFMA = 2, PLAN_OPS_TC = 3 };
 
 // The 3xTF32 tensor-core GEMMs take over where d_model >= 512 makes every
 // projection a large dense contraction.
-inline bool uses_tensor_cores(const tt_config &cfg) {
-  (void)cfg;
-  return false;
-}
+inline bool uses_tensor_cores(const tt_config &cfg) { return cfg.d_model >= 512; }
 
 struct LayerOffsets {
   size_t ln1_w, ln1_b, wqkv, bqkv, wo, bo, ln2_w, ln2_b, w1, b1, w2, b2;
@@ -77,10 +74,12 @@ struct WorkspaceLayout {
   size_t qkv = 0, ctx = 0, h = 0;
   size_t ln_hi = 0, ln_lo = 0, ctx_hi = 0, ctx_lo = 0, h_hi = 0, h_lo = 0;
   size_t total = 0;
+  bool tensor = false;  // buffers of the tensor-core schedule
 
   WorkspaceLayout(const tt_config &cfg, int64_t batch, int64_t seq) {
     const size_t T = (size_t)batch * (size_t)seq, D = cfg.d_model, F = cfg.ffn_dim;
     const size_t f4 = sizeof(float);
+    tensor = uses_tensor_cores(cfg) && cfg.plan != TT_PLAN_OPS_FFMA;
     size_t cur = 0;
     auto take = [&](size_t n_floats) {
       const size_t off = cur;
@@ -88,12 +87,14 @@ struct WorkspaceLayout {
       return off;
     };
     qkv = take(T * 3 * D);
-    ctx = take(T * D);
-    h = take(T * F);
-    if (uses_tensor_cores(cfg)) {
+    if (tensor) {
+      // A operands of the 3xTF32 GEMMs, as TF32 hi/lo pairs
       ln_hi = take(T * D); ln_lo = take(T * D);
       ctx_hi = take(T * D); ctx_lo = take(T * D);
       h_hi = take(T * F); h_lo = take(T * F);
+    } else {
+      ctx = take(T * D);
+      h = take(T * F);
     }
     total = cur;
   }
@@ -104,5 +105,8 @@ int forward_plan(const tt_config *cfg, int64_t batch, int64_t seq);
 int forward_ops(const tt_config &cfg, const ImageLayout &L, const char *image, const float *x,
                 const uint8_t *mask, int64_t batch, int64_t seq, float *y,
                 const WorkspaceLayout &W, char *ws, cudaStream_t stream);
+int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image, const float *x,
+                   const uint8_t *mask, int64_t batch, int64_t seq, float *y,
+                   const WorkspaceLayout &W, char *ws, cudaStream_t stream);
 
 }  // namespace tt

@@ -50,7 +50,7 @@ __global__ void __launch_bounds__(256) layernorm_vec_kernel(
   }
   const float rstd = rsqrtf(warp_sum(ss) / (float)d + eps);
   const bool zero = zero_masked_rows && row_mask != nullptr && row_mask[row] == 0;
-  float4 *yr = reinterpret_cast<float4 *>(y + row * d);
+  float4 *yr = y != nullptr ? reinterpret_cast<float4 *>(y + row * d) : nullptr;
   const float4 *g4 = reinterpret_cast<const float4 *>(gamma);
   const float4 *b4 = reinterpret_cast<const float4 *>(beta);
 #pragma unroll
@@ -67,7 +67,7 @@ __global__ void __launch_bounds__(256) layernorm_vec_kernel(
         o.z = (v[i].z - mean) * rstd * g.z + b.z;
         o.w = (v[i].w - mean) * rstd * g.w + b.w;
       }
-      yr[c] = o;
+      if (y != nullptr) yr[c] = o;
       if (y_hi != nullptr) {
         float4 h, l;
         h.x = tf32_round(o.x); l.x = o.x - h.x;
@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(256) layernorm_generic_kernel(
   // each element below is read and written by the same lane.
   for (int c = lane; c < d; c += 32) {
     const float o = zero ? 0.f : (xr[c] - mean) * rstd * gamma[c] + beta[c];
-    y[row * d + c] = o;
+    if (y != nullptr) y[row * d + c] = o;
     if (y_hi != nullptr) {
       const float h = tf32_round(o);
       y_hi[row * d + c] = h;

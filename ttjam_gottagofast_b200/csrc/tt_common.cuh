@@ -69,7 +69,8 @@ __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a -
 
 // Row LayerNorm, nn.LayerNorm(D) semantics (eps, biased variance). If
 // `zero_rows_mask` is set, rows whose mask byte is 0 are written as 0.
-// If y_hi/y_lo are given, also writes the TF32 split of the output.
+// If y_hi/y_lo are given, also writes the TF32 split of the output (y may then
+// be null).
 int launch_layernorm(const float *x, float *y, float *y_hi, float *y_lo, const float *gamma,
                      const float *beta, const uint8_t *row_mask, int zero_masked_rows,
                      int64_t rows, int d, float eps, cudaStream_t stream);
@@ -102,7 +103,7 @@ int launch_gemm_ffma(const GemmParams &p, cudaStream_t stream);
 
 struct AttentionParams {
   const float *qkv;      // [B*S, 3D]: q | k | v, head h at columns h*hd..h*hd+hd-1
-  float *ctx;            // [B*S, D]
+  float *ctx;            // [B*S, D], or null when only the split is wanted
   float *ctx_hi, *ctx_lo;  // optional TF32 split copies
   const uint8_t *mask;   // [B, S] or null
   int64_t batch;
