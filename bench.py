@@ -98,14 +98,14 @@ def max_over_ranks(v, world):
 
 
 def per_rank_batch(w, world, rank):
-    """Batch rows this rank owns: E splits its batch of 64 contiguously (strong
-    scaling); every other workload gives each rank a full batch (weak scaling)."""
+    """Batch rows this rank owns: E splits its batch of 64 into contiguous
+    slices (strong scaling, shard_range); every other workload gives each rank
+    a full batch of its own (weak scaling)."""
+    from ttjam_gottagofast_b200.shard import shard_range
     b = w.config.batch_size
     if w.name == "E":
-        if b % world:
-            raise SystemExit(f"batch {b} does not split over {world} GPUs")
-        per = b // world
-        return rank * per, per, "strong"
+        start, count = shard_range(b, world, rank)
+        return start, count, "strong"
     return 0, b, "weak"
 
 
@@ -331,7 +331,7 @@ def run_ours(args, world, rank, local):
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = max_over_ranks(sum(step_ms), world)
     med_ms = max_over_ranks(statistics.median(step_ms), world)
-    tokens_per_step_all = nb * S * world
+    tokens_per_step_all = (cfg.batch_size if scaling == "strong" else nb * world) * S
     value = tokens_per_step_all * args.steps * 1000.0 / total_ms
 
     code, detail = model.read_device_status()
@@ -392,7 +392,8 @@ def run_ours(args, world, rank, local):
         "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded generate_random_case, seeded random-init weights)",
         "config": workload_config(w, nb, world), "plan": plan,
-        "gpu_launches": launches * args.steps,
+        "gpu_launches": launches * args.steps * world,
+        "gpu_launches_note": "our kernels in the timed device steps, summed over ranks",
         "roofline": roofline,
         "e2e": {"value": e2e_value, "unit": "tokens/s",
                 "h2d_bytes_per_step": x_host.numel() * 4 + m_host.numel(),

@@ -1,0 +1,99 @@
+"""Batch sharding and the output gather on 2 CPU ranks (gloo), plus failure
+handling: a rank that raises makes its peer fail with a timeout error instead
+of hanging."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from ttjam_gottagofast_b200.shard import shard_range, sharded_forward
+
+
+def test_shard_ranges_cover_batch_exactly():
+    for batch in (0, 1, 7, 8, 64, 65):
+        for world in (1, 2, 3, 4, 8):
+            seen = []
+            for rank in range(world):
+                s, c = shard_range(batch, world, rank)
+                seen.extend(range(s, s + c))
+            assert seen == list(range(batch))
+            sizes = [shard_range(batch, world, r)[1] for r in range(world)]
+            assert max(sizes) - min(sizes) <= (1 if batch else 0)
+    with pytest.raises(ValueError):
+        shard_range(4, 2, 2)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _stand_in_forward(x, mask):
+    # any per-sequence function stands in for the GPU forward on CPU ranks
+    out = x * 2 + torch.arange(x.shape[1], dtype=x.dtype)[None, :, None]
+    if mask is not None:
+        out = out.masked_fill(~mask[..., None], 0)
+    return out
+
+
+def _worker(rank, world, port, batch, result_q, fail_rank):
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=10))
+    try:
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(batch, 5, 3, generator=g)
+        mask = torch.rand(batch, 5, generator=g) > 0.3
+        if rank == fail_rank:
+            raise RuntimeError("injected failure on the host before the gather")
+        y = sharded_forward(_stand_in_forward, x, mask)
+        ok = torch.equal(y, _stand_in_forward(x, mask))
+        result_q.put((rank, "ok" if ok else "mismatch"))
+    except Exception as e:  # noqa: BLE001 - report any failure to the parent
+        result_q.put((rank, f"error: {type(e).__name__}: {e}"))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def _run(world, batch, fail_rank=-1, timeout=60):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, batch, q, fail_rank))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+    out = {}
+    while not q.empty():
+        r, msg = q.get()
+        out[r] = msg
+    return out
+
+
+@pytest.mark.parametrize("batch", [8, 7, 1])
+def test_gather_reassembles_batch_on_two_ranks(batch):
+    out = _run(2, batch)
+    assert out == {0: "ok", 1: "ok"}, out
+
+
+def test_failed_rank_makes_peer_error_not_hang():
+    out = _run(2, 8, fail_rank=1)
+    assert out[1].startswith("error: RuntimeError")
+    assert 0 in out and out[0].startswith("error"), out
