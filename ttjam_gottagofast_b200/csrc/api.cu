@@ -3,6 +3,7 @@
 #include <cstring>
 #include <string>
 
+#include "attention_tc.cuh"
 #include "cluster_forward.cuh"
 #include "gemm_tc.cuh"
 #include "image.cuh"
@@ -166,7 +167,7 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
   const int64_t T = batch * seq;
   if (T > INT32_MAX) return fail(TT_ERR_UNSUPPORTED, "tensor-core schedule: too many tokens");
   auto WS = [&](size_t off) { return reinterpret_cast<float *>(ws + off); };
-  float *qkv = WS(W.qkv);
+  float *qkv = WS(W.qkv), *qkv_hi = WS(W.qkv_hi), *qkv_lo = WS(W.qkv_lo);
   float *ln_hi = WS(W.ln_hi), *ln_lo = WS(W.ln_lo);
   float *ctx_hi = WS(W.ctx_hi), *ctx_lo = WS(W.ctx_lo);
   float *h_hi = WS(W.h_hi), *h_lo = WS(W.h_lo);
@@ -182,14 +183,28 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
       return rc;
     TcGemmParams g{};
     g.A_hi = ln_hi; g.A_lo = ln_lo; g.lda = D; g.W_hi = P(o.wqkv_hi); g.W_lo = P(o.wqkv_lo);
-    g.bias = P(o.bqkv); g.C = qkv; g.ldc = 3LL * D; g.status = status;
+    g.bias = P(o.bqkv); g.ldc = 3LL * D; g.status = status;
     g.M = (int)T; g.N = 3 * D; g.K = D; g.epilogue = EPI_BIAS;
+    if (W.tc_attention) {
+      g.C_hi = qkv_hi; g.C_lo = qkv_lo;  // the attention consumes the split
+    } else {
+      g.C = qkv;
+    }
     if ((rc = launch_gemm_tc3(g, stream)) != TT_OK) return rc;
-    AttentionParams a{};
-    a.qkv = qkv; a.ctx = nullptr; a.ctx_hi = ctx_hi; a.ctx_lo = ctx_lo; a.mask = mask;
-    a.batch = batch; a.seq = (int)seq; a.d_model = D; a.num_heads = H; a.head_dim = hd;
-    a.causal = cfg.causal; a.scale = (float)(1.0 / std::sqrt((double)hd));
-    if ((rc = launch_attention_ffma(a, stream)) != TT_OK) return rc;
+    const float scale = (float)(1.0 / std::sqrt((double)hd));
+    if (W.tc_attention) {
+      AttentionTcParams a{};
+      a.qkv_hi = qkv_hi; a.qkv_lo = qkv_lo; a.ctx_hi = ctx_hi; a.ctx_lo = ctx_lo; a.mask = mask;
+      a.status = status; a.batch = batch; a.seq = (int)seq; a.d_model = D; a.num_heads = H;
+      a.head_dim = hd; a.causal = cfg.causal; a.scale = scale;
+      if ((rc = launch_attention_tc(a, stream)) != TT_OK) return rc;
+    } else {
+      AttentionParams a{};
+      a.qkv = qkv; a.ctx = nullptr; a.ctx_hi = ctx_hi; a.ctx_lo = ctx_lo; a.mask = mask;
+      a.batch = batch; a.seq = (int)seq; a.d_model = D; a.num_heads = H; a.head_dim = hd;
+      a.causal = cfg.causal; a.scale = scale;
+      if ((rc = launch_attention_ffma(a, stream)) != TT_OK) return rc;
+    }
     TcGemmParams go{};
     go.A_hi = ctx_hi; go.A_lo = ctx_lo; go.lda = D; go.W_hi = P(o.wo_hi); go.W_lo = P(o.wo_lo);
     go.bias = P(o.bo); go.R = xin; go.C = y; go.ldc = D; go.row_mask = mask; go.status = status;

@@ -1,0 +1,469 @@
+// Causal / key-padded flash attention on tensor cores (tcgen05, 3xTF32) for
+// head_dim 64 -- the attention core of the d_model >= 512 workloads.
+//
+// Semantics as the reference attention (torch_transformer_benchmark.py:97-117):
+// s = (q . k) * hd^-0.5, -inf for keys after the query (causal, :99-103) and
+// for padded keys (:105-108), fp32 softmax (:111), ctx = p . v written in
+// [B, S, H*hd] order. Queries without an allowed key (only padded queries)
+// get a zero context; their rows are zeroed after out_proj as in :120-121.
+//
+// Precision: both products use the TF32 split x = x_hi + x_lo with three
+// tensor-core products (hi.hi + hi.lo + lo.hi), accumulated in fp32: q, k, v
+// arrive split by the q|k|v GEMM, p = exp(s - m) is split by the softmax
+// threads. The running context accumulates in fp32 registers.
+//
+// CTA = (query tile of 128 rows, head, sequence); 256 threads:
+//   warp 0    TMA producer: per 64-key tile, K_hi K_lo V_hi V_lo (64 keys x
+//             64 dims, two 128-byte swizzle boxes each) into a 3-stage ring;
+//   warp 1    MMA issuer: S[j] = Q.K_j^T (A = Q from tensor memory, B = K tile,
+//             K-major) into a double-buffered S, then O_j = P_j.V_j (A = P
+//             from tensor memory, B = V tile read MN-major);
+//   warp 2    allocates / frees 512 tensor-memory columns;
+//   warps 4-7 softmax: thread t owns query row q0+t = tensor-memory lane t,
+//             loads its Q row into tensor memory, then per key tile reads S,
+//             applies scale + masks, updates the running max / sum, writes P
+//             (split) to tensor memory and folds O_j into its fp32 context.
+// Every mbarrier wait is bounded; a wait that gives up latches
+// TT_ERR_DEVICE_TIMEOUT and the kernel still frees tensor memory and returns.
+// No TMA load here uses cluster multicast.
+#include <cuda.h>
+#include <math_constants.h>
+
+#include "attention_tc.cuh"
+
+namespace tt {
+namespace {
+
+constexpr int HD = 64, BQ = 128, BKV = 64, STAGES = 3;
+constexpr int kThreads = 256;
+constexpr uint32_t HALF = BKV * 128;       // one [64 rows x 32 fp32] swizzled box: 8 KB
+constexpr uint32_t OPER = 2 * HALF;        // one 64 x 64 operand: 16 KB
+constexpr uint32_t STAGE = 4 * OPER;       // K_hi, K_lo, V_hi, V_lo: 64 KB
+constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE + 1024 + 256;
+// tensor-memory columns (fp32 cells): Q_hi, Q_lo, S[2], P_hi, P_lo, O
+constexpr uint32_t T_QHI = 0, T_QLO = 64, T_S0 = 128, T_PHI = 256, T_PLO = 320, T_O = 384;
+constexpr uint32_t TMEM_COLS = 512;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// Bounded wait: gives up after ~2^28 cycles, or at once when a wait anywhere
+// in the launch already gave up.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, DeviceStatus *st,
+                                          int detail) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (st != nullptr && *reinterpret_cast<volatile int32_t *>(&st->code) != 0) return false;
+    if (clock64() - t0 > (1LL << 28)) {
+      raise_status(st, TT_ERR_DEVICE_TIMEOUT, detail);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *tm, int c0, int c1,
+                                            int c2, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+// Shared-memory matrix descriptor, 128-byte swizzle, version 1.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+// Instruction descriptors: D fp32, A/B tf32, M = 128, N = 64.
+//   S = Q.K^T : A K-major (tensor memory), B K-major
+//   O = P.V   : A K-major (tensor memory), B MN-major (V rows are keys)
+constexpr uint32_t kIdescBase = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(64 >> 3) << 17) |
+                                ((uint32_t)(128 >> 4) << 24);
+constexpr uint32_t kIdescS = kIdescBase;
+constexpr uint32_t kIdescPV = kIdescBase | (1u << 16);
+
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float *v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_hi,
+                        const __grid_constant__ CUtensorMap tm_lo, const AttentionTcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ int s_kv_len;
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t bars = base + STAGES * STAGE;
+  auto kv_full = [&](int s) { return bars + 8u * s; };
+  auto kv_empty = [&](int s) { return bars + 8u * (STAGES + s); };
+  auto s_full = [&](int b) { return bars + 8u * (2 * STAGES + b); };
+  auto s_free = [&](int b) { return bars + 8u * (2 * STAGES + 2 + b); };
+  const uint32_t p_full = bars + 8u * (2 * STAGES + 4);
+  const uint32_t o_full = bars + 8u * (2 * STAGES + 5);
+  const uint32_t q_ready = bars + 8u * (2 * STAGES + 6);
+  const uint32_t tmem_slot = bars + 8u * (2 * STAGES + 7);
+  uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = p.seq, D = p.d_model;
+  const int qt = gridDim.x - 1 - blockIdx.x;  // heaviest (latest) query tiles first
+  const int h = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int q0 = qt * BQ;
+  const uint8_t *mrow = p.mask ? p.mask + b * S : nullptr;
+
+  // kv_len = 1 + last valid key; keys at or after it are all padding
+  if (threadIdx.x == 0) s_kv_len = mrow ? 0 : S;
+  __syncthreads();
+  if (mrow) {
+    int last = 0;
+    for (int j = threadIdx.x; j < S; j += kThreads)
+      if (mrow[j]) last = j + 1;
+    if (last) atomicMax(&s_kv_len, last);
+  }
+  __syncthreads();
+  const int kv_len = s_kv_len;
+  if (q0 >= kv_len) return;  // every query of this tile is padding (uniform exit)
+  const int kv_end = p.causal ? min(kv_len, q0 + BQ) : kv_len;
+  const int nkv = (kv_end + BKV - 1) / BKV;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(kv_full(s), 1);
+      mbar_init(kv_empty(s), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(s_full(i), 1);
+      mbar_init(s_free(i), 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_full, 1);
+    mbar_init(q_ready, 128);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tm = *tmem_slot_ptr;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer: K/V tiles -------------------------------------------
+    const int kcol = D + h * HD, vcol = 2 * D + h * HD;
+    for (int j = 0; j < nkv; ++j) {
+      const int s = j % STAGES, n = j / STAGES;
+      if (j >= STAGES) mbar_wait(kv_empty(s), (n - 1) & 1, p.status, 0x4100 + j);
+      const uint32_t st = base + s * STAGE;
+      mbar_expect_tx(kv_full(s), STAGE);
+      for (int half = 0; half < 2; ++half) {
+        tma_load_3d(st + half * HALF, &tm_hi, kcol + 32 * half, j * BKV, (int)b, kv_full(s));
+        tma_load_3d(st + OPER + half * HALF, &tm_lo, kcol + 32 * half, j * BKV, (int)b, kv_full(s));
+        tma_load_3d(st + 2 * OPER + half * HALF, &tm_hi, vcol + 32 * half, j * BKV, (int)b, kv_full(s));
+        tma_load_3d(st + 3 * OPER + half * HALF, &tm_lo, vcol + 32 * half, j * BKV, (int)b, kv_full(s));
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer --------------------------------------------------------
+    auto issue_s = [&](int j) {
+      const int s = j % STAGES, sb = j & 1;
+      mbar_wait(kv_full(s), (j / STAGES) & 1, p.status, 0x4200 + j);
+      if (j >= 2) mbar_wait(s_free(sb), ((j >> 1) - 1) & 1, p.status, 0x4300 + j);
+      fence_after();
+      const uint32_t kst = base + s * STAGE;
+      const uint32_t sd = tm + T_S0 + 64u * sb;
+#pragma unroll
+      for (int kk = 0; kk < HD / 8; ++kk) {  // 8 head dims per MMA
+        const uint32_t koff = (uint32_t)(kk >> 2) * HALF + (uint32_t)(kk & 3) * 32u;
+        const uint64_t khi = sdesc(kst + koff, 16, 1024);
+        const uint64_t klo = sdesc(kst + OPER + koff, 16, 1024);
+        mma_ts(sd, tm + T_QHI + 8u * kk, khi, kIdescS, kk > 0);
+        mma_ts(sd, tm + T_QHI + 8u * kk, klo, kIdescS, 1);
+        mma_ts(sd, tm + T_QLO + 8u * kk, khi, kIdescS, 1);
+      }
+      mma_commit(s_full(sb));
+    };
+    mbar_wait(q_ready, 0, p.status, 0x4000);
+    issue_s(0);
+    for (int j = 0; j < nkv; ++j) {
+      if (j + 1 < nkv) issue_s(j + 1);  // next scores overlap this tile's softmax
+      const int s = j % STAGES;
+      mbar_wait(p_full, j & 1, p.status, 0x4400 + j);
+      fence_after();
+      const uint32_t vst = base + s * STAGE + 2 * OPER;
+#pragma unroll
+      for (int kk = 0; kk < BKV / 8; ++kk) {  // 8 keys per MMA
+        const uint64_t vhi = sdesc(vst + (uint32_t)kk * 1024u, HALF, 1024);
+        const uint64_t vlo = sdesc(vst + OPER + (uint32_t)kk * 1024u, HALF, 1024);
+        mma_ts(tm + T_O, tm + T_PHI + 8u * kk, vhi, kIdescPV, kk > 0);
+        mma_ts(tm + T_O, tm + T_PHI + 8u * kk, vlo, kIdescPV, 1);
+        mma_ts(tm + T_O, tm + T_PLO + 8u * kk, vhi, kIdescPV, 1);
+      }
+      mma_commit(o_full);
+      mma_commit(kv_empty(s));
+    }
+  } else if (warp >= 4) {
+    // ---- softmax: thread t <-> query row q0+t <-> tensor-memory lane t -----
+    const int t = threadIdx.x - 128;
+    const int row = q0 + t;
+    const bool row_in = row < S;
+    const uint32_t lane_base = tm + ((uint32_t)((warp & 3) * 32) << 16);
+    {
+      const int64_t qoff = (b * S + (row_in ? row : 0)) * (int64_t)(3 * D) + (int64_t)h * HD;
+      float v[16];
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const float *src = (which ? p.qkv_lo : p.qkv_hi) + qoff;
+#pragma unroll
+        for (int c = 0; c < HD; c += 16) {
+#pragma unroll
+          for (int i = 0; i < 16; i += 4) {
+            const float4 x = row_in ? *reinterpret_cast<const float4 *>(src + c + i)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+            v[i] = x.x; v[i + 1] = x.y; v[i + 2] = x.z; v[i + 3] = x.w;
+          }
+          tmem_st16(lane_base + (which ? T_QLO : T_QHI) + c, v);
+        }
+      }
+      tmem_wait_st();
+      fence_before();
+      mbar_arrive(q_ready);
+    }
+    float o[HD];
+#pragma unroll
+    for (int c = 0; c < HD; ++c) o[c] = 0.f;
+    float m = -CUDART_INF_F, l = 0.f;
+    for (int j = 0; j < nkv; ++j) {
+      const int sb = j & 1;
+      mbar_wait(s_full(sb), (j >> 1) & 1, p.status, 0x4500 + j);
+      fence_after();
+      float sv[BKV];
+#pragma unroll
+      for (int c = 0; c < BKV; c += 16) tmem_ld16(lane_base + T_S0 + 64u * sb + c, sv + c);
+      tmem_wait_ld();
+      fence_before();
+      mbar_arrive(s_free(sb));
+      // scale and masks
+      float mx = -CUDART_INF_F;
+#pragma unroll
+      for (int c = 0; c < BKV; ++c) {
+        const int kj = j * BKV + c;
+        const bool ok = kj < kv_end && (mrow == nullptr || mrow[kj] != 0) &&
+                        (!p.causal || kj <= row);
+        sv[c] = ok ? sv[c] * p.scale : -CUDART_INF_F;
+        mx = fmaxf(mx, sv[c]);
+      }
+      const float m_new = fmaxf(m, mx);
+      float alpha, psum = 0.f;
+      if (m_new == -CUDART_INF_F) {  // nothing allowed yet for this row
+        alpha = 1.f;
+#pragma unroll
+        for (int c = 0; c < BKV; ++c) sv[c] = 0.f;
+      } else {
+        alpha = __expf(m - m_new);  // 0 when m is -inf
+#pragma unroll
+        for (int c = 0; c < BKV; ++c) {
+          sv[c] = __expf(sv[c] - m_new);
+          psum += sv[c];
+        }
+      }
+      l = l * alpha + psum;
+      m = m_new;
+      // P (TF32 split) -> tensor memory; the previous P.V finished (o_full)
+#pragma unroll
+      for (int c = 0; c < BKV; c += 16) {
+        float hi[16], lo[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          hi[i] = tf32_round(sv[c + i]);
+          lo[i] = sv[c + i] - hi[i];
+        }
+        tmem_st16(lane_base + T_PHI + c, hi);
+        tmem_st16(lane_base + T_PLO + c, lo);
+      }
+      tmem_wait_st();
+      fence_before();
+      mbar_arrive(p_full);
+      mbar_wait(o_full, j & 1, p.status, 0x4600 + j);
+      fence_after();
+      static_assert(HD == BKV, "the O tile reuses the score registers");
+#pragma unroll
+      for (int c = 0; c < HD; c += 16) tmem_ld16(lane_base + T_O + c, sv + c);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < HD; ++c) o[c] = fmaf(o[c], alpha, sv[c]);
+    }
+    if (row_in) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int64_t off = (b * S + row) * (int64_t)D + (int64_t)h * HD;
+#pragma unroll
+      for (int c = 0; c < HD; c += 4) {
+        float4 hv, lv;
+        const float v0 = o[c] * inv, v1 = o[c + 1] * inv, v2 = o[c + 2] * inv, v3 = o[c + 3] * inv;
+        hv.x = tf32_round(v0); lv.x = v0 - hv.x;
+        hv.y = tf32_round(v1); lv.y = v1 - hv.y;
+        hv.z = tf32_round(v2); lv.z = v2 - hv.z;
+        hv.w = tf32_round(v3); lv.w = v3 - hv.w;
+        *reinterpret_cast<float4 *>(p.ctx_hi + off + c) = hv;
+        *reinterpret_cast<float4 *>(p.ctx_lo + off + c) = lv;
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int encode_fn(EncodeTiledFn *out) {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    TT_CUDA_TRY(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q));
+    if (ptr == nullptr || q != cudaDriverEntryPointSuccess)
+      return fail(TT_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  *out = fn;
+  return TT_OK;
+}
+
+// [batch, seq, 3*d_model] fp32 view of a q|k|v buffer; box = 32 columns x 64
+// rows x 1 sequence, 128-byte swizzle, zero fill past the sequence end.
+int make_qkv_map(CUtensorMap *tm, const float *ptr, int64_t batch, int seq, int d_model) {
+  EncodeTiledFn encode;
+  int rc = encode_fn(&encode);
+  if (rc != TT_OK) return rc;
+  cuuint64_t dims[3] = {(cuuint64_t)(3 * d_model), (cuuint64_t)seq, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(3 * d_model) * 4, (cuuint64_t)seq * (3 * d_model) * 4};
+  cuuint32_t box[3] = {32, (cuuint32_t)BKV, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(ptr), dims,
+                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(TT_ERR_CUDA, "cuTensorMapEncodeTiled (q|k|v) failed with CUresult " +
+                                 std::to_string((int)r));
+  return TT_OK;
+}
+
+}  // namespace
+
+bool attention_tc_supported(int head_dim, int d_model) {
+  return head_dim == HD && d_model % 4 == 0;
+}
+
+int launch_attention_tc(const AttentionTcParams &p, cudaStream_t stream) {
+  if (p.batch <= 0 || p.seq <= 0) return TT_OK;
+  if (!attention_tc_supported(p.head_dim, p.d_model))
+    return fail(TT_ERR_UNSUPPORTED, "attention_tc: head_dim must be 64");
+  if (p.batch > 65535 || p.num_heads > 65535)
+    return fail(TT_ERR_UNSUPPORTED, "attention_tc: batch and num_heads must be <= 65535");
+  if (((reinterpret_cast<uintptr_t>(p.qkv_hi) | reinterpret_cast<uintptr_t>(p.qkv_lo) |
+        reinterpret_cast<uintptr_t>(p.ctx_hi) | reinterpret_cast<uintptr_t>(p.ctx_lo)) & 15) != 0)
+    return fail(TT_ERR_INVALID_ARGUMENT, "attention_tc: buffers must be 16-byte aligned");
+  CUtensorMap thi, tlo;
+  int rc;
+  if ((rc = make_qkv_map(&thi, p.qkv_hi, p.batch, p.seq, p.d_model)) ||
+      (rc = make_qkv_map(&tlo, p.qkv_lo, p.batch, p.seq, p.d_model)))
+    return rc;
+  static bool attr_set = false;
+  if (!attr_set) {
+    TT_CUDA_TRY(cudaFuncSetAttribute(attention_tc_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
+    attr_set = true;
+  }
+  dim3 grid((unsigned)((p.seq + BQ - 1) / BQ), (unsigned)p.num_heads, (unsigned)p.batch);
+  attention_tc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(thi, tlo, p);
+  TT_LAUNCH_CHECK("attention_tc");
+  return TT_OK;
+}
+
+}  // namespace tt

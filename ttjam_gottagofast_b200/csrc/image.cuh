@@ -9,9 +9,10 @@
 // Every array starts on a 256-byte boundary (TMA and float4 friendly).
 //
 // Workspace (per call, [T = batch*seq] tokens):
-//   qkv [T,3D] | ctx [T,D] | h [T,F]   and on the tensor-core path the TF32
-//   splits of the GEMM A operands: ln_hi/ln_lo [T,D], ctx_hi/ctx_lo [T,D],
-//   h_hi/h_lo [T,F].
+//   FFMA schedule:        qkv [T,3D] | ctx [T,D] | h [T,F]
+//   tensor-core schedule: qkv [T,3D] (or its TF32 split qkv_hi/qkv_lo when the
+//   attention also runs on tensor cores, head_dim 64) | the TF32 splits of the
+//   GEMM A operands: ln_hi/ln_lo [T,D], ctx_hi/ctx_lo [T,D], h_hi/h_lo [T,F].
 #pragma once
 
 #include <vector>
@@ -71,10 +72,11 @@ struct ImageLayout {
 };
 
 struct WorkspaceLayout {
-  size_t qkv = 0, ctx = 0, h = 0;
+  size_t qkv = 0, ctx = 0, h = 0, qkv_hi = 0, qkv_lo = 0;
   size_t ln_hi = 0, ln_lo = 0, ctx_hi = 0, ctx_lo = 0, h_hi = 0, h_lo = 0;
   size_t total = 0;
-  bool tensor = false;  // buffers of the tensor-core schedule
+  bool tensor = false;        // buffers of the tensor-core schedule
+  bool tc_attention = false;  // ... whose attention also runs on tensor cores
 
   WorkspaceLayout(const tt_config &cfg, int64_t batch, int64_t seq) {
     const size_t T = (size_t)batch * (size_t)seq, D = cfg.d_model, F = cfg.ffn_dim;
@@ -86,7 +88,13 @@ struct WorkspaceLayout {
       cur = align_up(cur + n_floats * f4, 256);
       return off;
     };
-    qkv = take(T * 3 * D);
+    tc_attention = tensor && cfg.d_model / cfg.num_heads == 64;
+    if (tc_attention) {
+      // q|k|v as a TF32 split for the tensor-core attention
+      qkv_hi = take(T * 3 * D); qkv_lo = take(T * 3 * D);
+    } else {
+      qkv = take(T * 3 * D);
+    }
     if (tensor) {
       // A operands of the 3xTF32 GEMMs, as TF32 hi/lo pairs
       ln_hi = take(T * D); ln_lo = take(T * D);
