@@ -13,11 +13,13 @@
 // threads. The running context accumulates in fp32 registers.
 //
 // CTA = (query tile of 128 rows, head, sequence); 256 threads:
-//   warp 0    TMA producer: per 64-key tile, K_hi K_lo V_hi V_lo (64 keys x
-//             64 dims, two 128-byte swizzle boxes each) into a 3-stage ring;
-//   warp 1    MMA issuer: S[j] = Q.K_j^T (A = Q from tensor memory, B = K tile,
-//             K-major) into a double-buffered S, then O_j = P_j.V_j (A = P
-//             from tensor memory, B = V tile read MN-major);
+//   warp 0    TMA producer: per 64-key tile, K_hi K_lo (64 keys x 64 dims) and
+//             Vt_hi Vt_lo (64 dims x 64 keys, from the transposed copy of v the
+//             q|k|v GEMM writes), two 128-byte swizzle boxes each, into a
+//             3-stage ring;
+//   warp 1    MMA issuer: S[j] = Q.K_j^T (A = Q from tensor memory, B = K tile)
+//             into a double-buffered S, then O_j = P_j.V_j (A = P from tensor
+//             memory, B = Vt tile); both B operands are K-major;
 //   warp 2    allocates / frees 512 tensor-memory columns;
 //   warps 4-7 softmax: thread t owns query row q0+t = tensor-memory lane t,
 //             loads its Q row into tensor memory, then per key tile reads S,
@@ -103,11 +105,10 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t
 }
 // Instruction descriptors: D fp32, A/B tf32, M = 128, N = 64.
 //   S = Q.K^T : A K-major (tensor memory), B K-major
-//   O = P.V   : A K-major (tensor memory), B MN-major (V rows are keys)
-constexpr uint32_t kIdescBase = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(64 >> 3) << 17) |
-                                ((uint32_t)(128 >> 4) << 24);
-constexpr uint32_t kIdescS = kIdescBase;
-constexpr uint32_t kIdescPV = kIdescBase | (1u << 16);
+//   O = P.V   : A K-major (tensor memory), B = V^T tile, K-major (keys contiguous)
+constexpr uint32_t kIdescS = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(64 >> 3) << 17) |
+                             ((uint32_t)(128 >> 4) << 24);
+constexpr uint32_t kIdescPV = kIdescS;
 
 __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
                                        uint32_t idesc, uint32_t accum) {
@@ -161,7 +162,9 @@ __device__ __forceinline__ void tmem_wait_st() {
 
 __global__ void __launch_bounds__(kThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_hi,
-                        const __grid_constant__ CUtensorMap tm_lo, const AttentionTcParams p) {
+                        const __grid_constant__ CUtensorMap tm_lo,
+                        const __grid_constant__ CUtensorMap tm_vhi,
+                        const __grid_constant__ CUtensorMap tm_vlo, const AttentionTcParams p) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ int s_kv_len;
   const uint32_t raw = smem_u32(smem_raw);
@@ -227,17 +230,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0 && lane == 0) {
     // ---- TMA producer: K/V tiles -------------------------------------------
-    const int kcol = D + h * HD, vcol = 2 * D + h * HD;
+    const int kcol = D + h * HD;
+    const int bh = (int)b * p.num_heads + h;
     for (int j = 0; j < nkv; ++j) {
       const int s = j % STAGES, n = j / STAGES;
       if (j >= STAGES) mbar_wait(kv_empty(s), (n - 1) & 1, p.status, 0x4100 + j);
       const uint32_t st = base + s * STAGE;
       mbar_expect_tx(kv_full(s), STAGE);
       for (int half = 0; half < 2; ++half) {
+        // K rows = keys, 32 dims per box; Vt rows = dims, 32 keys per box
         tma_load_3d(st + half * HALF, &tm_hi, kcol + 32 * half, j * BKV, (int)b, kv_full(s));
         tma_load_3d(st + OPER + half * HALF, &tm_lo, kcol + 32 * half, j * BKV, (int)b, kv_full(s));
-        tma_load_3d(st + 2 * OPER + half * HALF, &tm_hi, vcol + 32 * half, j * BKV, (int)b, kv_full(s));
-        tma_load_3d(st + 3 * OPER + half * HALF, &tm_lo, vcol + 32 * half, j * BKV, (int)b, kv_full(s));
+        tma_load_3d(st + 2 * OPER + half * HALF, &tm_vhi, j * BKV + 32 * half, 0, bh, kv_full(s));
+        tma_load_3d(st + 3 * OPER + half * HALF, &tm_vlo, j * BKV + 32 * half, 0, bh, kv_full(s));
       }
     }
   } else if (warp == 1 && lane == 0) {
@@ -270,8 +275,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t vst = base + s * STAGE + 2 * OPER;
 #pragma unroll
       for (int kk = 0; kk < BKV / 8; ++kk) {  // 8 keys per MMA
-        const uint64_t vhi = sdesc(vst + (uint32_t)kk * 1024u, HALF, 1024);
-        const uint64_t vlo = sdesc(vst + OPER + (uint32_t)kk * 1024u, HALF, 1024);
+        const uint32_t voff = (uint32_t)(kk >> 2) * HALF + (uint32_t)(kk & 3) * 32u;
+        const uint64_t vhi = sdesc(vst + voff, 16, 1024);
+        const uint64_t vlo = sdesc(vst + OPER + voff, 16, 1024);
         mma_ts(tm + T_O, tm + T_PHI + 8u * kk, vhi, kIdescPV, kk > 0);
         mma_ts(tm + T_O, tm + T_PHI + 8u * kk, vlo, kIdescPV, 1);
         mma_ts(tm + T_O, tm + T_PLO + 8u * kk, vhi, kIdescPV, 1);
@@ -434,6 +440,26 @@ int make_qkv_map(CUtensorMap *tm, const float *ptr, int64_t batch, int seq, int 
   return TT_OK;
 }
 
+// [batch*heads, 64, seq] view of a transposed value buffer (row stride seq_pad);
+// box = 32 keys x 64 dims x 1, 128-byte swizzle, zero fill past the sequence.
+int make_vt_map(CUtensorMap *tm, const float *ptr, int64_t bh, int seq, int seq_pad) {
+  EncodeTiledFn encode;
+  int rc = encode_fn(&encode);
+  if (rc != TT_OK) return rc;
+  cuuint64_t dims[3] = {(cuuint64_t)seq, (cuuint64_t)HD, (cuuint64_t)bh};
+  cuuint64_t strides[2] = {(cuuint64_t)seq_pad * 4, (cuuint64_t)seq_pad * HD * 4};
+  cuuint32_t box[3] = {32, (cuuint32_t)HD, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(ptr), dims,
+                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(TT_ERR_CUDA, "cuTensorMapEncodeTiled (v^T) failed with CUresult " +
+                                 std::to_string((int)r));
+  return TT_OK;
+}
+
 }  // namespace
 
 bool attention_tc_supported(int head_dim, int d_model) {
@@ -447,12 +473,17 @@ int launch_attention_tc(const AttentionTcParams &p, cudaStream_t stream) {
   if (p.batch > 65535 || p.num_heads > 65535)
     return fail(TT_ERR_UNSUPPORTED, "attention_tc: batch and num_heads must be <= 65535");
   if (((reinterpret_cast<uintptr_t>(p.qkv_hi) | reinterpret_cast<uintptr_t>(p.qkv_lo) |
-        reinterpret_cast<uintptr_t>(p.ctx_hi) | reinterpret_cast<uintptr_t>(p.ctx_lo)) & 15) != 0)
+        reinterpret_cast<uintptr_t>(p.ctx_hi) | reinterpret_cast<uintptr_t>(p.ctx_lo) |
+        reinterpret_cast<uintptr_t>(p.vt_hi) | reinterpret_cast<uintptr_t>(p.vt_lo)) & 15) != 0)
     return fail(TT_ERR_INVALID_ARGUMENT, "attention_tc: buffers must be 16-byte aligned");
-  CUtensorMap thi, tlo;
+  if (p.seq_pad < p.seq || p.seq_pad % 4 != 0)
+    return fail(TT_ERR_INVALID_ARGUMENT, "attention_tc: seq_pad must be >= seq and a multiple of 4");
+  CUtensorMap thi, tlo, tvhi, tvlo;
   int rc;
   if ((rc = make_qkv_map(&thi, p.qkv_hi, p.batch, p.seq, p.d_model)) ||
-      (rc = make_qkv_map(&tlo, p.qkv_lo, p.batch, p.seq, p.d_model)))
+      (rc = make_qkv_map(&tlo, p.qkv_lo, p.batch, p.seq, p.d_model)) ||
+      (rc = make_vt_map(&tvhi, p.vt_hi, p.batch * p.num_heads, p.seq, p.seq_pad)) ||
+      (rc = make_vt_map(&tvlo, p.vt_lo, p.batch * p.num_heads, p.seq, p.seq_pad)))
     return rc;
   static bool attr_set = false;
   if (!attr_set) {
@@ -461,7 +492,7 @@ int launch_attention_tc(const AttentionTcParams &p, cudaStream_t stream) {
     attr_set = true;
   }
   dim3 grid((unsigned)((p.seq + BQ - 1) / BQ), (unsigned)p.num_heads, (unsigned)p.batch);
-  attention_tc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(thi, tlo, p);
+  attention_tc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(thi, tlo, tvhi, tvlo, p);
   TT_LAUNCH_CHECK("attention_tc");
   return TT_OK;
 }

@@ -229,6 +229,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.epilogue == EPI_BIAS_GELU) x = gelu_erf(x);
         v[j] = x;
       }
+      if (p.vt_hi != nullptr && col0 >= p.vt_col0) {
+        // value columns: TF32 split, transposed per (sequence, head) so keys are
+        // contiguous; lanes are consecutive rows, so each store is coalesced
+        const int vc = col0 - p.vt_col0;
+        const int hh = vc / p.head_dim, d0 = vc % p.head_dim;
+        const int bb = row / p.seq, ss = row % p.seq;
+        const int64_t base_t = ((int64_t)(bb * p.heads + hh) * p.head_dim + d0) * p.seq_pad + ss;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (!full && col0 + j >= p.N) break;
+          const float hv = tf32_round(v[j]);
+          p.vt_hi[base_t + (int64_t)j * p.seq_pad] = hv;
+          p.vt_lo[base_t + (int64_t)j * p.seq_pad] = v[j] - hv;
+        }
+        continue;
+      }
       const int64_t off = (int64_t)row * p.ldc + col0;
       if (p.epilogue == EPI_BIAS_RESIDUAL) {
 #pragma unroll

@@ -18,6 +18,12 @@ struct TcGemmParams {
   DeviceStatus *status;       // device status word for bounded-wait timeouts
   int M, N, K;
   int epilogue;               // GemmEpilogue
+  // Optional transposed copy of the value columns of a q|k|v projection, for
+  // the tensor-core attention: columns [vt_col0, N) of row r = b*seq + s, head
+  // h, dim d go to vt_{hi,lo}[((b*heads + h)*head_dim + d)*seq_pad + s]
+  // (keys contiguous) instead of C_hi/C_lo.
+  float *vt_hi, *vt_lo;
+  int vt_col0, seq, seq_pad, heads, head_dim;
 };
 
 int launch_gemm_tc3(const TcGemmParams &p, cudaStream_t stream);

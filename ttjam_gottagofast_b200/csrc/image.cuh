@@ -72,7 +72,8 @@ struct ImageLayout {
 };
 
 struct WorkspaceLayout {
-  size_t qkv = 0, ctx = 0, h = 0, qkv_hi = 0, qkv_lo = 0;
+  size_t qkv = 0, ctx = 0, h = 0, qkv_hi = 0, qkv_lo = 0, vt_hi = 0, vt_lo = 0;
+  int seq_pad = 0;  // row stride of the transposed value copy (multiple of 4)
   size_t ln_hi = 0, ln_lo = 0, ctx_hi = 0, ctx_lo = 0, h_hi = 0, h_lo = 0;
   size_t total = 0;
   bool tensor = false;        // buffers of the tensor-core schedule
@@ -90,8 +91,11 @@ struct WorkspaceLayout {
     };
     tc_attention = tensor && cfg.d_model / cfg.num_heads == 64;
     if (tc_attention) {
-      // q|k|v as a TF32 split for the tensor-core attention
+      // q|k as a TF32 split, and v transposed per (sequence, head) with keys
+      // contiguous, for the tensor-core attention
+      seq_pad = (int)((seq + 3) / 4 * 4);
       qkv_hi = take(T * 3 * D); qkv_lo = take(T * 3 * D);
+      vt_hi = take((size_t)batch * seq_pad * D); vt_lo = take((size_t)batch * seq_pad * D);
     } else {
       qkv = take(T * 3 * D);
     }
