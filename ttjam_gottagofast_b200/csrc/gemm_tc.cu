@@ -15,18 +15,26 @@
 // (torch_transformer_benchmark.py:93-95), out_proj + residual (:118-121, :140),
 // ffn_in + GELU and ffn_out + residual (:141-144).
 //
-// CTA = one 128x128 output tile, 256 threads, warp-specialised:
-//   warp 0  TMA producer: 4 tiles per k-block (A_hi, A_lo, W_hi, W_lo; 128 rows
-//           x 32 fp32 = one 128-byte swizzle row each) into a 3-stage ring;
-//   warp 1  MMA issuer (one thread): per k-block 4 k-steps x 3 products of
-//           tcgen05.mma.cta_group::1.kind::tf32 M128 N128 K8, then
-//           tcgen05.commit frees the stage; a final commit signals the epilogue;
-//   warp 2  allocates / frees the 128 TMEM columns of the accumulator;
-//   warps 4-7 epilogue: tcgen05.ld 32x32b (TMEM lane = tile row), bias,
-//           GELU / residual / padded-row zeroing, fp32 and/or TF32-split stores.
+// Persistent kernel, one CTA per SM looping over 128 x BN output tiles
+// (BN = 256, or 128 when N is small), 384 threads, warp-specialised:
+//   warp 0    TMA producer: per 16-wide k-block 4 tiles (A_hi, A_lo, W_hi,
+//             W_lo; 64-byte swizzle) into a 4-stage ring that runs on across
+//             tiles;
+//   warp 1    MMA issuer (one thread): per k-block 2 k-steps x 3 products of
+//             tcgen05.mma.cta_group::1.kind::tf32 M128 x BN x K8 into one of
+//             two tensor-memory accumulators; tcgen05.commit frees the stage /
+//             hands the accumulator to the epilogue;
+//   warp 2    allocates / frees the 2 x BN tensor-memory columns;
+//   warps 4-11 epilogue: warp w reads tensor-memory lane quarter w%4 (tile row
+//             = lane) and column half (w-4)/4 with tcgen05.ld 32x32b, applies
+//             bias, GELU / residual / padded-row zeroing, stores fp32 and/or
+//             the TF32 split, then releases the accumulator -- so the
+//             epilogue of one tile overlaps the main loop of the next.
+// With TF32 operands an M128 x N128 MMA reads 8 KB of shared memory per 64
+// cycles, the whole shared-memory bandwidth; N = 256 halves that per FLOP.
 // Every mbarrier wait is bounded; a wait that gives up latches
-// TT_ERR_DEVICE_TIMEOUT and the kernel still frees its TMEM and returns.
-// No TMA load here uses cluster multicast.
+// TT_ERR_DEVICE_TIMEOUT and the kernel still frees its tensor memory and
+// returns. No TMA load here uses cluster multicast.
 #include <cuda.h>
 
 #include "gemm_tc.cuh"
@@ -34,13 +42,19 @@
 namespace tt {
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
-constexpr int kThreads = 256;
-constexpr uint32_t TILE_A = BM * BK * 4;               // 16 KB
-constexpr uint32_t TILE_W = BN * BK * 4;               // 16 KB
-constexpr uint32_t STAGE_BYTES = 2 * TILE_A + 2 * TILE_W;
-constexpr uint32_t TMEM_COLS = BN;                      // fp32 accumulator, 128 lanes x BN
-constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int BM = 128, BK = 16, STAGES = 4;
+constexpr int kThreads = 384;
+constexpr int kEpiWarps = 8;
+constexpr uint32_t TILE_A = BM * BK * 4;               // 8 KB
+
+template <int BN>
+struct TcShape {
+  static constexpr uint32_t TILE_W = BN * BK * 4;                       // 16 KB at BN 256
+  static constexpr uint32_t STAGE_BYTES = 2 * TILE_A + 2 * TILE_W;      // 48 KB at BN 256
+  static constexpr uint32_t TMEM_COLS = 2 * BN;                         // two accumulators
+  static constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+};
 
 // ---- PTX helpers ------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -88,28 +102,35 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *tm,
       "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(c0), "r"(c1)
       : "memory");
 }
-// UMMA shared-memory descriptor, K-major, 128-byte swizzle: rows of 128 bytes,
-// 8-row groups 1024 bytes apart (SBO), LBO unused (1), version 1 (sm_100).
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+// UMMA shared-memory descriptor, K-major, 64-byte swizzle: rows of 64 bytes
+// (16 fp32), 8-row groups 512 bytes apart (SBO), LBO unused (1), version 1.
+__device__ __forceinline__ uint64_t umma_desc_sw64(uint32_t saddr) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFF);
   d |= (uint64_t)1 << 16;                 // LBO (16-byte units)
-  d |= (uint64_t)(1024 >> 4) << 32;       // SBO (16-byte units)
+  d |= (uint64_t)(512 >> 4) << 32;        // SBO (16-byte units)
   d |= (uint64_t)1 << 46;                 // descriptor version
-  d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
+  d |= (uint64_t)4 << 61;                 // SWIZZLE_64B
   return d;
 }
-// Instruction descriptor: D fp32, A/B tf32, both K-major, N = BN, M = BM.
-constexpr uint32_t kIdescTF32 = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                                ((uint32_t)(BM >> 4) << 24);
+// Instruction descriptor: D fp32, A/B tf32, both K-major, M = 128, N = BN.
+template <int BN>
+constexpr uint32_t idesc_tf32() {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+         ((uint32_t)(BM >> 4) << 24);
+}
 
-__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accum) {
+__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                          uint32_t accum) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(kIdescTF32), "r"(accum)
+      "l"(a), "l"(b), "r"(idesc), "r"(accum)
       : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -135,37 +156,103 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Epilogue of one 16-column chunk of one row: bias, activation / residual,
+// stores. v holds the accumulator values of columns col0..col0+15.
+__device__ __forceinline__ void epilogue_chunk(const TcGemmParams &p, int row, bool valid,
+                                               int col0, float (&v)[16]) {
+  const bool full = col0 + 16 <= p.N;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int col = col0 + j;
+    float x = (full || col < p.N) ? v[j] + p.bias[col] : 0.f;
+    if (p.epilogue == EPI_BIAS_GELU) x = gelu_erf(x);
+    v[j] = x;
+  }
+  if (p.vt_hi != nullptr && col0 >= p.vt_col0) {
+    // value columns: TF32 split, transposed per (sequence, head) so keys are
+    // contiguous; lanes are consecutive rows, so each store is coalesced
+    const int vc = col0 - p.vt_col0;
+    const int hh = vc / p.head_dim, d0 = vc % p.head_dim;
+    const int bb = row / p.seq, ss = row % p.seq;
+    const int64_t base_t = ((int64_t)(bb * p.heads + hh) * p.head_dim + d0) * p.seq_pad + ss;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (!full && col0 + j >= p.N) break;
+      const float hv = tf32_round(v[j]);
+      p.vt_hi[base_t + (int64_t)j * p.seq_pad] = hv;
+      p.vt_lo[base_t + (int64_t)j * p.seq_pad] = v[j] - hv;
+    }
+    return;
+  }
+  const int64_t off = (int64_t)row * p.ldc + col0;
+  if (p.epilogue == EPI_BIAS_RESIDUAL) {
+#pragma unroll
+    for (int j = 0; j < 16; j += 4) {
+      if (!full && col0 + j >= p.N) break;
+      const float4 r4 = *reinterpret_cast<const float4 *>(p.R + off + j);
+      v[j + 0] = valid ? r4.x + v[j + 0] : 0.f;
+      v[j + 1] = valid ? r4.y + v[j + 1] : 0.f;
+      v[j + 2] = valid ? r4.z + v[j + 2] : 0.f;
+      v[j + 3] = valid ? r4.w + v[j + 3] : 0.f;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 16; j += 4) {
+    if (!full && col0 + j >= p.N) break;
+    const float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    if (p.C != nullptr) *reinterpret_cast<float4 *>(p.C + off + j) = o;
+    if (p.C_hi != nullptr) {
+      float4 h, l;
+      h.x = tf32_round(o.x); l.x = o.x - h.x;
+      h.y = tf32_round(o.y); l.y = o.y - h.y;
+      h.z = tf32_round(o.z); l.z = o.z - h.z;
+      h.w = tf32_round(o.w); l.w = o.w - h.w;
+      *reinterpret_cast<float4 *>(p.C_hi + off + j) = h;
+      *reinterpret_cast<float4 *>(p.C_lo + off + j) = l;
+    }
+  }
+}
+
+template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                     const __grid_constant__ CUtensorMap tm_a_lo,
                     const __grid_constant__ CUtensorMap tm_w_hi,
                     const __grid_constant__ CUtensorMap tm_w_lo, const TcGemmParams p) {
+  using Sh = TcShape<BN>;
+  constexpr uint32_t TILE_W = Sh::TILE_W, STAGE_BYTES = Sh::STAGE_BYTES;
+  constexpr uint32_t IDESC = idesc_tf32<BN>();
   extern __shared__ uint8_t smem_raw[];
-  // SW128 tiles need 1024-byte alignment
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
-  const uint32_t bars = base + STAGES * STAGE_BYTES;   // full[S] | empty[S] | acc | tmem addr
+  const uint32_t bars = base + STAGES * STAGE_BYTES;
+  // full[S] | empty[S] | acc_full[2] | acc_empty[2] | tmem address
   auto full_bar = [&](int s) { return bars + 8u * s; };
   auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
-  const uint32_t acc_bar = bars + 8u * (2 * STAGES);
-  const uint32_t tmem_slot = acc_bar + 8u;
+  auto acc_full = [&](int b) { return bars + 8u * (2 * STAGES + b); };
+  auto acc_empty = [&](int b) { return bars + 8u * (2 * STAGES + 2 + b); };
+  const uint32_t tmem_slot = bars + 8u * (2 * STAGES + 4);
   uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
   const int KB = (p.K + BK - 1) / BK;
+  const int MT = (p.M + BM - 1) / BM, NT = (p.N + BN - 1) / BN;
+  const int ntiles = MT * NT;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
-    mbar_init(acc_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full(b), 1);
+      mbar_init(acc_empty(b), kEpiWarps * 32);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 2) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot),
-                 "r"(TMEM_COLS)
+                 "r"(Sh::TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -175,103 +262,69 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot_ptr;
 
   if (warp == 0 && lane == 0) {
-    // ---- TMA producer --------------------------------------------------------
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % STAGES, n = kb / STAGES;
-      if (kb >= STAGES) mbar_wait(empty_bar(s), (n - 1) & 1, p.status, 0x1000 + kb);
-      const uint32_t st = base + s * STAGE_BYTES;
-      mbar_expect_tx(full_bar(s), STAGE_BYTES);
-      tma_load_2d(st, &tm_a_hi, kb * BK, m0, full_bar(s));
-      tma_load_2d(st + TILE_A, &tm_a_lo, kb * BK, m0, full_bar(s));
-      tma_load_2d(st + 2 * TILE_A, &tm_w_hi, kb * BK, n0, full_bar(s));
-      tma_load_2d(st + 2 * TILE_A + TILE_W, &tm_w_lo, kb * BK, n0, full_bar(s));
+    // ---- TMA producer: one k-block sequence running across all tiles --------
+    int it = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+      const int m0 = (tile / NT) * BM, n0 = (tile % NT) * BN;
+      for (int kb = 0; kb < KB; ++kb, ++it) {
+        const int s = it % STAGES, n = it / STAGES;
+        if (it >= STAGES) mbar_wait(empty_bar(s), (n - 1) & 1, p.status, 0x1000);
+        const uint32_t st = base + s * STAGE_BYTES;
+        mbar_expect_tx(full_bar(s), STAGE_BYTES);
+        tma_load_2d(st, &tm_a_hi, kb * BK, m0, full_bar(s));
+        tma_load_2d(st + TILE_A, &tm_a_lo, kb * BK, m0, full_bar(s));
+        tma_load_2d(st + 2 * TILE_A, &tm_w_hi, kb * BK, n0, full_bar(s));
+        tma_load_2d(st + 2 * TILE_A + TILE_W, &tm_w_lo, kb * BK, n0, full_bar(s));
+      }
     }
   } else if (warp == 1 && lane == 0) {
-    // ---- MMA issuer ----------------------------------------------------------
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % STAGES, n = kb / STAGES;
-      mbar_wait(full_bar(s), n & 1, p.status, 0x2000 + kb);
+    // ---- MMA issuer -------------------------------------------------------
+    int it = 0, local = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
+      const int ab = local & 1;
+      if (local >= 2) mbar_wait(acc_empty(ab), ((local >> 1) - 1) & 1, p.status, 0x2100);
       tc_fence_after();
-      const uint32_t st = base + s * STAGE_BYTES;
+      const uint32_t acc = tmem_base + (uint32_t)(ab * BN);
+      for (int kb = 0; kb < KB; ++kb, ++it) {
+        const int s = it % STAGES, n = it / STAGES;
+        mbar_wait(full_bar(s), n & 1, p.status, 0x2000);
+        tc_fence_after();
+        const uint32_t st = base + s * STAGE_BYTES;
 #pragma unroll
-      for (int k = 0; k < BK / 8; ++k) {  // K = 8 tf32 = 32 bytes per MMA
-        const uint64_t a_hi = umma_desc_sw128(st + k * 32);
-        const uint64_t a_lo = umma_desc_sw128(st + TILE_A + k * 32);
-        const uint64_t w_hi = umma_desc_sw128(st + 2 * TILE_A + k * 32);
-        const uint64_t w_lo = umma_desc_sw128(st + 2 * TILE_A + TILE_W + k * 32);
-        umma_tf32(tmem_base, a_hi, w_hi, (kb | k) != 0);
-        umma_tf32(tmem_base, a_hi, w_lo, 1);
-        umma_tf32(tmem_base, a_lo, w_hi, 1);
+        for (int k = 0; k < BK / 8; ++k) {  // K = 8 tf32 = 32 bytes per MMA
+          const uint64_t a_hi = umma_desc_sw64(st + k * 32);
+          const uint64_t a_lo = umma_desc_sw64(st + TILE_A + k * 32);
+          const uint64_t w_hi = umma_desc_sw64(st + 2 * TILE_A + k * 32);
+          const uint64_t w_lo = umma_desc_sw64(st + 2 * TILE_A + TILE_W + k * 32);
+          umma_tf32(acc, a_hi, w_hi, IDESC, (kb | k) != 0);
+          umma_tf32(acc, a_hi, w_lo, IDESC, 1);
+          umma_tf32(acc, a_lo, w_hi, IDESC, 1);
+        }
+        umma_commit(empty_bar(s));  // stage s is free once these MMAs have read it
       }
-      umma_commit(empty_bar(s));  // stage s is free once these MMAs have read it
+      umma_commit(acc_full(ab));    // accumulator ab complete
     }
-    umma_commit(acc_bar);  // accumulator complete
   } else if (warp >= 4) {
-    // ---- epilogue: TMEM -> registers -> global -------------------------------
-    const int q = warp & 3;                    // TMEM lane quarter of this warp
-    const int row = m0 + q * 32 + lane;        // TMEM lane = tile row
-    bool ok = mbar_wait(acc_bar, 0, p.status, 0x3000);
-    if (!ok) ok = mbar_wait(acc_bar, 0, p.status, 0x3001);  // one more bounded wait for MMAs in flight
-    tc_fence_after();
-    const bool row_in = row < p.M;
-    const bool valid = row_in && (p.row_mask == nullptr || p.row_mask[row] != 0);
+    // ---- epilogue: tensor memory -> registers -> global ---------------------
+    const int q = warp & 3;                 // tensor-memory lane quarter
+    const int chalf = (warp - 4) >> 2;      // column half of the tile
+    int local = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
+      const int ab = local & 1;
+      const int m0 = (tile / NT) * BM, n0 = (tile % NT) * BN;
+      mbar_wait(acc_full(ab), (local >> 1) & 1, p.status, 0x3000);
+      tc_fence_after();
+      const int row = m0 + q * 32 + lane;
+      const bool row_in = row < p.M;
+      const bool valid = row_in && (p.row_mask == nullptr || p.row_mask[row] != 0);
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-      float v[16];
-      tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
-      const int col0 = n0 + c0;
-      if (!row_in || col0 >= p.N) continue;
-      const bool full = col0 + 16 <= p.N;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int col = col0 + j;
-        float x = (full || col < p.N) ? v[j] + p.bias[col] : 0.f;
-        if (p.epilogue == EPI_BIAS_GELU) x = gelu_erf(x);
-        v[j] = x;
+      for (int c0 = chalf * (BN / 2); c0 < (chalf + 1) * (BN / 2); c0 += 16) {
+        float v[16];
+        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN + c0), v);
+        if (row_in && n0 + c0 < p.N) epilogue_chunk(p, row, valid, n0 + c0, v);
       }
-      if (p.vt_hi != nullptr && col0 >= p.vt_col0) {
-        // value columns: TF32 split, transposed per (sequence, head) so keys are
-        // contiguous; lanes are consecutive rows, so each store is coalesced
-        const int vc = col0 - p.vt_col0;
-        const int hh = vc / p.head_dim, d0 = vc % p.head_dim;
-        const int bb = row / p.seq, ss = row % p.seq;
-        const int64_t base_t = ((int64_t)(bb * p.heads + hh) * p.head_dim + d0) * p.seq_pad + ss;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if (!full && col0 + j >= p.N) break;
-          const float hv = tf32_round(v[j]);
-          p.vt_hi[base_t + (int64_t)j * p.seq_pad] = hv;
-          p.vt_lo[base_t + (int64_t)j * p.seq_pad] = v[j] - hv;
-        }
-        continue;
-      }
-      const int64_t off = (int64_t)row * p.ldc + col0;
-      if (p.epilogue == EPI_BIAS_RESIDUAL) {
-#pragma unroll
-        for (int j = 0; j < 16; j += 4) {
-          if (!full && col0 + j >= p.N) break;
-          const float4 r4 = *reinterpret_cast<const float4 *>(p.R + off + j);
-          v[j + 0] = valid ? r4.x + v[j + 0] : 0.f;
-          v[j + 1] = valid ? r4.y + v[j + 1] : 0.f;
-          v[j + 2] = valid ? r4.z + v[j + 2] : 0.f;
-          v[j + 3] = valid ? r4.w + v[j + 3] : 0.f;
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 16; j += 4) {
-        if (!full && col0 + j >= p.N) break;
-        const float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-        if (p.C != nullptr) *reinterpret_cast<float4 *>(p.C + off + j) = o;
-        if (p.C_hi != nullptr) {
-          float4 h, l;
-          h.x = tf32_round(o.x); l.x = o.x - h.x;
-          h.y = tf32_round(o.y); l.y = o.y - h.y;
-          h.z = tf32_round(o.z); l.z = o.z - h.z;
-          h.w = tf32_round(o.w); l.w = o.w - h.w;
-          *reinterpret_cast<float4 *>(p.C_hi + off + j) = h;
-          *reinterpret_cast<float4 *>(p.C_lo + off + j) = l;
-        }
-      }
+      tc_fence_before();
+      mbar_arrive(acc_empty(ab));
     }
   }
   tc_fence_before();
@@ -279,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 2) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(TMEM_COLS)
+                 "r"(Sh::TMEM_COLS)
                  : "memory");
   }
 }
@@ -306,7 +359,7 @@ int encode_fn(EncodeTiledFn *out) {
 }
 
 // 2-D fp32 tensor map over a row-major [rows, cols] matrix (leading dimension
-// ld floats), box = 32 columns (128 bytes) x box_rows rows, 128-byte swizzle,
+// ld floats), box = 16 columns (64 bytes) x box_rows rows, 64-byte swizzle,
 // zero fill outside the matrix.
 int make_tmap(CUtensorMap *tm, const float *ptr, int64_t rows, int64_t cols, int64_t ld,
               int box_rows) {
@@ -321,10 +374,37 @@ int make_tmap(CUtensorMap *tm, const float *ptr, int64_t rows, int64_t cols, int
   cuuint32_t estr[2] = {1, 1};
   const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(ptr), dims,
                             strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(TT_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string((int)r));
+  return TT_OK;
+}
+
+template <int BN>
+int launch_bn(const TcGemmParams &p, cudaStream_t stream) {
+  using Sh = TcShape<BN>;
+  CUtensorMap ta_hi, ta_lo, tw_hi, tw_lo;
+  int rc;
+  if ((rc = make_tmap(&ta_hi, p.A_hi, p.M, p.K, p.lda, BM)) ||
+      (rc = make_tmap(&ta_lo, p.A_lo, p.M, p.K, p.lda, BM)) ||
+      (rc = make_tmap(&tw_hi, p.W_hi, p.N, p.K, p.K, BN)) ||
+      (rc = make_tmap(&tw_lo, p.W_lo, p.N, p.K, p.K, BN)))
+    return rc;
+  static int sms = 0;
+  static bool attr_set = false;
+  if (!attr_set) {
+    TT_CUDA_TRY(cudaFuncSetAttribute(gemm_tc3_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)Sh::SMEM_BYTES));
+    int dev = 0;
+    TT_CUDA_TRY(cudaGetDevice(&dev));
+    TT_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    attr_set = true;
+  }
+  const int64_t tiles = (int64_t)((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
+  const int grid = (int)std::min<int64_t>(tiles, sms > 0 ? sms : 148);
+  gemm_tc3_kernel<BN><<<grid, kThreads, Sh::SMEM_BYTES, stream>>>(ta_hi, ta_lo, tw_hi, tw_lo, p);
+  TT_LAUNCH_CHECK("gemm_tc3");
   return TT_OK;
 }
 
@@ -334,25 +414,13 @@ int launch_gemm_tc3(const TcGemmParams &p, cudaStream_t stream) {
   if (p.M <= 0 || p.N <= 0) return TT_OK;
   if (p.K <= 0 || p.K % 4 != 0 || p.N % 4 != 0 || p.ldc % 4 != 0)
     return fail(TT_ERR_UNSUPPORTED, "gemm_tc: K, N and ldc must be multiples of 4");
-  if (p.M > INT32_MAX - BM || (int64_t)(p.M + BM - 1) / BM > 65535)
-    return fail(TT_ERR_UNSUPPORTED, "gemm_tc: too many rows");
-  CUtensorMap ta_hi, ta_lo, tw_hi, tw_lo;
-  int rc;
-  if ((rc = make_tmap(&ta_hi, p.A_hi, p.M, p.K, p.lda, BM)) ||
-      (rc = make_tmap(&ta_lo, p.A_lo, p.M, p.K, p.lda, BM)) ||
-      (rc = make_tmap(&tw_hi, p.W_hi, p.N, p.K, p.K, BN)) ||
-      (rc = make_tmap(&tw_lo, p.W_lo, p.N, p.K, p.K, BN)))
-    return rc;
-  static bool attr_set = false;
-  if (!attr_set) {
-    TT_CUDA_TRY(cudaFuncSetAttribute(gemm_tc3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)SMEM_BYTES));
-    attr_set = true;
-  }
-  dim3 grid((unsigned)((p.N + BN - 1) / BN), (unsigned)((p.M + BM - 1) / BM));
-  gemm_tc3_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(ta_hi, ta_lo, tw_hi, tw_lo, p);
-  TT_LAUNCH_CHECK("gemm_tc3");
-  return TT_OK;
+  if (p.vt_hi != nullptr && (p.vt_col0 % 16 != 0 || p.head_dim % 16 != 0))
+    return fail(TT_ERR_UNSUPPORTED, "gemm_tc: transposed value columns need 16-aligned heads");
+  // N = 256 tiles halve the shared-memory operand traffic per FLOP; narrow
+  // projections use 128-wide tiles so every SM still gets work
+  const int64_t tiles256 = (int64_t)((p.M + BM - 1) / BM) * ((p.N + 255) / 256);
+  if (tiles256 >= 2 * 148) return launch_bn<256>(p, stream);
+  return launch_bn<128>(p, stream);
 }
 
 }  // namespace tt
