@@ -156,6 +156,13 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float *v) {
       "r"(__float_as_uint(v[15]))
       : "memory");
 }
+// 2^x with the hardware's approximate base-2 exponential (ex2.approx.ftz);
+// 2^-inf = 0.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -315,9 +322,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     float o[HD];
 #pragma unroll
     for (int c = 0; c < HD; ++c) o[c] = 0.f;
-    float m = -CUDART_INF_F, l = 0.f;
+    // running max m2 and scores are kept in the log2 domain: t = s * scale * log2(e)
+    const float sl = p.scale * 1.4426950408889634f;
+    float m2 = -CUDART_INF_F, l = 0.f, alpha_prev = 1.f;
+    // Fold P_{j-1}.V_{j-1} (in tensor memory) into the fp32 context with the
+    // rescale of its tile, 16 columns at a time.
+    auto fold_o = [&](int jp, float alpha) {
+      mbar_wait(o_full, jp & 1, p.status, 0x4600 + jp);
+      fence_after();
+#pragma unroll
+      for (int c = 0; c < HD; c += 16) {
+        float ov[16];
+        tmem_ld16(lane_base + T_O + c, ov);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[c + i] = fmaf(o[c + i], alpha, ov[i]);
+      }
+    };
     for (int j = 0; j < nkv; ++j) {
       const int sb = j & 1;
+      const int k0 = j * BKV;
+      // validity of the tile's 64 keys: padding mask and kv_end, two ballots
+      uint32_t ok_lo, ok_hi;
+      {
+        const int ka = k0 + lane, kb = k0 + 32 + lane;
+        const bool va = ka < kv_end && (mrow == nullptr || mrow[ka] != 0);
+        const bool vb = kb < kv_end && (mrow == nullptr || mrow[kb] != 0);
+        ok_lo = __ballot_sync(0xffffffffu, va);
+        ok_hi = __ballot_sync(0xffffffffu, vb);
+      }
+      const bool diag = p.causal && k0 + BKV - 1 > q0;  // tile reaches past the first query
       mbar_wait(s_full(sb), (j >> 1) & 1, p.status, 0x4500 + j);
       fence_after();
       float sv[BKV];
@@ -326,33 +360,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_ld();
       fence_before();
       mbar_arrive(s_free(sb));
-      // scale and masks
       float mx = -CUDART_INF_F;
 #pragma unroll
       for (int c = 0; c < BKV; ++c) {
-        const int kj = j * BKV + c;
-        const bool ok = kj < kv_end && (mrow == nullptr || mrow[kj] != 0) &&
-                        (!p.causal || kj <= row);
-        sv[c] = ok ? sv[c] * p.scale : -CUDART_INF_F;
+        const uint32_t bit = ((c < 32 ? ok_lo : ok_hi) >> (c & 31)) & 1u;
+        const bool ok = bit != 0 && (!diag || k0 + c <= row);
+        sv[c] = ok ? sv[c] * sl : -CUDART_INF_F;
         mx = fmaxf(mx, sv[c]);
       }
-      const float m_new = fmaxf(m, mx);
+      const float m_new = fmaxf(m2, mx);
       float alpha, psum = 0.f;
       if (m_new == -CUDART_INF_F) {  // nothing allowed yet for this row
         alpha = 1.f;
 #pragma unroll
         for (int c = 0; c < BKV; ++c) sv[c] = 0.f;
       } else {
-        alpha = __expf(m - m_new);  // 0 when m is -inf
+        alpha = fast_exp2(m2 - m_new);  // 0 when m2 is -inf
 #pragma unroll
         for (int c = 0; c < BKV; ++c) {
-          sv[c] = __expf(sv[c] - m_new);
+          sv[c] = fast_exp2(sv[c] - m_new);
           psum += sv[c];
         }
       }
       l = l * alpha + psum;
-      m = m_new;
-      // P (TF32 split) -> tensor memory; the previous P.V finished (o_full)
+      m2 = m_new;
+      // the previous tile's P.V must be done before P is overwritten: fold it now
+      if (j > 0) fold_o(j - 1, alpha_prev);
+      alpha_prev = alpha;
+      // P (TF32 split) -> tensor memory
 #pragma unroll
       for (int c = 0; c < BKV; c += 16) {
         float hi[16], lo[16];
@@ -367,15 +402,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_st();
       fence_before();
       mbar_arrive(p_full);
-      mbar_wait(o_full, j & 1, p.status, 0x4600 + j);
-      fence_after();
-      static_assert(HD == BKV, "the O tile reuses the score registers");
-#pragma unroll
-      for (int c = 0; c < HD; c += 16) tmem_ld16(lane_base + T_O + c, sv + c);
-      tmem_wait_ld();
-#pragma unroll
-      for (int c = 0; c < HD; ++c) o[c] = fmaf(o[c], alpha, sv[c]);
     }
+    fold_o(nkv - 1, alpha_prev);
     if (row_in) {
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const int64_t off = (b * S + row) * (int64_t)D + (int64_t)h * HD;
