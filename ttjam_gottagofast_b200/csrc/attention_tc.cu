@@ -10,7 +10,7 @@
 // Precision: both products use the TF32 split x = x_hi + x_lo with three
 // tensor-core products (hi.hi + hi.lo + lo.hi), accumulated in fp32: q, k, v
 // arrive split by the q|k|v GEMM, p = exp(s - m) is split by the softmax
-// threads. The running context accumulates in fp32 registers.
+// threads. The context accumulates in fp32 in tensor memory.
 //
 // CTA = (query tile of 128 rows, head, sequence); 256 threads:
 //   warp 0    TMA producer: per 64-key tile, K_hi K_lo (64 keys x 64 dims) and
@@ -23,8 +23,10 @@
 //   warp 2    allocates / frees 512 tensor-memory columns;
 //   warps 4-7 softmax: thread t owns query row q0+t = tensor-memory lane t,
 //             loads its Q row into tensor memory, then per key tile reads S,
-//             applies scale + masks, updates the running max / sum, writes P
-//             (split) to tensor memory and folds O_j into its fp32 context.
+//             applies scale + masks, updates the running sum, writes P (split)
+//             to tensor memory; the P.V MMAs accumulate the context in tensor
+//             memory, rescaled by its row's thread only when the row max grows
+//             by more than 2^8.
 // Every mbarrier wait is bounded; a wait that gives up latches
 // TT_ERR_DEVICE_TIMEOUT and the kernel still frees tensor memory and returns.
 // No TMA load here uses cluster multicast.
@@ -285,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t voff = (uint32_t)(kk >> 2) * HALF + (uint32_t)(kk & 3) * 32u;
         const uint64_t vhi = sdesc(vst + voff, 16, 1024);
         const uint64_t vlo = sdesc(vst + OPER + voff, 16, 1024);
-        mma_ts(tm + T_O, tm + T_PHI + 8u * kk, vhi, kIdescPV, kk > 0);
+        mma_ts(tm + T_O, tm + T_PHI + 8u * kk, vhi, kIdescPV, (j | kk) != 0);
         mma_ts(tm + T_O, tm + T_PHI + 8u * kk, vlo, kIdescPV, 1);
         mma_ts(tm + T_O, tm + T_PLO + 8u * kk, vhi, kIdescPV, 1);
       }
@@ -319,26 +321,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_before();
       mbar_arrive(q_ready);
     }
-    float o[HD];
-#pragma unroll
-    for (int c = 0; c < HD; ++c) o[c] = 0.f;
-    // running max m2 and scores are kept in the log2 domain: t = s * scale * log2(e)
+    // Scores live in the log2 domain: t = s * scale * log2(e). P is taken
+    // relative to a reference max m_ref that is raised lazily: only when a
+    // row's max exceeds it by more than 2^8 is the row's running context (in
+    // tensor memory, accumulated by the P.V MMAs) and sum rescaled, so P <= 256
+    // and the usual case needs no tensor-memory round trip.
     const float sl = p.scale * 1.4426950408889634f;
-    float m2 = -CUDART_INF_F, l = 0.f, alpha_prev = 1.f;
-    // Fold P_{j-1}.V_{j-1} (in tensor memory) into the fp32 context with the
-    // rescale of its tile, 16 columns at a time.
-    auto fold_o = [&](int jp, float alpha) {
-      mbar_wait(o_full, jp & 1, p.status, 0x4600 + jp);
-      fence_after();
-#pragma unroll
-      for (int c = 0; c < HD; c += 16) {
-        float ov[16];
-        tmem_ld16(lane_base + T_O + c, ov);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) o[c + i] = fmaf(o[c + i], alpha, ov[i]);
-      }
-    };
+    constexpr float kLazy = 8.0f;
+    float m_ref = -CUDART_INF_F, l = 0.f;
     for (int j = 0; j < nkv; ++j) {
       const int sb = j & 1;
       const int k0 = j * BKV;
@@ -360,33 +350,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_ld();
       fence_before();
       mbar_arrive(s_free(sb));
-      float mx = -CUDART_INF_F;
+      float mx4[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
 #pragma unroll
       for (int c = 0; c < BKV; ++c) {
         const uint32_t bit = ((c < 32 ? ok_lo : ok_hi) >> (c & 31)) & 1u;
         const bool ok = bit != 0 && (!diag || k0 + c <= row);
         sv[c] = ok ? sv[c] * sl : -CUDART_INF_F;
-        mx = fmaxf(mx, sv[c]);
+        mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
       }
-      const float m_new = fmaxf(m2, mx);
-      float alpha, psum = 0.f;
-      if (m_new == -CUDART_INF_F) {  // nothing allowed yet for this row
-        alpha = 1.f;
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      // the previous tile's P.V has to finish before P (and, on a rescale, O)
+      // is touched
+      const bool wait_prev = j > 0;
+      if (wait_prev) mbar_wait(o_full, (j - 1) & 1, p.status, 0x4600 + j);
+      if (mx > m_ref + kLazy || (m_ref == -CUDART_INF_F && mx != -CUDART_INF_F)) {
+        const float alpha = fast_exp2(m_ref - mx);  // 0 when m_ref is -inf
+        if (j > 0 && m_ref != -CUDART_INF_F) {
+          fence_after();
 #pragma unroll
-        for (int c = 0; c < BKV; ++c) sv[c] = 0.f;
-      } else {
-        alpha = fast_exp2(m2 - m_new);  // 0 when m2 is -inf
+          for (int c = 0; c < HD; c += 16) {
+            float ov[16];
+            tmem_ld16(lane_base + T_O + c, ov);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) ov[i] *= alpha;
+            tmem_st16(lane_base + T_O + c, ov);
+          }
+        }
+        l *= alpha;
+        m_ref = mx;
+      }
+      float ps4[4] = {0.f, 0.f, 0.f, 0.f};
+      if (m_ref != -CUDART_INF_F) {
 #pragma unroll
         for (int c = 0; c < BKV; ++c) {
-          sv[c] = fast_exp2(sv[c] - m_new);
-          psum += sv[c];
+          sv[c] = fast_exp2(sv[c] - m_ref);  // 0 for masked keys
+          ps4[c & 3] += sv[c];
         }
+      } else {
+#pragma unroll
+        for (int c = 0; c < BKV; ++c) sv[c] = 0.f;
       }
-      l = l * alpha + psum;
-      m2 = m_new;
-      // the previous tile's P.V must be done before P is overwritten: fold it now
-      if (j > 0) fold_o(j - 1, alpha_prev);
-      alpha_prev = alpha;
+      l += (ps4[0] + ps4[1]) + (ps4[2] + ps4[3]);
       // P (TF32 split) -> tensor memory
 #pragma unroll
       for (int c = 0; c < BKV; c += 16) {
@@ -403,20 +408,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_before();
       mbar_arrive(p_full);
     }
-    fold_o(nkv - 1, alpha_prev);
-    if (row_in) {
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      const int64_t off = (b * S + row) * (int64_t)D + (int64_t)h * HD;
+    // context = O / l, written as a TF32 split for the out_proj GEMM
+    mbar_wait(o_full, (nkv - 1) & 1, p.status, 0x4700);
+    fence_after();
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const int64_t off = (b * S + (row_in ? row : 0)) * (int64_t)D + (int64_t)h * HD;
 #pragma unroll
-      for (int c = 0; c < HD; c += 4) {
-        float4 hv, lv;
-        const float v0 = o[c] * inv, v1 = o[c + 1] * inv, v2 = o[c + 2] * inv, v3 = o[c + 3] * inv;
-        hv.x = tf32_round(v0); lv.x = v0 - hv.x;
-        hv.y = tf32_round(v1); lv.y = v1 - hv.y;
-        hv.z = tf32_round(v2); lv.z = v2 - hv.z;
-        hv.w = tf32_round(v3); lv.w = v3 - hv.w;
-        *reinterpret_cast<float4 *>(p.ctx_hi + off + c) = hv;
-        *reinterpret_cast<float4 *>(p.ctx_lo + off + c) = lv;
+    for (int c = 0; c < HD; c += 16) {
+      float ov[16];
+      tmem_ld16(lane_base + T_O + c, ov);
+      tmem_wait_ld();
+      if (row_in) {
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          float4 hv, lv;
+          const float v0 = ov[i] * inv, v1 = ov[i + 1] * inv, v2 = ov[i + 2] * inv, v3 = ov[i + 3] * inv;
+          hv.x = tf32_round(v0); lv.x = v0 - hv.x;
+          hv.y = tf32_round(v1); lv.y = v1 - hv.y;
+          hv.z = tf32_round(v2); lv.z = v2 - hv.z;
+          hv.w = tf32_round(v3); lv.w = v3 - hv.w;
+          *reinterpret_cast<float4 *>(p.ctx_hi + off + c + i) = hv;
+          *reinterpret_cast<float4 *>(p.ctx_lo + off + c + i) = lv;
+        }
       }
     }
   }
