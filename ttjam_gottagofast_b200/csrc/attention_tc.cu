@@ -217,13 +217,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(kv_full(s), 1);
       mbar_init(kv_empty(s), 1);
     }
+    // the softmax warps arrive once per warp (an elected lane after __syncwarp)
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full(i), 1);
-      mbar_init(s_free(i), 128);
+      mbar_init(s_free(i), 4);
     }
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 4);
     mbar_init(o_full, 1);
-    mbar_init(q_ready, 128);
+    mbar_init(q_ready, 4);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 2) {
@@ -263,14 +264,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_after();
       const uint32_t kst = base + s * STAGE;
       const uint32_t sd = tm + T_S0 + 64u * sb;
+      // descriptors built once; a k-step only advances the start-address field
+      const uint64_t khi0 = sdesc(kst, 16, 1024), klo0 = sdesc(kst + OPER, 16, 1024);
 #pragma unroll
       for (int kk = 0; kk < HD / 8; ++kk) {  // 8 head dims per MMA
-        const uint32_t koff = (uint32_t)(kk >> 2) * HALF + (uint32_t)(kk & 3) * 32u;
-        const uint64_t khi = sdesc(kst + koff, 16, 1024);
-        const uint64_t klo = sdesc(kst + OPER + koff, 16, 1024);
-        mma_ts(sd, tm + T_QHI + 8u * kk, khi, kIdescS, kk > 0);
-        mma_ts(sd, tm + T_QHI + 8u * kk, klo, kIdescS, 1);
-        mma_ts(sd, tm + T_QLO + 8u * kk, khi, kIdescS, 1);
+        const uint64_t koff = ((kk >> 2) * HALF + (kk & 3) * 32u) >> 4;
+        mma_ts(sd, tm + T_QHI + 8u * kk, khi0 + koff, kIdescS, kk > 0);
+        mma_ts(sd, tm + T_QHI + 8u * kk, klo0 + koff, kIdescS, 1);
+        mma_ts(sd, tm + T_QLO + 8u * kk, khi0 + koff, kIdescS, 1);
       }
       mma_commit(s_full(sb));
     };
@@ -282,14 +283,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(p_full, j & 1, p.status, 0x4400 + j);
       fence_after();
       const uint32_t vst = base + s * STAGE + 2 * OPER;
+      const uint64_t vhi0 = sdesc(vst, 16, 1024), vlo0 = sdesc(vst + OPER, 16, 1024);
 #pragma unroll
       for (int kk = 0; kk < BKV / 8; ++kk) {  // 8 keys per MMA
-        const uint32_t voff = (uint32_t)(kk >> 2) * HALF + (uint32_t)(kk & 3) * 32u;
-        const uint64_t vhi = sdesc(vst + voff, 16, 1024);
-        const uint64_t vlo = sdesc(vst + OPER + voff, 16, 1024);
-        mma_ts(tm + T_O, tm + T_PHI + 8u * kk, vhi, kIdescPV, (j | kk) != 0);
-        mma_ts(tm + T_O, tm + T_PHI + 8u * kk, vlo, kIdescPV, 1);
-        mma_ts(tm + T_O, tm + T_PLO + 8u * kk, vhi, kIdescPV, 1);
+        const uint64_t voff = ((kk >> 2) * HALF + (kk & 3) * 32u) >> 4;
+        mma_ts(tm + T_O, tm + T_PHI + 8u * kk, vhi0 + voff, kIdescPV, (j | kk) != 0);
+        mma_ts(tm + T_O, tm + T_PHI + 8u * kk, vlo0 + voff, kIdescPV, 1);
+        mma_ts(tm + T_O, tm + T_PLO + 8u * kk, vhi0 + voff, kIdescPV, 1);
       }
       mma_commit(o_full);
       mma_commit(kv_empty(s));
@@ -319,7 +319,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tmem_wait_st();
       fence_before();
-      mbar_arrive(q_ready);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_ready);
     }
     // Scores live in the log2 domain: t = s * scale * log2(e). P is taken
     // relative to a reference max m_ref that is raised lazily: only when a
@@ -349,7 +350,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < BKV; c += 16) tmem_ld16(lane_base + T_S0 + 64u * sb + c, sv + c);
       tmem_wait_ld();
       fence_before();
-      mbar_arrive(s_free(sb));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free(sb));
       float mx4[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
 #pragma unroll
       for (int c = 0; c < BKV; ++c) {
@@ -406,7 +408,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tmem_wait_st();
       fence_before();
-      mbar_arrive(p_full);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
     }
     // context = O / l, written as a TF32 split for the out_proj GEMM
     mbar_wait(o_full, (nkv - 1) & 1, p.status, 0x4700);

@@ -246,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full(b), 1);
-      mbar_init(acc_empty(b), kEpiWarps * 32);
+      mbar_init(acc_empty(b), kEpiWarps);  // one elected arrive per epilogue warp
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -290,15 +290,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(full_bar(s), n & 1, p.status, 0x2000);
         tc_fence_after();
         const uint32_t st = base + s * STAGE_BYTES;
+        // descriptors built once per stage; a k-step only advances the
+        // start-address field (32 bytes = 2 units of 16 bytes)
+        const uint64_t a_hi = umma_desc_sw64(st), a_lo = umma_desc_sw64(st + TILE_A);
+        const uint64_t w_hi = umma_desc_sw64(st + 2 * TILE_A);
+        const uint64_t w_lo = umma_desc_sw64(st + 2 * TILE_A + TILE_W);
 #pragma unroll
         for (int k = 0; k < BK / 8; ++k) {  // K = 8 tf32 = 32 bytes per MMA
-          const uint64_t a_hi = umma_desc_sw64(st + k * 32);
-          const uint64_t a_lo = umma_desc_sw64(st + TILE_A + k * 32);
-          const uint64_t w_hi = umma_desc_sw64(st + 2 * TILE_A + k * 32);
-          const uint64_t w_lo = umma_desc_sw64(st + 2 * TILE_A + TILE_W + k * 32);
-          umma_tf32(acc, a_hi, w_hi, IDESC, (kb | k) != 0);
-          umma_tf32(acc, a_hi, w_lo, IDESC, 1);
-          umma_tf32(acc, a_lo, w_hi, IDESC, 1);
+          const uint64_t ko = (uint64_t)(k * 2);
+          umma_tf32(acc, a_hi + ko, w_hi + ko, IDESC, (kb | k) != 0);
+          umma_tf32(acc, a_hi + ko, w_lo + ko, IDESC, 1);
+          umma_tf32(acc, a_lo + ko, w_hi + ko, IDESC, 1);
         }
         umma_commit(empty_bar(s));  // stage s is free once these MMAs have read it
       }
@@ -324,7 +326,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (row_in && n0 + c0 < p.N) epilogue_chunk(p, row, valid, n0 + c0, v);
       }
       tc_fence_before();
-      mbar_arrive(acc_empty(ab));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty(ab));
     }
   }
   tc_fence_before();
