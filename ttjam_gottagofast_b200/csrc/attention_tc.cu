@@ -21,12 +21,13 @@
 //             into a double-buffered S, then O_j = P_j.V_j (A = P from tensor
 //             memory, B = Vt tile); both B operands are K-major;
 //   warp 2    allocates / frees 512 tensor-memory columns;
-//   warps 4-7 softmax: thread t owns query row q0+t = tensor-memory lane t,
-//             loads its Q row into tensor memory, then per key tile reads S,
-//             applies scale + masks, updates the running sum, writes P (split)
-//             to tensor memory; the P.V MMAs accumulate the context in tensor
-//             memory, rescaled by its row's thread only when the row max grows
-//             by more than 2^8.
+//   warps 4-11 softmax, two warps per tensor-memory lane quarter: query row
+//             q0+t (= tensor-memory lane t) is shared by two threads, one per
+//             half of the 64-key tile; they exchange the row max through shared
+//             memory (one named barrier per tile), write their half of P (split)
+//             to tensor memory and keep a partial row sum. The P.V MMAs
+//             accumulate the context in tensor memory, rescaled only when the
+//             row max grows by more than 2^8.
 // Every mbarrier wait is bounded; a wait that gives up latches
 // TT_ERR_DEVICE_TIMEOUT and the kernel still frees tensor memory and returns.
 // No TMA load here uses cluster multicast.
@@ -39,7 +40,7 @@ namespace tt {
 namespace {
 
 constexpr int HD = 64, BQ = 128, BKV = 64, STAGES = 3;
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;  // warps 0-3: TMA / MMA / TMEM; warps 4-11: softmax
 constexpr uint32_t HALF = BKV * 128;       // one [64 rows x 32 fp32] swizzled box: 8 KB
 constexpr uint32_t OPER = 2 * HALF;        // one 64 x 64 operand: 16 KB
 constexpr uint32_t STAGE = 4 * OPER;       // K_hi, K_lo, V_hi, V_lo: 64 KB
@@ -176,6 +177,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap tm_vlo, const AttentionTcParams p) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ int s_kv_len;
+  __shared__ float s_rowmax[2][2][128];  // [tile parity][key half][row]
+  __shared__ float s_rowsum[2][128];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   const uint32_t bars = base + STAGES * STAGE;
@@ -217,14 +220,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(kv_full(s), 1);
       mbar_init(kv_empty(s), 1);
     }
-    // the softmax warps arrive once per warp (an elected lane after __syncwarp)
+    // the 8 softmax warps arrive once per warp (an elected lane after __syncwarp)
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full(i), 1);
-      mbar_init(s_free(i), 4);
+      mbar_init(s_free(i), 8);
     }
-    mbar_init(p_full, 4);
+    mbar_init(p_full, 8);
     mbar_init(o_full, 1);
-    mbar_init(q_ready, 4);
+    mbar_init(q_ready, 8);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 2) {
@@ -295,26 +298,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(kv_empty(s));
     }
   } else if (warp >= 4) {
-    // ---- softmax: thread t <-> query row q0+t <-> tensor-memory lane t -----
-    const int t = threadIdx.x - 128;
+    // ---- softmax: rows split over two warpgroups by key half ----------------
+    const int t = (warp & 3) * 32 + lane;   // row within the tile = tensor-memory lane
+    const int kh = (warp - 4) >> 2;         // which 32 keys (and 32 dims) of a tile
     const int row = q0 + t;
     const bool row_in = row < S;
     const uint32_t lane_base = tm + ((uint32_t)((warp & 3) * 32) << 16);
+    const uint32_t col_off = 32u * kh;
     {
-      const int64_t qoff = (b * S + (row_in ? row : 0)) * (int64_t)(3 * D) + (int64_t)h * HD;
+      // Q row -> tensor memory: this thread loads dims [32*kh, 32*kh+32)
+      const int64_t qoff = (b * S + (row_in ? row : 0)) * (int64_t)(3 * D) + (int64_t)h * HD + col_off;
       float v[16];
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
         const float *src = (which ? p.qkv_lo : p.qkv_hi) + qoff;
 #pragma unroll
-        for (int c = 0; c < HD; c += 16) {
+        for (int c = 0; c < 32; c += 16) {
 #pragma unroll
           for (int i = 0; i < 16; i += 4) {
             const float4 x = row_in ? *reinterpret_cast<const float4 *>(src + c + i)
                                     : make_float4(0.f, 0.f, 0.f, 0.f);
             v[i] = x.x; v[i + 1] = x.y; v[i + 2] = x.z; v[i + 3] = x.w;
           }
-          tmem_st16(lane_base + (which ? T_QLO : T_QHI) + c, v);
+          tmem_st16(lane_base + (which ? T_QLO : T_QHI) + col_off + c, v);
         }
       }
       tmem_wait_st();
@@ -324,59 +330,57 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // Scores live in the log2 domain: t = s * scale * log2(e). P is taken
     // relative to a reference max m_ref that is raised lazily: only when a
-    // row's max exceeds it by more than 2^8 is the row's running context (in
+    // row's max exceeds it by more than 2^8 are the row's running context (in
     // tensor memory, accumulated by the P.V MMAs) and sum rescaled, so P <= 256
-    // and the usual case needs no tensor-memory round trip.
+    // and the usual case needs no tensor-memory round trip. Both threads of a
+    // row see the same maxima, so they take the same decisions.
     const float sl = p.scale * 1.4426950408889634f;
     constexpr float kLazy = 8.0f;
     float m_ref = -CUDART_INF_F, l = 0.f;
     for (int j = 0; j < nkv; ++j) {
       const int sb = j & 1;
-      const int k0 = j * BKV;
-      // validity of the tile's 64 keys: padding mask and kv_end, two ballots
-      uint32_t ok_lo, ok_hi;
+      const int k0 = j * BKV + 32 * kh;     // first key of this thread's half
+      uint32_t ok;
       {
-        const int ka = k0 + lane, kb = k0 + 32 + lane;
-        const bool va = ka < kv_end && (mrow == nullptr || mrow[ka] != 0);
-        const bool vb = kb < kv_end && (mrow == nullptr || mrow[kb] != 0);
-        ok_lo = __ballot_sync(0xffffffffu, va);
-        ok_hi = __ballot_sync(0xffffffffu, vb);
+        const int ka = k0 + lane;
+        ok = __ballot_sync(0xffffffffu, ka < kv_end && (mrow == nullptr || mrow[ka] != 0));
       }
-      const bool diag = p.causal && k0 + BKV - 1 > q0;  // tile reaches past the first query
+      const bool diag = p.causal && k0 + 31 > q0;  // half reaches past the first query
       mbar_wait(s_full(sb), (j >> 1) & 1, p.status, 0x4500 + j);
       fence_after();
-      float sv[BKV];
-#pragma unroll
-      for (int c = 0; c < BKV; c += 16) tmem_ld16(lane_base + T_S0 + 64u * sb + c, sv + c);
+      float sv[32];
+      tmem_ld16(lane_base + T_S0 + 64u * sb + col_off, sv);
+      tmem_ld16(lane_base + T_S0 + 64u * sb + col_off + 16, sv + 16);
       tmem_wait_ld();
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free(sb));
       float mx4[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
 #pragma unroll
-      for (int c = 0; c < BKV; ++c) {
-        const uint32_t bit = ((c < 32 ? ok_lo : ok_hi) >> (c & 31)) & 1u;
-        const bool ok = bit != 0 && (!diag || k0 + c <= row);
-        sv[c] = ok ? sv[c] * sl : -CUDART_INF_F;
+      for (int c = 0; c < 32; ++c) {
+        const bool okc = ((ok >> c) & 1u) != 0 && (!diag || k0 + c <= row);
+        sv[c] = okc ? sv[c] * sl : -CUDART_INF_F;
         mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
       }
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      s_rowmax[sb][kh][t] = mx;
+      asm volatile("bar.sync 1, 256;" ::: "memory");  // the 8 softmax warps
+      mx = fmaxf(mx, s_rowmax[sb][kh ^ 1][t]);
       // the previous tile's P.V has to finish before P (and, on a rescale, O)
       // is touched
-      const bool wait_prev = j > 0;
-      if (wait_prev) mbar_wait(o_full, (j - 1) & 1, p.status, 0x4600 + j);
+      if (j > 0) mbar_wait(o_full, (j - 1) & 1, p.status, 0x4600 + j);
       if (mx > m_ref + kLazy || (m_ref == -CUDART_INF_F && mx != -CUDART_INF_F)) {
         const float alpha = fast_exp2(m_ref - mx);  // 0 when m_ref is -inf
         if (j > 0 && m_ref != -CUDART_INF_F) {
           fence_after();
 #pragma unroll
-          for (int c = 0; c < HD; c += 16) {
+          for (int c = 0; c < 32; c += 16) {
             float ov[16];
-            tmem_ld16(lane_base + T_O + c, ov);
+            tmem_ld16(lane_base + T_O + col_off + c, ov);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 16; ++i) ov[i] *= alpha;
-            tmem_st16(lane_base + T_O + c, ov);
+            tmem_st16(lane_base + T_O + col_off + c, ov);
           }
         }
         l *= alpha;
@@ -385,41 +389,45 @@ __global__ void __launch_bounds__(kThreads, 1)
       float ps4[4] = {0.f, 0.f, 0.f, 0.f};
       if (m_ref != -CUDART_INF_F) {
 #pragma unroll
-        for (int c = 0; c < BKV; ++c) {
+        for (int c = 0; c < 32; ++c) {
           sv[c] = fast_exp2(sv[c] - m_ref);  // 0 for masked keys
           ps4[c & 3] += sv[c];
         }
       } else {
 #pragma unroll
-        for (int c = 0; c < BKV; ++c) sv[c] = 0.f;
+        for (int c = 0; c < 32; ++c) sv[c] = 0.f;
       }
       l += (ps4[0] + ps4[1]) + (ps4[2] + ps4[3]);
-      // P (TF32 split) -> tensor memory
+      // this half of P (TF32 split) -> tensor memory
 #pragma unroll
-      for (int c = 0; c < BKV; c += 16) {
+      for (int c = 0; c < 32; c += 16) {
         float hi[16], lo[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           hi[i] = tf32_round(sv[c + i]);
           lo[i] = sv[c + i] - hi[i];
         }
-        tmem_st16(lane_base + T_PHI + c, hi);
-        tmem_st16(lane_base + T_PLO + c, lo);
+        tmem_st16(lane_base + T_PHI + col_off + c, hi);
+        tmem_st16(lane_base + T_PLO + col_off + c, lo);
       }
       tmem_wait_st();
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    // context = O / l, written as a TF32 split for the out_proj GEMM
+    // row sum = both halves' partial sums
+    s_rowsum[kh][t] = l;
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    l += s_rowsum[kh ^ 1][t];
+    // context = O / l (this thread's 32 dims), written as a TF32 split
     mbar_wait(o_full, (nkv - 1) & 1, p.status, 0x4700);
     fence_after();
     const float inv = l > 0.f ? 1.f / l : 0.f;
-    const int64_t off = (b * S + (row_in ? row : 0)) * (int64_t)D + (int64_t)h * HD;
+    const int64_t off = (b * S + (row_in ? row : 0)) * (int64_t)D + (int64_t)h * HD + col_off;
 #pragma unroll
-    for (int c = 0; c < HD; c += 16) {
+    for (int c = 0; c < 32; c += 16) {
       float ov[16];
-      tmem_ld16(lane_base + T_O + c, ov);
+      tmem_ld16(lane_base + T_O + col_off + c, ov);
       tmem_wait_ld();
       if (row_in) {
 #pragma unroll
