@@ -1,5 +1,5 @@
 // Causal / key-padded flash attention on tensor cores (tcgen05, 3xTF32) for
-// head_dim 64 -- the attention core of the d_model >= 512 workloads.
+// head_dim 32 and 64.
 //
 // Semantics as the reference attention (torch_transformer_benchmark.py:97-117):
 // s = (q . k) * hd^-0.5, -inf for keys after the query (causal, :99-103) and
@@ -13,10 +13,10 @@
 // threads. The context accumulates in fp32 in tensor memory.
 //
 // CTA = (query tile of 128 rows, head, sequence); 256 threads:
-//   warp 0    TMA producer: per 64-key tile, K_hi K_lo (64 keys x 64 dims) and
-//             Vt_hi Vt_lo (64 dims x 64 keys, from the transposed copy of v the
-//             q|k|v GEMM writes), two 128-byte swizzle boxes each, into a
-//             3-stage ring;
+//   warp 0    TMA producer: per 64-key tile, K_hi K_lo (64 keys x HD dims) and
+//             Vt_hi Vt_lo (HD dims x 64 keys, from the transposed copy of v the
+//             q|k|v GEMM writes), in 128-byte swizzle boxes, into a 3-stage
+//             ring;
 //   warp 1    MMA issuer: S[j] = Q.K_j^T (A = Q from tensor memory, B = K tile)
 //             into a double-buffered S, then O_j = P_j.V_j (A = P from tensor
 //             memory, B = Vt tile); both B operands are K-major;
@@ -39,15 +39,31 @@
 namespace tt {
 namespace {
 
-constexpr int HD = 64, BQ = 128, BKV = 64, STAGES = 3;
+constexpr int BQ = 128, BKV = 64, STAGES = 3;
 constexpr int kThreads = 384;  // warps 0-3: TMA / MMA / TMEM; warps 4-11: softmax
-constexpr uint32_t HALF = BKV * 128;       // one [64 rows x 32 fp32] swizzled box: 8 KB
-constexpr uint32_t OPER = 2 * HALF;        // one 64 x 64 operand: 16 KB
-constexpr uint32_t STAGE = 4 * OPER;       // K_hi, K_lo, V_hi, V_lo: 64 KB
-constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE + 1024 + 256;
-// tensor-memory columns (fp32 cells): Q_hi, Q_lo, S[2], P_hi, P_lo, O
-constexpr uint32_t T_QHI = 0, T_QLO = 64, T_S0 = 128, T_PHI = 256, T_PLO = 320, T_O = 384;
-constexpr uint32_t TMEM_COLS = 512;
+
+// Shapes for head_dim HD (32 or 64). Shared-memory stage: K_hi, K_lo
+// (64 keys x HD, HD/32 boxes of 64 rows x 128 B) then Vt_hi, Vt_lo (HD rows x
+// 64 keys, 2 boxes of HD rows x 128 B). Tensor-memory columns (fp32 cells):
+// Q_hi, Q_lo, S[2] (64 each), P_hi, P_lo (64 each), O (HD).
+template <int HD>
+struct AtShape {
+  static constexpr uint32_t KBOX = 64 * 128;           // one 64-row K box
+  static constexpr uint32_t VBOX = HD * 128;           // one HD-row V^T box
+  static constexpr uint32_t OPK = (HD / 32) * KBOX;    // one K operand (hi or lo)
+  static constexpr uint32_t OPV = 2 * VBOX;            // one V^T operand (hi or lo)
+  static constexpr uint32_t STAGE = 2 * OPK + 2 * OPV;
+  static constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE + 1024 + 256;
+  static constexpr uint32_t T_QHI = 0, T_QLO = HD, T_S0 = 2 * HD, T_PHI = 2 * HD + 128,
+                            T_PLO = 2 * HD + 192, T_O = 2 * HD + 256;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static_assert(T_O + HD <= TMEM_COLS, "tensor memory");
+  // instruction descriptors: D fp32, A/B tf32, both K-major, M = 128
+  static constexpr uint32_t IDESC_S = (1u << 4) | (2u << 7) | (2u << 10) |
+                                      ((uint32_t)(64 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+  static constexpr uint32_t IDESC_PV = (1u << 4) | (2u << 7) | (2u << 10) |
+                                       ((uint32_t)(HD >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -106,13 +122,6 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t
   d |= (uint64_t)2 << 61;
   return d;
 }
-// Instruction descriptors: D fp32, A/B tf32, M = 128, N = 64.
-//   S = Q.K^T : A K-major (tensor memory), B K-major
-//   O = P.V   : A K-major (tensor memory), B = V^T tile, K-major (keys contiguous)
-constexpr uint32_t kIdescS = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(64 >> 3) << 17) |
-                             ((uint32_t)(128 >> 4) << 24);
-constexpr uint32_t kIdescPV = kIdescS;
-
 __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
                                        uint32_t idesc, uint32_t accum) {
   asm volatile(
@@ -170,11 +179,16 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+template <int HD>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_hi,
                         const __grid_constant__ CUtensorMap tm_lo,
                         const __grid_constant__ CUtensorMap tm_vhi,
                         const __grid_constant__ CUtensorMap tm_vlo, const AttentionTcParams p) {
+  using Sh = AtShape<HD>;
+  constexpr uint32_t STAGE = Sh::STAGE, OPK = Sh::OPK, OPV = Sh::OPV;
+  constexpr uint32_t T_QHI = Sh::T_QHI, T_QLO = Sh::T_QLO, T_S0 = Sh::T_S0, T_PHI = Sh::T_PHI,
+                     T_PLO = Sh::T_PLO, T_O = Sh::T_O, TMEM_COLS = Sh::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   __shared__ int s_kv_len;
   __shared__ float s_rowmax[2][2][128];  // [tile parity][key half][row]
@@ -250,12 +264,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (j >= STAGES) mbar_wait(kv_empty(s), (n - 1) & 1, p.status, 0x4100 + j);
       const uint32_t st = base + s * STAGE;
       mbar_expect_tx(kv_full(s), STAGE);
+      // K rows = keys, 32 dims per box; Vt rows = dims, 32 keys per box
+      for (int bx = 0; bx < HD / 32; ++bx) {
+        tma_load_3d(st + bx * Sh::KBOX, &tm_hi, kcol + 32 * bx, j * BKV, (int)b, kv_full(s));
+        tma_load_3d(st + OPK + bx * Sh::KBOX, &tm_lo, kcol + 32 * bx, j * BKV, (int)b, kv_full(s));
+      }
       for (int half = 0; half < 2; ++half) {
-        // K rows = keys, 32 dims per box; Vt rows = dims, 32 keys per box
-        tma_load_3d(st + half * HALF, &tm_hi, kcol + 32 * half, j * BKV, (int)b, kv_full(s));
-        tma_load_3d(st + OPER + half * HALF, &tm_lo, kcol + 32 * half, j * BKV, (int)b, kv_full(s));
-        tma_load_3d(st + 2 * OPER + half * HALF, &tm_vhi, j * BKV + 32 * half, 0, bh, kv_full(s));
-        tma_load_3d(st + 3 * OPER + half * HALF, &tm_vlo, j * BKV + 32 * half, 0, bh, kv_full(s));
+        tma_load_3d(st + 2 * OPK + half * Sh::VBOX, &tm_vhi, j * BKV + 32 * half, 0, bh, kv_full(s));
+        tma_load_3d(st + 2 * OPK + OPV + half * Sh::VBOX, &tm_vlo, j * BKV + 32 * half, 0, bh,
+                    kv_full(s));
       }
     }
   } else if (warp == 1 && lane == 0) {
@@ -268,13 +285,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t kst = base + s * STAGE;
       const uint32_t sd = tm + T_S0 + 64u * sb;
       // descriptors built once; a k-step only advances the start-address field
-      const uint64_t khi0 = sdesc(kst, 16, 1024), klo0 = sdesc(kst + OPER, 16, 1024);
+      const uint64_t khi0 = sdesc(kst, 16, 1024), klo0 = sdesc(kst + OPK, 16, 1024);
 #pragma unroll
       for (int kk = 0; kk < HD / 8; ++kk) {  // 8 head dims per MMA
-        const uint64_t koff = ((kk >> 2) * HALF + (kk & 3) * 32u) >> 4;
-        mma_ts(sd, tm + T_QHI + 8u * kk, khi0 + koff, kIdescS, kk > 0);
-        mma_ts(sd, tm + T_QHI + 8u * kk, klo0 + koff, kIdescS, 1);
-        mma_ts(sd, tm + T_QLO + 8u * kk, khi0 + koff, kIdescS, 1);
+        const uint64_t koff = ((kk >> 2) * Sh::KBOX + (kk & 3) * 32u) >> 4;
+        mma_ts(sd, tm + T_QHI + 8u * kk, khi0 + koff, Sh::IDESC_S, kk > 0);
+        mma_ts(sd, tm + T_QHI + 8u * kk, klo0 + koff, Sh::IDESC_S, 1);
+        mma_ts(sd, tm + T_QLO + 8u * kk, khi0 + koff, Sh::IDESC_S, 1);
       }
       mma_commit(s_full(sb));
     };
@@ -285,14 +302,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int s = j % STAGES;
       mbar_wait(p_full, j & 1, p.status, 0x4400 + j);
       fence_after();
-      const uint32_t vst = base + s * STAGE + 2 * OPER;
-      const uint64_t vhi0 = sdesc(vst, 16, 1024), vlo0 = sdesc(vst + OPER, 16, 1024);
+      const uint32_t vst = base + s * STAGE + 2 * OPK;
+      const uint64_t vhi0 = sdesc(vst, 16, 1024), vlo0 = sdesc(vst + OPV, 16, 1024);
 #pragma unroll
       for (int kk = 0; kk < BKV / 8; ++kk) {  // 8 keys per MMA
-        const uint64_t voff = ((kk >> 2) * HALF + (kk & 3) * 32u) >> 4;
-        mma_ts(tm + T_O, tm + T_PHI + 8u * kk, vhi0 + voff, kIdescPV, (j | kk) != 0);
-        mma_ts(tm + T_O, tm + T_PHI + 8u * kk, vlo0 + voff, kIdescPV, 1);
-        mma_ts(tm + T_O, tm + T_PLO + 8u * kk, vhi0 + voff, kIdescPV, 1);
+        const uint64_t voff = ((kk >> 2) * Sh::VBOX + (kk & 3) * 32u) >> 4;
+        mma_ts(tm + T_O, tm + T_PHI + 8u * kk, vhi0 + voff, Sh::IDESC_PV, (j | kk) != 0);
+        mma_ts(tm + T_O, tm + T_PHI + 8u * kk, vlo0 + voff, Sh::IDESC_PV, 1);
+        mma_ts(tm + T_O, tm + T_PLO + 8u * kk, vhi0 + voff, Sh::IDESC_PV, 1);
       }
       mma_commit(o_full);
       mma_commit(kv_empty(s));
@@ -304,23 +321,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = q0 + t;
     const bool row_in = row < S;
     const uint32_t lane_base = tm + ((uint32_t)((warp & 3) * 32) << 16);
-    const uint32_t col_off = 32u * kh;
+    const uint32_t col_off = 32u * kh;             // this thread's 32 keys of a tile
+    const uint32_t dim_off = (uint32_t)(HD / 2) * kh;  // ... and HD/2 dims of Q and O
     {
-      // Q row -> tensor memory: this thread loads dims [32*kh, 32*kh+32)
-      const int64_t qoff = (b * S + (row_in ? row : 0)) * (int64_t)(3 * D) + (int64_t)h * HD + col_off;
+      // Q row -> tensor memory: this thread loads dims [dim_off, dim_off + HD/2)
+      const int64_t qoff = (b * S + (row_in ? row : 0)) * (int64_t)(3 * D) + (int64_t)h * HD + dim_off;
       float v[16];
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
         const float *src = (which ? p.qkv_lo : p.qkv_hi) + qoff;
 #pragma unroll
-        for (int c = 0; c < 32; c += 16) {
+        for (int c = 0; c < HD / 2; c += 16) {
 #pragma unroll
           for (int i = 0; i < 16; i += 4) {
             const float4 x = row_in ? *reinterpret_cast<const float4 *>(src + c + i)
                                     : make_float4(0.f, 0.f, 0.f, 0.f);
             v[i] = x.x; v[i + 1] = x.y; v[i + 2] = x.z; v[i + 3] = x.w;
           }
-          tmem_st16(lane_base + (which ? T_QLO : T_QHI) + col_off + c, v);
+          tmem_st16(lane_base + (which ? T_QLO : T_QHI) + dim_off + c, v);
         }
       }
       tmem_wait_st();
@@ -374,13 +392,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j > 0 && m_ref != -CUDART_INF_F) {
           fence_after();
 #pragma unroll
-          for (int c = 0; c < 32; c += 16) {
+          for (int c = 0; c < HD / 2; c += 16) {
             float ov[16];
-            tmem_ld16(lane_base + T_O + col_off + c, ov);
+            tmem_ld16(lane_base + T_O + dim_off + c, ov);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 16; ++i) ov[i] *= alpha;
-            tmem_st16(lane_base + T_O + col_off + c, ov);
+            tmem_st16(lane_base + T_O + dim_off + c, ov);
           }
         }
         l *= alpha;
@@ -419,15 +437,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     s_rowsum[kh][t] = l;
     asm volatile("bar.sync 1, 256;" ::: "memory");
     l += s_rowsum[kh ^ 1][t];
-    // context = O / l (this thread's 32 dims), written as a TF32 split
+    // context = O / l (this thread's HD/2 dims), written as a TF32 split
     mbar_wait(o_full, (nkv - 1) & 1, p.status, 0x4700);
     fence_after();
     const float inv = l > 0.f ? 1.f / l : 0.f;
-    const int64_t off = (b * S + (row_in ? row : 0)) * (int64_t)D + (int64_t)h * HD + col_off;
+    const int64_t off = (b * S + (row_in ? row : 0)) * (int64_t)D + (int64_t)h * HD + dim_off;
 #pragma unroll
-    for (int c = 0; c < 32; c += 16) {
+    for (int c = 0; c < HD / 2; c += 16) {
       float ov[16];
-      tmem_ld16(lane_base + T_O + col_off + c, ov);
+      tmem_ld16(lane_base + T_O + dim_off + c, ov);
       tmem_wait_ld();
       if (row_in) {
 #pragma unroll
@@ -492,15 +510,15 @@ int make_qkv_map(CUtensorMap *tm, const float *ptr, int64_t batch, int seq, int 
   return TT_OK;
 }
 
-// [batch*heads, 64, seq] view of a transposed value buffer (row stride seq_pad);
-// box = 32 keys x 64 dims x 1, 128-byte swizzle, zero fill past the sequence.
-int make_vt_map(CUtensorMap *tm, const float *ptr, int64_t bh, int seq, int seq_pad) {
+// [batch*heads, hd, seq] view of a transposed value buffer (row stride seq_pad);
+// box = 32 keys x hd dims x 1, 128-byte swizzle, zero fill past the sequence.
+int make_vt_map(CUtensorMap *tm, const float *ptr, int64_t bh, int seq, int seq_pad, int hd) {
   EncodeTiledFn encode;
   int rc = encode_fn(&encode);
   if (rc != TT_OK) return rc;
-  cuuint64_t dims[3] = {(cuuint64_t)seq, (cuuint64_t)HD, (cuuint64_t)bh};
-  cuuint64_t strides[2] = {(cuuint64_t)seq_pad * 4, (cuuint64_t)seq_pad * HD * 4};
-  cuuint32_t box[3] = {32, (cuuint32_t)HD, 1};
+  cuuint64_t dims[3] = {(cuuint64_t)seq, (cuuint64_t)hd, (cuuint64_t)bh};
+  cuuint64_t strides[2] = {(cuuint64_t)seq_pad * 4, (cuuint64_t)seq_pad * hd * 4};
+  cuuint32_t box[3] = {32, (cuuint32_t)hd, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(ptr), dims,
                             strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -512,16 +530,33 @@ int make_vt_map(CUtensorMap *tm, const float *ptr, int64_t bh, int seq, int seq_
   return TT_OK;
 }
 
+template <int HD>
+int launch_hd(const AttentionTcParams &p, const CUtensorMap &thi, const CUtensorMap &tlo,
+              const CUtensorMap &tvhi, const CUtensorMap &tvlo, cudaStream_t stream) {
+  using Sh = AtShape<HD>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    TT_CUDA_TRY(cudaFuncSetAttribute(attention_tc_kernel<HD>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)Sh::SMEM_BYTES));
+    attr_set = true;
+  }
+  dim3 grid((unsigned)((p.seq + BQ - 1) / BQ), (unsigned)p.num_heads, (unsigned)p.batch);
+  attention_tc_kernel<HD><<<grid, kThreads, Sh::SMEM_BYTES, stream>>>(thi, tlo, tvhi, tvlo, p);
+  TT_LAUNCH_CHECK("attention_tc");
+  return TT_OK;
+}
+
 }  // namespace
 
 bool attention_tc_supported(int head_dim, int d_model) {
-  return head_dim == HD && d_model % 4 == 0;
+  return (head_dim == 32 || head_dim == 64) && d_model % 4 == 0;
 }
 
 int launch_attention_tc(const AttentionTcParams &p, cudaStream_t stream) {
   if (p.batch <= 0 || p.seq <= 0) return TT_OK;
   if (!attention_tc_supported(p.head_dim, p.d_model))
-    return fail(TT_ERR_UNSUPPORTED, "attention_tc: head_dim must be 64");
+    return fail(TT_ERR_UNSUPPORTED, "attention_tc: head_dim must be 32 or 64");
   if (p.batch > 65535 || p.num_heads > 65535)
     return fail(TT_ERR_UNSUPPORTED, "attention_tc: batch and num_heads must be <= 65535");
   if (((reinterpret_cast<uintptr_t>(p.qkv_hi) | reinterpret_cast<uintptr_t>(p.qkv_lo) |
@@ -534,19 +569,11 @@ int launch_attention_tc(const AttentionTcParams &p, cudaStream_t stream) {
   int rc;
   if ((rc = make_qkv_map(&thi, p.qkv_hi, p.batch, p.seq, p.d_model)) ||
       (rc = make_qkv_map(&tlo, p.qkv_lo, p.batch, p.seq, p.d_model)) ||
-      (rc = make_vt_map(&tvhi, p.vt_hi, p.batch * p.num_heads, p.seq, p.seq_pad)) ||
-      (rc = make_vt_map(&tvlo, p.vt_lo, p.batch * p.num_heads, p.seq, p.seq_pad)))
+      (rc = make_vt_map(&tvhi, p.vt_hi, p.batch * p.num_heads, p.seq, p.seq_pad, p.head_dim)) ||
+      (rc = make_vt_map(&tvlo, p.vt_lo, p.batch * p.num_heads, p.seq, p.seq_pad, p.head_dim)))
     return rc;
-  static bool attr_set = false;
-  if (!attr_set) {
-    TT_CUDA_TRY(cudaFuncSetAttribute(attention_tc_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
-    attr_set = true;
-  }
-  dim3 grid((unsigned)((p.seq + BQ - 1) / BQ), (unsigned)p.num_heads, (unsigned)p.batch);
-  attention_tc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(thi, tlo, tvhi, tvlo, p);
-  TT_LAUNCH_CHECK("attention_tc");
-  return TT_OK;
+  return p.head_dim == 32 ? launch_hd<32>(p, thi, tlo, tvhi, tvlo, stream)
+                          : launch_hd<64>(p, thi, tlo, tvhi, tvlo, stream);
 }
 
 }  // namespace tt

@@ -23,9 +23,12 @@ namespace tt {
 
 enum ForwardPlan : int { PLAN_CLUSTER = 1, PLAN_OPS_FFMA = 2, PLAN_OPS_TC = 3 };
 
-// The 3xTF32 tensor-core GEMMs take over where d_model >= 512 makes every
-// projection a large dense contraction.
-inline bool uses_tensor_cores(const tt_config &cfg) { return cfg.d_model >= 512; }
+// Shapes the 3xTF32 tensor-core schedule can run: every GEMM operand row must
+// be a whole number of 16-byte TMA units (d_model and ffn_dim multiples of 4).
+// The packed image then carries the TF32 split of every weight.
+inline bool uses_tensor_cores(const tt_config &cfg) {
+  return cfg.d_model % 4 == 0 && cfg.ffn_dim % 4 == 0;
+}
 
 struct LayerOffsets {
   size_t ln1_w, ln1_b, wqkv, bqkv, wo, bo, ln2_w, ln2_b, w1, b1, w2, b2;
@@ -89,7 +92,8 @@ struct WorkspaceLayout {
       cur = align_up(cur + n_floats * f4, 256);
       return off;
     };
-    tc_attention = tensor && cfg.d_model / cfg.num_heads == 64;
+    const int hd = cfg.d_model / cfg.num_heads;
+    tc_attention = tensor && (hd == 32 || hd == 64);
     if (tc_attention) {
       // q|k as a TF32 split, and v transposed per (sequence, head) with keys
       // contiguous, for the tensor-core attention
