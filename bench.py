@@ -18,8 +18,11 @@ Our arm prints one JSON line with
              (UserOptimizedTransformer.forward) from pinned host buffers, with
              the host->device copy of x and the mask and the device->host copy
              of y inside each timed step;
-  roofline   the forward against measured HBM bandwidth (algorithmic bytes:
-             packed weights read once + x read + y written);
+  roofline   the dominant kernel kind (largest share of the timed device
+             time, each launch bracketed by CUDA events on its stream through
+             the library's launch probe) against its bound: 3xTF32 tensor
+             (algorithmic fp32 FLOP; peak = measured bf16 / 2 / 3) or HBM
+             (algorithmic bytes floor); `kernels` lists every kind's share;
   cpu_baseline  the reference forward (oracle restatement, torch eager fp32)
              on this host's CPU cores, rank 0 at N=1 only.
 Multi-GPU runs use torchrun (one process per GPU, NCCL); every rank runs its
@@ -113,13 +116,44 @@ def per_rank_batch(w, world, rank):
 # measurement helpers
 # ---------------------------------------------------------------------------
 def load_peaks():
+    """(HBM GB/s, bf16 TFLOP/s burst, bf16 TFLOP/s sustained, source)."""
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(path) as fh:
             pk = json.load(fh)
-        return float(pk["hbm_gbs"]), float(pk["bf16_tflops"]), "measured"
+        return (float(pk["hbm_gbs"]), float(pk["bf16_tflops"]),
+                float(pk.get("bf16_tflops_sustained", pk["bf16_tflops"])), "measured")
     except Exception:
-        return 6650.0, 1590.0, "fallback"
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
+# dominant kernel kind, from one ncu capture per (workload, kind); the
+# profiles/ file named beside each entry gives the command and the capture.
+NCU_TRAFFIC = {}
+
+
+def kind_work(kind, cfg, b, s, lens, mask_bytes):
+    """Algorithmic (fp32 FLOP, bytes floor) of ONE launch of a kernel kind:
+    GEMMs count valid tokens only (2*Tv*N*K), attention counts causal valid
+    pairs (4*D*sum len(len+1)/2), bytes count each operand once."""
+    d, f = cfg.d_model, cfg.ffn_dim
+    t = b * s
+    tv = float(lens.sum())
+    pairs = float((lens * (lens + 1) / 2).sum()) if cfg.causal else float((lens * lens).sum())
+    if kind == "qkv":
+        return 2 * tv * 3 * d * d, 4 * (t * d + 3 * d * d + 3 * d + t * 3 * d)
+    if kind == "attention":
+        return 4 * d * pairs, 4 * (t * 3 * d + t * d) + mask_bytes
+    if kind == "out_proj":
+        return 2 * tv * d * d, 4 * (t * d + d * d + d + 2 * t * d) + mask_bytes
+    if kind == "ffn_in":
+        return 2 * tv * d * f, 4 * (t * d + f * d + f + t * f)
+    if kind == "ffn_out":
+        return 2 * tv * f * d, 4 * (t * f + d * f + d + 2 * t * d) + mask_bytes
+    if kind in ("layernorm", "final_norm"):
+        return 0.0, 4 * 2 * t * d
+    return None  # whole_forward: the caller uses the forward's totals
 
 
 class ClockSampler:
@@ -316,6 +350,9 @@ def run_ours(args, world, rank, local):
             step()
         torch.cuda.synchronize(dev)
 
+    launches = lib.tt_forward_launch_count(cfg_ref, nb, S)
+    probe_cap = launches * args.steps
+    _lib.check(lib.tt_launch_probe_start(probe_cap), "tt_launch_probe_start", lib)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     barrier(world)
@@ -329,6 +366,12 @@ def run_ours(args, world, rank, local):
     barrier(world)
     clocks = sampler.stop()
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    launch_ms = (ctypes.c_float * probe_cap)()
+    launch_kind = (ctypes.c_int32 * probe_cap)()
+    n_probed = lib.tt_launch_probe_read(launch_ms, launch_kind, probe_cap)
+    if n_probed < 0:
+        _lib.check(n_probed, "tt_launch_probe_read", lib)
+    lib.tt_launch_probe_start(0)
     total_ms = max_over_ranks(sum(step_ms), world)
     med_ms = max_over_ranks(statistics.median(step_ms), world)
     tokens_per_step_all = (cfg.batch_size if scaling == "strong" else nb * world) * S
@@ -365,25 +408,60 @@ def run_ours(args, world, rank, local):
     e2e_value = tokens_per_step_all * args.steps * 1000.0 / e_total
     assert torch.equal(yh, y.cpu()), "e2e output differs from the device-timed output"
 
-    # ---- roofline of the forward -------------------------------------------
-    hbm_peak, tc_peak, peak_kind = load_peaks()
-    launches = lib.tt_forward_launch_count(cfg_ref, nb, S)
+    # ---- roofline of the dominant kernel kind -------------------------------
+    hbm_peak, tc_burst, tc_sust, peak_kind = load_peaks()
     plan = _lib.PLAN_NAMES.get(lib.tt_forward_plan(cfg_ref, nb, S), "?")
+    if n_probed != probe_cap:
+        raise SystemExit(f"launch probe saw {n_probed} launches, expected {probe_cap}")
+    per_kind = {}
+    for i in range(n_probed):
+        k = _lib.KERNEL_KINDS.get(launch_kind[i], "?")
+        per_kind.setdefault(k, []).append(launch_ms[i])
+    probed_total = sum(sum(v) for v in per_kind.values())
+    kernels = {k: {"launches": len(v), "total_ms": round(sum(v), 4),
+                   "avg_us": round(sum(v) / len(v) * 1000.0, 2),
+                   "share": round(sum(v) / probed_total, 4)} for k, v in per_kind.items()}
+    dom = max(per_kind, key=lambda k: sum(per_kind[k]))
+    dom_us = sum(per_kind[dom]) / len(per_kind[dom]) * 1000.0
+    lens = m_host.sum(1).double()
+    work = kind_work(dom, cfg, nb, S, lens, mask.numel())
+    if work is None:
+        flops, nbytes = algorithmic_flops(cfg, m_host), algorithmic_bytes(cfg, nb, S, mask.numel())
+    else:
+        flops, nbytes = work
+    long_region = sum(step_ms) > 1000.0
+    tc_peak_bf16 = tc_sust if long_region else tc_burst
+    tc_peak = tc_peak_bf16 / 2.0 / 3.0  # TF32 MMA at half bf16's rate, 3 MMAs per product
+    on_tensor = plan == "ops_tc3xtf32" and dom != "whole_forward" and flops > 0
+    if on_tensor and flops / (tc_peak * 1e12) >= nbytes / (hbm_peak * 1e9):
+        achieved = flops / (dom_us * 1e-6) / 1e12
+        roofline = {
+            "bound": "tensor", "achieved": round(achieved, 2), "peak": round(tc_peak, 1),
+            "unit": "TFLOP/s", "frac": round(achieved / tc_peak, 4),
+            "peak_source": (f"{peak_kind}: bf16 {'sustained' if long_region else 'burst'} "
+                            f"{tc_peak_bf16} TFLOP/s (MEASURED_PEAKS.json) / 2 (TF32 MMA rate) "
+                            "/ 3 (3xTF32: 3 MMAs per fp32 product), of measured"),
+            "algorithmic_flops_per_launch": flops,
+        }
+    else:
+        achieved = nbytes / (dom_us * 1e-6) / 1e9
+        roofline = {
+            "bound": "hbm", "achieved": round(achieved, 2), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 5),
+            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs), of measured",
+            "algorithmic_flops_per_launch": flops,
+            "achieved_fp32_tflops": round(flops / (dom_us * 1e-6) / 1e12, 3),
+        }
+    roofline.update({
+        "traffic": NCU_TRAFFIC.get((w.name, dom)),
+        "kernel": f"{dom} ({len(per_kind[dom])} launches, plan {plan})",
+        "algorithmic_bytes_per_launch": nbytes,
+        "avg_launch_us": round(dom_us, 3),
+        "timing": "CUDA events around each launch on its stream, timed steps",
+    })
     mean_ms = sum(step_ms) / len(step_ms)
-    bytes_step = algorithmic_bytes(cfg, nb, S, mask.numel())
-    flops_step = algorithmic_flops(cfg, m_host)
-    achieved_gbs = bytes_step / (mean_ms * 1e-3) / 1e9
-    roofline = {
-        "bound": "hbm", "achieved": round(achieved_gbs, 2), "peak": hbm_peak,
-        "unit": "GB/s", "frac": round(achieved_gbs / hbm_peak, 5), "traffic": None,
-        "kernel": ("whole forward" if launches == 1 else
-                   f"whole forward ({launches} launches, plan {plan})"),
-        "algorithmic_bytes_per_launch": bytes_step if launches == 1 else None,
-        "algorithmic_bytes_per_step": bytes_step,
-        "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-        "fp32_flops_per_step": flops_step,
-        "achieved_fp32_tflops": round(flops_step / (mean_ms * 1e-3) / 1e12, 4),
-    }
+    f_all = algorithmic_flops(cfg, m_host)
+    roofline["forward_fp32_tflops"] = round(f_all / (mean_ms * 1e-3) / 1e12, 3)
 
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
@@ -394,7 +472,7 @@ def run_ours(args, world, rank, local):
         "config": workload_config(w, nb, world), "plan": plan,
         "gpu_launches": launches * args.steps * world,
         "gpu_launches_note": "our kernels in the timed device steps, summed over ranks",
-        "roofline": roofline,
+        "roofline": roofline, "kernels": kernels,
         "e2e": {"value": e2e_value, "unit": "tokens/s",
                 "h2d_bytes_per_step": x_host.numel() * 4 + m_host.numel(),
                 "d2h_bytes_per_step": x_host.numel() * 4,

@@ -163,6 +163,32 @@ int tt_read_status(const tt_config *cfg, const void *image, int32_t *code,
  * truncated to len). Returns the message length. */
 int tt_last_error(char *buf, size_t len);
 
+/* Kinds of kernel launch that tt_launch_probe_read reports. */
+#define TT_KERNEL_LAYERNORM 1     /* LayerNorm (+ TF32 split) ahead of a GEMM */
+#define TT_KERNEL_QKV 2           /* LN1 (when fused) + q|k|v projection */
+#define TT_KERNEL_ATTENTION 3     /* masked softmax(q k^T) v */
+#define TT_KERNEL_OUT_PROJ 4      /* out_proj + padded-row zeroing + residual */
+#define TT_KERNEL_FFN_IN 5        /* LN2 (when fused) + ffn_in + GELU */
+#define TT_KERNEL_FFN_OUT 6       /* ffn_out + residual + padded-row zeroing */
+#define TT_KERNEL_FINAL_NORM 7    /* final LayerNorm + padded-row zeroing */
+#define TT_KERNEL_WHOLE_FORWARD 8 /* the single-launch forward (TT_PLAN_CLUSTER) */
+
+/* Launch timing probe, a measurement aid with no counterpart in the
+ * reference. tt_launch_probe_start(capacity) creates 2 * capacity timing
+ * events for the calling host thread; from then on every kernel launch that
+ * tt_forward / tt_forward_noalloc make on this thread is bracketed by two
+ * events recorded on the launch's stream, until `capacity` launches have been
+ * recorded (later launches are not bracketed). capacity 0 stops the probe and
+ * destroys its events. Returns TT_OK or TT_ERR_CUDA. */
+int tt_launch_probe_start(int capacity);
+
+/* Waits for the probe's recorded events and writes, for each bracketed launch
+ * i < min(count, capacity), its device time in milliseconds to ms[i] and its
+ * TT_KERNEL_* kind to kinds[i]; then restarts the count at 0 (the events are
+ * kept). Returns the number of launches recorded since the last read, or a
+ * negative status. */
+int tt_launch_probe_read(float *ms, int32_t *kinds, int capacity);
+
 #ifdef __cplusplus
 }
 #endif

@@ -207,3 +207,39 @@ def test_runs_on_current_stream():
         y = model(x, mask)
     s.synchronize()
     check(oracle.forward(params, cfg, x, mask), y, "side stream")
+
+
+@pytest.mark.parametrize("name,plan", [("B1", "cluster"), ("A", "ops_ffma"), ("A", "ops_tc3xtf32")])
+def test_launch_probe_brackets_every_launch(name, plan):
+    """tt_launch_probe_* sees every launch of a forward, in schedule order,
+    each with a positive device time."""
+    import ctypes
+    from ttjam_gottagofast_b200 import _lib
+    cfg = WORKLOADS[name].config
+    model, _ = model_for(cfg)
+    x, mask = generate_random_case(cfg, "cpu", torch.float32, 5, 0.0, 1.0)
+    x, mask = x.to(DEV), mask.to(DEV)
+    lib = model._lib
+    model.set_plan(plan)
+    try:
+        n = lib.tt_forward_launch_count(ctypes.byref(model._cfg), cfg.batch_size, cfg.seq_len)
+        assert lib.tt_launch_probe_start(2 * n) == 0
+        with torch.inference_mode():
+            model(x, mask)
+            model(x, mask)
+        ms = (ctypes.c_float * (2 * n))()
+        kinds = (ctypes.c_int32 * (2 * n))()
+        assert lib.tt_launch_probe_read(ms, kinds, 2 * n) == 2 * n
+        assert lib.tt_launch_probe_read(ms, kinds, 2 * n) == 0  # read restarts the count
+    finally:
+        lib.tt_launch_probe_start(0)
+        model.set_plan("auto")
+    names = [_lib.KERNEL_KINDS[k] for k in kinds]
+    per_layer = {"cluster": [],
+                 "ops_ffma": ["qkv", "attention", "out_proj", "ffn_in", "ffn_out"],
+                 "ops_tc3xtf32": ["layernorm", "qkv", "attention", "out_proj", "layernorm",
+                                  "ffn_in", "ffn_out"]}[plan]
+    one = (["whole_forward"] if plan == "cluster"
+           else per_layer * cfg.num_layers + ["final_norm"])
+    assert names == one * 2
+    assert all(t > 0 for t in ms)

@@ -33,7 +33,12 @@ EXPORTED = (
     "tt_abi_version", "tt_validate_config", "tt_image_bytes", "tt_pack_image",
     "tt_workspace_bytes", "tt_forward", "tt_forward_plan", "tt_forward_launch_count",
     "tt_read_status", "tt_last_error", "tt_forward_noalloc",
+    "tt_launch_probe_start", "tt_launch_probe_read",
 )
+
+# TT_KERNEL_* launch kinds reported by tt_launch_probe_read.
+KERNEL_KINDS = {1: "layernorm", 2: "qkv", 3: "attention", 4: "out_proj", 5: "ffn_in",
+                6: "ffn_out", 7: "final_norm", 8: "whole_forward"}
 
 
 class TTConfig(ctypes.Structure):
@@ -95,6 +100,11 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         lib.tt_read_status.argtypes = [cfgp, vp, ctypes.POINTER(i32), ctypes.POINTER(i32), vp]
         lib.tt_last_error.restype = ctypes.c_int
         lib.tt_last_error.argtypes = [ctypes.c_char_p, sz]
+        lib.tt_launch_probe_start.restype = ctypes.c_int
+        lib.tt_launch_probe_start.argtypes = [ctypes.c_int]
+        lib.tt_launch_probe_read.restype = ctypes.c_int
+        lib.tt_launch_probe_read.argtypes = [ctypes.POINTER(ctypes.c_float),
+                                             ctypes.POINTER(i32), ctypes.c_int]
         if lib.tt_abi_version() != TT_ABI_VERSION:
             raise RuntimeError("libttjam_b200.so ABI version mismatch; rebuild it")
         _lib = lib

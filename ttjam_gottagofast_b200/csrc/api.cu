@@ -2,6 +2,7 @@
 // forward schedule. Declared in include/ttjam_b200.h.
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "attention_tc.cuh"
 #include "cluster_forward.cuh"
@@ -37,6 +38,33 @@ int split_tf32(const float *src, float *hi, float *lo, int64_t n, cudaStream_t s
 }
 
 bool misaligned(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; }
+
+// Launch timing probe (tt_launch_probe_start / _read): per host thread, a
+// pair of timing events around each kernel launch of the forward schedules.
+struct LaunchProbe {
+  std::vector<cudaEvent_t> events;  // 2 per launch: before, after
+  std::vector<int32_t> kinds;
+  int count = 0;
+  int capacity() const { return (int)kinds.size(); }
+};
+thread_local LaunchProbe g_probe;
+
+// Runs `launch` (which enqueues one kernel on `stream`), bracketed by the
+// probe's events while the probe is on and has room.
+template <class F>
+int timed_launch(int kind, cudaStream_t stream, F &&launch) {
+  LaunchProbe &pr = g_probe;
+  const int i = pr.count;
+  const bool on = i < pr.capacity();
+  if (on) TT_CUDA_TRY(cudaEventRecord(pr.events[2 * i], stream));
+  const int rc = launch();
+  if (on && rc == TT_OK) {
+    TT_CUDA_TRY(cudaEventRecord(pr.events[2 * i + 1], stream));
+    pr.kinds[i] = kind;
+    pr.count = i + 1;
+  }
+  return rc;
+}
 
 }  // namespace
 
@@ -102,7 +130,8 @@ int forward_cluster(const tt_config &cfg, const ClusterChoice &cc, const ImageLa
   a.causal = cfg.causal;
   a.scale = (float)(1.0 / std::sqrt((double)(cfg.d_model / cfg.num_heads)));
   a.eps = 1e-5f;
-  return launch_cluster_forward(cc, a, cfg.num_heads, stream);
+  return timed_launch(TT_KERNEL_WHOLE_FORWARD, stream,
+                      [&] { return launch_cluster_forward(cc, a, cfg.num_heads, stream); });
 }
 
 int forward_ops(const tt_config &cfg, const ImageLayout &L, const char *image, const float *x,
@@ -124,36 +153,44 @@ int forward_ops(const tt_config &cfg, const ImageLayout &L, const char *image, c
     g.A = xin; g.lda = D; g.W = P(o.wqkv); g.bias = P(o.bqkv); g.C = qkv; g.ldc = 3LL * D;
     g.ln_gamma = P(o.ln1_w); g.ln_beta = P(o.ln1_b); g.ln_eps = eps;
     g.M = T; g.N = 3 * D; g.K = D; g.epilogue = EPI_BIAS;
-    if ((rc = launch_gemm_ffma(g, stream)) != TT_OK) return rc;
+    if ((rc = timed_launch(TT_KERNEL_QKV, stream, [&] { return launch_gemm_ffma(g, stream); })))
+      return rc;
     // context = softmax(q k^T * scale + masks) v
     AttentionParams a{};
     a.qkv = qkv; a.ctx = ctx; a.mask = mask; a.batch = batch; a.seq = (int)seq;
     a.d_model = D; a.num_heads = H; a.head_dim = hd; a.causal = cfg.causal;
     a.scale = (float)(1.0 / std::sqrt((double)hd));
-    if ((rc = launch_attention_ffma(a, stream)) != TT_OK) return rc;
+    if ((rc = timed_launch(TT_KERNEL_ATTENTION, stream,
+                           [&] { return launch_attention_ffma(a, stream); })))
+      return rc;
     // y = x + masked(context . Wo^T + bo)
     GemmParams go{};
     go.A = ctx; go.lda = D; go.W = P(o.wo); go.bias = P(o.bo); go.R = xin; go.C = y;
     go.ldc = D; go.row_mask = mask; go.M = T; go.N = D; go.K = D;
     go.epilogue = EPI_BIAS_RESIDUAL;
-    if ((rc = launch_gemm_ffma(go, stream)) != TT_OK) return rc;
+    if ((rc = timed_launch(TT_KERNEL_OUT_PROJ, stream, [&] { return launch_gemm_ffma(go, stream); })))
+      return rc;
     // h = gelu(LayerNorm2(y) . W1^T + b1)
     GemmParams g1{};
     g1.A = y; g1.lda = D; g1.W = P(o.w1); g1.bias = P(o.b1); g1.C = hbuf; g1.ldc = F;
     g1.ln_gamma = P(o.ln2_w); g1.ln_beta = P(o.ln2_b); g1.ln_eps = eps;
     g1.M = T; g1.N = F; g1.K = D; g1.epilogue = EPI_BIAS_GELU;
-    if ((rc = launch_gemm_ffma(g1, stream)) != TT_OK) return rc;
+    if ((rc = timed_launch(TT_KERNEL_FFN_IN, stream, [&] { return launch_gemm_ffma(g1, stream); })))
+      return rc;
     // y = masked(y + h . W2^T + b2)
     GemmParams g2{};
     g2.A = hbuf; g2.lda = F; g2.W = P(o.w2); g2.bias = P(o.b2); g2.R = y; g2.C = y;
     g2.ldc = D; g2.row_mask = mask; g2.M = T; g2.N = D; g2.K = F;
     g2.epilogue = EPI_BIAS_RESIDUAL;
-    if ((rc = launch_gemm_ffma(g2, stream)) != TT_OK) return rc;
+    if ((rc = timed_launch(TT_KERNEL_FFN_OUT, stream, [&] { return launch_gemm_ffma(g2, stream); })))
+      return rc;
   }
-  return launch_layernorm(y, y, nullptr, nullptr,
-                          reinterpret_cast<const float *>(image + L.final_w),
-                          reinterpret_cast<const float *>(image + L.final_b), mask, 1, T, D,
-                          eps, stream);
+  return timed_launch(TT_KERNEL_FINAL_NORM, stream, [&] {
+    return launch_layernorm(y, y, nullptr, nullptr,
+                            reinterpret_cast<const float *>(image + L.final_w),
+                            reinterpret_cast<const float *>(image + L.final_b), mask, 1, T, D,
+                            eps, stream);
+  });
 }
 
 // Per-op schedule with 3xTF32 tensor-core GEMMs (d_model >= 512): per layer
@@ -179,8 +216,10 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
     auto P = [&](size_t off) { return reinterpret_cast<const float *>(image + off); };
     const float *xin = (l == 0) ? x : y;
     int rc;
-    if ((rc = launch_layernorm(xin, nullptr, ln_hi, ln_lo, P(o.ln1_w), P(o.ln1_b), nullptr, 0, T,
-                               D, eps, stream)) != TT_OK)
+    if ((rc = timed_launch(TT_KERNEL_LAYERNORM, stream, [&] {
+           return launch_layernorm(xin, nullptr, ln_hi, ln_lo, P(o.ln1_w), P(o.ln1_b), nullptr,
+                                   0, T, D, eps, stream);
+         })))
       return rc;
     TcGemmParams g{};
     g.A_hi = ln_hi; g.A_lo = ln_lo; g.lda = D; g.W_hi = P(o.wqkv_hi); g.W_lo = P(o.wqkv_lo);
@@ -193,7 +232,8 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
     } else {
       g.C = qkv;
     }
-    if ((rc = launch_gemm_tc3(g, stream)) != TT_OK) return rc;
+    if ((rc = timed_launch(TT_KERNEL_QKV, stream, [&] { return launch_gemm_tc3(g, stream); })))
+      return rc;
     const float scale = (float)(1.0 / std::sqrt((double)hd));
     if (W.tc_attention) {
       AttentionTcParams a{};
@@ -201,37 +241,48 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
       a.ctx_hi = ctx_hi; a.ctx_lo = ctx_lo; a.mask = mask; a.status = status;
       a.batch = batch; a.seq = (int)seq; a.seq_pad = W.seq_pad; a.d_model = D; a.num_heads = H;
       a.head_dim = hd; a.causal = cfg.causal; a.scale = scale;
-      if ((rc = launch_attention_tc(a, stream)) != TT_OK) return rc;
+      if ((rc = timed_launch(TT_KERNEL_ATTENTION, stream,
+                             [&] { return launch_attention_tc(a, stream); })))
+        return rc;
     } else {
       AttentionParams a{};
       a.qkv = qkv; a.ctx = nullptr; a.ctx_hi = ctx_hi; a.ctx_lo = ctx_lo; a.mask = mask;
       a.batch = batch; a.seq = (int)seq; a.d_model = D; a.num_heads = H; a.head_dim = hd;
       a.causal = cfg.causal; a.scale = scale;
-      if ((rc = launch_attention_ffma(a, stream)) != TT_OK) return rc;
+      if ((rc = timed_launch(TT_KERNEL_ATTENTION, stream,
+                             [&] { return launch_attention_ffma(a, stream); })))
+        return rc;
     }
     TcGemmParams go{};
     go.A_hi = ctx_hi; go.A_lo = ctx_lo; go.lda = D; go.W_hi = P(o.wo_hi); go.W_lo = P(o.wo_lo);
     go.bias = P(o.bo); go.R = xin; go.C = y; go.ldc = D; go.row_mask = mask; go.status = status;
     go.M = (int)T; go.N = D; go.K = D; go.epilogue = EPI_BIAS_RESIDUAL;
-    if ((rc = launch_gemm_tc3(go, stream)) != TT_OK) return rc;
-    if ((rc = launch_layernorm(y, nullptr, ln_hi, ln_lo, P(o.ln2_w), P(o.ln2_b), nullptr, 0, T, D,
-                               eps, stream)) != TT_OK)
+    if ((rc = timed_launch(TT_KERNEL_OUT_PROJ, stream, [&] { return launch_gemm_tc3(go, stream); })))
+      return rc;
+    if ((rc = timed_launch(TT_KERNEL_LAYERNORM, stream, [&] {
+           return launch_layernorm(y, nullptr, ln_hi, ln_lo, P(o.ln2_w), P(o.ln2_b), nullptr, 0,
+                                   T, D, eps, stream);
+         })))
       return rc;
     TcGemmParams g1{};
     g1.A_hi = ln_hi; g1.A_lo = ln_lo; g1.lda = D; g1.W_hi = P(o.w1_hi); g1.W_lo = P(o.w1_lo);
     g1.bias = P(o.b1); g1.C_hi = h_hi; g1.C_lo = h_lo; g1.ldc = F; g1.status = status;
     g1.M = (int)T; g1.N = F; g1.K = D; g1.epilogue = EPI_BIAS_GELU;
-    if ((rc = launch_gemm_tc3(g1, stream)) != TT_OK) return rc;
+    if ((rc = timed_launch(TT_KERNEL_FFN_IN, stream, [&] { return launch_gemm_tc3(g1, stream); })))
+      return rc;
     TcGemmParams g2{};
     g2.A_hi = h_hi; g2.A_lo = h_lo; g2.lda = F; g2.W_hi = P(o.w2_hi); g2.W_lo = P(o.w2_lo);
     g2.bias = P(o.b2); g2.R = y; g2.C = y; g2.ldc = D; g2.row_mask = mask; g2.status = status;
     g2.M = (int)T; g2.N = D; g2.K = F; g2.epilogue = EPI_BIAS_RESIDUAL;
-    if ((rc = launch_gemm_tc3(g2, stream)) != TT_OK) return rc;
+    if ((rc = timed_launch(TT_KERNEL_FFN_OUT, stream, [&] { return launch_gemm_tc3(g2, stream); })))
+      return rc;
   }
-  return launch_layernorm(y, y, nullptr, nullptr,
-                          reinterpret_cast<const float *>(image + L.final_w),
-                          reinterpret_cast<const float *>(image + L.final_b), mask, 1, T, D,
-                          eps, stream);
+  return timed_launch(TT_KERNEL_FINAL_NORM, stream, [&] {
+    return launch_layernorm(y, y, nullptr, nullptr,
+                            reinterpret_cast<const float *>(image + L.final_w),
+                            reinterpret_cast<const float *>(image + L.final_b), mask, 1, T, D,
+                            eps, stream);
+  });
 }
 
 }  // namespace tt
@@ -371,6 +422,40 @@ int tt_read_status(const tt_config *cfg, const void *image, int32_t *code, int32
   *code = st.code;
   if (detail) *detail = st.detail;
   return TT_OK;
+}
+
+int tt_launch_probe_start(int capacity) {
+  LaunchProbe &pr = g_probe;
+  if (capacity < 0) return fail(TT_ERR_INVALID_ARGUMENT, "tt_launch_probe_start: capacity < 0");
+  for (cudaEvent_t e : pr.events) cudaEventDestroy(e);
+  pr.events.clear();
+  pr.kinds.clear();
+  pr.count = 0;
+  std::vector<cudaEvent_t> ev((size_t)2 * capacity);
+  for (size_t i = 0; i < ev.size(); ++i) {
+    const cudaError_t err = cudaEventCreate(&ev[i]);
+    if (err != cudaSuccess) {
+      for (size_t j = 0; j < i; ++j) cudaEventDestroy(ev[j]);
+      return fail(TT_ERR_CUDA, std::string("cudaEventCreate: ") + cudaGetErrorString(err));
+    }
+  }
+  pr.events = std::move(ev);
+  pr.kinds.assign((size_t)capacity, 0);
+  return TT_OK;
+}
+
+int tt_launch_probe_read(float *ms, int32_t *kinds, int capacity) {
+  LaunchProbe &pr = g_probe;
+  const int n = pr.count;
+  for (int i = 0; i < n && i < capacity; ++i) {
+    TT_CUDA_TRY(cudaEventSynchronize(pr.events[2 * i + 1]));
+    float t = 0.f;
+    TT_CUDA_TRY(cudaEventElapsedTime(&t, pr.events[2 * i], pr.events[2 * i + 1]));
+    if (ms) ms[i] = t;
+    if (kinds) kinds[i] = pr.kinds[i];
+  }
+  pr.count = 0;
+  return n;
 }
 
 int tt_last_error(char *buf, size_t len) {

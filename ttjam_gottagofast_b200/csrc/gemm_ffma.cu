@@ -225,6 +225,117 @@ __global__ void __launch_bounds__(kThreads) gemm_ffma_kernel(GemmParams p) {
   }
 }
 
+// Whole-K variant for K <= 256 (the d_model = 128 projections): the CTA's
+// 64 rows of A and 64 rows of W are copied to shared memory in one batch of
+// 16-byte cp.async (rows past M or N are zero-filled), so a tile costs one
+// memory round trip instead of one per k-tile. LayerNorm statistics come from
+// the shared copy, which is normalised in place. Thread (tx, ty) owns rows
+// ty + 16i and columns tx + 16j (i, j < 4): float4 reads along K hit distinct
+// bank groups and the stores of a warp are coalesced along the columns.
+constexpr int WK_TILE = 64;
+
+__device__ __forceinline__ void cp_async16_zfill(void *dst, const void *src, bool valid) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads) gemm_ffma_wholek_kernel(GemmParams p) {
+  extern __shared__ __align__(16) float wk_smem[];
+  const int K = p.K, N = p.N;
+  const int KS = K + 4;                     // padded row stride: conflict-free float4 rows
+  float *sA = wk_smem;                      // [64][KS]
+  float *sW = wk_smem + WK_TILE * KS;       // [64][KS]
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int64_t m0 = (int64_t)blockIdx.y * WK_TILE;
+  const int n0 = blockIdx.x * WK_TILE;
+  const int k4n = K / 4;
+  for (int idx = tid; idx < 2 * WK_TILE * k4n; idx += kThreads) {
+    const int which = idx / (WK_TILE * k4n);
+    const int rr = (idx / k4n) % WK_TILE, k4 = idx % k4n;
+    if (which == 0) {
+      const bool ok = m0 + rr < p.M;
+      cp_async16_zfill(sA + rr * KS + 4 * k4, p.A + (ok ? (m0 + rr) * p.lda : 0) + 4 * k4, ok);
+    } else {
+      const bool ok = n0 + rr < N;
+      cp_async16_zfill(sW + rr * KS + 4 * k4, p.W + (int64_t)(ok ? n0 + rr : 0) * K + 4 * k4, ok);
+    }
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  if (p.ln_gamma != nullptr) {
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int rr = warp; rr < WK_TILE; rr += kThreads / 32) {
+      float *ar = sA + rr * KS;
+      float sum = 0.f;
+      for (int c = lane; c < K; c += 32) sum += ar[c];
+      const float mean = warp_sum(sum) / (float)K;
+      float ss = 0.f;
+      for (int c = lane; c < K; c += 32) {
+        const float t = ar[c] - mean;
+        ss += t * t;
+      }
+      const float rstd = rsqrtf(warp_sum(ss) / (float)K + p.ln_eps);
+      for (int c = lane; c < K; c += 32) ar[c] = (ar[c] - mean) * rstd * p.ln_gamma[c] + p.ln_beta[c];
+    }
+    __syncthreads();
+  }
+  float acc[4][4] = {};
+#pragma unroll 4
+  for (int k = 0; k < K; k += 4) {
+    float4 a[4], w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a[i] = *reinterpret_cast<const float4 *>(sA + (ty + 16 * i) * KS + k);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) w[j] = *reinterpret_cast<const float4 *>(sW + (tx + 16 * j) * KS + k);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[i][j] = fmaf(a[i].x, w[j].x, acc[i][j]);
+        acc[i][j] = fmaf(a[i].y, w[j].y, acc[i][j]);
+        acc[i][j] = fmaf(a[i].z, w[j].z, acc[i][j]);
+        acc[i][j] = fmaf(a[i].w, w[j].w, acc[i][j]);
+      }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t gr = m0 + ty + 16 * i;
+    if (gr >= p.M) continue;
+    const bool valid = p.row_mask == nullptr || p.row_mask[gr] != 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int gc = n0 + tx + 16 * j;
+      if (gc >= N) continue;
+      float v = acc[i][j] + p.bias[gc];
+      if (p.epilogue == EPI_BIAS_GELU) v = gelu_erf(v);
+      else if (p.epilogue == EPI_BIAS_RESIDUAL) v = valid ? p.R[gr * p.ldc + gc] + v : 0.f;
+      p.C[gr * p.ldc + gc] = v;
+      if (p.C_hi != nullptr) {
+        const float hv = tf32_round(v);
+        p.C_hi[gr * p.ldc + gc] = hv;
+        p.C_lo[gr * p.ldc + gc] = v - hv;
+      }
+    }
+  }
+}
+
+int launch_wholek(const GemmParams &p, cudaStream_t stream) {
+  const size_t smem = (size_t)2 * WK_TILE * (p.K + 4) * sizeof(float);
+  static size_t attr = 0;
+  if (smem > 48 * 1024 && smem > attr) {
+    TT_CUDA_TRY(cudaFuncSetAttribute(gemm_ffma_wholek_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr = smem;
+  }
+  dim3 grid((unsigned)ceil_div(p.N, WK_TILE), (unsigned)ceil_div(p.M, WK_TILE));
+  gemm_ffma_wholek_kernel<<<grid, kThreads, smem, stream>>>(p);
+  TT_LAUNCH_CHECK("gemm_ffma_wholek");
+  return TT_OK;
+}
+
 template <int BM, int BN>
 void launch_tile(const GemmParams &p, bool vec, cudaStream_t stream) {
   dim3 grid((unsigned)ceil_div(p.N, BN), (unsigned)ceil_div(p.M, BM));
@@ -244,6 +355,9 @@ int launch_gemm_ffma(const GemmParams &p, cudaStream_t stream) {
                          reinterpret_cast<uintptr_t>(p.C);
   const bool vec = (p.K % 4 == 0) && (p.lda % 4 == 0) && (p.ldc % 4 == 0) && (p.N % 4 == 0) &&
                    (bits & 15) == 0;
+  // Small K (the d_model = 128 projections): one memory round trip per tile.
+  if (vec && p.K <= 256 && ((reinterpret_cast<uintptr_t>(p.bias) & 3) == 0))
+    return launch_wholek(p, stream);
   // Pick the tile so that the grid covers the 148 SMs at least about once.
   const int64_t tiles128 = ceil_div(p.M, 128) * ceil_div(p.N, 128);
   if (tiles128 >= 148 * 2)
