@@ -12,7 +12,7 @@
 // arrive split by the q|k|v GEMM, p = exp(s - m) is split by the softmax
 // threads. The context accumulates in fp32 in tensor memory.
 //
-// CTA = (query tile of 128 rows, head, sequence); 256 threads:
+// CTA = (query tile of 128 rows, head, sequence); 384 threads:
 //   warp 0    TMA producer: per 64-key tile, K_hi K_lo (64 keys x HD dims) and
 //             Vt_hi Vt_lo (HD dims x 64 keys, from the transposed copy of v the
 //             q|k|v GEMM writes), in 128-byte swizzle boxes, into a 3-stage
