@@ -17,9 +17,12 @@
 //             Vt_hi Vt_lo (HD dims x 64 keys, from the transposed copy of v the
 //             q|k|v GEMM writes), in 128-byte swizzle boxes, into a 3-stage
 //             ring;
-//   warp 1    MMA issuer: S[j] = Q.K_j^T (A = Q from tensor memory, B = K tile)
-//             into a double-buffered S, then O_j = P_j.V_j (A = P from tensor
-//             memory, B = Vt tile); both B operands are K-major;
+//   warp 1    MMA issuer: S_j = Q.K_j^T (A = Q from tensor memory, B = K tile),
+//             then O += P_j.V_j (A = P_j from tensor memory, B = Vt tile); both
+//             B operands are K-major. S is single-buffered (the softmax copies
+//             it to registers at once, so S_{j+1} runs while the softmax of
+//             tile j works); P is double-buffered, so the softmax of tile j+1
+//             writes its P while P_j.V_j is still on the tensor pipe;
 //   warp 2    allocates / frees 512 tensor-memory columns;
 //   warps 4-11 softmax, two warps per tensor-memory lane quarter: query row
 //             q0+t (= tensor-memory lane t) is shared by two threads, one per
@@ -45,7 +48,7 @@ constexpr int kThreads = 384;  // warps 0-3: TMA / MMA / TMEM; warps 4-11: softm
 // Shapes for head_dim HD (32 or 64). Shared-memory stage: K_hi, K_lo
 // (64 keys x HD, HD/32 boxes of 64 rows x 128 B) then Vt_hi, Vt_lo (HD rows x
 // 64 keys, 2 boxes of HD rows x 128 B). Tensor-memory columns (fp32 cells):
-// Q_hi, Q_lo, S[2] (64 each), P_hi, P_lo (64 each), O (HD).
+// Q_hi, Q_lo (HD each), S (64), P_hi[b], P_lo[b] (64 each, b = 0, 1), O (HD).
 template <int HD>
 struct AtShape {
   static constexpr uint32_t KBOX = 64 * 128;           // one 64-row K box
@@ -54,8 +57,11 @@ struct AtShape {
   static constexpr uint32_t OPV = 2 * VBOX;            // one V^T operand (hi or lo)
   static constexpr uint32_t STAGE = 2 * OPK + 2 * OPV;
   static constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE + 1024 + 256;
-  static constexpr uint32_t T_QHI = 0, T_QLO = HD, T_S0 = 2 * HD, T_PHI = 2 * HD + 128,
-                            T_PLO = 2 * HD + 192, T_O = 2 * HD + 256;
+  static constexpr uint32_t T_QHI = 0, T_QLO = HD, T_S = 2 * HD, T_P = 2 * HD + 64,
+                            T_O = 2 * HD + 64 + 256;
+  // P buffer b: hi at T_P + 128 b, lo 64 columns after it
+  static constexpr uint32_t t_phi(int b) { return T_P + 128u * b; }
+  static constexpr uint32_t t_plo(int b) { return T_P + 128u * b + 64u; }
   static constexpr uint32_t TMEM_COLS = 512;
   static_assert(T_O + HD <= TMEM_COLS, "tensor memory");
   // instruction descriptors: D fp32, A/B tf32, both K-major, M = 128
@@ -187,8 +193,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap tm_vlo, const AttentionTcParams p) {
   using Sh = AtShape<HD>;
   constexpr uint32_t STAGE = Sh::STAGE, OPK = Sh::OPK, OPV = Sh::OPV;
-  constexpr uint32_t T_QHI = Sh::T_QHI, T_QLO = Sh::T_QLO, T_S0 = Sh::T_S0, T_PHI = Sh::T_PHI,
-                     T_PLO = Sh::T_PLO, T_O = Sh::T_O, TMEM_COLS = Sh::TMEM_COLS;
+  constexpr uint32_t T_QHI = Sh::T_QHI, T_QLO = Sh::T_QLO, T_S = Sh::T_S, T_O = Sh::T_O,
+                     TMEM_COLS = Sh::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   __shared__ int s_kv_len;
   __shared__ float s_rowmax[2][2][128];  // [tile parity][key half][row]
@@ -198,10 +204,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t bars = base + STAGES * STAGE;
   auto kv_full = [&](int s) { return bars + 8u * s; };
   auto kv_empty = [&](int s) { return bars + 8u * (STAGES + s); };
-  auto s_full = [&](int b) { return bars + 8u * (2 * STAGES + b); };
-  auto s_free = [&](int b) { return bars + 8u * (2 * STAGES + 2 + b); };
-  const uint32_t p_full = bars + 8u * (2 * STAGES + 4);
-  const uint32_t o_full = bars + 8u * (2 * STAGES + 5);
+  const uint32_t s_full = bars + 8u * (2 * STAGES);
+  const uint32_t s_free = bars + 8u * (2 * STAGES + 1);
+  auto p_full = [&](int b) { return bars + 8u * (2 * STAGES + 2 + b); };  // P buffer b written
+  auto o_done = [&](int b) { return bars + 8u * (2 * STAGES + 4 + b); };  // its P.V finished
   const uint32_t q_ready = bars + 8u * (2 * STAGES + 6);
   const uint32_t tmem_slot = bars + 8u * (2 * STAGES + 7);
   uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
@@ -235,12 +241,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(kv_empty(s), 1);
     }
     // the 8 softmax warps arrive once per warp (an elected lane after __syncwarp)
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 8);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(s_full(i), 1);
-      mbar_init(s_free(i), 8);
+      mbar_init(p_full(i), 8);
+      mbar_init(o_done(i), 1);
     }
-    mbar_init(p_full, 8);
-    mbar_init(o_full, 1);
     mbar_init(q_ready, 8);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -278,12 +284,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer --------------------------------------------------------
     auto issue_s = [&](int j) {
-      const int s = j % STAGES, sb = j & 1;
+      const int s = j % STAGES;
       mbar_wait(kv_full(s), (j / STAGES) & 1, p.status, 0x4200 + j);
-      if (j >= 2) mbar_wait(s_free(sb), ((j >> 1) - 1) & 1, p.status, 0x4300 + j);
+      // S is free once the softmax has copied S_{j-1} to registers
+      if (j >= 1) mbar_wait(s_free, (j - 1) & 1, p.status, 0x4300 + j);
       fence_after();
       const uint32_t kst = base + s * STAGE;
-      const uint32_t sd = tm + T_S0 + 64u * sb;
+      const uint32_t sd = tm + T_S;
       // descriptors built once; a k-step only advances the start-address field
       const uint64_t khi0 = sdesc(kst, 16, 1024), klo0 = sdesc(kst + OPK, 16, 1024);
 #pragma unroll
@@ -293,25 +300,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_ts(sd, tm + T_QHI + 8u * kk, klo0 + koff, Sh::IDESC_S, 1);
         mma_ts(sd, tm + T_QLO + 8u * kk, khi0 + koff, Sh::IDESC_S, 1);
       }
-      mma_commit(s_full(sb));
+      mma_commit(s_full);
     };
     mbar_wait(q_ready, 0, p.status, 0x4000);
     issue_s(0);
     for (int j = 0; j < nkv; ++j) {
       if (j + 1 < nkv) issue_s(j + 1);  // next scores overlap this tile's softmax
-      const int s = j % STAGES;
-      mbar_wait(p_full, j & 1, p.status, 0x4400 + j);
+      const int s = j % STAGES, pb = j & 1;
+      mbar_wait(p_full(pb), (j >> 1) & 1, p.status, 0x4400 + j);
       fence_after();
       const uint32_t vst = base + s * STAGE + 2 * OPK;
       const uint64_t vhi0 = sdesc(vst, 16, 1024), vlo0 = sdesc(vst + OPV, 16, 1024);
 #pragma unroll
       for (int kk = 0; kk < BKV / 8; ++kk) {  // 8 keys per MMA
         const uint64_t voff = ((kk >> 2) * Sh::VBOX + (kk & 3) * 32u) >> 4;
-        mma_ts(tm + T_O, tm + T_PHI + 8u * kk, vhi0 + voff, Sh::IDESC_PV, (j | kk) != 0);
-        mma_ts(tm + T_O, tm + T_PHI + 8u * kk, vlo0 + voff, Sh::IDESC_PV, 1);
-        mma_ts(tm + T_O, tm + T_PLO + 8u * kk, vhi0 + voff, Sh::IDESC_PV, 1);
+        mma_ts(tm + T_O, tm + Sh::t_phi(pb) + 8u * kk, vhi0 + voff, Sh::IDESC_PV, (j | kk) != 0);
+        mma_ts(tm + T_O, tm + Sh::t_phi(pb) + 8u * kk, vlo0 + voff, Sh::IDESC_PV, 1);
+        mma_ts(tm + T_O, tm + Sh::t_plo(pb) + 8u * kk, vhi0 + voff, Sh::IDESC_PV, 1);
       }
-      mma_commit(o_full);
+      mma_commit(o_done(pb));
       mma_commit(kv_empty(s));
     }
   } else if (warp >= 4) {
@@ -356,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr float kLazy = 8.0f;
     float m_ref = -CUDART_INF_F, l = 0.f;
     for (int j = 0; j < nkv; ++j) {
-      const int sb = j & 1;
+      const int pb = j & 1;
       const int k0 = j * BKV + 32 * kh;     // first key of this thread's half
       uint32_t ok;
       {
@@ -364,32 +371,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = __ballot_sync(0xffffffffu, ka < kv_end && (mrow == nullptr || mrow[ka] != 0));
       }
       const bool diag = p.causal && k0 + 31 > q0;  // half reaches past the first query
-      mbar_wait(s_full(sb), (j >> 1) & 1, p.status, 0x4500 + j);
+      mbar_wait(s_full, j & 1, p.status, 0x4500 + j);
       fence_after();
       float sv[32];
-      tmem_ld16(lane_base + T_S0 + 64u * sb + col_off, sv);
-      tmem_ld16(lane_base + T_S0 + 64u * sb + col_off + 16, sv + 16);
+      tmem_ld16(lane_base + T_S + col_off, sv);
+      tmem_ld16(lane_base + T_S + col_off + 16, sv + 16);
       tmem_wait_ld();
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(s_free(sb));
+      if (lane == 0) mbar_arrive(s_free);
+      // allowed keys of this half as one word: valid (ballot) and, on the
+      // diagonal, key k0 + c <= row, i.e. bits 0 .. row - k0 (one select per
+      // score below; a per-score && / || compiles to branches)
+      uint32_t allowed = ok;
+      if (diag) {
+        const int lim = row - k0;
+        allowed &= lim >= 31 ? 0xffffffffu : (lim < 0 ? 0u : (2u << lim) - 1u);
+      }
       float mx4[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
-        const bool okc = ((ok >> c) & 1u) != 0 && (!diag || k0 + c <= row);
-        sv[c] = okc ? sv[c] * sl : -CUDART_INF_F;
+        sv[c] = (allowed >> c) & 1u ? sv[c] * sl : -CUDART_INF_F;
         mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
       }
       float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-      s_rowmax[sb][kh][t] = mx;
+      s_rowmax[pb][kh][t] = mx;
       asm volatile("bar.sync 1, 256;" ::: "memory");  // the 8 softmax warps
-      mx = fmaxf(mx, s_rowmax[sb][kh ^ 1][t]);
-      // the previous tile's P.V has to finish before P (and, on a rescale, O)
-      // is touched
-      if (j > 0) mbar_wait(o_full, (j - 1) & 1, p.status, 0x4600 + j);
+      mx = fmaxf(mx, s_rowmax[pb][kh ^ 1][t]);
       if (mx > m_ref + kLazy || (m_ref == -CUDART_INF_F && mx != -CUDART_INF_F)) {
         const float alpha = fast_exp2(m_ref - mx);  // 0 when m_ref is -inf
         if (j > 0 && m_ref != -CUDART_INF_F) {
+          // the context in tensor memory must hold P_{j-1}.V_{j-1} before it
+          // is rescaled
+          mbar_wait(o_done((j - 1) & 1), ((j - 1) >> 1) & 1, p.status, 0x4600 + j);
           fence_after();
 #pragma unroll
           for (int c = 0; c < HD / 2; c += 16) {
@@ -416,6 +430,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 32; ++c) sv[c] = 0.f;
       }
       l += (ps4[0] + ps4[1]) + (ps4[2] + ps4[3]);
+      // P buffer pb last held P_{j-2}: its P.V must be done before it is
+      // overwritten
+      if (j >= 2) {
+        mbar_wait(o_done(pb), ((j - 2) >> 1) & 1, p.status, 0x4800 + j);
+        fence_after();
+      }
       // this half of P (TF32 split) -> tensor memory
 #pragma unroll
       for (int c = 0; c < 32; c += 16) {
@@ -425,20 +445,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           hi[i] = tf32_round(sv[c + i]);
           lo[i] = sv[c + i] - hi[i];
         }
-        tmem_st16(lane_base + T_PHI + col_off + c, hi);
-        tmem_st16(lane_base + T_PLO + col_off + c, lo);
+        tmem_st16(lane_base + Sh::t_phi(pb) + col_off + c, hi);
+        tmem_st16(lane_base + Sh::t_plo(pb) + col_off + c, lo);
       }
       tmem_wait_st();
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(p_full(pb));
     }
     // row sum = both halves' partial sums
     s_rowsum[kh][t] = l;
     asm volatile("bar.sync 1, 256;" ::: "memory");
     l += s_rowsum[kh ^ 1][t];
     // context = O / l (this thread's HD/2 dims), written as a TF32 split
-    mbar_wait(o_full, (nkv - 1) & 1, p.status, 0x4700);
+    // the last P.V (the tensor pipe runs the MMAs in order, so all of them)
+    mbar_wait(o_done((nkv - 1) & 1), ((nkv - 1) >> 1) & 1, p.status, 0x4700);
     fence_after();
     const float inv = l > 0.f ? 1.f / l : 0.f;
     const int64_t off = (b * S + (row_in ? row : 0)) * (int64_t)D + (int64_t)h * HD + dim_off;
