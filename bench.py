@@ -63,6 +63,9 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=10.0)
+    ap.add_argument("--batch", type=int, default=0,
+                    help="run the workload's shape with this batch instead (a smaller "
+                         "case of the same shape, e.g. for a profiler capture)")
     return ap.parse_args()
 
 
@@ -98,6 +101,17 @@ def max_over_ranks(v, world):
     t = torch.tensor([v], dtype=torch.float64, device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def select_workload(args):
+    """The named workload, with its batch replaced when --batch is given."""
+    import dataclasses
+    w = WORKLOADS[args.workload]
+    if args.batch > 0:
+        w = dataclasses.replace(
+            w, config=dataclasses.replace(w.config, batch_size=args.batch),
+            description=f"{w.description} [batch set to {args.batch}]")
+    return w
 
 
 def per_rank_batch(w, world, rank):
@@ -265,7 +279,7 @@ def cpu_reference_run(w, steps, warmup, budget_s):
 def run_reference_arm(args, world, rank):
     if rank != 0:
         return 0
-    w = WORKLOADS[args.workload]
+    w = select_workload(args)
     res = cpu_reference_run(w, args.steps, args.warmup, budget_s=120.0)
     cfg = w.config
     line = {
@@ -302,7 +316,7 @@ def run_ours(args, world, rank, local):
         raise SystemExit("bench.py needs a CUDA device for --impl ours")
     from ttjam_gottagofast_b200 import UserOptimizedTransformer
     dev = torch.device("cuda", local if world > 1 else 0)
-    w = WORKLOADS[args.workload]
+    w = select_workload(args)
     cfg = w.config
     b0, nb, scaling = per_rank_batch(w, world, rank)
     x_all, m_all = generate_random_case(cfg, "cpu", torch.float32, TIMING_DATA_SEED,

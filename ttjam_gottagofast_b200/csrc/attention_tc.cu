@@ -220,13 +220,42 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int q0 = qt * BQ;
   const uint8_t *mrow = p.mask ? p.mask + b * S : nullptr;
 
+  // The softmax threads' Q row (TF32 split, HD/2 dims each) and the mask
+  // bytes are requested together, so the prologue pays one memory latency.
+  float qv[HD];
+  if (warp >= 4) {
+    const int t = (warp & 3) * 32 + lane, kh = (warp - 4) >> 2;
+    const int row = q0 + t;
+    const int64_t qoff = (b * S + (row < S ? row : 0)) * (int64_t)(3 * D) + (int64_t)h * HD +
+                         (HD / 2) * kh;
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+      const float4 *src = reinterpret_cast<const float4 *>((which ? p.qkv_lo : p.qkv_hi) + qoff);
+#pragma unroll
+      for (int i = 0; i < HD / 8; ++i) {
+        const float4 x = row < S ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        float *d = qv + which * (HD / 2) + 4 * i;
+        d[0] = x.x; d[1] = x.y; d[2] = x.z; d[3] = x.w;
+      }
+    }
+  }
   // kv_len = 1 + last valid key; keys at or after it are all padding
   if (threadIdx.x == 0) s_kv_len = mrow ? 0 : S;
   __syncthreads();
   if (mrow) {
     int last = 0;
-    for (int j = threadIdx.x; j < S; j += kThreads)
-      if (mrow[j]) last = j + 1;
+    if ((reinterpret_cast<uintptr_t>(mrow) & 15) == 0 && S % 16 == 0) {
+      for (int j = threadIdx.x; j < S / 16; j += kThreads) {
+        const uint4 v = reinterpret_cast<const uint4 *>(mrow)[j];
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (w[k]) last = 16 * j + 4 * k + (31 - __clz((int)w[k])) / 8 + 1;
+      }
+    } else {
+      for (int j = threadIdx.x; j < S; j += kThreads)
+        if (mrow[j]) last = j + 1;
+    }
     if (last) atomicMax(&s_kv_len, last);
   }
   __syncthreads();
@@ -331,23 +360,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t col_off = 32u * kh;             // this thread's 32 keys of a tile
     const uint32_t dim_off = (uint32_t)(HD / 2) * kh;  // ... and HD/2 dims of Q and O
     {
-      // Q row -> tensor memory: this thread loads dims [dim_off, dim_off + HD/2)
-      const int64_t qoff = (b * S + (row_in ? row : 0)) * (int64_t)(3 * D) + (int64_t)h * HD + dim_off;
-      float v[16];
+      // Q row -> tensor memory: this thread's dims [dim_off, dim_off + HD/2)
 #pragma unroll
-      for (int which = 0; which < 2; ++which) {
-        const float *src = (which ? p.qkv_lo : p.qkv_hi) + qoff;
+      for (int which = 0; which < 2; ++which)
 #pragma unroll
-        for (int c = 0; c < HD / 2; c += 16) {
-#pragma unroll
-          for (int i = 0; i < 16; i += 4) {
-            const float4 x = row_in ? *reinterpret_cast<const float4 *>(src + c + i)
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-            v[i] = x.x; v[i + 1] = x.y; v[i + 2] = x.z; v[i + 3] = x.w;
-          }
-          tmem_st16(lane_base + (which ? T_QLO : T_QHI) + dim_off + c, v);
-        }
-      }
+        for (int c = 0; c < HD / 2; c += 16)
+          tmem_st16(lane_base + (which ? T_QLO : T_QHI) + dim_off + c, qv + which * (HD / 2) + c);
       tmem_wait_st();
       fence_before();
       __syncwarp();

@@ -27,9 +27,14 @@
 //   warp 2    allocates / frees the 2 x BN tensor-memory columns;
 //   warps 4-11 epilogue: warp w reads tensor-memory lane quarter w%4 (tile row
 //             = lane) and column half (w-4)/4 with tcgen05.ld 32x32b, applies
-//             bias, GELU / residual / padded-row zeroing, stores fp32 and/or
-//             the TF32 split, then releases the accumulator -- so the
-//             epilogue of one tile overlaps the main loop of the next.
+//             bias, GELU / residual / padded-row zeroing, then releases the
+//             accumulator -- so the epilogue of one tile overlaps the main
+//             loop of the next. Outputs leave through shared memory: each warp
+//             writes its 32-row x 16-column chunk (fp32, or the TF32 split) to
+//             a staging buffer in the 64-byte swizzle pattern (conflict-free)
+//             and one lane issues a TMA tensor store, which writes whole lines
+//             (a lane-per-row st.global would be 32 partial-line writes per
+//             instruction).
 // With TF32 operands an M128 x N128 MMA reads 8 KB of shared memory per 64
 // cycles, the whole shared-memory bandwidth; N = 256 halves that per FLOP.
 // Every mbarrier wait is bounded; a wait that gives up latches
@@ -47,13 +52,18 @@ constexpr int kThreads = 384;
 constexpr int kEpiWarps = 8;
 constexpr uint32_t TILE_A = BM * BK * 4;               // 8 KB
 
+constexpr uint32_t STG_WARP = 2 * 2048;               // per epilogue warp: two 32x16 fp32 chunks
+
 template <int BN>
 struct TcShape {
   static constexpr uint32_t TILE_W = BN * BK * 4;                       // 16 KB at BN 256
   static constexpr uint32_t STAGE_BYTES = 2 * TILE_A + 2 * TILE_W;      // 48 KB at BN 256
   static constexpr uint32_t TMEM_COLS = 2 * BN;                         // two accumulators
-  static constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr uint32_t STG_OFF = STAGES * STAGE_BYTES;             // output staging
+  static constexpr uint32_t BAR_OFF = STG_OFF + kEpiWarps * STG_WARP;   // mbarriers
+  static constexpr size_t SMEM_BYTES = (size_t)BAR_OFF + 256 + 1024;   // + alignment slack
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+  static_assert(STG_OFF % 1024 == 0, "staging buffers on the swizzle period");
 };
 
 // ---- PTX helpers ------------------------------------------------------------
@@ -102,6 +112,26 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *tm,
       "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(c0), "r"(c1)
       : "memory");
 }
+// TMA tensor store of a staged shared-memory box, and the bulk-group waits.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *tm, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tm)),
+               "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // UMMA shared-memory descriptor, K-major, 64-byte swizzle: rows of 64 bytes
 // (16 fp32), 8-row groups 512 bytes apart (SBO), LBO unused (1), version 1.
 __device__ __forceinline__ uint64_t umma_desc_sw64(uint32_t saddr) {
@@ -156,61 +186,61 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Epilogue of one 16-column chunk of one row: bias, activation / residual,
-// stores. v holds the accumulator values of columns col0..col0+15.
-__device__ __forceinline__ void epilogue_chunk(const TcGemmParams &p, int row, bool valid,
-                                               int col0, float (&v)[16]) {
+// Epilogue values of one 16-column chunk of one row: bias, then GELU or the
+// residual with padded-row zeroing. v holds the accumulator values of
+// columns col0..col0+15 (col0 < N, a multiple of 16).
+__device__ __forceinline__ void epilogue_values(const TcGemmParams &p, int row, bool row_in,
+                                                bool valid, int col0, float (&v)[16]) {
   const bool full = col0 + 16 <= p.N;
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const int col = col0 + j;
-    float x = (full || col < p.N) ? v[j] + p.bias[col] : 0.f;
-    if (p.epilogue == EPI_BIAS_GELU) x = gelu_erf(x);
-    v[j] = x;
+  for (int j = 0; j < 16; j += 4) {
+    float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (full || col0 + j < p.N) b4 = *reinterpret_cast<const float4 *>(p.bias + col0 + j);
+    v[j] += b4.x; v[j + 1] += b4.y; v[j + 2] += b4.z; v[j + 3] += b4.w;
   }
-  if (p.vt_hi != nullptr && col0 >= p.vt_col0) {
-    // value columns: TF32 split, transposed per (sequence, head) so keys are
-    // contiguous; lanes are consecutive rows, so each store is coalesced
-    const int vc = col0 - p.vt_col0;
-    const int hh = vc / p.head_dim, d0 = vc % p.head_dim;
-    const int bb = row / p.seq, ss = row % p.seq;
-    const int64_t base_t = ((int64_t)(bb * p.heads + hh) * p.head_dim + d0) * p.seq_pad + ss;
+  if (p.epilogue == EPI_BIAS_GELU) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      if (!full && col0 + j >= p.N) break;
-      const float hv = tf32_round(v[j]);
-      p.vt_hi[base_t + (int64_t)j * p.seq_pad] = hv;
-      p.vt_lo[base_t + (int64_t)j * p.seq_pad] = v[j] - hv;
-    }
-    return;
-  }
-  const int64_t off = (int64_t)row * p.ldc + col0;
-  if (p.epilogue == EPI_BIAS_RESIDUAL) {
+    for (int j = 0; j < 16; ++j) v[j] = gelu_erf(v[j]);
+  } else if (p.epilogue == EPI_BIAS_RESIDUAL) {
+    const int64_t off = (int64_t)row * p.ldc + col0;
 #pragma unroll
     for (int j = 0; j < 16; j += 4) {
-      if (!full && col0 + j >= p.N) break;
-      const float4 r4 = *reinterpret_cast<const float4 *>(p.R + off + j);
+      float4 r4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (row_in && (full || col0 + j < p.N)) r4 = *reinterpret_cast<const float4 *>(p.R + off + j);
       v[j + 0] = valid ? r4.x + v[j + 0] : 0.f;
       v[j + 1] = valid ? r4.y + v[j + 1] : 0.f;
       v[j + 2] = valid ? r4.z + v[j + 2] : 0.f;
       v[j + 3] = valid ? r4.w + v[j + 3] : 0.f;
     }
   }
+}
+
+// Value columns of a q|k|v projection: TF32 split, transposed per (sequence,
+// head) so keys are contiguous; lanes are consecutive rows, so each store is
+// coalesced.
+__device__ __forceinline__ void store_vt(const TcGemmParams &p, int row, int col0,
+                                         const float (&v)[16]) {
+  const bool full = col0 + 16 <= p.N;
+  const int vc = col0 - p.vt_col0;
+  const int hh = vc / p.head_dim, d0 = vc % p.head_dim;
+  const int bb = row / p.seq, ss = row % p.seq;
+  const int64_t base_t = ((int64_t)(bb * p.heads + hh) * p.head_dim + d0) * p.seq_pad + ss;
 #pragma unroll
-  for (int j = 0; j < 16; j += 4) {
+  for (int j = 0; j < 16; ++j) {
     if (!full && col0 + j >= p.N) break;
-    const float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-    if (p.C != nullptr) *reinterpret_cast<float4 *>(p.C + off + j) = o;
-    if (p.C_hi != nullptr) {
-      float4 h, l;
-      h.x = tf32_round(o.x); l.x = o.x - h.x;
-      h.y = tf32_round(o.y); l.y = o.y - h.y;
-      h.z = tf32_round(o.z); l.z = o.z - h.z;
-      h.w = tf32_round(o.w); l.w = o.w - h.w;
-      *reinterpret_cast<float4 *>(p.C_hi + off + j) = h;
-      *reinterpret_cast<float4 *>(p.C_lo + off + j) = l;
-    }
+    const float hv = tf32_round(v[j]);
+    p.vt_hi[base_t + (int64_t)j * p.seq_pad] = hv;
+    p.vt_lo[base_t + (int64_t)j * p.seq_pad] = v[j] - hv;
   }
+}
+
+// Writes row `lane` of a 32 x 16 fp32 chunk into a staging buffer laid out as
+// the 64-byte-swizzled box a TMA tensor store reads: 16-byte unit u of row r
+// sits at unit u ^ ((r >> 1) & 3).
+__device__ __forceinline__ void stage_row(uint8_t *buf, int lane, const float4 (&q)[4]) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+    *reinterpret_cast<float4 *>(buf + lane * 64 + ((u ^ ((lane >> 1) & 3)) << 4)) = q[u];
 }
 
 template <int BN>
@@ -218,14 +248,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                     const __grid_constant__ CUtensorMap tm_a_lo,
                     const __grid_constant__ CUtensorMap tm_w_hi,
-                    const __grid_constant__ CUtensorMap tm_w_lo, const TcGemmParams p) {
+                    const __grid_constant__ CUtensorMap tm_w_lo,
+                    const __grid_constant__ CUtensorMap tm_c,
+                    const __grid_constant__ CUtensorMap tm_c_hi,
+                    const __grid_constant__ CUtensorMap tm_c_lo, const TcGemmParams p) {
   using Sh = TcShape<BN>;
   constexpr uint32_t TILE_W = Sh::TILE_W, STAGE_BYTES = Sh::STAGE_BYTES;
   constexpr uint32_t IDESC = idesc_tf32<BN>();
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
-  const uint32_t bars = base + STAGES * STAGE_BYTES;
+  const uint32_t bars = base + Sh::BAR_OFF;
   // full[S] | empty[S] | acc_full[2] | acc_empty[2] | tmem address
   auto full_bar = [&](int s) { return bars + 8u * s; };
   auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
@@ -307,28 +340,71 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(acc_full(ab));    // accumulator ab complete
     }
   } else if (warp >= 4) {
-    // ---- epilogue: tensor memory -> registers -> global ---------------------
+    // ---- epilogue: tensor memory -> registers -> shared -> TMA store -------
     const int q = warp & 3;                 // tensor-memory lane quarter
     const int chalf = (warp - 4) >> 2;      // column half of the tile
+    const uint32_t stg = base + Sh::STG_OFF + (uint32_t)(warp - 4) * STG_WARP;
+    uint8_t *stg_ptr = smem_raw + (stg - raw);
+    const bool split_out = p.C_hi != nullptr;
     int local = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
       const int ab = local & 1;
       const int m0 = (tile / NT) * BM, n0 = (tile % NT) * BN;
       mbar_wait(acc_full(ab), (local >> 1) & 1, p.status, 0x3000);
       tc_fence_after();
-      const int row = m0 + q * 32 + lane;
+      const int row0 = m0 + q * 32;
+      const int row = row0 + lane;
       const bool row_in = row < p.M;
       const bool valid = row_in && (p.row_mask == nullptr || p.row_mask[row] != 0);
 #pragma unroll 1
       for (int c0 = chalf * (BN / 2); c0 < (chalf + 1) * (BN / 2); c0 += 16) {
         float v[16];
         tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN + c0), v);
-        if (row_in && n0 + c0 < p.N) epilogue_chunk(p, row, valid, n0 + c0, v);
+        const int col0 = n0 + c0;
+        if (col0 >= p.N || row0 >= p.M) continue;  // warp-uniform
+        epilogue_values(p, row, row_in, valid, col0, v);
+        if (p.vt_hi != nullptr && col0 >= p.vt_col0) {
+          if (row_in) store_vt(p, row, col0, v);
+          continue;
+        }
+        // the previous store of this warp must have read the staging buffers
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
+        if (split_out) {
+          float4 hq[4], lq[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float4 o = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+            hq[u] = make_float4(tf32_round(o.x), tf32_round(o.y), tf32_round(o.z), tf32_round(o.w));
+            lq[u] = make_float4(o.x - hq[u].x, o.y - hq[u].y, o.z - hq[u].z, o.w - hq[u].w);
+          }
+          stage_row(stg_ptr, lane, hq);
+          stage_row(stg_ptr + 2048, lane, lq);
+        } else {
+          float4 oq[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            oq[u] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+          stage_row(stg_ptr, lane, oq);
+        }
+        fence_proxy_async_smem();  // the generic-proxy writes, visible to the TMA
+        __syncwarp();
+        if (lane == 0) {
+          // rows past M and columns past N are clipped by the store
+          if (split_out) {
+            tma_store_2d(&tm_c_hi, stg, col0, row0);
+            tma_store_2d(&tm_c_lo, stg + 2048, col0, row0);
+          } else {
+            tma_store_2d(&tm_c, stg, col0, row0);
+          }
+          bulk_commit();
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty(ab));
     }
+    if (lane == 0) bulk_wait_all();  // stores complete before the CTA retires
   }
   tc_fence_before();
   __syncthreads();
@@ -394,6 +470,12 @@ int launch_bn(const TcGemmParams &p, cudaStream_t stream) {
       (rc = make_tmap(&tw_hi, p.W_hi, p.N, p.K, p.K, BN)) ||
       (rc = make_tmap(&tw_lo, p.W_lo, p.N, p.K, p.K, BN)))
     return rc;
+  // output maps (32-row x 16-column store boxes); an unused one repeats ta_hi
+  CUtensorMap tc = ta_hi, tc_hi = ta_hi, tc_lo = ta_hi;
+  if (p.C != nullptr && (rc = make_tmap(&tc, p.C, p.M, p.N, p.ldc, 32))) return rc;
+  if (p.C_hi != nullptr && ((rc = make_tmap(&tc_hi, p.C_hi, p.M, p.N, p.ldc, 32)) ||
+                            (rc = make_tmap(&tc_lo, p.C_lo, p.M, p.N, p.ldc, 32))))
+    return rc;
   static int sms = 0;
   static bool attr_set = false;
   if (!attr_set) {
@@ -406,7 +488,8 @@ int launch_bn(const TcGemmParams &p, cudaStream_t stream) {
   }
   const int64_t tiles = (int64_t)((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = (int)std::min<int64_t>(tiles, sms > 0 ? sms : 148);
-  gemm_tc3_kernel<BN><<<grid, kThreads, Sh::SMEM_BYTES, stream>>>(ta_hi, ta_lo, tw_hi, tw_lo, p);
+  gemm_tc3_kernel<BN><<<grid, kThreads, Sh::SMEM_BYTES, stream>>>(ta_hi, ta_lo, tw_hi, tw_lo, tc,
+                                                                  tc_hi, tc_lo, p);
   TT_LAUNCH_CHECK("gemm_tc3");
   return TT_OK;
 }
@@ -417,6 +500,8 @@ int launch_gemm_tc3(const TcGemmParams &p, cudaStream_t stream) {
   if (p.M <= 0 || p.N <= 0) return TT_OK;
   if (p.K <= 0 || p.K % 4 != 0 || p.N % 4 != 0 || p.ldc % 4 != 0)
     return fail(TT_ERR_UNSUPPORTED, "gemm_tc: K, N and ldc must be multiples of 4");
+  if ((p.C != nullptr) == (p.C_hi != nullptr) || (p.C_hi != nullptr) != (p.C_lo != nullptr))
+    return fail(TT_ERR_UNSUPPORTED, "gemm_tc: exactly one of C and the C_hi/C_lo split");
   if (p.vt_hi != nullptr && (p.vt_col0 % 16 != 0 || p.head_dim % 16 != 0))
     return fail(TT_ERR_UNSUPPORTED, "gemm_tc: transposed value columns need 16-aligned heads");
   // N = 256 tiles halve the shared-memory operand traffic per FLOP; narrow
