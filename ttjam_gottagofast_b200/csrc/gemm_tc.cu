@@ -416,6 +416,259 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+
+// ---- CTA-pair variant (tcgen05 cta_group::2) ----------------------------------
+// A cluster of two CTAs computes a 256 x 256 output tile: CTA r of the pair owns
+// rows m0 + 128 r (its A rows) and W rows n0 + 128 r (its half of the B
+// operand), both loaded by its own TMA into its own shared memory. One thread of
+// CTA 0 issues M256 x N256 x K8 MMAs that read both CTAs' operands and leave
+// each CTA's 128 rows in that CTA's tensor memory. A stage is 32 KB per CTA
+// (A_hi, A_lo, W half hi, lo) against 48 KB for the same MMA work in the
+// single-CTA kernel -- a third less L2 -> SM traffic, the limit measured there --
+// and six stages fit. Barriers: a stage's loads in both CTAs complete their
+// bytes on CTA 0's full barrier (TMA .cta_group::2); CTA 0's MMA thread commits
+// each stage to the empty barrier of both CTAs and each accumulator to the
+// acc_full barrier of both (one commit per CTA); both CTAs' epilogue warps
+// release an accumulator on CTA 0's acc_empty barrier. No load uses cluster
+// multicast.
+constexpr int PSTAGES = 6;
+constexpr int PBN = 256;                                    // pair tile N (128 per CTA in smem)
+constexpr uint32_t P_TILE = 128 * BK * 4;                   // 8 KB: A rows or W half rows
+constexpr uint32_t P_STAGE = 4 * P_TILE;                    // A_hi, A_lo, W_hi half, W_lo half
+constexpr uint32_t P_STG_OFF = PSTAGES * P_STAGE;
+constexpr uint32_t P_BAR_OFF = P_STG_OFF + kEpiWarps * STG_WARP;
+constexpr size_t P_SMEM = (size_t)P_BAR_OFF + 256 + 1024;
+constexpr uint32_t P_TMEM_COLS = 2 * PBN;                   // two 256-column accumulators
+constexpr uint32_t P_IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(PBN >> 3) << 17) |
+                             ((uint32_t)(256 >> 4) << 24);  // D fp32, A/B tf32 K-major, M 256
+static_assert(P_SMEM <= 227 * 1024, "shared memory");
+static_assert(P_STG_OFF % 1024 == 0, "staging buffers on the swizzle period");
+
+__device__ __forceinline__ uint32_t cta_rank_in_cluster() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t map_to_cta(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// TMA load into this CTA's shared memory whose bytes complete on an mbarrier
+// of either CTA of the pair (cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *tm, int c0, int c1,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void umma_tf32_pair(uint32_t tmem_d, uint64_t a, uint64_t b,
+                                               uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
+// Arrive on an mbarrier (cluster address, either CTA) once the MMAs issued so
+// far have completed.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar_cluster)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc3_pair_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
+                         const __grid_constant__ CUtensorMap tm_a_lo,
+                         const __grid_constant__ CUtensorMap tm_w_hi,
+                         const __grid_constant__ CUtensorMap tm_w_lo,
+                         const __grid_constant__ CUtensorMap tm_c,
+                         const __grid_constant__ CUtensorMap tm_c_hi,
+                         const __grid_constant__ CUtensorMap tm_c_lo, const TcGemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;  // same offset in both CTAs
+  const uint32_t bars = base + P_BAR_OFF;
+  auto full_bar = [&](int s) { return bars + 8u * s; };
+  auto empty_bar = [&](int s) { return bars + 8u * (PSTAGES + s); };
+  auto acc_full = [&](int b) { return bars + 8u * (2 * PSTAGES + b); };
+  auto acc_empty = [&](int b) { return bars + 8u * (2 * PSTAGES + 2 + b); };
+  const uint32_t tmem_slot = bars + 8u * (2 * PSTAGES + 4);
+  uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cta_rank_in_cluster();
+  const uint32_t peer = rank ^ 1u;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int KB = (p.K + BK - 1) / BK;
+  const int MT = (p.M + 255) / 256, NT = (p.N + PBN - 1) / PBN;
+  const int ntiles = MT * NT;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PSTAGES; ++s) {
+      mbar_init(full_bar(s), 1);   // CTA 0's: one expect_tx arrive per fill, both CTAs' bytes
+      mbar_init(empty_bar(s), 1);  // one commit per fill
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full(b), 1);
+      mbar_init(acc_empty(b), 2 * kEpiWarps);  // CTA 0's: every epilogue warp of the pair
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 2) {
+    // collective over the pair: the same warp of both CTAs allocates
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot),
+                 "r"(P_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers exist before any remote arrive or TMA
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot_ptr;
+  const uint32_t full0 = map_to_cta(full_bar(0), 0);  // CTA 0's full barriers (cluster addresses)
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer (both CTAs): this CTA's A rows and W half ------------
+    int it = 0;
+    for (int tile = pair; tile < ntiles; tile += npairs) {
+      const int m0 = (tile / NT) * 256 + 128 * (int)rank;
+      const int n0 = (tile % NT) * PBN + 128 * (int)rank;
+      for (int kb = 0; kb < KB; ++kb, ++it) {
+        const int s = it % PSTAGES, n = it / PSTAGES;
+        if (it >= PSTAGES) mbar_wait(empty_bar(s), (n - 1) & 1, p.status, 0x1100);
+        const uint32_t st = base + s * P_STAGE;
+        if (rank == 0) mbar_expect_tx(full_bar(s), 2 * P_STAGE);
+        const uint32_t fb = full0 + 8u * s;
+        tma_load_2d_pair(st, &tm_a_hi, kb * BK, m0, fb);
+        tma_load_2d_pair(st + P_TILE, &tm_a_lo, kb * BK, m0, fb);
+        tma_load_2d_pair(st + 2 * P_TILE, &tm_w_hi, kb * BK, n0, fb);
+        tma_load_2d_pair(st + 3 * P_TILE, &tm_w_lo, kb * BK, n0, fb);
+      }
+    }
+    // every stage's last release (a commit from CTA 0) has arrived before this
+    // CTA may retire
+    for (int k = it > PSTAGES ? it - PSTAGES : 0; k < it; ++k)
+      mbar_wait(empty_bar(k % PSTAGES), (k / PSTAGES) & 1, p.status, 0x1200);
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ---- MMA issuer (CTA 0 only) -------------------------------------------
+    const uint32_t peer_empty0 = map_to_cta(empty_bar(0), peer);
+    const uint32_t peer_accf0 = map_to_cta(acc_full(0), peer);
+    int it = 0, local = 0;
+    for (int tile = pair; tile < ntiles; tile += npairs, ++local) {
+      const int ab = local & 1;
+      if (local >= 2) mbar_wait(acc_empty(ab), ((local >> 1) - 1) & 1, p.status, 0x2100);
+      tc_fence_after();
+      const uint32_t acc = tmem_base + (uint32_t)(ab * PBN);
+      for (int kb = 0; kb < KB; ++kb, ++it) {
+        const int s = it % PSTAGES, n = it / PSTAGES;
+        mbar_wait(full_bar(s), n & 1, p.status, 0x2000);
+        tc_fence_after();
+        const uint32_t st = base + s * P_STAGE;
+        const uint64_t a_hi = umma_desc_sw64(st), a_lo = umma_desc_sw64(st + P_TILE);
+        const uint64_t w_hi = umma_desc_sw64(st + 2 * P_TILE);
+        const uint64_t w_lo = umma_desc_sw64(st + 3 * P_TILE);
+#pragma unroll
+        for (int k = 0; k < BK / 8; ++k) {
+          const uint64_t ko = (uint64_t)(k * 2);
+          umma_tf32_pair(acc, a_hi + ko, w_hi + ko, P_IDESC, (kb | k) != 0);
+          umma_tf32_pair(acc, a_hi + ko, w_lo + ko, P_IDESC, 1);
+          umma_tf32_pair(acc, a_lo + ko, w_hi + ko, P_IDESC, 1);
+        }
+        umma_commit_pair(map_to_cta(empty_bar(s), 0));  // stage s free in both CTAs
+        umma_commit_pair(peer_empty0 + 8u * s);
+      }
+      umma_commit_pair(map_to_cta(acc_full(ab), 0));    // accumulator ab complete in both
+      umma_commit_pair(peer_accf0 + 8u * ab);
+    }
+  } else if (warp >= 4) {
+    // ---- epilogue (both CTAs): this CTA's 128 rows --------------------------
+    const int q = warp & 3;
+    const int chalf = (warp - 4) >> 2;
+    const uint32_t stg = base + P_STG_OFF + (uint32_t)(warp - 4) * STG_WARP;
+    uint8_t *stg_ptr = smem_raw + (stg - raw);
+    const bool split_out = p.C_hi != nullptr;
+    const uint32_t acc_empty0 = map_to_cta(acc_empty(0), 0);
+    int local = 0;
+    for (int tile = pair; tile < ntiles; tile += npairs, ++local) {
+      const int ab = local & 1;
+      const int m0 = (tile / NT) * 256 + 128 * (int)rank, n0 = (tile % NT) * PBN;
+      mbar_wait(acc_full(ab), (local >> 1) & 1, p.status, 0x3000);
+      tc_fence_after();
+      const int row0 = m0 + q * 32;
+      const int row = row0 + lane;
+      const bool row_in = row < p.M;
+      const bool valid = row_in && (p.row_mask == nullptr || p.row_mask[row] != 0);
+#pragma unroll 1
+      for (int c0 = chalf * (PBN / 2); c0 < (chalf + 1) * (PBN / 2); c0 += 16) {
+        float v[16];
+        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * PBN + c0), v);
+        const int col0 = n0 + c0;
+        if (col0 >= p.N || row0 >= p.M) continue;  // warp-uniform
+        epilogue_values(p, row, row_in, valid, col0, v);
+        if (p.vt_hi != nullptr && col0 >= p.vt_col0) {
+          if (row_in) store_vt(p, row, col0, v);
+          continue;
+        }
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
+        if (split_out) {
+          float4 hq[4], lq[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float4 o = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+            hq[u] = make_float4(tf32_round(o.x), tf32_round(o.y), tf32_round(o.z), tf32_round(o.w));
+            lq[u] = make_float4(o.x - hq[u].x, o.y - hq[u].y, o.z - hq[u].z, o.w - hq[u].w);
+          }
+          stage_row(stg_ptr, lane, hq);
+          stage_row(stg_ptr + 2048, lane, lq);
+        } else {
+          float4 oq[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            oq[u] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+          stage_row(stg_ptr, lane, oq);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (split_out) {
+            tma_store_2d(&tm_c_hi, stg, col0, row0);
+            tma_store_2d(&tm_c_lo, stg + 2048, col0, row0);
+          } else {
+            tma_store_2d(&tm_c, stg, col0, row0);
+          }
+          bulk_commit();
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8u * ab);  // CTA 0's barrier
+    }
+    if (lane == 0) bulk_wait_all();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // no remote arrive or MMA can target a CTA that has retired
+  if (warp == 2) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(P_TMEM_COLS)
+                 : "memory");
+  }
+}
+
 // cuTensorMapEncodeTiled, resolved at run time through the runtime's driver
 // entry-point query so the library has no link-time dependency on libcuda.
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -494,6 +747,58 @@ int launch_bn(const TcGemmParams &p, cudaStream_t stream) {
   return TT_OK;
 }
 
+int launch_pair(const TcGemmParams &p, cudaStream_t stream, int sms) {
+  CUtensorMap ta_hi, ta_lo, tw_hi, tw_lo;
+  int rc;
+  if ((rc = make_tmap(&ta_hi, p.A_hi, p.M, p.K, p.lda, 128)) ||
+      (rc = make_tmap(&ta_lo, p.A_lo, p.M, p.K, p.lda, 128)) ||
+      (rc = make_tmap(&tw_hi, p.W_hi, p.N, p.K, p.K, 128)) ||
+      (rc = make_tmap(&tw_lo, p.W_lo, p.N, p.K, p.K, 128)))
+    return rc;
+  CUtensorMap tc = ta_hi, tc_hi = ta_hi, tc_lo = ta_hi;
+  if (p.C != nullptr && (rc = make_tmap(&tc, p.C, p.M, p.N, p.ldc, 32))) return rc;
+  if (p.C_hi != nullptr && ((rc = make_tmap(&tc_hi, p.C_hi, p.M, p.N, p.ldc, 32)) ||
+                            (rc = make_tmap(&tc_lo, p.C_lo, p.M, p.N, p.ldc, 32))))
+    return rc;
+  static bool attr_set = false;
+  if (!attr_set) {
+    TT_CUDA_TRY(cudaFuncSetAttribute(gemm_tc3_pair_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P_SMEM));
+    attr_set = true;
+  }
+  const int64_t tiles = (int64_t)((p.M + 255) / 256) * ((p.N + PBN - 1) / PBN);
+  const int pairs = (int)std::min<int64_t>(tiles, sms / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * pairs));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = P_SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  TT_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_tc3_pair_kernel, ta_hi, ta_lo, tw_hi, tw_lo, tc, tc_hi,
+                                 tc_lo, p));
+  TT_LAUNCH_CHECK("gemm_tc3_pair");
+  return TT_OK;
+}
+
+int sm_count() {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      cudaGetLastError();
+      sms = 148;
+    }
+  }
+  return sms;
+}
+
 }  // namespace
 
 int launch_gemm_tc3(const TcGemmParams &p, cudaStream_t stream) {
@@ -504,6 +809,14 @@ int launch_gemm_tc3(const TcGemmParams &p, cudaStream_t stream) {
     return fail(TT_ERR_UNSUPPORTED, "gemm_tc: exactly one of C and the C_hi/C_lo split");
   if (p.vt_hi != nullptr && (p.vt_col0 % 16 != 0 || p.head_dim % 16 != 0))
     return fail(TT_ERR_UNSUPPORTED, "gemm_tc: transposed value columns need 16-aligned heads");
+  // CTA pairs (256 x 256 tiles) cut the L2 -> SM operand traffic by a third
+  // and keep N = 256 MMAs; they run when the pair tiles fill at least one wave
+  // (measured on B200: M 16384 x N 512 x K 2048, 1.7 waves of pairs, beats
+  // 3.5 waves of single-CTA 128 x 128 tiles)
+  const int sms = sm_count();
+  const int64_t pair_tiles = (int64_t)((p.M + 255) / 256) * ((p.N + PBN - 1) / PBN);
+  if (pair_tiles >= sms / 2)
+    return launch_pair(p, stream, sms);
   // N = 256 tiles halve the shared-memory operand traffic per FLOP; narrow
   // projections use 128-wide tiles so every SM still gets work
   const int64_t tiles256 = (int64_t)((p.M + BM - 1) / BM) * ((p.N + 255) / 256);
