@@ -40,7 +40,8 @@ typedef enum tt_status {
   TT_ERR_WORKSPACE = -4,       /* workspace or image smaller than required */
   TT_ERR_CUDA = -5,            /* a CUDA runtime call or launch failed */
   TT_ERR_DEVICE_TIMEOUT = -6,  /* a bounded device-side wait gave up (status word) */
-  TT_ERR_DEVICE_FAULT = -7     /* a device-side self-check failed (status word) */
+  TT_ERR_DEVICE_FAULT = -7,    /* a device-side self-check failed (status word) */
+  TT_ERR_DEVICE_RANGE = -8     /* an attention operand beyond the fp16 range (status word) */
 } tt_status;
 
 /* Shape record: the fields of TransformerConfig that fix the weights

@@ -21,6 +21,7 @@ TT_ERR_WORKSPACE = -4
 TT_ERR_CUDA = -5
 TT_ERR_DEVICE_TIMEOUT = -6
 TT_ERR_DEVICE_FAULT = -7
+TT_ERR_DEVICE_RANGE = -8
 
 # Size of the library's fixed scratch array behind tt_forward_noalloc.
 TT_NOALLOC_SCRATCH_BYTES = 16 << 20

@@ -204,8 +204,9 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
   const int64_t T = batch * seq;
   if (T > INT32_MAX) return fail(TT_ERR_UNSUPPORTED, "tensor-core schedule: too many tokens");
   auto WS = [&](size_t off) { return reinterpret_cast<float *>(ws + off); };
-  float *qkv = WS(W.qkv), *qkv_hi = WS(W.qkv_hi), *qkv_lo = WS(W.qkv_lo);
-  float *vt_hi = WS(W.vt_hi), *vt_lo = WS(W.vt_lo);
+  auto WH = [&](size_t off) { return reinterpret_cast<uint16_t *>(ws + off); };
+  float *qkv = WS(W.qkv);
+  uint16_t *qk_hi = WH(W.qk_hi), *qk_lo = WH(W.qk_lo), *vt_hi = WH(W.vt_hi), *vt_lo = WH(W.vt_lo);
   float *ln_hi = WS(W.ln_hi), *ln_lo = WS(W.ln_lo);
   float *ctx_hi = WS(W.ctx_hi), *ctx_lo = WS(W.ctx_lo);
   float *h_hi = WS(W.h_hi), *h_lo = WS(W.h_lo);
@@ -226,8 +227,8 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
     g.bias = P(o.bqkv); g.ldc = 3LL * D; g.status = status;
     g.M = (int)T; g.N = 3 * D; g.K = D; g.epilogue = EPI_BIAS;
     if (W.tc_attention) {
-      g.C_hi = qkv_hi; g.C_lo = qkv_lo;  // the attention consumes the split
-      g.vt_hi = vt_hi; g.vt_lo = vt_lo;  // ... and v transposed
+      g.H_hi = qk_hi; g.H_lo = qk_lo; g.h_cols = 2 * D;  // the attention reads the fp16 split
+      g.vt_hi = vt_hi; g.vt_lo = vt_lo;                  // ... and v transposed
       g.vt_col0 = 2 * D; g.seq = (int)seq; g.seq_pad = W.seq_pad; g.heads = H; g.head_dim = hd;
     } else {
       g.C = qkv;
@@ -237,7 +238,7 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
     const float scale = (float)(1.0 / std::sqrt((double)hd));
     if (W.tc_attention) {
       AttentionTcParams a{};
-      a.qkv_hi = qkv_hi; a.qkv_lo = qkv_lo; a.vt_hi = vt_hi; a.vt_lo = vt_lo;
+      a.qk_hi = qk_hi; a.qk_lo = qk_lo; a.vt_hi = vt_hi; a.vt_lo = vt_lo;
       a.ctx_hi = ctx_hi; a.ctx_lo = ctx_lo; a.mask = mask; a.status = status;
       a.batch = batch; a.seq = (int)seq; a.seq_pad = W.seq_pad; a.d_model = D; a.num_heads = H;
       a.head_dim = hd; a.causal = cfg.causal; a.scale = scale;

@@ -1,5 +1,5 @@
-// Causal / key-padded flash attention on tensor cores (tcgen05, 3xTF32) for
-// head_dim 32 and 64.
+// Causal / key-padded flash attention on tensor cores (tcgen05) for head_dim
+// 32 and 64.
 //
 // Semantics as the reference attention (torch_transformer_benchmark.py:97-117):
 // s = (q . k) * hd^-0.5, -inf for keys after the query (causal, :99-103) and
@@ -7,22 +7,27 @@
 // [B, S, H*hd] order. Queries without an allowed key (only padded queries)
 // get a zero context; their rows are zeroed after out_proj as in :120-121.
 //
-// Precision: both products use the TF32 split x = x_hi + x_lo with three
-// tensor-core products (hi.hi + hi.lo + lo.hi), accumulated in fp32: q, k, v
-// arrive split by the q|k|v GEMM, p = exp(s - m) is split by the softmax
-// threads. The context accumulates in fp32 in tensor memory.
+// Precision: both products use a split x = x_hi + x_lo of each operand into
+// two binary16 values (hi = x rounded to fp16, lo = the rest rounded to fp16:
+// about 22 significant bits, as a TF32 pair) and three tensor-core products
+// (hi.hi + hi.lo + lo.hi, tcgen05 kind::f16) accumulated in fp32. q, k, v
+// arrive split by the q|k|v GEMM (which latches TT_ERR_DEVICE_RANGE for a
+// value beyond the fp16 range); p = exp(s - m) is split by the softmax
+// threads, scaled by 2^7 first so that its small values stay clear of the
+// fp16 subnormals (the scale cancels in p.v / sum p; lazy rescaling keeps the
+// scaled p below 2^15). The context accumulates in fp32 in tensor memory. A
+// 16-bit MMA does twice the work of a TF32 one in the same cycles at N = 64
+// and moves half the operand bytes.
 //
 // CTA = (query tile of 128 rows, head, sequence); 384 threads:
 //   warp 0    TMA producer: per 64-key tile, K_hi K_lo (64 keys x HD dims) and
 //             Vt_hi Vt_lo (HD dims x 64 keys, from the transposed copy of v the
-//             q|k|v GEMM writes), in 128-byte swizzle boxes, into a 3-stage
-//             ring;
-//   warp 1    MMA issuer: S_j = Q.K_j^T (A = Q from tensor memory, B = K tile),
-//             then O += P_j.V_j (A = P_j from tensor memory, B = Vt tile); both
-//             B operands are K-major. S is single-buffered (the softmax copies
-//             it to registers at once, so S_{j+1} runs while the softmax of
-//             tile j works); P is double-buffered, so the softmax of tile j+1
-//             writes its P while P_j.V_j is still on the tensor pipe;
+//             q|k|v GEMM writes) into a 4-stage ring;
+//   warp 1    MMA issuer: S_j = Q.K_j^T (A = Q from tensor memory, B = K tile)
+//             into one of two S buffers, then O += P_j.V_j (A = P_j from
+//             tensor memory, B = Vt tile); both B operands are K-major. S and P
+//             are double-buffered, so S_{j+1} and P_{j-1}.V_{j-1} run while the
+//             softmax works on tile j;
 //   warp 2    allocates / frees 512 tensor-memory columns;
 //   warps 4-11 softmax, two warps per tensor-memory lane quarter: query row
 //             q0+t (= tensor-memory lane t) is shared by two threads, one per
@@ -42,33 +47,38 @@
 namespace tt {
 namespace {
 
-constexpr int BQ = 128, BKV = 64, STAGES = 3;
+constexpr int BQ = 128, BKV = 64, STAGES = 4;
 constexpr int kThreads = 384;  // warps 0-3: TMA / MMA / TMEM; warps 4-11: softmax
 
-// Shapes for head_dim HD (32 or 64). Shared-memory stage: K_hi, K_lo
-// (64 keys x HD, HD/32 boxes of 64 rows x 128 B) then Vt_hi, Vt_lo (HD rows x
-// 64 keys, 2 boxes of HD rows x 128 B). Tensor-memory columns (fp32 cells):
-// Q_hi, Q_lo (HD each), S (64), P_hi[b], P_lo[b] (64 each, b = 0, 1), O (HD).
+// Shapes for head_dim HD (32 or 64). Shared-memory stage: K_hi, K_lo (64 keys
+// x HD fp16: rows of 2*HD bytes, 64-byte swizzle at HD 32, 128-byte at HD 64)
+// then Vt_hi, Vt_lo (HD rows x 64 keys: 128-byte rows, 128-byte swizzle).
+// Tensor-memory columns (32-bit cells; a 16-bit operand packs two values per
+// cell): Q_hi, Q_lo (HD/2 each), S[b] (64 each), P[b] = hi (32) | lo (32), O (HD).
 template <int HD>
 struct AtShape {
-  static constexpr uint32_t KBOX = 64 * 128;           // one 64-row K box
-  static constexpr uint32_t VBOX = HD * 128;           // one HD-row V^T box
-  static constexpr uint32_t OPK = (HD / 32) * KBOX;    // one K operand (hi or lo)
-  static constexpr uint32_t OPV = 2 * VBOX;            // one V^T operand (hi or lo)
+  static constexpr uint32_t KROW = 2 * HD;              // bytes of one K row
+  static constexpr uint32_t OPK = 64 * KROW;            // one K operand (hi or lo)
+  static constexpr uint32_t OPV = HD * 128;             // one V^T operand (hi or lo)
   static constexpr uint32_t STAGE = 2 * OPK + 2 * OPV;
   static constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE + 1024 + 256;
-  static constexpr uint32_t T_QHI = 0, T_QLO = HD, T_S = 2 * HD, T_P = 2 * HD + 64,
-                            T_O = 2 * HD + 64 + 256;
-  // P buffer b: hi at T_P + 128 b, lo 64 columns after it
-  static constexpr uint32_t t_phi(int b) { return T_P + 128u * b; }
-  static constexpr uint32_t t_plo(int b) { return T_P + 128u * b + 64u; }
+  static constexpr uint32_t T_QHI = 0, T_QLO = HD / 2, T_S = HD, T_P = HD + 128,
+                            T_O = HD + 256;
+  static constexpr uint32_t t_s(int b) { return T_S + 64u * b; }
+  static constexpr uint32_t t_phi(int b) { return T_P + 64u * b; }
+  static constexpr uint32_t t_plo(int b) { return T_P + 64u * b + 32u; }
   static constexpr uint32_t TMEM_COLS = 512;
   static_assert(T_O + HD <= TMEM_COLS, "tensor memory");
-  // instruction descriptors: D fp32, A/B tf32, both K-major, M = 128
-  static constexpr uint32_t IDESC_S = (1u << 4) | (2u << 7) | (2u << 10) |
-                                      ((uint32_t)(64 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-  static constexpr uint32_t IDESC_PV = (1u << 4) | (2u << 7) | (2u << 10) |
-                                       ((uint32_t)(HD >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+  static_assert(OPK % 1024 == 0 && OPV % 1024 == 0, "operands on the swizzle period");
+  // K operand descriptor fields: swizzle mode (4 = 64 B, 2 = 128 B) and the
+  // stride between 8-row groups
+  static constexpr uint32_t K_SWZ = HD == 32 ? 4u : 2u;
+  static constexpr uint32_t K_SBO = 8 * KROW;
+  // instruction descriptors: kind::f16, D fp32, A/B fp16, both K-major, M = 128
+  static constexpr uint32_t IDESC_S =
+      (1u << 4) | ((uint32_t)(64 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+  static constexpr uint32_t IDESC_PV =
+      (1u << 4) | ((uint32_t)(HD >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -118,14 +128,15 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *tm,
       "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
-// Shared-memory matrix descriptor, 128-byte swizzle, version 1.
-__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+// Shared-memory matrix descriptor, K-major, version 1: swizzle mode swz,
+// 8-row groups sbo bytes apart.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t sbo, uint32_t swz) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)1 << 16;
   d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
   d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
+  d |= (uint64_t)swz << 61;
   return d;
 }
 __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
@@ -133,7 +144,7 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accum)
       : "memory");
 }
@@ -162,17 +173,26 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float *v) {
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *v) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
       "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
-      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
-      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
-      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-      "r"(__float_as_uint(v[15]))
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15])
       : "memory");
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t *v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st16_f32(uint32_t taddr, const float *v) {  // fp32 cells
+  uint32_t r[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(v[i]);
+  tmem_st16(taddr, r);
 }
 // 2^x with the hardware's approximate base-2 exponential (ex2.approx.ftz);
 // 2^-inf = 0.
@@ -184,6 +204,20 @@ __device__ __forceinline__ float fast_exp2(float x) {
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
+// Two fp32 values -> their fp16 splits packed as (hi pair, lo pair), the
+// element with the lower index in the low 16 bits.
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t &hi, uint32_t &lo) {
+  uint32_t h;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));
+  float ha, hb;
+  asm("{\n\t.reg .f16 x, y;\n\tmov.b32 {x, y}, %2;\n\tcvt.f32.f16 %0, x;\n\tcvt.f32.f16 %1, y;\n\t}"
+      : "=f"(ha), "=f"(hb)
+      : "r"(h));
+  uint32_t l;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(l) : "f"(b - hb), "f"(a - ha));
+  hi = h;
+  lo = l;
+}
 
 template <int HD>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -193,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap tm_vlo, const AttentionTcParams p) {
   using Sh = AtShape<HD>;
   constexpr uint32_t STAGE = Sh::STAGE, OPK = Sh::OPK, OPV = Sh::OPV;
-  constexpr uint32_t T_QHI = Sh::T_QHI, T_QLO = Sh::T_QLO, T_S = Sh::T_S, T_O = Sh::T_O,
+  constexpr uint32_t T_QHI = Sh::T_QHI, T_QLO = Sh::T_QLO, T_O = Sh::T_O,
                      TMEM_COLS = Sh::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   __shared__ int s_kv_len;
@@ -204,12 +238,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t bars = base + STAGES * STAGE;
   auto kv_full = [&](int s) { return bars + 8u * s; };
   auto kv_empty = [&](int s) { return bars + 8u * (STAGES + s); };
-  const uint32_t s_full = bars + 8u * (2 * STAGES);
-  const uint32_t s_free = bars + 8u * (2 * STAGES + 1);
-  auto p_full = [&](int b) { return bars + 8u * (2 * STAGES + 2 + b); };  // P buffer b written
-  auto o_done = [&](int b) { return bars + 8u * (2 * STAGES + 4 + b); };  // its P.V finished
-  const uint32_t q_ready = bars + 8u * (2 * STAGES + 6);
-  const uint32_t tmem_slot = bars + 8u * (2 * STAGES + 7);
+  auto s_full = [&](int b) { return bars + 8u * (2 * STAGES + b); };      // S buffer b written
+  auto s_free = [&](int b) { return bars + 8u * (2 * STAGES + 2 + b); };  // ... and read
+  auto p_full = [&](int b) { return bars + 8u * (2 * STAGES + 4 + b); };  // P buffer b written
+  auto o_done = [&](int b) { return bars + 8u * (2 * STAGES + 6 + b); };  // its P.V finished
+  const uint32_t q_ready = bars + 8u * (2 * STAGES + 8);
+  const uint32_t tmem_slot = bars + 8u * (2 * STAGES + 9);
   uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -220,22 +254,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int q0 = qt * BQ;
   const uint8_t *mrow = p.mask ? p.mask + b * S : nullptr;
 
-  // The softmax threads' Q row (TF32 split, HD/2 dims each) and the mask
-  // bytes are requested together, so the prologue pays one memory latency.
-  float qv[HD];
+  // The softmax threads' Q row (fp16 split, HD/2 dims each: HD/4 packed cells)
+  // and the mask bytes are requested together, so the prologue pays one
+  // memory latency.
+  uint32_t qv[2][HD / 4];
   if (warp >= 4) {
     const int t = (warp & 3) * 32 + lane, kh = (warp - 4) >> 2;
     const int row = q0 + t;
-    const int64_t qoff = (b * S + (row < S ? row : 0)) * (int64_t)(3 * D) + (int64_t)h * HD +
+    const int64_t qoff = (b * S + (row < S ? row : 0)) * (int64_t)(2 * D) + (int64_t)h * HD +
                          (HD / 2) * kh;
 #pragma unroll
     for (int which = 0; which < 2; ++which) {
-      const float4 *src = reinterpret_cast<const float4 *>((which ? p.qkv_lo : p.qkv_hi) + qoff);
+      const uint4 *src = reinterpret_cast<const uint4 *>((which ? p.qk_lo : p.qk_hi) + qoff);
 #pragma unroll
-      for (int i = 0; i < HD / 8; ++i) {
-        const float4 x = row < S ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-        float *d = qv + which * (HD / 2) + 4 * i;
-        d[0] = x.x; d[1] = x.y; d[2] = x.z; d[3] = x.w;
+      for (int i = 0; i < HD / 16; ++i) {
+        const uint4 x = row < S ? src[i] : make_uint4(0u, 0u, 0u, 0u);
+        qv[which][4 * i] = x.x; qv[which][4 * i + 1] = x.y;
+        qv[which][4 * i + 2] = x.z; qv[which][4 * i + 3] = x.w;
       }
     }
   }
@@ -270,9 +305,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(kv_empty(s), 1);
     }
     // the 8 softmax warps arrive once per warp (an elected lane after __syncwarp)
-    mbar_init(s_full, 1);
-    mbar_init(s_free, 8);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(s_full(i), 1);
+      mbar_init(s_free(i), 8);
       mbar_init(p_full(i), 8);
       mbar_init(o_done(i), 1);
     }
@@ -292,44 +327,40 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0 && lane == 0) {
     // ---- TMA producer: K/V tiles -------------------------------------------
-    const int kcol = D + h * HD;
+    const int kcol = D + h * HD;  // first k column (fp16 elements) of this head
     const int bh = (int)b * p.num_heads + h;
     for (int j = 0; j < nkv; ++j) {
       const int s = j % STAGES, n = j / STAGES;
       if (j >= STAGES) mbar_wait(kv_empty(s), (n - 1) & 1, p.status, 0x4100 + j);
       const uint32_t st = base + s * STAGE;
       mbar_expect_tx(kv_full(s), STAGE);
-      // K rows = keys, 32 dims per box; Vt rows = dims, 32 keys per box
-      for (int bx = 0; bx < HD / 32; ++bx) {
-        tma_load_3d(st + bx * Sh::KBOX, &tm_hi, kcol + 32 * bx, j * BKV, (int)b, kv_full(s));
-        tma_load_3d(st + OPK + bx * Sh::KBOX, &tm_lo, kcol + 32 * bx, j * BKV, (int)b, kv_full(s));
-      }
-      for (int half = 0; half < 2; ++half) {
-        tma_load_3d(st + 2 * OPK + half * Sh::VBOX, &tm_vhi, j * BKV + 32 * half, 0, bh, kv_full(s));
-        tma_load_3d(st + 2 * OPK + OPV + half * Sh::VBOX, &tm_vlo, j * BKV + 32 * half, 0, bh,
-                    kv_full(s));
-      }
+      tma_load_3d(st, &tm_hi, kcol, j * BKV, (int)b, kv_full(s));
+      tma_load_3d(st + OPK, &tm_lo, kcol, j * BKV, (int)b, kv_full(s));
+      tma_load_3d(st + 2 * OPK, &tm_vhi, j * BKV, 0, bh, kv_full(s));
+      tma_load_3d(st + 2 * OPK + OPV, &tm_vlo, j * BKV, 0, bh, kv_full(s));
     }
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer --------------------------------------------------------
     auto issue_s = [&](int j) {
-      const int s = j % STAGES;
+      const int s = j % STAGES, sb = j & 1;
       mbar_wait(kv_full(s), (j / STAGES) & 1, p.status, 0x4200 + j);
-      // S is free once the softmax has copied S_{j-1} to registers
-      if (j >= 1) mbar_wait(s_free, (j - 1) & 1, p.status, 0x4300 + j);
+      // S buffer sb last held S_{j-2}; the softmax has copied it to registers
+      if (j >= 2) mbar_wait(s_free(sb), ((j >> 1) - 1) & 1, p.status, 0x4300 + j);
       fence_after();
       const uint32_t kst = base + s * STAGE;
-      const uint32_t sd = tm + T_S;
-      // descriptors built once; a k-step only advances the start-address field
-      const uint64_t khi0 = sdesc(kst, 16, 1024), klo0 = sdesc(kst + OPK, 16, 1024);
+      const uint32_t sd = tm + Sh::t_s(sb);
+      // descriptors built once; a k-step of 16 dims advances the start address
+      // by 32 bytes (2 units)
+      const uint64_t khi0 = sdesc(kst, Sh::K_SBO, Sh::K_SWZ);
+      const uint64_t klo0 = sdesc(kst + OPK, Sh::K_SBO, Sh::K_SWZ);
 #pragma unroll
-      for (int kk = 0; kk < HD / 8; ++kk) {  // 8 head dims per MMA
-        const uint64_t koff = ((kk >> 2) * Sh::KBOX + (kk & 3) * 32u) >> 4;
+      for (int kk = 0; kk < HD / 16; ++kk) {
+        const uint64_t koff = (uint64_t)(2 * kk);
         mma_ts(sd, tm + T_QHI + 8u * kk, khi0 + koff, Sh::IDESC_S, kk > 0);
         mma_ts(sd, tm + T_QHI + 8u * kk, klo0 + koff, Sh::IDESC_S, 1);
         mma_ts(sd, tm + T_QLO + 8u * kk, khi0 + koff, Sh::IDESC_S, 1);
       }
-      mma_commit(s_full);
+      mma_commit(s_full(sb));
     };
     mbar_wait(q_ready, 0, p.status, 0x4000);
     issue_s(0);
@@ -339,10 +370,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(p_full(pb), (j >> 1) & 1, p.status, 0x4400 + j);
       fence_after();
       const uint32_t vst = base + s * STAGE + 2 * OPK;
-      const uint64_t vhi0 = sdesc(vst, 16, 1024), vlo0 = sdesc(vst + OPV, 16, 1024);
+      const uint64_t vhi0 = sdesc(vst, 1024, 2), vlo0 = sdesc(vst + OPV, 1024, 2);
 #pragma unroll
-      for (int kk = 0; kk < BKV / 8; ++kk) {  // 8 keys per MMA
-        const uint64_t voff = ((kk >> 2) * Sh::VBOX + (kk & 3) * 32u) >> 4;
+      for (int kk = 0; kk < BKV / 16; ++kk) {  // 16 keys per MMA
+        const uint64_t voff = (uint64_t)(2 * kk);
         mma_ts(tm + T_O, tm + Sh::t_phi(pb) + 8u * kk, vhi0 + voff, Sh::IDESC_PV, (j | kk) != 0);
         mma_ts(tm + T_O, tm + Sh::t_phi(pb) + 8u * kk, vlo0 + voff, Sh::IDESC_PV, 1);
         mma_ts(tm + T_O, tm + Sh::t_plo(pb) + 8u * kk, vhi0 + voff, Sh::IDESC_PV, 1);
@@ -353,19 +384,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= 4) {
     // ---- softmax: rows split over two warpgroups by key half ----------------
     const int t = (warp & 3) * 32 + lane;   // row within the tile = tensor-memory lane
-    const int kh = (warp - 4) >> 2;         // which 32 keys (and 32 dims) of a tile
+    const int kh = (warp - 4) >> 2;         // which 32 keys (and HD/2 dims) of a tile
     const int row = q0 + t;
     const bool row_in = row < S;
     const uint32_t lane_base = tm + ((uint32_t)((warp & 3) * 32) << 16);
-    const uint32_t col_off = 32u * kh;             // this thread's 32 keys of a tile
-    const uint32_t dim_off = (uint32_t)(HD / 2) * kh;  // ... and HD/2 dims of Q and O
+    const uint32_t col_off = 32u * kh;                 // this thread's 32 scores of a tile
+    const uint32_t pcol_off = 16u * kh;                // ... as 16 packed P cells
+    const uint32_t dim_off = (uint32_t)(HD / 2) * kh;  // ... and HD/2 dims of O
     {
       // Q row -> tensor memory: this thread's dims [dim_off, dim_off + HD/2)
-#pragma unroll
-      for (int which = 0; which < 2; ++which)
-#pragma unroll
-        for (int c = 0; c < HD / 2; c += 16)
-          tmem_st16(lane_base + (which ? T_QLO : T_QHI) + dim_off + c, qv + which * (HD / 2) + c);
+      // as HD/4 packed cells of Q_hi and of Q_lo
+      const uint32_t qcol = (uint32_t)(HD / 4) * kh;
+      if (HD == 64) {
+        tmem_st16(lane_base + T_QHI + qcol, qv[0]);
+        tmem_st16(lane_base + T_QLO + qcol, qv[1]);
+      } else {
+        tmem_st8(lane_base + T_QHI + qcol, qv[0]);
+        tmem_st8(lane_base + T_QLO + qcol, qv[1]);
+      }
       tmem_wait_st();
       fence_before();
       __syncwarp();
@@ -375,13 +411,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // relative to a reference max m_ref that is raised lazily: only when a
     // row's max exceeds it by more than 2^8 are the row's running context (in
     // tensor memory, accumulated by the P.V MMAs) and sum rescaled, so P <= 256
-    // and the usual case needs no tensor-memory round trip. Both threads of a
-    // row see the same maxima, so they take the same decisions.
+    // (2^15 after the 2^7 scale) and the usual case needs no tensor-memory
+    // round trip. Both threads of a row see the same maxima, so they take the
+    // same decisions.
     const float sl = p.scale * 1.4426950408889634f;
     constexpr float kLazy = 8.0f;
+    constexpr float kPScale = 7.0f;  // log2 of the scale applied to P
     float m_ref = -CUDART_INF_F, l = 0.f;
     for (int j = 0; j < nkv; ++j) {
-      const int pb = j & 1;
+      const int sb = j & 1;
       const int k0 = j * BKV + 32 * kh;     // first key of this thread's half
       uint32_t ok;
       {
@@ -389,15 +427,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = __ballot_sync(0xffffffffu, ka < kv_end && (mrow == nullptr || mrow[ka] != 0));
       }
       const bool diag = p.causal && k0 + 31 > q0;  // half reaches past the first query
-      mbar_wait(s_full, j & 1, p.status, 0x4500 + j);
+      mbar_wait(s_full(sb), (j >> 1) & 1, p.status, 0x4500 + j);
       fence_after();
       float sv[32];
-      tmem_ld16(lane_base + T_S + col_off, sv);
-      tmem_ld16(lane_base + T_S + col_off + 16, sv + 16);
+      tmem_ld16(lane_base + Sh::t_s(sb) + col_off, sv);
+      tmem_ld16(lane_base + Sh::t_s(sb) + col_off + 16, sv + 16);
       tmem_wait_ld();
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(s_free);
+      if (lane == 0) mbar_arrive(s_free(sb));
       // allowed keys of this half as one word: valid (ballot) and, on the
       // diagonal, key k0 + c <= row, i.e. bits 0 .. row - k0 (one select per
       // score below; a per-score && / || compiles to branches)
@@ -413,9 +451,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
       }
       float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-      s_rowmax[pb][kh][t] = mx;
+      s_rowmax[sb][kh][t] = mx;
       asm volatile("bar.sync 1, 256;" ::: "memory");  // the 8 softmax warps
-      mx = fmaxf(mx, s_rowmax[pb][kh ^ 1][t]);
+      mx = fmaxf(mx, s_rowmax[sb][kh ^ 1][t]);
       if (mx > m_ref + kLazy || (m_ref == -CUDART_INF_F && mx != -CUDART_INF_F)) {
         const float alpha = fast_exp2(m_ref - mx);  // 0 when m_ref is -inf
         if (j > 0 && m_ref != -CUDART_INF_F) {
@@ -430,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 16; ++i) ov[i] *= alpha;
-            tmem_st16(lane_base + T_O + dim_off + c, ov);
+            tmem_st16_f32(lane_base + T_O + dim_off + c, ov);
           }
         }
         l *= alpha;
@@ -438,9 +476,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       float ps4[4] = {0.f, 0.f, 0.f, 0.f};
       if (m_ref != -CUDART_INF_F) {
+        const float off = m_ref - kPScale;
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          sv[c] = fast_exp2(sv[c] - m_ref);  // 0 for masked keys
+          sv[c] = fast_exp2(sv[c] - off);  // 2^7 p; 0 for masked keys
           ps4[c & 3] += sv[c];
         }
       } else {
@@ -448,28 +487,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 32; ++c) sv[c] = 0.f;
       }
       l += (ps4[0] + ps4[1]) + (ps4[2] + ps4[3]);
+      uint32_t phi[16], plo[16];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) split_pair(sv[2 * c], sv[2 * c + 1], phi[c], plo[c]);
       // P buffer pb last held P_{j-2}: its P.V must be done before it is
       // overwritten
       if (j >= 2) {
-        mbar_wait(o_done(pb), ((j - 2) >> 1) & 1, p.status, 0x4800 + j);
+        mbar_wait(o_done(sb), ((j - 2) >> 1) & 1, p.status, 0x4800 + j);
         fence_after();
       }
-      // this half of P (TF32 split) -> tensor memory
-#pragma unroll
-      for (int c = 0; c < 32; c += 16) {
-        float hi[16], lo[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          hi[i] = tf32_round(sv[c + i]);
-          lo[i] = sv[c + i] - hi[i];
-        }
-        tmem_st16(lane_base + Sh::t_phi(pb) + col_off + c, hi);
-        tmem_st16(lane_base + Sh::t_plo(pb) + col_off + c, lo);
-      }
+      tmem_st16(lane_base + Sh::t_phi(sb) + pcol_off, phi);
+      tmem_st16(lane_base + Sh::t_plo(sb) + pcol_off, plo);
       tmem_wait_st();
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full(pb));
+      if (lane == 0) mbar_arrive(p_full(sb));
     }
     // row sum = both halves' partial sums
     s_rowsum[kh][t] = l;
@@ -529,38 +561,40 @@ int encode_fn(EncodeTiledFn *out) {
   return TT_OK;
 }
 
-// [batch, seq, 3*d_model] fp32 view of a q|k|v buffer; box = 32 columns x 64
-// rows x 1 sequence, 128-byte swizzle, zero fill past the sequence end.
-int make_qkv_map(CUtensorMap *tm, const float *ptr, int64_t batch, int seq, int d_model) {
+// [batch, seq, 2*d_model] fp16 view of a q|k buffer; box = hd columns x 64
+// rows x 1 sequence (rows of 2*hd bytes: 64-byte swizzle at hd 32, 128-byte at
+// hd 64), zero fill past the sequence end.
+int make_qk_map(CUtensorMap *tm, const uint16_t *ptr, int64_t batch, int seq, int d_model, int hd) {
   EncodeTiledFn encode;
   int rc = encode_fn(&encode);
   if (rc != TT_OK) return rc;
-  cuuint64_t dims[3] = {(cuuint64_t)(3 * d_model), (cuuint64_t)seq, (cuuint64_t)batch};
-  cuuint64_t strides[2] = {(cuuint64_t)(3 * d_model) * 4, (cuuint64_t)seq * (3 * d_model) * 4};
-  cuuint32_t box[3] = {32, (cuuint32_t)BKV, 1};
+  cuuint64_t dims[3] = {(cuuint64_t)(2 * d_model), (cuuint64_t)seq, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(2 * d_model) * 2, (cuuint64_t)seq * (2 * d_model) * 2};
+  cuuint32_t box[3] = {(cuuint32_t)hd, (cuuint32_t)BKV, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(ptr), dims,
-                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<uint16_t *>(ptr),
+                            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            hd == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
-    return fail(TT_ERR_CUDA, "cuTensorMapEncodeTiled (q|k|v) failed with CUresult " +
+    return fail(TT_ERR_CUDA, "cuTensorMapEncodeTiled (q|k) failed with CUresult " +
                                  std::to_string((int)r));
   return TT_OK;
 }
 
-// [batch*heads, hd, seq] view of a transposed value buffer (row stride seq_pad);
-// box = 32 keys x hd dims x 1, 128-byte swizzle, zero fill past the sequence.
-int make_vt_map(CUtensorMap *tm, const float *ptr, int64_t bh, int seq, int seq_pad, int hd) {
+// [batch*heads, hd, seq] fp16 view of a transposed value buffer (row stride
+// seq_pad); box = 64 keys x hd dims x 1, 128-byte swizzle, zero fill past the
+// sequence.
+int make_vt_map(CUtensorMap *tm, const uint16_t *ptr, int64_t bh, int seq, int seq_pad, int hd) {
   EncodeTiledFn encode;
   int rc = encode_fn(&encode);
   if (rc != TT_OK) return rc;
   cuuint64_t dims[3] = {(cuuint64_t)seq, (cuuint64_t)hd, (cuuint64_t)bh};
-  cuuint64_t strides[2] = {(cuuint64_t)seq_pad * 4, (cuuint64_t)seq_pad * hd * 4};
-  cuuint32_t box[3] = {32, (cuuint32_t)hd, 1};
+  cuuint64_t strides[2] = {(cuuint64_t)seq_pad * 2, (cuuint64_t)seq_pad * hd * 2};
+  cuuint32_t box[3] = {(cuuint32_t)BKV, (cuuint32_t)hd, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(ptr), dims,
-                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<uint16_t *>(ptr),
+                            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
@@ -589,7 +623,7 @@ int launch_hd(const AttentionTcParams &p, const CUtensorMap &thi, const CUtensor
 }  // namespace
 
 bool attention_tc_supported(int head_dim, int d_model) {
-  return (head_dim == 32 || head_dim == 64) && d_model % 4 == 0;
+  return (head_dim == 32 || head_dim == 64) && d_model % 8 == 0;
 }
 
 int launch_attention_tc(const AttentionTcParams &p, cudaStream_t stream) {
@@ -598,16 +632,16 @@ int launch_attention_tc(const AttentionTcParams &p, cudaStream_t stream) {
     return fail(TT_ERR_UNSUPPORTED, "attention_tc: head_dim must be 32 or 64");
   if (p.batch > 65535 || p.num_heads > 65535)
     return fail(TT_ERR_UNSUPPORTED, "attention_tc: batch and num_heads must be <= 65535");
-  if (((reinterpret_cast<uintptr_t>(p.qkv_hi) | reinterpret_cast<uintptr_t>(p.qkv_lo) |
+  if (((reinterpret_cast<uintptr_t>(p.qk_hi) | reinterpret_cast<uintptr_t>(p.qk_lo) |
         reinterpret_cast<uintptr_t>(p.ctx_hi) | reinterpret_cast<uintptr_t>(p.ctx_lo) |
         reinterpret_cast<uintptr_t>(p.vt_hi) | reinterpret_cast<uintptr_t>(p.vt_lo)) & 15) != 0)
     return fail(TT_ERR_INVALID_ARGUMENT, "attention_tc: buffers must be 16-byte aligned");
-  if (p.seq_pad < p.seq || p.seq_pad % 4 != 0)
-    return fail(TT_ERR_INVALID_ARGUMENT, "attention_tc: seq_pad must be >= seq and a multiple of 4");
+  if (p.seq_pad < p.seq || p.seq_pad % 8 != 0)
+    return fail(TT_ERR_INVALID_ARGUMENT, "attention_tc: seq_pad must be >= seq and a multiple of 8");
   CUtensorMap thi, tlo, tvhi, tvlo;
   int rc;
-  if ((rc = make_qkv_map(&thi, p.qkv_hi, p.batch, p.seq, p.d_model)) ||
-      (rc = make_qkv_map(&tlo, p.qkv_lo, p.batch, p.seq, p.d_model)) ||
+  if ((rc = make_qk_map(&thi, p.qk_hi, p.batch, p.seq, p.d_model, p.head_dim)) ||
+      (rc = make_qk_map(&tlo, p.qk_lo, p.batch, p.seq, p.d_model, p.head_dim)) ||
       (rc = make_vt_map(&tvhi, p.vt_hi, p.batch * p.num_heads, p.seq, p.seq_pad, p.head_dim)) ||
       (rc = make_vt_map(&tvlo, p.vt_lo, p.batch * p.num_heads, p.seq, p.seq_pad, p.head_dim)))
     return rc;

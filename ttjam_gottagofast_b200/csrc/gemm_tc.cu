@@ -215,9 +215,28 @@ __device__ __forceinline__ void epilogue_values(const TcGemmParams &p, int row, 
   }
 }
 
-// Value columns of a q|k|v projection: TF32 split, transposed per (sequence,
-// head) so keys are contiguous; lanes are consecutive rows, so each store is
-// coalesced.
+// fp16 split of x: hi = x rounded to binary16, lo = x - hi rounded to
+// binary16 (bit patterns). |x| beyond the fp16 range latches
+// TT_ERR_DEVICE_RANGE.
+__device__ __forceinline__ uint16_t f16_bits(float x) {
+  uint16_t h;
+  asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(x));
+  return h;
+}
+__device__ __forceinline__ float f16_value(uint16_t h) {
+  float y;
+  asm("cvt.f32.f16 %0, %1;" : "=f"(y) : "h"(h));
+  return y;
+}
+__device__ __forceinline__ void f16_split(float x, uint16_t &hi, uint16_t &lo, bool &range_ok) {
+  range_ok = range_ok && fabsf(x) <= 65504.f;
+  hi = f16_bits(x);
+  lo = f16_bits(x - f16_value(hi));
+}
+
+// Value columns of a q|k|v projection for the tensor-core attention: fp16
+// split, transposed per (sequence, head) so keys are contiguous; lanes are
+// consecutive rows, so each store is coalesced.
 __device__ __forceinline__ void store_vt(const TcGemmParams &p, int row, int col0,
                                          const float (&v)[16]) {
   const bool full = col0 + 16 <= p.N;
@@ -225,13 +244,25 @@ __device__ __forceinline__ void store_vt(const TcGemmParams &p, int row, int col
   const int hh = vc / p.head_dim, d0 = vc % p.head_dim;
   const int bb = row / p.seq, ss = row % p.seq;
   const int64_t base_t = ((int64_t)(bb * p.heads + hh) * p.head_dim + d0) * p.seq_pad + ss;
+  bool ok = true;
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     if (!full && col0 + j >= p.N) break;
-    const float hv = tf32_round(v[j]);
-    p.vt_hi[base_t + (int64_t)j * p.seq_pad] = hv;
-    p.vt_lo[base_t + (int64_t)j * p.seq_pad] = v[j] - hv;
+    uint16_t hi, lo;
+    f16_split(v[j], hi, lo, ok);
+    p.vt_hi[base_t + (int64_t)j * p.seq_pad] = hi;
+    p.vt_lo[base_t + (int64_t)j * p.seq_pad] = lo;
   }
+  if (!ok) raise_status(p.status, TT_ERR_DEVICE_RANGE, col0);
+}
+
+// Writes row `lane` of a 32 x 16 fp16 chunk (two 16-byte units) into a
+// staging buffer laid out as the 32-byte-swizzled box a TMA tensor store
+// reads: unit u of row r sits at unit u ^ ((r >> 2) & 1).
+__device__ __forceinline__ void stage_row16(uint8_t *buf, int lane, const uint4 (&q)[2]) {
+#pragma unroll
+  for (int u = 0; u < 2; ++u)
+    *reinterpret_cast<uint4 *>(buf + lane * 32 + ((u ^ ((lane >> 2) & 1)) << 4)) = q[u];
 }
 
 // Writes row `lane` of a 32 x 16 fp32 chunk into a staging buffer laid out as
@@ -241,6 +272,72 @@ __device__ __forceinline__ void stage_row(uint8_t *buf, int lane, const float4 (
 #pragma unroll
   for (int u = 0; u < 4; ++u)
     *reinterpret_cast<float4 *>(buf + lane * 64 + ((u ^ ((lane >> 1) & 3)) << 4)) = q[u];
+}
+
+// One 16-column chunk of a warp's 32 rows through the epilogue: values (bias,
+// GELU / residual), then out -- transposed value columns by direct stores,
+// everything else through this warp's staging buffers (stg, two 2 KB halves)
+// and a TMA tensor store: fp32 C, its TF32 split, or the fp16 split H.
+__device__ __forceinline__ void epilogue_chunk_out(const TcGemmParams &p, const CUtensorMap *tm_c,
+                                                   const CUtensorMap *tm_hi,
+                                                   const CUtensorMap *tm_lo, uint32_t stg,
+                                                   uint8_t *stg_ptr, int lane, int row0,
+                                                   bool valid, int col0, float (&v)[16]) {
+  const int row = row0 + lane;
+  const bool row_in = row < p.M;
+  epilogue_values(p, row, row_in, valid, col0, v);
+  if (p.vt_hi != nullptr && col0 >= p.vt_col0) {
+    if (row_in) store_vt(p, row, col0, v);
+    return;
+  }
+  // the previous store of this warp must have read the staging buffers
+  if (lane == 0) bulk_wait_read_all();
+  __syncwarp();
+  if (p.H_hi != nullptr) {
+    bool ok = true;
+    uint32_t hw[8], lw[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint16_t h0, l0, h1, l1;
+      f16_split(v[2 * j], h0, l0, ok);
+      f16_split(v[2 * j + 1], h1, l1, ok);
+      hw[j] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+      lw[j] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+    }
+    if (!ok && row_in) raise_status(p.status, TT_ERR_DEVICE_RANGE, col0);
+    const uint4 hq[2] = {make_uint4(hw[0], hw[1], hw[2], hw[3]), make_uint4(hw[4], hw[5], hw[6], hw[7])};
+    const uint4 lq[2] = {make_uint4(lw[0], lw[1], lw[2], lw[3]), make_uint4(lw[4], lw[5], lw[6], lw[7])};
+    stage_row16(stg_ptr, lane, hq);
+    stage_row16(stg_ptr + 2048, lane, lq);
+  } else if (p.C_hi != nullptr) {
+    float4 hq[4], lq[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float4 o = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+      hq[u] = make_float4(tf32_round(o.x), tf32_round(o.y), tf32_round(o.z), tf32_round(o.w));
+      lq[u] = make_float4(o.x - hq[u].x, o.y - hq[u].y, o.z - hq[u].z, o.w - hq[u].w);
+    }
+    stage_row(stg_ptr, lane, hq);
+    stage_row(stg_ptr + 2048, lane, lq);
+  } else {
+    float4 oq[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      oq[u] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+    stage_row(stg_ptr, lane, oq);
+  }
+  fence_proxy_async_smem();  // the generic-proxy writes, visible to the TMA
+  __syncwarp();
+  if (lane == 0) {
+    // rows past M and columns past N are clipped by the store
+    if (p.H_hi != nullptr || p.C_hi != nullptr) {
+      tma_store_2d(tm_hi, stg, col0, row0);
+      tma_store_2d(tm_lo, stg + 2048, col0, row0);
+    } else {
+      tma_store_2d(tm_c, stg, col0, row0);
+    }
+    bulk_commit();
+  }
 }
 
 template <int BN>
@@ -345,7 +442,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int chalf = (warp - 4) >> 2;      // column half of the tile
     const uint32_t stg = base + Sh::STG_OFF + (uint32_t)(warp - 4) * STG_WARP;
     uint8_t *stg_ptr = smem_raw + (stg - raw);
-    const bool split_out = p.C_hi != nullptr;
     int local = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
       const int ab = local & 1;
@@ -362,43 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN + c0), v);
         const int col0 = n0 + c0;
         if (col0 >= p.N || row0 >= p.M) continue;  // warp-uniform
-        epilogue_values(p, row, row_in, valid, col0, v);
-        if (p.vt_hi != nullptr && col0 >= p.vt_col0) {
-          if (row_in) store_vt(p, row, col0, v);
-          continue;
-        }
-        // the previous store of this warp must have read the staging buffers
-        if (lane == 0) bulk_wait_read_all();
-        __syncwarp();
-        if (split_out) {
-          float4 hq[4], lq[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float4 o = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
-            hq[u] = make_float4(tf32_round(o.x), tf32_round(o.y), tf32_round(o.z), tf32_round(o.w));
-            lq[u] = make_float4(o.x - hq[u].x, o.y - hq[u].y, o.z - hq[u].z, o.w - hq[u].w);
-          }
-          stage_row(stg_ptr, lane, hq);
-          stage_row(stg_ptr + 2048, lane, lq);
-        } else {
-          float4 oq[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            oq[u] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
-          stage_row(stg_ptr, lane, oq);
-        }
-        fence_proxy_async_smem();  // the generic-proxy writes, visible to the TMA
-        __syncwarp();
-        if (lane == 0) {
-          // rows past M and columns past N are clipped by the store
-          if (split_out) {
-            tma_store_2d(&tm_c_hi, stg, col0, row0);
-            tma_store_2d(&tm_c_lo, stg + 2048, col0, row0);
-          } else {
-            tma_store_2d(&tm_c, stg, col0, row0);
-          }
-          bulk_commit();
-        }
+        epilogue_chunk_out(p, &tm_c, &tm_c_hi, &tm_c_lo, stg, stg_ptr, lane, row0, valid, col0, v);
       }
       tc_fence_before();
       __syncwarp();
@@ -599,7 +659,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int chalf = (warp - 4) >> 2;
     const uint32_t stg = base + P_STG_OFF + (uint32_t)(warp - 4) * STG_WARP;
     uint8_t *stg_ptr = smem_raw + (stg - raw);
-    const bool split_out = p.C_hi != nullptr;
     const uint32_t acc_empty0 = map_to_cta(acc_empty(0), 0);
     int local = 0;
     for (int tile = pair; tile < ntiles; tile += npairs, ++local) {
@@ -617,41 +676,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * PBN + c0), v);
         const int col0 = n0 + c0;
         if (col0 >= p.N || row0 >= p.M) continue;  // warp-uniform
-        epilogue_values(p, row, row_in, valid, col0, v);
-        if (p.vt_hi != nullptr && col0 >= p.vt_col0) {
-          if (row_in) store_vt(p, row, col0, v);
-          continue;
-        }
-        if (lane == 0) bulk_wait_read_all();
-        __syncwarp();
-        if (split_out) {
-          float4 hq[4], lq[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float4 o = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
-            hq[u] = make_float4(tf32_round(o.x), tf32_round(o.y), tf32_round(o.z), tf32_round(o.w));
-            lq[u] = make_float4(o.x - hq[u].x, o.y - hq[u].y, o.z - hq[u].z, o.w - hq[u].w);
-          }
-          stage_row(stg_ptr, lane, hq);
-          stage_row(stg_ptr + 2048, lane, lq);
-        } else {
-          float4 oq[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            oq[u] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
-          stage_row(stg_ptr, lane, oq);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          if (split_out) {
-            tma_store_2d(&tm_c_hi, stg, col0, row0);
-            tma_store_2d(&tm_c_lo, stg + 2048, col0, row0);
-          } else {
-            tma_store_2d(&tm_c, stg, col0, row0);
-          }
-          bulk_commit();
-        }
+        epilogue_chunk_out(p, &tm_c, &tm_c_hi, &tm_c_lo, stg, stg_ptr, lane, row0, valid, col0, v);
       }
       tc_fence_before();
       __syncwarp();
@@ -713,6 +738,44 @@ int make_tmap(CUtensorMap *tm, const float *ptr, int64_t rows, int64_t cols, int
   return TT_OK;
 }
 
+// 2-D fp16 tensor map over a row-major [rows, cols] matrix of binary16 values,
+// box = 16 columns (32 bytes) x 32 rows, 32-byte swizzle: the epilogue's
+// store box for the fp16 split.
+int make_tmap16(CUtensorMap *tm, const uint16_t *ptr, int64_t rows, int64_t cols) {
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0 || (cols * 2) % 16 != 0)
+    return fail(TT_ERR_INVALID_ARGUMENT, "gemm_tc: fp16 output must be 16-byte aligned, cols % 8 == 0");
+  EncodeTiledFn encode;
+  int rc = encode_fn(&encode);
+  if (rc != TT_OK) return rc;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
+  cuuint32_t box[2] = {16, 32};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t *>(ptr),
+                            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(TT_ERR_CUDA, "cuTensorMapEncodeTiled (fp16) failed with CUresult " + std::to_string((int)r));
+  return TT_OK;
+}
+
+// Store maps of the epilogue (32-row x 16-column boxes): fp32 C, its TF32
+// split, or the fp16 split H (in the hi/lo slots); unused maps repeat `unused`.
+int make_out_maps(const TcGemmParams &p, const CUtensorMap &unused, CUtensorMap *tc,
+                  CUtensorMap *thi, CUtensorMap *tlo) {
+  *tc = unused;
+  *thi = unused;
+  *tlo = unused;
+  int rc = TT_OK;
+  if (p.C != nullptr) rc = make_tmap(tc, p.C, p.M, p.N, p.ldc, 32);
+  else if (p.C_hi != nullptr)
+    (rc = make_tmap(thi, p.C_hi, p.M, p.N, p.ldc, 32)) || (rc = make_tmap(tlo, p.C_lo, p.M, p.N, p.ldc, 32));
+  else if (p.H_hi != nullptr)
+    (rc = make_tmap16(thi, p.H_hi, p.M, p.h_cols)) || (rc = make_tmap16(tlo, p.H_lo, p.M, p.h_cols));
+  return rc;
+}
+
 template <int BN>
 int launch_bn(const TcGemmParams &p, cudaStream_t stream) {
   using Sh = TcShape<BN>;
@@ -723,12 +786,8 @@ int launch_bn(const TcGemmParams &p, cudaStream_t stream) {
       (rc = make_tmap(&tw_hi, p.W_hi, p.N, p.K, p.K, BN)) ||
       (rc = make_tmap(&tw_lo, p.W_lo, p.N, p.K, p.K, BN)))
     return rc;
-  // output maps (32-row x 16-column store boxes); an unused one repeats ta_hi
-  CUtensorMap tc = ta_hi, tc_hi = ta_hi, tc_lo = ta_hi;
-  if (p.C != nullptr && (rc = make_tmap(&tc, p.C, p.M, p.N, p.ldc, 32))) return rc;
-  if (p.C_hi != nullptr && ((rc = make_tmap(&tc_hi, p.C_hi, p.M, p.N, p.ldc, 32)) ||
-                            (rc = make_tmap(&tc_lo, p.C_lo, p.M, p.N, p.ldc, 32))))
-    return rc;
+  CUtensorMap tc, tc_hi, tc_lo;
+  if ((rc = make_out_maps(p, ta_hi, &tc, &tc_hi, &tc_lo))) return rc;
   static int sms = 0;
   static bool attr_set = false;
   if (!attr_set) {
@@ -755,11 +814,8 @@ int launch_pair(const TcGemmParams &p, cudaStream_t stream, int sms) {
       (rc = make_tmap(&tw_hi, p.W_hi, p.N, p.K, p.K, 128)) ||
       (rc = make_tmap(&tw_lo, p.W_lo, p.N, p.K, p.K, 128)))
     return rc;
-  CUtensorMap tc = ta_hi, tc_hi = ta_hi, tc_lo = ta_hi;
-  if (p.C != nullptr && (rc = make_tmap(&tc, p.C, p.M, p.N, p.ldc, 32))) return rc;
-  if (p.C_hi != nullptr && ((rc = make_tmap(&tc_hi, p.C_hi, p.M, p.N, p.ldc, 32)) ||
-                            (rc = make_tmap(&tc_lo, p.C_lo, p.M, p.N, p.ldc, 32))))
-    return rc;
+  CUtensorMap tc, tc_hi, tc_lo;
+  if ((rc = make_out_maps(p, ta_hi, &tc, &tc_hi, &tc_lo))) return rc;
   static bool attr_set = false;
   if (!attr_set) {
     TT_CUDA_TRY(cudaFuncSetAttribute(gemm_tc3_pair_kernel,
@@ -805,9 +861,12 @@ int launch_gemm_tc3(const TcGemmParams &p, cudaStream_t stream) {
   if (p.M <= 0 || p.N <= 0) return TT_OK;
   if (p.K <= 0 || p.K % 4 != 0 || p.N % 4 != 0 || p.ldc % 4 != 0)
     return fail(TT_ERR_UNSUPPORTED, "gemm_tc: K, N and ldc must be multiples of 4");
-  if ((p.C != nullptr) == (p.C_hi != nullptr) || (p.C_hi != nullptr) != (p.C_lo != nullptr))
-    return fail(TT_ERR_UNSUPPORTED, "gemm_tc: exactly one of C and the C_hi/C_lo split");
-  if (p.vt_hi != nullptr && (p.vt_col0 % 16 != 0 || p.head_dim % 16 != 0))
+  if ((p.C != nullptr) + (p.C_hi != nullptr) + (p.H_hi != nullptr) != 1 ||
+      (p.C_hi != nullptr) != (p.C_lo != nullptr) || (p.H_hi != nullptr) != (p.H_lo != nullptr))
+    return fail(TT_ERR_UNSUPPORTED, "gemm_tc: exactly one of C, the C_hi/C_lo split, the H split");
+  if (p.H_hi != nullptr && (p.vt_hi == nullptr || p.h_cols != p.vt_col0 || p.h_cols % 16 != 0))
+    return fail(TT_ERR_UNSUPPORTED, "gemm_tc: the fp16 split covers the columns before v");
+  if (p.vt_hi != nullptr && (p.vt_col0 % 16 != 0 || p.head_dim % 16 != 0 || p.seq_pad % 8 != 0))
     return fail(TT_ERR_UNSUPPORTED, "gemm_tc: transposed value columns need 16-aligned heads");
   // CTA pairs (256 x 256 tiles) cut the L2 -> SM operand traffic by a third
   // and keep N = 256 MMAs; they run when the pair tiles fill at least one wave

@@ -18,11 +18,16 @@ struct TcGemmParams {
   DeviceStatus *status;       // device status word for bounded-wait timeouts
   int M, N, K;
   int epilogue;               // GemmEpilogue
-  // Optional transposed copy of the value columns of a q|k|v projection, for
-  // the tensor-core attention: columns [vt_col0, N) of row r = b*seq + s, head
-  // h, dim d go to vt_{hi,lo}[((b*heads + h)*head_dim + d)*seq_pad + s]
-  // (keys contiguous) instead of C_hi/C_lo.
-  float *vt_hi, *vt_lo;
+  // Operands of the tensor-core attention, written by a q|k|v projection as
+  // fp16 splits (x = hi + lo, binary16 bit patterns):
+  //   columns [0, h_cols) (q and k) to H_hi/H_lo [M, h_cols];
+  //   columns [vt_col0, N) (v) of row r = b*seq + s, head h, dim d transposed to
+  //   vt_{hi,lo}[((b*heads + h)*head_dim + d)*seq_pad + s] (keys contiguous).
+  // A value whose magnitude is beyond the fp16 range latches
+  // TT_ERR_DEVICE_RANGE in the status word.
+  uint16_t *H_hi, *H_lo;
+  int h_cols;
+  uint16_t *vt_hi, *vt_lo;
   int vt_col0, seq, seq_pad, heads, head_dim;
 };
 

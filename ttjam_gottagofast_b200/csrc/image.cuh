@@ -10,9 +10,10 @@
 //
 // Workspace (per call, [T = batch*seq] tokens):
 //   FFMA schedule:        qkv [T,3D] | ctx [T,D] | h [T,F]
-//   tensor-core schedule: qkv [T,3D] (or its TF32 split qkv_hi/qkv_lo when the
-//   attention also runs on tensor cores, head_dim 64) | the TF32 splits of the
-//   GEMM A operands: ln_hi/ln_lo [T,D], ctx_hi/ctx_lo [T,D], h_hi/h_lo [T,F].
+//   tensor-core schedule: qkv [T,3D] (or, when the attention also runs on
+//   tensor cores, head_dim 32 or 64, the fp16 split of q|k qk_hi/qk_lo [T,2D]
+//   and of v transposed vt_hi/vt_lo [B*H, hd, seq_pad]) | the TF32 splits of
+//   the GEMM A operands: ln_hi/ln_lo [T,D], ctx_hi/ctx_lo [T,D], h_hi/h_lo [T,F].
 #pragma once
 
 #include <vector>
@@ -75,7 +76,7 @@ struct ImageLayout {
 };
 
 struct WorkspaceLayout {
-  size_t qkv = 0, ctx = 0, h = 0, qkv_hi = 0, qkv_lo = 0, vt_hi = 0, vt_lo = 0;
+  size_t qkv = 0, ctx = 0, h = 0, qk_hi = 0, qk_lo = 0, vt_hi = 0, vt_lo = 0;
   int seq_pad = 0;  // row stride of the transposed value copy (multiple of 4)
   size_t ln_hi = 0, ln_lo = 0, ctx_hi = 0, ctx_lo = 0, h_hi = 0, h_lo = 0;
   size_t total = 0;
@@ -95,11 +96,12 @@ struct WorkspaceLayout {
     const int hd = cfg.d_model / cfg.num_heads;
     tc_attention = tensor && (hd == 32 || hd == 64);
     if (tc_attention) {
-      // q|k as a TF32 split, and v transposed per (sequence, head) with keys
-      // contiguous, for the tensor-core attention
-      seq_pad = (int)((seq + 3) / 4 * 4);
-      qkv_hi = take(T * 3 * D); qkv_lo = take(T * 3 * D);
-      vt_hi = take((size_t)batch * seq_pad * D); vt_lo = take((size_t)batch * seq_pad * D);
+      // q|k as an fp16 split, and v transposed per (sequence, head) with keys
+      // contiguous (rows of seq_pad fp16 values, a multiple of 16 bytes), for
+      // the tensor-core attention (sizes in floats: two fp16 values per float)
+      seq_pad = (int)((seq + 7) / 8 * 8);
+      qk_hi = take(T * D); qk_lo = take(T * D);
+      vt_hi = take((size_t)batch * seq_pad * D / 2); vt_lo = take((size_t)batch * seq_pad * D / 2);
     } else {
       qkv = take(T * 3 * D);
     }
