@@ -141,10 +141,20 @@ def load_peaks():
         return 6650.0, 1590.0, 1400.0, "fallback"
 
 
-# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
-# dominant kernel kind, from one ncu capture per (workload, kind); the
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) per
+# (workload, kernel kind), from ncu captures of the current kernels; the
 # profiles/ file named beside each entry gives the command and the capture.
-NCU_TRAFFIC = {}
+# E is captured at batch 4 and scaled to batch 64 (activation traffic x 16,
+# weight traffic once), as that file explains.
+NCU_TRAFFIC = {
+    ("B1", "whole_forward"): 1.690112e6,   # profiles/cluster_forward_B1.md
+    ("D", "ffn_out"): 341.537e6,           # profiles/ops_tc_workload_D.md
+    ("D", "attention"): 134.887e6,         # profiles/ops_tc_workload_D.md
+    ("E", "ffn_in"): 6.84982e9,            # profiles/ops_tc_workload_E_batch4.md
+    ("E", "ffn_out"): 5.85110e9,           # profiles/ops_tc_workload_E_batch4.md
+    ("E", "qkv"): 2.40568e9,               # profiles/ops_tc_workload_E_batch4.md
+    ("E", "attention"): 1.55568e9,         # profiles/ops_tc_workload_E_batch4.md
+}
 
 
 def kind_work(kind, cfg, b, s, lens, mask_bytes):
@@ -467,7 +477,8 @@ def run_ours(args, world, rank, local):
             "achieved_fp32_tflops": round(flops / (dom_us * 1e-6) / 1e12, 3),
         }
     roofline.update({
-        "traffic": NCU_TRAFFIC.get((w.name, dom)),
+        "traffic": (NCU_TRAFFIC.get((w.name, dom))
+                    if cfg.batch_size == WORKLOADS[w.name].config.batch_size else None),
         "kernel": f"{dom} ({len(per_kind[dom])} launches, plan {plan})",
         "algorithmic_bytes_per_launch": nbytes,
         "avg_launch_us": round(dom_us, 3),
