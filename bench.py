@@ -478,7 +478,7 @@ def run_ours(args, world, rank, local):
         }
     roofline.update({
         "traffic": (NCU_TRAFFIC.get((w.name, dom))
-                    if cfg.batch_size == WORKLOADS[w.name].config.batch_size else None),
+                    if nb == WORKLOADS[w.name].config.batch_size else None),
         "kernel": f"{dom} ({len(per_kind[dom])} launches, plan {plan})",
         "algorithmic_bytes_per_launch": nbytes,
         "avg_launch_us": round(dom_us, 3),
