@@ -20,8 +20,9 @@ Our arm prints one JSON line with
              of y inside each timed step;
   roofline   the dominant kernel kind (largest share of the timed device
              time, each launch bracketed by CUDA events on its stream through
-             the library's launch probe) against its bound: 3xTF32 tensor
-             (algorithmic fp32 FLOP; peak = measured bf16 / 2 / 3) or HBM
+             the library's launch probe) against its bound: split-precision
+             tensor (algorithmic fp32 FLOP; peak = measured bf16 / 3, three
+             fp16 MMAs per fp32 product) or HBM
              (algorithmic bytes floor); `kernels` lists every kind's share;
   cpu_baseline  the reference forward (oracle restatement, torch eager fp32)
              on this host's CPU cores, rank 0 at N=1 only.
@@ -455,7 +456,7 @@ def run_ours(args, world, rank, local):
         flops, nbytes = work
     long_region = sum(step_ms) > 1000.0
     tc_peak_bf16 = tc_sust if long_region else tc_burst
-    tc_peak = tc_peak_bf16 / 2.0 / 3.0  # TF32 MMA at half bf16's rate, 3 MMAs per product
+    tc_peak = tc_peak_bf16 / 3.0  # fp16-split operands: 3 kind::f16 MMAs (bf16 rate) per product
     on_tensor = plan == "ops_tc3xtf32" and dom != "whole_forward" and flops > 0
     if on_tensor and flops / (tc_peak * 1e12) >= nbytes / (hbm_peak * 1e9):
         achieved = flops / (dom_us * 1e-6) / 1e12
@@ -463,8 +464,9 @@ def run_ours(args, world, rank, local):
             "bound": "tensor", "achieved": round(achieved, 2), "peak": round(tc_peak, 1),
             "unit": "TFLOP/s", "frac": round(achieved / tc_peak, 4),
             "peak_source": (f"{peak_kind}: bf16 {'sustained' if long_region else 'burst'} "
-                            f"{tc_peak_bf16} TFLOP/s (MEASURED_PEAKS.json) / 2 (TF32 MMA rate) "
-                            "/ 3 (3xTF32: 3 MMAs per fp32 product), of measured"),
+                            f"{tc_peak_bf16} TFLOP/s (MEASURED_PEAKS.json) / 3 (fp16-split "
+                            "operands: 3 fp16 MMAs, at the bf16 rate, per fp32 product), "
+                            "of measured"),
             "algorithmic_flops_per_launch": flops,
         }
     else:

@@ -64,10 +64,11 @@ def test_image_and_workspace_sizes(lib):
     c = _cfg()
     n = lib.tt_image_bytes(ctypes.byref(c))
     per_layer = (4 * 128 * 128 + 2 * 128 * 128) * 4
-    # fp32 weights plus their TF32 hi/lo split for the tensor-core schedule
-    assert 3 * 4 * per_layer < n < 3 * 4 * per_layer + 64 * 1024
-    odd = _cfg(d=30, h=3, f=30)   # no TF32 split when rows are not 16-byte multiples
-    assert lib.tt_image_bytes(ctypes.byref(odd)) < 3 * 4 * (4 * 30 * 30 + 2 * 30 * 30) * 4
+    # fp32 weights plus their fp16 hi/lo split (same bytes again) for the
+    # tensor-core schedule
+    assert 2 * 4 * per_layer < n < 2 * 4 * per_layer + 64 * 1024
+    odd = _cfg(d=30, h=3, f=30)   # no split when fp16 rows are not 16-byte multiples
+    assert lib.tt_image_bytes(ctypes.byref(odd)) < 2 * 4 * (4 * 30 * 30 + 2 * 30 * 30) * 4
     ws = lib.tt_workspace_bytes(ctypes.byref(c), 4, 16)
     assert ws >= 64 * (3 * 128 + 128 + 128) * 4
     assert lib.tt_image_bytes(ctypes.byref(_cfg(h=3))) == 0

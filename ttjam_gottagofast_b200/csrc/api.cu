@@ -18,22 +18,48 @@ void set_last_error(const std::string &msg) { g_last_error = msg; }
 
 namespace {
 
-__global__ void tf32_split_kernel(const float *__restrict__ src, float *__restrict__ hi,
-                                  float *__restrict__ lo, int64_t n) {
+// Largest |w| of a weight matrix, as float bits (non-negative floats order
+// like their bit patterns), into *out (zeroed by the caller).
+__global__ void absmax_kernel(const float *__restrict__ src, int64_t n, unsigned *out) {
+  float m = 0.f;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const float v = src[i];
-    const float h = tf32_round(v);
-    hi[i] = h;
-    lo[i] = v - h;
-  }
+       i += (int64_t)gridDim.x * blockDim.x)
+    m = fmaxf(m, fabsf(src[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0 && m > 0.f) atomicMax(out, __float_as_uint(m));
 }
 
-int split_tf32(const float *src, float *hi, float *lo, int64_t n, cudaStream_t stream) {
+// fp16 split of w * 2^e with e chosen so the largest |w| * 2^e lies in
+// [2^14, 2^15): the pieces keep their full relative precision and stay
+// finite. Writes 2^-e (the GEMM's accumulator scale) to *acc_scale.
+__global__ void weight_split_kernel(const float *__restrict__ src, uint16_t *__restrict__ hi,
+                                    uint16_t *__restrict__ lo, int64_t n,
+                                    const unsigned *__restrict__ maxbits,
+                                    float *__restrict__ acc_scale) {
+  const float mx = __uint_as_float(*maxbits);
+  int e = 0;
+  if (mx > 0.f && isfinite(mx)) {
+    int ex;
+    frexpf(mx, &ex);  // mx = f * 2^ex, f in [0.5, 1)
+    e = min(max(15 - ex, -100), 100);
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) *acc_scale = ldexpf(1.0f, -e);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    f16_split(ldexpf(src[i], e), hi[i], lo[i]);
+}
+
+int split_weight(const float *src, uint16_t *hi, uint16_t *lo, int64_t n, unsigned *maxbits,
+                 float *acc_scale, cudaStream_t stream) {
   const int threads = 256;
   const int64_t blocks = std::min<int64_t>(ceil_div(n, threads), 148 * 8);
-  tf32_split_kernel<<<(unsigned)blocks, threads, 0, stream>>>(src, hi, lo, n);
-  TT_LAUNCH_CHECK("tf32_split");
+  TT_CUDA_TRY(cudaMemsetAsync(maxbits, 0, sizeof(unsigned), stream));
+  absmax_kernel<<<(unsigned)blocks, threads, 0, stream>>>(src, n, maxbits);
+  TT_LAUNCH_CHECK("absmax");
+  weight_split_kernel<<<(unsigned)blocks, threads, 0, stream>>>(src, hi, lo, n, maxbits,
+                                                                 acc_scale);
+  TT_LAUNCH_CHECK("weight_split");
   return TT_OK;
 }
 
@@ -193,10 +219,10 @@ int forward_ops(const tt_config &cfg, const ImageLayout &L, const char *image, c
   });
 }
 
-// Per-op schedule with 3xTF32 tensor-core GEMMs (d_model >= 512): per layer
-// LN1 -> TF32 split, q|k|v GEMM, attention (writes the split context),
-// out_proj GEMM + residual, LN2 -> split, ffn_in GEMM + GELU (writes the split
-// hidden), ffn_out GEMM + residual; then the final LayerNorm.
+// Per-op schedule with split-precision tensor-core GEMMs: per layer LN1 ->
+// fp16 split, q|k|v GEMM, attention (writes the split context), out_proj GEMM
+// + residual, LN2 -> split, ffn_in GEMM + GELU (writes the split hidden),
+// ffn_out GEMM + residual; then the final LayerNorm.
 int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image, const float *x,
                    const uint8_t *mask, int64_t batch, int64_t seq, float *y,
                    const WorkspaceLayout &W, char *ws, cudaStream_t stream) {
@@ -207,14 +233,16 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
   auto WH = [&](size_t off) { return reinterpret_cast<uint16_t *>(ws + off); };
   float *qkv = WS(W.qkv);
   uint16_t *qk_hi = WH(W.qk_hi), *qk_lo = WH(W.qk_lo), *vt_hi = WH(W.vt_hi), *vt_lo = WH(W.vt_lo);
-  float *ln_hi = WS(W.ln_hi), *ln_lo = WS(W.ln_lo);
-  float *ctx_hi = WS(W.ctx_hi), *ctx_lo = WS(W.ctx_lo);
-  float *h_hi = WS(W.h_hi), *h_lo = WS(W.h_lo);
+  uint16_t *ln_hi = WH(W.ln_hi), *ln_lo = WH(W.ln_lo);
+  uint16_t *ctx_hi = WH(W.ctx_hi), *ctx_lo = WH(W.ctx_lo);
+  uint16_t *h_hi = WH(W.h_hi), *h_lo = WH(W.h_lo);
   DeviceStatus *status = reinterpret_cast<DeviceStatus *>(const_cast<char *>(image) + L.status);
   const float eps = 1e-5f;
   for (int l = 0; l < cfg.num_layers; ++l) {
     const LayerOffsets &o = L.layer[l];
     auto P = [&](size_t off) { return reinterpret_cast<const float *>(image + off); };
+    auto PH = [&](size_t off) { return reinterpret_cast<const uint16_t *>(image + off); };
+    const float *wsc = P(o.wscale);  // accumulator scales of the four GEMMs
     const float *xin = (l == 0) ? x : y;
     int rc;
     if ((rc = timed_launch(TT_KERNEL_LAYERNORM, stream, [&] {
@@ -223,7 +251,8 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
          })))
       return rc;
     TcGemmParams g{};
-    g.A_hi = ln_hi; g.A_lo = ln_lo; g.lda = D; g.W_hi = P(o.wqkv_hi); g.W_lo = P(o.wqkv_lo);
+    g.A_hi = ln_hi; g.A_lo = ln_lo; g.lda = D; g.W_hi = PH(o.wqkv_hi); g.W_lo = PH(o.wqkv_lo);
+    g.acc_scale = wsc;
     g.bias = P(o.bqkv); g.ldc = 3LL * D; g.status = status;
     g.M = (int)T; g.N = 3 * D; g.K = D; g.epilogue = EPI_BIAS;
     if (W.tc_attention) {
@@ -255,7 +284,8 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
         return rc;
     }
     TcGemmParams go{};
-    go.A_hi = ctx_hi; go.A_lo = ctx_lo; go.lda = D; go.W_hi = P(o.wo_hi); go.W_lo = P(o.wo_lo);
+    go.A_hi = ctx_hi; go.A_lo = ctx_lo; go.lda = D; go.W_hi = PH(o.wo_hi); go.W_lo = PH(o.wo_lo);
+    go.acc_scale = wsc + 1;
     go.bias = P(o.bo); go.R = xin; go.C = y; go.ldc = D; go.row_mask = mask; go.status = status;
     go.M = (int)T; go.N = D; go.K = D; go.epilogue = EPI_BIAS_RESIDUAL;
     if ((rc = timed_launch(TT_KERNEL_OUT_PROJ, stream, [&] { return launch_gemm_tc3(go, stream); })))
@@ -266,13 +296,16 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
          })))
       return rc;
     TcGemmParams g1{};
-    g1.A_hi = ln_hi; g1.A_lo = ln_lo; g1.lda = D; g1.W_hi = P(o.w1_hi); g1.W_lo = P(o.w1_lo);
-    g1.bias = P(o.b1); g1.C_hi = h_hi; g1.C_lo = h_lo; g1.ldc = F; g1.status = status;
+    g1.A_hi = ln_hi; g1.A_lo = ln_lo; g1.lda = D; g1.W_hi = PH(o.w1_hi); g1.W_lo = PH(o.w1_lo);
+    g1.acc_scale = wsc + 2;
+    g1.bias = P(o.b1); g1.H_hi = h_hi; g1.H_lo = h_lo; g1.h_cols = F; g1.ldc = F;
+    g1.status = status;
     g1.M = (int)T; g1.N = F; g1.K = D; g1.epilogue = EPI_BIAS_GELU;
     if ((rc = timed_launch(TT_KERNEL_FFN_IN, stream, [&] { return launch_gemm_tc3(g1, stream); })))
       return rc;
     TcGemmParams g2{};
-    g2.A_hi = h_hi; g2.A_lo = h_lo; g2.lda = F; g2.W_hi = P(o.w2_hi); g2.W_lo = P(o.w2_lo);
+    g2.A_hi = h_hi; g2.A_lo = h_lo; g2.lda = F; g2.W_hi = PH(o.w2_hi); g2.W_lo = PH(o.w2_lo);
+    g2.acc_scale = wsc + 3;
     g2.bias = P(o.b2); g2.R = y; g2.C = y; g2.ldc = D; g2.row_mask = mask; g2.status = status;
     g2.M = (int)T; g2.N = D; g2.K = F; g2.epilogue = EPI_BIAS_RESIDUAL;
     if ((rc = timed_launch(TT_KERNEL_FFN_OUT, stream, [&] { return launch_gemm_tc3(g2, stream); })))
@@ -338,10 +371,13 @@ int tt_pack_image(const tt_config *cfg, const tt_layer_params *layers,
       return rc;
     if (L.tensor) {
       auto F_ = [&](size_t off) { return reinterpret_cast<float *>(img + off); };
-      if ((rc = split_tf32(F_(o.wqkv), F_(o.wqkv_hi), F_(o.wqkv_lo), 3 * D * D, stream)) ||
-          (rc = split_tf32(F_(o.wo), F_(o.wo_hi), F_(o.wo_lo), D * D, stream)) ||
-          (rc = split_tf32(F_(o.w1), F_(o.w1_hi), F_(o.w1_lo), F * D, stream)) ||
-          (rc = split_tf32(F_(o.w2), F_(o.w2_hi), F_(o.w2_lo), D * F, stream)))
+      auto H_ = [&](size_t off) { return reinterpret_cast<uint16_t *>(img + off); };
+      float *sc = F_(o.wscale);
+      unsigned *mx = reinterpret_cast<unsigned *>(sc + 4);
+      if ((rc = split_weight(F_(o.wqkv), H_(o.wqkv_hi), H_(o.wqkv_lo), 3 * D * D, mx, sc, stream)) ||
+          (rc = split_weight(F_(o.wo), H_(o.wo_hi), H_(o.wo_lo), D * D, mx + 1, sc + 1, stream)) ||
+          (rc = split_weight(F_(o.w1), H_(o.w1_hi), H_(o.w1_lo), F * D, mx + 2, sc + 2, stream)) ||
+          (rc = split_weight(F_(o.w2), H_(o.w2_hi), H_(o.w2_lo), D * F, mx + 3, sc + 3, stream)))
         return rc;
     }
   }

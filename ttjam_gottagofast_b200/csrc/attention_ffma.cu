@@ -167,9 +167,8 @@ __global__ void __launch_bounds__(kThreads) attention_ffma_kernel(AttentionParam
       const float v = o[d] * inv;
       if (p.ctx != nullptr) p.ctx[tok * D + (int64_t)h * hd + part * P + d] = v;
       if (p.ctx_hi != nullptr) {
-        const float hv = tf32_round(v);
-        p.ctx_hi[tok * D + (int64_t)h * hd + part * P + d] = hv;
-        p.ctx_lo[tok * D + (int64_t)h * hd + part * P + d] = v - hv;
+        f16_split(v, p.ctx_hi[tok * D + (int64_t)h * hd + part * P + d],
+                  p.ctx_lo[tok * D + (int64_t)h * hd + part * P + d]);
       }
     }
   }

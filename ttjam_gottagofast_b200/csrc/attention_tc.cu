@@ -507,7 +507,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     s_rowsum[kh][t] = l;
     asm volatile("bar.sync 1, 256;" ::: "memory");
     l += s_rowsum[kh ^ 1][t];
-    // context = O / l (this thread's HD/2 dims), written as a TF32 split
+    // context = O / l (this thread's HD/2 dims), written as an fp16 split (the
+    // out_proj GEMM's A operand)
     // the last P.V (the tensor pipe runs the MMAs in order, so all of them)
     mbar_wait(o_done((nkv - 1) & 1), ((nkv - 1) >> 1) & 1, p.status, 0x4700);
     fence_after();
@@ -519,17 +520,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld16(lane_base + T_O + dim_off + c, ov);
       tmem_wait_ld();
       if (row_in) {
+        uint32_t hw[8], lw[8];
 #pragma unroll
-        for (int i = 0; i < 16; i += 4) {
-          float4 hv, lv;
-          const float v0 = ov[i] * inv, v1 = ov[i + 1] * inv, v2 = ov[i + 2] * inv, v3 = ov[i + 3] * inv;
-          hv.x = tf32_round(v0); lv.x = v0 - hv.x;
-          hv.y = tf32_round(v1); lv.y = v1 - hv.y;
-          hv.z = tf32_round(v2); lv.z = v2 - hv.z;
-          hv.w = tf32_round(v3); lv.w = v3 - hv.w;
-          *reinterpret_cast<float4 *>(p.ctx_hi + off + c + i) = hv;
-          *reinterpret_cast<float4 *>(p.ctx_lo + off + c + i) = lv;
-        }
+        for (int i = 0; i < 8; ++i) split_pair(ov[2 * i] * inv, ov[2 * i + 1] * inv, hw[i], lw[i]);
+        uint4 *dh = reinterpret_cast<uint4 *>(p.ctx_hi + off + c);
+        uint4 *dl = reinterpret_cast<uint4 *>(p.ctx_lo + off + c);
+        dh[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        dh[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+        dl[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        dl[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
       }
     }
   }

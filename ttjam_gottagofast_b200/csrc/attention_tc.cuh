@@ -9,7 +9,7 @@ namespace tt {
 struct AttentionTcParams {
   const uint16_t *qk_hi, *qk_lo;  // [B*S, 2D] fp16 split of q | k (binary16 bits)
   const uint16_t *vt_hi, *vt_lo;  // [B*H, head_dim, seq_pad] fp16 split of v, keys contiguous
-  float *ctx_hi, *ctx_lo;         // [B*S, D] TF32 split of the context
+  uint16_t *ctx_hi, *ctx_lo;      // [B*S, D] fp16 split of the context
   const uint8_t *mask;            // [B, S] or null
   DeviceStatus *status;
   int64_t batch;

@@ -1,42 +1,52 @@
-// 3xTF32 tensor-core GEMM on sm_100a (tcgen05 + TMA + TMEM):
+// Split-precision tensor-core GEMM on sm_100a (tcgen05 + TMA + TMEM):
 //   C[M,N] = epilogue(A[M,K] . W[N,K]^T) in fp32 accuracy.
 //
-// Split-precision product (Ootomo & Yokota 2022, "Recovering single precision
-// accuracy from Tensor Cores while surpassing the FP32 theoretical peak
-// performance"): every operand arrives as a TF32 pair x = x_hi + x_lo (x_hi =
-// x rounded to TF32, x_lo = x - x_hi, exact in fp32), and
+// Split-precision product (as in Ootomo & Yokota 2022, "Recovering single
+// precision accuracy from Tensor Cores while surpassing the FP32 theoretical
+// peak performance", here with binary16 pieces): every operand arrives as a
+// pair x = x_hi + x_lo of fp16 values (x_hi = x rounded to fp16, x_lo = the
+// rest rounded to fp16: about 22 significant bits, as a TF32 pair), and
 //   A.W^T ~= A_hi.W_hi^T + A_hi.W_lo^T + A_lo.W_hi^T
 // accumulated in fp32 in tensor memory; the dropped A_lo.W_lo^T term is about
-// 2^-22 of the product. Plain TF32 fails the reference's accuracy gate
-// (max abs error 2e-3..9e-3 on the reference's own TF32 kernels); this keeps
-// fp32-level error.
+// 2^-22 of the product. A plain single-pass 16-bit or TF32 product fails the
+// reference's accuracy gate (max abs error 2e-3..9e-3 on the reference's own
+// TF32 kernels); this keeps fp32-level error. fp16 pieces (tcgen05
+// kind::f16) do twice the multiply-adds of TF32 pieces per MMA cycle and move
+// half the bytes. Weights are scaled by a power of two at pack time so their
+// largest magnitude sits just below 2^15 (the pieces then keep full relative
+// precision); acc_scale undoes it exactly. Activations are used as they are
+// (LayerNorm outputs, attention contexts and GELU outputs stay far inside the
+// fp16 range; a value beyond it gives an infinite piece and a non-finite
+// output, and the producers latch TT_ERR_DEVICE_RANGE).
 //
-// Used for the per-token projections when d_model >= 512: q|k|v
+// Used for the per-token projections of the tensor-core schedule: q|k|v
 // (torch_transformer_benchmark.py:93-95), out_proj + residual (:118-121, :140),
 // ffn_in + GELU and ffn_out + residual (:141-144).
 //
-// Persistent kernel, one CTA per SM looping over 128 x BN output tiles
-// (BN = 256, or 128 when N is small), 384 threads, warp-specialised:
-//   warp 0    TMA producer: per 16-wide k-block 4 tiles (A_hi, A_lo, W_hi,
-//             W_lo; 64-byte swizzle) into a 4-stage ring that runs on across
-//             tiles;
+// Two persistent kernels, 384 threads, warp-specialised:
+//   warp 0    TMA producer: per 32-wide k-block the operand tiles (A_hi, A_lo,
+//             W_hi, W_lo; rows of 64 bytes, 64-byte swizzle) into a ring that
+//             runs on across tiles;
 //   warp 1    MMA issuer (one thread): per k-block 2 k-steps x 3 products of
-//             tcgen05.mma.cta_group::1.kind::tf32 M128 x BN x K8 into one of
-//             two tensor-memory accumulators; tcgen05.commit frees the stage /
-//             hands the accumulator to the epilogue;
-//   warp 2    allocates / frees the 2 x BN tensor-memory columns;
+//             tcgen05.mma kind::f16 (K 16) into one of two tensor-memory
+//             accumulators; tcgen05.commit frees the stage / hands the
+//             accumulator to the epilogue;
+//   warp 2    allocates / frees the tensor-memory columns;
 //   warps 4-11 epilogue: warp w reads tensor-memory lane quarter w%4 (tile row
 //             = lane) and column half (w-4)/4 with tcgen05.ld 32x32b, applies
-//             bias, GELU / residual / padded-row zeroing, then releases the
-//             accumulator -- so the epilogue of one tile overlaps the main
-//             loop of the next. Outputs leave through shared memory: each warp
-//             writes its 32-row x 16-column chunk (fp32, or the TF32 split) to
-//             a staging buffer in the 64-byte swizzle pattern (conflict-free)
-//             and one lane issues a TMA tensor store, which writes whole lines
-//             (a lane-per-row st.global would be 32 partial-line writes per
-//             instruction).
-// With TF32 operands an M128 x N128 MMA reads 8 KB of shared memory per 64
-// cycles, the whole shared-memory bandwidth; N = 256 halves that per FLOP.
+//             acc_scale, bias, GELU / residual / padded-row zeroing, then
+//             releases the accumulator -- so the epilogue of one tile overlaps
+//             the main loop of the next. Outputs leave through shared memory:
+//             each warp writes its 32-row x 16-column chunk (fp32, or the fp16
+//             split) to a staging buffer in the TMA swizzle pattern
+//             (conflict-free) and one lane issues a TMA tensor store, which
+//             writes whole lines (a lane-per-row st.global would be 32
+//             partial-line writes per instruction).
+// The single-CTA kernel (gemm_tc3_kernel) computes 128 x BN tiles (BN 256, or
+// 128 when N is small); the CTA-pair kernel (gemm_tc3_pair_kernel, below)
+// computes 256 x 256 tiles on two SMs. At N = 256 an MMA reads 12 KB of
+// shared memory per 128 cycles; N = 128 would need the whole shared-memory
+// bandwidth.
 // Every mbarrier wait is bounded; a wait that gives up latches
 // TT_ERR_DEVICE_TIMEOUT and the kernel still frees its tensor memory and
 // returns. No TMA load here uses cluster multicast.
@@ -47,16 +57,16 @@
 namespace tt {
 namespace {
 
-constexpr int BM = 128, BK = 16, STAGES = 4;
+constexpr int BM = 128, BK = 32, STAGES = 4;  // BK in fp16 elements (64-byte rows)
 constexpr int kThreads = 384;
 constexpr int kEpiWarps = 8;
-constexpr uint32_t TILE_A = BM * BK * 4;               // 8 KB
+constexpr uint32_t TILE_A = BM * BK * 2;               // 8 KB
 
 constexpr uint32_t STG_WARP = 2 * 2048;               // per epilogue warp: two 32x16 fp32 chunks
 
 template <int BN>
 struct TcShape {
-  static constexpr uint32_t TILE_W = BN * BK * 4;                       // 16 KB at BN 256
+  static constexpr uint32_t TILE_W = BN * BK * 2;                       // 16 KB at BN 256
   static constexpr uint32_t STAGE_BYTES = 2 * TILE_A + 2 * TILE_W;      // 48 KB at BN 256
   static constexpr uint32_t TMEM_COLS = 2 * BN;                         // two accumulators
   static constexpr uint32_t STG_OFF = STAGES * STAGE_BYTES;             // output staging
@@ -143,19 +153,19 @@ __device__ __forceinline__ uint64_t umma_desc_sw64(uint32_t saddr) {
   d |= (uint64_t)4 << 61;                 // SWIZZLE_64B
   return d;
 }
-// Instruction descriptor: D fp32, A/B tf32, both K-major, M = 128, N = BN.
+// Instruction descriptor (kind::f16): D fp32, A/B fp16, both K-major, M = 128,
+// N = BN.
 template <int BN>
-constexpr uint32_t idesc_tf32() {
-  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
-         ((uint32_t)(BM >> 4) << 24);
+constexpr uint32_t idesc_f16() {
+  return (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
-                                          uint32_t accum) {
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accum) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(a), "l"(b), "r"(idesc), "r"(accum)
       : "memory");
 }
@@ -189,9 +199,12 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 // Epilogue values of one 16-column chunk of one row: bias, then GELU or the
 // residual with padded-row zeroing. v holds the accumulator values of
 // columns col0..col0+15 (col0 < N, a multiple of 16).
-__device__ __forceinline__ void epilogue_values(const TcGemmParams &p, int row, bool row_in,
-                                                bool valid, int col0, float (&v)[16]) {
+__device__ __forceinline__ void epilogue_values(const TcGemmParams &p, float acc_scale, int row,
+                                                bool row_in, bool valid, int col0,
+                                                float (&v)[16]) {
   const bool full = col0 + 16 <= p.N;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] *= acc_scale;
 #pragma unroll
   for (int j = 0; j < 16; j += 4) {
     float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -215,23 +228,12 @@ __device__ __forceinline__ void epilogue_values(const TcGemmParams &p, int row, 
   }
 }
 
-// fp16 split of x: hi = x rounded to binary16, lo = x - hi rounded to
-// binary16 (bit patterns). |x| beyond the fp16 range latches
-// TT_ERR_DEVICE_RANGE.
-__device__ __forceinline__ uint16_t f16_bits(float x) {
-  uint16_t h;
-  asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(x));
-  return h;
-}
-__device__ __forceinline__ float f16_value(uint16_t h) {
-  float y;
-  asm("cvt.f32.f16 %0, %1;" : "=f"(y) : "h"(h));
-  return y;
-}
-__device__ __forceinline__ void f16_split(float x, uint16_t &hi, uint16_t &lo, bool &range_ok) {
+// fp16 split (f16_split) that also clears range_ok when |x| is beyond the
+// fp16 range.
+__device__ __forceinline__ void f16_split_checked(float x, uint16_t &hi, uint16_t &lo,
+                                                  bool &range_ok) {
   range_ok = range_ok && fabsf(x) <= 65504.f;
-  hi = f16_bits(x);
-  lo = f16_bits(x - f16_value(hi));
+  f16_split(x, hi, lo);
 }
 
 // Value columns of a q|k|v projection for the tensor-core attention: fp16
@@ -249,7 +251,7 @@ __device__ __forceinline__ void store_vt(const TcGemmParams &p, int row, int col
   for (int j = 0; j < 16; ++j) {
     if (!full && col0 + j >= p.N) break;
     uint16_t hi, lo;
-    f16_split(v[j], hi, lo, ok);
+    f16_split_checked(v[j], hi, lo, ok);
     p.vt_hi[base_t + (int64_t)j * p.seq_pad] = hi;
     p.vt_lo[base_t + (int64_t)j * p.seq_pad] = lo;
   }
@@ -277,15 +279,16 @@ __device__ __forceinline__ void stage_row(uint8_t *buf, int lane, const float4 (
 // One 16-column chunk of a warp's 32 rows through the epilogue: values (bias,
 // GELU / residual), then out -- transposed value columns by direct stores,
 // everything else through this warp's staging buffers (stg, two 2 KB halves)
-// and a TMA tensor store: fp32 C, its TF32 split, or the fp16 split H.
+// and a TMA tensor store: fp32 C or the fp16 split H.
 __device__ __forceinline__ void epilogue_chunk_out(const TcGemmParams &p, const CUtensorMap *tm_c,
                                                    const CUtensorMap *tm_hi,
                                                    const CUtensorMap *tm_lo, uint32_t stg,
                                                    uint8_t *stg_ptr, int lane, int row0,
-                                                   bool valid, int col0, float (&v)[16]) {
+                                                   bool valid, int col0, float acc_scale,
+                                                   float (&v)[16]) {
   const int row = row0 + lane;
   const bool row_in = row < p.M;
-  epilogue_values(p, row, row_in, valid, col0, v);
+  epilogue_values(p, acc_scale, row, row_in, valid, col0, v);
   if (p.vt_hi != nullptr && col0 >= p.vt_col0) {
     if (row_in) store_vt(p, row, col0, v);
     return;
@@ -299,8 +302,8 @@ __device__ __forceinline__ void epilogue_chunk_out(const TcGemmParams &p, const 
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       uint16_t h0, l0, h1, l1;
-      f16_split(v[2 * j], h0, l0, ok);
-      f16_split(v[2 * j + 1], h1, l1, ok);
+      f16_split_checked(v[2 * j], h0, l0, ok);
+      f16_split_checked(v[2 * j + 1], h1, l1, ok);
       hw[j] = (uint32_t)h0 | ((uint32_t)h1 << 16);
       lw[j] = (uint32_t)l0 | ((uint32_t)l1 << 16);
     }
@@ -309,16 +312,6 @@ __device__ __forceinline__ void epilogue_chunk_out(const TcGemmParams &p, const 
     const uint4 lq[2] = {make_uint4(lw[0], lw[1], lw[2], lw[3]), make_uint4(lw[4], lw[5], lw[6], lw[7])};
     stage_row16(stg_ptr, lane, hq);
     stage_row16(stg_ptr + 2048, lane, lq);
-  } else if (p.C_hi != nullptr) {
-    float4 hq[4], lq[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const float4 o = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
-      hq[u] = make_float4(tf32_round(o.x), tf32_round(o.y), tf32_round(o.z), tf32_round(o.w));
-      lq[u] = make_float4(o.x - hq[u].x, o.y - hq[u].y, o.z - hq[u].z, o.w - hq[u].w);
-    }
-    stage_row(stg_ptr, lane, hq);
-    stage_row(stg_ptr + 2048, lane, lq);
   } else {
     float4 oq[4];
 #pragma unroll
@@ -330,7 +323,7 @@ __device__ __forceinline__ void epilogue_chunk_out(const TcGemmParams &p, const 
   __syncwarp();
   if (lane == 0) {
     // rows past M and columns past N are clipped by the store
-    if (p.H_hi != nullptr || p.C_hi != nullptr) {
+    if (p.H_hi != nullptr) {
       tma_store_2d(tm_hi, stg, col0, row0);
       tma_store_2d(tm_lo, stg + 2048, col0, row0);
     } else {
@@ -351,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tm_c_lo, const TcGemmParams p) {
   using Sh = TcShape<BN>;
   constexpr uint32_t TILE_W = Sh::TILE_W, STAGE_BYTES = Sh::STAGE_BYTES;
-  constexpr uint32_t IDESC = idesc_tf32<BN>();
+  constexpr uint32_t IDESC = idesc_f16<BN>();
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -426,11 +419,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t w_hi = umma_desc_sw64(st + 2 * TILE_A);
         const uint64_t w_lo = umma_desc_sw64(st + 2 * TILE_A + TILE_W);
 #pragma unroll
-        for (int k = 0; k < BK / 8; ++k) {  // K = 8 tf32 = 32 bytes per MMA
+        for (int k = 0; k < BK / 16; ++k) {  // K = 16 fp16 = 32 bytes per MMA
           const uint64_t ko = (uint64_t)(k * 2);
-          umma_tf32(acc, a_hi + ko, w_hi + ko, IDESC, (kb | k) != 0);
-          umma_tf32(acc, a_hi + ko, w_lo + ko, IDESC, 1);
-          umma_tf32(acc, a_lo + ko, w_hi + ko, IDESC, 1);
+          umma_f16(acc, a_hi + ko, w_hi + ko, IDESC, (kb | k) != 0);
+          umma_f16(acc, a_hi + ko, w_lo + ko, IDESC, 1);
+          umma_f16(acc, a_lo + ko, w_hi + ko, IDESC, 1);
         }
         umma_commit(empty_bar(s));  // stage s is free once these MMAs have read it
       }
@@ -442,6 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int chalf = (warp - 4) >> 2;      // column half of the tile
     const uint32_t stg = base + Sh::STG_OFF + (uint32_t)(warp - 4) * STG_WARP;
     uint8_t *stg_ptr = smem_raw + (stg - raw);
+    const float acc_scale = *p.acc_scale;
     int local = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
       const int ab = local & 1;
@@ -458,7 +452,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN + c0), v);
         const int col0 = n0 + c0;
         if (col0 >= p.N || row0 >= p.M) continue;  // warp-uniform
-        epilogue_chunk_out(p, &tm_c, &tm_c_hi, &tm_c_lo, stg, stg_ptr, lane, row0, valid, col0, v);
+        epilogue_chunk_out(p, &tm_c, &tm_c_hi, &tm_c_lo, stg, stg_ptr, lane, row0, valid, col0,
+                           acc_scale, v);
       }
       tc_fence_before();
       __syncwarp();
@@ -493,14 +488,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 // multicast.
 constexpr int PSTAGES = 6;
 constexpr int PBN = 256;                                    // pair tile N (128 per CTA in smem)
-constexpr uint32_t P_TILE = 128 * BK * 4;                   // 8 KB: A rows or W half rows
+constexpr uint32_t P_TILE = 128 * BK * 2;                   // 8 KB: A rows or W half rows
 constexpr uint32_t P_STAGE = 4 * P_TILE;                    // A_hi, A_lo, W_hi half, W_lo half
 constexpr uint32_t P_STG_OFF = PSTAGES * P_STAGE;
 constexpr uint32_t P_BAR_OFF = P_STG_OFF + kEpiWarps * STG_WARP;
 constexpr size_t P_SMEM = (size_t)P_BAR_OFF + 256 + 1024;
 constexpr uint32_t P_TMEM_COLS = 2 * PBN;                   // two 256-column accumulators
-constexpr uint32_t P_IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(PBN >> 3) << 17) |
-                             ((uint32_t)(256 >> 4) << 24);  // D fp32, A/B tf32 K-major, M 256
+constexpr uint32_t P_IDESC = (1u << 4) | ((uint32_t)(PBN >> 3) << 17) |
+                             ((uint32_t)(256 >> 4) << 24);  // kind::f16: D fp32, A/B fp16 K-major, M 256
 static_assert(P_SMEM <= 227 * 1024, "shared memory");
 static_assert(P_STG_OFF % 1024 == 0, "staging buffers on the swizzle period");
 
@@ -528,12 +523,12 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
       "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar_cluster), "r"(c0), "r"(c1)
       : "memory");
 }
-__device__ __forceinline__ void umma_tf32_pair(uint32_t tmem_d, uint64_t a, uint64_t b,
-                                               uint32_t idesc, uint32_t accum) {
+__device__ __forceinline__ void umma_f16_pair(uint32_t tmem_d, uint64_t a, uint64_t b,
+                                              uint32_t idesc, uint32_t accum) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(a), "l"(b), "r"(idesc), "r"(accum)
       : "memory");
 }
@@ -641,11 +636,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t w_hi = umma_desc_sw64(st + 2 * P_TILE);
         const uint64_t w_lo = umma_desc_sw64(st + 3 * P_TILE);
 #pragma unroll
-        for (int k = 0; k < BK / 8; ++k) {
+        for (int k = 0; k < BK / 16; ++k) {
           const uint64_t ko = (uint64_t)(k * 2);
-          umma_tf32_pair(acc, a_hi + ko, w_hi + ko, P_IDESC, (kb | k) != 0);
-          umma_tf32_pair(acc, a_hi + ko, w_lo + ko, P_IDESC, 1);
-          umma_tf32_pair(acc, a_lo + ko, w_hi + ko, P_IDESC, 1);
+          umma_f16_pair(acc, a_hi + ko, w_hi + ko, P_IDESC, (kb | k) != 0);
+          umma_f16_pair(acc, a_hi + ko, w_lo + ko, P_IDESC, 1);
+          umma_f16_pair(acc, a_lo + ko, w_hi + ko, P_IDESC, 1);
         }
         umma_commit_pair(map_to_cta(empty_bar(s), 0));  // stage s free in both CTAs
         umma_commit_pair(peer_empty0 + 8u * s);
@@ -659,6 +654,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int chalf = (warp - 4) >> 2;
     const uint32_t stg = base + P_STG_OFF + (uint32_t)(warp - 4) * STG_WARP;
     uint8_t *stg_ptr = smem_raw + (stg - raw);
+    const float acc_scale = *p.acc_scale;
     const uint32_t acc_empty0 = map_to_cta(acc_empty(0), 0);
     int local = 0;
     for (int tile = pair; tile < ntiles; tile += npairs, ++local) {
@@ -676,7 +672,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * PBN + c0), v);
         const int col0 = n0 + c0;
         if (col0 >= p.N || row0 >= p.M) continue;  // warp-uniform
-        epilogue_chunk_out(p, &tm_c, &tm_c_hi, &tm_c_lo, stg, stg_ptr, lane, row0, valid, col0, v);
+        epilogue_chunk_out(p, &tm_c, &tm_c_hi, &tm_c_lo, stg, stg_ptr, lane, row0, valid, col0,
+                           acc_scale, v);
       }
       tc_fence_before();
       __syncwarp();
@@ -715,64 +712,56 @@ int encode_fn(EncodeTiledFn *out) {
   return TT_OK;
 }
 
-// 2-D fp32 tensor map over a row-major [rows, cols] matrix (leading dimension
-// ld floats), box = 16 columns (64 bytes) x box_rows rows, 64-byte swizzle,
-// zero fill outside the matrix.
-int make_tmap(CUtensorMap *tm, const float *ptr, int64_t rows, int64_t cols, int64_t ld,
-              int box_rows) {
-  if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0 || (ld * 4) % 16 != 0)
-    return fail(TT_ERR_INVALID_ARGUMENT, "gemm_tc: operands must be 16-byte aligned with ld % 4 == 0");
+// 2-D tensor map over a row-major [rows, cols] matrix (leading dimension ld
+// elements of elem_bytes), box = box_cols x box_rows, zero fill outside the
+// matrix.
+int make_tmap_any(CUtensorMap *tm, const void *ptr, CUtensorMapDataType dtype, int elem_bytes,
+                  int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows,
+                  CUtensorMapSwizzle swizzle) {
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0 || (ld * elem_bytes) % 16 != 0)
+    return fail(TT_ERR_INVALID_ARGUMENT,
+                "gemm_tc: matrices must be 16-byte aligned with 16-byte rows");
   EncodeTiledFn encode;
   int rc = encode_fn(&encode);
   if (rc != TT_OK) return rc;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * elem_bytes)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(ptr), dims,
-                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                            CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUresult r = encode(tm, dtype, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(TT_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string((int)r));
   return TT_OK;
 }
 
-// 2-D fp16 tensor map over a row-major [rows, cols] matrix of binary16 values,
-// box = 16 columns (32 bytes) x 32 rows, 32-byte swizzle: the epilogue's
-// store box for the fp16 split.
-int make_tmap16(CUtensorMap *tm, const uint16_t *ptr, int64_t rows, int64_t cols) {
-  if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0 || (cols * 2) % 16 != 0)
-    return fail(TT_ERR_INVALID_ARGUMENT, "gemm_tc: fp16 output must be 16-byte aligned, cols % 8 == 0");
-  EncodeTiledFn encode;
-  int rc = encode_fn(&encode);
-  if (rc != TT_OK) return rc;
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
-  cuuint32_t box[2] = {16, 32};
-  cuuint32_t estr[2] = {1, 1};
-  const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t *>(ptr),
-                            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                            CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return fail(TT_ERR_CUDA, "cuTensorMapEncodeTiled (fp16) failed with CUresult " + std::to_string((int)r));
-  return TT_OK;
+// Operand map: fp16 [rows, K], box = BK elements (64 bytes) x box_rows rows,
+// 64-byte swizzle (the UMMA K-major layout of the descriptors above).
+int make_operand_map(CUtensorMap *tm, const uint16_t *ptr, int64_t rows, int64_t cols, int64_t ld,
+                     int box_rows) {
+  return make_tmap_any(tm, ptr, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, rows, cols, ld, BK, box_rows,
+                       CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
-// Store maps of the epilogue (32-row x 16-column boxes): fp32 C, its TF32
-// split, or the fp16 split H (in the hi/lo slots); unused maps repeat `unused`.
+// Store maps of the epilogue (32-row x 16-column boxes): fp32 C (64-byte
+// rows, 64-byte swizzle) or the fp16 split H (32-byte rows, 32-byte swizzle,
+// in the hi/lo slots); unused maps repeat `unused`.
 int make_out_maps(const TcGemmParams &p, const CUtensorMap &unused, CUtensorMap *tc,
                   CUtensorMap *thi, CUtensorMap *tlo) {
   *tc = unused;
   *thi = unused;
   *tlo = unused;
   int rc = TT_OK;
-  if (p.C != nullptr) rc = make_tmap(tc, p.C, p.M, p.N, p.ldc, 32);
-  else if (p.C_hi != nullptr)
-    (rc = make_tmap(thi, p.C_hi, p.M, p.N, p.ldc, 32)) || (rc = make_tmap(tlo, p.C_lo, p.M, p.N, p.ldc, 32));
-  else if (p.H_hi != nullptr)
-    (rc = make_tmap16(thi, p.H_hi, p.M, p.h_cols)) || (rc = make_tmap16(tlo, p.H_lo, p.M, p.h_cols));
+  if (p.C != nullptr) {
+    rc = make_tmap_any(tc, p.C, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.M, p.N, p.ldc, 16, 32,
+                       CU_TENSOR_MAP_SWIZZLE_64B);
+  } else if (p.H_hi != nullptr) {
+    (rc = make_tmap_any(thi, p.H_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.M, p.h_cols, p.h_cols,
+                        16, 32, CU_TENSOR_MAP_SWIZZLE_32B)) ||
+        (rc = make_tmap_any(tlo, p.H_lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.M, p.h_cols,
+                            p.h_cols, 16, 32, CU_TENSOR_MAP_SWIZZLE_32B));
+  }
   return rc;
 }
 
@@ -781,10 +770,10 @@ int launch_bn(const TcGemmParams &p, cudaStream_t stream) {
   using Sh = TcShape<BN>;
   CUtensorMap ta_hi, ta_lo, tw_hi, tw_lo;
   int rc;
-  if ((rc = make_tmap(&ta_hi, p.A_hi, p.M, p.K, p.lda, BM)) ||
-      (rc = make_tmap(&ta_lo, p.A_lo, p.M, p.K, p.lda, BM)) ||
-      (rc = make_tmap(&tw_hi, p.W_hi, p.N, p.K, p.K, BN)) ||
-      (rc = make_tmap(&tw_lo, p.W_lo, p.N, p.K, p.K, BN)))
+  if ((rc = make_operand_map(&ta_hi, p.A_hi, p.M, p.K, p.lda, BM)) ||
+      (rc = make_operand_map(&ta_lo, p.A_lo, p.M, p.K, p.lda, BM)) ||
+      (rc = make_operand_map(&tw_hi, p.W_hi, p.N, p.K, p.K, BN)) ||
+      (rc = make_operand_map(&tw_lo, p.W_lo, p.N, p.K, p.K, BN)))
     return rc;
   CUtensorMap tc, tc_hi, tc_lo;
   if ((rc = make_out_maps(p, ta_hi, &tc, &tc_hi, &tc_lo))) return rc;
@@ -809,10 +798,10 @@ int launch_bn(const TcGemmParams &p, cudaStream_t stream) {
 int launch_pair(const TcGemmParams &p, cudaStream_t stream, int sms) {
   CUtensorMap ta_hi, ta_lo, tw_hi, tw_lo;
   int rc;
-  if ((rc = make_tmap(&ta_hi, p.A_hi, p.M, p.K, p.lda, 128)) ||
-      (rc = make_tmap(&ta_lo, p.A_lo, p.M, p.K, p.lda, 128)) ||
-      (rc = make_tmap(&tw_hi, p.W_hi, p.N, p.K, p.K, 128)) ||
-      (rc = make_tmap(&tw_lo, p.W_lo, p.N, p.K, p.K, 128)))
+  if ((rc = make_operand_map(&ta_hi, p.A_hi, p.M, p.K, p.lda, 128)) ||
+      (rc = make_operand_map(&ta_lo, p.A_lo, p.M, p.K, p.lda, 128)) ||
+      (rc = make_operand_map(&tw_hi, p.W_hi, p.N, p.K, p.K, 128)) ||
+      (rc = make_operand_map(&tw_lo, p.W_lo, p.N, p.K, p.K, 128)))
     return rc;
   CUtensorMap tc, tc_hi, tc_lo;
   if ((rc = make_out_maps(p, ta_hi, &tc, &tc_hi, &tc_lo))) return rc;
@@ -859,12 +848,13 @@ int sm_count() {
 
 int launch_gemm_tc3(const TcGemmParams &p, cudaStream_t stream) {
   if (p.M <= 0 || p.N <= 0) return TT_OK;
-  if (p.K <= 0 || p.K % 4 != 0 || p.N % 4 != 0 || p.ldc % 4 != 0)
-    return fail(TT_ERR_UNSUPPORTED, "gemm_tc: K, N and ldc must be multiples of 4");
-  if ((p.C != nullptr) + (p.C_hi != nullptr) + (p.H_hi != nullptr) != 1 ||
-      (p.C_hi != nullptr) != (p.C_lo != nullptr) || (p.H_hi != nullptr) != (p.H_lo != nullptr))
-    return fail(TT_ERR_UNSUPPORTED, "gemm_tc: exactly one of C, the C_hi/C_lo split, the H split");
-  if (p.H_hi != nullptr && (p.vt_hi == nullptr || p.h_cols != p.vt_col0 || p.h_cols % 16 != 0))
+  if (p.acc_scale == nullptr) return fail(TT_ERR_INVALID_ARGUMENT, "gemm_tc: acc_scale is null");
+  if (p.K <= 0 || p.K % 8 != 0 || p.lda % 8 != 0 || p.N % 8 != 0 || p.ldc % 4 != 0)
+    return fail(TT_ERR_UNSUPPORTED, "gemm_tc: K, lda and N must be multiples of 8, ldc of 4");
+  if ((p.C != nullptr) == (p.H_hi != nullptr) || (p.H_hi != nullptr) != (p.H_lo != nullptr))
+    return fail(TT_ERR_UNSUPPORTED, "gemm_tc: exactly one of C and the H split");
+  if (p.H_hi != nullptr &&
+      (p.h_cols % 8 != 0 || (p.vt_hi != nullptr ? p.h_cols != p.vt_col0 : p.h_cols != p.N)))
     return fail(TT_ERR_UNSUPPORTED, "gemm_tc: the fp16 split covers the columns before v");
   if (p.vt_hi != nullptr && (p.vt_col0 % 16 != 0 || p.head_dim % 16 != 0 || p.seq_pad % 8 != 0))
     return fail(TT_ERR_UNSUPPORTED, "gemm_tc: transposed value columns need 16-aligned heads");

@@ -1,4 +1,4 @@
-// 3xTF32 tcgen05 GEMM (see gemm_tc.cu).
+// Split-precision tcgen05 GEMM (see gemm_tc.cu).
 #pragma once
 
 #include "tt_common.cuh"
@@ -6,21 +6,23 @@
 namespace tt {
 
 struct TcGemmParams {
-  const float *A_hi, *A_lo;   // [M, K] TF32 split of the A operand, leading dim lda
+  // Operands as fp16 splits x = hi + lo (binary16 bit patterns, see f16_split):
+  const uint16_t *A_hi, *A_lo;  // [M, K], leading dim lda (elements)
   int64_t lda;
-  const float *W_hi, *W_lo;   // [N, K] TF32 split of the weight (nn.Linear layout)
-  const float *bias;          // [N]
-  const float *R;             // residual [M, N] at ldc (may alias C)
-  float *C;                   // fp32 output [M, N] at ldc, or null
-  float *C_hi, *C_lo;         // TF32 split of the output, or null
+  const uint16_t *W_hi, *W_lo;  // [N, K] (nn.Linear layout), scaled by 1 / *acc_scale
+  const float *acc_scale;       // device pointer: the accumulator is multiplied by
+                                // *acc_scale (a power of 2, written at pack time)
+  const float *bias;            // [N]
+  const float *R;               // residual [M, N] at ldc (may alias C)
+  float *C;                     // fp32 output [M, N] at ldc, or null
   int64_t ldc;
-  const uint8_t *row_mask;    // [M] or null
-  DeviceStatus *status;       // device status word for bounded-wait timeouts
+  const uint8_t *row_mask;      // [M] or null
+  DeviceStatus *status;         // device status word for bounded-wait timeouts
   int M, N, K;
-  int epilogue;               // GemmEpilogue
-  // Operands of the tensor-core attention, written by a q|k|v projection as
-  // fp16 splits (x = hi + lo, binary16 bit patterns):
-  //   columns [0, h_cols) (q and k) to H_hi/H_lo [M, h_cols];
+  int epilogue;                 // GemmEpilogue
+  // Outputs feeding another tensor-core kernel, as fp16 splits:
+  //   columns [0, h_cols) to H_hi/H_lo [M, h_cols] (the next GEMM's A operand,
+  //   or q|k for the attention);
   //   columns [vt_col0, N) (v) of row r = b*seq + s, head h, dim d transposed to
   //   vt_{hi,lo}[((b*heads + h)*head_dim + d)*seq_pad + s] (keys contiguous).
   // A value whose magnitude is beyond the fp16 range latches

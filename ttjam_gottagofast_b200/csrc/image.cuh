@@ -4,7 +4,8 @@
 //   [status word, 256 B]
 //   per layer: ln1 w,b | Wqkv [3D,D] (q rows, then k, then v) | bqkv [3D] |
 //              Wo [D,D] | bo | ln2 w,b | W1 [F,D] | b1 [F] | W2 [D,F] | b2 [D]
-//              and, on the tensor-core path, the TF32 hi/lo split of each weight
+//              and, on the tensor-core path, the fp16 hi/lo split of each
+//              weight scaled by a power of two, and the four scales
 //   final_norm w,b
 // Every array starts on a 256-byte boundary (TMA and float4 friendly).
 //
@@ -12,7 +13,7 @@
 //   FFMA schedule:        qkv [T,3D] | ctx [T,D] | h [T,F]
 //   tensor-core schedule: qkv [T,3D] (or, when the attention also runs on
 //   tensor cores, head_dim 32 or 64, the fp16 split of q|k qk_hi/qk_lo [T,2D]
-//   and of v transposed vt_hi/vt_lo [B*H, hd, seq_pad]) | the TF32 splits of
+//   and of v transposed vt_hi/vt_lo [B*H, hd, seq_pad]) | the fp16 splits of
 //   the GEMM A operands: ln_hi/ln_lo [T,D], ctx_hi/ctx_lo [T,D], h_hi/h_lo [T,F].
 #pragma once
 
@@ -24,16 +25,20 @@ namespace tt {
 
 enum ForwardPlan : int { PLAN_CLUSTER = 1, PLAN_OPS_FFMA = 2, PLAN_OPS_TC = 3 };
 
-// Shapes the 3xTF32 tensor-core schedule can run: every GEMM operand row must
-// be a whole number of 16-byte TMA units (d_model and ffn_dim multiples of 4).
-// The packed image then carries the TF32 split of every weight.
+// Shapes the split-precision tensor-core schedule can run: every GEMM operand
+// row (fp16) must be a whole number of 16-byte TMA units (d_model and ffn_dim
+// multiples of 8). The packed image then carries the fp16 split of every
+// weight.
 inline bool uses_tensor_cores(const tt_config &cfg) {
-  return cfg.d_model % 4 == 0 && cfg.ffn_dim % 4 == 0;
+  return cfg.d_model % 8 == 0 && cfg.ffn_dim % 8 == 0;
 }
 
 struct LayerOffsets {
   size_t ln1_w, ln1_b, wqkv, bqkv, wo, bo, ln2_w, ln2_b, w1, b1, w2, b2;
-  size_t wqkv_hi, wqkv_lo, wo_hi, wo_lo, w1_hi, w1_lo, w2_hi, w2_lo;
+  size_t wqkv_hi, wqkv_lo, wo_hi, wo_lo, w1_hi, w1_lo, w2_hi, w2_lo;  // fp16 pieces
+  // [0..3] accumulator scales of the q|k|v, out_proj, ffn_in, ffn_out GEMMs
+  // (floats), [4..7] the weights' largest magnitudes (float bits, pack scratch)
+  size_t wscale;
 };
 
 struct ImageLayout {
@@ -61,12 +66,15 @@ struct ImageLayout {
       o.w1 = take(F * D); o.b1 = take(F);
       o.w2 = take(D * F); o.b2 = take(D);
       if (tensor) {
-        o.wqkv_hi = take(3 * D * D); o.wqkv_lo = take(3 * D * D);
-        o.wo_hi = take(D * D); o.wo_lo = take(D * D);
-        o.w1_hi = take(F * D); o.w1_lo = take(F * D);
-        o.w2_hi = take(D * F); o.w2_lo = take(D * F);
+        // fp16 pieces: two values per float of `take`
+        o.wqkv_hi = take(3 * D * D / 2); o.wqkv_lo = take(3 * D * D / 2);
+        o.wo_hi = take(D * D / 2); o.wo_lo = take(D * D / 2);
+        o.w1_hi = take(F * D / 2); o.w1_lo = take(F * D / 2);
+        o.w2_hi = take(D * F / 2); o.w2_lo = take(D * F / 2);
+        o.wscale = take(8);
       } else {
         o.wqkv_hi = o.wqkv_lo = o.wo_hi = o.wo_lo = o.w1_hi = o.w1_lo = o.w2_hi = o.w2_lo = 0;
+        o.wscale = 0;
       }
     }
     final_w = take(D);
@@ -106,10 +114,10 @@ struct WorkspaceLayout {
       qkv = take(T * 3 * D);
     }
     if (tensor) {
-      // A operands of the 3xTF32 GEMMs, as TF32 hi/lo pairs
-      ln_hi = take(T * D); ln_lo = take(T * D);
-      ctx_hi = take(T * D); ctx_lo = take(T * D);
-      h_hi = take(T * F); h_lo = take(T * F);
+      // A operands of the split-precision GEMMs, as fp16 hi/lo pairs
+      ln_hi = take(T * D / 2); ln_lo = take(T * D / 2);
+      ctx_hi = take(T * D / 2); ctx_lo = take(T * D / 2);
+      h_hi = take(T * F / 2); h_lo = take(T * F / 2);
     } else {
       ctx = take(T * D);
       h = take(T * F);

@@ -18,8 +18,8 @@ __device__ __forceinline__ float warp_sum(float v) {
 // Register-resident variant: D % 4 == 0 and D <= 128 * NV.
 template <int NV>
 __global__ void __launch_bounds__(256) layernorm_vec_kernel(
-    const float *__restrict__ x, float *__restrict__ y, float *__restrict__ y_hi,
-    float *__restrict__ y_lo, const float *__restrict__ gamma, const float *__restrict__ beta,
+    const float *__restrict__ x, float *__restrict__ y, uint16_t *__restrict__ y_hi,
+    uint16_t *__restrict__ y_lo, const float *__restrict__ gamma, const float *__restrict__ beta,
     const uint8_t *__restrict__ row_mask, int zero_masked_rows, int64_t rows, int d, float eps) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -69,13 +69,15 @@ __global__ void __launch_bounds__(256) layernorm_vec_kernel(
       }
       if (y != nullptr) yr[c] = o;
       if (y_hi != nullptr) {
-        float4 h, l;
-        h.x = tf32_round(o.x); l.x = o.x - h.x;
-        h.y = tf32_round(o.y); l.y = o.y - h.y;
-        h.z = tf32_round(o.z); l.z = o.z - h.z;
-        h.w = tf32_round(o.w); l.w = o.w - h.w;
-        reinterpret_cast<float4 *>(y_hi + row * d)[c] = h;
-        reinterpret_cast<float4 *>(y_lo + row * d)[c] = l;
+        uint16_t h[4], l[4];
+        f16_split(o.x, h[0], l[0]);
+        f16_split(o.y, h[1], l[1]);
+        f16_split(o.z, h[2], l[2]);
+        f16_split(o.w, h[3], l[3]);
+        reinterpret_cast<uint2 *>(y_hi + row * d)[c] =
+            make_uint2(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16));
+        reinterpret_cast<uint2 *>(y_lo + row * d)[c] =
+            make_uint2(l[0] | ((uint32_t)l[1] << 16), l[2] | ((uint32_t)l[3] << 16));
       }
     }
   }
@@ -83,8 +85,8 @@ __global__ void __launch_bounds__(256) layernorm_vec_kernel(
 
 // Generic variant for any D: two passes over the row in global memory.
 __global__ void __launch_bounds__(256) layernorm_generic_kernel(
-    const float *__restrict__ x, float *__restrict__ y, float *__restrict__ y_hi,
-    float *__restrict__ y_lo, const float *__restrict__ gamma, const float *__restrict__ beta,
+    const float *__restrict__ x, float *__restrict__ y, uint16_t *__restrict__ y_hi,
+    uint16_t *__restrict__ y_lo, const float *__restrict__ gamma, const float *__restrict__ beta,
     const uint8_t *__restrict__ row_mask, int zero_masked_rows, int64_t rows, int d, float eps) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -105,17 +107,13 @@ __global__ void __launch_bounds__(256) layernorm_generic_kernel(
   for (int c = lane; c < d; c += 32) {
     const float o = zero ? 0.f : (xr[c] - mean) * rstd * gamma[c] + beta[c];
     if (y != nullptr) y[row * d + c] = o;
-    if (y_hi != nullptr) {
-      const float h = tf32_round(o);
-      y_hi[row * d + c] = h;
-      y_lo[row * d + c] = o - h;
-    }
+    if (y_hi != nullptr) f16_split(o, y_hi[row * d + c], y_lo[row * d + c]);
   }
 }
 
 }  // namespace
 
-int launch_layernorm(const float *x, float *y, float *y_hi, float *y_lo, const float *gamma,
+int launch_layernorm(const float *x, float *y, uint16_t *y_hi, uint16_t *y_lo, const float *gamma,
                      const float *beta, const uint8_t *row_mask, int zero_masked_rows,
                      int64_t rows, int d, float eps, cudaStream_t stream) {
   if (rows <= 0) return TT_OK;
@@ -124,7 +122,8 @@ int launch_layernorm(const float *x, float *y, float *y_hi, float *y_lo, const f
   const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
                          reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta) |
                          reinterpret_cast<uintptr_t>(y_hi) | reinterpret_cast<uintptr_t>(y_lo)) &
-                        15) == 0;
+                        15) == 0 &&
+                       (y_hi == nullptr || d % 8 == 0);
   if (d % 4 == 0 && aligned && d <= 1024) {
     const int nv = (int)ceil_div(d, 128);
 #define TT_LN_CASE(NV)                                                                     \

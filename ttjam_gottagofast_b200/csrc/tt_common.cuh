@@ -60,6 +60,25 @@ __device__ __forceinline__ float tf32_round(float v) {
   return __uint_as_float(r);
 }
 
+// fp16 split used by the tensor-core path (binary16 bit patterns): hi = x
+// rounded to fp16 (round to nearest even), lo = x - hi (exact in fp32) rounded
+// to fp16; hi + lo carries about 22 significant bits while |x| <= 65504 (a
+// larger |x| gives an infinite hi).
+__device__ __forceinline__ uint16_t f16_bits(float x) {
+  uint16_t h;
+  asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(x));
+  return h;
+}
+__device__ __forceinline__ float f16_value(uint16_t h) {
+  float y;
+  asm("cvt.f32.f16 %0, %1;" : "=f"(y) : "h"(h));
+  return y;
+}
+__device__ __forceinline__ void f16_split(float x, uint16_t &hi, uint16_t &lo) {
+  hi = f16_bits(x);
+  lo = f16_bits(x - f16_value(hi));
+}
+
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -69,9 +88,9 @@ __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a -
 
 // Row LayerNorm, nn.LayerNorm(D) semantics (eps, biased variance). If
 // `zero_rows_mask` is set, rows whose mask byte is 0 are written as 0.
-// If y_hi/y_lo are given, also writes the TF32 split of the output (y may then
+// If y_hi/y_lo are given, also writes the fp16 split of the output (y may then
 // be null).
-int launch_layernorm(const float *x, float *y, float *y_hi, float *y_lo, const float *gamma,
+int launch_layernorm(const float *x, float *y, uint16_t *y_hi, uint16_t *y_lo, const float *gamma,
                      const float *beta, const uint8_t *row_mask, int zero_masked_rows,
                      int64_t rows, int d, float eps, cudaStream_t stream);
 
@@ -104,7 +123,7 @@ int launch_gemm_ffma(const GemmParams &p, cudaStream_t stream);
 struct AttentionParams {
   const float *qkv;      // [B*S, 3D]: q | k | v, head h at columns h*hd..h*hd+hd-1
   float *ctx;            // [B*S, D], or null when only the split is wanted
-  float *ctx_hi, *ctx_lo;  // optional TF32 split copies
+  uint16_t *ctx_hi, *ctx_lo;  // optional fp16 split copies
   const uint8_t *mask;   // [B, S] or null
   int64_t batch;
   int seq, d_model, num_heads, head_dim;
