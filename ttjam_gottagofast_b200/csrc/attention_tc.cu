@@ -19,17 +19,17 @@
 // 16-bit MMA does twice the work of a TF32 one in the same cycles at N = 64
 // and moves half the operand bytes.
 //
-// CTA = (query tile of 128 rows, head, sequence); 384 threads:
+// CTA = (query tile of 128 rows, head, sequence); 320 threads, two CTAs per
+// SM (256 tensor-memory columns and a 3-stage ring each), so that one CTA's
+// softmax runs while the other's MMAs use the tensor pipe:
 //   warp 0    TMA producer: per 64-key tile, K_hi K_lo (64 keys x HD dims) and
 //             Vt_hi Vt_lo (HD dims x 64 keys, from the transposed copy of v the
-//             q|k|v GEMM writes) into a 4-stage ring;
-//   warp 1    MMA issuer: S_j = Q.K_j^T (A = Q from tensor memory, B = K tile)
-//             into one of two S buffers, then O += P_j.V_j (A = P_j from
-//             tensor memory, B = Vt tile); both B operands are K-major. S and P
-//             are double-buffered, so S_{j+1} and P_{j-1}.V_{j-1} run while the
-//             softmax works on tile j;
-//   warp 2    allocates / frees 512 tensor-memory columns;
-//   warps 4-11 softmax, two warps per tensor-memory lane quarter: query row
+//             q|k|v GEMM writes) into the ring;
+//   warp 1    allocates / frees the tensor memory; then its lane 0 issues the
+//             MMAs: S_{j+1} = Q.K^T (A = Q from tensor memory, B = K tile) as
+//             soon as the softmax has read S_j, then O += P_j.V_j (A = P_j from
+//             tensor memory, B = Vt tile); both B operands are K-major;
+//   warps 2-9 softmax, two warps per tensor-memory lane quarter: query row
 //             q0+t (= tensor-memory lane t) is shared by two threads, one per
 //             half of the 64-key tile; they exchange the row max through shared
 //             memory (one named barrier per tile), write their half of P (split)
@@ -47,14 +47,15 @@
 namespace tt {
 namespace {
 
-constexpr int BQ = 128, BKV = 64, STAGES = 4;
-constexpr int kThreads = 384;  // warps 0-3: TMA / MMA / TMEM; warps 4-11: softmax
+constexpr int BQ = 128, BKV = 64, STAGES = 3;
+constexpr int kThreads = 320;  // warp 0: TMA; warp 1: TMEM + MMA; warps 2-9: softmax
+constexpr int kSoftWarp0 = 2;  // first softmax warp
 
 // Shapes for head_dim HD (32 or 64). Shared-memory stage: K_hi, K_lo (64 keys
 // x HD fp16: rows of 2*HD bytes, 64-byte swizzle at HD 32, 128-byte at HD 64)
 // then Vt_hi, Vt_lo (HD rows x 64 keys: 128-byte rows, 128-byte swizzle).
 // Tensor-memory columns (32-bit cells; a 16-bit operand packs two values per
-// cell): Q_hi, Q_lo (HD/2 each), S[b] (64 each), P[b] = hi (32) | lo (32), O (HD).
+// cell): Q_hi, Q_lo (HD/2 each), S (64), P = hi (32) | lo (32), O (HD).
 template <int HD>
 struct AtShape {
   static constexpr uint32_t KROW = 2 * HD;              // bytes of one K row
@@ -62,12 +63,9 @@ struct AtShape {
   static constexpr uint32_t OPV = HD * 128;             // one V^T operand (hi or lo)
   static constexpr uint32_t STAGE = 2 * OPK + 2 * OPV;
   static constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE + 1024 + 256;
-  static constexpr uint32_t T_QHI = 0, T_QLO = HD / 2, T_S = HD, T_P = HD + 128,
-                            T_O = HD + 256;
-  static constexpr uint32_t t_s(int b) { return T_S + 64u * b; }
-  static constexpr uint32_t t_phi(int b) { return T_P + 64u * b; }
-  static constexpr uint32_t t_plo(int b) { return T_P + 64u * b + 32u; }
-  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t T_QHI = 0, T_QLO = HD / 2, T_S = HD, T_PHI = HD + 64,
+                            T_PLO = HD + 96, T_O = HD + 128;
+  static constexpr uint32_t TMEM_COLS = 256;
   static_assert(T_O + HD <= TMEM_COLS, "tensor memory");
   static_assert(OPK % 1024 == 0 && OPV % 1024 == 0, "operands on the swizzle period");
   // K operand descriptor fields: swizzle mode (4 = 64 B, 2 = 128 B) and the
@@ -220,7 +218,7 @@ __device__ __forceinline__ void split_pair(float a, float b, uint32_t &hi, uint3
 }
 
 template <int HD>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_hi,
                         const __grid_constant__ CUtensorMap tm_lo,
                         const __grid_constant__ CUtensorMap tm_vhi,
@@ -238,12 +236,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t bars = base + STAGES * STAGE;
   auto kv_full = [&](int s) { return bars + 8u * s; };
   auto kv_empty = [&](int s) { return bars + 8u * (STAGES + s); };
-  auto s_full = [&](int b) { return bars + 8u * (2 * STAGES + b); };      // S buffer b written
-  auto s_free = [&](int b) { return bars + 8u * (2 * STAGES + 2 + b); };  // ... and read
-  auto p_full = [&](int b) { return bars + 8u * (2 * STAGES + 4 + b); };  // P buffer b written
-  auto o_done = [&](int b) { return bars + 8u * (2 * STAGES + 6 + b); };  // its P.V finished
-  const uint32_t q_ready = bars + 8u * (2 * STAGES + 8);
-  const uint32_t tmem_slot = bars + 8u * (2 * STAGES + 9);
+  const uint32_t s_full = bars + 8u * (2 * STAGES);      // S written
+  const uint32_t s_free = bars + 8u * (2 * STAGES + 1);  // ... and read by the softmax
+  const uint32_t p_full = bars + 8u * (2 * STAGES + 2);  // P written
+  const uint32_t o_done = bars + 8u * (2 * STAGES + 3);  // its P.V finished
+  const uint32_t q_ready = bars + 8u * (2 * STAGES + 4);
+  const uint32_t tmem_slot = bars + 8u * (2 * STAGES + 5);
   uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -258,8 +256,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // and the mask bytes are requested together, so the prologue pays one
   // memory latency.
   uint32_t qv[2][HD / 4];
-  if (warp >= 4) {
-    const int t = (warp & 3) * 32 + lane, kh = (warp - 4) >> 2;
+  if (warp >= kSoftWarp0) {
+    const int t = (warp & 3) * 32 + lane, kh = (warp - kSoftWarp0) >> 2;
     const int row = q0 + t;
     const int64_t qoff = (b * S + (row < S ? row : 0)) * (int64_t)(2 * D) + (int64_t)h * HD +
                          (HD / 2) * kh;
@@ -305,16 +303,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(kv_empty(s), 1);
     }
     // the 8 softmax warps arrive once per warp (an elected lane after __syncwarp)
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(s_full(i), 1);
-      mbar_init(s_free(i), 8);
-      mbar_init(p_full(i), 8);
-      mbar_init(o_done(i), 1);
-    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 8);
+    mbar_init(p_full, 8);
+    mbar_init(o_done, 1);
     mbar_init(q_ready, 8);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 2) {
+  if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot),
                  "r"(TMEM_COLS)
                  : "memory");
@@ -342,13 +338,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer --------------------------------------------------------
     auto issue_s = [&](int j) {
-      const int s = j % STAGES, sb = j & 1;
+      const int s = j % STAGES;
       mbar_wait(kv_full(s), (j / STAGES) & 1, p.status, 0x4200 + j);
-      // S buffer sb last held S_{j-2}; the softmax has copied it to registers
-      if (j >= 2) mbar_wait(s_free(sb), ((j >> 1) - 1) & 1, p.status, 0x4300 + j);
+      // S last held S_{j-1}; the softmax has copied it to registers
+      if (j >= 1) mbar_wait(s_free, (j - 1) & 1, p.status, 0x4300 + j);
       fence_after();
       const uint32_t kst = base + s * STAGE;
-      const uint32_t sd = tm + Sh::t_s(sb);
+      const uint32_t sd = tm + Sh::T_S;
       // descriptors built once; a k-step of 16 dims advances the start address
       // by 32 bytes (2 units)
       const uint64_t khi0 = sdesc(kst, Sh::K_SBO, Sh::K_SWZ);
@@ -360,31 +356,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_ts(sd, tm + T_QHI + 8u * kk, klo0 + koff, Sh::IDESC_S, 1);
         mma_ts(sd, tm + T_QLO + 8u * kk, khi0 + koff, Sh::IDESC_S, 1);
       }
-      mma_commit(s_full(sb));
+      mma_commit(s_full);
     };
     mbar_wait(q_ready, 0, p.status, 0x4000);
     issue_s(0);
     for (int j = 0; j < nkv; ++j) {
       if (j + 1 < nkv) issue_s(j + 1);  // next scores overlap this tile's softmax
-      const int s = j % STAGES, pb = j & 1;
-      mbar_wait(p_full(pb), (j >> 1) & 1, p.status, 0x4400 + j);
+      const int s = j % STAGES;
+      mbar_wait(p_full, j & 1, p.status, 0x4400 + j);
       fence_after();
       const uint32_t vst = base + s * STAGE + 2 * OPK;
       const uint64_t vhi0 = sdesc(vst, 1024, 2), vlo0 = sdesc(vst + OPV, 1024, 2);
 #pragma unroll
       for (int kk = 0; kk < BKV / 16; ++kk) {  // 16 keys per MMA
         const uint64_t voff = (uint64_t)(2 * kk);
-        mma_ts(tm + T_O, tm + Sh::t_phi(pb) + 8u * kk, vhi0 + voff, Sh::IDESC_PV, (j | kk) != 0);
-        mma_ts(tm + T_O, tm + Sh::t_phi(pb) + 8u * kk, vlo0 + voff, Sh::IDESC_PV, 1);
-        mma_ts(tm + T_O, tm + Sh::t_plo(pb) + 8u * kk, vhi0 + voff, Sh::IDESC_PV, 1);
+        mma_ts(tm + T_O, tm + Sh::T_PHI + 8u * kk, vhi0 + voff, Sh::IDESC_PV, (j | kk) != 0);
+        mma_ts(tm + T_O, tm + Sh::T_PHI + 8u * kk, vlo0 + voff, Sh::IDESC_PV, 1);
+        mma_ts(tm + T_O, tm + Sh::T_PLO + 8u * kk, vhi0 + voff, Sh::IDESC_PV, 1);
       }
-      mma_commit(o_done(pb));
+      mma_commit(o_done);
       mma_commit(kv_empty(s));
     }
-  } else if (warp >= 4) {
+  } else if (warp >= kSoftWarp0) {
     // ---- softmax: rows split over two warpgroups by key half ----------------
     const int t = (warp & 3) * 32 + lane;   // row within the tile = tensor-memory lane
-    const int kh = (warp - 4) >> 2;         // which 32 keys (and HD/2 dims) of a tile
+    const int kh = (warp - kSoftWarp0) >> 2;  // which 32 keys (and HD/2 dims) of a tile
     const int row = q0 + t;
     const bool row_in = row < S;
     const uint32_t lane_base = tm + ((uint32_t)((warp & 3) * 32) << 16);
@@ -427,15 +423,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = __ballot_sync(0xffffffffu, ka < kv_end && (mrow == nullptr || mrow[ka] != 0));
       }
       const bool diag = p.causal && k0 + 31 > q0;  // half reaches past the first query
-      mbar_wait(s_full(sb), (j >> 1) & 1, p.status, 0x4500 + j);
+      mbar_wait(s_full, j & 1, p.status, 0x4500 + j);
       fence_after();
       float sv[32];
-      tmem_ld16(lane_base + Sh::t_s(sb) + col_off, sv);
-      tmem_ld16(lane_base + Sh::t_s(sb) + col_off + 16, sv + 16);
+      tmem_ld16(lane_base + Sh::T_S + col_off, sv);
+      tmem_ld16(lane_base + Sh::T_S + col_off + 16, sv + 16);
       tmem_wait_ld();
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(s_free(sb));
+      if (lane == 0) mbar_arrive(s_free);
       // allowed keys of this half as one word: valid (ballot) and, on the
       // diagonal, key k0 + c <= row, i.e. bits 0 .. row - k0 (one select per
       // score below; a per-score && / || compiles to branches)
@@ -459,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j > 0 && m_ref != -CUDART_INF_F) {
           // the context in tensor memory must hold P_{j-1}.V_{j-1} before it
           // is rescaled
-          mbar_wait(o_done((j - 1) & 1), ((j - 1) >> 1) & 1, p.status, 0x4600 + j);
+          mbar_wait(o_done, (j - 1) & 1, p.status, 0x4600 + j);
           fence_after();
 #pragma unroll
           for (int c = 0; c < HD / 2; c += 16) {
@@ -490,18 +486,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phi[16], plo[16];
 #pragma unroll
       for (int c = 0; c < 16; ++c) split_pair(sv[2 * c], sv[2 * c + 1], phi[c], plo[c]);
-      // P buffer pb last held P_{j-2}: its P.V must be done before it is
-      // overwritten
-      if (j >= 2) {
-        mbar_wait(o_done(sb), ((j - 2) >> 1) & 1, p.status, 0x4800 + j);
+      // P last held P_{j-1}: its P.V must be done before it is overwritten
+      if (j >= 1) {
+        mbar_wait(o_done, (j - 1) & 1, p.status, 0x4800 + j);
         fence_after();
       }
-      tmem_st16(lane_base + Sh::t_phi(sb) + pcol_off, phi);
-      tmem_st16(lane_base + Sh::t_plo(sb) + pcol_off, plo);
+      tmem_st16(lane_base + Sh::T_PHI + pcol_off, phi);
+      tmem_st16(lane_base + Sh::T_PLO + pcol_off, plo);
       tmem_wait_st();
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full(sb));
+      if (lane == 0) mbar_arrive(p_full);
     }
     // row sum = both halves' partial sums
     s_rowsum[kh][t] = l;
@@ -510,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // context = O / l (this thread's HD/2 dims), written as an fp16 split (the
     // out_proj GEMM's A operand)
     // the last P.V (the tensor pipe runs the MMAs in order, so all of them)
-    mbar_wait(o_done((nkv - 1) & 1), ((nkv - 1) >> 1) & 1, p.status, 0x4700);
+    mbar_wait(o_done, (nkv - 1) & 1, p.status, 0x4700);
     fence_after();
     const float inv = l > 0.f ? 1.f / l : 0.f;
     const int64_t off = (b * S + (row_in ? row : 0)) * (int64_t)D + (int64_t)h * HD + dim_off;
@@ -534,7 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   fence_before();
   __syncthreads();
-  if (warp == 2) {
+  if (warp == 1) {
     fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm), "r"(TMEM_COLS)
                  : "memory");
