@@ -457,7 +457,7 @@ def run_ours(args, world, rank, local):
     long_region = sum(step_ms) > 1000.0
     tc_peak_bf16 = tc_sust if long_region else tc_burst
     tc_peak = tc_peak_bf16 / 3.0  # fp16-split operands: 3 kind::f16 MMAs (bf16 rate) per product
-    on_tensor = plan == "ops_tc3xtf32" and dom != "whole_forward" and flops > 0
+    on_tensor = plan == "ops_tc" and dom != "whole_forward" and flops > 0
     if on_tensor and flops / (tc_peak * 1e12) >= nbytes / (hbm_peak * 1e9):
         achieved = flops / (dom_us * 1e-6) / 1e12
         roofline = {

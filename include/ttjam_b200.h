@@ -62,7 +62,7 @@ typedef struct tt_config {
 #define TT_PLAN_AUTO 0
 #define TT_PLAN_CLUSTER 1   /* one launch: thread-block clusters run all layers */
 #define TT_PLAN_OPS_FFMA 2  /* per-op kernels, fp32 FFMA GEMMs */
-#define TT_PLAN_OPS_TC 3    /* per-op kernels, 3xTF32 tcgen05 GEMMs */
+#define TT_PLAN_OPS_TC 3    /* per-op kernels, split-precision tcgen05 GEMMs and attention */
 
 /* One BaselineTransformerBlock's parameters, nn.Linear layout W[out,in]
  * (torch_transformer_benchmark.py:125-132, :72-75). Device pointers, fp32,
@@ -165,7 +165,7 @@ int tt_read_status(const tt_config *cfg, const void *image, int32_t *code,
 int tt_last_error(char *buf, size_t len);
 
 /* Kinds of kernel launch that tt_launch_probe_read reports. */
-#define TT_KERNEL_LAYERNORM 1     /* LayerNorm (+ TF32 split) ahead of a GEMM */
+#define TT_KERNEL_LAYERNORM 1     /* LayerNorm (+ fp16 split) ahead of a GEMM */
 #define TT_KERNEL_QKV 2           /* LN1 (when fused) + q|k|v projection */
 #define TT_KERNEL_ATTENTION 3     /* masked softmax(q k^T) v */
 #define TT_KERNEL_OUT_PROJ 4      /* out_proj + padded-row zeroing + residual */

@@ -52,7 +52,7 @@ def applicable_plans(model, b, s):
     import ctypes
     from ttjam_gottagofast_b200 import _lib
     out = []
-    for name in ("cluster", "ops_ffma", "ops_tc3xtf32"):
+    for name in ("cluster", "ops_ffma", "ops_tc"):
         cfg = _lib.make_config(model.config, name)
         if model._lib.tt_forward_plan(ctypes.byref(cfg), b, s) > 0:
             out.append(name)
@@ -209,7 +209,7 @@ def test_runs_on_current_stream():
     check(oracle.forward(params, cfg, x, mask), y, "side stream")
 
 
-@pytest.mark.parametrize("name,plan", [("B1", "cluster"), ("A", "ops_ffma"), ("A", "ops_tc3xtf32")])
+@pytest.mark.parametrize("name,plan", [("B1", "cluster"), ("A", "ops_ffma"), ("A", "ops_tc")])
 def test_launch_probe_brackets_every_launch(name, plan):
     """tt_launch_probe_* sees every launch of a forward, in schedule order,
     each with a positive device time."""
@@ -237,7 +237,7 @@ def test_launch_probe_brackets_every_launch(name, plan):
     names = [_lib.KERNEL_KINDS[k] for k in kinds]
     per_layer = {"cluster": [],
                  "ops_ffma": ["qkv", "attention", "out_proj", "ffn_in", "ffn_out"],
-                 "ops_tc3xtf32": ["layernorm", "qkv", "attention", "out_proj", "layernorm",
+                 "ops_tc": ["layernorm", "qkv", "attention", "out_proj", "layernorm",
                                   "ffn_in", "ffn_out"]}[plan]
     one = (["whole_forward"] if plan == "cluster"
            else per_layer * cfg.num_layers + ["final_norm"])

@@ -211,16 +211,6 @@ __global__ void __launch_bounds__(kThreads) gemm_ffma_kernel(GemmParams p) {
         for (int j = 0; j < 4; ++j)
           if (gc0 + j < N) dst[j] = out[j];
       }
-      if (p.C_hi != nullptr) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if (gc0 + j < N) {
-            const float hv = tf32_round(out[j]);
-            p.C_hi[gr * p.ldc + gc0 + j] = hv;
-            p.C_lo[gr * p.ldc + gc0 + j] = out[j] - hv;
-          }
-        }
-      }
     }
   }
 }
@@ -313,11 +303,6 @@ __global__ void __launch_bounds__(kThreads) gemm_ffma_wholek_kernel(GemmParams p
       if (p.epilogue == EPI_BIAS_GELU) v = gelu_erf(v);
       else if (p.epilogue == EPI_BIAS_RESIDUAL) v = valid ? p.R[gr * p.ldc + gc] + v : 0.f;
       p.C[gr * p.ldc + gc] = v;
-      if (p.C_hi != nullptr) {
-        const float hv = tf32_round(v);
-        p.C_hi[gr * p.ldc + gc] = hv;
-        p.C_lo[gr * p.ldc + gc] = v - hv;
-      }
     }
   }
 }

@@ -52,14 +52,6 @@ __device__ __forceinline__ float gelu_erf(float v) {
   return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
 }
 
-// TF32 split used by the 3xTF32 tensor-core path: hi is v rounded to TF32
-// (round-to-nearest, ties away), lo = v - hi is exact in fp32.
-__device__ __forceinline__ float tf32_round(float v) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
-  return __uint_as_float(r);
-}
-
 // fp16 split used by the tensor-core path (binary16 bit patterns): hi = x
 // rounded to fp16 (round to nearest even), lo = x - hi (exact in fp32) rounded
 // to fp16; hi + lo carries about 22 significant bits while |x| <= 65504 (a
@@ -108,7 +100,6 @@ struct GemmParams {
   const float *R;        // residual [M, N], leading dim ldc (may alias C)
   float *C;              // [M, N], leading dim ldc
   int64_t ldc;
-  float *C_hi, *C_lo;    // optional TF32 split copies of C (same ldc)
   const uint8_t *row_mask;  // [M] row validity, or null (all valid)
   const float *ln_gamma, *ln_beta;  // LayerNorm prologue on A when non-null
   float ln_eps;

@@ -80,7 +80,7 @@ class UserOptimizedTransformer(nn.Module):
 
     # ---- packed image -----------------------------------------------------
     def set_plan(self, plan: str = "auto") -> None:
-        """Force a kernel schedule ("auto", "cluster", "ops_ffma", "ops_tc3xtf32")
+        """Force a kernel schedule ("auto", "cluster", "ops_ffma", "ops_tc")
         for tests and measurements; "auto" picks the fastest applicable one."""
         cfg = _lib.make_config(self.config, plan)
         _lib.check(self._lib.tt_validate_config(ctypes.byref(cfg)), "plan")
