@@ -666,9 +666,11 @@ ClusterChoice choose_cluster(const tt_config &cfg, int64_t batch, int64_t seq) {
   int64_t spc = (batch + ncl - 1) / ncl;
   spc = std::min<int64_t>(spc, rmax / seq);
   ncl = (batch + spc - 1) / spc;
-  // past two waves of clusters the per-op schedules are faster (measured on
-  // B200: batch 8 x seq 128 takes 2 waves and wins, batch 16 x seq 128 loses)
-  if (ncl > 2 * (int64_t)maxc) return c;
+  // past one wave of clusters the per-op tensor-core schedule is faster
+  // (measured on B200 at seq 128: batch 4, one wave, 172 us against 243 us;
+  // batch 8, two waves, 338 us against 241 us); a forced cluster plan runs
+  // any number of waves
+  if (cfg.plan == TT_PLAN_AUTO && ncl > (int64_t)maxc) return c;
   if (ncl * cl > INT32_MAX / 2) return c;
   c.cluster = cl;
   c.rmax = rmax;

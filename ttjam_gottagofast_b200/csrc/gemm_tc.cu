@@ -57,19 +57,22 @@
 namespace tt {
 namespace {
 
-constexpr int BM = 128, BK = 32, STAGES = 4;  // BK in fp16 elements (64-byte rows)
-constexpr int kThreads = 384;
-constexpr int kEpiWarps = 8;
+constexpr int BM = 128, BK = 32;  // BK in fp16 elements (64-byte rows)
+constexpr int kThreads = 512;   // warps 0-3: TMA, MMA, TMEM; warps 4-15: epilogue
+constexpr int kEpiWarps = 12;  // three per tensor-memory lane quarter
 constexpr uint32_t TILE_A = BM * BK * 2;               // 8 KB
 
-constexpr uint32_t STG_WARP = 2 * 2048;               // per epilogue warp: two 32x16 fp32 chunks
+// Per epilogue warp: one staging buffer holding a 32 x 16 chunk of fp32 C
+// (2 KB) or of the fp16 split (1 KB hi at +0, 1 KB lo at +2 KB).
+constexpr uint32_t STG_WARP = 4096;
 
 template <int BN>
 struct TcShape {
   static constexpr uint32_t TILE_W = BN * BK * 2;                       // 16 KB at BN 256
   static constexpr uint32_t STAGE_BYTES = 2 * TILE_A + 2 * TILE_W;      // 48 KB at BN 256
+  static constexpr int STAGES = BN == 256 ? 3 : 4;
   static constexpr uint32_t TMEM_COLS = 2 * BN;                         // two accumulators
-  static constexpr uint32_t STG_OFF = STAGES * STAGE_BYTES;             // output staging
+  static constexpr uint32_t STG_OFF = (uint32_t)STAGES * STAGE_BYTES;   // output staging
   static constexpr uint32_t BAR_OFF = STG_OFF + kEpiWarps * STG_WARP;   // mbarriers
   static constexpr size_t SMEM_BYTES = (size_t)BAR_OFF + 256 + 1024;   // + alignment slack
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
@@ -132,6 +135,7 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap *tm, uint32_t src
 __device__ __forceinline__ void bulk_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
+// Every bulk group committed so far has read its shared memory.
 __device__ __forceinline__ void bulk_wait_read_all() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
@@ -182,8 +186,8 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
+// Accumulator columns -> registers without waiting (complete with tmem_wait_ld).
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
       "%12, %13, %14, %15}, [%16];"
@@ -191,9 +195,9 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
         "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // Epilogue values of one 16-column chunk of one row: bias, then GELU or the
@@ -282,10 +286,10 @@ __device__ __forceinline__ void stage_row(uint8_t *buf, int lane, const float4 (
 // and a TMA tensor store: fp32 C or the fp16 split H.
 __device__ __forceinline__ void epilogue_chunk_out(const TcGemmParams &p, const CUtensorMap *tm_c,
                                                    const CUtensorMap *tm_hi,
-                                                   const CUtensorMap *tm_lo, uint32_t stg,
-                                                   uint8_t *stg_ptr, int lane, int row0,
-                                                   bool valid, int col0, float acc_scale,
-                                                   float (&v)[16]) {
+                                                   const CUtensorMap *tm_lo, uint32_t stg_base,
+                                                   uint8_t *stg_ptr_base, int &nstores, int lane,
+                                                   int row0, bool valid, int col0,
+                                                   float acc_scale, float (&v)[16]) {
   const int row = row0 + lane;
   const bool row_in = row < p.M;
   epilogue_values(p, acc_scale, row, row_in, valid, col0, v);
@@ -293,7 +297,9 @@ __device__ __forceinline__ void epilogue_chunk_out(const TcGemmParams &p, const 
     if (row_in) store_vt(p, row, col0, v);
     return;
   }
-  // the previous store of this warp must have read the staging buffers
+  // this warp's previous store must have read the staging buffer
+  const uint32_t stg = stg_base;
+  uint8_t *stg_ptr = stg_ptr_base;
   if (lane == 0) bulk_wait_read_all();
   __syncwarp();
   if (p.H_hi != nullptr) {
@@ -331,6 +337,7 @@ __device__ __forceinline__ void epilogue_chunk_out(const TcGemmParams &p, const 
     }
     bulk_commit();
   }
+  ++nstores;
 }
 
 template <int BN>
@@ -343,6 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tm_c_hi,
                     const __grid_constant__ CUtensorMap tm_c_lo, const TcGemmParams p) {
   using Sh = TcShape<BN>;
+  constexpr int STAGES = Sh::STAGES;
   constexpr uint32_t TILE_W = Sh::TILE_W, STAGE_BYTES = Sh::STAGE_BYTES;
   constexpr uint32_t IDESC = idesc_f16<BN>();
   extern __shared__ uint8_t smem_raw[];
@@ -432,10 +440,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= 4) {
     // ---- epilogue: tensor memory -> registers -> shared -> TMA store -------
     const int q = warp & 3;                 // tensor-memory lane quarter
-    const int chalf = (warp - 4) >> 2;      // column half of the tile
+    // column third of the tile, in 16-column chunks
+    const int cgrp = (warp - 4) >> 2;
+    const int c_lo = 16 * (cgrp * (BN / 16) / 3), c_hi = 16 * ((cgrp + 1) * (BN / 16) / 3);
     const uint32_t stg = base + Sh::STG_OFF + (uint32_t)(warp - 4) * STG_WARP;
     uint8_t *stg_ptr = smem_raw + (stg - raw);
     const float acc_scale = *p.acc_scale;
+    int nstores = 0;  // bulk store groups this warp has committed
     int local = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
       const int ab = local & 1;
@@ -446,14 +457,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = row0 + lane;
       const bool row_in = row < p.M;
       const bool valid = row_in && (p.row_mask == nullptr || p.row_mask[row] != 0);
+      // two 16-column chunks per step: both accumulator loads are in flight
+      // together, and each chunk leaves through the next staging buffer
 #pragma unroll 1
-      for (int c0 = chalf * (BN / 2); c0 < (chalf + 1) * (BN / 2); c0 += 16) {
-        float v[16];
-        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN + c0), v);
+      for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
+        uint32_t ra[16], rb[16];
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN + c0);
+        tmem_ld16_async(taddr, ra);
+        if (c0 + 16 < c_hi) tmem_ld16_async(taddr + 16, rb);  // warp-uniform
+        tmem_wait_ld();
         const int col0 = n0 + c0;
-        if (col0 >= p.N || row0 >= p.M) continue;  // warp-uniform
-        epilogue_chunk_out(p, &tm_c, &tm_c_hi, &tm_c_lo, stg, stg_ptr, lane, row0, valid, col0,
-                           acc_scale, v);
+        if (row0 >= p.M) continue;  // warp-uniform
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(ra[i]);
+        if (col0 < p.N)
+          epilogue_chunk_out(p, &tm_c, &tm_c_hi, &tm_c_lo, stg, stg_ptr, nstores, lane, row0,
+                             valid, col0, acc_scale, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(rb[i]);
+        if (c0 + 16 < c_hi && col0 + 16 < p.N)
+          epilogue_chunk_out(p, &tm_c, &tm_c_hi, &tm_c_lo, stg, stg_ptr, nstores, lane, row0,
+                             valid, col0 + 16, acc_scale, v);
       }
       tc_fence_before();
       __syncwarp();
@@ -486,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // acc_full barrier of both (one commit per CTA); both CTAs' epilogue warps
 // release an accumulator on CTA 0's acc_empty barrier. No load uses cluster
 // multicast.
-constexpr int PSTAGES = 6;
+constexpr int PSTAGES = 5;
 constexpr int PBN = 256;                                    // pair tile N (128 per CTA in smem)
 constexpr uint32_t P_TILE = 128 * BK * 2;                   // 8 KB: A rows or W half rows
 constexpr uint32_t P_STAGE = 4 * P_TILE;                    // A_hi, A_lo, W_hi half, W_lo half
@@ -651,10 +676,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= 4) {
     // ---- epilogue (both CTAs): this CTA's 128 rows --------------------------
     const int q = warp & 3;
-    const int chalf = (warp - 4) >> 2;
+    // column third of the tile, in 16-column chunks
+    const int cgrp = (warp - 4) >> 2;
+    const int c_lo = 16 * (cgrp * (PBN / 16) / 3), c_hi = 16 * ((cgrp + 1) * (PBN / 16) / 3);
     const uint32_t stg = base + P_STG_OFF + (uint32_t)(warp - 4) * STG_WARP;
     uint8_t *stg_ptr = smem_raw + (stg - raw);
     const float acc_scale = *p.acc_scale;
+    int nstores = 0;  // bulk store groups this warp has committed
     const uint32_t acc_empty0 = map_to_cta(acc_empty(0), 0);
     int local = 0;
     for (int tile = pair; tile < ntiles; tile += npairs, ++local) {
@@ -666,14 +694,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = row0 + lane;
       const bool row_in = row < p.M;
       const bool valid = row_in && (p.row_mask == nullptr || p.row_mask[row] != 0);
+      // two 16-column chunks per step: both accumulator loads are in flight
+      // together, and each chunk leaves through the next staging buffer
 #pragma unroll 1
-      for (int c0 = chalf * (PBN / 2); c0 < (chalf + 1) * (PBN / 2); c0 += 16) {
-        float v[16];
-        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * PBN + c0), v);
+      for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
+        uint32_t ra[16], rb[16];
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * PBN + c0);
+        tmem_ld16_async(taddr, ra);
+        if (c0 + 16 < c_hi) tmem_ld16_async(taddr + 16, rb);  // warp-uniform
+        tmem_wait_ld();
         const int col0 = n0 + c0;
-        if (col0 >= p.N || row0 >= p.M) continue;  // warp-uniform
-        epilogue_chunk_out(p, &tm_c, &tm_c_hi, &tm_c_lo, stg, stg_ptr, lane, row0, valid, col0,
-                           acc_scale, v);
+        if (row0 >= p.M) continue;  // warp-uniform
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(ra[i]);
+        if (col0 < p.N)
+          epilogue_chunk_out(p, &tm_c, &tm_c_hi, &tm_c_lo, stg, stg_ptr, nstores, lane, row0,
+                             valid, col0, acc_scale, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(rb[i]);
+        if (c0 + 16 < c_hi && col0 + 16 < p.N)
+          epilogue_chunk_out(p, &tm_c, &tm_c_hi, &tm_c_lo, stg, stg_ptr, nstores, lane, row0,
+                             valid, col0 + 16, acc_scale, v);
       }
       tc_fence_before();
       __syncwarp();
