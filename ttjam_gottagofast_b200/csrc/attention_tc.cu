@@ -38,7 +38,7 @@
 //             row max grows by more than 2^8.
 // Every mbarrier wait is bounded; a wait that gives up latches
 // TT_ERR_DEVICE_TIMEOUT and the kernel still frees tensor memory and returns.
-// No TMA load here uses cluster multicast.
+// Every TMA load here fills only the issuing CTA's own shared memory.
 #include <cuda.h>
 #include <math_constants.h>
 
@@ -448,7 +448,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       s_rowmax[sb][kh][t] = mx;
-      asm volatile("bar.sync 1, 256;" ::: "memory");  // the 8 softmax warps
+      // the two warps that share these 32 rows (one per key half)
+      asm volatile("bar.sync %0, 64;" ::"r"(1 + (warp & 3)) : "memory");
       mx = fmaxf(mx, s_rowmax[sb][kh ^ 1][t]);
       if (mx > m_ref + kLazy || (m_ref == -CUDART_INF_F && mx != -CUDART_INF_F)) {
         const float alpha = fast_exp2(m_ref - mx);  // 0 when m_ref is -inf
@@ -500,7 +501,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     // row sum = both halves' partial sums
     s_rowsum[kh][t] = l;
-    asm volatile("bar.sync 1, 256;" ::: "memory");
+    asm volatile("bar.sync %0, 64;" ::"r"(1 + (warp & 3)) : "memory");
     l += s_rowsum[kh ^ 1][t];
     // context = O / l (this thread's HD/2 dims), written as an fp16 split (the
     // out_proj GEMM's A operand)

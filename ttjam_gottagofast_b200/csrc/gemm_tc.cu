@@ -49,7 +49,7 @@
 // bandwidth.
 // Every mbarrier wait is bounded; a wait that gives up latches
 // TT_ERR_DEVICE_TIMEOUT and the kernel still frees its tensor memory and
-// returns. No TMA load here uses cluster multicast.
+// returns. Every TMA load here fills only the issuing CTA's own shared memory.
 #include <cuda.h>
 
 #include "gemm_tc.cuh"
@@ -509,8 +509,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // bytes on CTA 0's full barrier (TMA .cta_group::2); CTA 0's MMA thread commits
 // each stage to the empty barrier of both CTAs and each accumulator to the
 // acc_full barrier of both (one commit per CTA); both CTAs' epilogue warps
-// release an accumulator on CTA 0's acc_empty barrier. No load uses cluster
-// multicast.
+// release an accumulator on CTA 0's acc_empty barrier. Each CTA's loads fill
+// only its own shared memory.
 constexpr int PSTAGES = 5;
 constexpr int PBN = 256;                                    // pair tile N (128 per CTA in smem)
 constexpr uint32_t P_TILE = 128 * BK * 2;                   // 8 KB: A rows or W half rows
