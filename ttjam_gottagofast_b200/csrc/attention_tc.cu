@@ -205,20 +205,26 @@ __device__ __forceinline__ void tmem_wait_st() {
 // Two fp32 values -> their fp16 splits packed as (hi pair, lo pair), the
 // element with the lower index in the low 16 bits.
 __device__ __forceinline__ void split_pair(float a, float b, uint32_t &hi, uint32_t &lo) {
-  uint32_t h;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));
-  float ha, hb;
-  asm("{\n\t.reg .f16 x, y;\n\tmov.b32 {x, y}, %2;\n\tcvt.f32.f16 %0, x;\n\tcvt.f32.f16 %1, y;\n\t}"
-      : "=f"(ha), "=f"(hb)
-      : "r"(h));
-  uint32_t l;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(l) : "f"(b - hb), "f"(a - ha));
-  hi = h;
-  lo = l;
+  f16_split2(a, b, hi, lo);
 }
 
+// Named barrier of the two softmax warps that serve lane quarter q (ids 1-4,
+// immediates: a register id would make the compiler reserve all 16 barriers,
+// which leaves room for one CTA per SM).
+__device__ __forceinline__ void pair_barrier(int q) {
+  switch (q) {
+    case 0: asm volatile("bar.sync 1, 64;" ::: "memory"); break;
+    case 1: asm volatile("bar.sync 2, 64;" ::: "memory"); break;
+    case 2: asm volatile("bar.sync 3, 64;" ::: "memory"); break;
+    default: asm volatile("bar.sync 4, 64;" ::: "memory"); break;
+  }
+}
+
+// Two CTAs per SM: the warps of a 320-thread CTA fall 3, 3, 2, 2 on the four
+// SM sub-partitions, so two CTAs put 6 warps on one sub-partition, whose 16K
+// registers then allow 85 per thread: the kernel is held to 80.
 template <int HD>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __maxnreg__(80)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_hi,
                         const __grid_constant__ CUtensorMap tm_lo,
                         const __grid_constant__ CUtensorMap tm_vhi,
@@ -246,9 +252,14 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.seq, D = p.d_model;
-  const int qt = gridDim.x - 1 - blockIdx.x;  // heaviest (latest) query tiles first
-  const int h = blockIdx.y;
-  const int64_t b = blockIdx.z;
+  // one-dimensional grid ordered by query tile, latest (heaviest under the
+  // causal mask) first, so that the longest CTAs start first and the short
+  // ones fill the tail
+  const int64_t nbh = p.batch * p.num_heads;
+  const int qt = (S + BQ - 1) / BQ - 1 - (int)(blockIdx.x / nbh);
+  const int64_t bh_idx = blockIdx.x % nbh;
+  const int h = (int)(bh_idx % p.num_heads);
+  const int64_t b = bh_idx / p.num_heads;
   const int q0 = qt * BQ;
   const uint8_t *mrow = p.mask ? p.mask + b * S : nullptr;
 
@@ -449,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       s_rowmax[sb][kh][t] = mx;
       // the two warps that share these 32 rows (one per key half)
-      asm volatile("bar.sync %0, 64;" ::"r"(1 + (warp & 3)) : "memory");
+      pair_barrier(warp & 3);
       mx = fmaxf(mx, s_rowmax[sb][kh ^ 1][t]);
       if (mx > m_ref + kLazy || (m_ref == -CUDART_INF_F && mx != -CUDART_INF_F)) {
         const float alpha = fast_exp2(m_ref - mx);  // 0 when m_ref is -inf
@@ -501,7 +512,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     // row sum = both halves' partial sums
     s_rowsum[kh][t] = l;
-    asm volatile("bar.sync %0, 64;" ::"r"(1 + (warp & 3)) : "memory");
+    pair_barrier(warp & 3);
     l += s_rowsum[kh ^ 1][t];
     // context = O / l (this thread's HD/2 dims), written as an fp16 split (the
     // out_proj GEMM's A operand)
@@ -607,9 +618,14 @@ int launch_hd(const AttentionTcParams &p, const CUtensorMap &thi, const CUtensor
     TT_CUDA_TRY(cudaFuncSetAttribute(attention_tc_kernel<HD>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)Sh::SMEM_BYTES));
+    // two CTAs per SM need the largest shared-memory carveout
+    TT_CUDA_TRY(cudaFuncSetAttribute(attention_tc_kernel<HD>,
+                                     cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     (int)cudaSharedmemCarveoutMaxShared));
     attr_set = true;
   }
-  dim3 grid((unsigned)((p.seq + BQ - 1) / BQ), (unsigned)p.num_heads, (unsigned)p.batch);
+  const int64_t ctas = (int64_t)((p.seq + BQ - 1) / BQ) * p.num_heads * p.batch;
+  dim3 grid((unsigned)ctas);
   attention_tc_kernel<HD><<<grid, kThreads, Sh::SMEM_BYTES, stream>>>(thi, tlo, tvhi, tvlo, p);
   TT_LAUNCH_CHECK("attention_tc");
   return TT_OK;
@@ -625,8 +641,8 @@ int launch_attention_tc(const AttentionTcParams &p, cudaStream_t stream) {
   if (p.batch <= 0 || p.seq <= 0) return TT_OK;
   if (!attention_tc_supported(p.head_dim, p.d_model))
     return fail(TT_ERR_UNSUPPORTED, "attention_tc: head_dim must be 32 or 64");
-  if (p.batch > 65535 || p.num_heads > 65535)
-    return fail(TT_ERR_UNSUPPORTED, "attention_tc: batch and num_heads must be <= 65535");
+  if ((int64_t)((p.seq + BQ - 1) / BQ) * p.num_heads * p.batch > INT32_MAX)
+    return fail(TT_ERR_UNSUPPORTED, "attention_tc: more than 2^31 query tiles");
   if (((reinterpret_cast<uintptr_t>(p.qk_hi) | reinterpret_cast<uintptr_t>(p.qk_lo) |
         reinterpret_cast<uintptr_t>(p.ctx_hi) | reinterpret_cast<uintptr_t>(p.ctx_lo) |
         reinterpret_cast<uintptr_t>(p.vt_hi) | reinterpret_cast<uintptr_t>(p.vt_lo)) & 15) != 0)
@@ -644,4 +660,27 @@ int launch_attention_tc(const AttentionTcParams &p, cudaStream_t stream) {
                           : launch_hd<64>(p, thi, tlo, tvhi, tvlo, stream);
 }
 
+}  // namespace tt
+
+namespace tt {
+// CTAs of the tensor-core attention kernel resident per SM (diagnostics).
+int attention_tc_ctas_per_sm(int head_dim) {
+  int n = 0;
+  if (head_dim == 64) {
+    cudaFuncSetAttribute(attention_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)AtShape<64>::SMEM_BYTES);
+    cudaFuncSetAttribute(attention_tc_kernel<64>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                         (int)cudaSharedmemCarveoutMaxShared);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attention_tc_kernel<64>, kThreads,
+                                                  AtShape<64>::SMEM_BYTES);
+  } else {
+    cudaFuncSetAttribute(attention_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)AtShape<32>::SMEM_BYTES);
+    cudaFuncSetAttribute(attention_tc_kernel<32>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                         (int)cudaSharedmemCarveoutMaxShared);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attention_tc_kernel<32>, kThreads,
+                                                  AtShape<32>::SMEM_BYTES);
+  }
+  return n;
+}
 }  // namespace tt

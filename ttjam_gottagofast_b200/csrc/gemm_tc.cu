@@ -305,14 +305,13 @@ __device__ __forceinline__ void epilogue_chunk_out(const TcGemmParams &p, const 
   if (p.H_hi != nullptr) {
     bool ok = true;
     uint32_t hw[8], lw[8];
+    float amax = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      uint16_t h0, l0, h1, l1;
-      f16_split_checked(v[2 * j], h0, l0, ok);
-      f16_split_checked(v[2 * j + 1], h1, l1, ok);
-      hw[j] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-      lw[j] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+      amax = fmaxf(amax, fmaxf(fabsf(v[2 * j]), fabsf(v[2 * j + 1])));
+      f16_split2(v[2 * j], v[2 * j + 1], hw[j], lw[j]);
     }
+    ok = amax <= 65504.f;
     if (!ok && row_in) raise_status(p.status, TT_ERR_DEVICE_RANGE, col0);
     const uint4 hq[2] = {make_uint4(hw[0], hw[1], hw[2], hw[3]), make_uint4(hw[4], hw[5], hw[6], hw[7])};
     const uint4 lq[2] = {make_uint4(lw[0], lw[1], lw[2], lw[3]), make_uint4(lw[4], lw[5], lw[6], lw[7])};
