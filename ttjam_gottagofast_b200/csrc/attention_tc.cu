@@ -26,9 +26,10 @@
 //             Vt_hi Vt_lo (HD dims x 64 keys, from the transposed copy of v the
 //             q|k|v GEMM writes) into the ring;
 //   warp 1    allocates / frees the tensor memory; then its lane 0 issues the
-//             MMAs: S_{j+1} = Q.K^T (A = Q from tensor memory, B = K tile) as
-//             soon as the softmax has read S_j, then O += P_j.V_j (A = P_j from
-//             tensor memory, B = Vt tile); both B operands are K-major;
+//             MMAs: S_j = Q.K^T (A = Q from tensor memory, B = K tile) into
+//             S/P buffer j % 2, two tiles ahead of the softmax, and
+//             O += P_j.V_j (A = P_j from the same buffer, B = Vt tile) once
+//             the softmax has written P_j; both B operands are K-major;
 //   warps 2-9 softmax, two warps per tensor-memory lane quarter: query row
 //             q0+t (= tensor-memory lane t) is shared by two threads, one per
 //             half of the 64-key tile; they exchange the row max through shared
@@ -55,7 +56,11 @@ constexpr int kSoftWarp0 = 2;  // first softmax warp
 // x HD fp16: rows of 2*HD bytes, 64-byte swizzle at HD 32, 128-byte at HD 64)
 // then Vt_hi, Vt_lo (HD rows x 64 keys: 128-byte rows, 128-byte swizzle).
 // Tensor-memory columns (32-bit cells; a 16-bit operand packs two values per
-// cell): Q_hi, Q_lo (HD/2 each), S (64), P = hi (32) | lo (32), O (HD).
+// cell): Q_hi, Q_lo (HD/2 each), two S/P buffers of 64 columns, O (HD). A
+// buffer holds the fp32 scores S of a 64-key tile, then the fp16 split of P
+// over the same columns: the softmax thread of key half kh writes P_hi of its
+// 32 keys to cells [32 kh, 32 kh + 16) and P_lo to [32 kh + 16, 32 kh + 32),
+// inside the scores it has read itself.
 template <int HD>
 struct AtShape {
   static constexpr uint32_t KROW = 2 * HD;              // bytes of one K row
@@ -63,8 +68,7 @@ struct AtShape {
   static constexpr uint32_t OPV = HD * 128;             // one V^T operand (hi or lo)
   static constexpr uint32_t STAGE = 2 * OPK + 2 * OPV;
   static constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE + 1024 + 256;
-  static constexpr uint32_t T_QHI = 0, T_QLO = HD / 2, T_S = HD, T_PHI = HD + 64,
-                            T_PLO = HD + 96, T_O = HD + 128;
+  static constexpr uint32_t T_QHI = 0, T_QLO = HD / 2, T_SP = HD, T_O = HD + 128;
   static constexpr uint32_t TMEM_COLS = 256;
   static_assert(T_O + HD <= TMEM_COLS, "tensor memory");
   static_assert(OPK % 1024 == 0 && OPV % 1024 == 0, "operands on the swizzle period");
@@ -205,7 +209,13 @@ __device__ __forceinline__ void tmem_wait_st() {
 // Two fp32 values -> their fp16 splits packed as (hi pair, lo pair), the
 // element with the lower index in the low 16 bits.
 __device__ __forceinline__ void split_pair(float a, float b, uint32_t &hi, uint32_t &lo) {
-  f16_split2(a, b, hi, lo);
+  f16_split2_rn(a, b, hi, lo);
+}
+// max(a, b, c) in one instruction (three-input max.f32, sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 // Named barrier of the two softmax warps that serve lane quarter q (ids 1-4,
@@ -242,12 +252,13 @@ __global__ void __maxnreg__(80)
   const uint32_t bars = base + STAGES * STAGE;
   auto kv_full = [&](int s) { return bars + 8u * s; };
   auto kv_empty = [&](int s) { return bars + 8u * (STAGES + s); };
-  const uint32_t s_full = bars + 8u * (2 * STAGES);      // S written
-  const uint32_t s_free = bars + 8u * (2 * STAGES + 1);  // ... and read by the softmax
-  const uint32_t p_full = bars + 8u * (2 * STAGES + 2);  // P written
-  const uint32_t o_done = bars + 8u * (2 * STAGES + 3);  // its P.V finished
-  const uint32_t q_ready = bars + 8u * (2 * STAGES + 4);
-  const uint32_t tmem_slot = bars + 8u * (2 * STAGES + 5);
+  // per S/P buffer b: S of its next tile written, P of that tile written
+  auto s_full = [&](int b) { return bars + 8u * (2 * STAGES + b); };
+  auto p_full = [&](int b) { return bars + 8u * (2 * STAGES + 2 + b); };
+  const uint32_t o_done = bars + 8u * (2 * STAGES + 4);   // a P.V finished
+  const uint32_t q_ready = bars + 8u * (2 * STAGES + 5);
+  const uint32_t o_final = bars + 8u * (2 * STAGES + 6);  // every MMA finished
+  const uint32_t tmem_slot = bars + 8u * (2 * STAGES + 7);
   uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -314,11 +325,13 @@ __global__ void __maxnreg__(80)
       mbar_init(kv_empty(s), 1);
     }
     // the 8 softmax warps arrive once per warp (an elected lane after __syncwarp)
-    mbar_init(s_full, 1);
-    mbar_init(s_free, 8);
-    mbar_init(p_full, 8);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(s_full(b), 1);
+      mbar_init(p_full(b), 8);
+    }
     mbar_init(o_done, 1);
     mbar_init(q_ready, 8);
+    mbar_init(o_final, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -348,14 +361,14 @@ __global__ void __maxnreg__(80)
     }
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer --------------------------------------------------------
+    // S_j goes to buffer j & 1. The tensor pipe runs one thread's MMAs in
+    // issue order, so S_{j+2}, issued after P_j.V_j, overwrites P_j only after
+    // that product has read it.
     auto issue_s = [&](int j) {
       const int s = j % STAGES;
       mbar_wait(kv_full(s), (j / STAGES) & 1, p.status, 0x4200 + j);
-      // S last held S_{j-1}; the softmax has copied it to registers
-      if (j >= 1) mbar_wait(s_free, (j - 1) & 1, p.status, 0x4300 + j);
-      fence_after();
       const uint32_t kst = base + s * STAGE;
-      const uint32_t sd = tm + Sh::T_S;
+      const uint32_t sd = tm + Sh::T_SP + 64u * (j & 1);
       // descriptors built once; a k-step of 16 dims advances the start address
       // by 32 bytes (2 units)
       const uint64_t khi0 = sdesc(kst, Sh::K_SBO, Sh::K_SWZ);
@@ -367,27 +380,33 @@ __global__ void __maxnreg__(80)
         mma_ts(sd, tm + T_QHI + 8u * kk, klo0 + koff, Sh::IDESC_S, 1);
         mma_ts(sd, tm + T_QLO + 8u * kk, khi0 + koff, Sh::IDESC_S, 1);
       }
-      mma_commit(s_full);
+      mma_commit(s_full(j & 1));
     };
     mbar_wait(q_ready, 0, p.status, 0x4000);
+    fence_after();
     issue_s(0);
+    if (nkv > 1) issue_s(1);
     for (int j = 0; j < nkv; ++j) {
-      if (j + 1 < nkv) issue_s(j + 1);  // next scores overlap this tile's softmax
-      const int s = j % STAGES;
-      mbar_wait(p_full, j & 1, p.status, 0x4400 + j);
+      const int s = j % STAGES, b = j & 1;
+      mbar_wait(p_full(b), (j >> 1) & 1, p.status, 0x4400 + j);
       fence_after();
       const uint32_t vst = base + s * STAGE + 2 * OPK;
       const uint64_t vhi0 = sdesc(vst, 1024, 2), vlo0 = sdesc(vst + OPV, 1024, 2);
+      const uint32_t pb = tm + Sh::T_SP + 64u * b;
 #pragma unroll
       for (int kk = 0; kk < BKV / 16; ++kk) {  // 16 keys per MMA
         const uint64_t voff = (uint64_t)(2 * kk);
-        mma_ts(tm + T_O, tm + Sh::T_PHI + 8u * kk, vhi0 + voff, Sh::IDESC_PV, (j | kk) != 0);
-        mma_ts(tm + T_O, tm + Sh::T_PHI + 8u * kk, vlo0 + voff, Sh::IDESC_PV, 1);
-        mma_ts(tm + T_O, tm + Sh::T_PLO + 8u * kk, vhi0 + voff, Sh::IDESC_PV, 1);
+        // keys 16 kk .. 16 kk + 15: P_hi at cells 32 (kk / 2) + 8 (kk % 2), P_lo 16 further
+        const uint32_t phi = pb + 32u * (kk >> 1) + 8u * (kk & 1);
+        mma_ts(tm + T_O, phi, vhi0 + voff, Sh::IDESC_PV, (j | kk) != 0);
+        mma_ts(tm + T_O, phi, vlo0 + voff, Sh::IDESC_PV, 1);
+        mma_ts(tm + T_O, phi + 16u, vhi0 + voff, Sh::IDESC_PV, 1);
       }
       mma_commit(o_done);
       mma_commit(kv_empty(s));
+      if (j + 2 < nkv) issue_s(j + 2);  // into the buffer P_j.V_j has just read
     }
+    mma_commit(o_final);
   } else if (warp >= kSoftWarp0) {
     // ---- softmax: rows split over two warpgroups by key half ----------------
     const int t = (warp & 3) * 32 + lane;   // row within the tile = tensor-memory lane
@@ -396,7 +415,6 @@ __global__ void __maxnreg__(80)
     const bool row_in = row < S;
     const uint32_t lane_base = tm + ((uint32_t)((warp & 3) * 32) << 16);
     const uint32_t col_off = 32u * kh;                 // this thread's 32 scores of a tile
-    const uint32_t pcol_off = 16u * kh;                // ... as 16 packed P cells
     const uint32_t dim_off = (uint32_t)(HD / 2) * kh;  // ... and HD/2 dims of O
     {
       // Q row -> tensor memory: this thread's dims [dim_off, dim_off + HD/2)
@@ -434,30 +452,38 @@ __global__ void __maxnreg__(80)
         ok = __ballot_sync(0xffffffffu, ka < kv_end && (mrow == nullptr || mrow[ka] != 0));
       }
       const bool diag = p.causal && k0 + 31 > q0;  // half reaches past the first query
-      mbar_wait(s_full, j & 1, p.status, 0x4500 + j);
+      // every key of this half allowed for every row of the warp (warp-uniform)
+      const bool open = !diag && ok == 0xffffffffu;
+      const uint32_t sp = lane_base + Sh::T_SP + 64u * sb + col_off;  // this thread's cells
+      mbar_wait(s_full(sb), (j >> 1) & 1, p.status, 0x4500 + j);
       fence_after();
       float sv[32];
-      tmem_ld16(lane_base + Sh::T_S + col_off, sv);
-      tmem_ld16(lane_base + Sh::T_S + col_off + 16, sv + 16);
+      tmem_ld16(sp, sv);
+      tmem_ld16(sp + 16, sv + 16);
       tmem_wait_ld();
-      fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_free);
-      // allowed keys of this half as one word: valid (ballot) and, on the
-      // diagonal, key k0 + c <= row, i.e. bits 0 .. row - k0 (one select per
-      // score below; a per-score && / || compiles to branches)
-      uint32_t allowed = ok;
-      if (diag) {
-        const int lim = row - k0;
-        allowed &= lim >= 31 ? 0xffffffffu : (lim < 0 ? 0u : (2u << lim) - 1u);
-      }
-      float mx4[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
+      if (!open) {
+        // allowed keys of this half as one word: valid (ballot) and, on the
+        // diagonal, key k0 + c <= row, i.e. bits 0 .. row - k0 (one select
+        // per score; a per-score && / || compiles to branches)
+        uint32_t allowed = ok;
+        if (diag) {
+          const int lim = row - k0;
+          allowed &= lim >= 31 ? 0xffffffffu : (lim < 0 ? 0u : (2u << lim) - 1u);
+        }
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        sv[c] = (allowed >> c) & 1u ? sv[c] * sl : -CUDART_INF_F;
-        mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
+        for (int c = 0; c < 32; ++c) sv[c] = (allowed >> c) & 1u ? sv[c] : -CUDART_INF_F;
       }
-      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      // row max of the raw scores (the log2-domain scale sl > 0 keeps the
+      // order), four chains of three-input maxima
+      float mx4[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        mx4[i] = fmax3(sv[i], sv[i + 4], sv[i + 8]);
+        mx4[i] = fmax3(mx4[i], sv[i + 12], sv[i + 16]);
+        mx4[i] = fmax3(mx4[i], sv[i + 20], sv[i + 24]);
+        mx4[i] = fmaxf(mx4[i], sv[i + 28]);
+      }
+      float mx = fmaxf(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3]) * sl;
       s_rowmax[sb][kh][t] = mx;
       // the two warps that share these 32 rows (one per key half)
       pair_barrier(warp & 3);
@@ -466,7 +492,8 @@ __global__ void __maxnreg__(80)
         const float alpha = fast_exp2(m_ref - mx);  // 0 when m_ref is -inf
         if (j > 0 && m_ref != -CUDART_INF_F) {
           // the context in tensor memory must hold P_{j-1}.V_{j-1} before it
-          // is rescaled
+          // is rescaled. S_j was committed after P_{j-2}.V_{j-2}, so o_done
+          // has completed j - 1 or j phases here and the parity wait is exact.
           mbar_wait(o_done, (j - 1) & 1, p.status, 0x4600 + j);
           fence_after();
 #pragma unroll
@@ -484,10 +511,12 @@ __global__ void __maxnreg__(80)
       }
       float ps4[4] = {0.f, 0.f, 0.f, 0.f};
       if (m_ref != -CUDART_INF_F) {
-        const float off = m_ref - kPScale;
+        // 2^7 p = 2^(s * sl - (m_ref - 7)): one fused multiply-add and one
+        // exponential per score; 0 for masked keys (s = -inf)
+        const float noff = kPScale - m_ref;
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          sv[c] = fast_exp2(sv[c] - off);  // 2^7 p; 0 for masked keys
+          sv[c] = fast_exp2(fmaf(sv[c], sl, noff));
           ps4[c & 3] += sv[c];
         }
       } else {
@@ -498,17 +527,13 @@ __global__ void __maxnreg__(80)
       uint32_t phi[16], plo[16];
 #pragma unroll
       for (int c = 0; c < 16; ++c) split_pair(sv[2 * c], sv[2 * c + 1], phi[c], plo[c]);
-      // P last held P_{j-1}: its P.V must be done before it is overwritten
-      if (j >= 1) {
-        mbar_wait(o_done, (j - 1) & 1, p.status, 0x4800 + j);
-        fence_after();
-      }
-      tmem_st16(lane_base + Sh::T_PHI + pcol_off, phi);
-      tmem_st16(lane_base + Sh::T_PLO + pcol_off, plo);
+      // P_j over the scores S_j this thread has read
+      tmem_st16(sp, phi);
+      tmem_st16(sp + 16, plo);
       tmem_wait_st();
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(p_full(sb));
     }
     // row sum = both halves' partial sums
     s_rowsum[kh][t] = l;
@@ -516,8 +541,9 @@ __global__ void __maxnreg__(80)
     l += s_rowsum[kh ^ 1][t];
     // context = O / l (this thread's HD/2 dims), written as an fp16 split (the
     // out_proj GEMM's A operand)
-    // the last P.V (the tensor pipe runs the MMAs in order, so all of them)
-    mbar_wait(o_done, (nkv - 1) & 1, p.status, 0x4700);
+    // every P.V finished (o_done can be two phases behind here, so the
+    // final commit has a barrier of its own)
+    mbar_wait(o_final, 0, p.status, 0x4700);
     fence_after();
     const float inv = l > 0.f ? 1.f / l : 0.f;
     const int64_t off = (b * S + (row_in ? row : 0)) * (int64_t)D + (int64_t)h * HD + dim_off;

@@ -83,6 +83,19 @@ __device__ __forceinline__ void f16_split2(float a, float b, uint32_t &hi, uint3
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(__fsub_rn(b, hb)), "f"(__fsub_rn(a, ha)));
 }
 
+// Same split with hi = x rounded to the nearest fp16 (cvt.rn), lo = the
+// exact fp32 remainder x - hi rounded to fp16: one pack, two widenings and two
+// subtractions per pair, against the Veltkamp split's three operations per
+// value for hi.
+__device__ __forceinline__ void f16_split2_rn(float a, float b, uint32_t &hi, uint32_t &lo) {
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(b), "f"(a));
+  float ha, hb;
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\tcvt.f32.f16 %0, l;\n\tcvt.f32.f16 %1, h;\n\t}"
+      : "=f"(ha), "=f"(hb)
+      : "r"(hi));
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(__fsub_rn(b, hb)), "f"(__fsub_rn(a, ha)));
+}
+
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
