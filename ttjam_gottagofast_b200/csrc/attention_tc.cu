@@ -107,20 +107,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return done != 0;
 }
-// Bounded wait: gives up after ~2^28 cycles, or at once when a wait anywhere
+// Bounded wait: gives up after ~2^28 cycles, or within 32 polls once a wait anywhere
 // in the launch already gave up.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, DeviceStatus *st,
                                           int detail) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (st != nullptr && *reinterpret_cast<volatile int32_t *>(&st->code) != 0) return false;
-    if (clock64() - t0 > (1LL << 28)) {
-      raise_status(st, TT_ERR_DEVICE_TIMEOUT, detail);
-      return false;
+  // the status word (a global load) is read every 32nd poll only, so that a
+  // completed phase is seen without a memory round trip in the way
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 31) == 0) {
+      if (st != nullptr && *reinterpret_cast<volatile int32_t *>(&st->code) != 0) return false;
+      if (clock64() - t0 > (1LL << 28)) {
+        raise_status(st, TT_ERR_DEVICE_TIMEOUT, detail);
+        return false;
+      }
     }
   }
-  return true;
 }
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *tm, int c0, int c1,
                                             int c2, uint32_t bar) {
@@ -209,13 +213,7 @@ __device__ __forceinline__ void tmem_wait_st() {
 // Two fp32 values -> their fp16 splits packed as (hi pair, lo pair), the
 // element with the lower index in the low 16 bits.
 __device__ __forceinline__ void split_pair(float a, float b, uint32_t &hi, uint32_t &lo) {
-  f16_split2_rn(a, b, hi, lo);
-}
-// max(a, b, c) in one instruction (three-input max.f32, sm_100)
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
+  f16_split2(a, b, hi, lo);
 }
 
 // Named barrier of the two softmax warps that serve lane quarter q (ids 1-4,

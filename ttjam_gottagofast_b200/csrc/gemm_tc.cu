@@ -23,7 +23,7 @@
 // (torch_transformer_benchmark.py:93-95), out_proj + residual (:118-121, :140),
 // ffn_in + GELU and ffn_out + residual (:141-144).
 //
-// Two persistent kernels, 384 threads, warp-specialised:
+// Two persistent kernels, 512 threads, warp-specialised:
 //   warp 0    TMA producer: per 32-wide k-block the operand tiles (A_hi, A_lo,
 //             W_hi, W_lo; rows of 64 bytes, 64-byte swizzle) into a ring that
 //             runs on across tiles;
@@ -32,13 +32,13 @@
 //             accumulators; tcgen05.commit frees the stage / hands the
 //             accumulator to the epilogue;
 //   warp 2    allocates / frees the tensor-memory columns;
-//   warps 4-11 epilogue: warp w reads tensor-memory lane quarter w%4 (tile row
-//             = lane) and column half (w-4)/4 with tcgen05.ld 32x32b, applies
+//   warps 4-15 epilogue: warp w reads tensor-memory lane quarter w%4 (tile row
+//             = lane) and column third (w-4)/4 with tcgen05.ld 32x32b, applies
 //             acc_scale, bias, GELU / residual / padded-row zeroing, then
 //             releases the accumulator -- so the epilogue of one tile overlaps
 //             the main loop of the next. Outputs leave through shared memory:
 //             each warp writes its 32-row x 16-column chunk (fp32, or the fp16
-//             split) to a staging buffer in the TMA swizzle pattern
+//             split) to one of its two staging slots in the TMA swizzle pattern
 //             (conflict-free) and one lane issues a TMA tensor store, which
 //             writes whole lines (a lane-per-row st.global would be 32
 //             partial-line writes per instruction).
@@ -62,8 +62,9 @@ constexpr int kThreads = 512;   // warps 0-3: TMA, MMA, TMEM; warps 4-15: epilog
 constexpr int kEpiWarps = 12;  // three per tensor-memory lane quarter
 constexpr uint32_t TILE_A = BM * BK * 2;               // 8 KB
 
-// Per epilogue warp: one staging buffer holding a 32 x 16 chunk of fp32 C
-// (2 KB) or of the fp16 split (1 KB hi at +0, 1 KB lo at +2 KB).
+// Per epilogue warp: two 2 KB staging slots, used by alternate chunks, each
+// holding a 32 x 16 chunk of fp32 C or of the fp16 split (1 KB hi at +0,
+// 1 KB lo at +1 KB).
 constexpr uint32_t STG_WARP = 4096;
 
 template <int BN>
@@ -102,20 +103,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return done != 0;
 }
 // Bounded wait: false (and a latched timeout) after ~2^28 cycles (~0.14 s),
-// or at once when an earlier wait anywhere in the launch already gave up, so
+// or within 32 polls once an earlier wait anywhere in the launch gave up, so
 // a broken pipeline costs one timeout, not one per CTA and k-block.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, DeviceStatus *st,
                                           int detail) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (st != nullptr && *reinterpret_cast<volatile int32_t *>(&st->code) != 0) return false;
-    if (clock64() - t0 > (1LL << 28)) {
-      raise_status(st, TT_ERR_DEVICE_TIMEOUT, detail);
-      return false;
+  // the status word (a global load) is read every 32nd poll only, so that a
+  // completed phase is seen without a memory round trip in the way
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 31) == 0) {
+      if (st != nullptr && *reinterpret_cast<volatile int32_t *>(&st->code) != 0) return false;
+      if (clock64() - t0 > (1LL << 28)) {
+        raise_status(st, TT_ERR_DEVICE_TIMEOUT, detail);
+        return false;
+      }
     }
   }
-  return true;
 }
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *tm, int c0, int c1,
                                             uint32_t bar) {
@@ -138,6 +143,10 @@ __device__ __forceinline__ void bulk_commit() {
 // Every bulk group committed so far has read its shared memory.
 __device__ __forceinline__ void bulk_wait_read_all() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Every bulk group but the most recent one has read its shared memory.
+__device__ __forceinline__ void bulk_wait_read_but_last() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
 }
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
@@ -200,6 +209,19 @@ __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Residual row segment R[row, col0 .. col0+15] (zeros outside the matrix).
+__device__ __forceinline__ void load_residual(const TcGemmParams &p, int row, bool row_in,
+                                              int col0, float4 (&r)[4]) {
+  const bool full = col0 + 16 <= p.N;
+  const int64_t off = (int64_t)row * p.ldc + col0;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    r[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (row_in && (full || col0 + 4 * u < p.N))
+      r[u] = *reinterpret_cast<const float4 *>(p.R + off + 4 * u);
+  }
+}
+
 // Epilogue values of one 16-column chunk of one row: bias, then GELU or the
 // residual with padded-row zeroing. v holds the accumulator values of
 // columns col0..col0+15 (col0 < N, a multiple of 16).
@@ -219,11 +241,11 @@ __device__ __forceinline__ void epilogue_values(const TcGemmParams &p, float acc
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = gelu_erf(v[j]);
   } else if (p.epilogue == EPI_BIAS_RESIDUAL) {
-    const int64_t off = (int64_t)row * p.ldc + col0;
+    float4 r[4];
+    load_residual(p, row, row_in, col0, r);
 #pragma unroll
     for (int j = 0; j < 16; j += 4) {
-      float4 r4 = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (row_in && (full || col0 + j < p.N)) r4 = *reinterpret_cast<const float4 *>(p.R + off + j);
+      const float4 r4 = r[j / 4];
       v[j + 0] = valid ? r4.x + v[j + 0] : 0.f;
       v[j + 1] = valid ? r4.y + v[j + 1] : 0.f;
       v[j + 2] = valid ? r4.z + v[j + 2] : 0.f;
@@ -282,8 +304,8 @@ __device__ __forceinline__ void stage_row(uint8_t *buf, int lane, const float4 (
 
 // One 16-column chunk of a warp's 32 rows through the epilogue: values (bias,
 // GELU / residual), then out -- transposed value columns by direct stores,
-// everything else through this warp's staging buffers (stg, two 2 KB halves)
-// and a TMA tensor store: fp32 C or the fp16 split H.
+// everything else through one of this warp's two staging slots and a TMA
+// tensor store: fp32 C or the fp16 split H.
 __device__ __forceinline__ void epilogue_chunk_out(const TcGemmParams &p, const CUtensorMap *tm_c,
                                                    const CUtensorMap *tm_hi,
                                                    const CUtensorMap *tm_lo, uint32_t stg_base,
@@ -297,10 +319,12 @@ __device__ __forceinline__ void epilogue_chunk_out(const TcGemmParams &p, const 
     if (row_in) store_vt(p, row, col0, v);
     return;
   }
-  // this warp's previous store must have read the staging buffer
-  const uint32_t stg = stg_base;
-  uint8_t *stg_ptr = stg_ptr_base;
-  if (lane == 0) bulk_wait_read_all();
+  // slot nstores % 2; the store that used it last (two chunks back) must have
+  // read it, the previous chunk's store may still be reading the other slot
+  const uint32_t slot = (uint32_t)(nstores & 1) * 2048u;
+  const uint32_t stg = stg_base + slot;
+  uint8_t *stg_ptr = stg_ptr_base + slot;
+  if (lane == 0) bulk_wait_read_but_last();
   __syncwarp();
   if (p.H_hi != nullptr) {
     bool ok = true;
@@ -308,7 +332,7 @@ __device__ __forceinline__ void epilogue_chunk_out(const TcGemmParams &p, const 
     float amax = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      amax = fmaxf(amax, fmaxf(fabsf(v[2 * j]), fabsf(v[2 * j + 1])));
+      amax = fmax3(amax, fabsf(v[2 * j]), fabsf(v[2 * j + 1]));
       f16_split2(v[2 * j], v[2 * j + 1], hw[j], lw[j]);
     }
     ok = amax <= 65504.f;
@@ -316,7 +340,7 @@ __device__ __forceinline__ void epilogue_chunk_out(const TcGemmParams &p, const 
     const uint4 hq[2] = {make_uint4(hw[0], hw[1], hw[2], hw[3]), make_uint4(hw[4], hw[5], hw[6], hw[7])};
     const uint4 lq[2] = {make_uint4(lw[0], lw[1], lw[2], lw[3]), make_uint4(lw[4], lw[5], lw[6], lw[7])};
     stage_row16(stg_ptr, lane, hq);
-    stage_row16(stg_ptr + 2048, lane, lq);
+    stage_row16(stg_ptr + 1024, lane, lq);
   } else {
     float4 oq[4];
 #pragma unroll
@@ -330,7 +354,7 @@ __device__ __forceinline__ void epilogue_chunk_out(const TcGemmParams &p, const 
     // rows past M and columns past N are clipped by the store
     if (p.H_hi != nullptr) {
       tma_store_2d(tm_hi, stg, col0, row0);
-      tma_store_2d(tm_lo, stg + 2048, col0, row0);
+      tma_store_2d(tm_lo, stg + 1024, col0, row0);
     } else {
       tma_store_2d(tm_c, stg, col0, row0);
     }
@@ -497,31 +521,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 
 // ---- CTA-pair variant (tcgen05 cta_group::2) ----------------------------------
-// A cluster of two CTAs computes a 256 x 256 output tile: CTA r of the pair owns
-// rows m0 + 128 r (its A rows) and W rows n0 + 128 r (its half of the B
-// operand), both loaded by its own TMA into its own shared memory. One thread of
-// CTA 0 issues M256 x N256 x K8 MMAs that read both CTAs' operands and leave
-// each CTA's 128 rows in that CTA's tensor memory. A stage is 32 KB per CTA
-// (A_hi, A_lo, W half hi, lo) against 48 KB for the same MMA work in the
-// single-CTA kernel -- a third less L2 -> SM traffic, the limit measured there --
-// and six stages fit. Barriers: a stage's loads in both CTAs complete their
-// bytes on CTA 0's full barrier (TMA .cta_group::2); CTA 0's MMA thread commits
-// each stage to the empty barrier of both CTAs and each accumulator to the
+// A cluster of two CTAs computes a 256 x PBN output tile (PBN 256): CTA r of the pair owns
+// rows m0 + 128 r (its A rows) and W rows n0 + (PBN / 2) r (its half of the B
+// operand), both loaded by its own TMA into its own shared memory. One thread
+// of CTA 0 issues M256 x N PBN x K16 MMAs that read both CTAs' operands and
+// leave each CTA's 128 rows in that CTA's tensor memory. A stage is 32 KB per
+// CTA at PBN 256 (A_hi, A_lo, W half hi, lo) against 48 KB for the same MMA
+// work in the single-CTA kernel -- a third less L2 -> SM traffic, the limit
+// measured there. Barriers: a stage's loads in both CTAs complete their bytes
+// on CTA 0's full barrier (TMA .cta_group::2); CTA 0's MMA thread commits each
+// stage to the empty barrier of both CTAs and each accumulator to the
 // acc_full barrier of both (one commit per CTA); both CTAs' epilogue warps
 // release an accumulator on CTA 0's acc_empty barrier. Each CTA's loads fill
 // only its own shared memory.
-constexpr int PSTAGES = 5;
-constexpr int PBN = 256;                                    // pair tile N (128 per CTA in smem)
-constexpr uint32_t P_TILE = 128 * BK * 2;                   // 8 KB: A rows or W half rows
-constexpr uint32_t P_STAGE = 4 * P_TILE;                    // A_hi, A_lo, W_hi half, W_lo half
-constexpr uint32_t P_STG_OFF = PSTAGES * P_STAGE;
-constexpr uint32_t P_BAR_OFF = P_STG_OFF + kEpiWarps * STG_WARP;
-constexpr size_t P_SMEM = (size_t)P_BAR_OFF + 256 + 1024;
-constexpr uint32_t P_TMEM_COLS = 2 * PBN;                   // two 256-column accumulators
-constexpr uint32_t P_IDESC = (1u << 4) | ((uint32_t)(PBN >> 3) << 17) |
-                             ((uint32_t)(256 >> 4) << 24);  // kind::f16: D fp32, A/B fp16 K-major, M 256
-static_assert(P_SMEM <= 227 * 1024, "shared memory");
-static_assert(P_STG_OFF % 1024 == 0, "staging buffers on the swizzle period");
+template <int PBN>
+struct PairShape {
+  static constexpr int STAGES = PBN == 256 ? 5 : 6;
+  static constexpr uint32_t TILE_A = 128 * BK * 2;               // 8 KB: 128 A rows
+  static constexpr uint32_t TILE_W = (PBN / 2) * BK * 2;         // the CTA's W rows
+  static constexpr uint32_t STAGE = 2 * TILE_A + 2 * TILE_W;     // A_hi, A_lo, W_hi, W_lo
+  static constexpr uint32_t STG_OFF = STAGES * STAGE;
+  static constexpr uint32_t BAR_OFF = STG_OFF + kEpiWarps * STG_WARP;
+  static constexpr size_t SMEM = (size_t)BAR_OFF + 256 + 1024;
+  static constexpr uint32_t TMEM_COLS = 512;                      // two PBN-column accumulators
+  static constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(PBN >> 3) << 17) |
+                                    ((uint32_t)(256 >> 4) << 24);  // kind::f16, fp32 D, M 256
+  static_assert(PBN % 32 == 0 && 2 * PBN <= (int)TMEM_COLS, "tile width");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(STG_OFF % 1024 == 0 && STAGE % 1024 == 0 && TILE_W % 512 == 0,
+                "operands and staging buffers on the swizzle period");
+};
 
 __device__ __forceinline__ uint32_t cta_rank_in_cluster() {
   uint32_t r;
@@ -568,6 +597,7 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
                : "memory");
 }
 
+template <int PBN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc3_pair_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                          const __grid_constant__ CUtensorMap tm_a_lo,
@@ -576,10 +606,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                          const __grid_constant__ CUtensorMap tm_c,
                          const __grid_constant__ CUtensorMap tm_c_hi,
                          const __grid_constant__ CUtensorMap tm_c_lo, const TcGemmParams p) {
+  using Sh = PairShape<PBN>;
+  constexpr int PSTAGES = Sh::STAGES;
+  constexpr uint32_t P_STAGE = Sh::STAGE, P_TILE = Sh::TILE_A, P_TMEM_COLS = Sh::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;  // same offset in both CTAs
-  const uint32_t bars = base + P_BAR_OFF;
+  const uint32_t bars = base + Sh::BAR_OFF;
   auto full_bar = [&](int s) { return bars + 8u * s; };
   auto empty_bar = [&](int s) { return bars + 8u * (PSTAGES + s); };
   auto acc_full = [&](int b) { return bars + 8u * (2 * PSTAGES + b); };
@@ -624,7 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int it = 0;
     for (int tile = pair; tile < ntiles; tile += npairs) {
       const int m0 = (tile / NT) * 256 + 128 * (int)rank;
-      const int n0 = (tile % NT) * PBN + 128 * (int)rank;
+      const int n0 = (tile % NT) * PBN + (PBN / 2) * (int)rank;
       for (int kb = 0; kb < KB; ++kb, ++it) {
         const int s = it % PSTAGES, n = it / PSTAGES;
         if (it >= PSTAGES) mbar_wait(empty_bar(s), (n - 1) & 1, p.status, 0x1100);
@@ -634,7 +667,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d_pair(st, &tm_a_hi, kb * BK, m0, fb);
         tma_load_2d_pair(st + P_TILE, &tm_a_lo, kb * BK, m0, fb);
         tma_load_2d_pair(st + 2 * P_TILE, &tm_w_hi, kb * BK, n0, fb);
-        tma_load_2d_pair(st + 3 * P_TILE, &tm_w_lo, kb * BK, n0, fb);
+        tma_load_2d_pair(st + 2 * P_TILE + Sh::TILE_W, &tm_w_lo, kb * BK, n0, fb);
       }
     }
     // every stage's last release (a commit from CTA 0) has arrived before this
@@ -658,13 +691,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t st = base + s * P_STAGE;
         const uint64_t a_hi = umma_desc_sw64(st), a_lo = umma_desc_sw64(st + P_TILE);
         const uint64_t w_hi = umma_desc_sw64(st + 2 * P_TILE);
-        const uint64_t w_lo = umma_desc_sw64(st + 3 * P_TILE);
+        const uint64_t w_lo = umma_desc_sw64(st + 2 * P_TILE + Sh::TILE_W);
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k) {
           const uint64_t ko = (uint64_t)(k * 2);
-          umma_f16_pair(acc, a_hi + ko, w_hi + ko, P_IDESC, (kb | k) != 0);
-          umma_f16_pair(acc, a_hi + ko, w_lo + ko, P_IDESC, 1);
-          umma_f16_pair(acc, a_lo + ko, w_hi + ko, P_IDESC, 1);
+          umma_f16_pair(acc, a_hi + ko, w_hi + ko, Sh::IDESC, (kb | k) != 0);
+          umma_f16_pair(acc, a_hi + ko, w_lo + ko, Sh::IDESC, 1);
+          umma_f16_pair(acc, a_lo + ko, w_hi + ko, Sh::IDESC, 1);
         }
         umma_commit_pair(map_to_cta(empty_bar(s), 0));  // stage s free in both CTAs
         umma_commit_pair(peer_empty0 + 8u * s);
@@ -678,7 +711,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // column third of the tile, in 16-column chunks
     const int cgrp = (warp - 4) >> 2;
     const int c_lo = 16 * (cgrp * (PBN / 16) / 3), c_hi = 16 * ((cgrp + 1) * (PBN / 16) / 3);
-    const uint32_t stg = base + P_STG_OFF + (uint32_t)(warp - 4) * STG_WARP;
+    const uint32_t stg = base + Sh::STG_OFF + (uint32_t)(warp - 4) * STG_WARP;
     uint8_t *stg_ptr = smem_raw + (stg - raw);
     const float acc_scale = *p.acc_scale;
     int nstores = 0;  // bulk store groups this warp has committed
@@ -836,20 +869,22 @@ int launch_bn(const TcGemmParams &p, cudaStream_t stream) {
   return TT_OK;
 }
 
+template <int PBN>
 int launch_pair(const TcGemmParams &p, cudaStream_t stream, int sms) {
+  using Sh = PairShape<PBN>;
   CUtensorMap ta_hi, ta_lo, tw_hi, tw_lo;
   int rc;
   if ((rc = make_operand_map(&ta_hi, p.A_hi, p.M, p.K, p.lda, 128)) ||
       (rc = make_operand_map(&ta_lo, p.A_lo, p.M, p.K, p.lda, 128)) ||
-      (rc = make_operand_map(&tw_hi, p.W_hi, p.N, p.K, p.K, 128)) ||
-      (rc = make_operand_map(&tw_lo, p.W_lo, p.N, p.K, p.K, 128)))
+      (rc = make_operand_map(&tw_hi, p.W_hi, p.N, p.K, p.K, PBN / 2)) ||
+      (rc = make_operand_map(&tw_lo, p.W_lo, p.N, p.K, p.K, PBN / 2)))
     return rc;
   CUtensorMap tc, tc_hi, tc_lo;
   if ((rc = make_out_maps(p, ta_hi, &tc, &tc_hi, &tc_lo))) return rc;
   static bool attr_set = false;
   if (!attr_set) {
-    TT_CUDA_TRY(cudaFuncSetAttribute(gemm_tc3_pair_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P_SMEM));
+    TT_CUDA_TRY(cudaFuncSetAttribute(gemm_tc3_pair_kernel<PBN>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Sh::SMEM));
     attr_set = true;
   }
   const int64_t tiles = (int64_t)((p.M + 255) / 256) * ((p.N + PBN - 1) / PBN);
@@ -857,7 +892,7 @@ int launch_pair(const TcGemmParams &p, cudaStream_t stream, int sms) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * pairs));
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = P_SMEM;
+  cfg.dynamicSmemBytes = Sh::SMEM;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -866,8 +901,8 @@ int launch_pair(const TcGemmParams &p, cudaStream_t stream, int sms) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  TT_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_tc3_pair_kernel, ta_hi, ta_lo, tw_hi, tw_lo, tc, tc_hi,
-                                 tc_lo, p));
+  TT_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_tc3_pair_kernel<PBN>, ta_hi, ta_lo, tw_hi, tw_lo, tc,
+                                 tc_hi, tc_lo, p));
   TT_LAUNCH_CHECK("gemm_tc3_pair");
   return TT_OK;
 }
@@ -904,9 +939,11 @@ int launch_gemm_tc3(const TcGemmParams &p, cudaStream_t stream) {
   // (measured on B200: M 16384 x N 512 x K 2048, 1.7 waves of pairs, beats
   // 3.5 waves of single-CTA 128 x 128 tiles)
   const int sms = sm_count();
-  const int64_t pair_tiles = (int64_t)((p.M + 255) / 256) * ((p.N + PBN - 1) / PBN);
-  if (pair_tiles >= sms / 2)
-    return launch_pair(p, stream, sms);
+  const int64_t mt = (p.M + 255) / 256;
+  const int64_t pair_tiles = mt * ((p.N + 255) / 256);
+  // (192-wide pair tiles, which fill the last wave of M 16384 x N 1536 better,
+  // measured slower on B200: 70% of the MMA rate in the main loop against 84%)
+  if (pair_tiles >= sms / 2) return launch_pair<256>(p, stream, sms);
   // N = 256 tiles halve the shared-memory operand traffic per FLOP; narrow
   // projections use 128-wide tiles so every SM still gets work
   const int64_t tiles256 = (int64_t)((p.M + BM - 1) / BM) * ((p.N + 255) / 256);

@@ -53,47 +53,39 @@ __device__ __forceinline__ float gelu_erf(float v) {
 }
 
 // fp16 split used by the tensor-core path (binary16 bit patterns): hi = x
-// rounded to 11 significant bits, lo = x - hi (exact in fp32) rounded to fp16;
-// hi + lo carries about 22 significant bits while |x| <= 65504 (a larger |x|
-// gives an infinite hi). hi comes from Veltkamp's splitting (Dekker 1971, "A
-// floating-point technique for extending the available precision"): with
-// c = x * (2^13 + 1), hi = c - (c - x) keeps the top 24 - 13 = 11 bits, so it
-// converts to fp16 exactly (above the fp16 subnormal range) and no fp16 -> fp32
-// conversion is needed. The _rn intrinsics keep the three operations from
-// being contracted into fused multiply-adds, which would break the split.
-__device__ __forceinline__ float split_hi11(float x) {
-  const float c = __fmul_rn(x, 8193.0f);
-  return __fsub_rn(c, __fsub_rn(c, x));
-}
+// rounded to the nearest fp16 (cvt.rn), lo = x - hi, exact in fp32 (hi is x
+// rounded to 11 significant bits), rounded to fp16. hi + lo carries about 22
+// significant bits while |x| <= 65504; a larger |x| gives an infinite hi. For
+// a pair: one pack, two widenings, two subtractions and one pack.
 __device__ __forceinline__ uint16_t f16_bits(float x) {
   uint16_t h;
   asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(x));
   return h;
 }
+__device__ __forceinline__ float f16_value(uint16_t h) {
+  float x;
+  asm("cvt.f32.f16 %0, %1;" : "=f"(x) : "h"(h));
+  return x;
+}
 __device__ __forceinline__ void f16_split(float x, uint16_t &hi, uint16_t &lo) {
-  const float h = split_hi11(x);
-  hi = f16_bits(h);
-  lo = f16_bits(__fsub_rn(x, h));
+  hi = f16_bits(x);
+  lo = f16_bits(__fsub_rn(x, f16_value(hi)));
 }
 // Two values at once: hi and lo pieces packed as fp16 pairs, the element
 // with the lower index (a) in the low 16 bits.
 __device__ __forceinline__ void f16_split2(float a, float b, uint32_t &hi, uint32_t &lo) {
-  const float ha = split_hi11(a), hb = split_hi11(b);
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(hb), "f"(ha));
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(__fsub_rn(b, hb)), "f"(__fsub_rn(a, ha)));
-}
-
-// Same split with hi = x rounded to the nearest fp16 (cvt.rn), lo = the
-// exact fp32 remainder x - hi rounded to fp16: one pack, two widenings and two
-// subtractions per pair, against the Veltkamp split's three operations per
-// value for hi.
-__device__ __forceinline__ void f16_split2_rn(float a, float b, uint32_t &hi, uint32_t &lo) {
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(b), "f"(a));
   float ha, hb;
   asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\tcvt.f32.f16 %0, l;\n\tcvt.f32.f16 %1, h;\n\t}"
       : "=f"(ha), "=f"(hb)
       : "r"(hi));
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(__fsub_rn(b, hb)), "f"(__fsub_rn(a, ha)));
+}
+// max(a, b, c) in one instruction (three-input max.f32, sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
