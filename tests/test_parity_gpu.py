@@ -243,3 +243,69 @@ def test_launch_probe_brackets_every_launch(name, plan):
            else per_layer * cfg.num_layers + ["final_norm"])
     assert names == one * 2
     assert all(t > 0 for t in ms)
+
+
+@pytest.mark.parametrize("name,plan", [("A", "ops_tc"), ("A", "ops_ffma"), ("C", "ops_tc")])
+def test_graph_replay_matches_direct_launch(name, plan):
+    """From the second call with the same pointers on, the per-op schedules
+    replay a cached CUDA graph. A replay computes from the buffers' current
+    contents and is bit-identical to a direct launch (the launch probe forces
+    direct launches)."""
+    import ctypes
+    from ttjam_gottagofast_b200 import _lib
+    cfg = WORKLOADS[name].config
+    model, _ = model_for(cfg)
+    lib = model._lib
+    x1, m1 = generate_random_case(cfg, "cpu", torch.float32, 11, 0.25, 1.0)
+    x2, m2 = generate_random_case(cfg, "cpu", torch.float32, 12, 0.25, 1.0)
+    b, s = x1.shape[:2]
+    c = _lib.make_config(model.config, plan)
+    image = model._ensure_image(torch.device(DEV))
+    x, m = x1.to(DEV), m1.to(DEV)
+    y = torch.empty_like(x)
+    ws_bytes = lib.tt_workspace_bytes(ctypes.byref(c), b, s)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=DEV)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def fwd():
+        assert lib.tt_forward(ctypes.byref(c), image.data_ptr(), x.data_ptr(), m.data_ptr(), b, s,
+                              y.data_ptr(), ws.data_ptr(), ws_bytes, stream) == 0
+        return y.clone()
+
+    outs = [fwd() for _ in range(4)]  # direct, capture + replay, replay, replay
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    x.copy_(x2.to(DEV))
+    m.copy_(m2.to(DEV))
+    got = fwd()  # the same graph, new buffer contents
+    assert lib.tt_launch_probe_start(1000) == 0
+    try:
+        ref = fwd()
+    finally:
+        lib.tt_launch_probe_start(0)
+    assert torch.equal(got, ref)
+    assert not torch.equal(got, outs[0])
+    torch.cuda.synchronize()
+    assert model.read_device_status() == (0, 0)
+
+
+def test_forward_inside_caller_graph_capture():
+    """A caller capturing its stream gets the forward's launches in its own
+    graph (the library's graph cache stays out of the way)."""
+    cfg = WORKLOADS["A"].config
+    model, _ = model_for(cfg)
+    x, m = generate_random_case(cfg, "cpu", torch.float32, 13, 0.25, 1.0)
+    x, m = x.to(DEV), m.to(DEV)
+    with torch.inference_mode():
+        ref = model(x, m)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side), torch.inference_mode():
+        model(x, m)
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g), torch.inference_mode():
+        out = model(x, m)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)

@@ -1,5 +1,6 @@
 // C ABI of the forward pass: config validation, model-image packing and the
 // forward schedule. Declared in include/ttjam_b200.h.
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -15,6 +16,14 @@ namespace tt {
 static thread_local std::string g_last_error;
 
 void set_last_error(const std::string &msg) { g_last_error = msg; }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char *e = std::getenv("TT_PDL");
+    return e == nullptr || std::strcmp(e, "0") != 0;
+  }();
+  return on;
+}
 
 namespace {
 
@@ -93,6 +102,38 @@ int timed_launch(int kind, cudaStream_t stream, F &&launch) {
 }
 
 }  // namespace
+
+bool launch_probe_active() {
+  const LaunchProbe &pr = g_probe;
+  return pr.count < pr.capacity();
+}
+
+ForwardKey make_forward_key(const tt_config &cfg, int plan, const void *image, const float *x,
+                            const uint8_t *mask, int64_t batch, int64_t seq, const float *y,
+                            const void *scratch) {
+  ForwardKey k;
+  std::memset(&k, 0, sizeof(k));
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    dev = -1;
+  }
+  k.device = dev;
+  k.d_model = cfg.d_model;
+  k.num_heads = cfg.num_heads;
+  k.ffn_dim = cfg.ffn_dim;
+  k.num_layers = cfg.num_layers;
+  k.causal = cfg.causal;
+  k.plan = plan;
+  k.batch = batch;
+  k.seq = seq;
+  k.image = reinterpret_cast<uint64_t>(image);
+  k.x = reinterpret_cast<uint64_t>(x);
+  k.mask = reinterpret_cast<uint64_t>(mask);
+  k.y = reinterpret_cast<uint64_t>(y);
+  k.scratch = reinterpret_cast<uint64_t>(scratch);
+  return k;
+}
 
 int validate_config(const tt_config *cfg) {
   if (cfg == nullptr) return fail(TT_ERR_INVALID_ARGUMENT, "config is NULL");
@@ -435,11 +476,15 @@ int tt_forward(const tt_config *cfg, const void *image, const float *x, const ui
   if (workspace_bytes < W.total || (W.total > 0 && workspace == nullptr))
     return fail(TT_ERR_WORKSPACE, "tt_forward: workspace smaller than tt_workspace_bytes (" +
                                       std::to_string(W.total) + " bytes)");
-  if (plan == PLAN_OPS_TC)
-    return forward_ops_tc(*cfg, L, static_cast<const char *>(image), x, mask, batch, seq, y, W,
-                          static_cast<char *>(workspace), stream);
-  return forward_ops(*cfg, L, static_cast<const char *>(image), x, mask, batch, seq, y, W,
-                     static_cast<char *>(workspace), stream);
+  const char *img = static_cast<const char *>(image);
+  char *ws = static_cast<char *>(workspace);
+  const tt_config c = *cfg;
+  return run_forward_cached(
+      make_forward_key(c, plan, image, x, mask, batch, seq, y, workspace), stream,
+      [&](cudaStream_t s) {
+        return plan == PLAN_OPS_TC ? forward_ops_tc(c, L, img, x, mask, batch, seq, y, W, ws, s)
+                                   : forward_ops(c, L, img, x, mask, batch, seq, y, W, ws, s);
+      });
 }
 
 int tt_read_status(const tt_config *cfg, const void *image, int32_t *code, int32_t *detail,

@@ -38,6 +38,8 @@ __global__ void __launch_bounds__(kThreads) attention_ffma_kernel(AttentionParam
   float *sV = sK + BKV * G * PS;          // [BKV][G][PS]
   float *sOk = sV + BKV * G * PS;         // [BKV] key allowed by the padding mask
   __shared__ int s_kv_len;
+  pdl_trigger();
+  pdl_wait();
 
   const int S = p.seq, D = p.d_model, hd = p.head_dim;
   const int64_t ld = 3LL * D;
@@ -179,17 +181,20 @@ int launch_hd(const AttentionParams &p, bool vec, cudaStream_t stream) {
   using Sh = AttnShape<HDT>;
   dim3 grid((unsigned)ceil_div(p.seq, Sh::BQ), (unsigned)p.num_heads, (unsigned)p.batch);
   const size_t smem = Sh::smem_bytes;
-  if (vec) {
-    auto fn = attention_ffma_kernel<HDT, true>;
-    if (smem > 48 * 1024)
-      TT_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    fn<<<grid, kThreads, smem, stream>>>(p);
-  } else {
-    auto fn = attention_ffma_kernel<HDT, false>;
-    if (smem > 48 * 1024)
-      TT_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    fn<<<grid, kThreads, smem, stream>>>(p);
+  static bool attr_set = false;
+  if (!attr_set && smem > 48 * 1024) {
+    TT_CUDA_TRY(cudaFuncSetAttribute(attention_ffma_kernel<HDT, true>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    TT_CUDA_TRY(cudaFuncSetAttribute(attention_ffma_kernel<HDT, false>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   }
+  attr_set = true;
+  if (vec)
+    TT_CUDA_TRY(launch_kernel(attention_ffma_kernel<HDT, true>, grid, dim3(kThreads), smem, stream,
+                              1, p));
+  else
+    TT_CUDA_TRY(launch_kernel(attention_ffma_kernel<HDT, false>, grid, dim3(kThreads), smem, stream,
+                              1, p));
   TT_LAUNCH_CHECK("attention_ffma");
   return TT_OK;
 }

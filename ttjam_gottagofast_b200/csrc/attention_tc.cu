@@ -272,26 +272,7 @@ __global__ void __maxnreg__(80)
   const int q0 = qt * BQ;
   const uint8_t *mrow = p.mask ? p.mask + b * S : nullptr;
 
-  // The softmax threads' Q row (fp16 split, HD/2 dims each: HD/4 packed cells)
-  // and the mask bytes are requested together, so the prologue pays one
-  // memory latency.
-  uint32_t qv[2][HD / 4];
-  if (warp >= kSoftWarp0) {
-    const int t = (warp & 3) * 32 + lane, kh = (warp - kSoftWarp0) >> 2;
-    const int row = q0 + t;
-    const int64_t qoff = (b * S + (row < S ? row : 0)) * (int64_t)(2 * D) + (int64_t)h * HD +
-                         (HD / 2) * kh;
-#pragma unroll
-    for (int which = 0; which < 2; ++which) {
-      const uint4 *src = reinterpret_cast<const uint4 *>((which ? p.qk_lo : p.qk_hi) + qoff);
-#pragma unroll
-      for (int i = 0; i < HD / 16; ++i) {
-        const uint4 x = row < S ? src[i] : make_uint4(0u, 0u, 0u, 0u);
-        qv[which][4 * i] = x.x; qv[which][4 * i + 1] = x.y;
-        qv[which][4 * i + 2] = x.z; qv[which][4 * i + 3] = x.w;
-      }
-    }
-  }
+  pdl_trigger();
   // kv_len = 1 + last valid key; keys at or after it are all padding
   if (threadIdx.x == 0) s_kv_len = mrow ? 0 : S;
   __syncthreads();
@@ -342,7 +323,26 @@ __global__ void __maxnreg__(80)
   __syncthreads();
   fence_after();
   const uint32_t tm = *tmem_slot_ptr;
+  pdl_wait();  // q|k and v^T come from the previous kernel (the mask is the caller's input)
 
+  // The softmax threads' Q row (fp16 split, HD/2 dims each: HD/4 packed cells).
+  uint32_t qv[2][HD / 4];
+  if (warp >= kSoftWarp0) {
+    const int t = (warp & 3) * 32 + lane, kh = (warp - kSoftWarp0) >> 2;
+    const int row = q0 + t;
+    const int64_t qoff = (b * S + (row < S ? row : 0)) * (int64_t)(2 * D) + (int64_t)h * HD +
+                         (HD / 2) * kh;
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+      const uint4 *src = reinterpret_cast<const uint4 *>((which ? p.qk_lo : p.qk_hi) + qoff);
+#pragma unroll
+      for (int i = 0; i < HD / 16; ++i) {
+        const uint4 x = row < S ? src[i] : make_uint4(0u, 0u, 0u, 0u);
+        qv[which][4 * i] = x.x; qv[which][4 * i + 1] = x.y;
+        qv[which][4 * i + 2] = x.z; qv[which][4 * i + 3] = x.w;
+      }
+    }
+  }
   if (warp == 0 && lane == 0) {
     // ---- TMA producer: K/V tiles -------------------------------------------
     const int kcol = D + h * HD;  // first k column (fp16 elements) of this head
@@ -650,7 +650,8 @@ int launch_hd(const AttentionTcParams &p, const CUtensorMap &thi, const CUtensor
   }
   const int64_t ctas = (int64_t)((p.seq + BQ - 1) / BQ) * p.num_heads * p.batch;
   dim3 grid((unsigned)ctas);
-  attention_tc_kernel<HD><<<grid, kThreads, Sh::SMEM_BYTES, stream>>>(thi, tlo, tvhi, tvlo, p);
+  TT_CUDA_TRY(launch_kernel(attention_tc_kernel<HD>, grid, dim3(kThreads), Sh::SMEM_BYTES, stream,
+                            1, thi, tlo, tvhi, tvlo, p));
   TT_LAUNCH_CHECK("attention_tc");
   return TT_OK;
 }

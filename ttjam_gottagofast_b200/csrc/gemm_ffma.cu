@@ -35,6 +35,8 @@ __global__ void __launch_bounds__(kThreads) gemm_ffma_kernel(GemmParams p) {
   __shared__ __align__(16) float As[2][kBK][BM + 4];
   __shared__ __align__(16) float Ws[2][kBK][BN + 4];
   __shared__ float s_mean[BM], s_rstd[BM];
+  pdl_trigger();
+  pdl_wait();
 
   const int tid = threadIdx.x;
   const int tx = tid & 15, ty = tid >> 4;
@@ -233,6 +235,8 @@ __device__ __forceinline__ void cp_async16_zfill(void *dst, const void *src, boo
 
 __global__ void __launch_bounds__(kThreads) gemm_ffma_wholek_kernel(GemmParams p) {
   extern __shared__ __align__(16) float wk_smem[];
+  pdl_trigger();
+  pdl_wait();
   const int K = p.K, N = p.N;
   const int KS = K + 4;                     // padded row stride: conflict-free float4 rows
   float *sA = wk_smem;                      // [64][KS]
@@ -316,18 +320,19 @@ int launch_wholek(const GemmParams &p, cudaStream_t stream) {
     attr = smem;
   }
   dim3 grid((unsigned)ceil_div(p.N, WK_TILE), (unsigned)ceil_div(p.M, WK_TILE));
-  gemm_ffma_wholek_kernel<<<grid, kThreads, smem, stream>>>(p);
+  TT_CUDA_TRY(launch_kernel(gemm_ffma_wholek_kernel, grid, dim3(kThreads), smem, stream, 1, p));
   TT_LAUNCH_CHECK("gemm_ffma_wholek");
   return TT_OK;
 }
 
 template <int BM, int BN>
-void launch_tile(const GemmParams &p, bool vec, cudaStream_t stream) {
+int launch_tile(const GemmParams &p, bool vec, cudaStream_t stream) {
   dim3 grid((unsigned)ceil_div(p.N, BN), (unsigned)ceil_div(p.M, BM));
   if (vec)
-    gemm_ffma_kernel<BM, BN, true><<<grid, kThreads, 0, stream>>>(p);
+    TT_CUDA_TRY(launch_kernel(gemm_ffma_kernel<BM, BN, true>, grid, dim3(kThreads), 0, stream, 1, p));
   else
-    gemm_ffma_kernel<BM, BN, false><<<grid, kThreads, 0, stream>>>(p);
+    TT_CUDA_TRY(launch_kernel(gemm_ffma_kernel<BM, BN, false>, grid, dim3(kThreads), 0, stream, 1, p));
+  return TT_OK;
 }
 
 }  // namespace
@@ -345,12 +350,14 @@ int launch_gemm_ffma(const GemmParams &p, cudaStream_t stream) {
     return launch_wholek(p, stream);
   // Pick the tile so that the grid covers the 148 SMs at least about once.
   const int64_t tiles128 = ceil_div(p.M, 128) * ceil_div(p.N, 128);
+  int rc;
   if (tiles128 >= 148 * 2)
-    launch_tile<128, 128>(p, vec, stream);
+    rc = launch_tile<128, 128>(p, vec, stream);
   else if (ceil_div(p.M, 64) * ceil_div(p.N, 128) >= 148)
-    launch_tile<64, 128>(p, vec, stream);
+    rc = launch_tile<64, 128>(p, vec, stream);
   else
-    launch_tile<64, 64>(p, vec, stream);
+    rc = launch_tile<64, 64>(p, vec, stream);
+  if (rc != TT_OK) return rc;
   TT_LAUNCH_CHECK("gemm_ffma");
   return TT_OK;
 }

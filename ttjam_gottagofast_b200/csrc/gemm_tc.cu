@@ -392,6 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int KB = (p.K + BK - 1) / BK;
   const int MT = (p.M + BM - 1) / BM, NT = (p.N + BN - 1) / BN;
   const int ntiles = MT * NT;
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -414,6 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot_ptr;
+  pdl_wait();  // A (and R) come from the previous kernel
 
   if (warp == 0 && lane == 0) {
     // ---- TMA producer: one k-block sequence running across all tiles --------
@@ -627,6 +629,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int KB = (p.K + BK - 1) / BK;
   const int MT = (p.M + 255) / 256, NT = (p.N + PBN - 1) / PBN;
   const int ntiles = MT * NT;
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < PSTAGES; ++s) {
@@ -650,6 +653,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync_all();  // both CTAs' barriers exist before any remote arrive or TMA
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot_ptr;
+  pdl_wait();  // A (and R) come from the previous kernel
   const uint32_t full0 = map_to_cta(full_bar(0), 0);  // CTA 0's full barriers (cluster addresses)
 
   if (warp == 0 && lane == 0) {
@@ -863,8 +867,8 @@ int launch_bn(const TcGemmParams &p, cudaStream_t stream) {
   }
   const int64_t tiles = (int64_t)((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = (int)std::min<int64_t>(tiles, sms > 0 ? sms : 148);
-  gemm_tc3_kernel<BN><<<grid, kThreads, Sh::SMEM_BYTES, stream>>>(ta_hi, ta_lo, tw_hi, tw_lo, tc,
-                                                                  tc_hi, tc_lo, p);
+  TT_CUDA_TRY(launch_kernel(gemm_tc3_kernel<BN>, dim3(grid), dim3(kThreads), Sh::SMEM_BYTES,
+                            stream, 1, ta_hi, ta_lo, tw_hi, tw_lo, tc, tc_hi, tc_lo, p));
   TT_LAUNCH_CHECK("gemm_tc3");
   return TT_OK;
 }
@@ -889,20 +893,8 @@ int launch_pair(const TcGemmParams &p, cudaStream_t stream, int sms) {
   }
   const int64_t tiles = (int64_t)((p.M + 255) / 256) * ((p.N + PBN - 1) / PBN);
   const int pairs = (int)std::min<int64_t>(tiles, sms / 2);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(2 * pairs));
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = Sh::SMEM;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  TT_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_tc3_pair_kernel<PBN>, ta_hi, ta_lo, tw_hi, tw_lo, tc,
-                                 tc_hi, tc_lo, p));
+  TT_CUDA_TRY(launch_kernel(gemm_tc3_pair_kernel<PBN>, dim3((unsigned)(2 * pairs)), dim3(kThreads),
+                            Sh::SMEM, stream, 2, ta_hi, ta_lo, tw_hi, tw_lo, tc, tc_hi, tc_lo, p));
   TT_LAUNCH_CHECK("gemm_tc3_pair");
   return TT_OK;
 }

@@ -17,6 +17,8 @@
 //   the GEMM A operands: ln_hi/ln_lo [T,D], ctx_hi/ctx_lo [T,D], h_hi/h_lo [T,F].
 #pragma once
 
+#include <functional>
+
 #include <vector>
 
 #include "tt_common.cuh"
@@ -125,6 +127,22 @@ struct WorkspaceLayout {
     total = cur;
   }
 };
+
+// Everything a per-op forward's launch sequence depends on (graph_cache.cu):
+// compared bytewise, so only 64-bit fields (no padding) and zero-initialised.
+struct ForwardKey {
+  int64_t device, d_model, num_heads, ffn_dim, num_layers, causal, plan, batch, seq;
+  uint64_t image, x, mask, y, scratch;
+};
+ForwardKey make_forward_key(const tt_config &cfg, int plan, const void *image, const float *x,
+                            const uint8_t *mask, int64_t batch, int64_t seq, const float *y,
+                            const void *scratch);
+// Enqueues one forward on the given stream.
+using ForwardLaunch = std::function<int(cudaStream_t)>;
+// Runs launch on `stream`, directly or through a cached CUDA graph.
+int run_forward_cached(const ForwardKey &key, cudaStream_t stream, const ForwardLaunch &launch);
+// Whether the launch probe is timing the launches of this host thread.
+bool launch_probe_active();
 
 int validate_config(const tt_config *cfg);
 int forward_plan(const tt_config *cfg, int64_t batch, int64_t seq);

@@ -21,6 +21,8 @@ __global__ void __launch_bounds__(256) layernorm_vec_kernel(
     const float *__restrict__ x, float *__restrict__ y, uint16_t *__restrict__ y_hi,
     uint16_t *__restrict__ y_lo, const float *__restrict__ gamma, const float *__restrict__ beta,
     const uint8_t *__restrict__ row_mask, int zero_masked_rows, int64_t rows, int d, float eps) {
+  pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -88,6 +90,8 @@ __global__ void __launch_bounds__(256) layernorm_generic_kernel(
     const float *__restrict__ x, float *__restrict__ y, uint16_t *__restrict__ y_hi,
     uint16_t *__restrict__ y_lo, const float *__restrict__ gamma, const float *__restrict__ beta,
     const uint8_t *__restrict__ row_mask, int zero_masked_rows, int64_t rows, int d, float eps) {
+  pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -127,16 +131,18 @@ int launch_layernorm(const float *x, float *y, uint16_t *y_hi, uint16_t *y_lo, c
   if (d % 4 == 0 && aligned && d <= 1024) {
     const int nv = (int)ceil_div(d, 128);
 #define TT_LN_CASE(NV)                                                                     \
-  layernorm_vec_kernel<NV><<<(unsigned)blocks, threads, 0, stream>>>(                      \
-      x, y, y_hi, y_lo, gamma, beta, row_mask, zero_masked_rows, rows, d, eps)
+  TT_CUDA_TRY(launch_kernel(layernorm_vec_kernel<NV>, dim3((unsigned)blocks), dim3(threads), 0, \
+                            stream, 1, x, y, y_hi, y_lo, gamma, beta, row_mask,             \
+                            zero_masked_rows, rows, d, eps))
     if (nv == 1) TT_LN_CASE(1);
     else if (nv == 2) TT_LN_CASE(2);
     else if (nv <= 4) TT_LN_CASE(4);
     else TT_LN_CASE(8);
 #undef TT_LN_CASE
   } else {
-    layernorm_generic_kernel<<<(unsigned)blocks, threads, 0, stream>>>(
-        x, y, y_hi, y_lo, gamma, beta, row_mask, zero_masked_rows, rows, d, eps);
+    TT_CUDA_TRY(launch_kernel(layernorm_generic_kernel, dim3((unsigned)blocks), dim3(threads), 0,
+                              stream, 1, x, y, y_hi, y_lo, gamma, beta, row_mask,
+                              zero_masked_rows, rows, d, eps));
   }
   TT_LAUNCH_CHECK("layernorm");
   return TT_OK;

@@ -91,9 +91,12 @@ extern "C" int tt_forward_noalloc(const tt_config *cfg, const void *image, const
   void *scratch = nullptr;
   if ((rc = scratch_address(&scratch)) != TT_OK) return rc;
   const ImageLayout L(ops);
-  if (plan == PLAN_OPS_TC)
-    return forward_ops_tc(ops, L, static_cast<const char *>(image), x, mask, batch, seq, y, W,
-                          static_cast<char *>(scratch), static_cast<cudaStream_t>(stream_));
-  return forward_ops(ops, L, static_cast<const char *>(image), x, mask, batch, seq, y, W,
-                     static_cast<char *>(scratch), static_cast<cudaStream_t>(stream_));
+  const char *img = static_cast<const char *>(image);
+  char *ws = static_cast<char *>(scratch);
+  return run_forward_cached(
+      make_forward_key(ops, plan, image, x, mask, batch, seq, y, scratch),
+      static_cast<cudaStream_t>(stream_), [&](cudaStream_t s) {
+        return plan == PLAN_OPS_TC ? forward_ops_tc(ops, L, img, x, mask, batch, seq, y, W, ws, s)
+                                   : forward_ops(ops, L, img, x, mask, batch, seq, y, W, ws, s);
+      });
 }

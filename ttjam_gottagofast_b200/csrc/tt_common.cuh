@@ -47,6 +47,54 @@ inline int fail(int code, const std::string &msg) {
                                          cudaGetErrorString(err__));                   \
   } while (0)
 
+// Programmatic dependent launch. The kernels of the per-op schedules are
+// launched with programmatic stream serialization (launch_kernel). Each calls
+// pdl_trigger() first: once every CTA of its grid has started, the next
+// kernel on the stream may be scheduled, so that kernel's set-up (barriers,
+// tensor-memory allocation, reads of the weights and the mask, which no
+// kernel of a forward writes) overlaps this grid's tail. Each calls pdl_wait()
+// before its first read of data an earlier kernel wrote and before its first
+// global write: it returns once every earlier grid of the stream has
+// completed and its writes are visible. Without the launch attribute both are
+// no-ops.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Whether launch_kernel sets the attribute: on unless the environment sets
+// TT_PDL=0 (read once).
+bool pdl_enabled();
+
+// cudaLaunchKernelEx with programmatic stream serialization (when enabled)
+// and, for cluster_x > 1, a cluster of cluster_x CTAs along x.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t stream, unsigned cluster_x, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Exact GELU, F.gelu(approximate="none"): 0.5*x*(1+erf(x/sqrt(2))).
 __device__ __forceinline__ float gelu_erf(float v) {
   return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
