@@ -50,7 +50,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 from ttjam_gottagofast_b200 import _lib  # noqa: E402
-from ttjam_gottagofast_b200.config import MODEL_SEED, TIMING_DATA_SEED, WORKLOADS  # noqa: E402
+from ttjam_gottagofast_b200.config import BENCH_WORKLOADS, MODEL_SEED, TIMING_DATA_SEED  # noqa: E402
 from ttjam_gottagofast_b200.contract import generate_random_case  # noqa: E402
 
 METRIC = "fwd latency (us) & tokens/s"
@@ -62,7 +62,7 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--workload", default="B1", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="B1", choices=sorted(BENCH_WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=10.0)
@@ -109,7 +109,7 @@ def max_over_ranks(v, world):
 def select_workload(args):
     """The named workload, with its batch replaced when --batch is given."""
     import dataclasses
-    w = WORKLOADS[args.workload]
+    w = BENCH_WORKLOADS[args.workload]
     if args.batch > 0:
         w = dataclasses.replace(
             w, config=dataclasses.replace(w.config, batch_size=args.batch),
@@ -502,7 +502,7 @@ def run_ours(args, world, rank, local):
         }
     roofline.update({
         "traffic": (NCU_TRAFFIC.get((w.name, dom))
-                    if nb == WORKLOADS[w.name].config.batch_size else None),
+                    if nb == BENCH_WORKLOADS[w.name].config.batch_size else None),
         "kernel": f"{dom} ({len(per_kind[dom])} launches, plan {plan})",
         "algorithmic_bytes_per_launch": nbytes,
         "avg_launch_us": round(dom_us, 3),

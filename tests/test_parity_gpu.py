@@ -154,6 +154,31 @@ def test_workload_E_parity_sequence_sample():
     assert (y[~mask] == 0).all()
 
 
+OFFICIAL_CASES = [f"case{c}" for c in range(1, 14)]
+
+
+@pytest.mark.parametrize("name", OFFICIAL_CASES)
+def test_official_case_parity_sequence_sample(name):
+    """The reference's official shapes 1-13 (tools/shapes.py:9-24) at full
+    size through the default schedule; the oracle checks the first, a middle
+    and the last sequence (sequences are independent)."""
+    from ttjam_gottagofast_b200.config import OFFICIAL
+    w = OFFICIAL[name]
+    cfg = w.config
+    model, params = model_for(cfg)
+    x, mask = generate_random_case(cfg, "cpu", torch.float32, 101234, w.padding_ratio,
+                                   w.input_scale)
+    x, mask = x.to(DEV), mask.to(DEV)
+    with torch.inference_mode():
+        y = model(x, mask)
+    picks = sorted({0, cfg.batch_size // 2, cfg.batch_size - 1})
+    idx = torch.tensor(picks, device=DEV)
+    ref = oracle.forward(params, cfg, x[idx], mask[idx], batch_chunk=1)
+    check(ref, y[idx], f"{name}[{model.forward_plan(cfg.batch_size, cfg.seq_len)}]/seqs{picks}")
+    assert torch.isfinite(y).all()
+    assert model.read_device_status() == (0, 0)
+
+
 def test_output_depends_on_input_and_is_fresh():
     """The reference harness's anti-caching check (tools/harness.py:156-173):
     seeds 101, 202, 101 -- outputs held at the same time."""
