@@ -63,18 +63,26 @@ constexpr int kSoftWarp0 = 2;  // first softmax warp
 // inside the scores it has read itself.
 template <int HD>
 struct AtShape {
-  static constexpr uint32_t KROW = 2 * HD;              // bytes of one K row
-  static constexpr uint32_t OPK = 64 * KROW;            // one K operand (hi or lo)
+  // A K operand is KSPLIT boxes of 64 keys x KBOX dims (one swizzle row of
+  // 2*KBOX bytes: 64-byte swizzle at 32 dims, 128-byte at 64); head_dim 128
+  // takes two 64-dim boxes
+  static constexpr int KBOX = HD < 64 ? HD : 64;
+  static constexpr int KSPLIT = HD / KBOX;
+  static constexpr uint32_t KROW = 2 * KBOX;            // bytes of one K row of a box
+  static constexpr uint32_t KPART = 64 * KROW;          // one box
+  static constexpr uint32_t OPK = KSPLIT * KPART;       // one K operand (hi or lo)
   static constexpr uint32_t OPV = HD * 128;             // one V^T operand (hi or lo)
   static constexpr uint32_t STAGE = 2 * OPK + 2 * OPV;
   static constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE + 1024 + 256;
   static constexpr uint32_t T_QHI = 0, T_QLO = HD / 2, T_SP = HD, T_O = HD + 128;
-  static constexpr uint32_t TMEM_COLS = 256;
+  // two CTAs per SM up to head_dim 64 (256 columns each), one at 128
+  static constexpr uint32_t TMEM_COLS = 2 * HD + 128 <= 256 ? 256 : 512;
   static_assert(T_O + HD <= TMEM_COLS, "tensor memory");
-  static_assert(OPK % 1024 == 0 && OPV % 1024 == 0, "operands on the swizzle period");
+  static_assert(KPART % 1024 == 0 && OPV % 1024 == 0, "operands on the swizzle period");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
   // K operand descriptor fields: swizzle mode (4 = 64 B, 2 = 128 B) and the
   // stride between 8-row groups
-  static constexpr uint32_t K_SWZ = HD == 32 ? 4u : 2u;
+  static constexpr uint32_t K_SWZ = KBOX == 32 ? 4u : 2u;
   static constexpr uint32_t K_SBO = 8 * KROW;
   // instruction descriptors: kind::f16, D fp32, A/B fp16, both K-major, M = 128
   static constexpr uint32_t IDESC_S =
@@ -228,15 +236,12 @@ __device__ __forceinline__ void pair_barrier(int q) {
   }
 }
 
-// Two CTAs per SM: the warps of a 320-thread CTA fall 3, 3, 2, 2 on the four
-// SM sub-partitions, so two CTAs put 6 warps on one sub-partition, whose 16K
-// registers then allow 85 per thread: the kernel is held to 80.
 template <int HD>
-__global__ void __maxnreg__(80)
-    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_hi,
-                        const __grid_constant__ CUtensorMap tm_lo,
-                        const __grid_constant__ CUtensorMap tm_vhi,
-                        const __grid_constant__ CUtensorMap tm_vlo, const AttentionTcParams p) {
+__device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
+                                                  const CUtensorMap &tm_lo,
+                                                  const CUtensorMap &tm_vhi,
+                                                  const CUtensorMap &tm_vlo,
+                                                  const AttentionTcParams &p) {
   using Sh = AtShape<HD>;
   constexpr uint32_t STAGE = Sh::STAGE, OPK = Sh::OPK, OPV = Sh::OPV;
   constexpr uint32_t T_QHI = Sh::T_QHI, T_QLO = Sh::T_QLO, T_O = Sh::T_O,
@@ -352,8 +357,13 @@ __global__ void __maxnreg__(80)
       if (j >= STAGES) mbar_wait(kv_empty(s), (n - 1) & 1, p.status, 0x4100 + j);
       const uint32_t st = base + s * STAGE;
       mbar_expect_tx(kv_full(s), STAGE);
-      tma_load_3d(st, &tm_hi, kcol, j * BKV, (int)b, kv_full(s));
-      tma_load_3d(st + OPK, &tm_lo, kcol, j * BKV, (int)b, kv_full(s));
+#pragma unroll
+      for (int part = 0; part < Sh::KSPLIT; ++part) {
+        tma_load_3d(st + part * Sh::KPART, &tm_hi, kcol + part * Sh::KBOX, j * BKV, (int)b,
+                    kv_full(s));
+        tma_load_3d(st + OPK + part * Sh::KPART, &tm_lo, kcol + part * Sh::KBOX, j * BKV, (int)b,
+                    kv_full(s));
+      }
       tma_load_3d(st + 2 * OPK, &tm_vhi, j * BKV, 0, bh, kv_full(s));
       tma_load_3d(st + 2 * OPK + OPV, &tm_vlo, j * BKV, 0, bh, kv_full(s));
     }
@@ -367,13 +377,15 @@ __global__ void __maxnreg__(80)
       mbar_wait(kv_full(s), (j / STAGES) & 1, p.status, 0x4200 + j);
       const uint32_t kst = base + s * STAGE;
       const uint32_t sd = tm + Sh::T_SP + 64u * (j & 1);
-      // descriptors built once; a k-step of 16 dims advances the start address
-      // by 32 bytes (2 units)
-      const uint64_t khi0 = sdesc(kst, Sh::K_SBO, Sh::K_SWZ);
-      const uint64_t klo0 = sdesc(kst + OPK, Sh::K_SBO, Sh::K_SWZ);
+      // descriptors built once per box; a k-step of 16 dims advances the start
+      // address by 32 bytes (2 units) inside its box
+      constexpr int KK_BOX = Sh::KBOX / 16;  // k-steps per box
 #pragma unroll
       for (int kk = 0; kk < HD / 16; ++kk) {
-        const uint64_t koff = (uint64_t)(2 * kk);
+        const uint32_t kpart = kst + (uint32_t)(kk / KK_BOX) * Sh::KPART;
+        const uint64_t khi0 = sdesc(kpart, Sh::K_SBO, Sh::K_SWZ);
+        const uint64_t klo0 = sdesc(kpart + OPK, Sh::K_SBO, Sh::K_SWZ);
+        const uint64_t koff = (uint64_t)(2 * (kk % KK_BOX));
         mma_ts(sd, tm + T_QHI + 8u * kk, khi0 + koff, Sh::IDESC_S, kk > 0);
         mma_ts(sd, tm + T_QHI + 8u * kk, klo0 + koff, Sh::IDESC_S, 1);
         mma_ts(sd, tm + T_QLO + 8u * kk, khi0 + koff, Sh::IDESC_S, 1);
@@ -418,9 +430,12 @@ __global__ void __maxnreg__(80)
       // Q row -> tensor memory: this thread's dims [dim_off, dim_off + HD/2)
       // as HD/4 packed cells of Q_hi and of Q_lo
       const uint32_t qcol = (uint32_t)(HD / 4) * kh;
-      if (HD == 64) {
-        tmem_st16(lane_base + T_QHI + qcol, qv[0]);
-        tmem_st16(lane_base + T_QLO + qcol, qv[1]);
+      if (HD >= 64) {
+#pragma unroll
+        for (int c = 0; c < HD / 4; c += 16) {
+          tmem_st16(lane_base + T_QHI + qcol + c, qv[0] + c);
+          tmem_st16(lane_base + T_QLO + qcol + c, qv[1] + c);
+        }
       } else {
         tmem_st8(lane_base + T_QHI + qcol, qv[0]);
         tmem_st8(lane_base + T_QLO + qcol, qv[1]);
@@ -572,6 +587,27 @@ __global__ void __maxnreg__(80)
   }
 }
 
+// Two CTAs per SM up to head_dim 64: the warps of a 320-thread CTA fall 3, 3,
+// 2, 2 on the four SM sub-partitions, so two CTAs put 6 warps on one
+// sub-partition, whose 16K registers then allow 85 per thread: the kernel is
+// held to 80. Head_dim 128 runs one CTA per SM (512 tensor-memory columns).
+template <int HD>
+__global__ void __maxnreg__(80)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_hi,
+                        const __grid_constant__ CUtensorMap tm_lo,
+                        const __grid_constant__ CUtensorMap tm_vhi,
+                        const __grid_constant__ CUtensorMap tm_vlo, const AttentionTcParams p) {
+  attention_tc_body<HD>(tm_hi, tm_lo, tm_vhi, tm_vlo, p);
+}
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_tc_kernel_hd128(const __grid_constant__ CUtensorMap tm_hi,
+                              const __grid_constant__ CUtensorMap tm_lo,
+                              const __grid_constant__ CUtensorMap tm_vhi,
+                              const __grid_constant__ CUtensorMap tm_vlo,
+                              const AttentionTcParams p) {
+  attention_tc_body<128>(tm_hi, tm_lo, tm_vhi, tm_vlo, p);
+}
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                    const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
                                    const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -591,20 +627,22 @@ int encode_fn(EncodeTiledFn *out) {
   return TT_OK;
 }
 
-// [batch, seq, 2*d_model] fp16 view of a q|k buffer; box = hd columns x 64
-// rows x 1 sequence (rows of 2*hd bytes: 64-byte swizzle at hd 32, 128-byte at
-// hd 64), zero fill past the sequence end.
+// [batch, seq, 2*d_model] fp16 view of a q|k buffer; box = min(hd, 64)
+// columns x 64 rows x 1 sequence (rows of 64 bytes with 64-byte swizzle at hd
+// 32, of 128 bytes with 128-byte swizzle otherwise; hd 128 loads two boxes),
+// zero fill past the sequence end.
 int make_qk_map(CUtensorMap *tm, const uint16_t *ptr, int64_t batch, int seq, int d_model, int hd) {
   EncodeTiledFn encode;
   int rc = encode_fn(&encode);
   if (rc != TT_OK) return rc;
   cuuint64_t dims[3] = {(cuuint64_t)(2 * d_model), (cuuint64_t)seq, (cuuint64_t)batch};
   cuuint64_t strides[2] = {(cuuint64_t)(2 * d_model) * 2, (cuuint64_t)seq * (2 * d_model) * 2};
-  cuuint32_t box[3] = {(cuuint32_t)hd, (cuuint32_t)BKV, 1};
+  const int kbox = hd < 64 ? hd : 64;
+  cuuint32_t box[3] = {(cuuint32_t)kbox, (cuuint32_t)BKV, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<uint16_t *>(ptr),
                             dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                            hd == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                            kbox == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(TT_ERR_CUDA, "cuTensorMapEncodeTiled (q|k) failed with CUresult " +
@@ -634,24 +672,29 @@ int make_vt_map(CUtensorMap *tm, const uint16_t *ptr, int64_t bh, int seq, int s
 }
 
 template <int HD>
+constexpr auto attention_kernel_for() {
+  if constexpr (HD == 128) return &attention_tc_kernel_hd128;
+  else return &attention_tc_kernel<HD>;
+}
+
+template <int HD>
 int launch_hd(const AttentionTcParams &p, const CUtensorMap &thi, const CUtensorMap &tlo,
               const CUtensorMap &tvhi, const CUtensorMap &tvlo, cudaStream_t stream) {
   using Sh = AtShape<HD>;
+  constexpr auto fn = attention_kernel_for<HD>();
   static bool attr_set = false;
   if (!attr_set) {
-    TT_CUDA_TRY(cudaFuncSetAttribute(attention_tc_kernel<HD>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+    TT_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)Sh::SMEM_BYTES));
     // two CTAs per SM need the largest shared-memory carveout
-    TT_CUDA_TRY(cudaFuncSetAttribute(attention_tc_kernel<HD>,
-                                     cudaFuncAttributePreferredSharedMemoryCarveout,
+    TT_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
                                      (int)cudaSharedmemCarveoutMaxShared));
     attr_set = true;
   }
   const int64_t ctas = (int64_t)((p.seq + BQ - 1) / BQ) * p.num_heads * p.batch;
   dim3 grid((unsigned)ctas);
-  TT_CUDA_TRY(launch_kernel(attention_tc_kernel<HD>, grid, dim3(kThreads), Sh::SMEM_BYTES, stream,
-                            1, thi, tlo, tvhi, tvlo, p));
+  TT_CUDA_TRY(launch_kernel(fn, grid, dim3(kThreads), Sh::SMEM_BYTES, stream, 1, thi, tlo, tvhi,
+                            tvlo, p));
   TT_LAUNCH_CHECK("attention_tc");
   return TT_OK;
 }
@@ -659,13 +702,13 @@ int launch_hd(const AttentionTcParams &p, const CUtensorMap &thi, const CUtensor
 }  // namespace
 
 bool attention_tc_supported(int head_dim, int d_model) {
-  return (head_dim == 32 || head_dim == 64) && d_model % 8 == 0;
+  return (head_dim == 32 || head_dim == 64 || head_dim == 128) && d_model % 8 == 0;
 }
 
 int launch_attention_tc(const AttentionTcParams &p, cudaStream_t stream) {
   if (p.batch <= 0 || p.seq <= 0) return TT_OK;
   if (!attention_tc_supported(p.head_dim, p.d_model))
-    return fail(TT_ERR_UNSUPPORTED, "attention_tc: head_dim must be 32 or 64");
+    return fail(TT_ERR_UNSUPPORTED, "attention_tc: head_dim must be 32, 64 or 128");
   if ((int64_t)((p.seq + BQ - 1) / BQ) * p.num_heads * p.batch > INT32_MAX)
     return fail(TT_ERR_UNSUPPORTED, "attention_tc: more than 2^31 query tiles");
   if (((reinterpret_cast<uintptr_t>(p.qk_hi) | reinterpret_cast<uintptr_t>(p.qk_lo) |
@@ -681,31 +724,10 @@ int launch_attention_tc(const AttentionTcParams &p, cudaStream_t stream) {
       (rc = make_vt_map(&tvhi, p.vt_hi, p.batch * p.num_heads, p.seq, p.seq_pad, p.head_dim)) ||
       (rc = make_vt_map(&tvlo, p.vt_lo, p.batch * p.num_heads, p.seq, p.seq_pad, p.head_dim)))
     return rc;
-  return p.head_dim == 32 ? launch_hd<32>(p, thi, tlo, tvhi, tvlo, stream)
-                          : launch_hd<64>(p, thi, tlo, tvhi, tvlo, stream);
+  if (p.head_dim == 32) return launch_hd<32>(p, thi, tlo, tvhi, tvlo, stream);
+  if (p.head_dim == 64) return launch_hd<64>(p, thi, tlo, tvhi, tvlo, stream);
+  return launch_hd<128>(p, thi, tlo, tvhi, tvlo, stream);
 }
 
 }  // namespace tt
 
-namespace tt {
-// CTAs of the tensor-core attention kernel resident per SM (diagnostics).
-int attention_tc_ctas_per_sm(int head_dim) {
-  int n = 0;
-  if (head_dim == 64) {
-    cudaFuncSetAttribute(attention_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)AtShape<64>::SMEM_BYTES);
-    cudaFuncSetAttribute(attention_tc_kernel<64>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                         (int)cudaSharedmemCarveoutMaxShared);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attention_tc_kernel<64>, kThreads,
-                                                  AtShape<64>::SMEM_BYTES);
-  } else {
-    cudaFuncSetAttribute(attention_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)AtShape<32>::SMEM_BYTES);
-    cudaFuncSetAttribute(attention_tc_kernel<32>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                         (int)cudaSharedmemCarveoutMaxShared);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attention_tc_kernel<32>, kThreads,
-                                                  AtShape<32>::SMEM_BYTES);
-  }
-  return n;
-}
-}  // namespace tt

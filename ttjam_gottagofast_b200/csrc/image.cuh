@@ -21,6 +21,7 @@
 
 #include <vector>
 
+#include "attention_tc.cuh"
 #include "tt_common.cuh"
 
 namespace tt {
@@ -104,7 +105,7 @@ struct WorkspaceLayout {
       return off;
     };
     const int hd = cfg.d_model / cfg.num_heads;
-    tc_attention = tensor && (hd == 32 || hd == 64);
+    tc_attention = tensor && attention_tc_supported(hd, cfg.d_model);
     if (tc_attention) {
       // q|k as an fp16 split, and v transposed per (sequence, head) with keys
       // contiguous (rows of seq_pad fp16 values, a multiple of 16 bytes), for
