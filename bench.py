@@ -151,18 +151,18 @@ def load_peaks():
 # weight traffic once), as that file explains.
 NCU_TRAFFIC = {
     ("B1", "whole_forward"): 1.690112e6,   # profiles/cluster_forward_B1.md
-    ("D", "layernorm"): 33.7e6,            # profiles/ops_tc_workload_D.md
-    ("D", "qkv"): 83.9e6,                  # profiles/ops_tc_workload_D.md
-    ("D", "attention"): 138.2e6,           # profiles/ops_tc_workload_D.md
-    ("D", "out_proj"): 68.3e6,             # profiles/ops_tc_workload_D.md
-    ("D", "ffn_in"): 116.4e6,              # profiles/ops_tc_workload_D.md
-    ("D", "ffn_out"): 179.9e6,             # profiles/ops_tc_workload_D.md
-    ("E", "layernorm"): 0.537e9,           # profiles/ops_tc_workload_E_batch4.md
-    ("E", "qkv"): 1.393e9,                 # profiles/ops_tc_workload_E_batch4.md
-    ("E", "attention"): 1.517e9,           # profiles/ops_tc_workload_E_batch4.md
+    ("D", "layernorm"): 33.6e6,            # profiles/ops_tc_workload_D.md
+    ("D", "qkv"): 81.4e6,                  # profiles/ops_tc_workload_D.md
+    ("D", "attention"): 138.1e6,           # profiles/ops_tc_workload_D.md
+    ("D", "out_proj"): 68.4e6,             # profiles/ops_tc_workload_D.md
+    ("D", "ffn_in"): 115.9e6,              # profiles/ops_tc_workload_D.md
+    ("D", "ffn_out"): 181.1e6,             # profiles/ops_tc_workload_D.md
+    ("E", "layernorm"): 0.538e9,           # profiles/ops_tc_workload_E_batch4.md
+    ("E", "qkv"): 1.384e9,                 # profiles/ops_tc_workload_E_batch4.md
+    ("E", "attention"): 1.384e9,           # profiles/ops_tc_workload_E_batch4.md
     ("E", "out_proj"): 1.084e9,            # profiles/ops_tc_workload_E_batch4.md
-    ("E", "ffn_in"): 1.948e9,              # profiles/ops_tc_workload_E_batch4.md
-    ("E", "ffn_out"): 3.311e9,             # profiles/ops_tc_workload_E_batch4.md
+    ("E", "ffn_in"): 1.951e9,              # profiles/ops_tc_workload_E_batch4.md
+    ("E", "ffn_out"): 3.318e9,             # profiles/ops_tc_workload_E_batch4.md
 }
 
 
