@@ -47,6 +47,10 @@ CASES = [
     ("h1_hd128", (2, 33, 128, 1, 128, 4, True), 8, 1.0, 0.0, "gen"),
     ("h16_hd8", (2, 20, 128, 16, 128, 4, True), 9, 1.0, 0.3, "gen"),
     ("d1024_h4_hd256", (1, 24, 1024, 4, 1024, 1, True), 10, 1.0, 0.0, "gen"),
+    # head dims 16 and 8 on the tensor-core attention (8 runs padded to 16):
+    # several query and key tiles, padding, the last head's box past the row
+    ("h4_hd16", (2, 70, 64, 4, 96, 2, True), 17, 1.0, 0.4, "gen"),
+    ("h8_hd8_s150", (2, 150, 64, 8, 64, 2, True), 18, 1.0, 0.3, "gen"),
     # semantics corners
     ("noncausal_padded", (3, 19, 128, 4, 128, 2, False), 12, 1.0, 0.5, "gen"),
     ("seq1_noncausal", (5, 1, 128, 4, 128, 2, False), 13, 1.0, 0.0, "gen"),

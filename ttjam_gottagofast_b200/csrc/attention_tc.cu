@@ -64,8 +64,11 @@ constexpr int kSoftWarp0 = 2;  // first softmax warp
 template <int HD>
 struct AtShape {
   // A K operand is KSPLIT boxes of 64 keys x KBOX dims (one swizzle row of
-  // 2*KBOX bytes: 64-byte swizzle at 32 dims, 128-byte at 64); head_dim 128
-  // takes two 64-dim boxes
+  // 2*KBOX bytes: 32-byte swizzle at 16 dims, 64-byte at 32, 128-byte at 64);
+  // head_dim 128 takes two 64-dim boxes. HD 16 also serves head_dim 8: the
+  // Q dims 8..15 are zero in tensor memory, so the neighbouring head's k
+  // values that the 16-dim box brings in add nothing, and V^T rows 8..15
+  // (past the tensor, zero-filled) only feed O columns that are not stored.
   static constexpr int KBOX = HD < 64 ? HD : 64;
   static constexpr int KSPLIT = HD / KBOX;
   static constexpr uint32_t KROW = 2 * KBOX;            // bytes of one K row of a box
@@ -80,9 +83,11 @@ struct AtShape {
   static_assert(T_O + HD <= TMEM_COLS, "tensor memory");
   static_assert(KPART % 1024 == 0 && OPV % 1024 == 0, "operands on the swizzle period");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
-  // K operand descriptor fields: swizzle mode (4 = 64 B, 2 = 128 B) and the
-  // stride between 8-row groups
-  static constexpr uint32_t K_SWZ = KBOX == 32 ? 4u : 2u;
+  // K operand descriptor fields: swizzle mode (6 = 32 B, 4 = 64 B, 2 = 128 B)
+  // and the stride between 8-row groups
+  static constexpr uint32_t K_SWZ = KBOX == 16 ? 6u : KBOX == 32 ? 4u : 2u;
+  // O columns a softmax thread moves per tensor-memory access
+  static constexpr int OC = HD / 2 >= 16 ? 16 : 8;
   static constexpr uint32_t K_SBO = 8 * KROW;
   // instruction descriptors: kind::f16, D fp32, A/B fp16, both K-major, M = 128
   static constexpr uint32_t IDESC_S =
@@ -202,6 +207,33 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t *v) {
       "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
       : "memory");
 }
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t *v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr),
+               "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float *v) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+// n = 16 or 8 fp32 cells of one lane's row
+template <int N>
+__device__ __forceinline__ void tmem_ld_n(uint32_t taddr, float *v) {
+  if constexpr (N == 16) tmem_ld16(taddr, v);
+  else tmem_ld8(taddr, v);
+}
+__device__ __forceinline__ void tmem_st8_f32(uint32_t taddr, const float *v) {  // fp32 cells
+  uint32_t r[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) r[i] = __float_as_uint(v[i]);
+  tmem_st8(taddr, r);
+}
 __device__ __forceinline__ void tmem_st16_f32(uint32_t taddr, const float *v) {  // fp32 cells
   uint32_t r[16];
 #pragma unroll
@@ -265,7 +297,7 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
   uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int S = p.seq, D = p.d_model;
+  const int S = p.seq, D = p.d_model, hd = p.head_dim;  // hd < HD only for head_dim 8 (HD 16)
   // one-dimensional grid ordered by query tile, latest (heaviest under the
   // causal mask) first, so that the longest CTAs start first and the short
   // ones fill the tail
@@ -335,14 +367,17 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
   if (warp >= kSoftWarp0) {
     const int t = (warp & 3) * 32 + lane, kh = (warp - kSoftWarp0) >> 2;
     const int row = q0 + t;
-    const int64_t qoff = (b * S + (row < S ? row : 0)) * (int64_t)(2 * D) + (int64_t)h * HD +
-                         (HD / 2) * kh;
+    // dims [HD/2 kh, HD/2 kh + HD/2) of this head; those at or past hd (the
+    // padding of head_dim 8) are zero
+    const bool q_in = row < S && (HD / 2) * kh < hd;
+    const int64_t qoff = (b * S + (row < S ? row : 0)) * (int64_t)(2 * D) + (int64_t)h * hd +
+                         (q_in ? (HD / 2) * kh : 0);
 #pragma unroll
     for (int which = 0; which < 2; ++which) {
       const uint4 *src = reinterpret_cast<const uint4 *>((which ? p.qk_lo : p.qk_hi) + qoff);
 #pragma unroll
       for (int i = 0; i < HD / 16; ++i) {
-        const uint4 x = row < S ? src[i] : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 x = q_in ? src[i] : make_uint4(0u, 0u, 0u, 0u);
         qv[which][4 * i] = x.x; qv[which][4 * i + 1] = x.y;
         qv[which][4 * i + 2] = x.z; qv[which][4 * i + 3] = x.w;
       }
@@ -350,7 +385,7 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
   }
   if (warp == 0 && lane == 0) {
     // ---- TMA producer: K/V tiles -------------------------------------------
-    const int kcol = D + h * HD;  // first k column (fp16 elements) of this head
+    const int kcol = D + h * hd;  // first k column (fp16 elements) of this head
     const int bh = (int)b * p.num_heads + h;
     for (int j = 0; j < nkv; ++j) {
       const int s = j % STAGES, n = j / STAGES;
@@ -430,15 +465,18 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
       // Q row -> tensor memory: this thread's dims [dim_off, dim_off + HD/2)
       // as HD/4 packed cells of Q_hi and of Q_lo
       const uint32_t qcol = (uint32_t)(HD / 4) * kh;
-      if (HD >= 64) {
+      if constexpr (HD >= 64) {
 #pragma unroll
         for (int c = 0; c < HD / 4; c += 16) {
           tmem_st16(lane_base + T_QHI + qcol + c, qv[0] + c);
           tmem_st16(lane_base + T_QLO + qcol + c, qv[1] + c);
         }
-      } else {
+      } else if constexpr (HD == 32) {
         tmem_st8(lane_base + T_QHI + qcol, qv[0]);
         tmem_st8(lane_base + T_QLO + qcol, qv[1]);
+      } else {
+        tmem_st4(lane_base + T_QHI + qcol, qv[0]);
+        tmem_st4(lane_base + T_QLO + qcol, qv[1]);
       }
       tmem_wait_st();
       fence_before();
@@ -510,13 +548,14 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
           mbar_wait(o_done, (j - 1) & 1, p.status, 0x4600 + j);
           fence_after();
 #pragma unroll
-          for (int c = 0; c < HD / 2; c += 16) {
-            float ov[16];
-            tmem_ld16(lane_base + T_O + dim_off + c, ov);
+          for (int c = 0; c < HD / 2; c += Sh::OC) {
+            float ov[Sh::OC];
+            tmem_ld_n<Sh::OC>(lane_base + T_O + dim_off + c, ov);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) ov[i] *= alpha;
-            tmem_st16_f32(lane_base + T_O + dim_off + c, ov);
+            for (int i = 0; i < Sh::OC; ++i) ov[i] *= alpha;
+            if constexpr (Sh::OC == 16) tmem_st16_f32(lane_base + T_O + dim_off + c, ov);
+            else tmem_st8_f32(lane_base + T_O + dim_off + c, ov);
           }
         }
         l *= alpha;
@@ -559,22 +598,25 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
     mbar_wait(o_final, 0, p.status, 0x4700);
     fence_after();
     const float inv = l > 0.f ? 1.f / l : 0.f;
-    const int64_t off = (b * S + (row_in ? row : 0)) * (int64_t)D + (int64_t)h * HD + dim_off;
+    const int64_t off = (b * S + (row_in ? row : 0)) * (int64_t)D + (int64_t)h * hd + dim_off;
+    constexpr int OC = Sh::OC;
 #pragma unroll
-    for (int c = 0; c < HD / 2; c += 16) {
-      float ov[16];
-      tmem_ld16(lane_base + T_O + dim_off + c, ov);
+    for (int c = 0; c < HD / 2; c += OC) {
+      float ov[OC];
+      tmem_ld_n<OC>(lane_base + T_O + dim_off + c, ov);
       tmem_wait_ld();
-      if (row_in) {
-        uint32_t hw[8], lw[8];
+      if (row_in && (int)dim_off + c < hd) {  // the padding dims of head_dim 8 are not stored
+        uint32_t hw[OC / 2], lw[OC / 2];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) split_pair(ov[2 * i] * inv, ov[2 * i + 1] * inv, hw[i], lw[i]);
+        for (int i = 0; i < OC / 2; ++i)
+          split_pair(ov[2 * i] * inv, ov[2 * i + 1] * inv, hw[i], lw[i]);
         uint4 *dh = reinterpret_cast<uint4 *>(p.ctx_hi + off + c);
         uint4 *dl = reinterpret_cast<uint4 *>(p.ctx_lo + off + c);
-        dh[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        dh[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
-        dl[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-        dl[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+#pragma unroll
+        for (int u = 0; u < OC / 8; ++u) {
+          dh[u] = make_uint4(hw[4 * u], hw[4 * u + 1], hw[4 * u + 2], hw[4 * u + 3]);
+          dl[u] = make_uint4(lw[4 * u], lw[4 * u + 1], lw[4 * u + 2], lw[4 * u + 3]);
+        }
       }
     }
   }
@@ -627,22 +669,25 @@ int encode_fn(EncodeTiledFn *out) {
   return TT_OK;
 }
 
-// [batch, seq, 2*d_model] fp16 view of a q|k buffer; box = min(hd, 64)
-// columns x 64 rows x 1 sequence (rows of 64 bytes with 64-byte swizzle at hd
-// 32, of 128 bytes with 128-byte swizzle otherwise; hd 128 loads two boxes),
-// zero fill past the sequence end.
-int make_qk_map(CUtensorMap *tm, const uint16_t *ptr, int64_t batch, int seq, int d_model, int hd) {
+// [batch, seq, 2*d_model] fp16 view of a q|k buffer; box = kbox columns x 64
+// rows x 1 sequence, kbox = min(hd_mma, 64) (rows of 32, 64 or 128 bytes with
+// the matching swizzle; hd 128 loads two boxes), zero fill past the sequence
+// end and past the last column.
+int make_qk_map(CUtensorMap *tm, const uint16_t *ptr, int64_t batch, int seq, int d_model,
+                int hd_mma) {
   EncodeTiledFn encode;
   int rc = encode_fn(&encode);
   if (rc != TT_OK) return rc;
   cuuint64_t dims[3] = {(cuuint64_t)(2 * d_model), (cuuint64_t)seq, (cuuint64_t)batch};
   cuuint64_t strides[2] = {(cuuint64_t)(2 * d_model) * 2, (cuuint64_t)seq * (2 * d_model) * 2};
-  const int kbox = hd < 64 ? hd : 64;
+  const int kbox = hd_mma < 64 ? hd_mma : 64;
   cuuint32_t box[3] = {(cuuint32_t)kbox, (cuuint32_t)BKV, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<uint16_t *>(ptr),
                             dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                            kbox == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                            kbox == 16   ? CU_TENSOR_MAP_SWIZZLE_32B
+                            : kbox == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                         : CU_TENSOR_MAP_SWIZZLE_128B,
                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(TT_ERR_CUDA, "cuTensorMapEncodeTiled (q|k) failed with CUresult " +
@@ -651,15 +696,16 @@ int make_qk_map(CUtensorMap *tm, const uint16_t *ptr, int64_t batch, int seq, in
 }
 
 // [batch*heads, hd, seq] fp16 view of a transposed value buffer (row stride
-// seq_pad); box = 64 keys x hd dims x 1, 128-byte swizzle, zero fill past the
-// sequence.
-int make_vt_map(CUtensorMap *tm, const uint16_t *ptr, int64_t bh, int seq, int seq_pad, int hd) {
+// seq_pad); box = 64 keys x hd_mma dims x 1, 128-byte swizzle, zero fill past
+// the sequence (and past hd when hd_mma = 16 serves head_dim 8).
+int make_vt_map(CUtensorMap *tm, const uint16_t *ptr, int64_t bh, int seq, int seq_pad, int hd,
+                int hd_mma) {
   EncodeTiledFn encode;
   int rc = encode_fn(&encode);
   if (rc != TT_OK) return rc;
   cuuint64_t dims[3] = {(cuuint64_t)seq, (cuuint64_t)hd, (cuuint64_t)bh};
   cuuint64_t strides[2] = {(cuuint64_t)seq_pad * 2, (cuuint64_t)seq_pad * hd * 2};
-  cuuint32_t box[3] = {(cuuint32_t)BKV, (cuuint32_t)hd, 1};
+  cuuint32_t box[3] = {(cuuint32_t)BKV, (cuuint32_t)hd_mma, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<uint16_t *>(ptr),
                             dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -702,13 +748,15 @@ int launch_hd(const AttentionTcParams &p, const CUtensorMap &thi, const CUtensor
 }  // namespace
 
 bool attention_tc_supported(int head_dim, int d_model) {
-  return (head_dim == 32 || head_dim == 64 || head_dim == 128) && d_model % 8 == 0;
+  return (head_dim == 8 || head_dim == 16 || head_dim == 32 || head_dim == 64 ||
+          head_dim == 128) &&
+         d_model % 8 == 0;
 }
 
 int launch_attention_tc(const AttentionTcParams &p, cudaStream_t stream) {
   if (p.batch <= 0 || p.seq <= 0) return TT_OK;
   if (!attention_tc_supported(p.head_dim, p.d_model))
-    return fail(TT_ERR_UNSUPPORTED, "attention_tc: head_dim must be 32, 64 or 128");
+    return fail(TT_ERR_UNSUPPORTED, "attention_tc: head_dim must be 8, 16, 32, 64 or 128");
   if ((int64_t)((p.seq + BQ - 1) / BQ) * p.num_heads * p.batch > INT32_MAX)
     return fail(TT_ERR_UNSUPPORTED, "attention_tc: more than 2^31 query tiles");
   if (((reinterpret_cast<uintptr_t>(p.qk_hi) | reinterpret_cast<uintptr_t>(p.qk_lo) |
@@ -717,13 +765,17 @@ int launch_attention_tc(const AttentionTcParams &p, cudaStream_t stream) {
     return fail(TT_ERR_INVALID_ARGUMENT, "attention_tc: buffers must be 16-byte aligned");
   if (p.seq_pad < p.seq || p.seq_pad % 8 != 0)
     return fail(TT_ERR_INVALID_ARGUMENT, "attention_tc: seq_pad must be >= seq and a multiple of 8");
+  // head_dim 8 runs as 16 (zero Q padding, see AtShape)
+  const int hd_mma = p.head_dim < 16 ? 16 : p.head_dim;
   CUtensorMap thi, tlo, tvhi, tvlo;
   int rc;
-  if ((rc = make_qk_map(&thi, p.qk_hi, p.batch, p.seq, p.d_model, p.head_dim)) ||
-      (rc = make_qk_map(&tlo, p.qk_lo, p.batch, p.seq, p.d_model, p.head_dim)) ||
-      (rc = make_vt_map(&tvhi, p.vt_hi, p.batch * p.num_heads, p.seq, p.seq_pad, p.head_dim)) ||
-      (rc = make_vt_map(&tvlo, p.vt_lo, p.batch * p.num_heads, p.seq, p.seq_pad, p.head_dim)))
+  const int64_t bh = p.batch * p.num_heads;
+  if ((rc = make_qk_map(&thi, p.qk_hi, p.batch, p.seq, p.d_model, hd_mma)) ||
+      (rc = make_qk_map(&tlo, p.qk_lo, p.batch, p.seq, p.d_model, hd_mma)) ||
+      (rc = make_vt_map(&tvhi, p.vt_hi, bh, p.seq, p.seq_pad, p.head_dim, hd_mma)) ||
+      (rc = make_vt_map(&tvlo, p.vt_lo, bh, p.seq, p.seq_pad, p.head_dim, hd_mma)))
     return rc;
+  if (hd_mma == 16) return launch_hd<16>(p, thi, tlo, tvhi, tvlo, stream);
   if (p.head_dim == 32) return launch_hd<32>(p, thi, tlo, tvhi, tvlo, stream);
   if (p.head_dim == 64) return launch_hd<64>(p, thi, tlo, tvhi, tvlo, stream);
   return launch_hd<128>(p, thi, tlo, tvhi, tvlo, stream);

@@ -269,9 +269,10 @@ __device__ __forceinline__ void store_vt(const TcGemmParams &p, int row, int col
                                          const float (&v)[16]) {
   const bool full = col0 + 16 <= p.N;
   const int vc = col0 - p.vt_col0;
-  const int hh = vc / p.head_dim, d0 = vc % p.head_dim;
   const int bb = row / p.seq, ss = row % p.seq;
-  const int64_t base_t = ((int64_t)(bb * p.heads + hh) * p.head_dim + d0) * p.seq_pad + ss;
+  // column vc + j is dim (vc + j) % head_dim of head (vc + j) / head_dim; the
+  // row index (bb*heads + hh)*head_dim + d is then bb*heads*head_dim + vc + j
+  const int64_t base_t = ((int64_t)bb * p.heads * p.head_dim + vc) * p.seq_pad + ss;
   bool ok = true;
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
@@ -924,8 +925,8 @@ int launch_gemm_tc3(const TcGemmParams &p, cudaStream_t stream) {
   if (p.H_hi != nullptr &&
       (p.h_cols % 8 != 0 || (p.vt_hi != nullptr ? p.h_cols != p.vt_col0 : p.h_cols != p.N)))
     return fail(TT_ERR_UNSUPPORTED, "gemm_tc: the fp16 split covers the columns before v");
-  if (p.vt_hi != nullptr && (p.vt_col0 % 16 != 0 || p.head_dim % 16 != 0 || p.seq_pad % 8 != 0))
-    return fail(TT_ERR_UNSUPPORTED, "gemm_tc: transposed value columns need 16-aligned heads");
+  if (p.vt_hi != nullptr && (p.vt_col0 % 16 != 0 || p.head_dim % 8 != 0 || p.seq_pad % 8 != 0))
+    return fail(TT_ERR_UNSUPPORTED, "gemm_tc: transposed value columns need 8-aligned heads");
   // CTA pairs (256 x 256 tiles) cut the L2 -> SM operand traffic by a third
   // and keep N = 256 MMAs; they run when the pair tiles fill at least one wave
   // (measured on B200: M 16384 x N 512 x K 2048, 1.7 waves of pairs, beats
