@@ -48,7 +48,7 @@
 namespace tt {
 namespace {
 
-constexpr int BQ = 128, BKV = 64, STAGES = 3;
+constexpr int BQ = 128, BKV = 64;
 constexpr int kThreads = 320;  // warp 0: TMA; warp 1: TMEM + MMA; warps 2-9: softmax
 constexpr int kSoftWarp0 = 2;  // first softmax warp
 
@@ -74,26 +74,32 @@ struct AtShape {
   static constexpr uint32_t KROW = 2 * KBOX;            // bytes of one K row of a box
   static constexpr uint32_t KPART = 64 * KROW;          // one box
   static constexpr uint32_t OPK = KSPLIT * KPART;       // one K operand (hi or lo)
-  static constexpr uint32_t OPV = HD * 128;             // one V^T operand (hi or lo)
+  // output dims per CTA: head_dim 256 splits O over two CTAs of 128 dims each
+  // (both compute the full scores), so that Q, the S/P buffers and O fit 512
+  // tensor-memory columns
+  static constexpr int HDO = HD > 128 ? 128 : HD;
+  static constexpr int NSPLIT = HD / HDO;
+  static constexpr uint32_t OPV = HDO * 128;            // one V^T operand (hi or lo)
   static constexpr uint32_t STAGE = 2 * OPK + 2 * OPV;
-  static constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE + 1024 + 256;
+  static constexpr int NST = HD > 128 ? 2 : 3;          // ring stages
+  static constexpr size_t SMEM_BYTES = (size_t)NST * STAGE + 1024 + 256;
   static constexpr uint32_t T_QHI = 0, T_QLO = HD / 2, T_SP = HD, T_O = HD + 128;
-  // two CTAs per SM up to head_dim 64 (256 columns each), one at 128
-  static constexpr uint32_t TMEM_COLS = 2 * HD + 128 <= 256 ? 256 : 512;
-  static_assert(T_O + HD <= TMEM_COLS, "tensor memory");
+  // two CTAs per SM up to head_dim 64 (256 columns each), one above
+  static constexpr uint32_t TMEM_COLS = HD + 128 + HDO <= 256 ? 256 : 512;
+  static_assert(T_O + HDO <= TMEM_COLS, "tensor memory");
   static_assert(KPART % 1024 == 0 && OPV % 1024 == 0, "operands on the swizzle period");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
   // K operand descriptor fields: swizzle mode (6 = 32 B, 4 = 64 B, 2 = 128 B)
   // and the stride between 8-row groups
   static constexpr uint32_t K_SWZ = KBOX == 16 ? 6u : KBOX == 32 ? 4u : 2u;
   // O columns a softmax thread moves per tensor-memory access
-  static constexpr int OC = HD / 2 >= 16 ? 16 : 8;
+  static constexpr int OC = HDO / 2 >= 16 ? 16 : 8;
   static constexpr uint32_t K_SBO = 8 * KROW;
   // instruction descriptors: kind::f16, D fp32, A/B fp16, both K-major, M = 128
   static constexpr uint32_t IDESC_S =
       (1u << 4) | ((uint32_t)(64 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
   static constexpr uint32_t IDESC_PV =
-      (1u << 4) | ((uint32_t)(HD >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+      (1u << 4) | ((uint32_t)(HDO >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -276,6 +282,7 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
                                                   const AttentionTcParams &p) {
   using Sh = AtShape<HD>;
   constexpr uint32_t STAGE = Sh::STAGE, OPK = Sh::OPK, OPV = Sh::OPV;
+  constexpr int STAGES = Sh::NST, HDO = Sh::HDO;
   constexpr uint32_t T_QHI = Sh::T_QHI, T_QLO = Sh::T_QLO, T_O = Sh::T_O,
                      TMEM_COLS = Sh::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
@@ -302,8 +309,12 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
   // causal mask) first, so that the longest CTAs start first and the short
   // ones fill the tail
   const int64_t nbh = p.batch * p.num_heads;
-  const int qt = (S + BQ - 1) / BQ - 1 - (int)(blockIdx.x / nbh);
-  const int64_t bh_idx = blockIdx.x % nbh;
+  // head_dim 256: CTA pairs (consecutive) share a query tile and head, each
+  // computing output dims [oh * HDO, oh * HDO + HDO)
+  const int64_t per_tile = nbh * Sh::NSPLIT;
+  const int qt = (S + BQ - 1) / BQ - 1 - (int)(blockIdx.x / per_tile);
+  const int64_t bh_idx = (blockIdx.x % per_tile) / Sh::NSPLIT;
+  const int oh = (int)(blockIdx.x % Sh::NSPLIT);
   const int h = (int)(bh_idx % p.num_heads);
   const int64_t b = bh_idx / p.num_heads;
   const int q0 = qt * BQ;
@@ -362,27 +373,6 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
   const uint32_t tm = *tmem_slot_ptr;
   pdl_wait();  // q|k and v^T come from the previous kernel (the mask is the caller's input)
 
-  // The softmax threads' Q row (fp16 split, HD/2 dims each: HD/4 packed cells).
-  uint32_t qv[2][HD / 4];
-  if (warp >= kSoftWarp0) {
-    const int t = (warp & 3) * 32 + lane, kh = (warp - kSoftWarp0) >> 2;
-    const int row = q0 + t;
-    // dims [HD/2 kh, HD/2 kh + HD/2) of this head; those at or past hd (the
-    // padding of head_dim 8) are zero
-    const bool q_in = row < S && (HD / 2) * kh < hd;
-    const int64_t qoff = (b * S + (row < S ? row : 0)) * (int64_t)(2 * D) + (int64_t)h * hd +
-                         (q_in ? (HD / 2) * kh : 0);
-#pragma unroll
-    for (int which = 0; which < 2; ++which) {
-      const uint4 *src = reinterpret_cast<const uint4 *>((which ? p.qk_lo : p.qk_hi) + qoff);
-#pragma unroll
-      for (int i = 0; i < HD / 16; ++i) {
-        const uint4 x = q_in ? src[i] : make_uint4(0u, 0u, 0u, 0u);
-        qv[which][4 * i] = x.x; qv[which][4 * i + 1] = x.y;
-        qv[which][4 * i + 2] = x.z; qv[which][4 * i + 3] = x.w;
-      }
-    }
-  }
   if (warp == 0 && lane == 0) {
     // ---- TMA producer: K/V tiles -------------------------------------------
     const int kcol = D + h * hd;  // first k column (fp16 elements) of this head
@@ -399,8 +389,8 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
         tma_load_3d(st + OPK + part * Sh::KPART, &tm_lo, kcol + part * Sh::KBOX, j * BKV, (int)b,
                     kv_full(s));
       }
-      tma_load_3d(st + 2 * OPK, &tm_vhi, j * BKV, 0, bh, kv_full(s));
-      tma_load_3d(st + 2 * OPK + OPV, &tm_vlo, j * BKV, 0, bh, kv_full(s));
+      tma_load_3d(st + 2 * OPK, &tm_vhi, j * BKV, oh * HDO, bh, kv_full(s));
+      tma_load_3d(st + 2 * OPK + OPV, &tm_vlo, j * BKV, oh * HDO, bh, kv_full(s));
     }
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer --------------------------------------------------------
@@ -460,23 +450,32 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
     const bool row_in = row < S;
     const uint32_t lane_base = tm + ((uint32_t)((warp & 3) * 32) << 16);
     const uint32_t col_off = 32u * kh;                 // this thread's 32 scores of a tile
-    const uint32_t dim_off = (uint32_t)(HD / 2) * kh;  // ... and HD/2 dims of O
+    const uint32_t dim_off = (uint32_t)(HDO / 2) * kh;  // ... and HDO/2 dims of O
     {
-      // Q row -> tensor memory: this thread's dims [dim_off, dim_off + HD/2)
-      // as HD/4 packed cells of Q_hi and of Q_lo
+      // Q row -> tensor memory: this thread's dims [HD/2 kh, HD/2 kh + HD/2)
+      // as HD/4 packed cells of Q_hi and of Q_lo (dims at or past hd, the
+      // padding of head_dim 8, are zero), in chunks of at most 16 cells
+      const bool q_in = row_in && (HD / 2) * kh < hd;
+      const int64_t qoff = (b * S + (row_in ? row : 0)) * (int64_t)(2 * D) + (int64_t)h * hd +
+                           (q_in ? (HD / 2) * kh : 0);
       const uint32_t qcol = (uint32_t)(HD / 4) * kh;
-      if constexpr (HD >= 64) {
+      constexpr int QC = HD / 4 < 16 ? HD / 4 : 16;
 #pragma unroll
-        for (int c = 0; c < HD / 4; c += 16) {
-          tmem_st16(lane_base + T_QHI + qcol + c, qv[0] + c);
-          tmem_st16(lane_base + T_QLO + qcol + c, qv[1] + c);
+      for (int which = 0; which < 2; ++which) {
+        const uint4 *src = reinterpret_cast<const uint4 *>((which ? p.qk_lo : p.qk_hi) + qoff);
+        const uint32_t tcol = lane_base + (which ? T_QLO : T_QHI) + qcol;
+#pragma unroll
+        for (int c = 0; c < HD / 4; c += QC) {
+          uint32_t qv[QC];
+#pragma unroll
+          for (int i = 0; i < QC / 4; ++i) {
+            const uint4 v = q_in ? src[c / 4 + i] : make_uint4(0u, 0u, 0u, 0u);
+            qv[4 * i] = v.x; qv[4 * i + 1] = v.y; qv[4 * i + 2] = v.z; qv[4 * i + 3] = v.w;
+          }
+          if constexpr (QC == 16) tmem_st16(tcol + c, qv);
+          else if constexpr (QC == 8) tmem_st8(tcol + c, qv);
+          else tmem_st4(tcol + c, qv);
         }
-      } else if constexpr (HD == 32) {
-        tmem_st8(lane_base + T_QHI + qcol, qv[0]);
-        tmem_st8(lane_base + T_QLO + qcol, qv[1]);
-      } else {
-        tmem_st4(lane_base + T_QHI + qcol, qv[0]);
-        tmem_st4(lane_base + T_QLO + qcol, qv[1]);
       }
       tmem_wait_st();
       fence_before();
@@ -598,14 +597,16 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
     mbar_wait(o_final, 0, p.status, 0x4700);
     fence_after();
     const float inv = l > 0.f ? 1.f / l : 0.f;
-    const int64_t off = (b * S + (row_in ? row : 0)) * (int64_t)D + (int64_t)h * hd + dim_off;
+    const int64_t off = (b * S + (row_in ? row : 0)) * (int64_t)D + (int64_t)h * hd +
+                        oh * HDO + dim_off;
     constexpr int OC = Sh::OC;
 #pragma unroll
-    for (int c = 0; c < HD / 2; c += OC) {
+    for (int c = 0; c < HDO / 2; c += OC) {
       float ov[OC];
       tmem_ld_n<OC>(lane_base + T_O + dim_off + c, ov);
       tmem_wait_ld();
-      if (row_in && (int)dim_off + c < hd) {  // the padding dims of head_dim 8 are not stored
+      // the padding dims of head_dim 8 are not stored
+      if (row_in && oh * HDO + (int)dim_off + c < hd) {
         uint32_t hw[OC / 2], lw[OC / 2];
 #pragma unroll
         for (int i = 0; i < OC / 2; ++i)
@@ -648,6 +649,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                               const __grid_constant__ CUtensorMap tm_vlo,
                               const AttentionTcParams p) {
   attention_tc_body<128>(tm_hi, tm_lo, tm_vhi, tm_vlo, p);
+}
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_tc_kernel_hd256(const __grid_constant__ CUtensorMap tm_hi,
+                              const __grid_constant__ CUtensorMap tm_lo,
+                              const __grid_constant__ CUtensorMap tm_vhi,
+                              const __grid_constant__ CUtensorMap tm_vlo,
+                              const AttentionTcParams p) {
+  attention_tc_body<256>(tm_hi, tm_lo, tm_vhi, tm_vlo, p);
 }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -696,16 +705,17 @@ int make_qk_map(CUtensorMap *tm, const uint16_t *ptr, int64_t batch, int seq, in
 }
 
 // [batch*heads, hd, seq] fp16 view of a transposed value buffer (row stride
-// seq_pad); box = 64 keys x hd_mma dims x 1, 128-byte swizzle, zero fill past
-// the sequence (and past hd when hd_mma = 16 serves head_dim 8).
+// seq_pad); box = 64 keys x rows dims x 1 (rows = the dims one CTA outputs:
+// 128 of head_dim 256), 128-byte swizzle, zero fill past the sequence (and
+// past hd when 16 rows serve head_dim 8).
 int make_vt_map(CUtensorMap *tm, const uint16_t *ptr, int64_t bh, int seq, int seq_pad, int hd,
-                int hd_mma) {
+                int rows) {
   EncodeTiledFn encode;
   int rc = encode_fn(&encode);
   if (rc != TT_OK) return rc;
   cuuint64_t dims[3] = {(cuuint64_t)seq, (cuuint64_t)hd, (cuuint64_t)bh};
   cuuint64_t strides[2] = {(cuuint64_t)seq_pad * 2, (cuuint64_t)seq_pad * hd * 2};
-  cuuint32_t box[3] = {(cuuint32_t)BKV, (cuuint32_t)hd_mma, 1};
+  cuuint32_t box[3] = {(cuuint32_t)BKV, (cuuint32_t)rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<uint16_t *>(ptr),
                             dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -719,7 +729,8 @@ int make_vt_map(CUtensorMap *tm, const uint16_t *ptr, int64_t bh, int seq, int s
 
 template <int HD>
 constexpr auto attention_kernel_for() {
-  if constexpr (HD == 128) return &attention_tc_kernel_hd128;
+  if constexpr (HD == 256) return &attention_tc_kernel_hd256;
+  else if constexpr (HD == 128) return &attention_tc_kernel_hd128;
   else return &attention_tc_kernel<HD>;
 }
 
@@ -737,7 +748,7 @@ int launch_hd(const AttentionTcParams &p, const CUtensorMap &thi, const CUtensor
                                      (int)cudaSharedmemCarveoutMaxShared));
     attr_set = true;
   }
-  const int64_t ctas = (int64_t)((p.seq + BQ - 1) / BQ) * p.num_heads * p.batch;
+  const int64_t ctas = (int64_t)((p.seq + BQ - 1) / BQ) * p.num_heads * p.batch * Sh::NSPLIT;
   dim3 grid((unsigned)ctas);
   TT_CUDA_TRY(launch_kernel(fn, grid, dim3(kThreads), Sh::SMEM_BYTES, stream, 1, thi, tlo, tvhi,
                             tvlo, p));
@@ -749,15 +760,15 @@ int launch_hd(const AttentionTcParams &p, const CUtensorMap &thi, const CUtensor
 
 bool attention_tc_supported(int head_dim, int d_model) {
   return (head_dim == 8 || head_dim == 16 || head_dim == 32 || head_dim == 64 ||
-          head_dim == 128) &&
+          head_dim == 128 || head_dim == 256) &&
          d_model % 8 == 0;
 }
 
 int launch_attention_tc(const AttentionTcParams &p, cudaStream_t stream) {
   if (p.batch <= 0 || p.seq <= 0) return TT_OK;
   if (!attention_tc_supported(p.head_dim, p.d_model))
-    return fail(TT_ERR_UNSUPPORTED, "attention_tc: head_dim must be 8, 16, 32, 64 or 128");
-  if ((int64_t)((p.seq + BQ - 1) / BQ) * p.num_heads * p.batch > INT32_MAX)
+    return fail(TT_ERR_UNSUPPORTED, "attention_tc: head_dim must be 8, 16, 32, 64, 128 or 256");
+  if ((int64_t)((p.seq + BQ - 1) / BQ) * p.num_heads * p.batch * 2 > INT32_MAX)
     return fail(TT_ERR_UNSUPPORTED, "attention_tc: more than 2^31 query tiles");
   if (((reinterpret_cast<uintptr_t>(p.qk_hi) | reinterpret_cast<uintptr_t>(p.qk_lo) |
         reinterpret_cast<uintptr_t>(p.ctx_hi) | reinterpret_cast<uintptr_t>(p.ctx_lo) |
@@ -772,13 +783,14 @@ int launch_attention_tc(const AttentionTcParams &p, cudaStream_t stream) {
   const int64_t bh = p.batch * p.num_heads;
   if ((rc = make_qk_map(&thi, p.qk_hi, p.batch, p.seq, p.d_model, hd_mma)) ||
       (rc = make_qk_map(&tlo, p.qk_lo, p.batch, p.seq, p.d_model, hd_mma)) ||
-      (rc = make_vt_map(&tvhi, p.vt_hi, bh, p.seq, p.seq_pad, p.head_dim, hd_mma)) ||
-      (rc = make_vt_map(&tvlo, p.vt_lo, bh, p.seq, p.seq_pad, p.head_dim, hd_mma)))
+      (rc = make_vt_map(&tvhi, p.vt_hi, bh, p.seq, p.seq_pad, p.head_dim, hd_mma > 128 ? 128 : hd_mma)) ||
+      (rc = make_vt_map(&tvlo, p.vt_lo, bh, p.seq, p.seq_pad, p.head_dim, hd_mma > 128 ? 128 : hd_mma)))
     return rc;
   if (hd_mma == 16) return launch_hd<16>(p, thi, tlo, tvhi, tvlo, stream);
   if (p.head_dim == 32) return launch_hd<32>(p, thi, tlo, tvhi, tvlo, stream);
   if (p.head_dim == 64) return launch_hd<64>(p, thi, tlo, tvhi, tvlo, stream);
-  return launch_hd<128>(p, thi, tlo, tvhi, tvlo, stream);
+  if (p.head_dim == 128) return launch_hd<128>(p, thi, tlo, tvhi, tvlo, stream);
+  return launch_hd<256>(p, thi, tlo, tvhi, tvlo, stream);
 }
 
 }  // namespace tt
