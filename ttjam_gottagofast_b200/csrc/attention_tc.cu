@@ -1,5 +1,5 @@
 // Causal / key-padded flash attention on tensor cores (tcgen05) for head_dim
-// 32 and 64.
+// 8, 16, 32, 64, 128 and 256.
 //
 // Semantics as the reference attention (torch_transformer_benchmark.py:97-117):
 // s = (q . k) * hd^-0.5, -inf for keys after the query (causal, :99-103) and
@@ -19,9 +19,11 @@
 // 16-bit MMA does twice the work of a TF32 one in the same cycles at N = 64
 // and moves half the operand bytes.
 //
-// CTA = (query tile of 128 rows, head, sequence); 320 threads, two CTAs per
-// SM (256 tensor-memory columns and a 3-stage ring each), so that one CTA's
-// softmax runs while the other's MMAs use the tensor pipe:
+// CTA = (query tile of 128 rows, head, sequence; and, at head_dim 256, half
+// of the output dims); 320 threads. Up to head_dim 64 two CTAs share an SM
+// (256 tensor-memory columns and a 3-stage ring each), so that one CTA's
+// softmax runs while the other's MMAs use the tensor pipe; from head_dim 128
+// a CTA takes 512 columns and runs alone:
 //   warp 0    TMA producer: per 64-key tile, K_hi K_lo (64 keys x HD dims) and
 //             Vt_hi Vt_lo (HD dims x 64 keys, from the transposed copy of v the
 //             q|k|v GEMM writes) into the ring;
@@ -52,9 +54,10 @@ constexpr int BQ = 128, BKV = 64;
 constexpr int kThreads = 320;  // warp 0: TMA; warp 1: TMEM + MMA; warps 2-9: softmax
 constexpr int kSoftWarp0 = 2;  // first softmax warp
 
-// Shapes for head_dim HD (32 or 64). Shared-memory stage: K_hi, K_lo (64 keys
-// x HD fp16: rows of 2*HD bytes, 64-byte swizzle at HD 32, 128-byte at HD 64)
-// then Vt_hi, Vt_lo (HD rows x 64 keys: 128-byte rows, 128-byte swizzle).
+// Shapes for an MMA head dim HD (16, 32, 64, 128 or 256; head_dim 8 runs as
+// 16). Shared-memory stage: K_hi, K_lo (64 keys x HD fp16 in boxes of up to
+// 64 dims), then Vt_hi, Vt_lo (the CTA's output dims x 64 keys: 128-byte rows,
+// 128-byte swizzle).
 // Tensor-memory columns (32-bit cells; a 16-bit operand packs two values per
 // cell): Q_hi, Q_lo (HD/2 each), two S/P buffers of 64 columns, O (HD). A
 // buffer holds the fp32 scores S of a 64-key tile, then the fp16 split of P

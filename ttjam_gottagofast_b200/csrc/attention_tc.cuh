@@ -1,5 +1,5 @@
-// Tensor-core (tcgen05) flash attention for head_dim 32 and 64 (see
-// attention_tc.cu).
+// Tensor-core (tcgen05) flash attention for head_dim 8, 16, 32, 64, 128 and
+// 256 (see attention_tc.cu).
 #pragma once
 
 #include "tt_common.cuh"

@@ -71,7 +71,7 @@ template <int BN>
 struct TcShape {
   static constexpr uint32_t TILE_W = BN * BK * 2;                       // 16 KB at BN 256
   static constexpr uint32_t STAGE_BYTES = 2 * TILE_A + 2 * TILE_W;      // 48 KB at BN 256
-  static constexpr int STAGES = BN == 256 ? 3 : 4;
+  static constexpr int STAGES = BN == 256 ? 3 : BN == 128 ? 4 : 6;
   static constexpr uint32_t TMEM_COLS = 2 * BN;                         // two accumulators
   static constexpr uint32_t STG_OFF = (uint32_t)STAGES * STAGE_BYTES;   // output staging
   static constexpr uint32_t BAR_OFF = STG_OFF + kEpiWarps * STG_WARP;   // mbarriers
@@ -151,6 +151,11 @@ __device__ __forceinline__ void bulk_wait_read_but_last() {
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
+// Pulls a kernel-parameter tensor map into the TMA unit's descriptor cache
+// ahead of its first use.
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap *tm) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
+}
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -222,21 +227,34 @@ __device__ __forceinline__ void load_residual(const TcGemmParams &p, int row, bo
   }
 }
 
+// The bias of one epilogue warp's columns of a tile (at most 96: a third of
+// 256), lane l of register k holding column cbase + 32 k + l (0 past N or past
+// the warp's range). Loaded before the warp waits for the accumulator, so its
+// latency hides behind the main loop, and read back with shuffles.
+struct BiasRegs {
+  float w[3];
+};
+__device__ __forceinline__ void load_bias_regs(const TcGemmParams &p, int cbase, int ncols,
+                                               int lane, BiasRegs &b) {
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    const int i = 32 * k + lane, c = cbase + i;
+    b.w[k] = (i < ncols && c < p.N) ? p.bias[c] : 0.f;
+  }
+}
+
 // Epilogue values of one 16-column chunk of one row: bias, then GELU or the
 // residual with padded-row zeroing. v holds the accumulator values of
-// columns col0..col0+15 (col0 < N, a multiple of 16).
+// columns col0..col0+15 (col0 < N, a multiple of 16); boff = col0 minus the
+// first column of the bias registers (a multiple of 16).
 __device__ __forceinline__ void epilogue_values(const TcGemmParams &p, float acc_scale, int row,
                                                 bool row_in, bool valid, int col0,
+                                                const BiasRegs &bias, int boff,
                                                 float (&v)[16]) {
-  const bool full = col0 + 16 <= p.N;
+  const int sel = boff >> 5, src0 = boff & 31;  // both warp-uniform
+  const float breg = sel == 0 ? bias.w[0] : (sel == 1 ? bias.w[1] : bias.w[2]);
 #pragma unroll
-  for (int j = 0; j < 16; ++j) v[j] *= acc_scale;
-#pragma unroll
-  for (int j = 0; j < 16; j += 4) {
-    float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (full || col0 + j < p.N) b4 = *reinterpret_cast<const float4 *>(p.bias + col0 + j);
-    v[j] += b4.x; v[j + 1] += b4.y; v[j + 2] += b4.z; v[j + 3] += b4.w;
-  }
+  for (int j = 0; j < 16; ++j) v[j] = fmaf(v[j], acc_scale, __shfl_sync(0xffffffffu, breg, src0 + j));
   if (p.epilogue == EPI_BIAS_GELU) {
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = gelu_erf(v[j]);
@@ -312,10 +330,11 @@ __device__ __forceinline__ void epilogue_chunk_out(const TcGemmParams &p, const 
                                                    const CUtensorMap *tm_lo, uint32_t stg_base,
                                                    uint8_t *stg_ptr_base, int &nstores, int lane,
                                                    int row0, bool valid, int col0,
-                                                   float acc_scale, float (&v)[16]) {
+                                                   float acc_scale, const BiasRegs &bias,
+                                                   int boff, float (&v)[16]) {
   const int row = row0 + lane;
   const bool row_in = row < p.M;
-  epilogue_values(p, acc_scale, row, row_in, valid, col0, v);
+  epilogue_values(p, acc_scale, row, row_in, valid, col0, bias, boff, v);
   if (p.vt_hi != nullptr && col0 >= p.vt_col0) {
     if (row_in) store_vt(p, row, col0, v);
     return;
@@ -394,6 +413,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int MT = (p.M + BM - 1) / BM, NT = (p.N + BN - 1) / BN;
   const int ntiles = MT * NT;
   pdl_trigger();
+  if (threadIdx.x == 32) {
+    prefetch_tmap(&tm_a_hi); prefetch_tmap(&tm_a_lo); prefetch_tmap(&tm_w_hi);
+    prefetch_tmap(&tm_w_lo); prefetch_tmap(&tm_c); prefetch_tmap(&tm_c_hi);
+    prefetch_tmap(&tm_c_lo);
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -477,6 +501,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
       const int ab = local & 1;
       const int m0 = (tile / NT) * BM, n0 = (tile % NT) * BN;
+      BiasRegs bias;
+      load_bias_regs(p, n0 + c_lo, c_hi - c_lo, lane, bias);
       mbar_wait(acc_full(ab), (local >> 1) & 1, p.status, 0x3000);
       tc_fence_after();
       const int row0 = m0 + q * 32;
@@ -499,12 +525,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(ra[i]);
         if (col0 < p.N)
           epilogue_chunk_out(p, &tm_c, &tm_c_hi, &tm_c_lo, stg, stg_ptr, nstores, lane, row0,
-                             valid, col0, acc_scale, v);
+                             valid, col0, acc_scale, bias, c0 - c_lo, v);
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(rb[i]);
         if (c0 + 16 < c_hi && col0 + 16 < p.N)
           epilogue_chunk_out(p, &tm_c, &tm_c_hi, &tm_c_lo, stg, stg_ptr, nstores, lane, row0,
-                             valid, col0 + 16, acc_scale, v);
+                             valid, col0 + 16, acc_scale, bias, c0 + 16 - c_lo, v);
       }
       tc_fence_before();
       __syncwarp();
@@ -631,6 +657,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int MT = (p.M + 255) / 256, NT = (p.N + PBN - 1) / PBN;
   const int ntiles = MT * NT;
   pdl_trigger();
+  if (threadIdx.x == 32) {
+    prefetch_tmap(&tm_a_hi); prefetch_tmap(&tm_a_lo); prefetch_tmap(&tm_w_hi);
+    prefetch_tmap(&tm_w_lo); prefetch_tmap(&tm_c); prefetch_tmap(&tm_c_hi);
+    prefetch_tmap(&tm_c_lo);
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < PSTAGES; ++s) {
@@ -725,6 +756,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = pair; tile < ntiles; tile += npairs, ++local) {
       const int ab = local & 1;
       const int m0 = (tile / NT) * 256 + 128 * (int)rank, n0 = (tile % NT) * PBN;
+      BiasRegs bias;
+      load_bias_regs(p, n0 + c_lo, c_hi - c_lo, lane, bias);
       mbar_wait(acc_full(ab), (local >> 1) & 1, p.status, 0x3000);
       tc_fence_after();
       const int row0 = m0 + q * 32;
@@ -747,12 +780,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(ra[i]);
         if (col0 < p.N)
           epilogue_chunk_out(p, &tm_c, &tm_c_hi, &tm_c_lo, stg, stg_ptr, nstores, lane, row0,
-                             valid, col0, acc_scale, v);
+                             valid, col0, acc_scale, bias, c0 - c_lo, v);
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(rb[i]);
         if (c0 + 16 < c_hi && col0 + 16 < p.N)
           epilogue_chunk_out(p, &tm_c, &tm_c_hi, &tm_c_lo, stg, stg_ptr, nstores, lane, row0,
-                             valid, col0 + 16, acc_scale, v);
+                             valid, col0 + 16, acc_scale, bias, c0 + 16 - c_lo, v);
       }
       tc_fence_before();
       __syncwarp();
@@ -938,9 +971,14 @@ int launch_gemm_tc3(const TcGemmParams &p, cudaStream_t stream) {
   // measured slower on B200: 70% of the MMA rate in the main loop against 84%)
   if (pair_tiles >= sms / 2) return launch_pair<256>(p, stream, sms);
   // N = 256 tiles halve the shared-memory operand traffic per FLOP; narrow
-  // projections use 128-wide tiles so every SM still gets work
-  const int64_t tiles256 = (int64_t)((p.M + BM - 1) / BM) * ((p.N + 255) / 256);
+  // projections use 128-wide tiles so every SM still gets work, and 64-wide
+  // ones when even those would leave most SMs idle (small batches, where each
+  // CTA runs one tile and its latency is the kernel's)
+  const int64_t mt128 = (p.M + BM - 1) / BM;
+  const int64_t tiles256 = mt128 * ((p.N + 255) / 256);
   if (tiles256 >= 2 * 148) return launch_bn<256>(p, stream);
+  const int64_t tiles128 = mt128 * ((p.N + 127) / 128);
+  if (2 * tiles128 <= sms) return launch_bn<64>(p, stream);
   return launch_bn<128>(p, stream);
 }
 

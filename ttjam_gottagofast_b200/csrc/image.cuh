@@ -12,7 +12,7 @@
 // Workspace (per call, [T = batch*seq] tokens):
 //   FFMA schedule:        qkv [T,3D] | ctx [T,D] | h [T,F]
 //   tensor-core schedule: qkv [T,3D] (or, when the attention also runs on
-//   tensor cores, head_dim 32 or 64, the fp16 split of q|k qk_hi/qk_lo [T,2D]
+//   tensor cores, any head_dim attention_tc_supported takes, the fp16 split of q|k qk_hi/qk_lo [T,2D]
 //   and of v transposed vt_hi/vt_lo [B*H, hd, seq_pad]) | the fp16 splits of
 //   the GEMM A operands: ln_hi/ln_lo [T,D], ctx_hi/ctx_lo [T,D], h_hi/h_lo [T,F].
 #pragma once
