@@ -666,11 +666,12 @@ ClusterChoice choose_cluster(const tt_config &cfg, int64_t batch, int64_t seq) {
   int64_t spc = (batch + ncl - 1) / ncl;
   spc = std::min<int64_t>(spc, rmax / seq);
   ncl = (batch + spc - 1) / spc;
-  // past one wave of clusters the per-op tensor-core schedule is faster
-  // (measured on B200 at seq 128: batch 4, one wave, 172 us against 243 us;
-  // batch 8, two waves, 338 us against 241 us); a forced cluster plan runs
-  // any number of waves
-  if (cfg.plan == TT_PLAN_AUTO && ncl > (int64_t)maxc) return c;
+  // The per-op tensor-core schedule (replayed as a CUDA graph) is faster past
+  // one wave of clusters and once a cluster holds more than 64 token rows
+  // (measured on B200, d 128, 4 layers: batch 4 x seq 16, 37 us against 127;
+  // batch 4 x seq 64 with one head, 96 against 147; batch 4 x seq 128, 172
+  // against 141). A forced cluster plan runs any number of waves and rows.
+  if (cfg.plan == TT_PLAN_AUTO && (ncl > (int64_t)maxc || spc * seq > 64)) return c;
   if (ncl * cl > INT32_MAX / 2) return c;
   c.cluster = cl;
   c.rmax = rmax;
