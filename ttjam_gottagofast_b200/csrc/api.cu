@@ -264,6 +264,14 @@ int forward_ops(const tt_config &cfg, const ImageLayout &L, const char *image, c
 // fp16 split, q|k|v GEMM, attention (writes the split context), out_proj GEMM
 // + residual, LN2 -> split, ffn_in GEMM + GELU (writes the split hidden),
 // ffn_out GEMM + residual; then the final LayerNorm.
+// Whether the tensor-core schedule folds both LayerNorms of a block into the
+// GEMMs that read them (small problems with d_model <= 128: 5 launches per
+// layer instead of 7).
+bool ops_tc_fuses_ln(const tt_config &cfg, int64_t tokens) {
+  return gemm_ln_fusable(tokens, 3 * cfg.d_model, cfg.d_model) &&
+         gemm_ln_fusable(tokens, cfg.ffn_dim, cfg.d_model);
+}
+
 int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image, const float *x,
                    const uint8_t *mask, int64_t batch, int64_t seq, float *y,
                    const WorkspaceLayout &W, char *ws, cudaStream_t stream) {
@@ -279,6 +287,7 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
   uint16_t *h_hi = WH(W.h_hi), *h_lo = WH(W.h_lo);
   DeviceStatus *status = reinterpret_cast<DeviceStatus *>(const_cast<char *>(image) + L.status);
   const float eps = 1e-5f;
+  const bool fuse_ln = ops_tc_fuses_ln(cfg, T);
   for (int l = 0; l < cfg.num_layers; ++l) {
     const LayerOffsets &o = L.layer[l];
     auto P = [&](size_t off) { return reinterpret_cast<const float *>(image + off); };
@@ -286,7 +295,8 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
     const float *wsc = P(o.wscale);  // accumulator scales of the four GEMMs
     const float *xin = (l == 0) ? x : y;
     int rc;
-    if ((rc = timed_launch(TT_KERNEL_LAYERNORM, stream, [&] {
+    if (!fuse_ln &&
+        (rc = timed_launch(TT_KERNEL_LAYERNORM, stream, [&] {
            return launch_layernorm(xin, nullptr, ln_hi, ln_lo, P(o.ln1_w), P(o.ln1_b), nullptr,
                                    0, T, D, eps, stream);
          })))
@@ -303,7 +313,12 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
     } else {
       g.C = qkv;
     }
-    if ((rc = timed_launch(TT_KERNEL_QKV, stream, [&] { return launch_gemm_tc3(g, stream); })))
+    if (fuse_ln) {
+      g.ln_x = xin; g.ln_gamma = P(o.ln1_w); g.ln_beta = P(o.ln1_b); g.ln_eps = eps;
+    }
+    if ((rc = timed_launch(TT_KERNEL_QKV, stream, [&] {
+           return fuse_ln ? launch_gemm_ln_tc(g, stream) : launch_gemm_tc3(g, stream);
+         })))
       return rc;
     const float scale = (float)(1.0 / std::sqrt((double)hd));
     if (W.tc_attention) {
@@ -331,7 +346,8 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
     go.M = (int)T; go.N = D; go.K = D; go.epilogue = EPI_BIAS_RESIDUAL;
     if ((rc = timed_launch(TT_KERNEL_OUT_PROJ, stream, [&] { return launch_gemm_tc3(go, stream); })))
       return rc;
-    if ((rc = timed_launch(TT_KERNEL_LAYERNORM, stream, [&] {
+    if (!fuse_ln &&
+        (rc = timed_launch(TT_KERNEL_LAYERNORM, stream, [&] {
            return launch_layernorm(y, nullptr, ln_hi, ln_lo, P(o.ln2_w), P(o.ln2_b), nullptr, 0,
                                    T, D, eps, stream);
          })))
@@ -342,7 +358,12 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
     g1.bias = P(o.b1); g1.H_hi = h_hi; g1.H_lo = h_lo; g1.h_cols = F; g1.ldc = F;
     g1.status = status;
     g1.M = (int)T; g1.N = F; g1.K = D; g1.epilogue = EPI_BIAS_GELU;
-    if ((rc = timed_launch(TT_KERNEL_FFN_IN, stream, [&] { return launch_gemm_tc3(g1, stream); })))
+    if (fuse_ln) {
+      g1.ln_x = y; g1.ln_gamma = P(o.ln2_w); g1.ln_beta = P(o.ln2_b); g1.ln_eps = eps;
+    }
+    if ((rc = timed_launch(TT_KERNEL_FFN_IN, stream, [&] {
+           return fuse_ln ? launch_gemm_ln_tc(g1, stream) : launch_gemm_tc3(g1, stream);
+         })))
       return rc;
     TcGemmParams g2{};
     g2.A_hi = h_hi; g2.A_lo = h_lo; g2.lda = F; g2.W_hi = PH(o.w2_hi); g2.W_lo = PH(o.w2_lo);
@@ -447,7 +468,8 @@ int tt_forward_launch_count(const tt_config *cfg, int64_t batch, int64_t seq) {
   const int plan = forward_plan(cfg, batch, seq);
   if (plan < 0) return plan;
   if (plan == PLAN_CLUSTER) return 1;
-  if (plan == PLAN_OPS_TC) return 7 * cfg->num_layers + 1;
+  if (plan == PLAN_OPS_TC)
+    return (ops_tc_fuses_ln(*cfg, batch * seq) ? 5 : 7) * cfg->num_layers + 1;
   return 5 * cfg->num_layers + 1;
 }
 

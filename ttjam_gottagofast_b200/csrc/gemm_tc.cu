@@ -803,6 +803,224 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---- LayerNorm-prologue variant for small problems ---------------------------
+// One 128 x BN output tile per CTA (no persistence), K <= 128. All 16 warps
+// first turn the tile's 128 rows of x into LayerNorm(x) (nn.LayerNorm: biased
+// variance, two passes over the row held in registers, gamma / beta) and
+// write its fp16 split straight into shared memory in the 64-byte-swizzled
+// K-major layout the MMAs read (the layout the TMA would have written:
+// 16-byte unit u of row r of a k-block at unit u ^ ((r >> 1) & 3)), while
+// the TMA brings all of the tile's W k-blocks at once. Then one thread issues
+// the MMAs into a single accumulator and warps 4-15 run the usual epilogue.
+// This stands in for a LayerNorm launch plus the normal GEMM where a launch's
+// latency, not its work, is the cost.
+constexpr int LN_MAX_K = 128;
+
+template <int BN>
+struct LnShape {
+  static constexpr int KB_MAX = LN_MAX_K / BK;             // k-blocks of 32
+  static constexpr uint32_t A_KB = 2 * TILE_A;             // A_hi | A_lo of one k-block
+  static constexpr uint32_t TILE_W = BN * BK * 2;
+  static constexpr uint32_t W_KB = 2 * TILE_W;             // W_hi | W_lo of one k-block
+  static constexpr uint32_t W_OFF = KB_MAX * A_KB;
+  static constexpr uint32_t STG_OFF = W_OFF + KB_MAX * W_KB;
+  static constexpr uint32_t BAR_OFF = STG_OFF + kEpiWarps * STG_WARP;
+  static constexpr size_t SMEM_BYTES = (size_t)BAR_OFF + 256 + 1024;
+  static constexpr uint32_t TMEM_COLS = BN;
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+  static_assert(W_OFF % 1024 == 0 && STG_OFF % 1024 == 0, "swizzle period");
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_ln_tc_kernel(const __grid_constant__ CUtensorMap tm_w_hi,
+                      const __grid_constant__ CUtensorMap tm_w_lo,
+                      const __grid_constant__ CUtensorMap tm_c,
+                      const __grid_constant__ CUtensorMap tm_c_hi,
+                      const __grid_constant__ CUtensorMap tm_c_lo, const TcGemmParams p) {
+  using Sh = LnShape<BN>;
+  constexpr uint32_t IDESC = idesc_f16<BN>();
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t *base_ptr = smem_raw + (base - raw);
+  const uint32_t bars = base + Sh::BAR_OFF;
+  const uint32_t w_full = bars, acc_full = bars + 8u;
+  const uint32_t tmem_slot = bars + 16u;
+  uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int K = p.K, KB = (K + BK - 1) / BK;
+  const int NT = (p.N + BN - 1) / BN;
+  const int m0 = (int)(blockIdx.x / NT) * BM, n0 = (int)(blockIdx.x % NT) * BN;
+  pdl_trigger();
+  if (threadIdx.x == 32) {
+    prefetch_tmap(&tm_w_hi); prefetch_tmap(&tm_w_lo); prefetch_tmap(&tm_c);
+    prefetch_tmap(&tm_c_hi); prefetch_tmap(&tm_c_lo);
+  }
+  if (threadIdx.x == 0) {
+    mbar_init(w_full, 1);
+    mbar_init(acc_full, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot),
+                 "r"(Sh::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot_ptr;
+  if (threadIdx.x == 0) {
+    // the weights are packed once and no kernel of a forward writes them, so
+    // their loads start before the wait on the previous kernel
+    mbar_expect_tx(w_full, (uint32_t)KB * Sh::W_KB);
+    for (int kb = 0; kb < KB; ++kb) {
+      const uint32_t w = base + Sh::W_OFF + (uint32_t)kb * Sh::W_KB;
+      tma_load_2d(w, &tm_w_hi, kb * BK, n0, w_full);
+      tma_load_2d(w + Sh::TILE_W, &tm_w_lo, kb * BK, n0, w_full);
+    }
+  }
+  pdl_wait();  // x (and R) come from the previous kernel
+
+  // ---- LayerNorm rows -> fp16 split A tile in shared memory -----------------
+  {
+    // lane l holds features [4l, 4l + 4): k-block l / 8, 16-byte unit
+    // (l % 8) / 2, half (l % 2) of that unit
+    const int k = 4 * lane;
+    const bool kin = k < K;
+    const bool kpad = k < KB * BK;  // inside the tile's k-blocks (zeros past K)
+    float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f), b4 = g4;
+    if (kin) {
+      g4 = *reinterpret_cast<const float4 *>(p.ln_gamma + k);
+      b4 = *reinterpret_cast<const float4 *>(p.ln_beta + k);
+    }
+    const float inv_k = 1.0f / (float)K;
+    const int kb = lane >> 3, u = (lane & 7) >> 1, half = lane & 1;
+    // a warp's 8 rows (r = warp + 16 i) together: their loads are in flight at
+    // once and their shuffle reductions interleave
+    constexpr int RW = BM / (kThreads / 32);
+    float4 a[RW];
+#pragma unroll
+    for (int i = 0; i < RW; ++i) {
+      const int row = m0 + warp + 16 * i;
+      a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (kin && row < p.M) a[i] = *reinterpret_cast<const float4 *>(p.ln_x + (int64_t)row * K + k);
+    }
+    float st[RW];
+#pragma unroll
+    for (int i = 0; i < RW; ++i) st[i] = (a[i].x + a[i].y) + (a[i].z + a[i].w);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int i = 0; i < RW; ++i) st[i] += __shfl_xor_sync(0xffffffffu, st[i], o);
+#pragma unroll
+    for (int i = 0; i < RW; ++i) {
+      const float mean = st[i] * inv_k;
+      a[i].x = kin ? a[i].x - mean : 0.f;
+      a[i].y = kin ? a[i].y - mean : 0.f;
+      a[i].z = kin ? a[i].z - mean : 0.f;
+      a[i].w = kin ? a[i].w - mean : 0.f;
+      st[i] = (a[i].x * a[i].x + a[i].y * a[i].y) + (a[i].z * a[i].z + a[i].w * a[i].w);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int i = 0; i < RW; ++i) st[i] += __shfl_xor_sync(0xffffffffu, st[i], o);
+    if (kpad) {
+#pragma unroll
+      for (int i = 0; i < RW; ++i) {
+        const int r = warp + 16 * i;
+        const float rs = rsqrtf(st[i] * inv_k + p.ln_eps);
+        const float o0 = kin ? a[i].x * rs * g4.x + b4.x : 0.f;
+        const float o1 = kin ? a[i].y * rs * g4.y + b4.y : 0.f;
+        const float o2 = kin ? a[i].z * rs * g4.z + b4.z : 0.f;
+        const float o3 = kin ? a[i].w * rs * g4.w + b4.w : 0.f;
+        uint32_t h01, l01, h23, l23;
+        f16_split2(o0, o1, h01, l01);
+        f16_split2(o2, o3, h23, l23);
+        const uint32_t off = (uint32_t)kb * Sh::A_KB + (uint32_t)r * 64u +
+                             ((uint32_t)(u ^ ((r >> 1) & 3)) << 4) + 8u * half;
+        *reinterpret_cast<uint2 *>(base_ptr + off) = make_uint2(h01, h23);
+        *reinterpret_cast<uint2 *>(base_ptr + off + TILE_A) = make_uint2(l01, l23);
+      }
+    }
+  }
+  fence_proxy_async_smem();  // the generic-proxy writes, visible to the MMAs
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ---------------------------------------------------------
+    mbar_wait(w_full, 0, p.status, 0x5100);
+    tc_fence_after();
+    for (int kb = 0; kb < KB; ++kb) {
+      const uint32_t a = base + (uint32_t)kb * Sh::A_KB;
+      const uint32_t w = base + Sh::W_OFF + (uint32_t)kb * Sh::W_KB;
+      const uint64_t a_hi = umma_desc_sw64(a), a_lo = umma_desc_sw64(a + TILE_A);
+      const uint64_t w_hi = umma_desc_sw64(w), w_lo = umma_desc_sw64(w + Sh::TILE_W);
+#pragma unroll
+      for (int k = 0; k < BK / 16; ++k) {
+        const uint64_t ko = (uint64_t)(k * 2);
+        umma_f16(tmem_base, a_hi + ko, w_hi + ko, IDESC, (kb | k) != 0);
+        umma_f16(tmem_base, a_hi + ko, w_lo + ko, IDESC, 1);
+        umma_f16(tmem_base, a_lo + ko, w_hi + ko, IDESC, 1);
+      }
+    }
+    umma_commit(acc_full);
+  } else if (warp >= 4) {
+    // ---- epilogue: as in gemm_tc3_kernel, one tile ------------------------------
+    const int q = warp & 3;
+    const int cgrp = (warp - 4) >> 2;
+    const int c_lo = 16 * (cgrp * (BN / 16) / 3), c_hi = 16 * ((cgrp + 1) * (BN / 16) / 3);
+    const uint32_t stg = base + Sh::STG_OFF + (uint32_t)(warp - 4) * STG_WARP;
+    uint8_t *stg_ptr = smem_raw + (stg - raw);
+    const float acc_scale = *p.acc_scale;
+    int nstores = 0;
+    BiasRegs bias;
+    load_bias_regs(p, n0 + c_lo, c_hi - c_lo, lane, bias);
+    mbar_wait(acc_full, 0, p.status, 0x5200);
+    tc_fence_after();
+    const int row0 = m0 + q * 32;
+    const int row = row0 + lane;
+    const bool row_in = row < p.M;
+    const bool valid = row_in && (p.row_mask == nullptr || p.row_mask[row] != 0);
+#pragma unroll 1
+    for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
+      uint32_t ra[16], rb[16];
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
+      tmem_ld16_async(taddr, ra);
+      if (c0 + 16 < c_hi) tmem_ld16_async(taddr + 16, rb);  // warp-uniform
+      tmem_wait_ld();
+      const int col0 = n0 + c0;
+      if (row0 >= p.M) continue;  // warp-uniform
+      float v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(ra[i]);
+      if (col0 < p.N)
+        epilogue_chunk_out(p, &tm_c, &tm_c_hi, &tm_c_lo, stg, stg_ptr, nstores, lane, row0,
+                           valid, col0, acc_scale, bias, c0 - c_lo, v);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(rb[i]);
+      if (c0 + 16 < c_hi && col0 + 16 < p.N)
+        epilogue_chunk_out(p, &tm_c, &tm_c_hi, &tm_c_lo, stg, stg_ptr, nstores, lane, row0,
+                           valid, col0 + 16, acc_scale, bias, c0 + 16 - c_lo, v);
+    }
+    if (lane == 0) bulk_wait_all();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(Sh::TMEM_COLS)
+                 : "memory");
+  }
+}
+
 // cuTensorMapEncodeTiled, resolved at run time through the runtime's driver
 // entry-point query so the library has no link-time dependency on libcuda.
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -933,6 +1151,30 @@ int launch_pair(const TcGemmParams &p, cudaStream_t stream, int sms) {
   return TT_OK;
 }
 
+template <int BN>
+int launch_ln(const TcGemmParams &p, cudaStream_t stream) {
+  using Sh = LnShape<BN>;
+  CUtensorMap tw_hi, tw_lo;
+  int rc;
+  if ((rc = make_operand_map(&tw_hi, p.W_hi, p.N, p.K, p.K, BN)) ||
+      (rc = make_operand_map(&tw_lo, p.W_lo, p.N, p.K, p.K, BN)))
+    return rc;
+  CUtensorMap tc, tc_hi, tc_lo;
+  if ((rc = make_out_maps(p, tw_hi, &tc, &tc_hi, &tc_lo))) return rc;
+  static bool attr_set = false;
+  if (!attr_set) {
+    TT_CUDA_TRY(cudaFuncSetAttribute(gemm_ln_tc_kernel<BN>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)Sh::SMEM_BYTES));
+    attr_set = true;
+  }
+  const int64_t tiles = (int64_t)((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
+  TT_CUDA_TRY(launch_kernel(gemm_ln_tc_kernel<BN>, dim3((unsigned)tiles), dim3(kThreads),
+                            Sh::SMEM_BYTES, stream, 1, tw_hi, tw_lo, tc, tc_hi, tc_lo, p));
+  TT_LAUNCH_CHECK("gemm_ln_tc");
+  return TT_OK;
+}
+
 int sm_count() {
   static int sms = 0;
   if (sms == 0) {
@@ -980,6 +1222,41 @@ int launch_gemm_tc3(const TcGemmParams &p, cudaStream_t stream) {
   const int64_t tiles128 = mt128 * ((p.N + 127) / 128);
   if (2 * tiles128 <= sms) return launch_bn<64>(p, stream);
   return launch_bn<128>(p, stream);
+}
+
+bool gemm_ln_fusable(int64_t M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0 || K > LN_MAX_K || K % 8 != 0 || N % 8 != 0) return false;
+  // problems whose tiles (64 wide when 128-wide ones would fill under half the
+  // SMs, as launch_gemm_ln_tc picks) all run at once: the kernel is not
+  // persistent, and a second wave of CTAs, each with its own LayerNorm of the
+  // rows, costs more than the separate LayerNorm launch saves (measured on
+  // B200 at 8192 x 384 x 128: 192 tiles, 21 us against 15 for the unfused GEMM)
+  const int sms = sm_count();
+  const int64_t tiles128 = (M + BM - 1) / BM * ((N + 127) / 128);
+  const int64_t tiles = 2 * tiles128 <= sms ? 2 * tiles128 : tiles128;
+  return tiles <= sms;
+}
+
+int launch_gemm_ln_tc(const TcGemmParams &p, cudaStream_t stream) {
+  if (p.M <= 0 || p.N <= 0) return TT_OK;
+  if (p.ln_x == nullptr || p.ln_gamma == nullptr || p.ln_beta == nullptr ||
+      p.acc_scale == nullptr)
+    return fail(TT_ERR_INVALID_ARGUMENT, "gemm_ln_tc: ln_x, ln_gamma, ln_beta or acc_scale is null");
+  if (p.K <= 0 || p.K > LN_MAX_K || p.K % 8 != 0 || p.N % 8 != 0 || p.ldc % 4 != 0)
+    return fail(TT_ERR_UNSUPPORTED, "gemm_ln_tc: K must be a multiple of 8 up to 128, N of 8");
+  if ((reinterpret_cast<uintptr_t>(p.ln_x) | reinterpret_cast<uintptr_t>(p.ln_gamma) |
+       reinterpret_cast<uintptr_t>(p.ln_beta)) & 15)
+    return fail(TT_ERR_INVALID_ARGUMENT, "gemm_ln_tc: LayerNorm operands must be 16-byte aligned");
+  if ((p.C != nullptr) == (p.H_hi != nullptr) || (p.H_hi != nullptr) != (p.H_lo != nullptr))
+    return fail(TT_ERR_UNSUPPORTED, "gemm_ln_tc: exactly one of C and the H split");
+  if (p.H_hi != nullptr &&
+      (p.h_cols % 8 != 0 || (p.vt_hi != nullptr ? p.h_cols != p.vt_col0 : p.h_cols != p.N)))
+    return fail(TT_ERR_UNSUPPORTED, "gemm_ln_tc: the fp16 split covers the columns before v");
+  if (p.vt_hi != nullptr && (p.vt_col0 % 16 != 0 || p.head_dim % 8 != 0 || p.seq_pad % 8 != 0))
+    return fail(TT_ERR_UNSUPPORTED, "gemm_ln_tc: transposed value columns need 8-aligned heads");
+  const int64_t tiles128 = (p.M + BM - 1) / BM * ((p.N + 127) / 128);
+  if (2 * tiles128 <= sm_count()) return launch_ln<64>(p, stream);
+  return launch_ln<128>(p, stream);
 }
 
 }  // namespace tt

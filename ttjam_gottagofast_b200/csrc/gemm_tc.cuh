@@ -31,8 +31,23 @@ struct TcGemmParams {
   int h_cols;
   uint16_t *vt_hi, *vt_lo;
   int vt_col0, seq, seq_pad, heads, head_dim;
+  // LayerNorm prologue (launch_gemm_ln_tc only): A = LayerNorm(ln_x) over K
+  // features (nn.LayerNorm semantics, eps ln_eps), split in shared memory;
+  // A_hi / A_lo / lda are then unused
+  const float *ln_x;              // [M, K] fp32
+  const float *ln_gamma, *ln_beta;
+  float ln_eps;
 };
 
 int launch_gemm_tc3(const TcGemmParams &p, cudaStream_t stream);
+
+// Whether launch_gemm_ln_tc takes an M x N x K problem: K (the LayerNorm
+// width) at most 128 and a problem small enough for the single-CTA schedule.
+bool gemm_ln_fusable(int64_t M, int N, int K);
+// The same GEMM with its A operand computed in the kernel as the fp16 split of
+// LayerNorm(ln_x): one output tile per CTA, the whole A tile resident in
+// shared memory. It replaces a LayerNorm launch and its round trip through
+// memory for the small problems where each launch's latency is the cost.
+int launch_gemm_ln_tc(const TcGemmParams &p, cudaStream_t stream);
 
 }  // namespace tt
