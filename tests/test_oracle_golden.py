@@ -51,3 +51,16 @@ def test_oracle_batch_chunking_is_exact():
     a = oracle.forward(p, case.config, x, mask)
     b = oracle.forward(p, case.config, x, mask, batch_chunk=1)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("case", GOLDENS, ids=GOLDEN_IDS)
+def test_oracle_query_chunking_matches_reference_goldens(case):
+    """The query-blocked attention (for sequences too long for one [S,S] score
+    tensor) against the reference's own outputs: blocks of 16 query rows,
+    causal key truncation included, agree with the reference to rounding."""
+    p = oracle.init_params(case.config, seed=case.meta["model_seed"])
+    x = torch.from_numpy(case.x)
+    mask = torch.from_numpy(case.mask) if case.uses_mask else None
+    y = oracle.forward(p, case.config, x, mask, query_chunk=16).numpy()
+    assert np.isfinite(y).all()
+    np.testing.assert_allclose(y, case.y, rtol=0, atol=1e-5)
