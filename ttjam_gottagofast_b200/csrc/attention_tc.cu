@@ -289,7 +289,7 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
   constexpr uint32_t T_QHI = Sh::T_QHI, T_QLO = Sh::T_QLO, T_O = Sh::T_O,
                      TMEM_COLS = Sh::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ int s_kv_len;
+  __shared__ int s_kv_len, s_first_hole;
   __shared__ float s_rowmax[2][2][128];  // [tile parity][key half][row]
   __shared__ float s_rowsum[2][128];
   const uint32_t raw = smem_u32(smem_raw);
@@ -324,27 +324,43 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
   const uint8_t *mrow = p.mask ? p.mask + b * S : nullptr;
 
   pdl_trigger();
-  // kv_len = 1 + last valid key; keys at or after it are all padding
-  if (threadIdx.x == 0) s_kv_len = mrow ? 0 : S;
+  // kv_len = 1 + last valid key; keys at or after it are all padding.
+  // first_hole = the first padded key; when it is at or past kv_len the valid
+  // keys are a prefix and the tile loop takes them from kv_len alone,
+  // without reading the mask again.
+  if (threadIdx.x == 0) {
+    s_kv_len = mrow ? 0 : S;
+    s_first_hole = S;
+  }
   __syncthreads();
   if (mrow) {
-    int last = 0;
+    int last = 0, hole = S;
     if ((reinterpret_cast<uintptr_t>(mrow) & 15) == 0 && S % 16 == 0) {
       for (int j = threadIdx.x; j < S / 16; j += kThreads) {
         const uint4 v = reinterpret_cast<const uint4 *>(mrow)[j];
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
+        for (int k = 0; k < 4; ++k) {
           if (w[k]) last = 16 * j + 4 * k + (31 - __clz((int)w[k])) / 8 + 1;
+          // lowest zero byte of w[k] (the lowest flagged byte of this test
+          // is always a true zero)
+          const uint32_t z = (w[k] - 0x01010101u) & ~w[k] & 0x80808080u;
+          if (z) hole = min(hole, 16 * j + 4 * k + (__ffs((int)z) - 1) / 8);
+        }
       }
     } else {
-      for (int j = threadIdx.x; j < S; j += kThreads)
+      for (int j = threadIdx.x; j < S; j += kThreads) {
         if (mrow[j]) last = j + 1;
+        else hole = min(hole, j);
+      }
     }
     if (last) atomicMax(&s_kv_len, last);
+    if (hole < S) atomicMin(&s_first_hole, hole);
   }
   __syncthreads();
   const int kv_len = s_kv_len;
+  // the mask the tile loop reads: none when the valid keys are a prefix
+  const uint8_t *mtile = s_first_hole >= kv_len ? nullptr : mrow;
   if (q0 >= kv_len) return;  // every query of this tile is padding (uniform exit)
   const int kv_end = p.causal ? min(kv_len, q0 + BQ) : kv_len;
   const int nkv = (kv_end + BKV - 1) / BKV;
@@ -500,9 +516,13 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
       const int sb = j & 1;
       const int k0 = j * BKV + 32 * kh;     // first key of this thread's half
       uint32_t ok;
-      {
+      if (mtile == nullptr) {
+        // keys k0 .. kv_end - 1 of this half
+        const int n = kv_end - k0;
+        ok = n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : (1u << n) - 1u);
+      } else {
         const int ka = k0 + lane;
-        ok = __ballot_sync(0xffffffffu, ka < kv_end && (mrow == nullptr || mrow[ka] != 0));
+        ok = __ballot_sync(0xffffffffu, ka < kv_end && mtile[ka] != 0);
       }
       const bool diag = p.causal && k0 + 31 > q0;  // half reaches past the first query
       // every key of this half allowed for every row of the warp (warp-uniform)
