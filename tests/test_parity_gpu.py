@@ -213,6 +213,29 @@ def test_weight_update_repacks():
     check(ref, y1, "after in-place update")
 
 
+@pytest.mark.parametrize("d,h", [(128, 4), (256, 4), (128, 1), (256, 1)],
+                         ids=["hd32", "hd64", "hd128", "hd256"])
+def test_peaked_scores_rescale_the_context(d, h):
+    """Scores spread over hundreds of log2 units (q_proj weights x 32), so that
+    rows raise their softmax reference max at later key tiles and the
+    attention rescales the context it holds in tensor memory, rows of one warp
+    at different tiles. Every applicable schedule against the oracle, key
+    padding included."""
+    from ttjam_gottagofast_b200.config import TransformerConfig
+    cfg = TransformerConfig(batch_size=2, seq_len=300, d_model=d, num_heads=h, ffn_dim=128,
+                            num_layers=1, causal=True)
+    params = dict(oracle.init_params(cfg, seed=4321, device=DEV))
+    params["layers.0.attention.q_proj.weight"] = params["layers.0.attention.q_proj.weight"] * 32
+    model = UserOptimizedTransformer(cfg).to(DEV).eval()
+    model.load_state_dict(params, strict=True)
+    x, mask = generate_random_case(cfg, "cpu", torch.float32, 77, 0.3, 1.0)
+    x, mask = x.to(DEV), mask.to(DEV)
+    ref = oracle.forward(params, cfg, x, mask)
+    for plan, y in run_plans(model, x, mask).items():
+        check(ref, y, f"peaked d{d} h{h}[{plan}]")
+    assert model.read_device_status() == (0, 0)
+
+
 def test_no_mask_and_all_true_mask_agree():
     cfg = WORKLOADS["B1"].config
     model, _ = model_for(cfg)

@@ -561,25 +561,32 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
       // the two warps that share these 32 rows (one per key half)
       pair_barrier(warp & 3);
       mx = fmaxf(mx, s_rowmax[sb][kh ^ 1][t]);
-      if (mx > m_ref + kLazy || (m_ref == -CUDART_INF_F && mx != -CUDART_INF_F)) {
-        const float alpha = fast_exp2(m_ref - mx);  // 0 when m_ref is -inf
-        if (j > 0 && m_ref != -CUDART_INF_F) {
-          // the context in tensor memory must hold P_{j-1}.V_{j-1} before it
-          // is rescaled. S_j was committed after P_{j-2}.V_{j-2}, so o_done
-          // has completed j - 1 or j phases here and the parity wait is exact.
-          mbar_wait(o_done, (j - 1) & 1, p.status, 0x4600 + j);
-          fence_after();
+      const bool raise = mx > m_ref + kLazy || (m_ref == -CUDART_INF_F && mx != -CUDART_INF_F);
+      const float alpha = raise ? fast_exp2(m_ref - mx) : 1.f;  // 0 when m_ref is -inf
+      // The context rows of the warp are rescaled together when any of them
+      // needs it (alpha = 1 for the others): the tensor-memory loads and
+      // stores are warp-collective (.sync.aligned), so they run under a
+      // warp-uniform condition. A row whose m_ref is -inf has a zero context
+      // row, which alpha = 0 keeps.
+      if (__any_sync(0xffffffffu, raise && m_ref != -CUDART_INF_F) && j > 0) {
+        // the context in tensor memory must hold P_{j-1}.V_{j-1} before it
+        // is rescaled. S_j was committed after P_{j-2}.V_{j-2}, so o_done
+        // has completed j - 1 or j phases here and the parity wait is exact.
+        mbar_wait(o_done, (j - 1) & 1, p.status, 0x4600 + j);
+        fence_after();
+        // this thread's HDO / 2 context columns (HDO = HD up to head_dim 128)
 #pragma unroll
-          for (int c = 0; c < HD / 2; c += Sh::OC) {
-            float ov[Sh::OC];
-            tmem_ld_n<Sh::OC>(lane_base + T_O + dim_off + c, ov);
-            tmem_wait_ld();
+        for (int c = 0; c < HDO / 2; c += Sh::OC) {
+          float ov[Sh::OC];
+          tmem_ld_n<Sh::OC>(lane_base + T_O + dim_off + c, ov);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < Sh::OC; ++i) ov[i] *= alpha;
-            if constexpr (Sh::OC == 16) tmem_st16_f32(lane_base + T_O + dim_off + c, ov);
-            else tmem_st8_f32(lane_base + T_O + dim_off + c, ov);
-          }
+          for (int i = 0; i < Sh::OC; ++i) ov[i] *= alpha;
+          if constexpr (Sh::OC == 16) tmem_st16_f32(lane_base + T_O + dim_off + c, ov);
+          else tmem_st8_f32(lane_base + T_O + dim_off + c, ov);
         }
+      }
+      if (raise) {
         l *= alpha;
         m_ref = mx;
       }
