@@ -45,6 +45,8 @@
 #include <cuda.h>
 #include <math_constants.h>
 
+#include <algorithm>
+
 #include "attention_tc.cuh"
 
 namespace tt {
@@ -277,7 +279,7 @@ __device__ __forceinline__ void pair_barrier(int q) {
   }
 }
 
-template <int HD>
+template <int HD, bool GROUPED>
 __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
                                                   const CUtensorMap &tm_lo,
                                                   const CUtensorMap &tm_vhi,
@@ -308,15 +310,21 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.seq, D = p.d_model, hd = p.head_dim;  // hd < HD only for head_dim 8 (HD 16)
-  // one-dimensional grid ordered by query tile, latest (heaviest under the
-  // causal mask) first, so that the longest CTAs start first and the short
-  // ones fill the tail
-  const int64_t nbh = p.batch * p.num_heads;
+  // Grid: along x, query tiles latest (heaviest under the causal mask)
+  // first, every (sequence, head) pair per tile, so that the longest CTAs
+  // start first and the short ones fill the tail. GROUPED (very long
+  // sequences, whose K/V far exceed the L2): blockIdx.y is a group of
+  // bh_group pairs and x covers only the group's pairs; the groups run one
+  // after another, so the CTAs running at one time share the K/V of a few
+  // pairs through the L2. (Two instantiations: the group arithmetic costs
+  // registers that the common case does not pay.)
   // head_dim 256: CTA pairs (consecutive) share a query tile and head, each
   // computing output dims [oh * HDO, oh * HDO + HDO)
-  const int64_t per_tile = nbh * Sh::NSPLIT;
+  const int64_t group = GROUPED ? (int64_t)p.bh_group : p.batch * p.num_heads;
+  const int64_t per_tile = group * Sh::NSPLIT;
   const int qt = (S + BQ - 1) / BQ - 1 - (int)(blockIdx.x / per_tile);
-  const int64_t bh_idx = (blockIdx.x % per_tile) / Sh::NSPLIT;
+  const int64_t bh_idx = (GROUPED ? (int64_t)blockIdx.y * group : 0) +
+                         (int64_t)((blockIdx.x % per_tile) / Sh::NSPLIT);
   const int oh = (int)(blockIdx.x % Sh::NSPLIT);
   const int h = (int)(bh_idx % p.num_heads);
   const int64_t b = bh_idx / p.num_heads;
@@ -664,29 +672,31 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
 // 2, 2 on the four SM sub-partitions, so two CTAs put 6 warps on one
 // sub-partition, whose 16K registers then allow 85 per thread: the kernel is
 // held to 80. Head_dim 128 runs one CTA per SM (512 tensor-memory columns).
-template <int HD>
+template <int HD, bool GROUPED>
 __global__ void __maxnreg__(80)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_hi,
                         const __grid_constant__ CUtensorMap tm_lo,
                         const __grid_constant__ CUtensorMap tm_vhi,
                         const __grid_constant__ CUtensorMap tm_vlo, const AttentionTcParams p) {
-  attention_tc_body<HD>(tm_hi, tm_lo, tm_vhi, tm_vlo, p);
+  attention_tc_body<HD, GROUPED>(tm_hi, tm_lo, tm_vhi, tm_vlo, p);
 }
+template <bool GROUPED>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_tc_kernel_hd128(const __grid_constant__ CUtensorMap tm_hi,
                               const __grid_constant__ CUtensorMap tm_lo,
                               const __grid_constant__ CUtensorMap tm_vhi,
                               const __grid_constant__ CUtensorMap tm_vlo,
                               const AttentionTcParams p) {
-  attention_tc_body<128>(tm_hi, tm_lo, tm_vhi, tm_vlo, p);
+  attention_tc_body<128, GROUPED>(tm_hi, tm_lo, tm_vhi, tm_vlo, p);
 }
+template <bool GROUPED>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_tc_kernel_hd256(const __grid_constant__ CUtensorMap tm_hi,
                               const __grid_constant__ CUtensorMap tm_lo,
                               const __grid_constant__ CUtensorMap tm_vhi,
                               const __grid_constant__ CUtensorMap tm_vlo,
                               const AttentionTcParams p) {
-  attention_tc_body<256>(tm_hi, tm_lo, tm_vhi, tm_vlo, p);
+  attention_tc_body<256, GROUPED>(tm_hi, tm_lo, tm_vhi, tm_vlo, p);
 }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -757,18 +767,18 @@ int make_vt_map(CUtensorMap *tm, const uint16_t *ptr, int64_t bh, int seq, int s
   return TT_OK;
 }
 
-template <int HD>
+template <int HD, bool GROUPED>
 constexpr auto attention_kernel_for() {
-  if constexpr (HD == 256) return &attention_tc_kernel_hd256;
-  else if constexpr (HD == 128) return &attention_tc_kernel_hd128;
-  else return &attention_tc_kernel<HD>;
+  if constexpr (HD == 256) return &attention_tc_kernel_hd256<GROUPED>;
+  else if constexpr (HD == 128) return &attention_tc_kernel_hd128<GROUPED>;
+  else return &attention_tc_kernel<HD, GROUPED>;
 }
 
-template <int HD>
-int launch_hd(const AttentionTcParams &p, const CUtensorMap &thi, const CUtensorMap &tlo,
-              const CUtensorMap &tvhi, const CUtensorMap &tvlo, cudaStream_t stream) {
+template <int HD, bool GROUPED>
+int launch_hd_as(const AttentionTcParams &p, const CUtensorMap &thi, const CUtensorMap &tlo,
+                 const CUtensorMap &tvhi, const CUtensorMap &tvlo, cudaStream_t stream) {
   using Sh = AtShape<HD>;
-  constexpr auto fn = attention_kernel_for<HD>();
+  constexpr auto fn = attention_kernel_for<HD, GROUPED>();
   static bool attr_set = false;
   if (!attr_set) {
     TT_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -778,12 +788,21 @@ int launch_hd(const AttentionTcParams &p, const CUtensorMap &thi, const CUtensor
                                      (int)cudaSharedmemCarveoutMaxShared));
     attr_set = true;
   }
-  const int64_t ctas = (int64_t)((p.seq + BQ - 1) / BQ) * p.num_heads * p.batch * Sh::NSPLIT;
-  dim3 grid((unsigned)ctas);
+  const int64_t ctas_x = (int64_t)((p.seq + BQ - 1) / BQ) * p.bh_group * Sh::NSPLIT;
+  const int64_t groups = p.batch * p.num_heads / p.bh_group;
+  dim3 grid((unsigned)ctas_x, (unsigned)groups);
   TT_CUDA_TRY(launch_kernel(fn, grid, dim3(kThreads), Sh::SMEM_BYTES, stream, 1, thi, tlo, tvhi,
                             tvlo, p));
   TT_LAUNCH_CHECK("attention_tc");
   return TT_OK;
+}
+
+template <int HD>
+int launch_hd(const AttentionTcParams &p, const CUtensorMap &thi, const CUtensorMap &tlo,
+              const CUtensorMap &tvhi, const CUtensorMap &tvlo, cudaStream_t stream) {
+  if (p.bh_group < p.batch * p.num_heads)
+    return launch_hd_as<HD, true>(p, thi, tlo, tvhi, tvlo, stream);
+  return launch_hd_as<HD, false>(p, thi, tlo, tvhi, tvlo, stream);
 }
 
 }  // namespace
@@ -816,11 +835,29 @@ int launch_attention_tc(const AttentionTcParams &p, cudaStream_t stream) {
       (rc = make_vt_map(&tvhi, p.vt_hi, bh, p.seq, p.seq_pad, p.head_dim, hd_mma > 128 ? 128 : hd_mma)) ||
       (rc = make_vt_map(&tvlo, p.vt_lo, bh, p.seq, p.seq_pad, p.head_dim, hd_mma > 128 ? 128 : hd_mma)))
     return rc;
-  if (hd_mma == 16) return launch_hd<16>(p, thi, tlo, tvhi, tvlo, stream);
-  if (p.head_dim == 32) return launch_hd<32>(p, thi, tlo, tvhi, tvlo, stream);
-  if (p.head_dim == 64) return launch_hd<64>(p, thi, tlo, tvhi, tvlo, stream);
-  if (p.head_dim == 128) return launch_hd<128>(p, thi, tlo, tvhi, tvlo, stream);
-  return launch_hd<256>(p, thi, tlo, tvhi, tvlo, stream);
+  // Grid order. Each CTA streams its pair's K/V from key 0 to its diagonal;
+  // CTAs running at one time reuse each other's K/V through the L2 only if
+  // few pairs are in flight. When all pairs' K/V exceed 64 MB and sequences
+  // are long (32 query tiles or more), the grid runs groups of pairs whose
+  // K/V total at most 32 MB (at least one pair), one group after another.
+  AttentionTcParams q = p;
+  q.bh_group = (int)bh;
+  const int64_t kv_pair = (int64_t)p.seq * p.head_dim * 8;  // k, v x hi, lo x 2 B
+  const int ntq = (p.seq + BQ - 1) / BQ;
+  if (bh * kv_pair > (64LL << 20) && ntq >= 32) {
+    const int64_t gmax = std::max<int64_t>(1, (32LL << 20) / kv_pair);
+    for (int64_t g = std::min(gmax, bh); g >= 1; --g)
+      if (bh % g == 0) {
+        // the groups go on grid y (at most 65535)
+        if (bh / g <= 65535) q.bh_group = (int)g;
+        break;
+      }
+  }
+  if (hd_mma == 16) return launch_hd<16>(q, thi, tlo, tvhi, tvlo, stream);
+  if (p.head_dim == 32) return launch_hd<32>(q, thi, tlo, tvhi, tvlo, stream);
+  if (p.head_dim == 64) return launch_hd<64>(q, thi, tlo, tvhi, tvlo, stream);
+  if (p.head_dim == 128) return launch_hd<128>(q, thi, tlo, tvhi, tvlo, stream);
+  return launch_hd<256>(q, thi, tlo, tvhi, tvlo, stream);
 }
 
 }  // namespace tt

@@ -16,6 +16,9 @@ struct AttentionTcParams {
   int seq, seq_pad, d_model, num_heads, head_dim;
   int causal;
   float scale;
+  // set by launch_attention_tc: (sequence, head) pairs per group of the grid
+  // order (see the kernel); a divisor of batch * num_heads
+  int bh_group;
 };
 
 bool attention_tc_supported(int head_dim, int d_model);
