@@ -838,13 +838,13 @@ int launch_attention_tc(const AttentionTcParams &p, cudaStream_t stream) {
   // Grid order. Each CTA streams its pair's K/V from key 0 to its diagonal;
   // CTAs running at one time reuse each other's K/V through the L2 only if
   // few pairs are in flight. When all pairs' K/V exceed 64 MB and sequences
-  // are long (32 query tiles or more), the grid runs groups of pairs whose
-  // K/V total at most 32 MB (at least one pair), one group after another.
+  // have 8 query tiles or more, the grid runs groups of pairs whose K/V
+  // total at most 32 MB (at least one pair), one group after another.
   AttentionTcParams q = p;
   q.bh_group = (int)bh;
   const int64_t kv_pair = (int64_t)p.seq * p.head_dim * 8;  // k, v x hi, lo x 2 B
   const int ntq = (p.seq + BQ - 1) / BQ;
-  if (bh * kv_pair > (64LL << 20) && ntq >= 32) {
+  if (bh * kv_pair > (64LL << 20) && ntq >= 8) {
     const int64_t gmax = std::max<int64_t>(1, (32LL << 20) / kv_pair);
     for (int64_t g = std::min(gmax, bh); g >= 1; --g)
       if (bh % g == 0) {
