@@ -1,13 +1,16 @@
 #!/usr/bin/env python3
 """Benchmark of the pre-norm Transformer forward on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload B1]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload E]
     python bench.py --impl reference ...          # the reference forward on host CPU cores
 
 One step = one forward pass over one batch of the workload. The default
-workload is B1: d_model 128, 4 heads, ffn 128, 4 layers, causal, batch 4 x seq
-16, x ~ N(0,1) -- the launch-bound small shape. Other workloads (A, B2, C, D,
-E) are selectable for measurement; see ttjam_gottagofast_b200/config.py.
+workload is E, the largest configuration that fits one GPU: d_model 1024, 16
+heads, ffn 4096, 12 layers, causal + key padding (valid lengths uniform in
+[1024, 2048]), batch 64 x seq 2048, x ~ N(0,1). Its batch of 64 is split over
+the ranks at N > 1 (strong scaling) with the length-balanced assignment. Other
+workloads (A, B1, B2, C, D, the official cases 1-14) are selectable; see
+ttjam_gottagofast_b200/config.py.
 
 Our arm prints one JSON line with
   value      whole-job tokens/s (B*S tokens per rank per step, all ranks), timed
@@ -28,9 +31,10 @@ Our arm prints one JSON line with
              (algorithmic bytes floor); `kernels` lists every kind's share;
   cpu_baseline  the reference forward (oracle restatement, torch eager fp32)
              on this host's CPU cores, rank 0 at N=1 only.
-Multi-GPU runs use torchrun (one process per GPU, NCCL); every rank runs its
-own batch (weak scaling; workload E splits its batch of 64 across ranks, strong
-scaling). There is no collective inside a step.
+Multi-GPU runs use torchrun (one process per GPU, NCCL): workload E splits its
+batch of 64 across the ranks (strong scaling, equal sequence counts, attention
+work balanced by valid length); every other workload gives each rank a batch of
+its own (weak scaling). There is no collective inside a step.
 """
 from __future__ import annotations
 
@@ -60,9 +64,9 @@ L2_FLUSH_BYTES = 256 << 20
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--workload", default="B1", choices=sorted(BENCH_WORKLOADS))
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="E", choices=sorted(BENCH_WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=10.0)
@@ -106,6 +110,17 @@ def max_over_ranks(v, world):
     return float(t.item())
 
 
+def all_ranks(v, world, rank):
+    """[value of rank 0, ..., value of rank world-1] on every rank."""
+    if world == 1:
+        return [v]
+    import torch.distributed as dist
+    t = torch.zeros(world, dtype=torch.float64, device="cuda")
+    t[rank] = v
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return [float(a) for a in t.tolist()]
+
+
 def select_workload(args):
     """The named workload, with its batch replaced when --batch is given."""
     import dataclasses
@@ -117,16 +132,17 @@ def select_workload(args):
     return w
 
 
-def per_rank_batch(w, world, rank):
-    """Batch rows this rank owns: E splits its batch of 64 into contiguous
-    slices (strong scaling, shard_range); every other workload gives each rank
-    a full batch of its own (weak scaling)."""
-    from ttjam_gottagofast_b200.shard import shard_range
+def rank_sequences(w, mask, world, rank):
+    """Sequence indices of the workload's batch this rank runs: E splits its
+    batch of 64 over the ranks with the length-balanced assignment (strong
+    scaling, balanced_assignment); every other workload gives each rank the
+    full batch of its own (weak scaling)."""
+    from ttjam_gottagofast_b200.shard import balanced_assignment
     b = w.config.batch_size
-    if w.name == "E":
-        start, count = shard_range(b, world, rank)
-        return start, count, "strong"
-    return 0, b, "weak"
+    if w.name == "E" and world > 1:
+        ix = balanced_assignment(mask.sum(1).tolist(), world, w.config.seq_len)[rank]
+        return ix, "strong"
+    return list(range(b)), ("strong" if w.name == "E" else "weak")
 
 
 # ---------------------------------------------------------------------------
@@ -145,24 +161,26 @@ def load_peaks():
 
 
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) per
-# (workload, kernel kind), from ncu captures of the current kernels; the
-# profiles/ file named beside each entry gives the command and the capture.
-# E is captured at batch 4 and scaled to batch 64 (activation traffic x 16,
-# weight traffic once), as that file explains.
+# (workload, kernel kind), from one-pass ncu launch lists of the current
+# kernels (`ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum` over a
+# forward of the workload, averaged per kernel kind). B1: the single-launch
+# forward kernel. D: the graph-replayed per-op forward at batch 16. E: the
+# per-op forward captured at batch 4 and scaled to batch 64 (activation
+# traffic x 16, weight traffic once).
 NCU_TRAFFIC = {
-    ("B1", "whole_forward"): 1.690112e6,   # profiles/cluster_forward_B1.md
-    ("D", "layernorm"): 33.6e6,            # profiles/ops_tc_workload_D.md
-    ("D", "qkv"): 81.4e6,                  # profiles/ops_tc_workload_D.md
-    ("D", "attention"): 138.1e6,           # profiles/ops_tc_workload_D.md
-    ("D", "out_proj"): 68.4e6,             # profiles/ops_tc_workload_D.md
-    ("D", "ffn_in"): 115.9e6,              # profiles/ops_tc_workload_D.md
-    ("D", "ffn_out"): 181.1e6,             # profiles/ops_tc_workload_D.md
-    ("E", "layernorm"): 0.538e9,           # profiles/ops_tc_workload_E_batch4.md
-    ("E", "qkv"): 1.384e9,                 # profiles/ops_tc_workload_E_batch4.md
-    ("E", "attention"): 1.384e9,           # profiles/ops_tc_workload_E_batch4.md
-    ("E", "out_proj"): 1.084e9,            # profiles/ops_tc_workload_E_batch4.md
-    ("E", "ffn_in"): 1.951e9,              # profiles/ops_tc_workload_E_batch4.md
-    ("E", "ffn_out"): 3.318e9,             # profiles/ops_tc_workload_E_batch4.md
+    ("B1", "whole_forward"): 1.690112e6,
+    ("D", "layernorm"): 33.6e6,
+    ("D", "qkv"): 81.4e6,
+    ("D", "attention"): 138.1e6,
+    ("D", "out_proj"): 68.4e6,
+    ("D", "ffn_in"): 115.9e6,
+    ("D", "ffn_out"): 181.1e6,
+    ("E", "layernorm"): 0.538e9,
+    ("E", "qkv"): 1.384e9,
+    ("E", "attention"): 1.384e9,
+    ("E", "out_proj"): 1.084e9,
+    ("E", "ffn_in"): 1.951e9,
+    ("E", "ffn_out"): 3.318e9,
 }
 
 
@@ -292,13 +310,17 @@ def cpu_reference_run(w, steps, warmup, budget_s):
         samples.append((time.perf_counter_ns() - t0) / 1e6)
     med = statistics.median(samples)
     tokens = nb * cfg.seq_len
+    sample = (f"{nb} of {cfg.batch_size} sequences x seq {cfg.seq_len} per step, "
+              f"median of {steps} steps after {warmup} warm-up, torch eager fp32 "
+              f"restatement of BaselineTransformer.forward, {threads} threads"
+              + (f", attention in blocks of {qc} query rows" if qc else ""))
+    if nb < cfg.batch_size:
+        sample += (f"; extrapolated: the tokens/s of this {nb}-sequence slice stands for "
+                   f"the whole batch of {cfg.batch_size} (sequences are independent, so "
+                   "the work is linear in the batch)")
     return {
         "value": tokens * 1000.0 / med, "unit": "tokens/s", "cores": threads,
-        "kind": "port", "ms_per_step": med,
-        "sample": (f"{nb} of {cfg.batch_size} sequences x seq {cfg.seq_len} per step, "
-                   f"median of {steps} steps after {warmup} warm-up, torch eager fp32 "
-                   f"restatement of BaselineTransformer.forward, {threads} threads"
-                   + (f", attention in blocks of {qc} query rows" if qc else "")),
+        "kind": "port", "ms_per_step": med, "sample": sample,
     }
 
 
@@ -344,13 +366,18 @@ def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local if world > 1 else 0)
     w = select_workload(args)
     cfg = w.config
-    b0, nb, scaling = per_rank_batch(w, world, rank)
     x_all, m_all = generate_random_case(cfg, "cpu", torch.float32, TIMING_DATA_SEED,
                                         w.padding_ratio, w.input_scale)
+    seqs, scaling = rank_sequences(w, m_all, world, rank)
+    nb = len(seqs)
     # pinned once here and used as the e2e host buffers too (a large workload
     # holds no second host copy of its input)
-    x_host = x_all[b0:b0 + nb].pin_memory()
-    m_host = m_all[b0:b0 + nb].pin_memory()
+    if seqs == list(range(cfg.batch_size)):
+        x_host, m_host = x_all.pin_memory(), m_all.pin_memory()
+    else:
+        idx = torch.tensor(seqs)
+        x_host = x_all.index_select(0, idx).pin_memory()
+        m_host = m_all.index_select(0, idx).pin_memory()
     del x_all, m_all
     S = cfg.seq_len
 
@@ -433,6 +460,7 @@ def run_ours(args, world, rank, local):
     if n_probed < 0:
         _lib.check(n_probed, "tt_launch_probe_read", lib)
     lib.tt_launch_probe_start(0)
+    rank_total_ms = all_ranks(sum(step_ms), world, rank)
     total_ms = max_over_ranks(sum(step_ms), world)
     med_ms = max_over_ranks(statistics.median(step_ms), world)
     tokens_per_step_all = (cfg.batch_size if scaling == "strong" else nb * world) * S
@@ -549,6 +577,7 @@ def run_ours(args, world, rank, local):
         "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded generate_random_case, seeded random-init weights)",
         "config": workload_config(w, nb, world), "plan": plan,
+        "per_rank_ms_per_step": [round(t / args.steps, 4) for t in rank_total_ms],
         "gpu_launches": launches * args.steps * world,
         "gpu_launches_note": "our kernels in the timed device steps, summed over ranks",
         "roofline": roofline, "kernels": kernels,

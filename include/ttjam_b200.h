@@ -11,11 +11,17 @@
  * sizes, no torch types. Every pointer argument that names tensor data is a
  * device pointer unless stated otherwise; every entry point that launches work
  * takes a `cudaStream_t` passed as `void*` and never synchronises it (except
- * `tt_read_status`, which says so).
+ * `tt_read_status` and `tt_fp16_operand_bound`, which say so).
  *
- * Ownership: the library allocates nothing. The caller owns the packed model
- * image (`tt_image_bytes`), the per-call workspace (`tt_workspace_bytes`), the
- * input, the mask and the output.
+ * Ownership: the caller owns the packed model image (`tt_image_bytes`), the
+ * per-call workspace (`tt_workspace_bytes`), the input, the mask and the
+ * output; the library never allocates device memory for tensors. Two things
+ * it does create on its own: the 16 MiB static scratch array behind
+ * `tt_forward_noalloc` (reserved per device when the module loads), and, from
+ * the second `tt_forward` call with the same pointers and sizes on, one
+ * private capture stream per device and an instantiated CUDA graph per cached
+ * call (at most 16), which the driver backs with memory of its own. Setting
+ * TT_GRAPHS=0 in the environment turns the graphs off.
  *
  * Return codes: 0 on success, a negative `tt_status` value on failure; the last
  * failure's message is available from `tt_last_error` (per host thread).
@@ -30,7 +36,7 @@
 extern "C" {
 #endif
 
-#define TT_ABI_VERSION 1
+#define TT_ABI_VERSION 2
 
 typedef enum tt_status {
   TT_OK = 0,
@@ -55,8 +61,16 @@ typedef struct tt_config {
   int32_t plan;        /* 0 = pick automatically; else force one TT_PLAN_* schedule
                           (tests and benchmarks); an inapplicable plan is
                           TT_ERR_UNSUPPORTED */
-  int32_t reserved[2]; /* must be 0 */
+  int32_t flags;       /* TT_FLAG_* bits, 0 by default */
+  int32_t reserved;    /* must be 0 */
 } tt_config;
+
+/* tt_config.flags: TT_PLAN_AUTO never picks TT_PLAN_OPS_TC. Set it for a model
+ * whose tt_fp16_operand_bound is not below TT_FP16_MAX: the split-precision
+ * schedule stores activations as fp16 pieces, which cannot hold such values,
+ * while the FFMA and cluster schedules compute in fp32 throughout. */
+#define TT_FLAG_FP32_ONLY 1
+#define TT_FP16_MAX 65504.0f
 
 /* Kernel schedules of tt_forward. */
 #define TT_PLAN_AUTO 0
@@ -100,6 +114,22 @@ int tt_pack_image(const tt_config *cfg, const tt_layer_params *layers,
                   const float *final_norm_weight, const float *final_norm_bias,
                   void *image, size_t image_bytes, void *stream);
 
+/* An upper bound, valid for every input, on the magnitude of each activation
+ * that the split-precision schedule (TT_PLAN_OPS_TC) stores as fp16 pieces:
+ * the LayerNorm outputs (|gamma_i| * sqrt(D - 1) + |beta_i|, since a
+ * normalised row has at most sqrt(D - 1) in any element), the q|k|v
+ * projections and the attention contexts they average (row sums of
+ * |W_qkv| times the LayerNorm bound, plus |b|), and the GELU outputs of ffn_in
+ * (likewise). The residual stream, the scores and every accumulator stay fp32
+ * and need no bound. Reads the packed fp32 weights of `image` on `stream`,
+ * synchronises it and writes the bound to *bound (+inf when a weight is not
+ * finite). When the bound is not below TT_FP16_MAX, the caller sets
+ * TT_FLAG_FP32_ONLY (the Python module does so when it packs the weights); a
+ * forced TT_PLAN_OPS_TC then produces non-finite outputs and latches
+ * TT_ERR_DEVICE_RANGE. The reference computes every such model in fp32
+ * (torch_transformer_benchmark.py:93-95, :141); this keeps that true here. */
+int tt_fp16_operand_bound(const tt_config *cfg, const void *image, float *bound, void *stream);
+
 /* Bytes of scratch `tt_forward` needs for one [batch, seq] call. */
 size_t tt_workspace_bytes(const tt_config *cfg, int64_t batch, int64_t seq);
 
@@ -135,7 +165,18 @@ int tt_forward_launch_count(const tt_config *cfg, int64_t batch, int64_t seq);
  * or a process whose device memory already belongs to its own pool. It takes
  * no workspace: its per-call scratch is a TT_NOALLOC_SCRATCH_BYTES (16 MiB)
  * array of static device memory inside the library, which every GPU that
- * loads the library holds until the process exits. It calls no allocator.
+ * loads the library holds until the process exits. It launches its kernels
+ * directly on `stream` (never through the cached CUDA graphs of tt_forward)
+ * and calls no allocator.
+ *
+ * The array is committed on a device when the library's module is loaded
+ * there, which tt_pack_image forces: it looks up the array's device address
+ * with the image's device current and caches it. So a caller that packs its
+ * model before it hands its memory to a pool has the array in place, and the
+ * no-alloc calls themselves only read the cached address. Should a no-alloc
+ * call find no cached address for its device (no image was packed there), it
+ * looks the address up then, which may load the module and reserve the array
+ * at that moment; make such a first call before any stream capture.
  *
  * It runs the per-op schedule (TT_PLAN_OPS_*; TT_PLAN_AUTO picks the one
  * tt_forward uses when it does not take the single-launch path, and
@@ -143,12 +184,11 @@ int tt_forward_launch_count(const tt_config *cfg, int64_t batch, int64_t seq);
  * whose scratch (tt_workspace_bytes of that schedule) exceeds the array is
  * rejected with TT_ERR_WORKSPACE and a message giving both sizes.
  *
- * The first call on each device looks up the array's device address (with
- * that device current) and caches it; make that first call before any stream
- * capture. All calls share the one array: calls whose GPU work overlaps
- * (unordered streams, concurrent host threads) race on it. Nothing in it needs
- * to start at zero. Arguments as for tt_forward. This entry point has no
- * counterpart in the reference. */
+ * All calls share the one array and it keeps the previous call's contents:
+ * calls whose GPU work overlaps (unordered streams, concurrent host threads)
+ * race on it. Each call writes every scratch element before reading it, so
+ * nothing in it needs to start at zero. Arguments as for tt_forward. This
+ * entry point has no counterpart in the reference. */
 int tt_forward_noalloc(const tt_config *cfg, const void *image, const float *x,
                        const uint8_t *mask, int64_t batch, int64_t seq, float *y,
                        void *stream);

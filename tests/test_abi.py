@@ -56,8 +56,14 @@ def test_validate_config_codes(lib):
     bad.plan = 9
     assert lib.tt_validate_config(ctypes.byref(bad)) == _lib.TT_ERR_INVALID_CONFIG
     bad = _cfg()
-    bad.reserved[1] = 1
+    bad.reserved = 1
     assert lib.tt_validate_config(ctypes.byref(bad)) == _lib.TT_ERR_INVALID_CONFIG
+    bad = _cfg()
+    bad.flags = 2
+    assert lib.tt_validate_config(ctypes.byref(bad)) == _lib.TT_ERR_INVALID_CONFIG
+    ok = _cfg()
+    ok.flags = _lib.TT_FLAG_FP32_ONLY
+    assert lib.tt_validate_config(ctypes.byref(ok)) == 0
 
 
 def test_image_and_workspace_sizes(lib):
@@ -105,3 +111,27 @@ def test_forward_plan(lib):
     big = _cfg(d=512, h=8, f=2048, l=6)
     big.plan = _lib.PLAN_IDS["cluster"]
     assert lib.tt_forward_plan(ctypes.byref(big), 4, 16) == _lib.TT_ERR_UNSUPPORTED
+
+
+def test_fp32_only_flag_keeps_auto_plan_off_the_split_schedule(lib):
+    d_cfg = _cfg(d=512, h=8, f=2048, l=6)
+    assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(d_cfg), 16, 1024)] == "ops_tc"
+    d_cfg.flags = _lib.TT_FLAG_FP32_ONLY
+    assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(d_cfg), 16, 1024)] == "ops_ffma"
+    forced = _cfg(d=512, h=8, f=2048, l=6)
+    forced.plan = _lib.PLAN_IDS["ops_ffma"]
+    # the workspace is the FFMA schedule's
+    assert (lib.tt_workspace_bytes(ctypes.byref(d_cfg), 16, 1024) ==
+            lib.tt_workspace_bytes(ctypes.byref(forced), 16, 1024))
+    assert lib.tt_forward_launch_count(ctypes.byref(d_cfg), 16, 1024) == 5 * 6 + 1
+    # a forced split schedule stays forced
+    d_cfg.plan = _lib.PLAN_IDS["ops_tc"]
+    assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(d_cfg), 16, 1024)] == "ops_tc"
+
+
+def test_fp16_operand_bound_argument_errors_need_no_gpu(lib):
+    b = ctypes.c_float(0)
+    assert lib.tt_fp16_operand_bound(ctypes.byref(_cfg()), None, ctypes.byref(b),
+                                     None) == _lib.TT_ERR_INVALID_ARGUMENT
+    assert lib.tt_fp16_operand_bound(ctypes.byref(_cfg()), 256, None,
+                                     None) == _lib.TT_ERR_INVALID_ARGUMENT

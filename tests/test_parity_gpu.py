@@ -133,25 +133,106 @@ def test_workload_parity_full_size(name, variant):
         check(ref, out, f"{name}/{variant['name']}[{plan}]")
 
 
-@pytest.mark.parametrize("variant", [{"name": "own"}, HARNESS_VARIANTS[1], HARNESS_VARIANTS[4]],
-                         ids=["own", "large_scale", "padded_heavy"])
+D_E_VARIANTS = [{"name": "own"}] + HARNESS_VARIANTS
+
+
+@pytest.mark.parametrize("variant", D_E_VARIANTS, ids=[v["name"] for v in D_E_VARIANTS])
 def test_workload_D_parity_full_size(variant):
+    """D (d512 h8 ffn2048 L6, batch 16 x 1024) at full size, every sequence,
+    at its own x0.05 inputs and at each harness variant (x1, x8, x0.05,
+    padded, heavily padded)."""
     cfg, params, x, mask, y = _full_size_case("D", variant)
     ref = oracle.forward(params, cfg, x, mask, batch_chunk=2)
     check(ref, y, f"D/{variant['name']}")
+    assert (y[~mask] == 0).all()
+    model, _ = model_for(cfg)
+    assert model.forward_plan(cfg.batch_size, cfg.seq_len) == "ops_tc"
+    assert model.read_device_status() == (0, 0)
 
 
-def test_workload_E_parity_sequence_sample():
-    """Full-size E forward; the oracle checks the shortest, the longest and one
-    middle sequence (sequences are independent)."""
-    cfg, params, x, mask, y = _full_size_case("E", {"name": "own"})
+@pytest.mark.parametrize("variant", D_E_VARIANTS, ids=[v["name"] for v in D_E_VARIANTS])
+def test_workload_E_parity_sequence_sample(variant):
+    """Full-size E forward (d1024 h16 ffn4096 L12, batch 64 x 2048) at its own
+    inputs and at each harness variant; the oracle checks 8 sequences per
+    variant -- the shortest, the longest and six spread over the batch
+    (sequences are independent)."""
+    cfg, params, x, mask, y = _full_size_case("E", variant)
     lengths = mask.sum(1)
-    picks = sorted({int(lengths.argmin()), int(lengths.argmax()), cfg.batch_size // 2})
+    picks = {int(lengths.argmin()), int(lengths.argmax())}
+    for i in range(0, cfg.batch_size, cfg.batch_size // 8):
+        if len(picks) >= 8:
+            break
+        picks.add(i + 3)
+    picks = sorted(picks)
+    assert len(picks) == 8
     idx = torch.tensor(picks, device=DEV)
     ref = oracle.forward(params, cfg, x[idx], mask[idx], batch_chunk=1)
-    check(ref, y[idx], f"E/seqs{picks}")
+    check(ref, y[idx], f"E/{variant['name']}/seqs{picks}")
     assert torch.isfinite(y).all()
     assert (y[~mask] == 0).all()
+    model, _ = model_for(cfg)
+    assert model.forward_plan(cfg.batch_size, cfg.seq_len) == "ops_tc"
+    assert model.read_device_status() == (0, 0)
+
+
+def _inflated_v_model(plan="auto"):
+    """A d256 model (a tensor-core shape) whose v_proj weights are scaled by
+    1e5: its v values and attention contexts reach ~1e5-1e6, beyond the
+    largest fp16 value, while every fp32 intermediate stays finite."""
+    from ttjam_gottagofast_b200.config import TransformerConfig
+    cfg = TransformerConfig(batch_size=3, seq_len=96, d_model=256, num_heads=4, ffn_dim=256,
+                            num_layers=2, causal=True)
+    params = dict(oracle.init_params(cfg, seed=2024, device=DEV))
+    for l in range(cfg.num_layers):
+        key = f"layers.{l}.attention.v_proj.weight"
+        params[key] = params[key] * 1e5
+    model = UserOptimizedTransformer(cfg).to(DEV).eval()
+    model.load_state_dict(params, strict=True)
+    model.set_plan(plan)
+    x, mask = generate_random_case(cfg, "cpu", torch.float32, 8, 0.3, 1.0)
+    return cfg, params, model, x.to(DEV), mask.to(DEV)
+
+
+def test_fp16_range_bound_keeps_such_a_model_on_fp32_schedules():
+    """The packed weights bound every activation the split-precision schedule
+    holds as fp16 pieces; past 65504 the automatic plan runs the FFMA schedule
+    on the GPU (never the CPU) and matches the oracle."""
+    cfg, params, model, x, mask = _inflated_v_model()
+    with torch.inference_mode():
+        y = model(x, mask)
+    assert model.fp16_operand_bound > 65504.0
+    assert model.forward_plan(cfg.batch_size, cfg.seq_len) == "ops_ffma"
+    ref = oracle.forward(params, cfg, x, mask)
+    assert ref.abs().max() > 0
+    check(ref, y, "inflated v, automatic plan")
+    assert model.read_device_status() == (0, 0)
+
+
+def test_forced_split_schedule_latches_range_error():
+    """Forcing the split-precision schedule on that model fails loudly: the
+    q|k|v epilogue latches TT_ERR_DEVICE_RANGE in the status word and the
+    output is not finite; it never returns silently wrong numbers."""
+    from ttjam_gottagofast_b200 import _lib
+    cfg, params, model, x, mask = _inflated_v_model("ops_tc")
+    with torch.inference_mode():
+        y = model(x, mask)
+    code, detail = model.read_device_status()
+    assert code == _lib.TT_ERR_DEVICE_RANGE, (code, detail)
+    assert not torch.isfinite(y).all()
+    model.set_plan("auto")
+    with torch.inference_mode():
+        y2 = model(x, mask)
+    check(oracle.forward(params, cfg, x, mask), y2, "inflated v, back on the automatic plan")
+    assert model.read_device_status() == (0, 0)
+
+
+@pytest.mark.parametrize("name", ["A", "C", "D", "E"])
+def test_default_models_stay_on_split_precision(name):
+    cfg = WORKLOADS[name].config
+    model, _ = model_for(cfg)
+    model._ensure_image(torch.device(DEV))
+    assert 0 < model.fp16_operand_bound < 65504.0 / 8
+    assert model._cfg.flags == 0
 
 
 OFFICIAL_CASES = [f"case{c}" for c in range(1, 14)]

@@ -9,7 +9,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from ttjam_gottagofast_b200.shard import shard_range, sharded_forward
+from ttjam_gottagofast_b200.shard import balanced_assignment, shard_range, sharded_forward
 
 
 def test_shard_ranges_cover_batch_exactly():
@@ -24,6 +24,23 @@ def test_shard_ranges_cover_batch_exactly():
             assert max(sizes) - min(sizes) <= (1 if batch else 0)
     with pytest.raises(ValueError):
         shard_range(4, 2, 2)
+
+
+def test_balanced_assignment_partitions_and_evens_attention_work():
+    g = torch.Generator().manual_seed(3)
+    for n, world in ((64, 8), (64, 2), (7, 3), (3, 4), (0, 2)):
+        lengths = torch.randint(1024, 2049, (n,), generator=g).tolist()
+        a = balanced_assignment(lengths, world, 2048)
+        assert sorted(i for ix in a for i in ix) == list(range(n))
+        assert [len(ix) for ix in a] == [shard_range(n, world, r)[1] for r in range(world)]
+        assert all(ix == sorted(ix) for ix in a)
+        assert a == balanced_assignment(lengths, world, 2048)  # deterministic
+    lengths = torch.randint(1024, 2049, (64,), generator=g).tolist()
+    work = lambda ix: sum(lengths[i] ** 2 for i in ix)  # noqa: E731
+    bal = [work(ix) for ix in balanced_assignment(lengths, 8, 2048)]
+    cont = [work(range(r * 8, r * 8 + 8)) for r in range(8)]
+    assert max(bal) / min(bal) < 1.05
+    assert max(bal) <= max(cont)
 
 
 def _free_port():
@@ -42,7 +59,7 @@ def _stand_in_forward(x, mask):
     return out
 
 
-def _worker(rank, world, port, batch, result_q, fail_rank):
+def _worker(rank, world, port, batch, result_q, fail_rank, balanced=False):
     import datetime
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -54,7 +71,9 @@ def _worker(rank, world, port, batch, result_q, fail_rank):
         mask = torch.rand(batch, 5, generator=g) > 0.3
         if rank == fail_rank:
             raise RuntimeError("injected failure on the host before the gather")
-        y = sharded_forward(_stand_in_forward, x, mask)
+        assignment = (balanced_assignment(mask.sum(1).tolist(), world, x.shape[1])
+                      if balanced else None)
+        y = sharded_forward(_stand_in_forward, x, mask, assignment=assignment)
         ok = torch.equal(y, _stand_in_forward(x, mask))
         result_q.put((rank, "ok" if ok else "mismatch"))
     except Exception as e:  # noqa: BLE001 - report any failure to the parent
@@ -66,11 +85,11 @@ def _worker(rank, world, port, batch, result_q, fail_rank):
             pass
 
 
-def _run(world, batch, fail_rank=-1, timeout=60):
+def _run(world, batch, fail_rank=-1, timeout=60, balanced=False):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, batch, q, fail_rank))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, batch, q, fail_rank, balanced))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -90,6 +109,12 @@ def _run(world, batch, fail_rank=-1, timeout=60):
 @pytest.mark.parametrize("batch", [8, 7, 1])
 def test_gather_reassembles_batch_on_two_ranks(batch):
     out = _run(2, batch)
+    assert out == {0: "ok", 1: "ok"}, out
+
+
+@pytest.mark.parametrize("batch", [8, 5])
+def test_gather_undoes_balanced_assignment_on_two_ranks(batch):
+    out = _run(2, batch, balanced=True)
     assert out == {0: "ok", 1: "ok"}, out
 
 

@@ -83,6 +83,31 @@ def test_noalloc_matches_workspace_forward_twice(shape):
 
 
 @pytest.mark.gpu
+def test_noalloc_ragged_tensor_core_call_after_a_larger_call():
+    """A tensor-core call whose sequence length is not a multiple of 8 (its
+    transposed value copy has padding columns) right after a larger FFMA call
+    has filled the shared array with other data: the leftovers never reach the
+    output."""
+    big = TransformerConfig(8, 256, 128, 4, 128, 2, True)
+    model_big = _model(big, seed=5)
+    x, mask = generate_random_case(big, "cpu", torch.float32, 31, 0.0, 1.0)
+    _noalloc(model_big, _lib.make_config(big, "ops_ffma"), x.to(DEV), mask.to(DEV))
+    cfg = TransformerConfig(3, 61, 128, 4, 128, 2, True)
+    model = _model(cfg, seed=6)
+    cfg_c = _lib.make_config(cfg, "ops_tc")
+    for seed in (41, 42):
+        x, mask = generate_random_case(cfg, "cpu", torch.float32, seed, 0.4, 1.0)
+        x, mask = x.to(DEV), mask.to(DEV)
+        ref = _with_workspace(model, cfg_c, x, mask)
+        out = _noalloc(model, cfg_c, x, mask)
+        torch.cuda.synchronize()
+        res = compare_outputs(ref, out, rtol=RTOL, atol=ATOL)
+        assert res.passed, res
+        assert (out[~mask] == 0).all()
+    assert model.read_device_status() == (0, 0)
+
+
+@pytest.mark.gpu
 def test_noalloc_rejects_calls_beyond_its_scratch():
     cfg = TransformerConfig(64, 1024, 128, 4, 128, 1, True)  # ~168 MB of scratch
     lib = _lib.load()

@@ -11,7 +11,7 @@ import threading
 
 from . import build as _build
 
-TT_ABI_VERSION = 1
+TT_ABI_VERSION = 2
 
 TT_OK = 0
 TT_ERR_INVALID_CONFIG = -1
@@ -23,6 +23,12 @@ TT_ERR_DEVICE_TIMEOUT = -6
 TT_ERR_DEVICE_FAULT = -7
 TT_ERR_DEVICE_RANGE = -8
 
+# tt_config.flags: the automatic plan never picks the fp16-split schedule.
+TT_FLAG_FP32_ONLY = 1
+# Largest finite fp16 value; tt_fp16_operand_bound must stay below it for the
+# split-precision schedule.
+TT_FP16_MAX = 65504.0
+
 # Size of the library's fixed scratch array behind tt_forward_noalloc.
 TT_NOALLOC_SCRATCH_BYTES = 16 << 20
 
@@ -33,7 +39,7 @@ PLAN_IDS = {"auto": 0, **{v: k for k, v in PLAN_NAMES.items()}}
 EXPORTED = (
     "tt_abi_version", "tt_validate_config", "tt_image_bytes", "tt_pack_image",
     "tt_workspace_bytes", "tt_forward", "tt_forward_plan", "tt_forward_launch_count",
-    "tt_read_status", "tt_last_error", "tt_forward_noalloc",
+    "tt_read_status", "tt_last_error", "tt_forward_noalloc", "tt_fp16_operand_bound",
     "tt_launch_probe_start", "tt_launch_probe_read",
 )
 
@@ -46,7 +52,7 @@ class TTConfig(ctypes.Structure):
     _fields_ = [("d_model", ctypes.c_int32), ("num_heads", ctypes.c_int32),
                 ("ffn_dim", ctypes.c_int32), ("num_layers", ctypes.c_int32),
                 ("causal", ctypes.c_int32), ("plan", ctypes.c_int32),
-                ("reserved", ctypes.c_int32 * 2)]
+                ("flags", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 
 class TTLayerParams(ctypes.Structure):
@@ -97,6 +103,8 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         lib.tt_forward_launch_count.argtypes = [cfgp, i64, i64]
         lib.tt_forward_noalloc.restype = ctypes.c_int
         lib.tt_forward_noalloc.argtypes = [cfgp, vp, vp, vp, i64, i64, vp, vp]
+        lib.tt_fp16_operand_bound.restype = ctypes.c_int
+        lib.tt_fp16_operand_bound.argtypes = [cfgp, vp, ctypes.POINTER(ctypes.c_float), vp]
         lib.tt_read_status.restype = ctypes.c_int
         lib.tt_read_status.argtypes = [cfgp, vp, ctypes.POINTER(i32), ctypes.POINTER(i32), vp]
         lib.tt_last_error.restype = ctypes.c_int
@@ -132,10 +140,11 @@ def check(rc: int, what: str, lib=None) -> None:
     raise RuntimeError(msg)
 
 
-def make_config(cfg, plan: str = "auto") -> TTConfig:
+def make_config(cfg, plan: str = "auto", flags: int = 0) -> TTConfig:
     """A tt_config from any object with TransformerConfig's fields."""
     c = TTConfig()
     c.plan = PLAN_IDS[plan]
+    c.flags = flags
     c.d_model = int(cfg.d_model)
     c.num_heads = int(cfg.num_heads)
     c.ffn_dim = int(cfg.ffn_dim)

@@ -72,6 +72,48 @@ int split_weight(const float *src, uint16_t *hi, uint16_t *lo, int64_t n, unsign
   return TT_OK;
 }
 
+// Bound of one LayerNorm output element: a normalised row z of D elements has
+// sum z = 0 and sum z^2 <= D, so |z_i| <= sqrt(D - 1); the affine map adds
+// |gamma_i| * that + |beta_i|.
+__device__ __forceinline__ float ln_bound(const float *gamma, const float *beta, int i,
+                                          float zmax) {
+  return fabsf(gamma[i]) * zmax + fabsf(beta[i]);
+}
+
+// One warp per weight row j: out = max over rows of
+//   sum_i |W[j,i]| * ln_bound(i) + |b[j]|   (gelu: max with 0.17, the largest
+// |gelu| of a negative argument), and of every ln_bound(i) itself. Results
+// are non-negative floats combined with atomicMax on their bits (+inf and
+// NaN bit patterns order above every finite value).
+__global__ void operand_bound_kernel(const float *__restrict__ W, const float *__restrict__ b,
+                                     const float *__restrict__ gamma,
+                                     const float *__restrict__ beta, int rows, int D, int gelu,
+                                     unsigned *out) {
+  const float zmax = sqrtf((float)(D > 1 ? D - 1 : 0));
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  float m = 0.f;
+  for (int j = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; j < rows; j += warps) {
+    const float *w = W + (int64_t)j * D;
+    float acc = 0.f;
+    for (int i = lane; i < D; i += 32) acc = fmaf(fabsf(w[i]), ln_bound(gamma, beta, i, zmax), acc);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    acc += fabsf(b[j]);
+    if (!(acc == acc)) acc = __int_as_float(0x7f800000);  // NaN -> +inf
+    m = fmaxf(m, gelu ? fmaxf(acc, 0.17f) : acc);
+  }
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < D; i += blockDim.x) {
+      float v = ln_bound(gamma, beta, i, zmax);
+      if (!(v == v)) v = __int_as_float(0x7f800000);
+      m = fmaxf(m, v);
+    }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) atomicMax(out, __float_as_uint(m));
+}
+
 bool misaligned(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; }
 
 // Launch timing probe (tt_launch_probe_start / _read): per host thread, a
@@ -151,8 +193,9 @@ int validate_config(const tt_config *cfg) {
     return fail(TT_ERR_INVALID_CONFIG, "causal must be 0 or 1");
   if (cfg->plan < TT_PLAN_AUTO || cfg->plan > TT_PLAN_OPS_TC)
     return fail(TT_ERR_INVALID_CONFIG, "plan must be one of TT_PLAN_*");
-  for (int i = 0; i < 2; ++i)
-    if (cfg->reserved[i] != 0) return fail(TT_ERR_INVALID_CONFIG, "reserved fields must be 0");
+  if ((cfg->flags & ~TT_FLAG_FP32_ONLY) != 0)
+    return fail(TT_ERR_INVALID_CONFIG, "flags holds an unknown TT_FLAG_* bit");
+  if (cfg->reserved != 0) return fail(TT_ERR_INVALID_CONFIG, "reserved field must be 0");
   if (cfg->d_model / cfg->num_heads > 256)
     return fail(TT_ERR_UNSUPPORTED, "head_dim > 256 is not supported by this build");
   if (cfg->d_model > 65536 || cfg->ffn_dim > (1 << 20))
@@ -160,11 +203,16 @@ int validate_config(const tt_config *cfg) {
   return TT_OK;
 }
 
+int auto_ops_plan(const tt_config &cfg) {
+  return uses_tensor_cores(cfg) && (cfg.flags & TT_FLAG_FP32_ONLY) == 0 ? PLAN_OPS_TC
+                                                                        : PLAN_OPS_FFMA;
+}
+
 int forward_plan(const tt_config *cfg, int64_t batch, int64_t seq) {
   const int ops = uses_tensor_cores(*cfg) ? PLAN_OPS_TC : PLAN_OPS_FFMA;
   switch (cfg->plan) {
     case TT_PLAN_AUTO:
-      return choose_cluster(*cfg, batch, seq).cluster > 0 ? PLAN_CLUSTER : ops;
+      return choose_cluster(*cfg, batch, seq).cluster > 0 ? PLAN_CLUSTER : auto_ops_plan(*cfg);
     case TT_PLAN_CLUSTER:
       if (choose_cluster(*cfg, batch, seq).cluster > 0) return PLAN_CLUSTER;
       return fail(TT_ERR_UNSUPPORTED, "cluster schedule needs d_model = ffn_dim = 128, "
@@ -445,6 +493,45 @@ int tt_pack_image(const tt_config *cfg, const tt_layer_params *layers,
   }
   if ((rc = copy(L.final_w, final_norm_weight, D)) || (rc = copy(L.final_b, final_norm_bias, D)))
     return rc;
+  // set-up of tt_forward_noalloc on this device: looking up its scratch
+  // array's address loads the module that holds it, so the array is reserved
+  // now rather than inside a later no-alloc call
+  void *scratch = nullptr;
+  return noalloc_scratch_address(&scratch);
+}
+
+int tt_fp16_operand_bound(const tt_config *cfg, const void *image, float *bound, void *stream_) {
+  int rc = validate_config(cfg);
+  if (rc != TT_OK) return rc;
+  if (image == nullptr || bound == nullptr)
+    return fail(TT_ERR_INVALID_ARGUMENT, "tt_fp16_operand_bound: NULL argument");
+  if (misaligned(image)) return fail(TT_ERR_INVALID_ARGUMENT, "image must be 16-byte aligned");
+  const ImageLayout L(*cfg);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const char *img = static_cast<const char *>(image);
+  auto P = [&](size_t off) { return reinterpret_cast<const float *>(img + off); };
+  // the accumulator lives in the status block's spare words (pad[0])
+  DeviceStatus *st = reinterpret_cast<DeviceStatus *>(const_cast<char *>(img) + L.status);
+  unsigned *acc = reinterpret_cast<unsigned *>(&st->pad[0]);
+  TT_CUDA_TRY(cudaMemsetAsync(acc, 0, sizeof(unsigned), stream));
+  const int D = cfg->d_model, F = cfg->ffn_dim;
+  for (int l = 0; l < cfg->num_layers; ++l) {
+    const LayerOffsets &o = L.layer[l];
+    const int blocks_qkv = (int)std::min<int64_t>(ceil_div(3LL * D, 8), 148 * 4);
+    operand_bound_kernel<<<blocks_qkv, 256, 0, stream>>>(P(o.wqkv), P(o.bqkv), P(o.ln1_w),
+                                                           P(o.ln1_b), 3 * D, D, 0, acc);
+    TT_LAUNCH_CHECK("operand_bound (q|k|v)");
+    const int blocks_f = (int)std::min<int64_t>(ceil_div((int64_t)F, 8), 148 * 4);
+    operand_bound_kernel<<<blocks_f, 256, 0, stream>>>(P(o.w1), P(o.b1), P(o.ln2_w), P(o.ln2_b),
+                                                         F, D, 1, acc);
+    TT_LAUNCH_CHECK("operand_bound (ffn_in)");
+  }
+  unsigned bits = 0;
+  TT_CUDA_TRY(cudaMemcpyAsync(&bits, acc, sizeof(unsigned), cudaMemcpyDeviceToHost, stream));
+  TT_CUDA_TRY(cudaStreamSynchronize(stream));
+  float v;
+  std::memcpy(&v, &bits, sizeof v);
+  *bound = v;
   return TT_OK;
 }
 

@@ -97,7 +97,11 @@ struct WorkspaceLayout {
   WorkspaceLayout(const tt_config &cfg, int64_t batch, int64_t seq) {
     const size_t T = (size_t)batch * (size_t)seq, D = cfg.d_model, F = cfg.ffn_dim;
     const size_t f4 = sizeof(float);
-    tensor = uses_tensor_cores(cfg) && cfg.plan != TT_PLAN_OPS_FFMA;
+    // the buffers of the schedule the call runs: forced, or what TT_PLAN_AUTO
+    // picks when it does not take the single-launch one (which needs none)
+    tensor = uses_tensor_cores(cfg) &&
+             (cfg.plan == TT_PLAN_OPS_TC ||
+              (cfg.plan == TT_PLAN_AUTO && (cfg.flags & TT_FLAG_FP32_ONLY) == 0));
     size_t cur = 0;
     auto take = [&](size_t n_floats) {
       const size_t off = cur;
@@ -147,6 +151,12 @@ bool launch_probe_active();
 
 int validate_config(const tt_config *cfg);
 int forward_plan(const tt_config *cfg, int64_t batch, int64_t seq);
+// The per-op schedule TT_PLAN_AUTO uses (when the single-launch one does not
+// apply): the tensor-core one unless the shape or TT_FLAG_FP32_ONLY rules it out.
+int auto_ops_plan(const tt_config &cfg);
+// Device address of tt_forward_noalloc's scratch array on the current device,
+// looked up once per device and cached (noalloc.cu).
+int noalloc_scratch_address(void **out);
 int forward_ops(const tt_config &cfg, const ImageLayout &L, const char *image, const float *x,
                 const uint8_t *mask, int64_t batch, int64_t seq, float *y,
                 const WorkspaceLayout &W, char *ws, cudaStream_t stream);

@@ -12,11 +12,19 @@
 // tt_workspace_bytes) comes from here.
 //
 // The array is TT_NOALLOC_SCRATCH_BYTES (16 MiB) of static device memory, so
-// every GPU on which this library is loaded holds it until the process exits.
-// All calls share it: two calls whose work overlaps on the GPU (different
-// streams without ordering, or different host threads) race on it and
-// corrupt each other's results. Each call overwrites every scratch element it
-// reads before reading it, so nothing in the array has to start at zero and
+// every GPU on which this library's module is loaded holds it until the
+// process exits. The module is loaded on a device when the array's address is
+// first looked up there; tt_pack_image does that (set-up time, the image's
+// device current), so the no-alloc calls that follow find the address cached
+// and neither load anything nor reserve memory. The calls launch their kernels
+// directly on the caller's stream: they never go through the graph cache of
+// tt_forward, whose capture stream and instantiated graphs the driver backs
+// with memory of its own.
+//
+// All calls share the array: two calls whose work overlaps on the GPU
+// (different streams without ordering, or different host threads) race on it
+// and corrupt each other's results. Each call overwrites every scratch element
+// it reads before reading it, so nothing in the array has to start at zero and
 // the previous call's leftovers never reach an output.
 #include <mutex>
 
@@ -32,10 +40,12 @@ constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mutex;
 void *g_scratch_ptr[kMaxDevices] = {};
 
+}  // namespace
+
 // The device address of the scratch array on the current device. The array's
 // name in host code is only a host-side handle, never a device address; the
 // address is looked up once per device (with that device current) and cached.
-int scratch_address(void **out) {
+int noalloc_scratch_address(void **out) {
   int dev = 0;
   TT_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices)
@@ -51,7 +61,6 @@ int scratch_address(void **out) {
   return TT_OK;
 }
 
-}  // namespace
 }  // namespace tt
 
 using namespace tt;
@@ -78,7 +87,7 @@ extern "C" int tt_forward_noalloc(const tt_config *cfg, const void *image, const
   // the per-op schedule this call runs: forced by cfg->plan, else the one
   // tt_forward would use when it does not take the single-launch path
   tt_config ops = *cfg;
-  if (ops.plan == TT_PLAN_AUTO) ops.plan = uses_tensor_cores(*cfg) ? TT_PLAN_OPS_TC : TT_PLAN_OPS_FFMA;
+  if (ops.plan == TT_PLAN_AUTO) ops.plan = auto_ops_plan(*cfg);
   const int plan = forward_plan(&ops, batch, seq);
   if (plan < 0) return plan;
   const WorkspaceLayout W(ops, batch, seq);
@@ -89,14 +98,11 @@ extern "C" int tt_forward_noalloc(const tt_config *cfg, const void *image, const
                     std::to_string((size_t)TT_NOALLOC_SCRATCH_BYTES) +
                     "; use tt_forward with a caller workspace, or a smaller batch*seq");
   void *scratch = nullptr;
-  if ((rc = scratch_address(&scratch)) != TT_OK) return rc;
+  if ((rc = noalloc_scratch_address(&scratch)) != TT_OK) return rc;
   const ImageLayout L(ops);
   const char *img = static_cast<const char *>(image);
   char *ws = static_cast<char *>(scratch);
-  return run_forward_cached(
-      make_forward_key(ops, plan, image, x, mask, batch, seq, y, scratch),
-      static_cast<cudaStream_t>(stream_), [&](cudaStream_t s) {
-        return plan == PLAN_OPS_TC ? forward_ops_tc(ops, L, img, x, mask, batch, seq, y, W, ws, s)
-                                   : forward_ops(ops, L, img, x, mask, batch, seq, y, W, ws, s);
-      });
+  cudaStream_t s = static_cast<cudaStream_t>(stream_);
+  return plan == PLAN_OPS_TC ? forward_ops_tc(ops, L, img, x, mask, batch, seq, y, W, ws, s)
+                             : forward_ops(ops, L, img, x, mask, batch, seq, y, W, ws, s);
 }

@@ -11,12 +11,20 @@ The module mirrors the reference contract (torch_transformer_benchmark.py):
   (:203-213) work unchanged and `torch.manual_seed(s)` draws identical weights;
 * `forward(x, valid_token_mask=None)` -> [B, S, d_model] (:185-199).
 
+The contract declares `class UserOptimizedTransformer(BaselineTransformer)`
+(:175). `derive_user_optimized(BaselineTransformer)` builds exactly that class
+from the caller's own base; the stand-alone `UserOptimizedTransformer` here
+holds the same parameters in classes of its own, for callers without the
+reference module. Both run the forward below.
+
 The forward is CUDA only. It packs the parameters into a device image on first
-use (and again whenever a parameter changes: `load_state_dict`, `.to()`, or
-an in-place write seen through the tensor version counters), allocates its
-output and scratch from PyTorch's caching allocator, and enqueues the kernels
-on `torch.cuda.current_stream()` without a host sync. There is no CPU path:
-a CPU or non-fp32 input raises.
+use and again whenever they change: `load_state_dict`, `.to()`, or an
+in-place write through an autograd-visible op (tensor version counters). A
+write through `.data`, or replacing a Parameter object, is invisible to those
+counters: call `invalidate()` after one. The output and the scratch come from
+PyTorch's caching allocator, and the kernels run on
+`torch.cuda.current_stream()` without a host sync. There is no CPU path: a CPU
+or non-fp32 input raises.
 """
 from __future__ import annotations
 
@@ -58,23 +66,23 @@ class TransformerBlock(nn.Module):
         self.ffn_out = nn.Linear(ffn_dim, d_model)
 
 
-class UserOptimizedTransformer(nn.Module):
-    """The reference's drop-in hook (:175-200), backed by libttjam_b200.so."""
+class TTForward:
+    """The forward pass on libttjam_b200.so, for any nn.Module that holds the
+    reference's parameters under the reference's names (`layers.{i}...`,
+    `final_norm`) and its config as `self.config`."""
 
-    def __init__(self, config) -> None:
-        super().__init__()
+    def _tt_setup(self, config) -> None:
         config.validate()
-        self.config = config
-        self.layers = nn.ModuleList([
-            TransformerBlock(config.d_model, config.num_heads, config.ffn_dim)
-            for _ in range(config.num_layers)])
-        self.final_norm = nn.LayerNorm(config.d_model)
         self._lib = _lib.load()
+        self._plan = "auto"
+        self._flags = 0
         self._cfg = _lib.make_config(config)
         _lib.check(self._lib.tt_validate_config(ctypes.byref(self._cfg)), "config")
         self._image: Optional[torch.Tensor] = None
         self._image_key = None
         self._plist = None
+        self._ws_bytes = {}
+        self.fp16_operand_bound = None
         self.register_load_state_dict_post_hook(
             lambda module, incompatible: module.invalidate())
 
@@ -82,37 +90,51 @@ class UserOptimizedTransformer(nn.Module):
     def set_plan(self, plan: str = "auto") -> None:
         """Force a kernel schedule ("auto", "cluster", "ops_ffma", "ops_tc")
         for tests and measurements; "auto" picks the fastest applicable one."""
-        cfg = _lib.make_config(self.config, plan)
+        cfg = _lib.make_config(self.config, plan, self._flags)
         _lib.check(self._lib.tt_validate_config(ctypes.byref(cfg)), "plan")
+        self._plan = plan
         self._cfg = cfg
+        self._ws_bytes = {}
+
+    def _set_flags(self, flags: int) -> None:
+        if flags != self._flags:
+            self._flags = flags
+            self._cfg = _lib.make_config(self.config, self._plan, flags)
+            self._ws_bytes = {}
 
     def invalidate(self) -> None:
         """Drop the packed device image; the next forward repacks it."""
         self._image = None
         self._image_key = None
+        self._plist = None
 
     def _apply(self, fn, *args, **kwargs):
         self.invalidate()
         return super()._apply(fn, *args, **kwargs)
 
     def _param_key(self):
+        # Version counters only grow, so their sum changes with any in-place
+        # write to any parameter; the parameter objects are fixed between
+        # invalidations (load_state_dict and .to() invalidate).
         plist = self._plist
         if plist is None:
-            plist = self._plist = [p for p in self.parameters()]
-        return [(p.data_ptr(), p._version) for p in plist]
+            plist = self._plist = tuple(self.parameters())
+        return sum(p._version for p in plist)
 
     def _ensure_image(self, device: torch.device) -> torch.Tensor:
         key = self._param_key()
-        if self._image is not None and key == self._image_key:
-            return self._image
+        image = self._image
+        if image is not None and key == self._image_key and image.device == device:
+            return image
         self._plist = None
         key = self._param_key()
         for name, p in self.named_parameters():
             if p.device != device or p.dtype != torch.float32 or not p.is_contiguous():
                 raise ValueError(f"parameter {name} must be a contiguous float32 tensor "
                                  f"on {device} (got {p.dtype} on {p.device})")
-        lib, cfg = self._lib, self._cfg
-        nbytes = lib.tt_image_bytes(ctypes.byref(cfg))
+        lib = self._lib
+        pcfg = _lib.make_config(self.config)
+        nbytes = lib.tt_image_bytes(ctypes.byref(pcfg))
         image = torch.empty(nbytes, dtype=torch.uint8, device=device)
         arr = (_lib.TTLayerParams * len(self.layers))()
         for i, blk in enumerate(self.layers):
@@ -129,9 +151,19 @@ class UserOptimizedTransformer(nn.Module):
             for field, t in ptrs.items():
                 setattr(arr[i], field, t.data_ptr())
         stream = torch.cuda.current_stream(device).cuda_stream
-        _lib.check(lib.tt_pack_image(ctypes.byref(cfg), arr, self.final_norm.weight.data_ptr(),
+        _lib.check(lib.tt_pack_image(ctypes.byref(pcfg), arr, self.final_norm.weight.data_ptr(),
                                      self.final_norm.bias.data_ptr(), image.data_ptr(),
-                                     nbytes, stream), "tt_pack_image")
+                                     nbytes, stream), "tt_pack_image", lib)
+        # The split-precision schedule holds activations as fp16 pieces; when
+        # the weights allow one beyond the fp16 range for some input, the
+        # automatic plan keeps to the fp32 schedules (set-up time: this syncs).
+        bound = ctypes.c_float(0.0)
+        _lib.check(lib.tt_fp16_operand_bound(ctypes.byref(pcfg), image.data_ptr(),
+                                             ctypes.byref(bound), stream),
+                   "tt_fp16_operand_bound", lib)
+        self.fp16_operand_bound = bound.value
+        safe = bound.value < _lib.TT_FP16_MAX  # False for inf and NaN too
+        self._set_flags(0 if safe else _lib.TT_FLAG_FP32_ONLY)
         self._image = image
         self._image_key = key
         return image
@@ -163,14 +195,20 @@ class UserOptimizedTransformer(nn.Module):
                 m = m.contiguous()
             valid_token_mask = m
             mask_ptr = m.data_ptr()
-        image = self._ensure_image(x.device)
+        device = x.device
+        image = self._ensure_image(device)
         lib, cfg = self._lib, self._cfg
         y = torch.empty_like(x)
-        ws_bytes = lib.tt_workspace_bytes(ctypes.byref(cfg), b, s)
-        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
-        stream = torch.cuda.current_stream(x.device).cuda_stream
+        ws_bytes = self._ws_bytes.get((b, s))
+        if ws_bytes is None:
+            ws_bytes = self._ws_bytes[(b, s)] = lib.tt_workspace_bytes(ctypes.byref(cfg), b, s)
+        ws_ptr = None
+        if ws_bytes:
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+            ws_ptr = ws.data_ptr()
+        stream = torch.cuda.current_stream(device).cuda_stream
         rc = lib.tt_forward(ctypes.byref(cfg), image.data_ptr(), x.data_ptr(), mask_ptr, b, s,
-                            y.data_ptr(), ws.data_ptr(), ws_bytes, stream)
+                            y.data_ptr(), ws_ptr, ws_bytes, stream)
         if rc != 0:
             _lib.check(rc, "tt_forward", lib)
         return y
@@ -193,3 +231,39 @@ class UserOptimizedTransformer(nn.Module):
                                             ctypes.byref(code), ctypes.byref(detail), stream),
                    "tt_read_status", self._lib)
         return code.value, detail.value
+
+
+class UserOptimizedTransformer(TTForward, nn.Module):
+    """The reference's drop-in hook (:175-200), backed by libttjam_b200.so,
+    with parameter holders of its own (no reference import needed)."""
+
+    def __init__(self, config) -> None:
+        nn.Module.__init__(self)
+        config.validate()
+        self.config = config
+        self.layers = nn.ModuleList([
+            TransformerBlock(config.d_model, config.num_heads, config.ffn_dim)
+            for _ in range(config.num_layers)])
+        self.final_norm = nn.LayerNorm(config.d_model)
+        self._tt_setup(config)
+
+
+_DERIVED = {}
+
+
+def derive_user_optimized(baseline_cls):
+    """`class UserOptimizedTransformer(BaselineTransformer)` as the contract
+    declares it (torch_transformer_benchmark.py:175): the caller's own
+    `BaselineTransformer` builds the parameters (same modules, same seeded
+    init) and this module's forward replaces its forward. One class per base."""
+    cls = _DERIVED.get(baseline_cls)
+    if cls is None:
+        def __init__(self, config):
+            baseline_cls.__init__(self, config)
+            self._tt_setup(config)
+
+        cls = type("UserOptimizedTransformer", (TTForward, baseline_cls),
+                   {"__init__": __init__, "__doc__": UserOptimizedTransformer.__doc__,
+                    "__module__": __name__})
+        _DERIVED[baseline_cls] = cls
+    return cls
