@@ -230,6 +230,23 @@ int tt_launch_probe_start(int capacity);
  * negative status. */
 int tt_launch_probe_read(float *ms, int32_t *kinds, int capacity);
 
+/* Test support, with no counterpart in the reference: shows that a bounded
+ * device wait that runs out ends its kernel cleanly. Arms a one-shot switch:
+ * the next launch, in this process, of the single-CTA split-precision GEMM
+ * kernel (the tensor-core schedule's projections when the 256-row CTA-pair
+ * tiles would not fill the GPU) runs with CTA 0's TMA producer skipping the
+ * loads of its first k-block, so nothing ever completes that stage, and with
+ * bounded waits of 2^budget_log2 cycles (16..28; 2^28 is the normal budget).
+ * The waits held up by that stage then run out: the kernel latches
+ * TT_ERR_DEVICE_TIMEOUT in the image's status word (detail 0x1000, 0x2000 or
+ * 0x3000: the producer's, the MMA thread's or the epilogue's wait, whichever
+ * gives up first), stops issuing work, waits (bounded) for the copies and tensor-core operations it
+ * already started, frees its tensor memory and returns; that call's output is
+ * not meaningful, later calls are unaffected. While armed, tt_forward launches
+ * directly (no cached graph takes the switch). Returns TT_OK or
+ * TT_ERR_INVALID_ARGUMENT. */
+int tt_test_arm_wait_timeout(int budget_log2);
+
 #ifdef __cplusplus
 }
 #endif

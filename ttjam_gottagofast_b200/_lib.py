@@ -40,7 +40,7 @@ EXPORTED = (
     "tt_abi_version", "tt_validate_config", "tt_image_bytes", "tt_pack_image",
     "tt_workspace_bytes", "tt_forward", "tt_forward_plan", "tt_forward_launch_count",
     "tt_read_status", "tt_last_error", "tt_forward_noalloc", "tt_fp16_operand_bound",
-    "tt_launch_probe_start", "tt_launch_probe_read",
+    "tt_launch_probe_start", "tt_launch_probe_read", "tt_test_arm_wait_timeout",
 )
 
 # TT_KERNEL_* launch kinds reported by tt_launch_probe_read.
@@ -114,6 +114,8 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         lib.tt_launch_probe_read.restype = ctypes.c_int
         lib.tt_launch_probe_read.argtypes = [ctypes.POINTER(ctypes.c_float),
                                              ctypes.POINTER(i32), ctypes.c_int]
+        lib.tt_test_arm_wait_timeout.restype = ctypes.c_int
+        lib.tt_test_arm_wait_timeout.argtypes = [ctypes.c_int]
         if lib.tt_abi_version() != TT_ABI_VERSION:
             raise RuntimeError("libttjam_b200.so ABI version mismatch; rebuild it")
         _lib = lib

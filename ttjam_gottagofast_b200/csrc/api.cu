@@ -649,6 +649,8 @@ int tt_launch_probe_read(float *ms, int32_t *kinds, int capacity) {
   return n;
 }
 
+int tt_test_arm_wait_timeout(int budget_log2) { return arm_gemm_wait_timeout(budget_log2); }
+
 int tt_last_error(char *buf, size_t len) {
   const std::string &m = g_last_error;
   if (buf != nullptr && len > 0) {

@@ -40,8 +40,10 @@
 //             accumulate the context in tensor memory, rescaled only when the
 //             row max grows by more than 2^8.
 // Every mbarrier wait is bounded; a wait that gives up latches
-// TT_ERR_DEVICE_TIMEOUT and the kernel still frees tensor memory and returns.
-// Every TMA load here fills only the issuing CTA's own shared memory.
+// TT_ERR_DEVICE_TIMEOUT, the producer and MMA roles stop and wait (bounded)
+// for the loads and MMAs they started, and the kernel frees its tensor memory
+// and returns. Every TMA load here fills only the issuing CTA's own shared
+// memory.
 #include <cuda.h>
 #include <math_constants.h>
 
@@ -131,22 +133,38 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return done != 0;
 }
-// Bounded wait: gives up after ~2^28 cycles, or within 32 polls once a wait anywhere
-// in the launch already gave up.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, DeviceStatus *st,
-                                          int detail) {
+// Bounded wait: false after ~2^28 cycles (latching TT_ERR_DEVICE_TIMEOUT with
+// `detail` and setting this CTA's abort word), or within 32 polls once the
+// abort word is set (another thread of this CTA gave up first). Other CTAs and
+// launches do not look at the abort word. It is polled every 32nd poll only,
+// so that a completed phase is seen without a round trip in the way.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_w,
+                                          DeviceStatus *st, int detail) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  // the status word (a global load) is read every 32nd poll only, so that a
-  // completed phase is seen without a memory round trip in the way
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 31) == 0) {
-      if (st != nullptr && *reinterpret_cast<volatile int32_t *>(&st->code) != 0) return false;
+      if (*abort_w != 0) return false;
       if (clock64() - t0 > (1LL << 28)) {
+        *abort_w = 1;
         raise_status(st, TT_ERR_DEVICE_TIMEOUT, detail);
         return false;
       }
+    }
+  }
+}
+// Bounded wait for work this thread started itself (TMA loads, MMAs) before
+// the CTA frees its resources: ignores the abort word; latches the timeout and
+// returns when it runs out.
+__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity, DeviceStatus *st,
+                                           int detail) {
+  const long long t0 = clock64();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(bar, parity)) return;
+    if ((i & 31) == 31 && clock64() - t0 > (1LL << 28)) {
+      raise_status(st, TT_ERR_DEVICE_TIMEOUT, detail);
+      return;
     }
   }
 }
@@ -306,7 +324,9 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
   const uint32_t q_ready = bars + 8u * (2 * STAGES + 5);
   const uint32_t o_final = bars + 8u * (2 * STAGES + 6);  // every MMA finished
   const uint32_t tmem_slot = bars + 8u * (2 * STAGES + 7);
+  const uint32_t drain_bar = bars + 8u * (2 * STAGES + 8);  // the MMA thread's last commit
   uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
+  volatile int *abort_w = reinterpret_cast<volatile int *>(smem_raw + (tmem_slot + 4 - raw));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.seq, D = p.d_model, hd = p.head_dim;  // hd < HD only for head_dim 8 (HD 16)
@@ -386,6 +406,8 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
     mbar_init(o_done, 1);
     mbar_init(q_ready, 8);
     mbar_init(o_final, 1);
+    mbar_init(drain_bar, 1);
+    *abort_w = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -400,13 +422,21 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
   const uint32_t tm = *tmem_slot_ptr;
   pdl_wait();  // q|k and v^T come from the previous kernel (the mask is the caller's input)
 
+  // A wait that gives up in the producer or the MMA thread stops that role (no
+  // further loads, MMAs or commits, so no barrier phase is armed twice); the
+  // producer then waits for the loads it started and the MMA thread for its
+  // MMAs, bounded, before the CTA frees its tensor memory. The softmax threads
+  // run on through their (then failing) waits with unchanged control flow, so
+  // the pair barriers of their two warps always match.
   if (warp == 0 && lane == 0) {
     // ---- TMA producer: K/V tiles -------------------------------------------
     const int kcol = D + h * hd;  // first k column (fp16 elements) of this head
     const int bh = (int)b * p.num_heads + h;
-    for (int j = 0; j < nkv; ++j) {
+    int j = 0;
+    for (; j < nkv; ++j) {
       const int s = j % STAGES, n = j / STAGES;
-      if (j >= STAGES) mbar_wait(kv_empty(s), (n - 1) & 1, p.status, 0x4100 + j);
+      if (j >= STAGES && !mbar_wait(kv_empty(s), (n - 1) & 1, abort_w, p.status, 0x4100 + j))
+        break;
       const uint32_t st = base + s * STAGE;
       mbar_expect_tx(kv_full(s), STAGE);
 #pragma unroll
@@ -419,14 +449,17 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
       tma_load_3d(st + 2 * OPK, &tm_vhi, j * BKV, oh * HDO, bh, kv_full(s));
       tma_load_3d(st + 2 * OPK + OPV, &tm_vlo, j * BKV, oh * HDO, bh, kv_full(s));
     }
+    // the last phase armed on each stage has landed before the CTA retires
+    for (int k = j > STAGES ? j - STAGES : 0; k < j; ++k)
+      mbar_drain(kv_full(k % STAGES), (k / STAGES) & 1, p.status, 0x4F00);
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer --------------------------------------------------------
     // S_j goes to buffer j & 1. The tensor pipe runs one thread's MMAs in
     // issue order, so S_{j+2}, issued after P_j.V_j, overwrites P_j only after
     // that product has read it.
-    auto issue_s = [&](int j) {
+    auto issue_s = [&](int j) -> bool {
       const int s = j % STAGES;
-      mbar_wait(kv_full(s), (j / STAGES) & 1, p.status, 0x4200 + j);
+      if (!mbar_wait(kv_full(s), (j / STAGES) & 1, abort_w, p.status, 0x4200 + j)) return false;
       const uint32_t kst = base + s * STAGE;
       const uint32_t sd = tm + Sh::T_SP + 64u * (j & 1);
       // descriptors built once per box; a k-step of 16 dims advances the start
@@ -443,14 +476,18 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
         mma_ts(sd, tm + T_QLO + 8u * kk, khi0 + koff, Sh::IDESC_S, 1);
       }
       mma_commit(s_full(j & 1));
+      return true;
     };
-    mbar_wait(q_ready, 0, p.status, 0x4000);
+    bool ok = mbar_wait(q_ready, 0, abort_w, p.status, 0x4000);
     fence_after();
-    issue_s(0);
-    if (nkv > 1) issue_s(1);
-    for (int j = 0; j < nkv; ++j) {
+    ok = ok && issue_s(0);
+    if (nkv > 1) ok = ok && issue_s(1);
+    for (int j = 0; ok && j < nkv; ++j) {
       const int s = j % STAGES, b = j & 1;
-      mbar_wait(p_full(b), (j >> 1) & 1, p.status, 0x4400 + j);
+      if (!mbar_wait(p_full(b), (j >> 1) & 1, abort_w, p.status, 0x4400 + j)) {
+        ok = false;
+        break;
+      }
       fence_after();
       const uint32_t vst = base + s * STAGE + 2 * OPK;
       const uint64_t vhi0 = sdesc(vst, 1024, 2), vlo0 = sdesc(vst + OPV, 1024, 2);
@@ -466,9 +503,12 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
       }
       mma_commit(o_done);
       mma_commit(kv_empty(s));
-      if (j + 2 < nkv) issue_s(j + 2);  // into the buffer P_j.V_j has just read
+      if (j + 2 < nkv) ok = issue_s(j + 2);  // into the buffer P_j.V_j has just read
     }
-    mma_commit(o_final);
+    if (ok) mma_commit(o_final);
+    // every MMA issued above has completed before the tensor memory is freed
+    mma_commit(drain_bar);
+    mbar_drain(drain_bar, 0, p.status, 0x4F10);
   } else if (warp >= kSoftWarp0) {
     // ---- softmax: rows split over two warpgroups by key half ----------------
     const int t = (warp & 3) * 32 + lane;   // row within the tile = tensor-memory lane
@@ -536,7 +576,7 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
       // every key of this half allowed for every row of the warp (warp-uniform)
       const bool open = !diag && ok == 0xffffffffu;
       const uint32_t sp = lane_base + Sh::T_SP + 64u * sb + col_off;  // this thread's cells
-      mbar_wait(s_full(sb), (j >> 1) & 1, p.status, 0x4500 + j);
+      mbar_wait(s_full(sb), (j >> 1) & 1, abort_w, p.status, 0x4500 + j);
       fence_after();
       float sv[32];
       tmem_ld16(sp, sv);
@@ -580,7 +620,7 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
         // the context in tensor memory must hold P_{j-1}.V_{j-1} before it
         // is rescaled. S_j was committed after P_{j-2}.V_{j-2}, so o_done
         // has completed j - 1 or j phases here and the parity wait is exact.
-        mbar_wait(o_done, (j - 1) & 1, p.status, 0x4600 + j);
+        mbar_wait(o_done, (j - 1) & 1, abort_w, p.status, 0x4600 + j);
         fence_after();
         // this thread's HDO / 2 context columns (HDO = HD up to head_dim 128)
 #pragma unroll
@@ -632,7 +672,7 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
     // out_proj GEMM's A operand)
     // every P.V finished (o_done can be two phases behind here, so the
     // final commit has a barrier of its own)
-    mbar_wait(o_final, 0, p.status, 0x4700);
+    mbar_wait(o_final, 0, abort_w, p.status, 0x4700);
     fence_after();
     const float inv = l > 0.f ? 1.f / l : 0.f;
     const int64_t off = (b * S + (row_in ? row : 0)) * (int64_t)D + (int64_t)h * hd +

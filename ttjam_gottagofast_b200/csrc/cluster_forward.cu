@@ -81,7 +81,8 @@ struct CS {
   static constexpr int OFF_V = OFF_K + RMAX * HDP;
   static constexpr int OFF_VALID = OFF_V + RMAX * HDP;     // [RMAX]
   static constexpr int OFF_BAR = (OFF_VALID + RMAX + 3) / 4 * 4;  // 5 phase mbarriers
-  static constexpr int FLOATS = OFF_BAR + 10;
+  static constexpr int OFF_ABORT = OFF_BAR + 10;                   // the CTA's abort word
+  static constexpr int FLOATS = OFF_ABORT + 1;
   static_assert(FLOATS <= cluster_smem_floats(CL, H, RMAX), "layout");
   static_assert(WB % 4 == 0 && AUX % 4 == 0 && OFF_K % 4 == 0, "16-byte buffers");
   static constexpr size_t BYTES = (size_t)FLOATS * sizeof(float);
@@ -153,16 +154,18 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 // Bounded wait for one exchange phase. Gives up after ~2^28 cycles (~0.14 s),
-// or at once when a wait anywhere in the launch already gave up, and latches a
-// timeout; the caller carries on so that every CTA still reaches the closing
-// cluster barrier.
-__device__ __forceinline__ void wait_phase(uint32_t bar, uint32_t parity, DeviceStatus *st,
-                                           int code) {
+// latching a timeout and setting this CTA's abort word, or at once when the
+// abort word is already set (a wait of this CTA gave up before); the caller
+// carries on so that every CTA still reaches the closing cluster barrier.
+// Other CTAs and other launches do not look at the abort word.
+__device__ __forceinline__ void wait_phase(uint32_t bar, uint32_t parity, volatile int *abort_w,
+                                           DeviceStatus *st, int code) {
   if (mbar_try_wait(bar, parity)) return;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (st != nullptr && *reinterpret_cast<volatile int32_t *>(&st->code) != 0) return;
+    if (*abort_w != 0) return;
     if (clock64() - t0 > (1LL << 28)) {
+      *abort_w = 1;
       raise_status(st, TT_ERR_DEVICE_TIMEOUT, code);
       return;
     }
@@ -344,8 +347,10 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
   const int64_t row0 = (int64_t)seq0 * S;
   const int h = rank / G, sub = rank % G;
 
+  volatile int *abort_w = reinterpret_cast<volatile int *>(sm + C::OFF_ABORT);
   if (tid == 0) {
     for (int p = 0; p < NPH; ++p) mbar_init(bar0 + 8 * p, 1);
+    *abort_w = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   load_layer_part<CL, H>(a, 0, 0, sW, rank);  // async group: layer 0, q/k/v part
@@ -405,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
           st_async4(cluster_map(base, h * G + g) + off, v, cluster_map(bar0 + 8 * PH_QKV, h * G + g));
       }
     });
-    wait_phase(bar0 + 8 * PH_QKV, par, a.status, 0x100 + l);
+    wait_phase(bar0 + 8 * PH_QKV, par, abort_w, a.status, 0x100 + l);
     // every thread of this CTA is past its q/k/v GEMM (the exchange that just
     // completed includes its own rows), so the q/k/v part of the buffer is
     // free: stream in layer l+1's while the later phases compute
@@ -477,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
           st_async4(cluster_map(cb_l, g) + off, v4, cluster_map(bar0 + 8 * PH_CTX, g));
       }
     }
-    wait_phase(bar0 + 8 * PH_CTX, par, a.status, 0x200 + l);
+    wait_phase(bar0 + 8 * PH_CTX, par, abort_w, a.status, 0x200 + l);
 
     // layer l's out_proj / ffn part: older than layer l+1's q/k/v part when
     // that one was issued
@@ -498,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
       for (int g = ls; ok && g < CL; g += 8)
         st_async4(cluster_map(xs_l, g) + off, o, cluster_map(bar0 + 8 * PH_X1, g));
     });
-    wait_phase(bar0 + 8 * PH_X1, par, a.status, 0x300 + l);
+    wait_phase(bar0 + 8 * PH_X1, par, abort_w, a.status, 0x300 + l);
 
     // ---- ffn_in + exact GELU on LayerNorm2(X): CB[:, own cols] -------------
     warp_gemm<NC / 8, true>(sX, wb + 4 * NC * kST, R, aux + 2 * kD, aux + 3 * kD, a.eps,
@@ -511,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
       for (int g = ls; ok && g < CL; g += 8)
         st_async4(cluster_map(cb_l, g) + off, o, cluster_map(bar0 + 8 * PH_H, g));
     });
-    wait_phase(bar0 + 8 * PH_H, par, a.status, 0x400 + l);
+    wait_phase(bar0 + 8 * PH_H, par, abort_w, a.status, 0x400 + l);
 
     // ---- ffn_out + residual + block-end padded-row zeroing -----------------
     warp_gemm<NC / 8, false>(sCB, wb + 5 * NC * kST, R, nullptr, nullptr, 0.f,
@@ -528,7 +533,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
       for (int g = ls; ok && g < CL; g += 8)
         st_async4(cluster_map(xs_l, g) + off, o, cluster_map(bar0 + 8 * PH_X2, g));
     });
-    wait_phase(bar0 + 8 * PH_X2, par, a.status, 0x500 + l);
+    wait_phase(bar0 + 8 * PH_X2, par, abort_w, a.status, 0x500 + l);
     // every thread of this CTA is past its out_proj / ffn GEMMs: stream in
     // layer l+1's part while its q/k/v phase and attention run
     if (l + 1 < L) load_layer_part<CL, H>(a, l + 1, 1, sW, rank);

@@ -52,10 +52,16 @@
 // returns. Every TMA load here fills only the issuing CTA's own shared memory.
 #include <cuda.h>
 
+#include <atomic>
+
 #include "gemm_tc.cuh"
 
 namespace tt {
 namespace {
+
+// tt_test_arm_wait_timeout: the budget (log2 cycles) of the next single-CTA
+// launch that takes the test switch, or 0 when none is armed.
+std::atomic<int> g_armed_timeout{0};
 
 constexpr int BM = 128, BK = 32;  // BK in fp16 elements (64-byte rows)
 constexpr int kThreads = 512;   // warps 0-3: TMA, MMA, TMEM; warps 4-15: epilogue
@@ -102,23 +108,41 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return done != 0;
 }
-// Bounded wait: false (and a latched timeout) after ~2^28 cycles (~0.14 s),
-// or within 32 polls once an earlier wait anywhere in the launch gave up, so
-// a broken pipeline costs one timeout, not one per CTA and k-block.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, DeviceStatus *st,
-                                          int detail) {
+// Bounded wait on an mbarrier phase. Returns false after 2^budget_log2
+// cycles (2^28 by default, ~0.14 s), latching TT_ERR_DEVICE_TIMEOUT with
+// `detail` in the image's status word and setting this CTA's abort word; or,
+// within 32 polls, once the abort word is set (another thread of this CTA gave
+// up first), so a broken pipeline costs one timeout per CTA, not one per wait.
+// Other CTAs and other launches do not look at the abort word. The abort word
+// (shared memory) is polled every 32nd poll only, so that a completed phase is
+// seen without a memory round trip in the way.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_w,
+                                          DeviceStatus *st, int detail, int budget_log2 = 28) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  // the status word (a global load) is read every 32nd poll only, so that a
-  // completed phase is seen without a memory round trip in the way
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 31) == 0) {
-      if (st != nullptr && *reinterpret_cast<volatile int32_t *>(&st->code) != 0) return false;
-      if (clock64() - t0 > (1LL << 28)) {
+      if (*abort_w != 0) return false;
+      if (clock64() - t0 > (1LL << budget_log2)) {
+        *abort_w = 1;
         raise_status(st, TT_ERR_DEVICE_TIMEOUT, detail);
         return false;
       }
+    }
+  }
+}
+// Bounded wait for work this thread started itself (its TMA loads, its MMAs)
+// before the CTA frees its resources: it ignores the abort word, and on
+// running out latches the timeout and returns (it never waits unbounded).
+__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity, DeviceStatus *st,
+                                           int detail, int budget_log2 = 28) {
+  const long long t0 = clock64();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(bar, parity)) return;
+    if ((i & 31) == 31 && clock64() - t0 > (1LL << budget_log2)) {
+      raise_status(st, TT_ERR_DEVICE_TIMEOUT, detail);
+      return;
     }
   }
 }
@@ -400,18 +424,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   const uint32_t bars = base + Sh::BAR_OFF;
-  // full[S] | empty[S] | acc_full[2] | acc_empty[2] | tmem address
+  // full[S] | empty[S] | acc_full[2] | acc_empty[2] | tmem address, abort word |
+  // drain barrier
   auto full_bar = [&](int s) { return bars + 8u * s; };
   auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
   auto acc_full = [&](int b) { return bars + 8u * (2 * STAGES + b); };
   auto acc_empty = [&](int b) { return bars + 8u * (2 * STAGES + 2 + b); };
   const uint32_t tmem_slot = bars + 8u * (2 * STAGES + 4);
+  const uint32_t drain_bar = bars + 8u * (2 * STAGES + 5);
   uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
+  volatile int *abort_w = reinterpret_cast<volatile int *>(smem_raw + (tmem_slot + 4 - raw));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KB = (p.K + BK - 1) / BK;
   const int MT = (p.M + BM - 1) / BM, NT = (p.N + BN - 1) / BN;
   const int ntiles = MT * NT;
+  const int budget = p.wait_budget_log2 > 0 ? p.wait_budget_log2 : 28;
+  // test switch (tt_test_arm_wait_timeout): CTA 0's producer never starts the
+  // loads of its first k-block, so nothing ever completes that stage
+  const bool skip_first = p.test_skip_first_load != 0 && blockIdx.x == 0;
   pdl_trigger();
   if (threadIdx.x == 32) {
     prefetch_tmap(&tm_a_hi); prefetch_tmap(&tm_a_lo); prefetch_tmap(&tm_w_hi);
@@ -428,6 +459,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(acc_full(b), 1);
       mbar_init(acc_empty(b), kEpiWarps);  // one elected arrive per epilogue warp
     }
+    mbar_init(drain_bar, 1);
+    *abort_w = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 2) {
@@ -442,14 +475,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot_ptr;
   pdl_wait();  // A (and R) come from the previous kernel
 
+  // A wait that gives up stops its role: no further loads, MMAs, commits or
+  // arrivals (each stage is armed only after its previous phase was consumed,
+  // and consumed only after its loads completed, so no barrier phase is ever
+  // armed twice). Before the CTA frees its tensor memory and returns, the
+  // producer waits for the loads it started and the MMA thread for the MMAs it
+  // issued, each with a bounded wait of its own.
   if (warp == 0 && lane == 0) {
     // ---- TMA producer: one k-block sequence running across all tiles --------
     int it = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
       const int m0 = (tile / NT) * BM, n0 = (tile % NT) * BN;
       for (int kb = 0; kb < KB; ++kb, ++it) {
         const int s = it % STAGES, n = it / STAGES;
-        if (it >= STAGES) mbar_wait(empty_bar(s), (n - 1) & 1, p.status, 0x1000);
+        if (it >= STAGES && !mbar_wait(empty_bar(s), (n - 1) & 1, abort_w, p.status, 0x1000,
+                                       budget)) {
+          ok = false;
+          break;
+        }
+        if (skip_first && it == 0) continue;
         const uint32_t st = base + s * STAGE_BYTES;
         mbar_expect_tx(full_bar(s), STAGE_BYTES);
         tma_load_2d(st, &tm_a_hi, kb * BK, m0, full_bar(s));
@@ -458,17 +503,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d(st + 2 * TILE_A + TILE_W, &tm_w_lo, kb * BK, n0, full_bar(s));
       }
     }
+    // the last phase armed on each stage (iterations [it - STAGES, it)) has
+    // landed before this CTA may retire; earlier phases completed before
+    // their stage was re-armed
+    for (int k = it > STAGES ? it - STAGES : 0; k < it; ++k)
+      if (!(skip_first && k == 0)) mbar_drain(full_bar(k % STAGES), (k / STAGES) & 1, p.status,
+                                              0x1F00, budget);
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer -------------------------------------------------------
     int it = 0, local = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++local) {
       const int ab = local & 1;
-      if (local >= 2) mbar_wait(acc_empty(ab), ((local >> 1) - 1) & 1, p.status, 0x2100);
+      if (local >= 2 && !mbar_wait(acc_empty(ab), ((local >> 1) - 1) & 1, abort_w, p.status,
+                                   0x2100, budget)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       const uint32_t acc = tmem_base + (uint32_t)(ab * BN);
       for (int kb = 0; kb < KB; ++kb, ++it) {
         const int s = it % STAGES, n = it / STAGES;
-        mbar_wait(full_bar(s), n & 1, p.status, 0x2000);
+        if (!mbar_wait(full_bar(s), n & 1, abort_w, p.status, 0x2000, budget)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint32_t st = base + s * STAGE_BYTES;
         // descriptors built once per stage; a k-step only advances the
@@ -485,8 +544,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         umma_commit(empty_bar(s));  // stage s is free once these MMAs have read it
       }
-      umma_commit(acc_full(ab));    // accumulator ab complete
+      if (ok) umma_commit(acc_full(ab));  // accumulator ab complete
     }
+    // every MMA issued above has completed before the tensor memory is freed
+    umma_commit(drain_bar);
+    mbar_drain(drain_bar, 0, p.status, 0x2F00, budget);
   } else if (warp >= 4) {
     // ---- epilogue: tensor memory -> registers -> shared -> TMA store -------
     const int q = warp & 3;                 // tensor-memory lane quarter
@@ -503,7 +565,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m0 = (tile / NT) * BM, n0 = (tile % NT) * BN;
       BiasRegs bias;
       load_bias_regs(p, n0 + c_lo, c_hi - c_lo, lane, bias);
-      mbar_wait(acc_full(ab), (local >> 1) & 1, p.status, 0x3000);
+      // warp-uniform outcome (the tensor-memory loads below are warp-collective)
+      if (!__all_sync(0xffffffffu, mbar_wait(acc_full(ab), (local >> 1) & 1, abort_w, p.status,
+                                             0x3000, budget)))
+        break;
       tc_fence_after();
       const int row0 = m0 + q * 32;
       const int row = row0 + lane;
@@ -648,6 +713,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto acc_empty = [&](int b) { return bars + 8u * (2 * PSTAGES + 2 + b); };
   const uint32_t tmem_slot = bars + 8u * (2 * PSTAGES + 4);
   uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
+  volatile int *abort_w = reinterpret_cast<volatile int *>(smem_raw + (tmem_slot + 4 - raw));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cta_rank_in_cluster();
@@ -672,6 +738,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(acc_full(b), 1);
       mbar_init(acc_empty(b), 2 * kEpiWarps);  // CTA 0's: every epilogue warp of the pair
     }
+    *abort_w = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 2) {
@@ -696,7 +763,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n0 = (tile % NT) * PBN + (PBN / 2) * (int)rank;
       for (int kb = 0; kb < KB; ++kb, ++it) {
         const int s = it % PSTAGES, n = it / PSTAGES;
-        if (it >= PSTAGES) mbar_wait(empty_bar(s), (n - 1) & 1, p.status, 0x1100);
+        if (it >= PSTAGES) mbar_wait(empty_bar(s), (n - 1) & 1, abort_w, p.status, 0x1100);
         const uint32_t st = base + s * P_STAGE;
         if (rank == 0) mbar_expect_tx(full_bar(s), 2 * P_STAGE);
         const uint32_t fb = full0 + 8u * s;
@@ -709,7 +776,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // every stage's last release (a commit from CTA 0) has arrived before this
     // CTA may retire
     for (int k = it > PSTAGES ? it - PSTAGES : 0; k < it; ++k)
-      mbar_wait(empty_bar(k % PSTAGES), (k / PSTAGES) & 1, p.status, 0x1200);
+      mbar_wait(empty_bar(k % PSTAGES), (k / PSTAGES) & 1, abort_w, p.status, 0x1200);
   } else if (warp == 1 && lane == 0 && rank == 0) {
     // ---- MMA issuer (CTA 0 only) -------------------------------------------
     const uint32_t peer_empty0 = map_to_cta(empty_bar(0), peer);
@@ -717,12 +784,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     int it = 0, local = 0;
     for (int tile = pair; tile < ntiles; tile += npairs, ++local) {
       const int ab = local & 1;
-      if (local >= 2) mbar_wait(acc_empty(ab), ((local >> 1) - 1) & 1, p.status, 0x2100);
+      if (local >= 2) mbar_wait(acc_empty(ab), ((local >> 1) - 1) & 1, abort_w, p.status, 0x2100);
       tc_fence_after();
       const uint32_t acc = tmem_base + (uint32_t)(ab * PBN);
       for (int kb = 0; kb < KB; ++kb, ++it) {
         const int s = it % PSTAGES, n = it / PSTAGES;
-        mbar_wait(full_bar(s), n & 1, p.status, 0x2000);
+        mbar_wait(full_bar(s), n & 1, abort_w, p.status, 0x2000);
         tc_fence_after();
         const uint32_t st = base + s * P_STAGE;
         const uint64_t a_hi = umma_desc_sw64(st), a_lo = umma_desc_sw64(st + P_TILE);
@@ -758,7 +825,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m0 = (tile / NT) * 256 + 128 * (int)rank, n0 = (tile % NT) * PBN;
       BiasRegs bias;
       load_bias_regs(p, n0 + c_lo, c_hi - c_lo, lane, bias);
-      mbar_wait(acc_full(ab), (local >> 1) & 1, p.status, 0x3000);
+      mbar_wait(acc_full(ab), (local >> 1) & 1, abort_w, p.status, 0x3000);
       tc_fence_after();
       const int row0 = m0 + q * 32;
       const int row = row0 + lane;
@@ -846,8 +913,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t *base_ptr = smem_raw + (base - raw);
   const uint32_t bars = base + Sh::BAR_OFF;
   const uint32_t w_full = bars, acc_full = bars + 8u;
-  const uint32_t tmem_slot = bars + 16u;
+  const uint32_t tmem_slot = bars + 16u, drain_bar = bars + 24u;
   uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
+  volatile int *abort_w = reinterpret_cast<volatile int *>(smem_raw + (tmem_slot + 4 - raw));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K = p.K, KB = (K + BK - 1) / BK;
@@ -861,6 +929,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(w_full, 1);
     mbar_init(acc_full, 1);
+    mbar_init(drain_bar, 1);
+    *abort_w = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 2) {
@@ -955,9 +1025,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 1 && lane == 0) {
     // ---- MMA issuer ---------------------------------------------------------
-    mbar_wait(w_full, 0, p.status, 0x5100);
+    // a wait that gives up issues nothing; either way the weight loads this
+    // thread's CTA started and the MMAs it issued complete before the tensor
+    // memory is freed
+    const bool ok = mbar_wait(w_full, 0, abort_w, p.status, 0x5100);
     tc_fence_after();
-    for (int kb = 0; kb < KB; ++kb) {
+    for (int kb = 0; ok && kb < KB; ++kb) {
       const uint32_t a = base + (uint32_t)kb * Sh::A_KB;
       const uint32_t w = base + Sh::W_OFF + (uint32_t)kb * Sh::W_KB;
       const uint64_t a_hi = umma_desc_sw64(a), a_lo = umma_desc_sw64(a + TILE_A);
@@ -970,7 +1043,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_f16(tmem_base, a_lo + ko, w_hi + ko, IDESC, 1);
       }
     }
-    umma_commit(acc_full);
+    if (ok) umma_commit(acc_full);
+    mbar_drain(w_full, 0, p.status, 0x5F00);
+    umma_commit(drain_bar);
+    mbar_drain(drain_bar, 0, p.status, 0x5F10);
   } else if (warp >= 4) {
     // ---- epilogue: as in gemm_tc3_kernel, one tile ------------------------------
     const int q = warp & 3;
@@ -982,14 +1058,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     int nstores = 0;
     BiasRegs bias;
     load_bias_regs(p, n0 + c_lo, c_hi - c_lo, lane, bias);
-    mbar_wait(acc_full, 0, p.status, 0x5200);
+    // warp-uniform outcome (the tensor-memory loads below are warp-collective)
+    const bool got = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, abort_w, p.status, 0x5200));
     tc_fence_after();
     const int row0 = m0 + q * 32;
     const int row = row0 + lane;
     const bool row_in = row < p.M;
     const bool valid = row_in && (p.row_mask == nullptr || p.row_mask[row] != 0);
 #pragma unroll 1
-    for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
+    for (int c0 = c_lo; got && c0 < c_hi; c0 += 32) {
       uint32_t ra[16], rb[16];
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
       tmem_ld16_async(taddr, ra);
@@ -1119,8 +1196,14 @@ int launch_bn(const TcGemmParams &p, cudaStream_t stream) {
   }
   const int64_t tiles = (int64_t)((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = (int)std::min<int64_t>(tiles, sms > 0 ? sms : 148);
+  TcGemmParams q = p;
+  const int armed = g_armed_timeout.exchange(0);  // test switch: this launch takes it
+  if (armed > 0) {
+    q.test_skip_first_load = 1;
+    q.wait_budget_log2 = armed;
+  }
   TT_CUDA_TRY(launch_kernel(gemm_tc3_kernel<BN>, dim3(grid), dim3(kThreads), Sh::SMEM_BYTES,
-                            stream, 1, ta_hi, ta_lo, tw_hi, tw_lo, tc, tc_hi, tc_lo, p));
+                            stream, 1, ta_hi, ta_lo, tw_hi, tw_lo, tc, tc_hi, tc_lo, q));
   TT_LAUNCH_CHECK("gemm_tc3");
   return TT_OK;
 }
@@ -1223,6 +1306,15 @@ int launch_gemm_tc3(const TcGemmParams &p, cudaStream_t stream) {
   if (2 * tiles128 <= sms) return launch_bn<64>(p, stream);
   return launch_bn<128>(p, stream);
 }
+
+int arm_gemm_wait_timeout(int budget_log2) {
+  if (budget_log2 < 16 || budget_log2 > 28)
+    return fail(TT_ERR_INVALID_ARGUMENT, "tt_test_arm_wait_timeout: budget_log2 must be in [16, 28]");
+  g_armed_timeout.store(budget_log2);
+  return TT_OK;
+}
+
+bool gemm_wait_timeout_armed() { return g_armed_timeout.load() != 0; }
 
 bool gemm_ln_fusable(int64_t M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0 || K > LN_MAX_K || K % 8 != 0 || N % 8 != 0) return false;

@@ -37,9 +37,20 @@ struct TcGemmParams {
   const float *ln_x;              // [M, K] fp32
   const float *ln_gamma, *ln_beta;
   float ln_eps;
+  // Bounded waits give up after 2^wait_budget_log2 cycles (0: 2^28). The test
+  // switch makes CTA 0's producer skip the loads of its first k-block (set by
+  // the launcher when tt_test_arm_wait_timeout armed it, 0 otherwise).
+  int wait_budget_log2;
+  int test_skip_first_load;
 };
 
 int launch_gemm_tc3(const TcGemmParams &p, cudaStream_t stream);
+
+// Test support (tt_test_arm_wait_timeout): the next launch of the single-CTA
+// kernel of launch_gemm_tc3 in this process runs with its test switch on and
+// a wait budget of 2^budget_log2 cycles; whether such a launch is pending.
+int arm_gemm_wait_timeout(int budget_log2);
+bool gemm_wait_timeout_armed();
 
 // Whether launch_gemm_ln_tc takes an M x N x K problem: K (the LayerNorm
 // width) at most 128 and a problem small enough for the single-CTA schedule.

@@ -19,14 +19,16 @@
 // directly: the kernels read their inputs when they run.
 //
 // Direct launches are used instead when TT_GRAPHS=0 is set in the
-// environment, while the launch probe is timing individual launches, and when
-// the caller's stream is itself being captured (the launches then go into the
-// caller's graph).
+// environment, while the launch probe is timing individual launches, while a
+// test switch is armed (tt_test_arm_wait_timeout), and when the caller's
+// stream is itself being captured (the launches then go into the caller's
+// graph).
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
 
+#include "gemm_tc.cuh"
 #include "image.cuh"
 #include "tt_common.cuh"
 
@@ -86,7 +88,9 @@ int capture(const ForwardLaunch &launch, cudaStream_t cap, cudaGraphExec_t *exec
 }  // namespace
 
 int run_forward_cached(const ForwardKey &key, cudaStream_t stream, const ForwardLaunch &launch) {
-  if (!graphs_enabled() || launch_probe_active()) return launch(stream);
+  // an armed test switch must reach exactly one launch, never a cached graph
+  if (!graphs_enabled() || launch_probe_active() || gemm_wait_timeout_armed())
+    return launch(stream);
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
   TT_CUDA_TRY(cudaStreamIsCapturing(stream, &cs));
   if (cs != cudaStreamCaptureStatusNone) return launch(stream);
