@@ -213,6 +213,7 @@ int tt_last_error(char *buf, size_t len);
 #define TT_KERNEL_FFN_OUT 6       /* ffn_out + residual + padded-row zeroing */
 #define TT_KERNEL_FINAL_NORM 7    /* final LayerNorm + padded-row zeroing */
 #define TT_KERNEL_WHOLE_FORWARD 8 /* the single-launch forward (TT_PLAN_CLUSTER) */
+#define TT_KERNEL_ROW_SCAN 9      /* valid lengths and live row tiles of a padded batch */
 
 /* Launch timing probe, a measurement aid with no counterpart in the
  * reference. tt_launch_probe_start(capacity) creates 2 * capacity timing

@@ -135,3 +135,14 @@ def test_fp16_operand_bound_argument_errors_need_no_gpu(lib):
                                      None) == _lib.TT_ERR_INVALID_ARGUMENT
     assert lib.tt_fp16_operand_bound(ctypes.byref(_cfg()), 256, None,
                                      None) == _lib.TT_ERR_INVALID_ARGUMENT
+
+
+def test_launch_count_includes_the_row_scan_of_gemm_heavy_shapes(lib):
+    e = _cfg(d=1024, h=16, f=4096, l=12)
+    # 7 launches per layer, the final LayerNorm, and the live-row scan
+    assert lib.tt_forward_launch_count(ctypes.byref(e), 64, 2048) == 7 * 12 + 1 + 1
+    small = _cfg(d=1024, h=16, f=4096, l=12)
+    assert lib.tt_forward_launch_count(ctypes.byref(small), 1, 512) == 7 * 12 + 1
+    d128 = _cfg()
+    d128.plan = _lib.PLAN_IDS["ops_tc"]
+    assert lib.tt_forward_launch_count(ctypes.byref(d128), 32, 512) == 7 * 4 + 1

@@ -175,6 +175,51 @@ def test_workload_E_parity_sequence_sample(variant):
     assert model.read_device_status() == (0, 0)
 
 
+def _lengths_mask(b, s, lengths):
+    m = torch.zeros(b, s, dtype=torch.bool)
+    for i, n in enumerate(lengths):
+        m[i, :n] = True
+    return m
+
+
+@pytest.mark.parametrize("seq,kind", [(300, "prefix"), (512, "prefix"), (1000, "prefix"),
+                                      (512, "holes"), (384, "none")])
+def test_dead_row_tiles_are_skipped_safely(seq, kind):
+    """GEMM-heavy shapes skip the 256-row tiles of the batch that hold only
+    rows past each sequence's last valid key (rounded up to 64). Sequence
+    lengths here include 0 (all padding), 1, odd lengths and full ones; a
+    sequence length that is not a multiple of 64 or 256 puts sequence
+    boundaries inside tiles; a mask with holes skips only its trailing part.
+    Every schedule matches the oracle and padded rows are exactly 0."""
+    from ttjam_gottagofast_b200.config import TransformerConfig
+    b = 6
+    cfg = TransformerConfig(batch_size=b, seq_len=seq, d_model=256, num_heads=4, ffn_dim=512,
+                            num_layers=2, causal=True)
+    model, params = model_for(cfg, seed=77)
+    g = torch.Generator().manual_seed(seq)
+    x = torch.randn(b, seq, 256, generator=g)
+    if kind == "none":
+        mask = None
+    elif kind == "prefix":
+        lengths = [0, 1, seq, seq // 3 + 1, seq - 63, 2 * seq // 3 - 5]
+        mask = _lengths_mask(b, seq, lengths)
+    else:
+        mask = _lengths_mask(b, seq, [seq, seq // 2, 300, 5, seq, 257])
+        mask[0, 100:300] = False   # a hole wider than a 256-row tile
+        mask[4, 10:20] = False
+    if mask is not None:
+        x = x.masked_fill(~mask[..., None], 0)
+        mask = mask.to(DEV)
+    x = x.to(DEV)
+    ref = oracle.forward(params, cfg, x, mask)
+    for plan, y in run_plans(model, x, mask).items():
+        check(ref, y, f"dead rows s{seq} {kind}[{plan}]")
+        assert torch.isfinite(y).all()
+        if mask is not None:
+            assert (y[~mask] == 0).all()
+    assert model.read_device_status() == (0, 0)
+
+
 def _inflated_v_model(plan="auto"):
     """A d256 model (a tensor-core shape) whose v_proj weights are scaled by
     1e5: its v values and attention contexts reach ~1e5-1e6, beyond the

@@ -45,7 +45,7 @@ EXPORTED = (
 
 # TT_KERNEL_* launch kinds reported by tt_launch_probe_read.
 KERNEL_KINDS = {1: "layernorm", 2: "qkv", 3: "attention", 4: "out_proj", 5: "ffn_in",
-                6: "ffn_out", 7: "final_norm", 8: "whole_forward"}
+                6: "ffn_out", 7: "final_norm", 8: "whole_forward", 9: "row_scan"}
 
 
 class TTConfig(ctypes.Structure):

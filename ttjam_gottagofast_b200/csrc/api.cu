@@ -320,6 +320,14 @@ bool ops_tc_fuses_ln(const tt_config &cfg, int64_t tokens) {
          gemm_ln_fusable(tokens, cfg.ffn_dim, cfg.d_model);
 }
 
+// GEMM-heavy shapes (d_model >= 256, at least four 256-row tiles) list the
+// live row tiles of the batch first (live_rows.cu) and their GEMMs skip the
+// rest: one small launch that reads the mask, against projections whose
+// cost per row tile is large. Without a mask every tile is live.
+bool ops_tc_skips_dead_rows(const tt_config &cfg, int64_t tokens) {
+  return cfg.d_model >= 256 && tokens >= 4 * 256;
+}
+
 int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image, const float *x,
                    const uint8_t *mask, int64_t batch, int64_t seq, float *y,
                    const WorkspaceLayout &W, char *ws, cudaStream_t stream) {
@@ -336,6 +344,24 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
   DeviceStatus *status = reinterpret_cast<DeviceStatus *>(const_cast<char *>(image) + L.status);
   const float eps = 1e-5f;
   const bool fuse_ln = ops_tc_fuses_ln(cfg, T);
+  const int *live = nullptr;  // live-row lists, or null: every tile
+  if (ops_tc_skips_dead_rows(cfg, T)) {
+    int *lv = reinterpret_cast<int *>(ws + W.live);
+    int rc;
+    if ((rc = timed_launch(TT_KERNEL_ROW_SCAN, stream, [&] {
+           return launch_live_rows(mask, batch, (int)seq, lv, stream);
+         })))
+      return rc;
+    live = lv;
+  }
+  const int64_t nst = (T + 255) / 256;
+  auto set_live = [&](TcGemmParams &g) {
+    if (live == nullptr) return;
+    g.live_count256 = live;
+    g.live_count128 = live + 1;
+    g.live_list256 = live + 2;
+    g.live_list128 = live + 2 + nst;
+  };
   for (int l = 0; l < cfg.num_layers; ++l) {
     const LayerOffsets &o = L.layer[l];
     auto P = [&](size_t off) { return reinterpret_cast<const float *>(image + off); };
@@ -363,6 +389,8 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
     }
     if (fuse_ln) {
       g.ln_x = xin; g.ln_gamma = P(o.ln1_w); g.ln_beta = P(o.ln1_b); g.ln_eps = eps;
+    } else {
+      set_live(g);
     }
     if ((rc = timed_launch(TT_KERNEL_QKV, stream, [&] {
            return fuse_ln ? launch_gemm_ln_tc(g, stream) : launch_gemm_tc3(g, stream);
@@ -392,6 +420,7 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
     go.acc_scale = wsc + 1;
     go.bias = P(o.bo); go.R = xin; go.C = y; go.ldc = D; go.row_mask = mask; go.status = status;
     go.M = (int)T; go.N = D; go.K = D; go.epilogue = EPI_BIAS_RESIDUAL;
+    set_live(go);
     if ((rc = timed_launch(TT_KERNEL_OUT_PROJ, stream, [&] { return launch_gemm_tc3(go, stream); })))
       return rc;
     if (!fuse_ln &&
@@ -408,6 +437,8 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
     g1.M = (int)T; g1.N = F; g1.K = D; g1.epilogue = EPI_BIAS_GELU;
     if (fuse_ln) {
       g1.ln_x = y; g1.ln_gamma = P(o.ln2_w); g1.ln_beta = P(o.ln2_b); g1.ln_eps = eps;
+    } else {
+      set_live(g1);
     }
     if ((rc = timed_launch(TT_KERNEL_FFN_IN, stream, [&] {
            return fuse_ln ? launch_gemm_ln_tc(g1, stream) : launch_gemm_tc3(g1, stream);
@@ -418,6 +449,7 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
     g2.acc_scale = wsc + 3;
     g2.bias = P(o.b2); g2.R = y; g2.C = y; g2.ldc = D; g2.row_mask = mask; g2.status = status;
     g2.M = (int)T; g2.N = D; g2.K = F; g2.epilogue = EPI_BIAS_RESIDUAL;
+    set_live(g2);
     if ((rc = timed_launch(TT_KERNEL_FFN_OUT, stream, [&] { return launch_gemm_tc3(g2, stream); })))
       return rc;
   }
@@ -556,7 +588,8 @@ int tt_forward_launch_count(const tt_config *cfg, int64_t batch, int64_t seq) {
   if (plan < 0) return plan;
   if (plan == PLAN_CLUSTER) return 1;
   if (plan == PLAN_OPS_TC)
-    return (ops_tc_fuses_ln(*cfg, batch * seq) ? 5 : 7) * cfg->num_layers + 1;
+    return (ops_tc_fuses_ln(*cfg, batch * seq) ? 5 : 7) * cfg->num_layers + 1 +
+           (ops_tc_skips_dead_rows(*cfg, batch * seq) ? 1 : 0);
   return 5 * cfg->num_layers + 1;
 }
 

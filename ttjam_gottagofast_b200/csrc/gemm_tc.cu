@@ -438,7 +438,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KB = (p.K + BK - 1) / BK;
   const int MT = (p.M + BM - 1) / BM, NT = (p.N + BN - 1) / BN;
-  const int ntiles = MT * NT;
   const int budget = p.wait_budget_log2 > 0 ? p.wait_budget_log2 : 28;
   // test switch (tt_test_arm_wait_timeout): CTA 0's producer never starts the
   // loads of its first k-block, so nothing ever completes that stage
@@ -473,7 +472,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot_ptr;
-  pdl_wait();  // A (and R) come from the previous kernel
+  pdl_wait();  // A (and R) come from the previous kernel, the live-tile list too
+  // tiles: the live 128-row tiles (all when there is no list) x NT column tiles
+  const int ntiles = (p.live_count128 != nullptr ? *p.live_count128 : MT) * NT;
+  auto tile_m0 = [&](int tile) {
+    const int i = tile / NT;
+    return (p.live_list128 != nullptr ? p.live_list128[i] : i) * BM;
+  };
 
   // A wait that gives up stops its role: no further loads, MMAs, commits or
   // arrivals (each stage is armed only after its previous phase was consumed,
@@ -486,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-      const int m0 = (tile / NT) * BM, n0 = (tile % NT) * BN;
+      const int m0 = tile_m0(tile), n0 = (tile % NT) * BN;
       for (int kb = 0; kb < KB; ++kb, ++it) {
         const int s = it % STAGES, n = it / STAGES;
         if (it >= STAGES && !mbar_wait(empty_bar(s), (n - 1) & 1, abort_w, p.status, 0x1000,
@@ -562,7 +567,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int local = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
       const int ab = local & 1;
-      const int m0 = (tile / NT) * BM, n0 = (tile % NT) * BN;
+      const int m0 = tile_m0(tile), n0 = (tile % NT) * BN;
       BiasRegs bias;
       load_bias_regs(p, n0 + c_lo, c_hi - c_lo, lane, bias);
       // warp-uniform outcome (the tensor-memory loads below are warp-collective)
@@ -721,7 +726,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int KB = (p.K + BK - 1) / BK;
   const int MT = (p.M + 255) / 256, NT = (p.N + PBN - 1) / PBN;
-  const int ntiles = MT * NT;
   pdl_trigger();
   if (threadIdx.x == 32) {
     prefetch_tmap(&tm_a_hi); prefetch_tmap(&tm_a_lo); prefetch_tmap(&tm_w_hi);
@@ -752,14 +756,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync_all();  // both CTAs' barriers exist before any remote arrive or TMA
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot_ptr;
-  pdl_wait();  // A (and R) come from the previous kernel
+  pdl_wait();  // A (and R) come from the previous kernel, the live-tile list too
+  // tiles: the live 256-row tiles (all when there is no list) x NT column tiles
+  const int ntiles = (p.live_count256 != nullptr ? *p.live_count256 : MT) * NT;
+  auto tile_m = [&](int tile) {  // first row of the pair's 256-row tile
+    const int i = tile / NT;
+    return (p.live_list256 != nullptr ? p.live_list256[i] : i) * 256;
+  };
   const uint32_t full0 = map_to_cta(full_bar(0), 0);  // CTA 0's full barriers (cluster addresses)
 
   if (warp == 0 && lane == 0) {
     // ---- TMA producer (both CTAs): this CTA's A rows and W half ------------
     int it = 0;
     for (int tile = pair; tile < ntiles; tile += npairs) {
-      const int m0 = (tile / NT) * 256 + 128 * (int)rank;
+      const int m0 = tile_m(tile) + 128 * (int)rank;
       const int n0 = (tile % NT) * PBN + (PBN / 2) * (int)rank;
       for (int kb = 0; kb < KB; ++kb, ++it) {
         const int s = it % PSTAGES, n = it / PSTAGES;
@@ -822,7 +832,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int local = 0;
     for (int tile = pair; tile < ntiles; tile += npairs, ++local) {
       const int ab = local & 1;
-      const int m0 = (tile / NT) * 256 + 128 * (int)rank, n0 = (tile % NT) * PBN;
+      const int m0 = tile_m(tile) + 128 * (int)rank, n0 = (tile % NT) * PBN;
       BiasRegs bias;
       load_bias_regs(p, n0 + c_lo, c_hi - c_lo, lane, bias);
       mbar_wait(acc_full(ab), (local >> 1) & 1, abort_w, p.status, 0x3000);

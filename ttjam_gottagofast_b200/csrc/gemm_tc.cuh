@@ -42,6 +42,11 @@ struct TcGemmParams {
   // the launcher when tt_test_arm_wait_timeout armed it, 0 otherwise).
   int wait_budget_log2;
   int test_skip_first_load;
+  // Live row tiles (live_rows.cu), written by an earlier kernel of the
+  // forward: the count and ascending list of 256-row tiles (CTA-pair kernel)
+  // and of 128-row tiles (single-CTA kernel) to compute; the others are
+  // skipped. Null: every tile.
+  const int *live_count256, *live_list256, *live_count128, *live_list128;
 };
 
 int launch_gemm_tc3(const TcGemmParams &p, cudaStream_t stream);

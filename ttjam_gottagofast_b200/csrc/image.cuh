@@ -86,8 +86,14 @@ struct ImageLayout {
   }
 };
 
+// Live-row lists of a padded batch (live_rows.cu): ints in the workspace.
+size_t live_rows_ints(int64_t batch, int64_t seq);
+int launch_live_rows(const uint8_t *mask, int64_t batch, int seq, int *ws_ints,
+                     cudaStream_t stream);
+
 struct WorkspaceLayout {
   size_t qkv = 0, ctx = 0, h = 0, qk_hi = 0, qk_lo = 0, vt_hi = 0, vt_lo = 0;
+  size_t live = 0;  // live-row lists (ints), tensor-core schedule
   int seq_pad = 0;  // row stride of the transposed value copy (multiple of 4)
   size_t ln_hi = 0, ln_lo = 0, ctx_hi = 0, ctx_lo = 0, h_hi = 0, h_lo = 0;
   size_t total = 0;
@@ -125,6 +131,7 @@ struct WorkspaceLayout {
       ln_hi = take(T * D / 2); ln_lo = take(T * D / 2);
       ctx_hi = take(T * D / 2); ctx_lo = take(T * D / 2);
       h_hi = take(T * F / 2); h_lo = take(T * F / 2);
+      live = take(live_rows_ints(batch, seq));
     } else {
       ctx = take(T * D);
       h = take(T * F);
@@ -160,6 +167,9 @@ int noalloc_scratch_address(void **out);
 int forward_ops(const tt_config &cfg, const ImageLayout &L, const char *image, const float *x,
                 const uint8_t *mask, int64_t batch, int64_t seq, float *y,
                 const WorkspaceLayout &W, char *ws, cudaStream_t stream);
+// Whether the tensor-core schedule lists the live row tiles of the batch and
+// lets its GEMMs skip the rest (one extra launch): GEMM-heavy shapes only.
+bool ops_tc_skips_dead_rows(const tt_config &cfg, int64_t tokens);
 int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image, const float *x,
                    const uint8_t *mask, int64_t batch, int64_t seq, float *y,
                    const WorkspaceLayout &W, char *ws, cudaStream_t stream);
