@@ -17,10 +17,11 @@ Our arm prints one JSON line with
              on the device with CUDA events around each step on the launching
              stream, inputs resident in HBM, L2 flushed between steps (a 256 MiB
              write), max over ranks;
-  e2e        the same metric through the public module call
-             (UserOptimizedTransformer.forward) from pinned host buffers, with
-             the host->device copy of x and the mask and the device->host copy
-             of y inside each timed step;
+  e2e        the same metric through the public host-buffer call
+             (UserOptimizedTransformer.forward_host) from pinned host buffers,
+             with the host->device copy of x and the mask and the device->host
+             copy of y inside each timed step (overlapped with the compute of
+             other slices of the batch);
   roofline   the dominant kernel kind (largest share of the device time in
              a separate pass of K steps, each launch bracketed by CUDA events on
              its stream through the library's launch probe; the timed steps
@@ -493,27 +494,28 @@ def run_ours(args, world, rank, local):
     e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     with torch.inference_mode():
         for _ in range(3):
-            xd = xh.to(dev, non_blocking=True)
-            md = mh.to(dev, non_blocking=True)
-            yh.copy_(model(xd, md), non_blocking=True)
-        del xd, md
+            model.forward_host(xh, mh, out=yh, device=dev)
         torch.cuda.synchronize(dev)
         barrier(world)
         for i in range(args.steps):
             flush.fill_(i & 0xFF)
             e_starts[i].record(stream)
-            xd = xh.to(dev, non_blocking=True)
-            md = mh.to(dev, non_blocking=True)
-            yd = model(xd, md)
-            yh.copy_(yd, non_blocking=True)
+            # host buffers in, host buffer out: copies overlapped with compute
+            model.forward_host(xh, mh, out=yh, device=dev)
             e_ends[i].record(stream)
-            del xd, md, yd  # stream-ordered reuse by the next step
         torch.cuda.synchronize(dev)
         barrier(world)
     e_total = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(e_starts, e_ends)), world)
     e2e_value = tokens_per_step_all * args.steps * 1000.0 / e_total
     got = yh if check_rows is None else yh.view(nb * S, -1)[check_rows]
-    assert torch.equal(got, y_check), "e2e output differs from the device-timed output"
+    e2e_bitwise = torch.equal(got, y_check)
+    if not e2e_bitwise:
+        # the host path runs the batch in slices of whole sequences; the rows
+        # are the same computations, so only rounding could differ
+        from ttjam_gottagofast_b200.contract import compare_outputs
+        res = compare_outputs(y_check, got)
+        assert res.passed and res.max_abs_error <= 1e-4, \
+            f"e2e output differs from the device-timed output: {res}"
 
     # ---- roofline of the dominant kernel kind -------------------------------
     hbm_peak, tc_burst, tc_sust, peak_kind = load_peaks()
@@ -586,7 +588,10 @@ def run_ours(args, world, rank, local):
         "e2e": {"value": e2e_value, "unit": "tokens/s",
                 "h2d_bytes_per_step": x_host.numel() * 4 + m_host.numel(),
                 "d2h_bytes_per_step": x_host.numel() * 4,
-                "path": "UserOptimizedTransformer.forward from pinned host buffers"},
+                "path": ("UserOptimizedTransformer.forward_host from pinned host buffers to a "
+                         "pinned host buffer (batch in slices of whole sequences, copies on "
+                         "their own streams overlapped with compute)"),
+                "equal_to_device_output": "bitwise" if e2e_bitwise else "within 1e-4"},
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

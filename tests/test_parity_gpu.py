@@ -488,3 +488,25 @@ def test_forward_inside_caller_graph_capture():
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("slices", [1, 3, 4])
+def test_forward_host_matches_device_forward(slices):
+    """forward_host: host buffers in and out, the batch in slices whose copies
+    overlap the compute on their own streams; the result equals the device
+    forward's (the same row computations) and the current stream is ordered
+    after the last copy."""
+    from ttjam_gottagofast_b200.config import TransformerConfig
+    cfg = TransformerConfig(batch_size=7, seq_len=256, d_model=256, num_heads=4, ffn_dim=512,
+                            num_layers=2, causal=True)
+    model, params = model_for(cfg, seed=31)
+    x, mask = generate_random_case(cfg, "cpu", torch.float32, 17, 0.5, 1.0)
+    xh, mh = x.pin_memory(), mask.pin_memory()
+    with torch.inference_mode():
+        ref_dev = model(x.to(DEV), mask.to(DEV)).cpu()
+        out = model.forward_host(xh, mh, slices=slices)
+    torch.cuda.current_stream().synchronize()
+    res = compare_outputs(ref_dev, out)
+    assert res.passed and res.max_abs_error <= 1e-5, res
+    assert (out[~mask] == 0).all()
+    check(oracle.forward(params, cfg, x.to(DEV), mask.to(DEV)).cpu(), out, f"host x{slices}")

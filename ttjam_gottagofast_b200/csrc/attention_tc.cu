@@ -20,23 +20,26 @@
 // and moves half the operand bytes.
 //
 // CTA = (query tile of 128 rows, head, sequence; and, at head_dim 256, half
-// of the output dims); 320 threads. Up to head_dim 64 two CTAs share an SM
-// (256 tensor-memory columns and a 3-stage ring each), so that one CTA's
-// softmax runs while the other's MMAs use the tensor pipe; from head_dim 128
-// a CTA takes 512 columns and runs alone:
+// of the output dims). Up to head_dim 64 two CTAs share an SM (256
+// tensor-memory columns each), so that one CTA's softmax runs while the
+// other's MMAs use the tensor pipe; from head_dim 128 a CTA takes 512 columns
+// and runs alone:
 //   warp 0    TMA producer: per 64-key tile, K_hi K_lo (64 keys x HD dims) and
 //             Vt_hi Vt_lo (HD dims x 64 keys, from the transposed copy of v the
 //             q|k|v GEMM writes) into the ring;
 //   warp 1    allocates / frees the tensor memory; then its lane 0 issues the
 //             MMAs: S_j = Q.K^T (A = Q from tensor memory, B = K tile) into
-//             S/P buffer j % 2, two tiles ahead of the softmax, and
-//             O += P_j.V_j (A = P_j from the same buffer, B = Vt tile) once
-//             the softmax has written P_j; both B operands are K-major;
-//   warps 2-9 softmax, two warps per tensor-memory lane quarter: query row
-//             q0+t (= tensor-memory lane t) is shared by two threads, one per
-//             half of the 64-key tile; they exchange the row max through shared
-//             memory (one named barrier per tile), write their half of P (split)
-//             to tensor memory and keep a partial row sum. The P.V MMAs
+//             S/P buffer j % NB (NB = 3 up to head_dim 32, else 2), NB tiles
+//             ahead of the softmax, and O += P_j.V_j (A = P_j from the same
+//             buffer, B = Vt tile) once the softmax has written P_j; both B
+//             operands are K-major;
+//   softmax   up to head_dim 64, warps 2-5 (192 threads per CTA): query row
+//             q0+t (= tensor-memory lane t) belongs to one thread, which reads
+//             the 64 scores of each tile, takes the row max on its own, and
+//             writes P (split) over them; two CTAs per SM leave 128 registers
+//             per thread. From head_dim 128, warps 2-9 (320 threads): two
+//             threads per row, one per 32-key half, exchange the row max
+//             through shared memory (one named barrier per tile). The P.V MMAs
 //             accumulate the context in tensor memory, rescaled only when the
 //             row max grows by more than 2^8.
 // Every mbarrier wait is bounded; a wait that gives up latches
@@ -56,6 +59,7 @@ namespace {
 
 constexpr int BQ = 128, BKV = 64;
 constexpr int kThreads = 320;  // warp 0: TMA; warp 1: TMEM + MMA; warps 2-9: softmax
+constexpr int kThreadsRow1 = 192;  // the same with softmax warps 2-5, one thread per row
 constexpr int kSoftWarp0 = 2;  // first softmax warp
 
 // Shapes for an MMA head dim HD (16, 32, 64, 128 or 256; head_dim 8 runs as
@@ -88,11 +92,18 @@ struct AtShape {
   static constexpr int NSPLIT = HD / HDO;
   static constexpr uint32_t OPV = HDO * 128;            // one V^T operand (hi or lo)
   static constexpr uint32_t STAGE = 2 * OPK + 2 * OPV;
-  static constexpr int NST = HD > 128 ? 2 : 3;          // ring stages
+  // S/P buffers in tensor memory: the scores of tile j + NB are issued after
+  // P_j.V_j has read buffer j % NB, so NB tiles are in flight between the
+  // MMAs and the softmax; three where the columns allow it (head_dim up to 32)
+  static constexpr int NB = HD <= 32 ? 3 : 2;
+  // ring stages: a stage holds tile j's K and V from their load until P_j.V_j
+  // has read them, so one stage more than S/P buffers lets the next load start
+  // a tile early
+  static constexpr int NST = HD > 128 ? 2 : NB + 1;
   static constexpr size_t SMEM_BYTES = (size_t)NST * STAGE + 1024 + 256;
-  static constexpr uint32_t T_QHI = 0, T_QLO = HD / 2, T_SP = HD, T_O = HD + 128;
+  static constexpr uint32_t T_QHI = 0, T_QLO = HD / 2, T_SP = HD, T_O = HD + 64 * NB;
   // two CTAs per SM up to head_dim 64 (256 columns each), one above
-  static constexpr uint32_t TMEM_COLS = HD + 128 + HDO <= 256 ? 256 : 512;
+  static constexpr uint32_t TMEM_COLS = HD + 64 * NB + HDO <= 256 ? 256 : 512;
   static_assert(T_O + HDO <= TMEM_COLS, "tensor memory");
   static_assert(KPART % 1024 == 0 && OPV % 1024 == 0, "operands on the swizzle period");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
@@ -284,6 +295,49 @@ __device__ __forceinline__ void tmem_wait_st() {
 __device__ __forceinline__ void split_pair(float a, float b, uint32_t &hi, uint32_t &lo) {
   f16_split2(a, b, hi, lo);
 }
+// The same split for two non-negative values below 65504 (the scaled
+// probabilities P): hi = x rounded to fp16, lo = x - hi rounded to fp16, with
+// hi widened back to fp32 by integer operations instead of conversions: the
+// fp16 bit pattern shifted into the fp32 exponent field is 2^-112 times its
+// value, for normal and subnormal fp16 alike, so one multiply by 2^112
+// (without flush-to-zero) gives it exactly.
+__device__ __forceinline__ float widen_f16_nonneg(uint32_t h16) {
+  float r;
+  asm("mul.rn.f32 %0, %1, 0f77800000;" : "=f"(r) : "f"(__uint_as_float(h16 << 13)));
+  return r;
+}
+__device__ __forceinline__ void split_pair_nonneg(float a, float b, uint32_t &hi, uint32_t &lo) {
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(b), "f"(a));
+  const float ha = widen_f16_nonneg(hi & 0xffffu), hb = widen_f16_nonneg(hi >> 16);
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(__fsub_rn(b, hb)), "f"(__fsub_rn(a, ha)));
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t *v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+      "%29, %30, %31, %32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
+      "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
+      "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
 
 // Named barrier of the two softmax warps that serve lane quarter q (ids 1-4,
 // immediates: a register id would make the compiler reserve all 16 barriers,
@@ -297,7 +351,12 @@ __device__ __forceinline__ void pair_barrier(int q) {
   }
 }
 
-template <int HD, bool GROUPED>
+// ROW1 (head_dim up to 64): one softmax thread per query row, all 64 keys of
+// a tile, 4 softmax warps and 192 threads per CTA -- no row-max exchange
+// between threads, and two CTAs per SM leave 128 registers per thread.
+// Otherwise two threads per row (one per 32-key half) exchange the row max
+// through shared memory: 8 softmax warps, 320 threads.
+template <int HD, bool GROUPED, bool ROW1>
 __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
                                                   const CUtensorMap &tm_lo,
                                                   const CUtensorMap &tm_vhi,
@@ -305,26 +364,30 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
                                                   const AttentionTcParams &p) {
   using Sh = AtShape<HD>;
   constexpr uint32_t STAGE = Sh::STAGE, OPK = Sh::OPK, OPV = Sh::OPV;
-  constexpr int STAGES = Sh::NST, HDO = Sh::HDO;
+  constexpr int STAGES = Sh::NST, HDO = Sh::HDO, NB = Sh::NB;
   constexpr uint32_t T_QHI = Sh::T_QHI, T_QLO = Sh::T_QLO, T_O = Sh::T_O,
                      TMEM_COLS = Sh::TMEM_COLS;
+  constexpr int NTHREADS = ROW1 ? kThreadsRow1 : kThreads;
+  constexpr int NSOFT = ROW1 ? 4 : 8;  // softmax warps (one arrival each per barrier phase)
+  static_assert(!ROW1 || HD <= 64, "one thread per row up to head_dim 64");
   extern __shared__ uint8_t smem_raw[];
   __shared__ int s_kv_len, s_first_hole;
-  __shared__ float s_rowmax[2][2][128];  // [tile parity][key half][row]
-  __shared__ float s_rowsum[2][128];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   const uint32_t bars = base + STAGES * STAGE;
   auto kv_full = [&](int s) { return bars + 8u * s; };
   auto kv_empty = [&](int s) { return bars + 8u * (STAGES + s); };
-  // per S/P buffer b: S of its next tile written, P of that tile written
+  // per S/P buffer b: S of its next tile written, P of that tile written, and
+  // the P.V that read it finished
   auto s_full = [&](int b) { return bars + 8u * (2 * STAGES + b); };
-  auto p_full = [&](int b) { return bars + 8u * (2 * STAGES + 2 + b); };
-  const uint32_t o_done = bars + 8u * (2 * STAGES + 4);   // a P.V finished
-  const uint32_t q_ready = bars + 8u * (2 * STAGES + 5);
-  const uint32_t o_final = bars + 8u * (2 * STAGES + 6);  // every MMA finished
-  const uint32_t tmem_slot = bars + 8u * (2 * STAGES + 7);
-  const uint32_t drain_bar = bars + 8u * (2 * STAGES + 8);  // the MMA thread's last commit
+  auto p_full = [&](int b) { return bars + 8u * (2 * STAGES + NB + b); };
+  auto o_done = [&](int b) { return bars + 8u * (2 * STAGES + 2 * NB + b); };
+  constexpr uint32_t XB = 2 * STAGES + 3 * NB;  // the barriers after those
+  const uint32_t q_ready = bars + 8u * XB;
+  const uint32_t o_final = bars + 8u * (XB + 1);  // every MMA finished
+  const uint32_t tmem_slot = bars + 8u * (XB + 2);
+  const uint32_t drain_bar = bars + 8u * (XB + 3);  // the MMA thread's last commit
+  static_assert(8 * (XB + 4) <= 256, "barrier area");
   uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
   volatile int *abort_w = reinterpret_cast<volatile int *>(smem_raw + (tmem_slot + 4 - raw));
 
@@ -364,7 +427,7 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
   if (mrow) {
     int last = 0, hole = S;
     if ((reinterpret_cast<uintptr_t>(mrow) & 15) == 0 && S % 16 == 0) {
-      for (int j = threadIdx.x; j < S / 16; j += kThreads) {
+      for (int j = threadIdx.x; j < S / 16; j += NTHREADS) {
         const uint4 v = reinterpret_cast<const uint4 *>(mrow)[j];
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -377,7 +440,7 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
         }
       }
     } else {
-      for (int j = threadIdx.x; j < S; j += kThreads) {
+      for (int j = threadIdx.x; j < S; j += NTHREADS) {
         if (mrow[j]) last = j + 1;
         else hole = min(hole, j);
       }
@@ -399,12 +462,12 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
       mbar_init(kv_empty(s), 1);
     }
     // the 8 softmax warps arrive once per warp (an elected lane after __syncwarp)
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NB; ++b) {
       mbar_init(s_full(b), 1);
-      mbar_init(p_full(b), 8);
+      mbar_init(p_full(b), NSOFT);
+      mbar_init(o_done(b), 1);
     }
-    mbar_init(o_done, 1);
-    mbar_init(q_ready, 8);
+    mbar_init(q_ready, NSOFT);
     mbar_init(o_final, 1);
     mbar_init(drain_bar, 1);
     *abort_w = 0;
@@ -454,14 +517,14 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
       mbar_drain(kv_full(k % STAGES), (k / STAGES) & 1, p.status, 0x4F00);
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer --------------------------------------------------------
-    // S_j goes to buffer j & 1. The tensor pipe runs one thread's MMAs in
-    // issue order, so S_{j+2}, issued after P_j.V_j, overwrites P_j only after
+    // S_j goes to buffer j % NB. The tensor pipe runs one thread's MMAs in
+    // issue order, so S_{j+NB}, issued after P_j.V_j, overwrites P_j only after
     // that product has read it.
     auto issue_s = [&](int j) -> bool {
       const int s = j % STAGES;
       if (!mbar_wait(kv_full(s), (j / STAGES) & 1, abort_w, p.status, 0x4200 + j)) return false;
       const uint32_t kst = base + s * STAGE;
-      const uint32_t sd = tm + Sh::T_SP + 64u * (j & 1);
+      const uint32_t sd = tm + Sh::T_SP + 64u * (uint32_t)(j % NB);
       // descriptors built once per box; a k-step of 16 dims advances the start
       // address by 32 bytes (2 units) inside its box
       constexpr int KK_BOX = Sh::KBOX / 16;  // k-steps per box
@@ -475,16 +538,15 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
         mma_ts(sd, tm + T_QHI + 8u * kk, klo0 + koff, Sh::IDESC_S, 1);
         mma_ts(sd, tm + T_QLO + 8u * kk, khi0 + koff, Sh::IDESC_S, 1);
       }
-      mma_commit(s_full(j & 1));
+      mma_commit(s_full(j % NB));
       return true;
     };
     bool ok = mbar_wait(q_ready, 0, abort_w, p.status, 0x4000);
     fence_after();
-    ok = ok && issue_s(0);
-    if (nkv > 1) ok = ok && issue_s(1);
+    for (int j = 0; j < NB && j < nkv; ++j) ok = ok && issue_s(j);
     for (int j = 0; ok && j < nkv; ++j) {
-      const int s = j % STAGES, b = j & 1;
-      if (!mbar_wait(p_full(b), (j >> 1) & 1, abort_w, p.status, 0x4400 + j)) {
+      const int s = j % STAGES, b = j % NB;
+      if (!mbar_wait(p_full(b), (j / NB) & 1, abort_w, p.status, 0x4400 + j)) {
         ok = false;
         break;
       }
@@ -501,16 +563,182 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
         mma_ts(tm + T_O, phi, vlo0 + voff, Sh::IDESC_PV, 1);
         mma_ts(tm + T_O, phi + 16u, vhi0 + voff, Sh::IDESC_PV, 1);
       }
-      mma_commit(o_done);
+      mma_commit(o_done(b));
       mma_commit(kv_empty(s));
-      if (j + 2 < nkv) ok = issue_s(j + 2);  // into the buffer P_j.V_j has just read
+      if (j + NB < nkv) ok = issue_s(j + NB);  // into the buffer P_j.V_j has just read
     }
     if (ok) mma_commit(o_final);
     // every MMA issued above has completed before the tensor memory is freed
     mma_commit(drain_bar);
     mbar_drain(drain_bar, 0, p.status, 0x4F10);
   } else if (warp >= kSoftWarp0) {
+   if constexpr (ROW1) {
+    // ---- softmax, one thread per query row (warps 2-5) ----------------------
+    const int t = (warp & 3) * 32 + lane;   // row within the tile = tensor-memory lane
+    const int row = q0 + t;
+    const bool row_in = row < S;
+    const uint32_t lane_base = tm + ((uint32_t)((warp & 3) * 32) << 16);
+    {
+      // Q row -> tensor memory: HD dims as HD/2 packed cells of Q_hi and of
+      // Q_lo; dims at or past hd (the padding of head_dim 8) are zero
+      const int64_t qoff = (b * S + (row_in ? row : 0)) * (int64_t)(2 * D) + (int64_t)h * hd;
+      constexpr int QC = HD / 2 < 16 ? HD / 2 : 16;  // cells per store
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const uint4 *src = reinterpret_cast<const uint4 *>((which ? p.qk_lo : p.qk_hi) + qoff);
+        const uint32_t tcol = lane_base + (which ? T_QLO : T_QHI);
+#pragma unroll
+        for (int c = 0; c < HD / 2; c += QC) {
+          uint32_t qv[QC];
+#pragma unroll
+          for (int i = 0; i < QC / 4; ++i) {
+            const int d0 = 2 * c + 8 * i;  // first dim of this 16-byte chunk
+            const uint4 v = (row_in && d0 < hd) ? src[d0 / 8] : make_uint4(0u, 0u, 0u, 0u);
+            qv[4 * i] = v.x; qv[4 * i + 1] = v.y; qv[4 * i + 2] = v.z; qv[4 * i + 3] = v.w;
+          }
+          if constexpr (QC == 16) tmem_st16(tcol + c, qv);
+          else if constexpr (QC == 8) tmem_st8(tcol + c, qv);
+          else tmem_st4(tcol + c, qv);
+        }
+      }
+      tmem_wait_st();
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_ready);
+    }
+    // log2-domain scores, lazy reference max and the 2^7 scale of P as in the
+    // two-threads-per-row form below, with the whole row in this thread
+    const float sl = p.scale * 1.4426950408889634f;
+    constexpr float kLazy = 8.0f;
+    constexpr float kPScale = 7.0f;
+    float m_ref = -CUDART_INF_F, l = 0.f;
+    for (int j = 0; j < nkv; ++j) {
+      const int sb = j % NB;
+      const int k0 = j * BKV;
+      // allowed keys k0 .. k0 + 31 (ok0) and k0 + 32 .. k0 + 63 (ok1)
+      uint32_t ok0, ok1;
+      if (mtile == nullptr) {
+        const int n = kv_end - k0, n1 = n - 32;
+        ok0 = n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : (1u << n) - 1u);
+        ok1 = n1 >= 32 ? 0xffffffffu : (n1 <= 0 ? 0u : (1u << n1) - 1u);
+      } else {
+        const int ka = k0 + lane, kb2 = k0 + 32 + lane;
+        ok0 = __ballot_sync(0xffffffffu, ka < kv_end && mtile[ka] != 0);
+        ok1 = __ballot_sync(0xffffffffu, kb2 < kv_end && mtile[kb2] != 0);
+      }
+      const bool diag = p.causal && k0 + 63 > q0;  // tile reaches past the first query
+      const bool open = !diag && (ok0 & ok1) == 0xffffffffu;  // warp-uniform
+      const uint32_t sp = lane_base + Sh::T_SP + 64u * sb;
+      mbar_wait(s_full(sb), (j / NB) & 1, abort_w, p.status, 0x4500 + j);
+      fence_after();
+      float sv[64];
+      tmem_ld32(sp, sv);
+      tmem_ld32(sp + 32, sv + 32);
+      tmem_wait_ld();
+      if (!open) {
+        uint32_t a0 = ok0, a1 = ok1;
+        if (diag) {
+          const int lim = row - k0, lim1 = lim - 32;  // keys k0 + c <= row
+          a0 &= lim >= 31 ? 0xffffffffu : (lim < 0 ? 0u : (2u << lim) - 1u);
+          a1 &= lim1 >= 31 ? 0xffffffffu : (lim1 < 0 ? 0u : (2u << lim1) - 1u);
+        }
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          sv[c] = (a0 >> c) & 1u ? sv[c] : -CUDART_INF_F;
+          sv[32 + c] = (a1 >> c) & 1u ? sv[32 + c] : -CUDART_INF_F;
+        }
+      }
+      // row max of the raw scores, eight chains of three-input maxima
+      float mx8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        mx8[i] = fmax3(sv[i], sv[i + 8], sv[i + 16]);
+        mx8[i] = fmax3(mx8[i], sv[i + 24], sv[i + 32]);
+        mx8[i] = fmax3(mx8[i], sv[i + 40], sv[i + 48]);
+        mx8[i] = fmaxf(mx8[i], sv[i + 56]);
+      }
+      const float mx = fmaxf(fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]),
+                                   mx8[6]),
+                             mx8[7]) * sl;
+      const bool raise = mx > m_ref + kLazy || (m_ref == -CUDART_INF_F && mx != -CUDART_INF_F);
+      const float alpha = raise ? fast_exp2(m_ref - mx) : 1.f;  // 0 when m_ref is -inf
+      // context rows of the warp rescaled together (warp-collective tensor-
+      // memory access; alpha = 1 for the rows that need none), after
+      // P_{j-1}.V_{j-1} has landed in them (the parity wait is exact as below)
+      if (__any_sync(0xffffffffu, raise && m_ref != -CUDART_INF_F) && j > 0) {
+        mbar_wait(o_done((j - 1) % NB), ((j - 1) / NB) & 1, abort_w, p.status, 0x4600 + j);
+        fence_after();
+        constexpr int OC = HDO >= 16 ? 16 : 8;
+#pragma unroll
+        for (int c = 0; c < HDO; c += OC) {
+          float ov[OC];
+          tmem_ld_n<OC>(lane_base + T_O + c, ov);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < OC; ++i) ov[i] *= alpha;
+          if constexpr (OC == 16) tmem_st16_f32(lane_base + T_O + c, ov);
+          else tmem_st8_f32(lane_base + T_O + c, ov);
+        }
+      }
+      if (raise) {
+        l *= alpha;
+        m_ref = mx;
+      }
+      // 2^7 p = 2^(s * sl - (m_ref - 7)), 0 for masked keys; each pair of
+      // probabilities is split as soon as it exists, and P_j goes over S_j,
+      // each 32-key half as 16 cells of P_hi then 16 of P_lo
+      const bool live = m_ref != -CUDART_INF_F;
+      const float noff = kPScale - m_ref;
+      float ps4[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t w[32];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const float e0 = live ? fast_exp2(fmaf(sv[32 * half + 2 * c], sl, noff)) : 0.f;
+          const float e1 = live ? fast_exp2(fmaf(sv[32 * half + 2 * c + 1], sl, noff)) : 0.f;
+          ps4[(2 * c) & 3] += e0;
+          ps4[(2 * c + 1) & 3] += e1;
+          split_pair_nonneg(e0, e1, w[c], w[16 + c]);
+        }
+        tmem_st32(sp + 32u * half, w);
+      }
+      l += (ps4[0] + ps4[1]) + (ps4[2] + ps4[3]);
+      tmem_wait_st();
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full(sb));
+    }
+    // context = O / l, written as an fp16 split (the out_proj GEMM's A operand)
+    mbar_wait(o_final, 0, abort_w, p.status, 0x4700);
+    fence_after();
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const int64_t off = (b * S + (row_in ? row : 0)) * (int64_t)D + (int64_t)h * hd;
+    // 8-dim chunks at HD 16, so that head_dim 8 (run as 16) stores only its own
+    constexpr int OC = HDO >= 32 ? 16 : 8;
+#pragma unroll
+    for (int c = 0; c < HDO; c += OC) {
+      float ov[OC];
+      tmem_ld_n<OC>(lane_base + T_O + c, ov);
+      tmem_wait_ld();
+      if (row_in && c < hd) {  // the padding dims of head_dim 8 are not stored
+        uint32_t hw[OC / 2], lw[OC / 2];
+#pragma unroll
+        for (int i = 0; i < OC / 2; ++i)
+          split_pair(ov[2 * i] * inv, ov[2 * i + 1] * inv, hw[i], lw[i]);
+        uint4 *dh = reinterpret_cast<uint4 *>(p.ctx_hi + off + c);
+        uint4 *dl = reinterpret_cast<uint4 *>(p.ctx_lo + off + c);
+#pragma unroll
+        for (int u = 0; u < OC / 8; ++u) {
+          dh[u] = make_uint4(hw[4 * u], hw[4 * u + 1], hw[4 * u + 2], hw[4 * u + 3]);
+          dl[u] = make_uint4(lw[4 * u], lw[4 * u + 1], lw[4 * u + 2], lw[4 * u + 3]);
+        }
+      }
+    }
+   } else {
     // ---- softmax: rows split over two warpgroups by key half ----------------
+    __shared__ float s_rowmax[2][2][128];  // [tile parity][key half][row]
+    __shared__ float s_rowsum[2][128];
     const int t = (warp & 3) * 32 + lane;   // row within the tile = tensor-memory lane
     const int kh = (warp - kSoftWarp0) >> 2;  // which 32 keys (and HD/2 dims) of a tile
     const int row = q0 + t;
@@ -561,7 +789,7 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
     constexpr float kPScale = 7.0f;  // log2 of the scale applied to P
     float m_ref = -CUDART_INF_F, l = 0.f;
     for (int j = 0; j < nkv; ++j) {
-      const int sb = j & 1;
+      const int sb = j % NB;
       const int k0 = j * BKV + 32 * kh;     // first key of this thread's half
       uint32_t ok;
       if (mtile == nullptr) {
@@ -576,7 +804,7 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
       // every key of this half allowed for every row of the warp (warp-uniform)
       const bool open = !diag && ok == 0xffffffffu;
       const uint32_t sp = lane_base + Sh::T_SP + 64u * sb + col_off;  // this thread's cells
-      mbar_wait(s_full(sb), (j >> 1) & 1, abort_w, p.status, 0x4500 + j);
+      mbar_wait(s_full(sb), (j / NB) & 1, abort_w, p.status, 0x4500 + j);
       fence_after();
       float sv[32];
       tmem_ld16(sp, sv);
@@ -605,10 +833,10 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
         mx4[i] = fmaxf(mx4[i], sv[i + 28]);
       }
       float mx = fmaxf(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3]) * sl;
-      s_rowmax[sb][kh][t] = mx;
+      s_rowmax[j & 1][kh][t] = mx;
       // the two warps that share these 32 rows (one per key half)
       pair_barrier(warp & 3);
-      mx = fmaxf(mx, s_rowmax[sb][kh ^ 1][t]);
+      mx = fmaxf(mx, s_rowmax[j & 1][kh ^ 1][t]);
       const bool raise = mx > m_ref + kLazy || (m_ref == -CUDART_INF_F && mx != -CUDART_INF_F);
       const float alpha = raise ? fast_exp2(m_ref - mx) : 1.f;  // 0 when m_ref is -inf
       // The context rows of the warp are rescaled together when any of them
@@ -618,9 +846,12 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
       // row, which alpha = 0 keeps.
       if (__any_sync(0xffffffffu, raise && m_ref != -CUDART_INF_F) && j > 0) {
         // the context in tensor memory must hold P_{j-1}.V_{j-1} before it
-        // is rescaled. S_j was committed after P_{j-2}.V_{j-2}, so o_done
-        // has completed j - 1 or j phases here and the parity wait is exact.
-        mbar_wait(o_done, (j - 1) & 1, abort_w, p.status, 0x4600 + j);
+        // is rescaled. That product completes phase (j-1)/NB of buffer
+        // (j-1) % NB's o_done; the phase before belongs to P_{j-1-NB}.V_{j-1-NB},
+        // which completed before S_{j-1} (issued after it, and waited for
+        // above), and no later phase can start before P_{j-1+NB} exists, so
+        // the parity wait is exact.
+        mbar_wait(o_done((j - 1) % NB), ((j - 1) / NB) & 1, abort_w, p.status, 0x4600 + j);
         fence_after();
         // this thread's HDO / 2 context columns (HDO = HD up to head_dim 128)
 #pragma unroll
@@ -698,6 +929,7 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
         }
       }
     }
+   }
   }
   fence_before();
   __syncthreads();
@@ -708,17 +940,16 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
   }
 }
 
-// Two CTAs per SM up to head_dim 64: the warps of a 320-thread CTA fall 3, 3,
-// 2, 2 on the four SM sub-partitions, so two CTAs put 6 warps on one
-// sub-partition, whose 16K registers then allow 85 per thread: the kernel is
-// held to 80. Head_dim 128 runs one CTA per SM (512 tensor-memory columns).
+// One softmax thread per row (head_dim up to 64): 6 warps fall 2, 2, 1, 1 on
+// the four SM sub-partitions, so two CTAs per SM put 4 warps on one, whose 16K
+// registers allow 128 per thread.
 template <int HD, bool GROUPED>
-__global__ void __maxnreg__(80)
-    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_hi,
-                        const __grid_constant__ CUtensorMap tm_lo,
-                        const __grid_constant__ CUtensorMap tm_vhi,
-                        const __grid_constant__ CUtensorMap tm_vlo, const AttentionTcParams p) {
-  attention_tc_body<HD, GROUPED>(tm_hi, tm_lo, tm_vhi, tm_vlo, p);
+__global__ void __maxnreg__(128)
+    attention_tc_row_kernel(const __grid_constant__ CUtensorMap tm_hi,
+                            const __grid_constant__ CUtensorMap tm_lo,
+                            const __grid_constant__ CUtensorMap tm_vhi,
+                            const __grid_constant__ CUtensorMap tm_vlo, const AttentionTcParams p) {
+  attention_tc_body<HD, GROUPED, true>(tm_hi, tm_lo, tm_vhi, tm_vlo, p);
 }
 template <bool GROUPED>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -727,7 +958,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                               const __grid_constant__ CUtensorMap tm_vhi,
                               const __grid_constant__ CUtensorMap tm_vlo,
                               const AttentionTcParams p) {
-  attention_tc_body<128, GROUPED>(tm_hi, tm_lo, tm_vhi, tm_vlo, p);
+  attention_tc_body<128, GROUPED, false>(tm_hi, tm_lo, tm_vhi, tm_vlo, p);
 }
 template <bool GROUPED>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -736,7 +967,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                               const __grid_constant__ CUtensorMap tm_vhi,
                               const __grid_constant__ CUtensorMap tm_vlo,
                               const AttentionTcParams p) {
-  attention_tc_body<256, GROUPED>(tm_hi, tm_lo, tm_vhi, tm_vlo, p);
+  attention_tc_body<256, GROUPED, false>(tm_hi, tm_lo, tm_vhi, tm_vlo, p);
 }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -807,18 +1038,19 @@ int make_vt_map(CUtensorMap *tm, const uint16_t *ptr, int64_t bh, int seq, int s
   return TT_OK;
 }
 
-template <int HD, bool GROUPED>
+template <int HD, bool GROUPED, bool ROW1>
 constexpr auto attention_kernel_for() {
+  static_assert(ROW1 == (HD <= 64), "one thread per row exactly up to head_dim 64");
   if constexpr (HD == 256) return &attention_tc_kernel_hd256<GROUPED>;
   else if constexpr (HD == 128) return &attention_tc_kernel_hd128<GROUPED>;
-  else return &attention_tc_kernel<HD, GROUPED>;
+  else return &attention_tc_row_kernel<HD, GROUPED>;
 }
 
-template <int HD, bool GROUPED>
+template <int HD, bool GROUPED, bool ROW1>
 int launch_hd_as(const AttentionTcParams &p, const CUtensorMap &thi, const CUtensorMap &tlo,
                  const CUtensorMap &tvhi, const CUtensorMap &tvlo, cudaStream_t stream) {
   using Sh = AtShape<HD>;
-  constexpr auto fn = attention_kernel_for<HD, GROUPED>();
+  constexpr auto fn = attention_kernel_for<HD, GROUPED, ROW1>();
   static bool attr_set = false;
   if (!attr_set) {
     TT_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -831,8 +1063,8 @@ int launch_hd_as(const AttentionTcParams &p, const CUtensorMap &thi, const CUten
   const int64_t ctas_x = (int64_t)((p.seq + BQ - 1) / BQ) * p.bh_group * Sh::NSPLIT;
   const int64_t groups = p.batch * p.num_heads / p.bh_group;
   dim3 grid((unsigned)ctas_x, (unsigned)groups);
-  TT_CUDA_TRY(launch_kernel(fn, grid, dim3(kThreads), Sh::SMEM_BYTES, stream, 1, thi, tlo, tvhi,
-                            tvlo, p));
+  TT_CUDA_TRY(launch_kernel(fn, grid, dim3(ROW1 ? kThreadsRow1 : kThreads), Sh::SMEM_BYTES,
+                            stream, 1, thi, tlo, tvhi, tvlo, p));
   TT_LAUNCH_CHECK("attention_tc");
   return TT_OK;
 }
@@ -840,9 +1072,11 @@ int launch_hd_as(const AttentionTcParams &p, const CUtensorMap &thi, const CUten
 template <int HD>
 int launch_hd(const AttentionTcParams &p, const CUtensorMap &thi, const CUtensorMap &tlo,
               const CUtensorMap &tvhi, const CUtensorMap &tvlo, cudaStream_t stream) {
+  // one softmax thread per row up to head_dim 64, two (one per key half) above
+  constexpr bool ROW1 = HD <= 64;
   if (p.bh_group < p.batch * p.num_heads)
-    return launch_hd_as<HD, true>(p, thi, tlo, tvhi, tvlo, stream);
-  return launch_hd_as<HD, false>(p, thi, tlo, tvhi, tvlo, stream);
+    return launch_hd_as<HD, true, ROW1>(p, thi, tlo, tvhi, tvlo, stream);
+  return launch_hd_as<HD, false, ROW1>(p, thi, tlo, tvhi, tvlo, stream);
 }
 
 }  // namespace

@@ -213,6 +213,77 @@ class TTForward:
             _lib.check(rc, "tt_forward", lib)
         return y
 
+    def forward_host(self, x_host: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None,
+                     out: Optional[torch.Tensor] = None, device=None,
+                     slices: Optional[int] = None) -> torch.Tensor:
+        """The forward pass from host buffers to host buffers, with the copies
+        overlapped with the compute: the batch runs as `slices` consecutive
+        slices of whole sequences (sequences are independent); slice i+1's
+        inputs cross to the device on one copy stream while slice i computes on
+        the current stream, and slice i's output crosses back on another
+        while slice i+1 computes. Pinned host buffers make the copies
+        asynchronous (pageable ones still give correct results, without the
+        overlap).
+
+        `x_host` is [B, S, d_model] float32 on the CPU, `valid_token_mask`
+        [B, S] bool on the CPU or None, `out` an optional [B, S, d_model]
+        float32 CPU tensor to write (allocated pinned when omitted). Returns
+        `out`. Like a non_blocking copy, the call returns once the work is
+        enqueued: the current stream of `device` (default: the current CUDA
+        device) has the whole forward and the last copy ordered before
+        anything enqueued on it later, so synchronise that stream before
+        reading `out`."""
+        if x_host.is_cuda:
+            raise ValueError("forward_host takes host buffers; call the module for device tensors")
+        if x_host.dtype != torch.float32 or x_host.dim() != 3:
+            raise ValueError("expected a float32 [B, S, d_model] host tensor")
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else \
+            torch.device(device)
+        b, s, d = x_host.shape
+        if out is None:
+            out = torch.empty((b, s, d), dtype=torch.float32, pin_memory=True)
+        if out.shape != x_host.shape or out.dtype != torch.float32 or out.is_cuda:
+            raise ValueError("out must be a float32 host tensor shaped like x")
+        if b == 0 or s == 0:
+            return out
+        if slices is None:
+            # a few slices when there is enough work per slice to hide a copy
+            slices = 4 if b >= 4 and b * s * d >= (1 << 24) else 1
+        slices = max(1, min(slices, b))
+        cur = torch.cuda.current_stream(dev)
+        if slices == 1:
+            xd = x_host.to(dev, non_blocking=True)
+            md = None if valid_token_mask is None else valid_token_mask.to(dev, non_blocking=True)
+            out.copy_(self.forward(xd, md), non_blocking=True)
+            return out
+        cin = torch.cuda.Stream(dev)
+        cout = torch.cuda.Stream(dev)
+        x_dev = torch.empty((b, s, d), dtype=torch.float32, device=dev)
+        m_dev = (None if valid_token_mask is None else
+                 torch.empty((b, s), dtype=valid_token_mask.dtype, device=dev))
+        cin.wait_stream(cur)   # the buffers come from the current stream's pool
+        cout.wait_stream(cur)
+        bounds = [b * i // slices for i in range(slices + 1)]
+        for i in range(slices):
+            lo, hi = bounds[i], bounds[i + 1]
+            if lo == hi:
+                continue
+            with torch.cuda.stream(cin):
+                x_dev[lo:hi].copy_(x_host[lo:hi], non_blocking=True)
+                if m_dev is not None:
+                    m_dev[lo:hi].copy_(valid_token_mask[lo:hi], non_blocking=True)
+            cur.wait_stream(cin)
+            y = self.forward(x_dev[lo:hi], None if m_dev is None else m_dev[lo:hi])
+            cout.wait_stream(cur)
+            with torch.cuda.stream(cout):
+                out[lo:hi].copy_(y, non_blocking=True)
+            y.record_stream(cout)
+        cur.wait_stream(cout)
+        x_dev.record_stream(cin)
+        if m_dev is not None:
+            m_dev.record_stream(cin)
+        return out
+
     # ---- diagnostics ------------------------------------------------------
     def forward_plan(self, batch: int, seq: int) -> str:
         rc = self._lib.tt_forward_plan(ctypes.byref(self._cfg), batch, seq)
