@@ -580,20 +580,30 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
     const uint32_t lane_base = tm + ((uint32_t)((warp & 3) * 32) << 16);
     {
       // Q row -> tensor memory: HD dims as HD/2 packed cells of Q_hi and of
-      // Q_lo; dims at or past hd (the padding of head_dim 8) are zero
+      // Q_lo; dims at or past hd (the padding of head_dim 8) are zero. Every
+      // global load of the row is issued before the first tensor-memory store
+      // (the stores are ordered against memory), so the row costs one memory
+      // round trip rather than one per 16-byte chunk.
       const int64_t qoff = (b * S + (row_in ? row : 0)) * (int64_t)(2 * D) + (int64_t)h * hd;
       constexpr int QC = HD / 2 < 16 ? HD / 2 : 16;  // cells per store
+      constexpr int NQ = HD / 8;                     // 16-byte chunks of hi (and of lo)
+      uint4 qraw[2][NQ];
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
         const uint4 *src = reinterpret_cast<const uint4 *>((which ? p.qk_lo : p.qk_hi) + qoff);
+#pragma unroll
+        for (int u = 0; u < NQ; ++u)
+          qraw[which][u] = (row_in && 8 * u < hd) ? src[u] : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
         const uint32_t tcol = lane_base + (which ? T_QLO : T_QHI);
 #pragma unroll
         for (int c = 0; c < HD / 2; c += QC) {
           uint32_t qv[QC];
 #pragma unroll
           for (int i = 0; i < QC / 4; ++i) {
-            const int d0 = 2 * c + 8 * i;  // first dim of this 16-byte chunk
-            const uint4 v = (row_in && d0 < hd) ? src[d0 / 8] : make_uint4(0u, 0u, 0u, 0u);
+            const uint4 v = qraw[which][c / 4 + i];  // dims 2c + 8i .. + 7
             qv[4 * i] = v.x; qv[4 * i + 1] = v.y; qv[4 * i + 2] = v.z; qv[4 * i + 3] = v.w;
           }
           if constexpr (QC == 16) tmem_st16(tcol + c, qv);
@@ -755,16 +765,25 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
                            (q_in ? (HD / 2) * kh : 0);
       const uint32_t qcol = (uint32_t)(HD / 4) * kh;
       constexpr int QC = HD / 4 < 16 ? HD / 4 : 16;
+      // every global load of the half row before the first tensor-memory
+      // store (the stores are ordered against memory): one round trip
+      constexpr int NQ = HD / 16;  // 16-byte chunks of hi (and of lo)
+      uint4 qraw[2][NQ];
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
         const uint4 *src = reinterpret_cast<const uint4 *>((which ? p.qk_lo : p.qk_hi) + qoff);
+#pragma unroll
+        for (int u = 0; u < NQ; ++u) qraw[which][u] = q_in ? src[u] : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
         const uint32_t tcol = lane_base + (which ? T_QLO : T_QHI) + qcol;
 #pragma unroll
         for (int c = 0; c < HD / 4; c += QC) {
           uint32_t qv[QC];
 #pragma unroll
           for (int i = 0; i < QC / 4; ++i) {
-            const uint4 v = q_in ? src[c / 4 + i] : make_uint4(0u, 0u, 0u, 0u);
+            const uint4 v = qraw[which][c / 4 + i];
             qv[4 * i] = v.x; qv[4 * i + 1] = v.y; qv[4 * i + 2] = v.z; qv[4 * i + 3] = v.w;
           }
           if constexpr (QC == 16) tmem_st16(tcol + c, qv);

@@ -247,8 +247,10 @@ class TTForward:
         if b == 0 or s == 0:
             return out
         if slices is None:
-            # a few slices when there is enough work per slice to hide a copy
-            slices = 4 if b >= 4 and b * s * d >= (1 << 24) else 1
+            # slices of at least 32768 tokens (smaller ones leave the GPU part
+            # idle in each launch), at most 8: only the first slice's copy in
+            # and the last one's copy out are not hidden
+            slices = min(8, b, max(1, (b * s) // 32768))
         slices = max(1, min(slices, b))
         cur = torch.cuda.current_stream(dev)
         if slices == 1:
