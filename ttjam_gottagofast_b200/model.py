@@ -265,7 +265,7 @@ class TTForward:
                  torch.empty((b, s), dtype=valid_token_mask.dtype, device=dev))
         cin.wait_stream(cur)   # the buffers come from the current stream's pool
         cout.wait_stream(cur)
-        bounds = [b * i // slices for i in range(slices + 1)]
+        bounds = self._slice_bounds(b, slices)
         for i in range(slices):
             lo, hi = bounds[i], bounds[i + 1]
             if lo == hi:
@@ -285,6 +285,18 @@ class TTForward:
         if m_dev is not None:
             m_dev.record_stream(cin)
         return out
+
+    @staticmethod
+    def _slice_bounds(b: int, slices: int):
+        """Sequence boundaries of the slices: with three or more, the first
+        and the last are a quarter of the others (only the first one's copy
+        in and the last one's copy out are not overlapped), the rest equal."""
+        if slices < 3:
+            return [b * i // slices for i in range(slices + 1)]
+        edge = max(1, b // (4 * slices))
+        inner = b - 2 * edge
+        mids = [edge + inner * i // (slices - 2) for i in range(slices - 1)]
+        return [0] + mids + [b]
 
     # ---- diagnostics ------------------------------------------------------
     def forward_plan(self, batch: int, seq: int) -> str:
