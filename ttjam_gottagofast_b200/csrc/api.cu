@@ -354,6 +354,11 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
       return rc;
     live = lv;
   }
+  // the persistent attention's work counter, zeroed by the q|k|v GEMM of each
+  // layer before the attention takes items from it
+  int *attn_counter = W.tc_attention && attention_tc_persistent(hd)
+                          ? reinterpret_cast<int *>(ws + W.attn_counter)
+                          : nullptr;
   const int64_t nst = (T + 255) / 256;
   auto set_live = [&](TcGemmParams &g) {
     if (live == nullptr) return;
@@ -384,6 +389,7 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
       g.H_hi = qk_hi; g.H_lo = qk_lo; g.h_cols = 2 * D;  // the attention reads the fp16 split
       g.vt_hi = vt_hi; g.vt_lo = vt_lo;                  // ... and v transposed
       g.vt_col0 = 2 * D; g.seq = (int)seq; g.seq_pad = W.seq_pad; g.heads = H; g.head_dim = hd;
+      g.zero_word = attn_counter;
     } else {
       g.C = qkv;
     }
@@ -402,7 +408,7 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
       a.qk_hi = qk_hi; a.qk_lo = qk_lo; a.vt_hi = vt_hi; a.vt_lo = vt_lo;
       a.ctx_hi = ctx_hi; a.ctx_lo = ctx_lo; a.mask = mask; a.status = status;
       a.batch = batch; a.seq = (int)seq; a.seq_pad = W.seq_pad; a.d_model = D; a.num_heads = H;
-      a.head_dim = hd; a.causal = cfg.causal; a.scale = scale;
+      a.head_dim = hd; a.causal = cfg.causal; a.scale = scale; a.counter = attn_counter;
       if ((rc = timed_launch(TT_KERNEL_ATTENTION, stream,
                              [&] { return launch_attention_tc(a, stream); })))
         return rc;

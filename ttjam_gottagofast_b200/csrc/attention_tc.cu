@@ -51,6 +51,7 @@
 #include <math_constants.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "attention_tc.cuh"
 
@@ -959,6 +960,494 @@ __device__ __forceinline__ void attention_tc_body(const CUtensorMap &tm_hi,
   }
 }
 
+// ---- persistent form (head_dim up to 64) ------------------------------------
+// One CTA per scheduling slot (two per SM), each running work items (query
+// tile, head, sequence) one after another, taken heaviest first from a
+// counter with atomicAdd; the tensor memory, the barriers and the K/V ring
+// stay with the CTA across items. Roles as in the form above, with one
+// softmax thread per row, plus:
+//   warp 0    (all lanes) takes the next item, scans its sequence's mask for
+//             the valid length, publishes the item's record in one of two
+//             shared slots, then (lane 0) streams the item's K/V tiles into
+//             the ring -- which it keeps doing while the other roles finish
+//             the previous item, so the next item's first tiles are loaded
+//             by the time its scores are issued;
+//   softmax   after an item's last tile (every score of the item read, so
+//             the Q columns are free), loads the next item's Q row and writes
+//             it to tensor memory, then waits for the item's last P.V and
+//             stores the context -- the MMA thread issues the next item's
+//             first scores meanwhile.
+// Ring stages and S/P buffers are indexed by a tile count that runs on across
+// items; q_ready and o_final complete one phase per item that has work. The
+// next item's first P.V overwrites the context only after the softmax has
+// read it: that product waits for P of the item's first tile, which the
+// softmax writes after the context store (program order). Work items are
+// ordered as the grid of the form above: group of bh_group (sequence, head)
+// pairs, then query tile latest first, then pair. The counter must be zero
+// when the kernel starts (the q|k|v GEMM before it zeroes it); CTA c takes
+// item c first, then gridDim.x + the counter's old value.
+// Measured against the one-CTA-per-item form on B200 (forward attention,
+// CUDA events): E (head_dim 64, 16384 items) 2007 -> 1761 us, D 94.7 -> 85.7,
+// C (head_dim 32) 28.1 -> 26.2, official case 13 131.9 -> 114.5. The gain is
+// the per-CTA start-up (barrier set-up, tensor-memory allocation, the mask
+// scan and the first K/V loads) that the next item's hand-off hides.
+template <int HD>
+__device__ __forceinline__ void attention_tc_persist_body(const CUtensorMap &tm_hi,
+                                                          const CUtensorMap &tm_lo,
+                                                          const CUtensorMap &tm_vhi,
+                                                          const CUtensorMap &tm_vlo,
+                                                          const AttentionTcParams &p) {
+  using Sh = AtShape<HD>;
+  static_assert(HD <= 64, "persistent form up to head_dim 64");
+  constexpr uint32_t STAGE = Sh::STAGE, OPK = Sh::OPK, OPV = Sh::OPV;
+  constexpr int STAGES = Sh::NST, HDO = Sh::HDO, NB = Sh::NB;
+  constexpr uint32_t T_QHI = Sh::T_QHI, T_QLO = Sh::T_QLO, T_O = Sh::T_O,
+                     TMEM_COLS = Sh::TMEM_COLS;
+  constexpr int NSOFT = 4;
+  extern __shared__ uint8_t smem_raw[];
+  // item records: valid (1 work, 0 all queries padded, -1 no more items),
+  // sequence, head, first query, kv_len, kv_end, key tiles, mask has holes
+  __shared__ int s_rec[2][8];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t bars = base + STAGES * STAGE;
+  auto kv_full = [&](int s) { return bars + 8u * s; };
+  auto kv_empty = [&](int s) { return bars + 8u * (STAGES + s); };
+  auto s_full = [&](int b) { return bars + 8u * (2 * STAGES + b); };
+  auto p_full = [&](int b) { return bars + 8u * (2 * STAGES + NB + b); };
+  auto o_done = [&](int b) { return bars + 8u * (2 * STAGES + 2 * NB + b); };
+  constexpr uint32_t XB = 2 * STAGES + 3 * NB;
+  const uint32_t q_ready = bars + 8u * XB;
+  const uint32_t o_final = bars + 8u * (XB + 1);
+  auto info_ready = [&](int k) { return bars + 8u * (XB + 2 + k); };  // record k % 2 written
+  auto info_free = [&](int k) { return bars + 8u * (XB + 4 + k); };   // record k % 2 read
+  const uint32_t tmem_slot = bars + 8u * (XB + 6);
+  const uint32_t drain_bar = bars + 8u * (XB + 7);
+  static_assert(8 * (XB + 8) <= 256, "barrier area");
+  uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
+  volatile int *abort_w = reinterpret_cast<volatile int *>(smem_raw + (tmem_slot + 4 - raw));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = p.seq, D = p.d_model, hd = p.head_dim;
+  const int ntq = (S + BQ - 1) / BQ;
+  const int64_t bh_all = p.batch * p.num_heads;
+  const int64_t gsz = p.bh_group;  // pairs per group
+  const int64_t n_items = (int64_t)ntq * bh_all;
+
+  pdl_trigger();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(kv_full(s), 1);
+      mbar_init(kv_empty(s), 1);
+    }
+    for (int b = 0; b < NB; ++b) {
+      mbar_init(s_full(b), 1);
+      mbar_init(p_full(b), NSOFT);
+      mbar_init(o_done(b), 1);
+    }
+    mbar_init(q_ready, NSOFT);
+    mbar_init(o_final, 1);
+    for (int k = 0; k < 2; ++k) {
+      mbar_init(info_ready(k), 1);
+      mbar_init(info_free(k), 1 + NSOFT);  // the MMA thread and the softmax warps
+    }
+    mbar_init(drain_bar, 1);
+    *abort_w = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tm = *tmem_slot_ptr;
+  // q|k, v^T and the zeroed item counter come from the previous kernel: each
+  // role waits for it (griddepcontrol.wait) before its first read of them.
+  // The first item's record needs only the mask, the caller's input, so the
+  // producer publishes it before its wait.
+
+  if (warp == 0) {
+    // ---- items, mask scans and K/V tiles ------------------------------------
+    int it = 0;  // K/V tiles loaded (ring index), over all items
+    bool ok = true;
+    for (int n = 0; ok; ++n) {
+      int item = 0;
+      if (lane == 0) item = n == 0 ? (int)blockIdx.x : atomicAdd(p.counter, 1) + (int)gridDim.x;
+      item = __shfl_sync(0xffffffffu, item, 0);
+      const int slot = n & 1;
+      // record n - 2 (the same slot) has been read by every role
+      if (n >= 2 && !__all_sync(0xffffffffu, mbar_wait(info_free(slot), ((n - 2) >> 1) & 1,
+                                                       abort_w, p.status, 0x4800))) {
+        ok = false;
+        break;
+      }
+      int valid = -1, bb = 0, hh = 0, q0 = 0, kv_len = 0, kv_end = 0, nkv = 0, holes = 0;
+      if (item < n_items) {
+        const int64_t per_group = (int64_t)ntq * gsz;
+        const int64_t grp = item / per_group, r = item % per_group;
+        const int qt = ntq - 1 - (int)(r / gsz);
+        const int64_t bh = grp * gsz + r % gsz;
+        bb = (int)(bh / p.num_heads);
+        hh = (int)(bh % p.num_heads);
+        q0 = qt * BQ;
+        int last = S, hole = S;
+        if (p.mask != nullptr) {
+          const uint8_t *mrow = p.mask + (int64_t)bb * S;
+          last = 0;
+          if ((reinterpret_cast<uintptr_t>(mrow) & 15) == 0 && S % 16 == 0) {
+            for (int j = lane; j < S / 16; j += 32) {
+              const uint4 v = reinterpret_cast<const uint4 *>(mrow)[j];
+              const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                if (w[k]) last = 16 * j + 4 * k + (31 - __clz((int)w[k])) / 8 + 1;
+                const uint32_t z = (w[k] - 0x01010101u) & ~w[k] & 0x80808080u;
+                if (z) hole = min(hole, 16 * j + 4 * k + (__ffs((int)z) - 1) / 8);
+              }
+            }
+          } else {
+            for (int j = lane; j < S; j += 32) {
+              if (mrow[j]) last = j + 1;
+              else hole = min(hole, j);
+            }
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
+            hole = min(hole, __shfl_xor_sync(0xffffffffu, hole, o));
+          }
+        }
+        kv_len = last;
+        holes = hole < kv_len ? 1 : 0;
+        valid = q0 < kv_len ? 1 : 0;  // 0: every query of the tile is padding
+        kv_end = p.causal ? min(kv_len, q0 + BQ) : kv_len;
+        nkv = valid ? (kv_end + BKV - 1) / BKV : 0;
+      }
+      if (lane == 0) {
+        int *rec = s_rec[slot];
+        rec[0] = valid; rec[1] = bb; rec[2] = hh; rec[3] = q0;
+        rec[4] = kv_len; rec[5] = kv_end; rec[6] = nkv; rec[7] = holes;
+        mbar_arrive(info_ready(slot));  // release: the record is visible to its waiters
+      }
+      if (n == 0) pdl_wait();
+      if (valid < 0) break;
+      if (lane == 0) {
+        const int kcol = D + hh * hd;
+        const int bh = bb * p.num_heads + hh;
+        for (int j = 0; j < nkv; ++j, ++it) {
+          const int s = it % STAGES, ph = it / STAGES;
+          if (it >= STAGES &&
+              !mbar_wait(kv_empty(s), (ph - 1) & 1, abort_w, p.status, 0x4100 + (j & 0xff))) {
+            ok = false;
+            break;
+          }
+          const uint32_t st = base + s * STAGE;
+          mbar_expect_tx(kv_full(s), STAGE);
+#pragma unroll
+          for (int part = 0; part < Sh::KSPLIT; ++part) {
+            tma_load_3d(st + part * Sh::KPART, &tm_hi, kcol + part * Sh::KBOX, j * BKV, bb,
+                        kv_full(s));
+            tma_load_3d(st + OPK + part * Sh::KPART, &tm_lo, kcol + part * Sh::KBOX, j * BKV, bb,
+                        kv_full(s));
+          }
+          tma_load_3d(st + 2 * OPK, &tm_vhi, j * BKV, 0, bh, kv_full(s));
+          tma_load_3d(st + 2 * OPK + OPV, &tm_vlo, j * BKV, 0, bh, kv_full(s));
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      it = __shfl_sync(0xffffffffu, it, 0);
+    }
+    // the last phase armed on each stage has landed before the CTA retires
+    if (lane == 0)
+      for (int k = it > STAGES ? it - STAGES : 0; k < it; ++k)
+        mbar_drain(kv_full(k % STAGES), (k / STAGES) & 1, p.status, 0x4F00);
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ---------------------------------------------------------
+    pdl_wait();
+    int g = 0, m = 0;  // tiles consumed over all items; items with work
+    bool ok = true;
+    auto issue_s = [&](int t) -> bool {  // S of tile t (over all items) into buffer t % NB
+      const int s = t % STAGES;
+      if (!mbar_wait(kv_full(s), (t / STAGES) & 1, abort_w, p.status, 0x4200)) return false;
+      const uint32_t kst = base + s * STAGE;
+      const uint32_t sd = tm + Sh::T_SP + 64u * (uint32_t)(t % NB);
+      constexpr int KK_BOX = Sh::KBOX / 16;
+#pragma unroll
+      for (int kk = 0; kk < HD / 16; ++kk) {
+        const uint32_t kpart = kst + (uint32_t)(kk / KK_BOX) * Sh::KPART;
+        const uint64_t khi0 = sdesc(kpart, Sh::K_SBO, Sh::K_SWZ);
+        const uint64_t klo0 = sdesc(kpart + OPK, Sh::K_SBO, Sh::K_SWZ);
+        const uint64_t koff = (uint64_t)(2 * (kk % KK_BOX));
+        mma_ts(sd, tm + T_QHI + 8u * kk, khi0 + koff, Sh::IDESC_S, kk > 0);
+        mma_ts(sd, tm + T_QHI + 8u * kk, klo0 + koff, Sh::IDESC_S, 1);
+        mma_ts(sd, tm + T_QLO + 8u * kk, khi0 + koff, Sh::IDESC_S, 1);
+      }
+      mma_commit(s_full(t % NB));
+      return true;
+    };
+    for (int n = 0; ok; ++n) {
+      const int slot = n & 1;
+      if (!mbar_wait(info_ready(slot), (n >> 1) & 1, abort_w, p.status, 0x4810)) break;
+      const int valid = s_rec[slot][0], nkv = s_rec[slot][6];
+      mbar_arrive(info_free(slot));
+      if (valid < 0) break;
+      if (valid == 0) continue;
+      if (!mbar_wait(q_ready, m & 1, abort_w, p.status, 0x4000)) break;
+      fence_after();
+      for (int j = 0; j < NB && j < nkv; ++j) ok = ok && issue_s(g + j);
+      for (int j = 0; ok && j < nkv; ++j) {
+        const int t = g + j, s = t % STAGES, b = t % NB;
+        if (!mbar_wait(p_full(b), (t / NB) & 1, abort_w, p.status, 0x4400)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const uint32_t vst = base + s * STAGE + 2 * OPK;
+        const uint64_t vhi0 = sdesc(vst, 1024, 2), vlo0 = sdesc(vst + OPV, 1024, 2);
+        const uint32_t pb = tm + Sh::T_SP + 64u * b;
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          const uint64_t voff = (uint64_t)(2 * kk);
+          const uint32_t phi = pb + 32u * (kk >> 1) + 8u * (kk & 1);
+          mma_ts(tm + T_O, phi, vhi0 + voff, Sh::IDESC_PV, (j | kk) != 0);
+          mma_ts(tm + T_O, phi, vlo0 + voff, Sh::IDESC_PV, 1);
+          mma_ts(tm + T_O, phi + 16u, vhi0 + voff, Sh::IDESC_PV, 1);
+        }
+        mma_commit(o_done(b));
+        mma_commit(kv_empty(s));
+        if (j + NB < nkv) ok = issue_s(t + NB);
+      }
+      if (ok) mma_commit(o_final);
+      g += nkv;
+      ++m;
+    }
+    mma_commit(drain_bar);
+    mbar_drain(drain_bar, 0, p.status, 0x4F10);
+  } else if (warp >= kSoftWarp0) {
+    // ---- softmax, one thread per query row (warps 2-5) ----------------------
+    const int t_row = (warp & 3) * 32 + lane;  // row within the tile = tensor-memory lane
+    const uint32_t lane_base = tm + ((uint32_t)((warp & 3) * 32) << 16);
+    const float sl = p.scale * 1.4426950408889634f;
+    constexpr float kLazy = 8.0f;
+    constexpr float kPScale = 7.0f;
+    constexpr int NQ = HD / 8;  // 16-byte chunks of Q_hi (and of Q_lo)
+    constexpr int QC = HD / 2 < 16 ? HD / 2 : 16;
+    int n = 0;  // records read
+    // the next record with work (or the end), read and released
+    auto next_rec = [&](int *rec) -> bool {
+      for (;;) {
+        const int slot = n & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(info_ready(slot), (n >> 1) & 1, abort_w,
+                                               p.status, 0x4820)))
+          return false;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rec[i] = s_rec[slot][i];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(info_free(slot));
+        ++n;
+        if (rec[0] != 0) return rec[0] > 0;
+      }
+    };
+    // Q row of an item -> tensor memory, then q_ready (every global load of
+    // the row is issued before the first store)
+    auto put_q = [&](const int *rec) {
+      uint4 qraw[2][NQ];
+      const int row = rec[3] + t_row;
+      const bool row_in = row < S;
+      const int64_t qoff = ((int64_t)rec[1] * S + (row_in ? row : 0)) * (int64_t)(2 * D) +
+                           (int64_t)rec[2] * hd;
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const uint4 *src = reinterpret_cast<const uint4 *>((which ? p.qk_lo : p.qk_hi) + qoff);
+#pragma unroll
+        for (int u = 0; u < NQ; ++u)
+          qraw[which][u] = (row_in && 8 * u < hd) ? src[u] : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const uint32_t tcol = lane_base + (which ? T_QLO : T_QHI);
+#pragma unroll
+        for (int c = 0; c < HD / 2; c += QC) {
+          uint32_t qv[QC];
+#pragma unroll
+          for (int i = 0; i < QC / 4; ++i) {
+            const uint4 v = qraw[which][c / 4 + i];
+            qv[4 * i] = v.x; qv[4 * i + 1] = v.y; qv[4 * i + 2] = v.z; qv[4 * i + 3] = v.w;
+          }
+          if constexpr (QC == 16) tmem_st16(tcol + c, qv);
+          else if constexpr (QC == 8) tmem_st8(tcol + c, qv);
+          else tmem_st4(tcol + c, qv);
+        }
+      }
+      tmem_wait_st();
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_ready);
+    };
+    int cur[8];
+    bool have = next_rec(cur);
+    pdl_wait();
+    if (have) put_q(cur);
+    int g = 0, m = 0;
+    while (have) {
+      const int bb = cur[1], hh = cur[2], q0 = cur[3], kv_end = cur[5], nkv = cur[6];
+      const uint8_t *mtile = cur[7] ? p.mask + (int64_t)bb * S : nullptr;
+      const int row = q0 + t_row;
+      const bool row_in = row < S;
+      float m_ref = -CUDART_INF_F, l = 0.f;
+      for (int j = 0; j < nkv; ++j) {
+        const int t = g + j, sb = t % NB;
+        const int k0 = j * BKV;
+        uint32_t ok0, ok1;
+        if (mtile == nullptr) {
+          const int nn = kv_end - k0, n1 = nn - 32;
+          ok0 = nn >= 32 ? 0xffffffffu : (nn <= 0 ? 0u : (1u << nn) - 1u);
+          ok1 = n1 >= 32 ? 0xffffffffu : (n1 <= 0 ? 0u : (1u << n1) - 1u);
+        } else {
+          const int ka = k0 + lane, kb2 = k0 + 32 + lane;
+          ok0 = __ballot_sync(0xffffffffu, ka < kv_end && mtile[ka] != 0);
+          ok1 = __ballot_sync(0xffffffffu, kb2 < kv_end && mtile[kb2] != 0);
+        }
+        const bool diag = p.causal && k0 + 63 > q0;
+        const bool open = !diag && (ok0 & ok1) == 0xffffffffu;
+        const uint32_t sp = lane_base + Sh::T_SP + 64u * sb;
+        mbar_wait(s_full(sb), (t / NB) & 1, abort_w, p.status, 0x4500);
+        fence_after();
+        float sv[64];
+        tmem_ld32(sp, sv);
+        tmem_ld32(sp + 32, sv + 32);
+        tmem_wait_ld();
+        if (!open) {
+          uint32_t a0 = ok0, a1 = ok1;
+          if (diag) {
+            const int lim = row - k0, lim1 = lim - 32;
+            a0 &= lim >= 31 ? 0xffffffffu : (lim < 0 ? 0u : (2u << lim) - 1u);
+            a1 &= lim1 >= 31 ? 0xffffffffu : (lim1 < 0 ? 0u : (2u << lim1) - 1u);
+          }
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            sv[c] = (a0 >> c) & 1u ? sv[c] : -CUDART_INF_F;
+            sv[32 + c] = (a1 >> c) & 1u ? sv[32 + c] : -CUDART_INF_F;
+          }
+        }
+        float mx8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          mx8[i] = fmax3(sv[i], sv[i + 8], sv[i + 16]);
+          mx8[i] = fmax3(mx8[i], sv[i + 24], sv[i + 32]);
+          mx8[i] = fmax3(mx8[i], sv[i + 40], sv[i + 48]);
+          mx8[i] = fmaxf(mx8[i], sv[i + 56]);
+        }
+        const float mx = fmaxf(fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]),
+                                     mx8[6]),
+                               mx8[7]) * sl;
+        const bool raise = mx > m_ref + kLazy || (m_ref == -CUDART_INF_F && mx != -CUDART_INF_F);
+        const float alpha = raise ? fast_exp2(m_ref - mx) : 1.f;
+        if (__any_sync(0xffffffffu, raise && m_ref != -CUDART_INF_F) && j > 0) {
+          // P.V of the item's previous tile has landed in the context: phase
+          // (t-1)/NB of buffer (t-1) % NB's o_done, exact as in the form above
+          mbar_wait(o_done((t - 1) % NB), ((t - 1) / NB) & 1, abort_w, p.status, 0x4600);
+          fence_after();
+          constexpr int OC = HDO >= 16 ? 16 : 8;
+#pragma unroll
+          for (int c = 0; c < HDO; c += OC) {
+            float ov[OC];
+            tmem_ld_n<OC>(lane_base + T_O + c, ov);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < OC; ++i) ov[i] *= alpha;
+            if constexpr (OC == 16) tmem_st16_f32(lane_base + T_O + c, ov);
+            else tmem_st8_f32(lane_base + T_O + c, ov);
+          }
+        }
+        if (raise) {
+          l *= alpha;
+          m_ref = mx;
+        }
+        const bool live = m_ref != -CUDART_INF_F;
+        const float noff = kPScale - m_ref;
+        float ps4[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t w[32];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const float e0 = live ? fast_exp2(fmaf(sv[32 * half + 2 * c], sl, noff)) : 0.f;
+            const float e1 = live ? fast_exp2(fmaf(sv[32 * half + 2 * c + 1], sl, noff)) : 0.f;
+            ps4[(2 * c) & 3] += e0;
+            ps4[(2 * c + 1) & 3] += e1;
+            split_pair_nonneg(e0, e1, w[c], w[16 + c]);
+          }
+          tmem_st32(sp + 32u * half, w);
+        }
+        l += (ps4[0] + ps4[1]) + (ps4[2] + ps4[3]);
+        tmem_wait_st();
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full(sb));
+      }
+      // every score of this item has been read (each s_full waited above), so
+      // the next item's Q may replace this one's while the last P.V runs
+      int nxt[8];
+      const bool more = next_rec(nxt);
+      if (more) put_q(nxt);
+      mbar_wait(o_final, m & 1, abort_w, p.status, 0x4700);
+      fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int64_t off = ((int64_t)bb * S + (row_in ? row : 0)) * (int64_t)D + (int64_t)hh * hd;
+      constexpr int OC = HDO >= 32 ? 16 : 8;
+#pragma unroll
+      for (int c = 0; c < HDO; c += OC) {
+        float ov[OC];
+        tmem_ld_n<OC>(lane_base + T_O + c, ov);
+        tmem_wait_ld();
+        if (row_in && c < hd) {
+          uint32_t hw[OC / 2], lw[OC / 2];
+#pragma unroll
+          for (int i = 0; i < OC / 2; ++i)
+            split_pair(ov[2 * i] * inv, ov[2 * i + 1] * inv, hw[i], lw[i]);
+          uint4 *dh = reinterpret_cast<uint4 *>(p.ctx_hi + off + c);
+          uint4 *dl = reinterpret_cast<uint4 *>(p.ctx_lo + off + c);
+#pragma unroll
+          for (int u = 0; u < OC / 8; ++u) {
+            dh[u] = make_uint4(hw[4 * u], hw[4 * u + 1], hw[4 * u + 2], hw[4 * u + 3]);
+            dl[u] = make_uint4(lw[4 * u], lw[4 * u + 1], lw[4 * u + 2], lw[4 * u + 3]);
+          }
+        }
+      }
+      // the context reads complete (tcgen05.wait::ld above) before the arrive
+      // on p_full of the next item's first tile, which the P.V that
+      // overwrites the context waits for
+      g += nkv;
+      ++m;
+      have = more;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) cur[i] = nxt[i];
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+template <int HD>
+__global__ void __maxnreg__(128)
+    attention_tc_persist_kernel(const __grid_constant__ CUtensorMap tm_hi,
+                                const __grid_constant__ CUtensorMap tm_lo,
+                                const __grid_constant__ CUtensorMap tm_vhi,
+                                const __grid_constant__ CUtensorMap tm_vlo,
+                                const AttentionTcParams p) {
+  attention_tc_persist_body<HD>(tm_hi, tm_lo, tm_vhi, tm_vlo, p);
+}
+
 // One softmax thread per row (head_dim up to 64): 6 warps fall 2, 2, 1, 1 on
 // the four SM sub-partitions, so two CTAs per SM put 4 warps on one, whose 16K
 // registers allow 128 per thread.
@@ -1088,9 +1577,68 @@ int launch_hd_as(const AttentionTcParams &p, const CUtensorMap &thi, const CUten
   return TT_OK;
 }
 
+// CTAs of the persistent form that fit on the current device at once, from
+// the SM's shared memory (each CTA also holds 64 static bytes and the
+// per-block reservation): two per SM by design -- 128 registers x 192 threads
+// and 256 tensor-memory columns each leave room for two. (The runtime's
+// occupancy query answers one for this kernel on B200, whose launches run two
+// per SM.)
+template <int HD>
+int persist_slots(int *slots_out) {
+  using Sh = AtShape<HD>;
+  static int slots_dev = -1, slots = 0;
+  int dev = 0;
+  TT_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev != slots_dev) {
+    int smem_sm = 0, reserved = 0, sms = 0;
+    TT_CUDA_TRY(cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev));
+    TT_CUDA_TRY(cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev));
+    TT_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int per_sm = std::min(2, smem_sm / ((int)Sh::SMEM_BYTES + 64 + reserved));
+    if (per_sm <= 0 || sms <= 0)
+      return fail(TT_ERR_CUDA, "attention_tc: the persistent kernel fits no SM");
+    slots = per_sm * sms;
+    slots_dev = dev;
+  }
+  *slots_out = slots;
+  return TT_OK;
+}
+
+// The persistent form: one CTA per slot, each running work items until none
+// are left.
+template <int HD>
+int launch_persist(const AttentionTcParams &p, const CUtensorMap &thi, const CUtensorMap &tlo,
+                   const CUtensorMap &tvhi, const CUtensorMap &tvlo, int slots,
+                   cudaStream_t stream) {
+  using Sh = AtShape<HD>;
+  constexpr auto fn = &attention_tc_persist_kernel<HD>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    TT_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)Sh::SMEM_BYTES));
+    TT_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     (int)cudaSharedmemCarveoutMaxShared));
+    attr_set = true;
+  }
+  TT_CUDA_TRY(launch_kernel(fn, dim3((unsigned)slots), dim3(kThreadsRow1), Sh::SMEM_BYTES,
+                            stream, 1, thi, tlo, tvhi, tvlo, p));
+  TT_LAUNCH_CHECK("attention_tc_persist");
+  return TT_OK;
+}
+
 template <int HD>
 int launch_hd(const AttentionTcParams &p, const CUtensorMap &thi, const CUtensorMap &tlo,
               const CUtensorMap &tvhi, const CUtensorMap &tvlo, cudaStream_t stream) {
+  if constexpr (HD <= 64) {
+    // persistent when the items outnumber the slots (with one item per CTA it
+    // only adds the item hand-off, measured 1 us per launch slower)
+    if (p.counter != nullptr) {
+      int slots = 0, rc;
+      if ((rc = persist_slots<HD>(&slots))) return rc;
+      const int64_t items = (int64_t)((p.seq + BQ - 1) / BQ) * p.batch * p.num_heads;
+      if (items > slots) return launch_persist<HD>(p, thi, tlo, tvhi, tvlo, slots, stream);
+    }
+  }
   // one softmax thread per row up to head_dim 64, two (one per key half) above
   constexpr bool ROW1 = HD <= 64;
   if (p.bh_group < p.batch * p.num_heads)
@@ -1099,6 +1647,15 @@ int launch_hd(const AttentionTcParams &p, const CUtensorMap &thi, const CUtensor
 }
 
 }  // namespace
+
+bool attention_tc_persistent(int head_dim) {
+  // TT_ATTENTION_PERSISTENT=0 selects the one-CTA-per-item form throughout
+  static const bool off = [] {
+    const char *e = std::getenv("TT_ATTENTION_PERSISTENT");
+    return e != nullptr && e[0] == '0';
+  }();
+  return head_dim <= 64 && !off;
+}
 
 bool attention_tc_supported(int head_dim, int d_model) {
   return (head_dim == 8 || head_dim == 16 || head_dim == 32 || head_dim == 64 ||

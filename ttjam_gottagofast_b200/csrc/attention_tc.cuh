@@ -19,7 +19,15 @@ struct AttentionTcParams {
   // set by launch_attention_tc: (sequence, head) pairs per group of the grid
   // order (see the kernel); a divisor of batch * num_heads
   int bh_group;
+  // work-item counter of the persistent form (head_dim up to 64): zero when
+  // the kernel starts (the q|k|v GEMM before it zeroes it), taken with
+  // atomicAdd; null selects the one-CTA-per-item form
+  int *counter;
 };
+
+// Whether launch_attention_tc runs head_dim `hd` on the persistent form,
+// which needs p.counter.
+bool attention_tc_persistent(int head_dim);
 
 bool attention_tc_supported(int head_dim, int d_model);
 int launch_attention_tc(const AttentionTcParams &p, cudaStream_t stream);

@@ -473,6 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot_ptr;
   pdl_wait();  // A (and R) come from the previous kernel, the live-tile list too
+  if (p.zero_word != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *p.zero_word = 0;
   // tiles: the live 128-row tiles (all when there is no list) x NT column tiles
   const int ntiles = (p.live_count128 != nullptr ? *p.live_count128 : MT) * NT;
   auto tile_m0 = [&](int tile) {
@@ -757,6 +758,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot_ptr;
   pdl_wait();  // A (and R) come from the previous kernel, the live-tile list too
+  if (p.zero_word != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *p.zero_word = 0;
   // tiles: the live 256-row tiles (all when there is no list) x NT column tiles
   const int ntiles = (p.live_count256 != nullptr ? *p.live_count256 : MT) * NT;
   auto tile_m = [&](int tile) {  // first row of the pair's 256-row tile
@@ -964,6 +966,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   pdl_wait();  // x (and R) come from the previous kernel
+  if (p.zero_word != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *p.zero_word = 0;
 
   // ---- LayerNorm rows -> fp16 split A tile in shared memory -----------------
   {

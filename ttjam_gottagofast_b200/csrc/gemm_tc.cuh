@@ -47,6 +47,10 @@ struct TcGemmParams {
   // and of 128-row tiles (single-CTA kernel) to compute; the others are
   // skipped. Null: every tile.
   const int *live_count256, *live_list256, *live_count128, *live_list128;
+  // Optional: an int that one thread of the kernel sets to zero once every
+  // kernel before it has finished (after its griddepcontrol.wait) -- the work
+  // counter of the persistent attention that follows the q|k|v projection.
+  int *zero_word;
 };
 
 int launch_gemm_tc3(const TcGemmParams &p, cudaStream_t stream);

@@ -94,6 +94,7 @@ int launch_live_rows(const uint8_t *mask, int64_t batch, int seq, int *ws_ints,
 struct WorkspaceLayout {
   size_t qkv = 0, ctx = 0, h = 0, qk_hi = 0, qk_lo = 0, vt_hi = 0, vt_lo = 0;
   size_t live = 0;  // live-row lists (ints), tensor-core schedule
+  size_t attn_counter = 0;  // work counter of the persistent attention (one int)
   int seq_pad = 0;  // row stride of the transposed value copy (multiple of 4)
   size_t ln_hi = 0, ln_lo = 0, ctx_hi = 0, ctx_lo = 0, h_hi = 0, h_lo = 0;
   size_t total = 0;
@@ -123,6 +124,7 @@ struct WorkspaceLayout {
       seq_pad = (int)((seq + 7) / 8 * 8);
       qk_hi = take(T * D); qk_lo = take(T * D);
       vt_hi = take((size_t)batch * seq_pad * D / 2); vt_lo = take((size_t)batch * seq_pad * D / 2);
+      attn_counter = take(1);
     } else {
       qkv = take(T * 3 * D);
     }
