@@ -9,7 +9,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from ttjam_gottagofast_b200.shard import balanced_assignment, shard_range, sharded_forward
+from ttjam_gottagofast_b200.shard import (balanced_assignment, sequence_cost, shard_range,
+                                          sharded_forward)
 
 
 def test_shard_ranges_cover_batch_exactly():
@@ -41,6 +42,33 @@ def test_balanced_assignment_partitions_and_evens_attention_work():
     cont = [work(range(r * 8, r * 8 + 8)) for r in range(8)]
     assert max(bal) / min(bal) < 1.05
     assert max(bal) <= max(cont)
+
+
+def test_sequence_cost_counts_live_row_tiles():
+    # all rows without row_tile; with it, the 256-row tiles up to the last
+    # valid key rounded up to 64 (1000 -> 1024 -> 4 tiles; 1025 -> 1088 -> 5)
+    assert sequence_cost(1000, 2048, 0.0) == 2048
+    assert sequence_cost(1000, 2048, 0.0, row_tile=256) == 1024
+    assert sequence_cost(1025, 2048, 0.0, row_tile=256) == 1280
+    assert sequence_cost(2048, 2048, 0.0, row_tile=256) == 2048
+    assert sequence_cost(0, 2048, 0.0, row_tile=256) == 0
+    # a tile size that does not divide seq_len falls back to all rows
+    assert sequence_cost(100, 1000, 0.0, row_tile=256) == 1000
+    assert sequence_cost(64, 128, 2.0) == 128 + 2.0 * 64 * 65 / 256
+
+
+def test_balanced_assignment_with_live_rows_evens_estimated_work():
+    g = torch.Generator().manual_seed(11)
+    lengths = torch.randint(1024, 2049, (64,), generator=g).tolist()
+    for world in (2, 4, 8):
+        a = balanced_assignment(lengths, world, 2048, attn_weight=0.72, row_tile=256)
+        assert sorted(i for ix in a for i in ix) == list(range(64))
+        assert [len(ix) for ix in a] == [64 // world] * world
+        load = [sum(sequence_cost(lengths[i], 2048, 0.72, 256) for i in ix) for ix in a]
+        cont = [sum(sequence_cost(lengths[i], 2048, 0.72, 256)
+                    for i in range(r * 64 // world, (r + 1) * 64 // world)) for r in range(world)]
+        assert max(load) <= max(cont)
+        assert max(load) / min(load) < 1.03
 
 
 def _free_port():

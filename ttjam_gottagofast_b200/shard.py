@@ -6,12 +6,14 @@ into whole sequences with replicated weights and no exchange inside the step.
 Two assignments:
 
 * `shard_range`: contiguous slices, sizes differing by at most one;
-* `balanced_assignment`: the same number of sequences per rank (every
-  projection GEMM runs over all batch x seq rows, so its cost per sequence is
-  fixed), chosen so that the attention work -- which grows with the square of
-  each sequence's valid length under the causal and key-padding masks -- is as
-  even as a greedy largest-first placement makes it. The slowest rank sets the
-  step time, so this is what evens the ranks out for random lengths.
+* `balanced_assignment`: the same number of sequences per rank, chosen so
+  that the estimated work -- the projections over each sequence's rows plus
+  the attention, which grows with the square of its valid length under the
+  causal and key-padding masks -- is as even as a greedy largest-first
+  placement makes it. The projections run over all rows, or (with
+  `row_tile`, the tensor-core schedule's dead-row tiling) over the row tiles
+  up to the last valid key rounded up to 64. The slowest rank sets the step
+  time, so this is what evens the ranks out for random lengths.
 
 The only collective is the optional gather of the outputs afterwards
 (`all_gather_into_tensor` over NCCL / NVLink on GPUs, gloo on CPU), which pads
@@ -39,27 +41,34 @@ def shard_range(batch: int, world: int, rank: int) -> Tuple[int, int]:
     return start, count
 
 
-def sequence_cost(length: int, seq_len: int, attn_weight: float = 1.0) -> float:
-    """Relative cost of one sequence: the projections over its seq_len rows
-    (fixed) plus the causal attention over its valid length (length^2 / 2
-    query-key pairs), in units of one row's projection work scaled by
-    attn_weight / seq_len."""
-    return seq_len + attn_weight * length * (length + 1) / (2.0 * max(seq_len, 1))
+def sequence_cost(length: int, seq_len: int, attn_weight: float = 1.0,
+                  row_tile: int = 0) -> float:
+    """Relative cost of one sequence, in units of one row's projection work:
+    the projections over its rows -- all seq_len of them, or with row_tile > 0
+    the tiles of row_tile rows up to its last valid key rounded up to 64 (when
+    row_tile divides seq_len, the tiles of one sequence are its own) -- plus
+    the causal attention over its valid length (length^2 / 2 query-key pairs),
+    each pair weighing attn_weight / seq_len."""
+    rows = seq_len
+    if row_tile > 0 and seq_len % row_tile == 0:
+        live = -(-length // 64) * 64
+        rows = min(seq_len, -(-live // row_tile) * row_tile)
+    return rows + attn_weight * length * (length + 1) / (2.0 * max(seq_len, 1))
 
 
 def balanced_assignment(lengths: Sequence[int], world: int, seq_len: Optional[int] = None,
-                        attn_weight: float = 1.0) -> List[List[int]]:
+                        attn_weight: float = 1.0, row_tile: int = 0) -> List[List[int]]:
     """Sequence indices per rank: as many per rank as `shard_range` gives
-    (sizes differ by at most one), placed largest cost first onto the rank
-    with the least cost so far among those with room; each rank's indices in
-    ascending order. Deterministic: ties go to the lower rank, then the lower
-    index."""
+    (sizes differ by at most one), placed largest `sequence_cost` first onto
+    the rank with the least cost so far among those with room; each rank's
+    indices in ascending order. Deterministic: ties go to the lower rank, then
+    the lower index."""
     if world <= 0:
         raise ValueError("world must be positive")
     n = len(lengths)
     s = int(seq_len if seq_len is not None else (max(lengths) if n else 0))
     caps = [shard_range(n, world, r)[1] for r in range(world)]
-    cost = [sequence_cost(int(l), s, attn_weight) for l in lengths]
+    cost = [sequence_cost(int(l), s, attn_weight, row_tile) for l in lengths]
     order = sorted(range(n), key=lambda i: (-cost[i], i))
     load = [0.0] * world
     out: List[List[int]] = [[] for _ in range(world)]
