@@ -71,6 +71,8 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=10.0)
+    ap.add_argument("--plan", default="auto", choices=("auto", "cluster", "ops_ffma", "ops_tc", "tile"),
+                    help="kernel schedule (the one the library picks by default)")
     ap.add_argument("--batch", type=int, default=0,
                     help="run the workload's shape with this batch instead (a smaller "
                          "case of the same shape, e.g. for a profiler capture)")
@@ -391,6 +393,7 @@ def run_ours(args, world, rank, local):
 
     torch.manual_seed(MODEL_SEED)
     model = UserOptimizedTransformer(cfg).to(dev).eval()
+    model.set_plan(args.plan)
     lib, tcfg = model._lib, model._cfg
     x = x_host.to(dev)
     mask = m_host.to(dev)

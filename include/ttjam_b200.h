@@ -65,7 +65,7 @@ typedef struct tt_config {
   int32_t reserved;    /* must be 0 */
 } tt_config;
 
-/* tt_config.flags: TT_PLAN_AUTO never picks TT_PLAN_OPS_TC. Set it for a model
+/* tt_config.flags: TT_PLAN_AUTO never picks TT_PLAN_OPS_TC or TT_PLAN_TILE. Set it for a model
  * whose tt_fp16_operand_bound is not below TT_FP16_MAX: the split-precision
  * schedule stores activations as fp16 pieces, which cannot hold such values,
  * while the FFMA and cluster schedules compute in fp32 throughout. */
@@ -77,6 +77,9 @@ typedef struct tt_config {
 #define TT_PLAN_CLUSTER 1   /* one launch: thread-block clusters run all layers */
 #define TT_PLAN_OPS_FFMA 2  /* per-op kernels, fp32 FFMA GEMMs */
 #define TT_PLAN_OPS_TC 3    /* per-op kernels, split-precision tcgen05 GEMMs and attention */
+#define TT_PLAN_TILE 4      /* one launch: one CTA per 128 token rows of whole sequences runs
+                               all layers on split-precision tcgen05 MMAs (d_model = ffn_dim =
+                               128, 4 heads, seq a divisor of 128) */
 
 /* One BaselineTransformerBlock's parameters, nn.Linear layout W[out,in]
  * (torch_transformer_benchmark.py:125-132, :72-75). Device pointers, fp32,
@@ -179,8 +182,9 @@ int tt_forward_launch_count(const tt_config *cfg, int64_t batch, int64_t seq);
  * at that moment; make such a first call before any stream capture.
  *
  * It runs the per-op schedule (TT_PLAN_OPS_*; TT_PLAN_AUTO picks the one
- * tt_forward uses when it does not take the single-launch path, and
- * TT_PLAN_CLUSTER, which needs no scratch, is TT_ERR_UNSUPPORTED). A call
+ * tt_forward uses when it does not take a single-launch path, and
+ * TT_PLAN_CLUSTER and TT_PLAN_TILE, which need no scratch, are
+ * TT_ERR_UNSUPPORTED). A call
  * whose scratch (tt_workspace_bytes of that schedule) exceeds the array is
  * rejected with TT_ERR_WORKSPACE and a message giving both sizes.
  *
@@ -212,7 +216,7 @@ int tt_last_error(char *buf, size_t len);
 #define TT_KERNEL_FFN_IN 5        /* LN2 (when fused) + ffn_in + GELU */
 #define TT_KERNEL_FFN_OUT 6       /* ffn_out + residual + padded-row zeroing */
 #define TT_KERNEL_FINAL_NORM 7    /* final LayerNorm + padded-row zeroing */
-#define TT_KERNEL_WHOLE_FORWARD 8 /* the single-launch forward (TT_PLAN_CLUSTER) */
+#define TT_KERNEL_WHOLE_FORWARD 8 /* a single-launch forward (TT_PLAN_CLUSTER, TT_PLAN_TILE) */
 #define TT_KERNEL_ROW_SCAN 9      /* valid lengths and live row tiles of a padded batch */
 
 /* Launch timing probe, a measurement aid with no counterpart in the

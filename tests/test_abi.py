@@ -75,8 +75,9 @@ def test_image_and_workspace_sizes(lib):
     assert 2 * 4 * per_layer < n < 2 * 4 * per_layer + 64 * 1024
     odd = _cfg(d=30, h=3, f=30)   # no split when fp16 rows are not 16-byte multiples
     assert lib.tt_image_bytes(ctypes.byref(odd)) < 2 * 4 * (4 * 30 * 30 + 2 * 30 * 30) * 4
-    ws = lib.tt_workspace_bytes(ctypes.byref(c), 4, 16)
-    assert ws >= 64 * (3 * 128 + 128 + 128) * 4
+    # a per-op schedule (seq 24 does not divide 128, so no single-launch one)
+    ws = lib.tt_workspace_bytes(ctypes.byref(c), 4, 24)
+    assert ws >= 96 * (3 * 128 + 128 + 128) * 4
     assert lib.tt_image_bytes(ctypes.byref(_cfg(h=3))) == 0
 
 
@@ -84,8 +85,9 @@ def test_forward_argument_errors_need_no_gpu(lib):
     c = _cfg()
     rc = lib.tt_forward(ctypes.byref(c), None, None, None, 4, 16, None, None, 0, None)
     assert rc == _lib.TT_ERR_INVALID_ARGUMENT
-    # sizes are checked before anything is launched
-    rc = lib.tt_forward(ctypes.byref(c), 256, 512, None, 4, 16, 1024, 2048, 16, None)
+    # sizes are checked before anything is launched (a per-op schedule: seq 24
+    # does not divide 128)
+    rc = lib.tt_forward(ctypes.byref(c), 256, 512, None, 4, 24, 1024, 2048, 16, None)
     assert rc == _lib.TT_ERR_WORKSPACE
     assert "workspace" in _lib.last_error(lib)
     rc = lib.tt_forward(ctypes.byref(c), 256, 512, None, -1, 16, 1024, 2048, 16, None)
@@ -127,6 +129,39 @@ def test_fp32_only_flag_keeps_auto_plan_off_the_split_schedule(lib):
     # a forced split schedule stays forced
     d_cfg.plan = _lib.PLAN_IDS["ops_tc"]
     assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(d_cfg), 16, 1024)] == "ops_tc"
+
+
+def test_tile_plan_takes_batches_of_short_sequences_of_the_d128_model(lib):
+    # d_model = ffn_dim = 128, 4 heads, seq dividing 128, at least 2048 rows
+    # (official case 1: batch 64 x 128)
+    a = _cfg()
+    assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(a), 64, 128)] == "tile"
+    assert lib.tt_forward_launch_count(ctypes.byref(a), 64, 128) == 1
+    assert lib.tt_workspace_bytes(ctypes.byref(a), 64, 128) == 0
+    # (seq 128: never the cluster schedule, which takes short sequences on a GPU)
+    for b, s in ((16, 128), (10000, 128)):
+        assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(a), b, s)] == "tile"
+    # fewer rows (config A: batch 8 x 128), seq not a divisor of 128, or
+    # another head count: the per-op schedule
+    assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(a), 8, 128)] == "ops_tc"
+    assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(a), 32, 512)] == "ops_tc"
+    assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(a), 100, 24)] == "ops_tc"
+    h2 = _cfg(h=2)
+    assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(h2), 64, 128)] == "ops_tc"
+    # fp16 pieces: never under TT_FLAG_FP32_ONLY unless forced; forced, any
+    # number of rows
+    a.flags = _lib.TT_FLAG_FP32_ONLY
+    assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(a), 64, 128)] == "ops_ffma"
+    a.plan = _lib.PLAN_IDS["tile"]
+    assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(a), 8, 128)] == "tile"
+    assert lib.tt_forward_launch_count(ctypes.byref(a), 8, 128) == 1
+    assert lib.tt_forward_plan(ctypes.byref(a), 32, 512) == _lib.TT_ERR_UNSUPPORTED
+    assert lib.tt_forward_plan(ctypes.byref(h2), 64, 128) > 0
+    h2.plan = _lib.PLAN_IDS["tile"]
+    assert lib.tt_forward_plan(ctypes.byref(h2), 64, 128) == _lib.TT_ERR_UNSUPPORTED
+    bad = _cfg()
+    bad.plan = 5
+    assert lib.tt_validate_config(ctypes.byref(bad)) == _lib.TT_ERR_INVALID_CONFIG
 
 
 def test_fp16_operand_bound_argument_errors_need_no_gpu(lib):

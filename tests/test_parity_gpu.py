@@ -52,7 +52,7 @@ def applicable_plans(model, b, s):
     import ctypes
     from ttjam_gottagofast_b200 import _lib
     out = []
-    for name in ("cluster", "ops_ffma", "ops_tc"):
+    for name in ("cluster", "ops_ffma", "ops_tc", "tile"):
         cfg = _lib.make_config(model.config, name)
         if model._lib.tt_forward_plan(ctypes.byref(cfg), b, s) > 0:
             out.append(name)
@@ -109,14 +109,85 @@ def _full_size_case(name, variant):
 
 
 def test_small_shapes_run_in_one_launch():
-    """The launch-bound workloads take the single-launch cluster schedule."""
+    """The launch-bound workloads take a single-launch schedule: the cluster
+    forward for B1 and B2, the tile forward for the reference's official case
+    1 (batch 64 x 128 of the d128 model)."""
     import ctypes
-    for name in ("B1", "B2"):
-        cfg = WORKLOADS[name].config
+    from ttjam_gottagofast_b200.config import OFFICIAL
+    for w, plan in ((WORKLOADS["B1"], "cluster"), (WORKLOADS["B2"], "cluster"),
+                    (OFFICIAL["case1"], "tile")):
+        cfg = w.config
         model, _ = model_for(cfg)
-        assert model.forward_plan(cfg.batch_size, cfg.seq_len) == "cluster"
+        assert model.forward_plan(cfg.batch_size, cfg.seq_len) == plan
         assert model._lib.tt_forward_launch_count(ctypes.byref(model._cfg), cfg.batch_size,
                                                   cfg.seq_len) == 1
+
+
+# Shapes of the tile forward the goldens do not reach: masks with holes,
+# non-causal sequences longer than one token, a partial last tile (rows not a
+# multiple of 128), one layer, and each input scale of the harness.
+TILE_CASES = [
+    # batch, seq, causal, layers, padding ratio, input scale, holes
+    (3, 32, 1, 2, 0.5, 1.0, True),
+    (3, 64, 0, 2, 0.5, 1.0, False),
+    (5, 16, 0, 1, 0.0, 1.0, True),
+    (3, 128, 1, 1, 0.4, 8.0, False),
+    (7, 64, 1, 3, 0.3, 0.05, False),
+    (2, 2, 1, 2, 0.0, 1.0, False),
+    (33, 128, 1, 4, 0.5, 1.0, True),
+]
+
+
+@pytest.mark.parametrize("variant", HARNESS_VARIANTS, ids=[v["name"] for v in HARNESS_VARIANTS])
+def test_tile_forward_workload_A_variants(variant):
+    """Workload A (batch 8 x 128, which the default picks the per-op schedule
+    for) forced onto the tile forward, at each harness input variant."""
+    w = WORKLOADS["A"]
+    cfg = w.config
+    model, params = model_for(cfg)
+    x, mask = generate_random_case(cfg, "cpu", torch.float32, variant.get("seed", 101234),
+                                   variant.get("padding_ratio", w.padding_ratio),
+                                   variant.get("input_scale", w.input_scale))
+    x, mask = x.to(DEV), mask.to(DEV)
+    model.set_plan("tile")
+    try:
+        with torch.inference_mode():
+            y = model(x, mask)
+    finally:
+        model.set_plan("auto")
+    ref = oracle.forward(params, cfg, x, mask)
+    check(ref, y, f"A[tile]/{variant['name']}")
+    assert (y[~mask] == 0).all()
+    assert model.read_device_status() == (0, 0)
+
+
+@pytest.mark.parametrize("case", TILE_CASES, ids=[f"b{c[0]}_s{c[1]}_c{c[2]}_l{c[3]}"
+                                                  f"_x{c[5]}{'_holes' if c[6] else ''}"
+                                                  for c in TILE_CASES])
+def test_tile_forward_matches_oracle(case):
+    from ttjam_gottagofast_b200.config import TransformerConfig
+    b, s, causal, layers, pad, scale, holes = case
+    cfg = TransformerConfig(b, s, 128, 4, 128, layers, bool(causal))
+    model, params = model_for(cfg, seed=777)
+    x, mask = generate_random_case(cfg, "cpu", torch.float32, 4242 + b * s, pad, scale)
+    if holes:
+        g = torch.Generator().manual_seed(b * 1000 + s)
+        mask = mask & (torch.rand(b, s, generator=g) > 0.25)
+        mask[:, 0] = True
+    x, mask = x.to(DEV), mask.to(DEV)
+    model.set_plan("tile")
+    try:
+        assert model.forward_plan(b, s) == "tile"
+        with torch.inference_mode():
+            y = model(x, mask)
+            y2 = model(x, mask)
+    finally:
+        model.set_plan("auto")
+    ref = oracle.forward(params, cfg, x, mask)
+    check(ref, y, f"tile b{b} s{s} causal{causal} L{layers} x{scale}")
+    assert (y[~mask] == 0).all(), "padded rows must be exactly zero"
+    assert torch.equal(y, y2), "the tile forward is deterministic"
+    assert model.read_device_status() == (0, 0)
 
 
 SMALL_WORKLOAD_CASES = [(n, v) for n in ("A", "B1", "B2", "C")

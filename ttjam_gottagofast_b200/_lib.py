@@ -32,7 +32,7 @@ TT_FP16_MAX = 65504.0
 # Size of the library's fixed scratch array behind tt_forward_noalloc.
 TT_NOALLOC_SCRATCH_BYTES = 16 << 20
 
-PLAN_NAMES = {1: "cluster", 2: "ops_ffma", 3: "ops_tc"}
+PLAN_NAMES = {1: "cluster", 2: "ops_ffma", 3: "ops_tc", 4: "tile"}
 PLAN_IDS = {"auto": 0, **{v: k for k, v in PLAN_NAMES.items()}}
 
 # Every entry point include/ttjam_b200.h declares.

@@ -21,7 +21,8 @@ LIB_NAME = "libttjam_b200.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
 
 SOURCES = ["api.cu", "layernorm.cu", "gemm_ffma.cu", "attention_ffma.cu", "cluster_forward.cu",
-           "gemm_tc.cu", "attention_tc.cu", "noalloc.cu", "graph_cache.cu", "live_rows.cu"]
+           "gemm_tc.cu", "attention_tc.cu", "noalloc.cu", "graph_cache.cu", "live_rows.cu",
+           "tile_forward.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

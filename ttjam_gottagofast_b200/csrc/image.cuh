@@ -26,7 +26,7 @@
 
 namespace tt {
 
-enum ForwardPlan : int { PLAN_CLUSTER = 1, PLAN_OPS_FFMA = 2, PLAN_OPS_TC = 3 };
+enum ForwardPlan : int { PLAN_CLUSTER = 1, PLAN_OPS_FFMA = 2, PLAN_OPS_TC = 3, PLAN_TILE = 4 };
 
 // Shapes the split-precision tensor-core schedule can run: every GEMM operand
 // row (fp16) must be a whole number of 16-byte TMA units (d_model and ffn_dim

@@ -78,10 +78,10 @@ extern "C" int tt_forward_noalloc(const tt_config *cfg, const void *image, const
   if (((reinterpret_cast<uintptr_t>(image) | reinterpret_cast<uintptr_t>(x) |
         reinterpret_cast<uintptr_t>(y)) & 15) != 0)
     return fail(TT_ERR_INVALID_ARGUMENT, "tt_forward_noalloc: pointers must be 16-byte aligned");
-  if (cfg->plan == TT_PLAN_CLUSTER)
+  if (cfg->plan == TT_PLAN_CLUSTER || cfg->plan == TT_PLAN_TILE)
     return fail(TT_ERR_UNSUPPORTED,
-                "tt_forward_noalloc runs the per-op schedule; TT_PLAN_CLUSTER needs no scratch "
-                "and is served by tt_forward");
+                "tt_forward_noalloc runs the per-op schedule; TT_PLAN_CLUSTER and TT_PLAN_TILE "
+                "need no scratch and are served by tt_forward");
   if (seq > (int64_t)INT32_MAX || batch > ((int64_t)1 << 40) / seq)
     return fail(TT_ERR_UNSUPPORTED, "tt_forward_noalloc: batch*seq too large");
   // the per-op schedule this call runs: forced by cfg->plan, else the one
