@@ -214,7 +214,7 @@ def kind_work(kind, cfg, b, s, lens, mask_bytes):
     if kind in ("layernorm", "final_norm"):
         return 0.0, 4 * 2 * t * d
     if kind == "row_scan":
-        return 0.0, mask_bytes + 4 * (b + t // 128 + t // 256)
+        return 0.0, mask_bytes + 4 * (b + t // 128 + 1)
     return None  # whole_forward: the caller uses the forward's totals
 
 

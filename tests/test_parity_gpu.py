@@ -256,7 +256,7 @@ def _lengths_mask(b, s, lengths):
 @pytest.mark.parametrize("seq,kind", [(300, "prefix"), (512, "prefix"), (1000, "prefix"),
                                       (512, "holes"), (384, "none")])
 def test_dead_row_tiles_are_skipped_safely(seq, kind):
-    """GEMM-heavy shapes skip the 256-row tiles of the batch that hold only
+    """GEMM-heavy shapes skip the 128-row tiles of the batch that hold only
     rows past each sequence's last valid key (rounded up to 64). Sequence
     lengths here include 0 (all padding), 1, odd lengths and full ones; a
     sequence length that is not a multiple of 64 or 256 puts sequence
@@ -288,6 +288,35 @@ def test_dead_row_tiles_are_skipped_safely(seq, kind):
         assert torch.isfinite(y).all()
         if mask is not None:
             assert (y[~mask] == 0).all()
+    assert model.read_device_status() == (0, 0)
+
+
+@pytest.mark.parametrize("seq", [512, 200])
+def test_dead_row_tiles_on_the_cta_pair_gemm(seq):
+    """A batch large enough for the CTA-pair GEMM, whose two CTAs take two
+    live 128-row tiles of the list (adjacent or not): random lengths from 0 to
+    seq, so live tiles come in odd numbers and one CTA of the last pair gets
+    rows past the matrix."""
+    from ttjam_gottagofast_b200.config import TransformerConfig
+    b = 96 if seq == 200 else 48
+    cfg = TransformerConfig(batch_size=b, seq_len=seq, d_model=256, num_heads=4, ffn_dim=512,
+                            num_layers=2, causal=True)
+    model, params = model_for(cfg, seed=78)
+    g = torch.Generator().manual_seed(1000 + seq)
+    x = torch.randn(b, seq, 256, generator=g)
+    lengths = torch.randint(0, seq + 1, (b,), generator=g).tolist()
+    lengths[0], lengths[1] = 0, seq
+    mask = _lengths_mask(b, seq, lengths)
+    x = x.masked_fill(~mask[..., None], 0).to(DEV)
+    mask = mask.to(DEV)
+    with torch.inference_mode():
+        y = model(x, mask)
+    picks = [0, 1, 2, b // 2, b - 1]
+    idx = torch.tensor(picks, device=DEV)
+    ref = oracle.forward(params, cfg, x[idx], mask[idx])
+    check(ref, y[idx], f"dead rows on the pair GEMM s{seq}/seqs{picks}")
+    assert torch.isfinite(y).all()
+    assert (y[~mask] == 0).all()
     assert model.read_device_status() == (0, 0)
 
 

@@ -400,13 +400,10 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
   int *attn_counter = W.tc_attention && attention_tc_persistent(hd)
                           ? reinterpret_cast<int *>(ws + W.attn_counter)
                           : nullptr;
-  const int64_t nst = (T + 255) / 256;
   auto set_live = [&](TcGemmParams &g) {
     if (live == nullptr) return;
-    g.live_count256 = live;
-    g.live_count128 = live + 1;
-    g.live_list256 = live + 2;
-    g.live_list128 = live + 2 + nst;
+    g.live_count128 = live;
+    g.live_list128 = live + 1;
   };
   for (int l = 0; l < cfg.num_layers; ++l) {
     const LayerOffsets &o = L.layer[l];

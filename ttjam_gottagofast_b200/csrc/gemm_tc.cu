@@ -726,7 +726,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t peer = rank ^ 1u;
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int KB = (p.K + BK - 1) / BK;
-  const int MT = (p.M + 255) / 256, NT = (p.N + PBN - 1) / PBN;
+  const int NT = (p.N + PBN - 1) / PBN;
   pdl_trigger();
   if (threadIdx.x == 32) {
     prefetch_tmap(&tm_a_hi); prefetch_tmap(&tm_a_lo); prefetch_tmap(&tm_w_hi);
@@ -759,11 +759,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot_ptr;
   pdl_wait();  // A (and R) come from the previous kernel, the live-tile list too
   if (p.zero_word != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *p.zero_word = 0;
-  // tiles: the live 256-row tiles (all when there is no list) x NT column tiles
-  const int ntiles = (p.live_count256 != nullptr ? *p.live_count256 : MT) * NT;
-  auto tile_m = [&](int tile) {  // first row of the pair's 256-row tile
-    const int i = tile / NT;
-    return (p.live_list256 != nullptr ? p.live_list256[i] : i) * 256;
+  // tiles: pairs of live 128-row tiles (all when there is no list), CTA r of
+  // the pair taking the pair's r-th, x NT column tiles. A pair without a
+  // second tile (an odd count) gives CTA 1 rows past the matrix: its A loads
+  // read the zero fill and its epilogue stores nothing.
+  const int n128 = p.live_count128 != nullptr ? *p.live_count128 : (p.M + 127) / 128;
+  const int ntiles = (n128 + 1) / 2 * NT;
+  const int m_past = (p.M + 127) / 128 * 128;
+  auto tile_m = [&](int tile) {  // first row of this CTA's 128-row tile
+    const int i = 2 * (tile / NT) + (int)rank;
+    if (i >= n128) return m_past;
+    return (p.live_list128 != nullptr ? p.live_list128[i] : i) * 128;
   };
   const uint32_t full0 = map_to_cta(full_bar(0), 0);  // CTA 0's full barriers (cluster addresses)
 
@@ -771,7 +777,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- TMA producer (both CTAs): this CTA's A rows and W half ------------
     int it = 0;
     for (int tile = pair; tile < ntiles; tile += npairs) {
-      const int m0 = tile_m(tile) + 128 * (int)rank;
+      const int m0 = tile_m(tile);
       const int n0 = (tile % NT) * PBN + (PBN / 2) * (int)rank;
       for (int kb = 0; kb < KB; ++kb, ++it) {
         const int s = it % PSTAGES, n = it / PSTAGES;
@@ -834,7 +840,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int local = 0;
     for (int tile = pair; tile < ntiles; tile += npairs, ++local) {
       const int ab = local & 1;
-      const int m0 = tile_m(tile) + 128 * (int)rank, n0 = (tile % NT) * PBN;
+      const int m0 = tile_m(tile), n0 = (tile % NT) * PBN;
       BiasRegs bias;
       load_bias_regs(p, n0 + c_lo, c_hi - c_lo, lane, bias);
       mbar_wait(acc_full(ab), (local >> 1) & 1, abort_w, p.status, 0x3000);

@@ -43,10 +43,10 @@ struct TcGemmParams {
   int wait_budget_log2;
   int test_skip_first_load;
   // Live row tiles (live_rows.cu), written by an earlier kernel of the
-  // forward: the count and ascending list of 256-row tiles (CTA-pair kernel)
-  // and of 128-row tiles (single-CTA kernel) to compute; the others are
+  // forward: the count and ascending list of the 128-row tiles to compute (the
+  // CTA-pair kernel gives its two CTAs consecutive entries); the others are
   // skipped. Null: every tile.
-  const int *live_count256, *live_list256, *live_count128, *live_list128;
+  const int *live_count128, *live_list128;
   // Optional: an int that one thread of the kernel sets to zero once every
   // kernel before it has finished (after its griddepcontrol.wait) -- the work
   // counter of the persistent attention that follows the q|k|v projection.

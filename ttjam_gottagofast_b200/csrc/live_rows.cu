@@ -10,19 +10,17 @@
 // valid key, so value rows up to that tile's end must be finite (they meet
 // probability 0, and 0 times a stale NaN would not be 0). So a row is dead
 // when its position in its sequence is at or past the last valid key rounded
-// up to a multiple of 64; a 256-row tile of the batch (a super-tile) is dead
-// when all its rows are. Every GEMM of the forward skips the dead super-tiles
-// (the CTA-pair kernel's 256-row tiles are the super-tiles, the single-CTA
-// kernel takes the two 128-row halves of each live one), so every row of a
-// live super-tile is written by every GEMM and no computed tile reads a row of
-// a dead one.
+// up to a multiple of 64; a 128-row tile of the batch is dead when all its
+// rows are. Every GEMM of the forward skips the dead tiles (the single-CTA
+// kernel takes one live tile per CTA, the CTA-pair kernel two consecutive
+// entries of the list, adjacent or not), so every row of a live tile is
+// written by every GEMM and no computed tile reads a row of a dead one.
 //
 // One launch, one CTA of 1024 threads: each warp finds the valid length of
 // its sequences (the last non-zero mask byte, 16-byte loads), then the CTA
-// lists the live super-tiles in order with a block-wide prefix count.
-// Output (ints): [0] live super-tiles, [1] live 128-row tiles, [2 ..] the
-// super-tile list, then the 128-row tile list; per-sequence lengths go to
-// `kvlen`. HBM traffic is the mask (B x S bytes) plus a few KB.
+// lists the live tiles in order with a block-wide prefix count.
+// Output (ints): [0] live 128-row tiles, [1 ..] their list; per-sequence
+// lengths go to `kvlen`. HBM traffic is the mask (B x S bytes) plus a few KB.
 #include "image.cuh"
 #include "tt_common.cuh"
 
@@ -67,18 +65,17 @@ __global__ void __launch_bounds__(kScanThreads) live_rows_kernel(const uint8_t *
     if (lane == 0) kvlen[b] = last;
   }
   __syncthreads();  // kvlen (global, written by this CTA) visible to the CTA
-  // ---- live super-tiles, listed in order ---------------------------------------
+  // ---- live 128-row tiles, listed in order --------------------------------------
   __shared__ int warp_count[kWarps];
   const int64_t rows = batch * (int64_t)seq;
-  const int64_t nst = (rows + 255) / 256, nmt = (rows + 127) / 128;
-  int *list256 = out + 2;
-  int *list128 = out + 2 + nst;
+  const int64_t nmt = (rows + 127) / 128;
+  int *list = out + 1;
   int base = 0;
-  for (int64_t s0 = 0; s0 < nst; s0 += kScanThreads) {
+  for (int64_t s0 = 0; s0 < nmt; s0 += kScanThreads) {
     const int64_t s = s0 + tid;
     bool live = false;
-    if (s < nst) {
-      const int64_t r0 = 256 * s, r1 = min(r0 + 256, rows);
+    if (s < nmt) {
+      const int64_t r0 = 128 * s, r1 = min(r0 + 128, rows);
       for (int64_t b = r0 / seq; !live && b * seq < r1; ++b) {
         const int64_t lo = max(r0, b * seq) - b * seq;
         const int lim = min(seq, (kvlen[b] + 63) / 64 * 64);
@@ -93,36 +90,25 @@ __global__ void __launch_bounds__(kScanThreads) live_rows_kernel(const uint8_t *
       before += w < warp ? warp_count[w] : 0;
       sum += warp_count[w];
     }
-    if (live) {
-      const int k = base + before + __popc(bal & ((1u << lane) - 1u));
-      list256[k] = (int)s;
-      list128[2 * k] = (int)(2 * s);
-      if (2 * s + 1 < nmt) list128[2 * k + 1] = (int)(2 * s + 1);
-    }
+    if (live) list[base + before + __popc(bal & ((1u << lane) - 1u))] = (int)s;
     base += sum;
     __syncthreads();  // warp_count is reused by the next chunk
   }
-  if (tid == 0) {
-    // only the last super-tile can hold a single 128-row tile, and it is the
-    // last one listed when live
-    const bool odd_tail = (nmt & 1) != 0 && base > 0 && list256[base - 1] == (int)(nst - 1);
-    out[0] = base;
-    out[1] = 2 * base - (odd_tail ? 1 : 0);
-  }
+  if (tid == 0) out[0] = base;
 }
 
 }  // namespace
 
 size_t live_rows_ints(int64_t batch, int64_t seq) {
   const int64_t rows = batch * seq;
-  return (size_t)(2 + (rows + 255) / 256 + (rows + 127) / 128 + batch);
+  return (size_t)(1 + (rows + 127) / 128 + batch);
 }
 
 int launch_live_rows(const uint8_t *mask, int64_t batch, int seq, int *ws_ints,
                      cudaStream_t stream) {
   const int64_t rows = batch * (int64_t)seq;
   int *out = ws_ints;
-  int *kvlen = ws_ints + 2 + (rows + 255) / 256 + (rows + 127) / 128;
+  int *kvlen = ws_ints + 1 + (rows + 127) / 128;
   TT_CUDA_TRY(launch_kernel(live_rows_kernel, dim3(1), dim3(kScanThreads), 0, stream, 1, mask,
                             batch, seq, kvlen, out));
   TT_LAUNCH_CHECK("live_rows");
