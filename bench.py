@@ -143,12 +143,12 @@ def rank_sequences(w, mask, world, rank):
     from ttjam_gottagofast_b200.shard import balanced_assignment
     b = w.config.batch_size
     if w.name == "E" and world > 1:
-        # E's projections skip dead 256-row tiles; one query-key pair of its
-        # attention costs 0.72 / 2048 of a row's projections (per layer on
-        # B200: attention 1761 us over 8.7e7 causal pairs, the four
-        # projections 6454 us over 1.11e5 live rows)
+        # E's projections skip dead 128-row tiles; one query-key pair of its
+        # attention costs 0.70 / 2048 of a row's projections (per layer on
+        # B200: attention 1719 us over 8.7e7 causal pairs, the four
+        # projections 6228 us over 1.075e5 live rows)
         ix = balanced_assignment(mask.sum(1).tolist(), world, w.config.seq_len,
-                                 attn_weight=0.72, row_tile=256)[rank]
+                                 attn_weight=0.70, row_tile=128)[rank]
         return ix, "strong"
     return list(range(b)), ("strong" if w.name == "E" else "weak")
 
