@@ -400,6 +400,9 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
   int *attn_counter = W.tc_attention && attention_tc_persistent(hd)
                           ? reinterpret_cast<int *>(ws + W.attn_counter)
                           : nullptr;
+  // per-tile flags for the LayerNorms ahead of the GEMMs (the final one still
+  // writes every row: it zeroes the padded rows of y)
+  const int *live_tiles = live != nullptr ? live_rows_flags(live, batch, seq) : nullptr;
   auto set_live = [&](TcGemmParams &g) {
     if (live == nullptr) return;
     g.live_count128 = live;
@@ -415,7 +418,7 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
     if (!fuse_ln &&
         (rc = timed_launch(TT_KERNEL_LAYERNORM, stream, [&] {
            return launch_layernorm(xin, nullptr, ln_hi, ln_lo, P(o.ln1_w), P(o.ln1_b), nullptr,
-                                   0, T, D, eps, stream);
+                                   0, T, D, eps, stream, live_tiles);
          })))
       return rc;
     TcGemmParams g{};
@@ -470,7 +473,7 @@ int forward_ops_tc(const tt_config &cfg, const ImageLayout &L, const char *image
     if (!fuse_ln &&
         (rc = timed_launch(TT_KERNEL_LAYERNORM, stream, [&] {
            return launch_layernorm(y, nullptr, ln_hi, ln_lo, P(o.ln2_w), P(o.ln2_b), nullptr, 0,
-                                   T, D, eps, stream);
+                                   T, D, eps, stream, live_tiles);
          })))
       return rc;
     TcGemmParams g1{};

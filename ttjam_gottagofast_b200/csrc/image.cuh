@@ -88,6 +88,8 @@ struct ImageLayout {
 
 // Live-row lists of a padded batch (live_rows.cu): ints in the workspace.
 size_t live_rows_ints(int64_t batch, int64_t seq);
+// The per-tile live flags inside the list that launch_live_rows writes.
+const int *live_rows_flags(const int *ws_ints, int64_t batch, int64_t seq);
 int launch_live_rows(const uint8_t *mask, int64_t batch, int seq, int *ws_ints,
                      cudaStream_t stream);
 

@@ -20,12 +20,16 @@ template <int NV>
 __global__ void __launch_bounds__(256) layernorm_vec_kernel(
     const float *__restrict__ x, float *__restrict__ y, uint16_t *__restrict__ y_hi,
     uint16_t *__restrict__ y_lo, const float *__restrict__ gamma, const float *__restrict__ beta,
-    const uint8_t *__restrict__ row_mask, int zero_masked_rows, int64_t rows, int d, float eps) {
+    const uint8_t *__restrict__ row_mask, int zero_masked_rows, int64_t rows, int d, float eps,
+    const int *__restrict__ live_tile) {
   pdl_trigger();
   pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
+  // rows of a dead 128-row tile: their outputs feed only GEMM tiles that are
+  // skipped (a block's 8 rows lie in one tile)
+  if (live_tile != nullptr && live_tile[row >> 7] == 0) return;
   const int d4 = d >> 2;
   const float4 *xr = reinterpret_cast<const float4 *>(x + row * d);
   float4 v[NV];
@@ -119,7 +123,7 @@ __global__ void __launch_bounds__(256) layernorm_generic_kernel(
 
 int launch_layernorm(const float *x, float *y, uint16_t *y_hi, uint16_t *y_lo, const float *gamma,
                      const float *beta, const uint8_t *row_mask, int zero_masked_rows,
-                     int64_t rows, int d, float eps, cudaStream_t stream) {
+                     int64_t rows, int d, float eps, cudaStream_t stream, const int *live_tile) {
   if (rows <= 0) return TT_OK;
   const int threads = 256, rows_per_block = threads / 32;
   const int64_t blocks = ceil_div(rows, rows_per_block);
@@ -133,7 +137,7 @@ int launch_layernorm(const float *x, float *y, uint16_t *y_hi, uint16_t *y_lo, c
 #define TT_LN_CASE(NV)                                                                     \
   TT_CUDA_TRY(launch_kernel(layernorm_vec_kernel<NV>, dim3((unsigned)blocks), dim3(threads), 0, \
                             stream, 1, x, y, y_hi, y_lo, gamma, beta, row_mask,             \
-                            zero_masked_rows, rows, d, eps))
+                            zero_masked_rows, rows, d, eps, live_tile))
     if (nv == 1) TT_LN_CASE(1);
     else if (nv == 2) TT_LN_CASE(2);
     else if (nv <= 4) TT_LN_CASE(4);

@@ -19,8 +19,10 @@
 // One launch, one CTA of 1024 threads: each warp finds the valid length of
 // its sequences (the last non-zero mask byte, 16-byte loads), then the CTA
 // lists the live tiles in order with a block-wide prefix count.
-// Output (ints): [0] live 128-row tiles, [1 ..] their list; per-sequence
-// lengths go to `kvlen`. HBM traffic is the mask (B x S bytes) plus a few KB.
+// Output (ints): [0] live 128-row tiles, [1 ..] their list; then the
+// per-sequence lengths (`kvlen`) and one flag per 128-row tile (1 live, 0
+// dead; the LayerNorms ahead of the GEMMs skip dead tiles with it). HBM
+// traffic is the mask (B x S bytes) plus a few KB.
 #include "image.cuh"
 #include "tt_common.cuh"
 
@@ -32,6 +34,7 @@ constexpr int kScanThreads = 1024;
 __global__ void __launch_bounds__(kScanThreads) live_rows_kernel(const uint8_t *__restrict__ mask,
                                                                  int64_t batch, int seq,
                                                                  int *__restrict__ kvlen,
+                                                                 int *__restrict__ flags,
                                                                  int *__restrict__ out) {
   pdl_trigger();
   pdl_wait();  // the previous forward on this stream may still read the lists
@@ -82,6 +85,7 @@ __global__ void __launch_bounds__(kScanThreads) live_rows_kernel(const uint8_t *
         live = lo < lim;
       }
     }
+    if (s < nmt) flags[s] = live ? 1 : 0;
     const uint32_t bal = __ballot_sync(0xffffffffu, live);
     if (lane == 0) warp_count[warp] = __popc(bal);
     __syncthreads();
@@ -101,7 +105,11 @@ __global__ void __launch_bounds__(kScanThreads) live_rows_kernel(const uint8_t *
 
 size_t live_rows_ints(int64_t batch, int64_t seq) {
   const int64_t rows = batch * seq;
-  return (size_t)(1 + (rows + 127) / 128 + batch);
+  return (size_t)(1 + 2 * ((rows + 127) / 128) + batch);
+}
+
+const int *live_rows_flags(const int *ws_ints, int64_t batch, int64_t seq) {
+  return ws_ints + 1 + (batch * seq + 127) / 128 + batch;
 }
 
 int launch_live_rows(const uint8_t *mask, int64_t batch, int seq, int *ws_ints,
@@ -109,8 +117,9 @@ int launch_live_rows(const uint8_t *mask, int64_t batch, int seq, int *ws_ints,
   const int64_t rows = batch * (int64_t)seq;
   int *out = ws_ints;
   int *kvlen = ws_ints + 1 + (rows + 127) / 128;
+  int *flags = kvlen + batch;
   TT_CUDA_TRY(launch_kernel(live_rows_kernel, dim3(1), dim3(kScanThreads), 0, stream, 1, mask,
-                            batch, seq, kvlen, out));
+                            batch, seq, kvlen, flags, out));
   TT_LAUNCH_CHECK("live_rows");
   return TT_OK;
 }

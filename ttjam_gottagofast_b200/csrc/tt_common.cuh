@@ -146,10 +146,12 @@ __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a -
 // Row LayerNorm, nn.LayerNorm(D) semantics (eps, biased variance). If
 // `zero_rows_mask` is set, rows whose mask byte is 0 are written as 0.
 // If y_hi/y_lo are given, also writes the fp16 split of the output (y may then
-// be null).
+// be null). With live_tile (one int per 128-row tile, 0 = dead), the rows of
+// dead tiles may be left unwritten.
 int launch_layernorm(const float *x, float *y, uint16_t *y_hi, uint16_t *y_lo, const float *gamma,
                      const float *beta, const uint8_t *row_mask, int zero_masked_rows,
-                     int64_t rows, int d, float eps, cudaStream_t stream);
+                     int64_t rows, int d, float eps, cudaStream_t stream,
+                     const int *live_tile = nullptr);
 
 enum GemmEpilogue : int {
   EPI_BIAS = 0,             // C = A W^T + b
