@@ -176,8 +176,12 @@ def test_launch_count_includes_the_row_scan_of_gemm_heavy_shapes(lib):
     e = _cfg(d=1024, h=16, f=4096, l=12)
     # 7 launches per layer, the final LayerNorm, and the live-row scan
     assert lib.tt_forward_launch_count(ctypes.byref(e), 64, 2048) == 7 * 12 + 1 + 1
+    # fewer than 1024 rows: no scan
     small = _cfg(d=1024, h=16, f=4096, l=12)
     assert lib.tt_forward_launch_count(ctypes.byref(small), 1, 512) == 7 * 12 + 1
+    # the d128 model: its GEMMs are latency-bound, no scan (workload C; workload
+    # A, whose LayerNorm-prologue GEMMs take 5 launches per layer)
     d128 = _cfg()
     d128.plan = _lib.PLAN_IDS["ops_tc"]
     assert lib.tt_forward_launch_count(ctypes.byref(d128), 32, 512) == 7 * 4 + 1
+    assert lib.tt_forward_launch_count(ctypes.byref(d128), 8, 128) == 5 * 4 + 1

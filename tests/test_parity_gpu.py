@@ -518,8 +518,12 @@ def test_launch_probe_brackets_every_launch(name, plan):
                  "ops_tc": (["qkv", "attention", "out_proj", "ffn_in", "ffn_out"] if fused else
                             ["layernorm", "qkv", "attention", "out_proj", "layernorm",
                              "ffn_in", "ffn_out"])}[plan]
+    # tensor-core shapes with d_model >= 256 and at least 1024 rows start with
+    # the live-row scan
+    scan = (["row_scan"] if plan == "ops_tc" and cfg.d_model >= 256 and
+            cfg.batch_size * cfg.seq_len >= 1024 else [])
     one = (["whole_forward"] if plan == "cluster"
-           else per_layer * cfg.num_layers + ["final_norm"])
+           else scan + per_layer * cfg.num_layers + ["final_norm"])
     assert names == one * 2
     assert all(t > 0 for t in ms)
 
