@@ -159,6 +159,38 @@ int tt_forward_plan(const tt_config *cfg, int64_t batch, int64_t seq);
  * sees per forward). Negative on error. */
 int tt_forward_launch_count(const tt_config *cfg, int64_t batch, int64_t seq);
 
+/* Element types of the typed entry points below. */
+#define TT_DTYPE_F32 0   /* float32: the typed calls are then tt_pack_image / tt_forward */
+#define TT_DTYPE_F16 1   /* IEEE binary16 (torch.float16) */
+#define TT_DTYPE_BF16 2  /* bfloat16 (torch.bfloat16) */
+
+/* tt_pack_image for a model whose parameters are stored in `dtype`. The
+ * reference benchmarks float16 and bfloat16 by moving the whole model and its
+ * input to that type (torch_transformer_benchmark.py:225-231, :698-699).
+ * Every pointer in `layers` and the two final-norm pointers address elements
+ * of `dtype` (cast to the struct's pointer type), at any alignment. Each value
+ * widens exactly to fp32, and the image is the one tt_pack_image makes from
+ * those fp32 values: a 16-bit model runs the same fp32-accurate schedules. */
+int tt_pack_image_typed(const tt_config *cfg, int dtype, const tt_layer_params *layers,
+                        const void *final_norm_weight, const void *final_norm_bias,
+                        void *image, size_t image_bytes, void *stream);
+
+/* Bytes of scratch tt_forward_typed needs for one [batch, seq] call:
+ * tt_workspace_bytes plus, for a 16-bit dtype, fp32 copies of x and y. */
+size_t tt_typed_workspace_bytes(const tt_config *cfg, int dtype, int64_t batch, int64_t seq);
+
+/* tt_forward with x and y of element type `dtype` (the reference's forward of
+ * a float16 or bfloat16 model, torch_transformer_benchmark.py:698-699, :185-199).
+ * For TT_DTYPE_F16 and TT_DTYPE_BF16 it widens x exactly to fp32 (one
+ * kernel), runs tt_forward's schedule on it, and rounds the fp32 output to
+ * nearest even in `dtype` (one kernel): two launches more than tt_forward
+ * (TT_KERNEL_CONVERT). So y is the fp32-accurate forward of the 16-bit model
+ * rounded once; the reference's own 16-bit forward rounds after every
+ * operation and lands farther from that value. x and y are 16-byte aligned. */
+int tt_forward_typed(const tt_config *cfg, const void *image, int dtype, const void *x,
+                     const uint8_t *mask, int64_t batch, int64_t seq, void *y,
+                     void *workspace, size_t workspace_bytes, void *stream);
+
 /* Bytes of the device scratch array behind tt_forward_noalloc. */
 #define TT_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
 
@@ -218,6 +250,7 @@ int tt_last_error(char *buf, size_t len);
 #define TT_KERNEL_FINAL_NORM 7    /* final LayerNorm + padded-row zeroing */
 #define TT_KERNEL_WHOLE_FORWARD 8 /* a single-launch forward (TT_PLAN_CLUSTER, TT_PLAN_TILE) */
 #define TT_KERNEL_ROW_SCAN 9      /* valid lengths and live row tiles of a padded batch */
+#define TT_KERNEL_CONVERT 10      /* 16-bit x widened to fp32, or fp32 y rounded to 16 bits */
 
 /* Launch timing probe, a measurement aid with no counterpart in the
  * reference. tt_launch_probe_start(capacity) creates 2 * capacity timing

@@ -59,6 +59,32 @@ GOLDENS = load_goldens()
 GOLDEN_IDS = [g.name for g in GOLDENS]
 
 
+class GoldenCase16(GoldenCase):
+    """A 16-bit golden: x and the reference's 16-bit output `y` (as float32,
+    exact), and `y_f32`, the reference module's fp32 forward of the same
+    16-bit weights and input (make_golden_16bit.py)."""
+
+    def __init__(self, meta, arrays):
+        super().__init__(meta, arrays)
+        self.y_f32 = arrays[self.name + "/y_f32"]
+
+    @property
+    def dtype(self):
+        import torch
+        return getattr(torch, self.meta["dtype"])
+
+
+def load_goldens_16bit():
+    with open(os.path.join(GOLDEN_DIR, "manifest_16bit.json")) as fh:
+        manifest = json.load(fh)
+    arrays = np.load(os.path.join(GOLDEN_DIR, "goldens_16bit.npz"))
+    return [GoldenCase16(m, arrays) for m in manifest["cases"]]
+
+
+GOLDENS_16BIT = load_goldens_16bit()
+GOLDEN_16BIT_IDS = [g.name for g in GOLDENS_16BIT]
+
+
 @pytest.fixture(scope="session")
 def goldens():
     return GOLDENS

@@ -39,10 +39,18 @@ def test_every_declared_symbol_is_exported(lib):
         assert hasattr(lib, name), name
 
 
-def _cfg(d=128, h=4, f=128, l=4, causal=1):
+def _cfg(d=128, h=4, f=128, l=4, causal=1, plan="auto"):
     c = _lib.TTConfig()
     c.d_model, c.num_heads, c.ffn_dim, c.num_layers, c.causal = d, h, f, l, causal
+    c.plan = _lib.PLAN_IDS[plan]
     return c
+
+
+def _ops_cfg():
+    """The d128 model forced onto a per-op schedule: its calls check their
+    workspace before anything is launched, with or without a GPU (the automatic
+    plan may pick a single-launch schedule, which takes no workspace)."""
+    return _cfg(plan="ops_ffma")
 
 
 def test_validate_config_codes(lib):
@@ -75,18 +83,16 @@ def test_image_and_workspace_sizes(lib):
     assert 2 * 4 * per_layer < n < 2 * 4 * per_layer + 64 * 1024
     odd = _cfg(d=30, h=3, f=30)   # no split when fp16 rows are not 16-byte multiples
     assert lib.tt_image_bytes(ctypes.byref(odd)) < 2 * 4 * (4 * 30 * 30 + 2 * 30 * 30) * 4
-    # a per-op schedule (seq 24 does not divide 128, so no single-launch one)
-    ws = lib.tt_workspace_bytes(ctypes.byref(c), 4, 24)
+    ws = lib.tt_workspace_bytes(ctypes.byref(_ops_cfg()), 4, 24)
     assert ws >= 96 * (3 * 128 + 128 + 128) * 4
     assert lib.tt_image_bytes(ctypes.byref(_cfg(h=3))) == 0
 
 
 def test_forward_argument_errors_need_no_gpu(lib):
-    c = _cfg()
+    c = _ops_cfg()
     rc = lib.tt_forward(ctypes.byref(c), None, None, None, 4, 16, None, None, 0, None)
     assert rc == _lib.TT_ERR_INVALID_ARGUMENT
-    # sizes are checked before anything is launched (a per-op schedule: seq 24
-    # does not divide 128)
+    # sizes are checked before anything is launched
     rc = lib.tt_forward(ctypes.byref(c), 256, 512, None, 4, 24, 1024, 2048, 16, None)
     assert rc == _lib.TT_ERR_WORKSPACE
     assert "workspace" in _lib.last_error(lib)
@@ -185,3 +191,38 @@ def test_launch_count_includes_the_row_scan_of_gemm_heavy_shapes(lib):
     d128.plan = _lib.PLAN_IDS["ops_tc"]
     assert lib.tt_forward_launch_count(ctypes.byref(d128), 32, 512) == 7 * 4 + 1
     assert lib.tt_forward_launch_count(ctypes.byref(d128), 8, 128) == 5 * 4 + 1
+
+
+def test_typed_entry_points_need_no_gpu_for_their_checks(lib):
+    """The 16-bit entry points: workspace sizes (fp32 copies of x and y ahead
+    of the schedule's own scratch) and argument checks before any launch."""
+    c = _ops_cfg()
+    b, s = 4, 24
+    base = lib.tt_workspace_bytes(ctypes.byref(c), b, s)
+    assert lib.tt_typed_workspace_bytes(ctypes.byref(c), _lib.TT_DTYPE_F32, b, s) == base
+    io = (b * s * 128 * 4 + 255) // 256 * 256
+    for dt in (_lib.TT_DTYPE_F16, _lib.TT_DTYPE_BF16):
+        assert lib.tt_typed_workspace_bytes(ctypes.byref(c), dt, b, s) == 2 * io + base
+    assert lib.tt_typed_workspace_bytes(ctypes.byref(c), 7, b, s) == 0
+    # whatever the schedule (a single-launch one needs no scratch of its own),
+    # the fp32 copies come first
+    assert lib.tt_typed_workspace_bytes(ctypes.byref(c), _lib.TT_DTYPE_BF16, 4, 16) == \
+        2 * ((4 * 16 * 128 * 4 + 255) // 256 * 256) + lib.tt_workspace_bytes(ctypes.byref(c), 4, 16)
+    rc = lib.tt_forward_typed(ctypes.byref(c), 256, 7, 512, None, b, s, 1024, 2048, 1 << 30, None)
+    assert rc == _lib.TT_ERR_INVALID_ARGUMENT and "dtype" in _lib.last_error(lib)
+    rc = lib.tt_forward_typed(ctypes.byref(c), 256, _lib.TT_DTYPE_F16, 512, None, b, s, 1024,
+                              2048, 16, None)
+    assert rc == _lib.TT_ERR_WORKSPACE and "tt_typed_workspace_bytes" in _lib.last_error(lib)
+    rc = lib.tt_forward_typed(ctypes.byref(c), 256, _lib.TT_DTYPE_BF16, 512, None, b, s, 1024,
+                              None, 1 << 30, None)
+    assert rc == _lib.TT_ERR_INVALID_ARGUMENT
+    rc = lib.tt_forward_typed(ctypes.byref(c), 256, _lib.TT_DTYPE_BF16, 520, None, b, s, 1024,
+                              2048, 1 << 30, None)
+    assert rc == _lib.TT_ERR_INVALID_ARGUMENT and "aligned" in _lib.last_error(lib)
+    assert lib.tt_forward_typed(ctypes.byref(c), None, _lib.TT_DTYPE_F16, None, None, 0, s,
+                                None, None, 0, None) == 0
+    rc = lib.tt_pack_image_typed(ctypes.byref(c), 5, None, None, None, None, 0, None)
+    assert rc == _lib.TT_ERR_INVALID_ARGUMENT and "dtype" in _lib.last_error(lib)
+    rc = lib.tt_pack_image_typed(ctypes.byref(c), _lib.TT_DTYPE_BF16, None, None, None, None, 0,
+                                 None)
+    assert rc == _lib.TT_ERR_INVALID_ARGUMENT

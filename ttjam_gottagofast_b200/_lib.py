@@ -41,11 +41,18 @@ EXPORTED = (
     "tt_workspace_bytes", "tt_forward", "tt_forward_plan", "tt_forward_launch_count",
     "tt_read_status", "tt_last_error", "tt_forward_noalloc", "tt_fp16_operand_bound",
     "tt_launch_probe_start", "tt_launch_probe_read", "tt_test_arm_wait_timeout",
+    "tt_pack_image_typed", "tt_typed_workspace_bytes", "tt_forward_typed",
 )
+
+# Element types of the typed entry points (TT_DTYPE_*), by torch dtype name.
+TT_DTYPE_F32 = 0
+TT_DTYPE_F16 = 1
+TT_DTYPE_BF16 = 2
+DTYPE_CODES = {"float32": TT_DTYPE_F32, "float16": TT_DTYPE_F16, "bfloat16": TT_DTYPE_BF16}
 
 # TT_KERNEL_* launch kinds reported by tt_launch_probe_read.
 KERNEL_KINDS = {1: "layernorm", 2: "qkv", 3: "attention", 4: "out_proj", 5: "ffn_in",
-                6: "ffn_out", 7: "final_norm", 8: "whole_forward", 9: "row_scan"}
+                6: "ffn_out", 7: "final_norm", 8: "whole_forward", 9: "row_scan", 10: "convert"}
 
 
 class TTConfig(ctypes.Structure):
@@ -93,6 +100,13 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         lib.tt_image_bytes.argtypes = [cfgp]
         lib.tt_pack_image.restype = ctypes.c_int
         lib.tt_pack_image.argtypes = [cfgp, ctypes.POINTER(TTLayerParams), vp, vp, vp, sz, vp]
+        lib.tt_pack_image_typed.restype = ctypes.c_int
+        lib.tt_pack_image_typed.argtypes = [cfgp, ctypes.c_int, ctypes.POINTER(TTLayerParams),
+                                            vp, vp, vp, sz, vp]
+        lib.tt_typed_workspace_bytes.restype = sz
+        lib.tt_typed_workspace_bytes.argtypes = [cfgp, ctypes.c_int, i64, i64]
+        lib.tt_forward_typed.restype = ctypes.c_int
+        lib.tt_forward_typed.argtypes = [cfgp, vp, ctypes.c_int, vp, vp, i64, i64, vp, vp, sz, vp]
         lib.tt_workspace_bytes.restype = sz
         lib.tt_workspace_bytes.argtypes = [cfgp, i64, i64]
         lib.tt_forward.restype = ctypes.c_int

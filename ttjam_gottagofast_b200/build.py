@@ -22,7 +22,7 @@ LIB_PATH = os.path.join(HERE, LIB_NAME)
 
 SOURCES = ["api.cu", "layernorm.cu", "gemm_ffma.cu", "attention_ffma.cu", "cluster_forward.cu",
            "gemm_tc.cu", "attention_tc.cu", "noalloc.cu", "graph_cache.cu", "live_rows.cu",
-           "tile_forward.cu"]
+           "tile_forward.cu", "typed_io.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

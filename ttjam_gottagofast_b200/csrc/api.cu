@@ -529,8 +529,17 @@ size_t tt_image_bytes(const tt_config *cfg) {
 int tt_pack_image(const tt_config *cfg, const tt_layer_params *layers,
                   const float *final_norm_weight, const float *final_norm_bias, void *image,
                   size_t image_bytes, void *stream_) {
+  return tt_pack_image_typed(cfg, TT_DTYPE_F32, layers, final_norm_weight, final_norm_bias,
+                             image, image_bytes, stream_);
+}
+
+int tt_pack_image_typed(const tt_config *cfg, int dtype, const tt_layer_params *layers,
+                        const void *final_norm_weight, const void *final_norm_bias, void *image,
+                        size_t image_bytes, void *stream_) {
   int rc = validate_config(cfg);
   if (rc != TT_OK) return rc;
+  if (dtype != TT_DTYPE_F32 && dtype != TT_DTYPE_F16 && dtype != TT_DTYPE_BF16)
+    return fail(TT_ERR_INVALID_ARGUMENT, "tt_pack_image: dtype must be a TT_DTYPE_* value");
   if (layers == nullptr || final_norm_weight == nullptr || final_norm_bias == nullptr ||
       image == nullptr)
     return fail(TT_ERR_INVALID_ARGUMENT, "tt_pack_image: NULL pointer argument");
@@ -541,8 +550,11 @@ int tt_pack_image(const tt_config *cfg, const tt_layer_params *layers,
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   char *img = static_cast<char *>(image);
   const size_t D = cfg->d_model, F = cfg->ffn_dim, f4 = sizeof(float);
-  auto copy = [&](size_t off, const float *src, size_t n) -> int {
+  // fp32 parameters are copied; 16-bit ones widen exactly to fp32
+  auto copy = [&](size_t off, const void *src, size_t n) -> int {
     if (src == nullptr) return fail(TT_ERR_INVALID_ARGUMENT, "tt_pack_image: NULL parameter");
+    if (dtype != TT_DTYPE_F32)
+      return launch_widen(dtype, src, reinterpret_cast<float *>(img + off), (int64_t)n, stream);
     TT_CUDA_TRY(cudaMemcpyAsync(img + off, src, n * f4, cudaMemcpyDeviceToDevice, stream));
     return TT_OK;
   };
@@ -679,6 +691,53 @@ int tt_forward(const tt_config *cfg, const void *image, const float *x, const ui
         return plan == PLAN_OPS_TC ? forward_ops_tc(c, L, img, x, mask, batch, seq, y, W, ws, s)
                                    : forward_ops(c, L, img, x, mask, batch, seq, y, W, ws, s);
       });
+}
+
+size_t tt_typed_workspace_bytes(const tt_config *cfg, int dtype, int64_t batch, int64_t seq) {
+  if (validate_config(cfg) != TT_OK || batch < 0 || seq < 0) return 0;
+  if (dtype == TT_DTYPE_F32) return tt_workspace_bytes(cfg, batch, seq);
+  if (dtype != TT_DTYPE_F16 && dtype != TT_DTYPE_BF16) return 0;
+  const size_t io = align_up((size_t)batch * (size_t)seq * (size_t)cfg->d_model * sizeof(float), 256);
+  return 2 * io + tt_workspace_bytes(cfg, batch, seq);
+}
+
+int tt_forward_typed(const tt_config *cfg, const void *image, int dtype, const void *x,
+                     const uint8_t *mask, int64_t batch, int64_t seq, void *y, void *workspace,
+                     size_t workspace_bytes, void *stream_) {
+  if (dtype == TT_DTYPE_F32)
+    return tt_forward(cfg, image, static_cast<const float *>(x), mask, batch, seq,
+                      static_cast<float *>(y), workspace, workspace_bytes, stream_);
+  int rc = validate_config(cfg);
+  if (rc != TT_OK) return rc;
+  if (dtype != TT_DTYPE_F16 && dtype != TT_DTYPE_BF16)
+    return fail(TT_ERR_INVALID_ARGUMENT, "tt_forward_typed: dtype must be a TT_DTYPE_* value");
+  if (batch < 0 || seq < 0) return fail(TT_ERR_INVALID_ARGUMENT, "batch and seq must be >= 0");
+  if (batch == 0 || seq == 0) return TT_OK;
+  if (image == nullptr || x == nullptr || y == nullptr || workspace == nullptr)
+    return fail(TT_ERR_INVALID_ARGUMENT, "tt_forward_typed: NULL image, x, y or workspace");
+  if (x == y) return fail(TT_ERR_INVALID_ARGUMENT, "tt_forward_typed: y may not alias x");
+  if (misaligned(x) || misaligned(y) || misaligned(workspace))
+    return fail(TT_ERR_INVALID_ARGUMENT, "tt_forward_typed: pointers must be 16-byte aligned");
+  if (seq > (int64_t)INT32_MAX || batch * seq > ((int64_t)1 << 40))
+    return fail(TT_ERR_UNSUPPORTED, "tt_forward_typed: batch*seq too large");
+  const size_t need = tt_typed_workspace_bytes(cfg, dtype, batch, seq);
+  if (workspace_bytes < need)
+    return fail(TT_ERR_WORKSPACE, "tt_forward_typed: workspace smaller than "
+                                  "tt_typed_workspace_bytes (" + std::to_string(need) + " bytes)");
+  const int64_t n = batch * seq * (int64_t)cfg->d_model;
+  const size_t io = align_up((size_t)n * sizeof(float), 256);
+  char *ws = static_cast<char *>(workspace);
+  float *x32 = reinterpret_cast<float *>(ws);
+  float *y32 = reinterpret_cast<float *>(ws + io);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if ((rc = timed_launch(TT_KERNEL_CONVERT, stream,
+                         [&] { return launch_widen(dtype, x, x32, n, stream); })))
+    return rc;
+  if ((rc = tt_forward(cfg, image, x32, mask, batch, seq, y32, ws + 2 * io,
+                       workspace_bytes - 2 * io, stream_)))
+    return rc;
+  return timed_launch(TT_KERNEL_CONVERT, stream,
+                      [&] { return launch_narrow(dtype, y32, y, n, stream); });
 }
 
 int tt_read_status(const tt_config *cfg, const void *image, int32_t *code, int32_t *detail,

@@ -192,4 +192,9 @@ struct AttentionParams {
 // Flash-style causal / key-padded attention with fp32 online softmax.
 int launch_attention_ffma(const AttentionParams &p, cudaStream_t stream);
 
+// Widening of `n` elements of TT_DTYPE_F16 / TT_DTYPE_BF16 to fp32, and the
+// rounding (to nearest even) of fp32 to them (typed_io.cu). Any alignment.
+int launch_widen(int dtype, const void *src, float *dst, int64_t n, cudaStream_t stream);
+int launch_narrow(int dtype, const float *src, void *dst, int64_t n, cudaStream_t stream);
+
 }  // namespace tt

@@ -24,7 +24,13 @@ write through `.data`, or replacing a Parameter object, is invisible to those
 counters: call `invalidate()` after one. The output and the scratch come from
 PyTorch's caching allocator, and the kernels run on
 `torch.cuda.current_stream()` without a host sync. There is no CPU path: a CPU
-or non-fp32 input raises.
+input raises.
+
+Parameters and inputs may be float32, float16 or bfloat16 (the reference's
+`--dtype`, :225-231, moves model and input to one of them). The parameters
+share one dtype; the input's may differ; the output has the input's dtype.
+16-bit values widen exactly to fp32 and every schedule computes in fp32
+accuracy; a 16-bit output is that result rounded once to nearest even.
 """
 from __future__ import annotations
 
@@ -128,10 +134,17 @@ class TTForward:
             return image
         self._plist = None
         key = self._param_key()
+        # float32, float16 or bfloat16 parameters, all of one dtype (the
+        # reference's --dtype moves the whole model, :698-699); 16-bit ones
+        # widen exactly to fp32 as they are packed
+        pdtype = next(self.parameters()).dtype
         for name, p in self.named_parameters():
-            if p.device != device or p.dtype != torch.float32 or not p.is_contiguous():
-                raise ValueError(f"parameter {name} must be a contiguous float32 tensor "
-                                 f"on {device} (got {p.dtype} on {p.device})")
+            if (p.device != device or p.dtype != pdtype or not p.is_contiguous()
+                    or str(p.dtype).split(".")[-1] not in _lib.DTYPE_CODES):
+                raise ValueError(f"parameter {name} must be a contiguous float32, float16 or "
+                                 f"bfloat16 tensor on {device}, all parameters of one dtype "
+                                 f"(got {p.dtype} on {p.device}; the first is {pdtype})")
+        dcode = _lib.DTYPE_CODES[str(pdtype).split(".")[-1]]
         lib = self._lib
         pcfg = _lib.make_config(self.config)
         nbytes = lib.tt_image_bytes(ctypes.byref(pcfg))
@@ -151,9 +164,10 @@ class TTForward:
             for field, t in ptrs.items():
                 setattr(arr[i], field, t.data_ptr())
         stream = torch.cuda.current_stream(device).cuda_stream
-        _lib.check(lib.tt_pack_image(ctypes.byref(pcfg), arr, self.final_norm.weight.data_ptr(),
-                                     self.final_norm.bias.data_ptr(), image.data_ptr(),
-                                     nbytes, stream), "tt_pack_image", lib)
+        _lib.check(lib.tt_pack_image_typed(ctypes.byref(pcfg), dcode, arr,
+                                           self.final_norm.weight.data_ptr(),
+                                           self.final_norm.bias.data_ptr(), image.data_ptr(),
+                                           nbytes, stream), "tt_pack_image", lib)
         # The split-precision schedule holds activations as fp16 pieces; when
         # the weights allow one beyond the fp16 range for some input, the
         # automatic plan keeps to the fp32 schedules (set-up time: this syncs).
@@ -173,8 +187,10 @@ class TTForward:
                 valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
         if not x.is_cuda:
             raise RuntimeError("UserOptimizedTransformer runs on CUDA only (no CPU path)")
-        if x.dtype != torch.float32:
-            raise ValueError(f"expected float32 input, got {x.dtype}")
+        dname = str(x.dtype).split(".")[-1]
+        if dname not in _lib.DTYPE_CODES:
+            raise ValueError(f"expected a float32, float16 or bfloat16 input, got {x.dtype}")
+        dcode = _lib.DTYPE_CODES[dname]
         if x.dim() != 3 or x.shape[-1] != self.config.d_model:
             raise ValueError(f"expected x of shape [B, S, {self.config.d_model}], "
                              f"got {tuple(x.shape)}")
@@ -199,16 +215,22 @@ class TTForward:
         image = self._ensure_image(device)
         lib, cfg = self._lib, self._cfg
         y = torch.empty_like(x)
-        ws_bytes = self._ws_bytes.get((b, s))
+        ws_bytes = self._ws_bytes.get((b, s, dcode))
         if ws_bytes is None:
-            ws_bytes = self._ws_bytes[(b, s)] = lib.tt_workspace_bytes(ctypes.byref(cfg), b, s)
+            ws_bytes = self._ws_bytes[(b, s, dcode)] = lib.tt_typed_workspace_bytes(
+                ctypes.byref(cfg), dcode, b, s)
         ws_ptr = None
         if ws_bytes:
             ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
             ws_ptr = ws.data_ptr()
         stream = torch.cuda.current_stream(device).cuda_stream
-        rc = lib.tt_forward(ctypes.byref(cfg), image.data_ptr(), x.data_ptr(), mask_ptr, b, s,
-                            y.data_ptr(), ws_ptr, ws_bytes, stream)
+        if dcode == _lib.TT_DTYPE_F32:
+            rc = lib.tt_forward(ctypes.byref(cfg), image.data_ptr(), x.data_ptr(), mask_ptr, b,
+                                s, y.data_ptr(), ws_ptr, ws_bytes, stream)
+        else:
+            # 16-bit x and y: widened to fp32, the fp32 schedule, rounded back
+            rc = lib.tt_forward_typed(ctypes.byref(cfg), image.data_ptr(), dcode, x.data_ptr(),
+                                      mask_ptr, b, s, y.data_ptr(), ws_ptr, ws_bytes, stream)
         if rc != 0:
             _lib.check(rc, "tt_forward", lib)
         return y
