@@ -184,12 +184,13 @@ NCU_TRAFFIC = {
     ("D", "out_proj"): 68.4e6,
     ("D", "ffn_in"): 115.9e6,
     ("D", "ffn_out"): 181.1e6,
-    ("E", "layernorm"): 0.539e9,
-    ("E", "qkv"): 0.912e9,
-    ("E", "attention"): 1.406e9,
-    ("E", "out_proj"): 0.846e9,
-    ("E", "ffn_in"): 1.366e9,
-    ("E", "ffn_out"): 2.449e9,
+    ("E", "layernorm"): 0.403e9,
+    ("E", "qkv"): 0.850e9,
+    ("E", "attention"): 1.402e9,
+    ("E", "out_proj"): 0.811e9,
+    ("E", "ffn_in"): 1.276e9,
+    ("E", "ffn_out"): 2.311e9,
+    ("E", "final_norm"): 0.537e9,
 }
 
 
