@@ -191,6 +191,24 @@ int tt_forward_typed(const tt_config *cfg, const void *image, int dtype, const v
                      const uint8_t *mask, int64_t batch, int64_t seq, void *y,
                      void *workspace, size_t workspace_bytes, void *stream);
 
+/* Bytes of scratch tt_forward_host needs for one [batch, seq] call: device
+ * room for x, y and the mask plus tt_workspace_bytes. */
+size_t tt_host_workspace_bytes(const tt_config *cfg, int64_t batch, int64_t seq);
+
+/* One forward step from and to host memory, in one call: the whole step of a
+ * caller whose input arrives in, and whose output leaves through, host
+ * buffers (the reference's benchmark moves x to the device and the output
+ * back around each forward, torch_transformer_benchmark.py:381-392,
+ * :486-506). Enqueues on `stream` the copy of x (and of the mask, unless it is
+ * NULL) into the workspace, tt_forward on it, and the copy of y back; returns
+ * after enqueuing, and y is complete once `stream` has passed the call.
+ * Page-locked host buffers keep the copies asynchronous (pageable ones work,
+ * with the driver's staging). For small calls, where the caller's own per-call
+ * work is what limits the step, this is one entry instead of four. */
+int tt_forward_host(const tt_config *cfg, const void *image, const float *x_host,
+                    const uint8_t *mask_host, int64_t batch, int64_t seq, float *y_host,
+                    void *workspace, size_t workspace_bytes, void *stream);
+
 /* Bytes of the device scratch array behind tt_forward_noalloc. */
 #define TT_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
 

@@ -226,3 +226,20 @@ def test_typed_entry_points_need_no_gpu_for_their_checks(lib):
     rc = lib.tt_pack_image_typed(ctypes.byref(c), _lib.TT_DTYPE_BF16, None, None, None, None, 0,
                                  None)
     assert rc == _lib.TT_ERR_INVALID_ARGUMENT
+
+
+def test_host_entry_point_checks_need_no_gpu(lib):
+    """tt_forward_host: device room for x, y and the mask ahead of the
+    schedule's own scratch, and the checks made before anything is enqueued."""
+    c = _ops_cfg()
+    b, s = 4, 24
+    base = lib.tt_workspace_bytes(ctypes.byref(c), b, s)
+    io = (b * s * 128 * 4 + 255) // 256 * 256
+    assert lib.tt_host_workspace_bytes(ctypes.byref(c), b, s) == 2 * io + 256 + base
+    assert lib.tt_forward_host(ctypes.byref(c), None, None, None, b, s, None, None, 0, None) == \
+        _lib.TT_ERR_INVALID_ARGUMENT
+    assert lib.tt_forward_host(ctypes.byref(c), None, None, None, 0, s, None, None, 0, None) == 0
+    rc = lib.tt_forward_host(ctypes.byref(c), 256, 4096, None, b, s, 8192, 2048, 16, None)
+    assert rc == _lib.TT_ERR_WORKSPACE and "tt_host_workspace_bytes" in _lib.last_error(lib)
+    rc = lib.tt_forward_host(ctypes.byref(c), 256, 4096, None, b, s, 8192, 2056, 1 << 30, None)
+    assert rc == _lib.TT_ERR_INVALID_ARGUMENT and "aligned" in _lib.last_error(lib)

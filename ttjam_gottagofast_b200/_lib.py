@@ -42,6 +42,7 @@ EXPORTED = (
     "tt_read_status", "tt_last_error", "tt_forward_noalloc", "tt_fp16_operand_bound",
     "tt_launch_probe_start", "tt_launch_probe_read", "tt_test_arm_wait_timeout",
     "tt_pack_image_typed", "tt_typed_workspace_bytes", "tt_forward_typed",
+    "tt_host_workspace_bytes", "tt_forward_host",
 )
 
 # Element types of the typed entry points (TT_DTYPE_*), by torch dtype name.
@@ -107,6 +108,10 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         lib.tt_typed_workspace_bytes.argtypes = [cfgp, ctypes.c_int, i64, i64]
         lib.tt_forward_typed.restype = ctypes.c_int
         lib.tt_forward_typed.argtypes = [cfgp, vp, ctypes.c_int, vp, vp, i64, i64, vp, vp, sz, vp]
+        lib.tt_host_workspace_bytes.restype = sz
+        lib.tt_host_workspace_bytes.argtypes = [cfgp, i64, i64]
+        lib.tt_forward_host.restype = ctypes.c_int
+        lib.tt_forward_host.argtypes = [cfgp, vp, vp, vp, i64, i64, vp, vp, sz, vp]
         lib.tt_workspace_bytes.restype = sz
         lib.tt_workspace_bytes.argtypes = [cfgp, i64, i64]
         lib.tt_forward.restype = ctypes.c_int

@@ -740,6 +740,49 @@ int tt_forward_typed(const tt_config *cfg, const void *image, int dtype, const v
                       [&] { return launch_narrow(dtype, y32, y, n, stream); });
 }
 
+size_t tt_host_workspace_bytes(const tt_config *cfg, int64_t batch, int64_t seq) {
+  if (validate_config(cfg) != TT_OK || batch < 0 || seq < 0) return 0;
+  const size_t T = (size_t)batch * (size_t)seq;
+  return 2 * align_up(T * (size_t)cfg->d_model * sizeof(float), 256) + align_up(T, 256) +
+         tt_workspace_bytes(cfg, batch, seq);
+}
+
+int tt_forward_host(const tt_config *cfg, const void *image, const float *x_host,
+                    const uint8_t *mask_host, int64_t batch, int64_t seq, float *y_host,
+                    void *workspace, size_t workspace_bytes, void *stream_) {
+  int rc = validate_config(cfg);
+  if (rc != TT_OK) return rc;
+  if (batch < 0 || seq < 0) return fail(TT_ERR_INVALID_ARGUMENT, "batch and seq must be >= 0");
+  if (batch == 0 || seq == 0) return TT_OK;
+  if (image == nullptr || x_host == nullptr || y_host == nullptr)
+    return fail(TT_ERR_INVALID_ARGUMENT, "tt_forward_host: NULL image, x or y");
+  if (x_host == y_host) return fail(TT_ERR_INVALID_ARGUMENT, "tt_forward_host: y may not alias x");
+  if (misaligned(workspace))
+    return fail(TT_ERR_INVALID_ARGUMENT, "tt_forward_host: workspace must be 16-byte aligned");
+  if (seq > (int64_t)INT32_MAX || batch * seq > ((int64_t)1 << 40))
+    return fail(TT_ERR_UNSUPPORTED, "tt_forward_host: batch*seq too large");
+  const size_t need = tt_host_workspace_bytes(cfg, batch, seq);
+  if (workspace_bytes < need || workspace == nullptr)
+    return fail(TT_ERR_WORKSPACE, "tt_forward_host: workspace smaller than "
+                                  "tt_host_workspace_bytes (" + std::to_string(need) + " bytes)");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const size_t T = (size_t)batch * (size_t)seq;
+  const size_t xb = T * (size_t)cfg->d_model * sizeof(float), io = align_up(xb, 256);
+  char *ws = static_cast<char *>(workspace);
+  float *xs = reinterpret_cast<float *>(ws);
+  float *ys = reinterpret_cast<float *>(ws + io);
+  uint8_t *ms = reinterpret_cast<uint8_t *>(ws + 2 * io);
+  const size_t used = 2 * io + align_up(T, 256);
+  TT_CUDA_TRY(cudaMemcpyAsync(xs, x_host, xb, cudaMemcpyHostToDevice, stream));
+  if (mask_host != nullptr)
+    TT_CUDA_TRY(cudaMemcpyAsync(ms, mask_host, T, cudaMemcpyHostToDevice, stream));
+  if ((rc = tt_forward(cfg, image, xs, mask_host != nullptr ? ms : nullptr, batch, seq, ys,
+                       ws + used, workspace_bytes - used, stream_)))
+    return rc;
+  TT_CUDA_TRY(cudaMemcpyAsync(y_host, ys, xb, cudaMemcpyDeviceToHost, stream));
+  return TT_OK;
+}
+
 int tt_read_status(const tt_config *cfg, const void *image, int32_t *code, int32_t *detail,
                    void *stream_) {
   int rc = validate_config(cfg);

@@ -88,6 +88,7 @@ class TTForward:
         self._image_key = None
         self._plist = None
         self._ws_bytes = {}
+        self._host_inflight = []  # (event, host buffers) of tt_forward_host calls in flight
         self.fp16_operand_bound = None
         self.register_load_state_dict_post_hook(
             lambda module, incompatible: module.invalidate())
@@ -245,7 +246,8 @@ class TTForward:
         the current stream, and slice i's output crosses back on another
         while slice i+1 computes. Pinned host buffers make the copies
         asynchronous (pageable ones still give correct results, without the
-        overlap).
+        overlap). A call small enough for one slice is one library call
+        (tt_forward_host: copy in, forward, copy out).
 
         `x_host` is [B, S, d_model] float32 on the CPU, `valid_token_mask`
         [B, S] bool on the CPU or None, `out` an optional [B, S, d_model]
@@ -276,9 +278,7 @@ class TTForward:
         slices = max(1, min(slices, b))
         cur = torch.cuda.current_stream(dev)
         if slices == 1:
-            xd = x_host.to(dev, non_blocking=True)
-            md = None if valid_token_mask is None else valid_token_mask.to(dev, non_blocking=True)
-            out.copy_(self.forward(xd, md), non_blocking=True)
+            self._host_step(x_host, valid_token_mask, out, dev)
             return out
         cin = torch.cuda.Stream(dev)
         cout = torch.cuda.Stream(dev)
@@ -307,6 +307,44 @@ class TTForward:
         if m_dev is not None:
             m_dev.record_stream(cin)
         return out
+
+    def _host_step(self, x_host, mask, out, dev) -> None:
+        """One small host-buffer step as one library call (tt_forward_host):
+        the copy in, the forward and the copy out are enqueued in C, so the
+        per-call host work that limits small steps is a single entry."""
+        b, s, _ = x_host.shape
+        if mask is not None:
+            if mask.shape != (b, s) or mask.dtype not in (torch.bool, torch.uint8):
+                raise ValueError(f"valid_token_mask must be a bool [B, S] = {(b, s)} tensor")
+            if not mask.is_contiguous():
+                mask = mask.contiguous()
+        if not x_host.is_contiguous():
+            x_host = x_host.contiguous()
+        with torch.cuda.device(dev):
+            image = self._ensure_image(dev)
+            lib, cfg = self._lib, self._cfg
+            key = (b, s, "host")
+            nbytes = self._ws_bytes.get(key)
+            if nbytes is None:
+                nbytes = self._ws_bytes[key] = lib.tt_host_workspace_bytes(ctypes.byref(cfg), b, s)
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+            stream = torch.cuda.current_stream(dev).cuda_stream
+            rc = lib.tt_forward_host(ctypes.byref(cfg), image.data_ptr(), x_host.data_ptr(),
+                                     None if mask is None else mask.data_ptr(), b, s,
+                                     out.data_ptr(), ws.data_ptr(), nbytes, stream)
+            if rc == 0:
+                # the copies are asynchronous: keep the host buffers alive until the
+                # stream has passed them, so a freed pinned block is not handed out
+                # again (by torch's host allocator) while a copy still reads or
+                # writes it
+                inflight = self._host_inflight
+                while inflight and inflight[0][0].query():
+                    inflight.pop(0)
+                ev = torch.cuda.Event()
+                ev.record(torch.cuda.current_stream(dev))
+                inflight.append((ev, x_host, mask, out))
+        if rc != 0:
+            _lib.check(rc, "tt_forward_host", lib)
 
     @staticmethod
     def _slice_bounds(b: int, slices: int):
