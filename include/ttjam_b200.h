@@ -303,6 +303,13 @@ int tt_launch_probe_read(float *ms, int32_t *kinds, int capacity);
  * TT_ERR_INVALID_ARGUMENT. */
 int tt_test_arm_wait_timeout(int budget_log2);
 
+/* Test support, with no counterpart in the reference: y[i] = GELU(x[i]) for
+ * n device floats on `stream`, computed by the device function every schedule
+ * applies after ffn_in (F.gelu(approximate="none"), torch_transformer_benchmark.py:141),
+ * so that its accuracy can be checked against a float64 GELU over any set of
+ * arguments. Returns TT_OK, TT_ERR_INVALID_ARGUMENT or TT_ERR_CUDA. */
+int tt_test_gelu(const float *x, float *y, int64_t n, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

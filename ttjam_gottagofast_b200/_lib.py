@@ -42,7 +42,7 @@ EXPORTED = (
     "tt_read_status", "tt_last_error", "tt_forward_noalloc", "tt_fp16_operand_bound",
     "tt_launch_probe_start", "tt_launch_probe_read", "tt_test_arm_wait_timeout",
     "tt_pack_image_typed", "tt_typed_workspace_bytes", "tt_forward_typed",
-    "tt_host_workspace_bytes", "tt_forward_host",
+    "tt_host_workspace_bytes", "tt_forward_host", "tt_test_gelu",
 )
 
 # Element types of the typed entry points (TT_DTYPE_*), by torch dtype name.
@@ -133,6 +133,8 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         lib.tt_launch_probe_read.restype = ctypes.c_int
         lib.tt_launch_probe_read.argtypes = [ctypes.POINTER(ctypes.c_float),
                                              ctypes.POINTER(i32), ctypes.c_int]
+        lib.tt_test_gelu.restype = ctypes.c_int
+        lib.tt_test_gelu.argtypes = [vp, vp, i64, vp]
         lib.tt_test_arm_wait_timeout.restype = ctypes.c_int
         lib.tt_test_arm_wait_timeout.argtypes = [ctypes.c_int]
         if lib.tt_abi_version() != TT_ABI_VERSION:

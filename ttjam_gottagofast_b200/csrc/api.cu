@@ -117,6 +117,13 @@ __global__ void operand_bound_kernel(const float *__restrict__ W, const float *_
 
 bool misaligned(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; }
 
+// y[i] = gelu_erf(x[i]): the GELU every schedule applies, for its accuracy test.
+__global__ void gelu_test_kernel(const float *__restrict__ x, float *__restrict__ y, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = gelu_erf(x[i]);
+}
+
 // Launch timing probe (tt_launch_probe_start / _read): per host thread, a
 // pair of timing events around each kernel launch of the forward schedules.
 struct LaunchProbe {
@@ -837,6 +844,16 @@ int tt_launch_probe_read(float *ms, int32_t *kinds, int capacity) {
 }
 
 int tt_test_arm_wait_timeout(int budget_log2) { return arm_gemm_wait_timeout(budget_log2); }
+
+int tt_test_gelu(const float *x, float *y, int64_t n, void *stream_) {
+  if (n < 0 || (n > 0 && (x == nullptr || y == nullptr)))
+    return fail(TT_ERR_INVALID_ARGUMENT, "tt_test_gelu: NULL pointer or negative size");
+  if (n == 0) return TT_OK;
+  const int64_t blocks = std::min<int64_t>(ceil_div(n, 256), 148 * 8);
+  gelu_test_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream_)>>>(x, y, n);
+  TT_LAUNCH_CHECK("gelu_test");
+  return TT_OK;
+}
 
 int tt_last_error(char *buf, size_t len) {
   const std::string &m = g_last_error;
