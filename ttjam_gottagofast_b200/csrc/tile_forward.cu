@@ -9,7 +9,7 @@
 // threads r and r + 128, each taking one half of the row's columns (and of its
 // keys in the softmax), with partial row statistics exchanged through shared
 // memory -- and thread 0 also issues every MMA; warp 8 (one lane) streams the
-// weights through a 6-stage ring with
+// weights through a 5-stage ring with
 // TMA (3-D tensor maps over [layer, out rows, k] of the packed fp16 pieces, so
 // one map per matrix covers all layers). Every product is split precision as
 // in the per-op tensor-core schedule (gemm_tc.cu): operands as fp16 hi/lo
@@ -26,10 +26,12 @@
 // rows in the 64-byte swizzle the MMA reads), Q, K and V^T of the current head
 // in the same layout (V^T as 32 dims x 128 keys), and the weight ring.
 //
-// One layer is twelve MMA groups, each committed to one barrier that the row
-// threads wait on: q|k|v of head 0 (N = 96: its q, k and v rows), then per
-// head h the scores S = Q K^T (N = 128), and P.V (N = 32) together with the
-// q|k|v projection of head h+1; then out_proj, ffn_in and ffn_out (N = 128).
+// One layer is twelve MMA groups: q|k|v of head 0 (N = 96: its q, k and v
+// rows), then per head h the scores S = Q K^T (N = 128), issued together with
+// the q|k|v projection of head h+1 (which then runs under head h's softmax,
+// completing on a barrier of its own), and P.V (N = 32); then out_proj, ffn_in
+// and ffn_out (N = 128). V^T is double-buffered by head parity, so head h+1's
+// q|k|v epilogue writes it while head h's P.V still reads the other buffer.
 // The row threads between groups: the q|k|v epilogue (bias, range check,
 // Q and K rows and the transposed V^T into shared memory), the softmax (the
 // whole row at once: exact max, 2^7-scaled P split into tensor memory), the
@@ -56,7 +58,7 @@ namespace {
 constexpr int D = 128, H = 4, HD = 32, TR = 128;  // model width, heads, head dim, tile rows
 constexpr int kRowThreads = 256;  // warps 0-7: two threads per tile row, one per column half
 constexpr int kThreads = kRowThreads + 32;  // warp 8: weight loads
-constexpr int NST = 6;                             // weight ring stages
+constexpr int NST = 5;                             // weight ring stages
 
 // shared memory, offsets from a 1024-byte aligned base
 constexpr uint32_t KBLK = 16384;  // a 32-wide k-block of a 128-row split operand: hi | lo
@@ -64,9 +66,10 @@ constexpr uint32_t HALF = 8192;   // lo piece offset inside a k-block (and a wei
 constexpr uint32_t OFF_A = 0;                 // A operand: 4 k-blocks
 constexpr uint32_t OFF_Q = 4 * KBLK;          // Q of one head (one k-block)
 constexpr uint32_t OFF_K = OFF_Q + KBLK;      // K of one head (one k-block)
-constexpr uint32_t OFF_VT = OFF_K + KBLK;     // V^T of one head: 4 k-blocks of 32 keys
+constexpr uint32_t OFF_VT = OFF_K + KBLK;     // V^T of two heads (h even, h odd): 4 k-blocks each
 constexpr uint32_t VT_KB = 4096, VT_HALF = 2048;  // a V^T k-block: 32 dims x 64 B, hi | lo
-constexpr uint32_t OFF_W = OFF_VT + 4 * VT_KB;    // weight ring
+constexpr uint32_t VT_BUF = 4 * VT_KB;            // one head's V^T
+constexpr uint32_t OFF_W = OFF_VT + 2 * VT_BUF;   // weight ring
 constexpr uint32_t WSTAGE = 16384;  // up to 128 weight rows x one k-block: hi | lo
 constexpr uint32_t OFF_KW = OFF_W + NST * WSTAGE;  // 4 words: valid key rows of the tile
 // partial row statistics of the two threads of a row: [2 arrays][2 halves][128]
@@ -369,10 +372,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto empty = [&](int s) { return bars + 8u * (NST + s); };
   const uint32_t mma_bar = bars + 8u * (2 * NST);
   const uint32_t drain_bar = bars + 8u * (2 * NST + 1);
-  const uint32_t tmem_slot = bars + 8u * (2 * NST + 2);
-  static_assert(8 * (2 * NST + 3) + 8 <= 256, "barrier area");
-  uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(bp + OFF_BAR + 8 * (2 * NST + 2));
-  volatile int *abort_w = reinterpret_cast<volatile int *>(bp + OFF_BAR + 8 * (2 * NST + 2) + 4);
+  const uint32_t qkv_bar = bars + 8u * (2 * NST + 2);
+  const uint32_t tmem_slot = bars + 8u * (2 * NST + 3);
+  static_assert(8 * (2 * NST + 4) + 8 <= 256, "barrier area");
+  uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(bp + OFF_BAR + 8 * (2 * NST + 3));
+  volatile int *abort_w = reinterpret_cast<volatile int *>(bp + OFF_BAR + 8 * (2 * NST + 3) + 4);
   uint32_t *kword = reinterpret_cast<uint32_t *>(bp + OFF_KW);
   float *xch = reinterpret_cast<float *>(bp + OFF_XCH);
   float *xl = reinterpret_cast<float *>(bp + OFF_XL);
@@ -393,6 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(mma_bar, 1);
     mbar_init(drain_bar, 1);
+    mbar_init(qkv_bar, 1);
     *abort_w = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -465,7 +470,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int jend = a.causal ? r + 1 : j0 + a.seq;
     bool ok = true;        // thread 0: MMAs are issued while no wait has given up
     int ws = 0;            // thread 0: weight stages consumed
-    uint32_t phase = 0;    // completed MMA groups
+    uint32_t phase = 0;    // completed MMA groups on mma_bar
+    uint32_t qphase = 0;   // completed q|k|v groups on qkv_bar (heads 1..3 of each layer)
     // thread 0: one projection over the four k-blocks of the A operand into
     // tensor-memory column d_col, B rows from the next four weight stages
     auto gemm = [&](uint32_t d_col, uint32_t id) {
@@ -495,6 +501,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto wait_mma = [&](int detail) {
       mbar_wait(mma_bar, phase & 1, abort_w, a.status, detail);
       ++phase;
+      tc_fence_after();
+    };
+    auto wait_qkv = [&](int detail) {
+      mbar_wait(qkv_bar, qphase & 1, abort_w, a.status, detail);
+      ++qphase;
       tc_fence_after();
     };
     // all row threads: shared-memory operands and tensor-memory writes of this
@@ -556,7 +567,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int h = 0; h < H; ++h) {
         // ---- q|k|v epilogue of head h: half 0 takes q and value dims 0-15,
         // half 1 takes k and value dims 16-31 ------------------------------
-        wait_mma(0x6300 + h);
+        if (h == 0)
+          wait_mma(0x6300);
+        else
+          wait_qkv(0x6300 + h);
         {
           float t[HD], bv[HD];
           tmem_ld32(lb + T_ACC + HD * hf, t);
@@ -575,7 +589,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float4 q = *reinterpret_cast<const float4 *>(bvv + i);
             bv16[i] = q.x; bv16[i + 1] = q.y; bv16[i + 2] = q.z; bv16[i + 3] = q.w;
           }
-          uint8_t *vt = bp + OFF_VT + (uint32_t)(r >> 5) * VT_KB;
+          uint8_t *vt = bp + OFF_VT + (uint32_t)(h & 1) * VT_BUF + (uint32_t)(r >> 5) * VT_KB;
           const int c = r & 31;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
@@ -592,19 +606,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!(amax <= 65504.f) && in) raise_status(a.status, TT_ERR_DEVICE_RANGE, 0x6400 + h);
         }
         step_done();
-        if (tid == 0 && ok) {
-          // S = Q K^T over the tile's 128 keys
+        if (tid == 0) {
+          if (ok) {
+            // S = Q K^T over the tile's 128 keys (issued after P.V of the
+            // previous head, which read the S/P cells it overwrites)
 #pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint64_t ko = (uint64_t)(2 * kk);
-            const uint64_t qh = desc_sw64(base + OFF_Q) + ko, ql = desc_sw64(base + OFF_Q + HALF) + ko;
-            const uint64_t kh = desc_sw64(base + OFF_K) + ko, kl = desc_sw64(base + OFF_K + HALF) + ko;
-            mma_ss(tm + T_SP, qh, kh, IDESC_128, kk > 0);
-            mma_ss(tm + T_SP, qh, kl, IDESC_128, 1);
-            mma_ss(tm + T_SP, ql, kh, IDESC_128, 1);
+            for (int kk = 0; kk < HD / 16; ++kk) {
+              const uint64_t ko = (uint64_t)(2 * kk);
+              const uint64_t qh = desc_sw64(base + OFF_Q) + ko, ql = desc_sw64(base + OFF_Q + HALF) + ko;
+              const uint64_t kh = desc_sw64(base + OFF_K) + ko, kl = desc_sw64(base + OFF_K + HALF) + ko;
+              mma_ss(tm + T_SP, qh, kh, IDESC_128, kk > 0);
+              mma_ss(tm + T_SP, qh, kl, IDESC_128, 1);
+              mma_ss(tm + T_SP, ql, kh, IDESC_128, 1);
+            }
+          }
+          mma_commit(mma_bar);
+          // q|k|v of the next head now (the accumulator was read above), so it
+          // runs under this head's softmax, off the row threads' path
+          if (h + 1 < H) {
+            gemm(T_ACC, IDESC_QKV);
+            mma_commit(qkv_bar);
           }
         }
-        if (tid == 0) mma_commit(mma_bar);
         // ---- softmax of row r, keys split by half: the row max (the halves'
         // maxima meet in xch), then 2^7-scaled P over S and the partial sums
         wait_mma(0x6500 + h);
@@ -682,7 +705,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t od = tm + T_O + (uint32_t)(h * HD);
 #pragma unroll
             for (int kk = 0; kk < TR / 16; ++kk) {
-              const uint32_t vb = base + OFF_VT + (uint32_t)(kk >> 1) * VT_KB;
+              const uint32_t vb = base + OFF_VT + (uint32_t)(h & 1) * VT_BUF + (uint32_t)(kk >> 1) * VT_KB;
               const uint64_t ko = (uint64_t)(2 * (kk & 1));
               const uint64_t vh = desc_sw64(vb) + ko, vl = desc_sw64(vb + VT_HALF) + ko;
               const uint32_t ph = tm + T_SP + 32u * (uint32_t)(kk >> 1) + 8u * (uint32_t)(kk & 1);
@@ -691,8 +714,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               mma_ts(od, ph + 16u, vh, IDESC_PV, 1);
             }
           }
-          if (h + 1 < H) gemm(T_ACC, IDESC_QKV);  // q|k|v of the next head
-          mma_commit(mma_bar);
+          // the last head's P.V completes the context; earlier ones complete
+          // with the next head's scores, which are issued after them
+          if (h + 1 == H) mma_commit(mma_bar);
         }
       }
       // ---- context O / l -> A operand: half hf takes heads 2 hf, 2 hf + 1 ---
