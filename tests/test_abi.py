@@ -138,18 +138,19 @@ def test_fp32_only_flag_keeps_auto_plan_off_the_split_schedule(lib):
 
 
 def test_tile_plan_takes_batches_of_short_sequences_of_the_d128_model(lib):
-    # d_model = ffn_dim = 128, 4 heads, seq dividing 128, at least 2048 rows
-    # (official case 1: batch 64 x 128)
+    # d_model = ffn_dim = 128, 4 heads, seq dividing 128, at least one tile of
+    # 128 rows (official case 1: batch 64 x 128; workload A: batch 8 x 128)
     a = _cfg()
     assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(a), 64, 128)] == "tile"
     assert lib.tt_forward_launch_count(ctypes.byref(a), 64, 128) == 1
     assert lib.tt_workspace_bytes(ctypes.byref(a), 64, 128) == 0
     # (seq 128: never the cluster schedule, which takes short sequences on a GPU)
-    for b, s in ((16, 128), (10000, 128)):
+    for b, s in ((1, 128), (8, 128), (16, 128), (10000, 128), (4, 32)):
         assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(a), b, s)] == "tile"
-    # fewer rows (config A: batch 8 x 128), seq not a divisor of 128, or
-    # another head count: the per-op schedule
-    assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(a), 8, 128)] == "ops_tc"
+    # fewer rows than a tile (without a GPU, where the cluster schedule is not
+    # offered), seq not a divisor of 128, or another head count: the per-op
+    # schedule
+    assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(a), 4, 16)] == "ops_tc"
     assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(a), 32, 512)] == "ops_tc"
     assert _lib.PLAN_NAMES[lib.tt_forward_plan(ctypes.byref(a), 100, 24)] == "ops_tc"
     h2 = _cfg(h=2)

@@ -223,12 +223,13 @@ int forward_plan(const tt_config *cfg, int64_t batch, int64_t seq) {
       if (choose_cluster(*cfg, batch, seq).cluster > 0) return PLAN_CLUSTER;
       // the tile forward holds activations as fp16 pieces, as the per-op
       // tensor-core schedule does. It runs a tile's four layers in about
-      // 160 us whatever the number of tiles up to one per SM, and beats the
-      // per-op schedule from 16 tiles on (measured on B200, d 128, 4 layers:
-      // 16 tiles 160 us against 174, 64 tiles 161 against 189, 10000 tiles
-      // 9.9 ms against 15.8; 8 tiles 164 against 152)
+      // 132 us whatever the number of tiles up to one per SM, and beats the
+      // per-op schedule from one full tile on (measured on B200, d 128, 4
+      // layers: 1 tile 132 us against 140, 8 tiles (workload A) 131.5 against
+      // 148, 64 tiles 132 against 189, 10000 tiles 8.1 ms against 15.8). Below
+      // 128 rows the cluster forward, or the per-op schedule, is faster.
       if ((cfg->flags & TT_FLAG_FP32_ONLY) == 0 && tile_forward_supported(*cfg, batch, seq) &&
-          batch * seq >= 2048)
+          batch * seq >= 128)
         return PLAN_TILE;
       return auto_ops_plan(*cfg);
     case TT_PLAN_TILE:

@@ -5,10 +5,11 @@
 // holding whole sequences (seq divides 128, so a tile's rows never attend to
 // another tile's), and runs every layer on it with no exchange between CTAs.
 //
-// Per CTA (288 threads): warps 0-7 are the row threads -- tile row r belongs to
+// Per CTA (320 threads): warps 0-7 are the row threads -- tile row r belongs to
 // threads r and r + 128, each taking one half of the row's columns (and of its
 // keys in the softmax), with partial row statistics exchanged through shared
-// memory -- and thread 0 also issues every MMA; warp 8 (one lane) streams the
+// memory; warp 9 (one lane) issues every MMA once the row warps have arrived
+// on the barrier of the step that feeds it; warp 8 (one lane) streams the
 // weights through a 5-stage ring with
 // TMA (3-D tensor maps over [layer, out rows, k] of the packed fp16 pieces, so
 // one map per matrix covers all layers). Every product is split precision as
@@ -57,7 +58,7 @@ namespace {
 
 constexpr int D = 128, H = 4, HD = 32, TR = 128;  // model width, heads, head dim, tile rows
 constexpr int kRowThreads = 256;  // warps 0-7: two threads per tile row, one per column half
-constexpr int kThreads = kRowThreads + 32;  // warp 8: weight loads
+constexpr int kThreads = kRowThreads + 64;  // warp 8: weight loads; warp 9: MMA issue
 constexpr int NST = 5;                             // weight ring stages
 
 // shared memory, offsets from a 1024-byte aligned base
@@ -184,6 +185,9 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b), "r"(id), "r"(accum)
       : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -377,6 +381,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   static_assert(8 * (2 * NST + 4) + 8 <= 256, "barrier area");
   uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(bp + OFF_BAR + 8 * (2 * NST + 3));
   volatile int *abort_w = reinterpret_cast<volatile int *>(bp + OFF_BAR + 8 * (2 * NST + 3) + 4);
+  // row threads -> MMA thread: one arrive per row warp once a step's operands
+  // are in place; one barrier per kind of step, so that the row threads are
+  // never two phases of one barrier ahead of the MMA thread's waits
+  const uint32_t rows_misc = bars + 8u * (2 * NST + 4);  // LayerNorm 1, context, LayerNorm 2, GELU
+  const uint32_t rows_epi = bars + 8u * (2 * NST + 5);   // a head's q|k|v epilogue
+  const uint32_t rows_sm = bars + 8u * (2 * NST + 6);    // a head's softmax
+  static_assert(8 * (2 * NST + 7) <= 256, "barrier area");
   uint32_t *kword = reinterpret_cast<uint32_t *>(bp + OFF_KW);
   float *xch = reinterpret_cast<float *>(bp + OFF_XCH);
   float *xl = reinterpret_cast<float *>(bp + OFF_XL);
@@ -398,6 +409,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(mma_bar, 1);
     mbar_init(drain_bar, 1);
     mbar_init(qkv_bar, 1);
+    mbar_init(rows_misc, kRowThreads / 32);
+    mbar_init(rows_epi, kRowThreads / 32);
+    mbar_init(rows_sm, kRowThreads / 32);
     *abort_w = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -452,6 +466,106 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int k = ws > NST ? ws - NST : 0; k < ws; ++k)
         mbar_drain(full(k % NST), (k / NST) & 1, a.status, 0x6F00);
     }
+  } else if (warp == kRowThreads / 32 + 1) {
+    // ---- MMA issue (one lane): each group once the row threads' step that
+    // feeds it is done, in the order the row threads consume the results ----
+    if (lane == 0) {
+      bool ok = true;  // MMAs are issued while no wait has given up
+      int ws = 0;      // weight stages consumed
+      uint32_t pm = 0, pe = 0, ps = 0;  // phases waited on rows_misc, rows_epi, rows_sm
+      // one projection over the four k-blocks of the A operand into
+      // tensor-memory column d_col, B rows from the next four weight stages
+      auto gemm = [&](uint32_t d_col, uint32_t id) {
+#pragma unroll 1
+        for (int kb = 0; kb < 4; ++kb, ++ws) {
+          const int s = ws % NST;
+          if (!ok || !mbar_wait(full(s), (ws / NST) & 1, abort_w, a.status, 0x6200 + kb)) {
+            ok = false;
+            continue;
+          }
+          tc_fence_after();
+          const uint32_t ab = base + OFF_A + (uint32_t)kb * KBLK;
+          const uint32_t wb = base + OFF_W + (uint32_t)s * WSTAGE;
+          const uint64_t ah = desc_sw64(ab), al = desc_sw64(ab + HALF);
+          const uint64_t wh = desc_sw64(wb), wl = desc_sw64(wb + HALF);
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const uint64_t ko = (uint64_t)(2 * k);
+            mma_ss(tm + d_col, ah + ko, wh + ko, id, (kb | k) != 0);
+            mma_ss(tm + d_col, ah + ko, wl + ko, id, 1);
+            mma_ss(tm + d_col, al + ko, wh + ko, id, 1);
+          }
+          mma_commit(empty(s));
+        }
+      };
+      auto rows_wait = [&](uint32_t bar, uint32_t &ph, int detail) {
+        if (!mbar_wait(bar, ph & 1, abort_w, a.status, detail)) ok = false;
+        ++ph;
+        tc_fence_after();
+      };
+#pragma unroll 1
+      for (int l = 0; l < L; ++l) {
+        rows_wait(rows_misc, pm, 0x6B00);  // LayerNorm 1 in the A operand
+        gemm(T_ACC, IDESC_QKV);            // q|k|v of head 0
+        mma_commit(mma_bar);
+#pragma unroll 1
+        for (int h = 0; h < H; ++h) {
+          rows_wait(rows_epi, pe, 0x6B10 + h);  // Q, K and V^T of head h in shared memory
+          if (ok) {
+            // S = Q K^T over the tile's 128 keys (after P.V of the previous
+            // head, which read the S/P cells it overwrites)
+#pragma unroll
+            for (int kk = 0; kk < HD / 16; ++kk) {
+              const uint64_t ko = (uint64_t)(2 * kk);
+              const uint64_t qh = desc_sw64(base + OFF_Q) + ko, ql = desc_sw64(base + OFF_Q + HALF) + ko;
+              const uint64_t kh = desc_sw64(base + OFF_K) + ko, kl = desc_sw64(base + OFF_K + HALF) + ko;
+              mma_ss(tm + T_SP, qh, kh, IDESC_128, kk > 0);
+              mma_ss(tm + T_SP, qh, kl, IDESC_128, 1);
+              mma_ss(tm + T_SP, ql, kh, IDESC_128, 1);
+            }
+          }
+          mma_commit(mma_bar);
+          // q|k|v of the next head (the row threads have read the
+          // accumulator): it runs under this head's softmax
+          if (h + 1 < H) {
+            gemm(T_ACC, IDESC_QKV);
+            mma_commit(qkv_bar);
+          }
+          rows_wait(rows_sm, ps, 0x6B20 + h);  // P of head h in tensor memory
+          if (ok) {
+            // O_h = P V_h: keys 16 kk .. 16 kk + 15 are P_hi cells
+            // 32 (kk / 2) + 8 (kk % 2) .. + 7 and P_lo 16 cells further
+            const uint32_t od = tm + T_O + (uint32_t)(h * HD);
+#pragma unroll
+            for (int kk = 0; kk < TR / 16; ++kk) {
+              const uint32_t vb = base + OFF_VT + (uint32_t)(h & 1) * VT_BUF + (uint32_t)(kk >> 1) * VT_KB;
+              const uint64_t ko = (uint64_t)(2 * (kk & 1));
+              const uint64_t vh = desc_sw64(vb) + ko, vl = desc_sw64(vb + VT_HALF) + ko;
+              const uint32_t ph = tm + T_SP + 32u * (uint32_t)(kk >> 1) + 8u * (uint32_t)(kk & 1);
+              mma_ts(od, ph, vh, IDESC_PV, kk > 0);
+              mma_ts(od, ph, vl, IDESC_PV, 1);
+              mma_ts(od, ph + 16u, vh, IDESC_PV, 1);
+            }
+          }
+          // the last head's P.V completes the context; earlier ones complete
+          // with the next head's scores, which are issued after them
+          if (h + 1 == H) mma_commit(mma_bar);
+        }
+        rows_wait(rows_misc, pm, 0x6B30);  // context in the A operand
+        gemm(T_ACC, IDESC_128);            // out_proj
+        mma_commit(mma_bar);
+        rows_wait(rows_misc, pm, 0x6B40);  // LayerNorm 2
+        gemm(T_ACC, IDESC_128);            // ffn_in
+        mma_commit(mma_bar);
+        rows_wait(rows_misc, pm, 0x6B50);  // GELU output
+        gemm(T_ACC, IDESC_128);            // ffn_out
+        mma_commit(mma_bar);
+      }
+      // every MMA this thread issued has completed before the tensor memory
+      // is freed
+      mma_commit(drain_bar);
+      mbar_drain(drain_bar, 0, a.status, 0x6F10);
+    }
   } else {
     // ---- row threads: r = tile row (tensor-memory lane), hf = column half --
     const int r = tid & (TR - 1), hf = tid >> 7;
@@ -468,35 +582,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // allowed keys of row r: its sequence's rows of the tile, up to r (causal)
     const int j0 = (r / a.seq) * a.seq;
     const int jend = a.causal ? r + 1 : j0 + a.seq;
-    bool ok = true;        // thread 0: MMAs are issued while no wait has given up
-    int ws = 0;            // thread 0: weight stages consumed
     uint32_t phase = 0;    // completed MMA groups on mma_bar
     uint32_t qphase = 0;   // completed q|k|v groups on qkv_bar (heads 1..3 of each layer)
-    // thread 0: one projection over the four k-blocks of the A operand into
-    // tensor-memory column d_col, B rows from the next four weight stages
-    auto gemm = [&](uint32_t d_col, uint32_t id) {
-#pragma unroll 1
-      for (int kb = 0; kb < 4; ++kb, ++ws) {
-        const int s = ws % NST;
-        if (!ok || !mbar_wait(full(s), (ws / NST) & 1, abort_w, a.status, 0x6200 + kb)) {
-          ok = false;
-          continue;
-        }
-        tc_fence_after();
-        const uint32_t ab = base + OFF_A + (uint32_t)kb * KBLK;
-        const uint32_t wb = base + OFF_W + (uint32_t)s * WSTAGE;
-        const uint64_t ah = desc_sw64(ab), al = desc_sw64(ab + HALF);
-        const uint64_t wh = desc_sw64(wb), wl = desc_sw64(wb + HALF);
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const uint64_t ko = (uint64_t)(2 * k);
-          mma_ss(tm + d_col, ah + ko, wh + ko, id, (kb | k) != 0);
-          mma_ss(tm + d_col, ah + ko, wl + ko, id, 1);
-          mma_ss(tm + d_col, al + ko, wh + ko, id, 1);
-        }
-        mma_commit(empty(s));
-      }
-    };
     // all row threads: the last committed MMA group has completed
     auto wait_mma = [&](int detail) {
       mbar_wait(mma_bar, phase & 1, abort_w, a.status, detail);
@@ -508,13 +595,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++qphase;
       tc_fence_after();
     };
-    // all row threads: shared-memory operands and tensor-memory writes of this
-    // step are complete before thread 0 issues the next MMA group
-    auto step_done = [&]() {
+    // all row threads: this step's shared-memory operands and tensor-memory
+    // writes are complete; the MMA thread waits for all eight row warps on
+    // `bar` before it issues the next MMA group
+    auto step_done = [&](uint32_t bar) {
       fence_proxy_async_smem();
       tc_fence_before();
-      rows_sync();
-      if (tid == 0) tc_fence_after();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar);
     };
     auto to_a = [&](int c, float *v) { put_kblock_row(bp + OFF_A + c * KBLK, HALF, r, v); };
     // this thread's chunks: x = valid ? x + acc * scale + bias : 0
@@ -557,11 +645,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float s_qkv = wsc[0], s_o = wsc[1], s_1 = wsc[2], s_2 = wsc[3];
       // LayerNorm 1 -> A operand
       layer_norm_half(lb + T_X, r, hf, xch, P(a.off.ln1_w), P(a.off.ln1_b), a.eps, to_a);
-      step_done();
-      if (tid == 0) {
-        gemm(T_ACC, IDESC_QKV);
-        mma_commit(mma_bar);
-      }
+      step_done(rows_misc);
       const float *bqkv = P(a.off.bqkv);
 #pragma unroll 1
       for (int h = 0; h < H; ++h) {
@@ -605,29 +689,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (!(amax <= 65504.f) && in) raise_status(a.status, TT_ERR_DEVICE_RANGE, 0x6400 + h);
         }
-        step_done();
-        if (tid == 0) {
-          if (ok) {
-            // S = Q K^T over the tile's 128 keys (issued after P.V of the
-            // previous head, which read the S/P cells it overwrites)
-#pragma unroll
-            for (int kk = 0; kk < HD / 16; ++kk) {
-              const uint64_t ko = (uint64_t)(2 * kk);
-              const uint64_t qh = desc_sw64(base + OFF_Q) + ko, ql = desc_sw64(base + OFF_Q + HALF) + ko;
-              const uint64_t kh = desc_sw64(base + OFF_K) + ko, kl = desc_sw64(base + OFF_K + HALF) + ko;
-              mma_ss(tm + T_SP, qh, kh, IDESC_128, kk > 0);
-              mma_ss(tm + T_SP, qh, kl, IDESC_128, 1);
-              mma_ss(tm + T_SP, ql, kh, IDESC_128, 1);
-            }
-          }
-          mma_commit(mma_bar);
-          // q|k|v of the next head now (the accumulator was read above), so it
-          // runs under this head's softmax, off the row threads' path
-          if (h + 1 < H) {
-            gemm(T_ACC, IDESC_QKV);
-            mma_commit(qkv_bar);
-          }
-        }
+        step_done(rows_epi);
         // ---- softmax of row r, keys split by half: the row max (the halves'
         // maxima meet in xch), then 2^7-scaled P over S and the partial sums
         wait_mma(0x6500 + h);
@@ -697,27 +759,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_st();
           xl[(h * 2 + hf) * TR + r] = lsum;
         }
-        step_done();
-        if (tid == 0) {
-          if (ok) {
-            // O_h = P V_h: keys 16 kk .. 16 kk + 15 are P_hi cells
-            // 32 (kk / 2) + 8 (kk % 2) .. + 7 and P_lo 16 cells further
-            const uint32_t od = tm + T_O + (uint32_t)(h * HD);
-#pragma unroll
-            for (int kk = 0; kk < TR / 16; ++kk) {
-              const uint32_t vb = base + OFF_VT + (uint32_t)(h & 1) * VT_BUF + (uint32_t)(kk >> 1) * VT_KB;
-              const uint64_t ko = (uint64_t)(2 * (kk & 1));
-              const uint64_t vh = desc_sw64(vb) + ko, vl = desc_sw64(vb + VT_HALF) + ko;
-              const uint32_t ph = tm + T_SP + 32u * (uint32_t)(kk >> 1) + 8u * (uint32_t)(kk & 1);
-              mma_ts(od, ph, vh, IDESC_PV, kk > 0);
-              mma_ts(od, ph, vl, IDESC_PV, 1);
-              mma_ts(od, ph + 16u, vh, IDESC_PV, 1);
-            }
-          }
-          // the last head's P.V completes the context; earlier ones complete
-          // with the next head's scores, which are issued after them
-          if (h + 1 == H) mma_commit(mma_bar);
-        }
+        step_done(rows_sm);
       }
       // ---- context O / l -> A operand: half hf takes heads 2 hf, 2 hf + 1 ---
       wait_mma(0x6600);
@@ -733,20 +775,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < HD; ++i) o[i] *= il;
         put_kblock_row(bp + OFF_A + h * KBLK, HALF, r, o);
       }
-      step_done();
-      if (tid == 0) {
-        gemm(T_ACC, IDESC_128);
-        mma_commit(mma_bar);
-      }
+      step_done(rows_misc);
       // ---- out_proj: x = valid ? x + ctx Wo^T + bo : 0, then LayerNorm 2 -----
       wait_mma(0x6700);
       residual(s_o, P(a.off.bo));
       layer_norm_half(lb + T_X, r, hf, xch, P(a.off.ln2_w), P(a.off.ln2_b), a.eps, to_a);
-      step_done();
-      if (tid == 0) {
-        gemm(T_ACC, IDESC_128);
-        mma_commit(mma_bar);
-      }
+      step_done(rows_misc);
       // ---- ffn_in + GELU -> A operand -----------------------------------------
       wait_mma(0x6800);
       {
@@ -765,11 +799,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!(amax <= 65504.f) && in) raise_status(a.status, TT_ERR_DEVICE_RANGE, 0x6900);
       }
-      step_done();
-      if (tid == 0) {
-        gemm(T_ACC, IDESC_128);
-        mma_commit(mma_bar);
-      }
+      step_done(rows_misc);
       // ---- ffn_out: x = valid ? x + h W2^T + b2 : 0 -----------------------------
       wait_mma(0x6A00);
       residual(s_2, P(a.off.b2));
@@ -783,12 +813,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         dst[i] = valid ? make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3])
                        : make_float4(0.f, 0.f, 0.f, 0.f);
     });
-    if (tid == 0) {
-      // every MMA this thread issued has completed before the tensor memory
-      // is freed
-      mma_commit(drain_bar);
-      mbar_drain(drain_bar, 0, a.status, 0x6F10);
-    }
   }
   tc_fence_before();
   __syncthreads();
