@@ -186,6 +186,12 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       "r"(a_tmem), "l"(b), "r"(id), "r"(accum)
       : "memory");
 }
+__device__ __forceinline__ void prefetch_l2(const void *p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+__device__ __forceinline__ void prefetch_l1(const void *p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -467,6 +473,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_drain(full(k % NST), (k / NST) & 1, a.status, 0x6F00);
     }
   } else if (warp == kRowThreads / 32 + 1) {
+    // the small per-layer vectors the row threads read from global memory
+    // (LayerNorm gammas and betas, biases, accumulator scales), every layer's,
+    // into L2 by the lanes that issue no MMAs: their first reads in a layer
+    // then find them there, not in HBM
+    if (lane != 0) {
+      const int li = lane - 1;  // 0..30
+      for (int l = 0; l < L; ++l) {
+        const char *lbase = a.image + (size_t)l * a.layer_stride;
+        if (li < 4) {  // the 512-byte vectors: four 128-byte lines each
+          const int o = 128 * li;
+          prefetch_l2(lbase + a.off.ln1_w + o);
+          prefetch_l2(lbase + a.off.ln1_b + o);
+          prefetch_l2(lbase + a.off.bo + o);
+          prefetch_l2(lbase + a.off.ln2_w + o);
+          prefetch_l2(lbase + a.off.ln2_b + o);
+          prefetch_l2(lbase + a.off.b1 + o);
+          prefetch_l2(lbase + a.off.b2 + o);
+        }
+        if (li < 12) prefetch_l2(lbase + a.off.bqkv + 128 * li);  // q|k|v bias, 1536 bytes
+        if (li == 12) prefetch_l2(lbase + a.off.wscale);
+      }
+      if (li < 4) {
+        prefetch_l2(reinterpret_cast<const char *>(a.final_w) + 128 * li);
+        prefetch_l2(reinterpret_cast<const char *>(a.final_b) + 128 * li);
+      }
+    }
     // ---- MMA issue (one lane): each group once the row threads' step that
     // feeds it is done, in the order the row threads consume the results ----
     if (lane == 0) {
@@ -605,6 +637,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(bar);
     };
     auto to_a = [&](int c, float *v) { put_kblock_row(bp + OFF_A + c * KBLK, HALF, r, v); };
+    // this thread's two 32-float chunks of a per-layer vector, into L1 ahead
+    // of the step that reads them (issued before an MMA wait)
+    auto pf_vec = [&](const float *v) {
+      prefetch_l1(v + 64 * hf);
+      prefetch_l1(v + 64 * hf + 32);
+    };
     // this thread's chunks: x = valid ? x + acc * scale + bias : 0
     auto residual = [&](float scale, const float *bias) {
 #pragma unroll 1
@@ -636,6 +674,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_st32(lb + T_X + 32 * c, reinterpret_cast<uint32_t *>(v));
     }
     tmem_wait_st();
+    pf_vec(reinterpret_cast<const float *>(a.image + a.off.ln1_w));
+    pf_vec(reinterpret_cast<const float *>(a.image + a.off.ln1_b));
     rows_sync();  // kword written
 #pragma unroll 1
     for (int l = 0; l < L; ++l) {
@@ -651,6 +691,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int h = 0; h < H; ++h) {
         // ---- q|k|v epilogue of head h: half 0 takes q and value dims 0-15,
         // half 1 takes k and value dims 16-31 ------------------------------
+        prefetch_l1(bqkv + hf * D + h * HD);
+        prefetch_l1(bqkv + 2 * D + h * HD + 16 * hf);
         if (h == 0)
           wait_mma(0x6300);
         else
@@ -777,11 +819,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       step_done(rows_misc);
       // ---- out_proj: x = valid ? x + ctx Wo^T + bo : 0, then LayerNorm 2 -----
+      pf_vec(P(a.off.bo));
+      pf_vec(P(a.off.ln2_w));
+      pf_vec(P(a.off.ln2_b));
       wait_mma(0x6700);
       residual(s_o, P(a.off.bo));
       layer_norm_half(lb + T_X, r, hf, xch, P(a.off.ln2_w), P(a.off.ln2_b), a.eps, to_a);
       step_done(rows_misc);
       // ---- ffn_in + GELU -> A operand -----------------------------------------
+      pf_vec(P(a.off.b1));
       wait_mma(0x6800);
       {
         const float *b1 = P(a.off.b1);
@@ -801,6 +847,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       step_done(rows_misc);
       // ---- ffn_out: x = valid ? x + h W2^T + b2 : 0 -----------------------------
+      pf_vec(P(a.off.b2));
+      if (l + 1 < L) {
+        const char *nbase = lbase + a.layer_stride;
+        pf_vec(reinterpret_cast<const float *>(nbase + a.off.ln1_w));
+        pf_vec(reinterpret_cast<const float *>(nbase + a.off.ln1_b));
+        prefetch_l1(nbase + a.off.wscale);
+      } else {
+        pf_vec(a.final_w);
+        pf_vec(a.final_b);
+      }
       wait_mma(0x6A00);
       residual(s_2, P(a.off.b2));
     }
