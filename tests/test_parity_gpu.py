@@ -462,13 +462,23 @@ def test_peaked_scores_rescale_the_context(d, h):
     assert model.read_device_status() == (0, 0)
 
 
-def test_no_mask_and_all_true_mask_agree():
-    cfg = WORKLOADS["B1"].config
+@pytest.mark.parametrize("name", ["B1", "A", "C"])
+def test_no_mask_and_all_true_mask_agree(name):
+    """mask=None and an all-true mask give the same bits on every schedule
+    (forward_host relies on it to skip an all-true mask's copy)."""
+    w = WORKLOADS[name]
+    cfg = w.config
     model, _ = model_for(cfg)
-    x, mask = generate_random_case(cfg, "cpu", torch.float32, 9, 0.0, 1.0)
+    x, mask = generate_random_case(cfg, "cpu", torch.float32, 9, 0.0, w.input_scale)
     x, mask = x.to(DEV), mask.to(DEV)
-    with torch.inference_mode():
-        torch.testing.assert_close(model(x, None), model(x, mask), rtol=0, atol=0)
+    assert bool(mask.all())
+    try:
+        for plan in applicable_plans(model, x.shape[0], x.shape[1]):
+            model.set_plan(plan)
+            with torch.inference_mode():
+                assert torch.equal(model(x, None), model(x, mask)), plan
+    finally:
+        model.set_plan("auto")
 
 
 def test_runs_on_current_stream():
