@@ -89,6 +89,7 @@ class TTForward:
         self._plist = None
         self._ws_bytes = {}
         self._host_inflight = []  # (event, host buffers) of tt_forward_host calls in flight
+        self._host_events = []    # events of finished entries, for reuse
         self.fp16_operand_bound = None
         self.register_load_state_dict_post_hook(
             lambda module, incompatible: module.invalidate())
@@ -263,6 +264,8 @@ class TTForward:
             raise ValueError("expected a float32 [B, S, d_model] host tensor")
         dev = torch.device("cuda", torch.cuda.current_device()) if device is None else \
             torch.device(device)
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
         b, s, d = x_host.shape
         if out is None:
             out = torch.empty((b, s, d), dtype=torch.float32, pin_memory=True)
@@ -324,29 +327,31 @@ class TTForward:
                 mask = None
         if not x_host.is_contiguous():
             x_host = x_host.contiguous()
-        with torch.cuda.device(dev):
-            image = self._ensure_image(dev)
-            lib, cfg = self._lib, self._cfg
-            key = (b, s, "host")
-            nbytes = self._ws_bytes.get(key)
-            if nbytes is None:
-                nbytes = self._ws_bytes[key] = lib.tt_host_workspace_bytes(ctypes.byref(cfg), b, s)
-            ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-            stream = torch.cuda.current_stream(dev).cuda_stream
-            rc = lib.tt_forward_host(ctypes.byref(cfg), image.data_ptr(), x_host.data_ptr(),
-                                     None if mask is None else mask.data_ptr(), b, s,
-                                     out.data_ptr(), ws.data_ptr(), nbytes, stream)
-            if rc == 0:
-                # the copies are asynchronous: keep the host buffers alive until the
-                # stream has passed them, so a freed pinned block is not handed out
-                # again (by torch's host allocator) while a copy still reads or
-                # writes it
-                inflight = self._host_inflight
-                while inflight and inflight[0][0].query():
-                    inflight.pop(0)
-                ev = torch.cuda.Event()
-                ev.record(torch.cuda.current_stream(dev))
-                inflight.append((ev, x_host, mask, out))
+        if dev.index != torch.cuda.current_device():
+            with torch.cuda.device(dev):
+                return self._host_step(x_host, mask, out, dev)
+        image = self._ensure_image(dev)
+        lib, cfg = self._lib, self._cfg
+        key = (b, s, "host")
+        nbytes = self._ws_bytes.get(key)
+        if nbytes is None:
+            nbytes = self._ws_bytes[key] = lib.tt_host_workspace_bytes(ctypes.byref(cfg), b, s)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        cur = torch.cuda.current_stream(dev)
+        rc = lib.tt_forward_host(ctypes.byref(cfg), image.data_ptr(), x_host.data_ptr(),
+                                 None if mask is None else mask.data_ptr(), b, s,
+                                 out.data_ptr(), ws.data_ptr(), nbytes, cur.cuda_stream)
+        if rc == 0:
+            # the copies are asynchronous: keep the host buffers alive until the
+            # stream has passed them, so a freed pinned block is not handed out
+            # again (by torch's host allocator) while a copy still reads or
+            # writes it; finished entries give their events back for reuse
+            inflight, free = self._host_inflight, self._host_events
+            while inflight and inflight[0][0].query():
+                free.append(inflight.pop(0)[0])
+            ev = free.pop() if free else torch.cuda.Event()
+            ev.record(cur)
+            inflight.append((ev, x_host, mask, out))
         if rc != 0:
             _lib.check(rc, "tt_forward_host", lib)
 
