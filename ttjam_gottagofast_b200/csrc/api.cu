@@ -748,6 +748,23 @@ int tt_forward_typed(const tt_config *cfg, const void *image, int dtype, const v
                       [&] { return launch_narrow(dtype, y32, y, n, stream); });
 }
 
+// Largest x (bytes) that tt_forward_host moves with copy kernels.
+constexpr size_t kHostKernelCopyMax = (size_t)1 << 20;
+
+// The device address of a page-locked host buffer mapped for the device, or
+// null (pageable memory, device memory, or misaligned): read, not assumed.
+static const void *mapped_host(const void *p) {
+  if ((reinterpret_cast<uintptr_t>(p) & 15) != 0) return nullptr;
+  cudaPointerAttributes at{};
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (at.type != cudaMemoryTypeHost || at.devicePointer == nullptr) return nullptr;
+  if ((reinterpret_cast<uintptr_t>(at.devicePointer) & 15) != 0) return nullptr;
+  return at.devicePointer;
+}
+
 size_t tt_host_workspace_bytes(const tt_config *cfg, int64_t batch, int64_t seq) {
   if (validate_config(cfg) != TT_OK || batch < 0 || seq < 0) return 0;
   const size_t T = (size_t)batch * (size_t)seq;
@@ -781,12 +798,34 @@ int tt_forward_host(const tt_config *cfg, const void *image, const float *x_host
   float *ys = reinterpret_cast<float *>(ws + io);
   uint8_t *ms = reinterpret_cast<uint8_t *>(ws + 2 * io);
   const size_t used = 2 * io + align_up(T, 256);
-  TT_CUDA_TRY(cudaMemcpyAsync(xs, x_host, xb, cudaMemcpyHostToDevice, stream));
-  if (mask_host != nullptr)
-    TT_CUDA_TRY(cudaMemcpyAsync(ms, mask_host, T, cudaMemcpyHostToDevice, stream));
+  // Small steps whose buffers are page-locked and mapped for the device copy
+  // with kernels (every 16-byte piece in flight at once, one round trip over
+  // the host link) instead of DMA copies, whose fixed set-up cost dominates
+  // a step of a few tens of microseconds.
+  const void *xd = nullptr, *md = nullptr;
+  void *yd = nullptr;
+  const bool small = xb <= kHostKernelCopyMax && (xd = mapped_host(x_host)) != nullptr &&
+                     (yd = const_cast<void *>(mapped_host(y_host))) != nullptr &&
+                     (mask_host == nullptr || (md = mapped_host(mask_host)) != nullptr);
+  if (small) {
+    if ((rc = timed_launch(TT_KERNEL_CONVERT, stream,
+                           [&] { return launch_small_copy(xd, xs, (int64_t)xb, stream); })))
+      return rc;
+    if (mask_host != nullptr &&
+        (rc = timed_launch(TT_KERNEL_CONVERT, stream,
+                           [&] { return launch_small_copy(md, ms, (int64_t)T, stream); })))
+      return rc;
+  } else {
+    TT_CUDA_TRY(cudaMemcpyAsync(xs, x_host, xb, cudaMemcpyHostToDevice, stream));
+    if (mask_host != nullptr)
+      TT_CUDA_TRY(cudaMemcpyAsync(ms, mask_host, T, cudaMemcpyHostToDevice, stream));
+  }
   if ((rc = tt_forward(cfg, image, xs, mask_host != nullptr ? ms : nullptr, batch, seq, ys,
                        ws + used, workspace_bytes - used, stream_)))
     return rc;
+  if (small)
+    return timed_launch(TT_KERNEL_CONVERT, stream,
+                        [&] { return launch_small_copy(ys, yd, (int64_t)xb, stream); });
   TT_CUDA_TRY(cudaMemcpyAsync(y_host, ys, xb, cudaMemcpyDeviceToHost, stream));
   return TT_OK;
 }

@@ -224,5 +224,9 @@ int launch_attention_ffma(const AttentionParams &p, cudaStream_t stream);
 // rounding (to nearest even) of fp32 to them (typed_io.cu). Any alignment.
 int launch_widen(int dtype, const void *src, float *dst, int64_t n, cudaStream_t stream);
 int launch_narrow(int dtype, const float *src, void *dst, int64_t n, cudaStream_t stream);
+// Copy of n bytes by a kernel, every 16-byte piece in flight at once; for
+// small transfers to or from page-locked host memory mapped for the device
+// (typed_io.cu). Both addresses 16-byte aligned.
+int launch_small_copy(const void *src, void *dst, int64_t n, cudaStream_t stream);
 
 }  // namespace tt

@@ -80,7 +80,35 @@ int aligned16(const void *a, const void *b) {
   return ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15) == 0;
 }
 
+// dst[0 .. n) = src[0 .. n): one 16-byte load and store per thread and step
+// (src and dst 16-byte aligned), the n % 16 tail bytes one by one.
+__global__ void __launch_bounds__(256) small_copy_kernel(const uint8_t *__restrict__ src,
+                                                         uint8_t *__restrict__ dst, int64_t n) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t vecs = n >> 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (int64_t v = t0; v < vecs; v += stride)
+    reinterpret_cast<uint4 *>(dst)[v] = reinterpret_cast<const uint4 *>(src)[v];
+  for (int64_t i = (vecs << 4) + t0; i < n; i += stride) dst[i] = src[i];
+}
+
 }  // namespace
+
+int launch_small_copy(const void *src, void *dst, int64_t n, cudaStream_t stream) {
+  if (n <= 0) return TT_OK;
+  if (!aligned16(src, dst))
+    return fail(TT_ERR_INVALID_ARGUMENT, "small copy: addresses must be 16-byte aligned");
+  const int64_t threads = std::max<int64_t>(1, ceil_div(n, 16));
+  const dim3 grid((unsigned)std::min<int64_t>(ceil_div(threads, 256), 148 * 8)), block(256);
+  const cudaError_t err = launch_kernel(small_copy_kernel, grid, block, 0, stream, 1,
+                                        static_cast<const uint8_t *>(src),
+                                        static_cast<uint8_t *>(dst), n);
+  if (err != cudaSuccess)
+    return fail(TT_ERR_CUDA, std::string("launch of small copy: ") + cudaGetErrorString(err));
+  return TT_OK;
+}
 
 int launch_widen(int dtype, const void *src, float *dst, int64_t n, cudaStream_t stream) {
   if (n <= 0) return TT_OK;
