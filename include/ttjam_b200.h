@@ -204,7 +204,12 @@ size_t tt_host_workspace_bytes(const tt_config *cfg, int64_t batch, int64_t seq)
  * after enqueuing, and y is complete once `stream` has passed the call.
  * Page-locked host buffers keep the copies asynchronous (pageable ones work,
  * with the driver's staging). For small calls, where the caller's own per-call
- * work is what limits the step, this is one entry instead of four. */
+ * work is what limits the step, this is one entry instead of four. When x is
+ * at most 1 MiB and every host buffer is page-locked and mapped for the device
+ * (cudaHostAlloc'd memory on this platform; checked with
+ * cudaPointerGetAttributes), the copies are small kernels that put every
+ * 16-byte piece in flight at once (TT_KERNEL_CONVERT in the launch probe)
+ * instead of DMA copies, whose fixed set-up cost dominates a short step. */
 int tt_forward_host(const tt_config *cfg, const void *image, const float *x_host,
                     const uint8_t *mask_host, int64_t batch, int64_t seq, float *y_host,
                     void *workspace, size_t workspace_bytes, void *stream);
