@@ -24,8 +24,9 @@
 // of P (128), and the four heads' attention outputs O (128).
 // Shared memory: the A operand of the next projection (LayerNorm output,
 // context or GELU output; 128 rows x 128 k as four 32-wide k-blocks of 64-byte
-// rows in the 64-byte swizzle the MMA reads), Q, K and V^T of the current head
-// in the same layout (V^T as 32 dims x 128 keys), and the weight ring.
+// rows in the 64-byte swizzle the MMA reads), Q and K of the current head and
+// V^T of two heads in the same layout (V^T as 32 dims x 128 keys), and the
+// weight ring.
 //
 // One layer is twelve MMA groups: q|k|v of head 0 (N = 96: its q, k and v
 // rows), then per head h the scores S = Q K^T (N = 128), issued together with
