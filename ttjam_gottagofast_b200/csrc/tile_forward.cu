@@ -301,33 +301,32 @@ template <typename Out>
 __device__ __forceinline__ void layer_norm_half(uint32_t xaddr, int r, int hf, float *xch,
                                                 const float *g, const float *b, float eps,
                                                 Out out) {
-  float s = 0.f;
+  // one pass over this thread's 64 columns: sums shifted by the half's first
+  // element (no cancellation while that element lies within a few standard
+  // deviations of the mean), then the two halves' means and squared-deviation
+  // sums combined with Chan, Golub and LeVeque's pairwise formula
+  float s = 0.f, q = 0.f, k0 = 0.f;
 #pragma unroll 1
   for (int cc = 0; cc < 2; ++cc) {
     float v[32];
     tmem_ld32(xaddr + 32 * (2 * hf + cc), v);
     tmem_wait_ld();
-#pragma unroll
-    for (int i = 0; i < 32; ++i) s += v[i];
-  }
-  xch[hf * TR + r] = s;
-  rows_sync();
-  const float mean = (xch[r] + xch[TR + r]) * (1.0f / D);
-  float q = 0.f;
-#pragma unroll 1
-  for (int cc = 0; cc < 2; ++cc) {
-    float v[32];
-    tmem_ld32(xaddr + 32 * (2 * hf + cc), v);
-    tmem_wait_ld();
+    if (cc == 0) k0 = v[0];
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      const float d = v[i] - mean;
+      const float d = v[i] - k0;
+      s += d;
       q = fmaf(d, d, q);
     }
   }
-  xch[2 * TR + hf * TR + r] = q;
+  constexpr float kHalf = 1.0f / (D / 2);
+  xch[hf * TR + r] = fmaf(s, kHalf, k0);           // mean of the half
+  xch[2 * TR + hf * TR + r] = fmaf(-s, s * kHalf, q);  // its squared deviations
   rows_sync();
-  const float rs = rsqrtf((xch[2 * TR + r] + xch[3 * TR + r]) * (1.0f / D) + eps);
+  const float m0 = xch[r], m1 = xch[TR + r], dm = m1 - m0;
+  const float mean = 0.5f * (m0 + m1);
+  const float m2 = xch[2 * TR + r] + xch[3 * TR + r] + dm * dm * (0.25f * D);
+  const float rs = rsqrtf(fmaxf(m2, 0.f) * (1.0f / D) + eps);
 #pragma unroll 1
   for (int cc = 0; cc < 2; ++cc) {
     const int c = 2 * hf + cc;
