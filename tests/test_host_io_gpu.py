@@ -94,3 +94,36 @@ def test_host_step_keeps_inputs_alive_until_copied():
     torch.cuda.synchronize()
     for out in outs:
         assert torch.equal(out, ref)
+
+
+def test_small_host_steps_copy_with_kernels():
+    """x up to 1 MiB in page-locked buffers: the copies are small kernels
+    (TT_KERNEL_CONVERT in the launch probe) around the forward's own launch;
+    pageable buffers take DMA copies (no such launches). Same bits either way."""
+    cfg = WORKLOADS["B1"].config
+    model = _model(cfg)
+    x, mask = generate_random_case(cfg, "cpu", torch.float32, 12, 0.5, 1.0)
+    assert not bool(mask.all())
+    lib = model._lib
+    with torch.inference_mode():
+        ref = model(x.to(DEV), mask.to(DEV)).cpu()
+
+    def kinds_of(xh, mh, yh):
+        torch.cuda.synchronize()
+        assert lib.tt_launch_probe_start(16) == 0
+        try:
+            _host_call(model, xh, mh, yh)
+            ms = (ctypes.c_float * 16)()
+            kinds = (ctypes.c_int32 * 16)()
+            n = lib.tt_launch_probe_read(ms, kinds, 16)
+        finally:
+            lib.tt_launch_probe_start(0)
+        return list(kinds)[:n]
+
+    yh = torch.empty_like(x).pin_memory()
+    # x and the mask in, the forward, y out
+    assert kinds_of(x.pin_memory(), mask.pin_memory(), yh) == [10, 10, 8, 10]
+    assert torch.equal(yh, ref)
+    y2 = torch.empty_like(x)
+    assert kinds_of(x, mask, y2) == [8]
+    assert torch.equal(y2, ref)

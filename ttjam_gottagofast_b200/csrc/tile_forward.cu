@@ -290,17 +290,17 @@ __device__ __forceinline__ float put_kblock_row(uint8_t *kb, uint32_t lo_off, in
 
 // LayerNorm of row r, its 128 columns split between the row's two threads:
 // this thread's half hf is chunks 2 hf and 2 hf + 1 (32 columns each) of the
-// row in tensor memory at xaddr. The mean, then the biased variance of the
-// centred values, each from the two halves' partial sums, which meet in xch
-// ([2 arrays][2 halves][128 rows]) across a barrier of the row threads; then
-// this thread's chunks normalised, scaled by g and shifted by b and handed to
-// out(chunk, values). Loops over chunks are not unrolled: the kernel runs
+// row in tensor memory at xaddr, which load(chunk, values) reads (and may
+// update first: the residual add). The mean and the biased variance from the
+// two halves' partial statistics, which meet in xch ([2 arrays][2 halves][128
+// rows]) across a barrier of the row threads; then this thread's chunks
+// normalised, scaled by g and shifted by b and handed to out(chunk, values). Loops over chunks are not unrolled: the kernel runs
 // each phase once per head or layer, so short loop bodies (which stay in the
 // instruction cache) matter more than the loop overhead.
-template <typename Out>
+template <typename Load, typename Out>
 __device__ __forceinline__ void layer_norm_half(uint32_t xaddr, int r, int hf, float *xch,
                                                 const float *g, const float *b, float eps,
-                                                Out out) {
+                                                Load load, Out out) {
   // one pass over this thread's 64 columns: sums shifted by the half's first
   // element (no cancellation while that element lies within a few standard
   // deviations of the mean), then the two halves' means and squared-deviation
@@ -309,8 +309,9 @@ __device__ __forceinline__ void layer_norm_half(uint32_t xaddr, int r, int hf, f
 #pragma unroll 1
   for (int cc = 0; cc < 2; ++cc) {
     float v[32];
-    tmem_ld32(xaddr + 32 * (2 * hf + cc), v);
-    tmem_wait_ld();
+    // chunk c of the row: as it is in tensor memory, or (the residual add)
+    // updated and written back there first
+    load(2 * hf + cc, v);
     if (cc == 0) k0 = v[0];
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -319,6 +320,7 @@ __device__ __forceinline__ void layer_norm_half(uint32_t xaddr, int r, int hf, f
       q = fmaf(d, d, q);
     }
   }
+  tmem_wait_st();  // the rows written back above, before the second pass reads them
   constexpr float kHalf = 1.0f / (D / 2);
   xch[hf * TR + r] = fmaf(s, kHalf, k0);           // mean of the half
   xch[2 * TR + hf * TR + r] = fmaf(-s, s * kHalf, q);  // its squared deviations
@@ -644,20 +646,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_l1(v + 64 * hf + 32);
     };
     // this thread's chunks: x = valid ? x + acc * scale + bias : 0
-    auto residual = [&](float scale, const float *bias) {
-#pragma unroll 1
-      for (int cc = 0; cc < 2; ++cc) {
-        const int c = 2 * hf + cc;
-        float acc[32], xr[32], bv[32];
+    // chunk c of the residual stream as it is, for a LayerNorm
+    auto x_as_is = [&](int c, float *v) {
+      tmem_ld32(lb + T_X + 32 * c, v);
+      tmem_wait_ld();
+    };
+    // chunk c of the residual stream after the residual add
+    // x = valid ? x + acc * scale + bias : 0, written back to tensor memory:
+    // the LayerNorm that follows takes its statistics in the same pass
+    auto x_plus = [&](float scale, const float *bias) {
+      return [&, scale, bias](int c, float *v) {
+        float acc[32], bv[32];
         tmem_ld32(lb + T_ACC + 32 * c, acc);
-        tmem_ld32(lb + T_X + 32 * c, xr);
+        tmem_ld32(lb + T_X + 32 * c, v);
         load32(bias + 32 * c, bv);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) xr[i] = valid ? xr[i] + fmaf(acc[i], scale, bv[i]) : 0.f;
-        tmem_st32(lb + T_X + 32 * c, reinterpret_cast<uint32_t *>(xr));
-      }
-      tmem_wait_st();
+        for (int i = 0; i < 32; ++i) v[i] = valid ? v[i] + fmaf(acc[i], scale, bv[i]) : 0.f;
+        tmem_st32(lb + T_X + 32 * c, reinterpret_cast<uint32_t *>(v));
+      };
     };
 
     // x row -> tensor memory (zeros past the batch), this thread's chunks
@@ -677,15 +684,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     pf_vec(reinterpret_cast<const float *>(a.image + a.off.ln1_w));
     pf_vec(reinterpret_cast<const float *>(a.image + a.off.ln1_b));
     rows_sync();  // kword written
+    // LayerNorm 1 of layer 0 -> A operand (later layers': after ffn_out)
+    layer_norm_half(lb + T_X, r, hf, xch, reinterpret_cast<const float *>(a.image + a.off.ln1_w),
+                    reinterpret_cast<const float *>(a.image + a.off.ln1_b), a.eps, x_as_is, to_a);
 #pragma unroll 1
     for (int l = 0; l < L; ++l) {
       const char *lbase = a.image + (size_t)l * a.layer_stride;
       auto P = [&](size_t off) { return reinterpret_cast<const float *>(lbase + off); };
       const float *wsc = P(a.off.wscale);
       const float s_qkv = wsc[0], s_o = wsc[1], s_1 = wsc[2], s_2 = wsc[3];
-      // LayerNorm 1 -> A operand
-      layer_norm_half(lb + T_X, r, hf, xch, P(a.off.ln1_w), P(a.off.ln1_b), a.eps, to_a);
-      step_done(rows_misc);
+      step_done(rows_misc);  // LayerNorm 1 in the A operand
       const float *bqkv = P(a.off.bqkv);
 #pragma unroll 1
       for (int h = 0; h < H; ++h) {
@@ -823,8 +831,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       pf_vec(P(a.off.ln2_w));
       pf_vec(P(a.off.ln2_b));
       wait_mma(0x6700);
-      residual(s_o, P(a.off.bo));
-      layer_norm_half(lb + T_X, r, hf, xch, P(a.off.ln2_w), P(a.off.ln2_b), a.eps, to_a);
+      layer_norm_half(lb + T_X, r, hf, xch, P(a.off.ln2_w), P(a.off.ln2_b), a.eps,
+                      x_plus(s_o, P(a.off.bo)), to_a);
       step_done(rows_misc);
       // ---- ffn_in + GELU -> A operand -----------------------------------------
       pf_vec(P(a.off.b1));
@@ -846,7 +854,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(amax <= 65504.f) && in) raise_status(a.status, TT_ERR_DEVICE_RANGE, 0x6900);
       }
       step_done(rows_misc);
-      // ---- ffn_out: x = valid ? x + h W2^T + b2 : 0 -----------------------------
+      // the ffn_out step's vectors, ahead of its wait
       pf_vec(P(a.off.b2));
       if (l + 1 < L) {
         const char *nbase = lbase + a.layer_stride;
@@ -858,17 +866,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         pf_vec(a.final_b);
       }
       wait_mma(0x6A00);
-      residual(s_2, P(a.off.b2));
-    }
-    // ---- final LayerNorm; padded rows zero ------------------------------------
-    layer_norm_half(lb + T_X, r, hf, xch, a.final_w, a.final_b, a.eps, [&](int c, float *v) {
-      if (!in) return;
-      float4 *dst = reinterpret_cast<float4 *>(a.y + g * D + 32 * c);
+      // ---- ffn_out: x = valid ? x + h W2^T + b2 : 0, with the next layer's
+      // LayerNorm 1 -> A operand, or the final LayerNorm -> y (padded rows 0)
+      if (l + 1 < L) {
+        const char *nbase = lbase + a.layer_stride;
+        layer_norm_half(lb + T_X, r, hf, xch, reinterpret_cast<const float *>(nbase + a.off.ln1_w),
+                        reinterpret_cast<const float *>(nbase + a.off.ln1_b), a.eps,
+                        x_plus(s_2, P(a.off.b2)), to_a);
+      } else {
+        layer_norm_half(lb + T_X, r, hf, xch, a.final_w, a.final_b, a.eps,
+                        x_plus(s_2, P(a.off.b2)), [&](int c, float *v) {
+                          if (!in) return;
+                          float4 *dst = reinterpret_cast<float4 *>(a.y + g * D + 32 * c);
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        dst[i] = valid ? make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3])
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
-    });
+                          for (int i = 0; i < 8; ++i)
+                            dst[i] = valid ? make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2],
+                                                         v[4 * i + 3])
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+                        });
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
