@@ -348,6 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
   const int h = rank / G, sub = rank % G;
 
   volatile int *abort_w = reinterpret_cast<volatile int *>(sm + C::OFF_ABORT);
+  pdl_trigger();  // the next kernel on the stream may start its own set-up
   if (tid == 0) {
     for (int p = 0; p < NPH; ++p) mbar_init(bar0 + 8 * p, 1);
     *abort_w = 0;
@@ -355,6 +356,10 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_forward_kernel(const Clus
   }
   load_layer_part<CL, H>(a, 0, 0, sW, rank);  // async group: layer 0, q/k/v part
   load_layer_part<CL, H>(a, 0, 1, sW, rank);  // async group: layer 0, rest
+  // the weights are packed before any forward and no kernel writes them, so
+  // their loads start before the wait for the previous kernel (which may
+  // write x or the mask); y is written only after it
+  pdl_wait();
   // residual stream and row validity for this cluster's sequences
   for (int i = tid; i < R * (kD / 4); i += kThreads) {
     const int r = i / (kD / 4), c4 = i % (kD / 4);
@@ -574,13 +579,19 @@ int launch_cl(const ClusterArgs &a, int nclusters, cudaStream_t stream) {
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = C::BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = CL;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  unsigned n = 1;
+  if (pdl_enabled()) {  // programmatic dependent launch, as the other kernels
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    n = 2;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = n;
   TT_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, a));
   return TT_OK;
 }
