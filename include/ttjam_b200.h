@@ -273,12 +273,14 @@ int tt_last_error(char *buf, size_t len);
 #define TT_KERNEL_FINAL_NORM 7    /* final LayerNorm + padded-row zeroing */
 #define TT_KERNEL_WHOLE_FORWARD 8 /* a single-launch forward (TT_PLAN_CLUSTER, TT_PLAN_TILE) */
 #define TT_KERNEL_ROW_SCAN 9      /* valid lengths and live row tiles of a padded batch */
-#define TT_KERNEL_CONVERT 10      /* 16-bit x widened to fp32, or fp32 y rounded to 16 bits */
+#define TT_KERNEL_CONVERT 10      /* 16-bit x widened to fp32, fp32 y rounded to 16 bits, or a
+                                     copy kernel of tt_forward_host (x, mask in; y out) */
 
 /* Launch timing probe, a measurement aid with no counterpart in the
  * reference. tt_launch_probe_start(capacity) creates 2 * capacity timing
  * events for the calling host thread; from then on every kernel launch that
- * tt_forward / tt_forward_noalloc make on this thread is bracketed by two
+ * tt_forward, tt_forward_typed, tt_forward_host and tt_forward_noalloc make on
+ * this thread is bracketed by two
  * events recorded on the launch's stream, until `capacity` launches have been
  * recorded (later launches are not bracketed). capacity 0 stops the probe and
  * destroys its events. Returns TT_OK or TT_ERR_CUDA. */
