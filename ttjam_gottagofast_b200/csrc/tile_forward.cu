@@ -32,8 +32,10 @@
 // rows), then per head h the scores S = Q K^T (N = 128), issued together with
 // the q|k|v projection of head h+1 (which then runs under head h's softmax,
 // completing on a barrier of its own), and P.V (N = 32); then out_proj, ffn_in
-// and ffn_out (N = 128). V^T is double-buffered by head parity, so head h+1's
-// q|k|v epilogue writes it while head h's P.V still reads the other buffer.
+// and ffn_out (N = 128); out_proj's first three k-blocks (heads 0-2's
+// contexts) are issued under the last head's softmax, its last k-block once
+// that head's context is in. V^T is double-buffered by head parity, so head
+// h+1's q|k|v epilogue writes it while head h's P.V still reads the other one.
 // The row threads between groups: the q|k|v epilogue (bias, range check,
 // Q and K rows and the transposed V^T into shared memory), the softmax (the
 // whole row at once: exact max, 2^7-scaled P split into tensor memory), the
@@ -395,7 +397,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t rows_misc = bars + 8u * (2 * NST + 4);  // LayerNorm 1, context, LayerNorm 2, GELU
   const uint32_t rows_epi = bars + 8u * (2 * NST + 5);   // a head's q|k|v epilogue
   const uint32_t rows_sm = bars + 8u * (2 * NST + 6);    // a head's softmax
-  static_assert(8 * (2 * NST + 7) <= 256, "barrier area");
+  const uint32_t rows_ctx = bars + 8u * (2 * NST + 7);   // heads 0-2's contexts
+  static_assert(8 * (2 * NST + 8) <= 256, "barrier area");
   uint32_t *kword = reinterpret_cast<uint32_t *>(bp + OFF_KW);
   float *xch = reinterpret_cast<float *>(bp + OFF_XCH);
   float *xl = reinterpret_cast<float *>(bp + OFF_XL);
@@ -420,6 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(rows_misc, kRowThreads / 32);
     mbar_init(rows_epi, kRowThreads / 32);
     mbar_init(rows_sm, kRowThreads / 32);
+    mbar_init(rows_ctx, kRowThreads / 32);
     *abort_w = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -506,12 +510,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       bool ok = true;  // MMAs are issued while no wait has given up
       int ws = 0;      // weight stages consumed
-      uint32_t pm = 0, pe = 0, ps = 0;  // phases waited on rows_misc, rows_epi, rows_sm
-      // one projection over the four k-blocks of the A operand into
-      // tensor-memory column d_col, B rows from the next four weight stages
-      auto gemm = [&](uint32_t d_col, uint32_t id) {
+      uint32_t pm = 0, pe = 0, ps = 0, pc = 0;  // phases waited on rows_misc, _epi, _sm, _ctx
+      // one projection over k-blocks kb0 .. kb1 - 1 of the A operand into
+      // tensor-memory column d_col (k-block 0 starts the sum), B rows from the
+      // next weight stages
+      auto gemm = [&](uint32_t d_col, uint32_t id, int kb0 = 0, int kb1 = 4) {
 #pragma unroll 1
-        for (int kb = 0; kb < 4; ++kb, ++ws) {
+        for (int kb = kb0; kb < kb1; ++kb, ++ws) {
           const int s = ws % NST;
           if (!ok || !mbar_wait(full(s), (ws / NST) & 1, abort_w, a.status, 0x6200 + kb)) {
             ok = false;
@@ -564,6 +569,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (h + 1 < H) {
             gemm(T_ACC, IDESC_QKV);
             mma_commit(qkv_bar);
+          } else {
+            // heads 0-2's contexts in the A operand: out_proj's first three
+            // k-blocks run under the last head's softmax
+            rows_wait(rows_ctx, pc, 0x6B28);
+            gemm(T_ACC, IDESC_128, 0, H - 1);
           }
           rows_wait(rows_sm, ps, 0x6B20 + h);  // P of head h in tensor memory
           if (ok) {
@@ -585,8 +595,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           // with the next head's scores, which are issued after them
           if (h + 1 == H) mma_commit(mma_bar);
         }
-        rows_wait(rows_misc, pm, 0x6B30);  // context in the A operand
-        gemm(T_ACC, IDESC_128);            // out_proj
+        rows_wait(rows_misc, pm, 0x6B30);  // the last head's context in the A operand
+        gemm(T_ACC, IDESC_128, H - 1, H);  // out_proj's last k-block
         mma_commit(mma_bar);
         rows_wait(rows_misc, pm, 0x6B40);  // LayerNorm 2
         gemm(T_ACC, IDESC_128);            // ffn_in
@@ -639,6 +649,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(bar);
     };
     auto to_a = [&](int c, float *v) { put_kblock_row(bp + OFF_A + c * KBLK, HALF, r, v); };
+    // head h's context O_h / l -> k-block h of the A operand
+    auto ctx_to_a = [&](int h) {
+      float o[HD];
+      tmem_ld32(lb + T_O + h * HD, o);
+      tmem_wait_ld();
+      const float lsum = xl[(h * 2) * TR + r] + xl[(h * 2 + 1) * TR + r];
+      const float il = lsum > 0.f ? 1.0f / lsum : 0.f;
+#pragma unroll
+      for (int i = 0; i < HD; ++i) o[i] *= il;
+      put_kblock_row(bp + OFF_A + h * KBLK, HALF, r, o);
+    };
     // this thread's two 32-float chunks of a per-layer vector, into L1 ahead
     // of the step that reads them (issued before an MMA wait)
     auto pf_vec = [&](const float *v) {
@@ -743,6 +764,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---- softmax of row r, keys split by half: the row max (the halves'
         // maxima meet in xch), then 2^7-scaled P over S and the partial sums
         wait_mma(0x6500 + h);
+        if (h + 1 == H) {
+          // heads 0-2 are complete (their P.V ran before these scores, and
+          // so did the last q|k|v read of the A operand): their contexts go
+          // in now, half 0 taking heads 0 and 1, half 1 head 2
+          ctx_to_a(2 * hf);
+          if (hf == 0) ctx_to_a(1);
+          step_done(rows_ctx);
+        }
         {
           // a 32-key word no row of the warp may see (above the causal
           // diagonal, another sequence, padding) is skipped; one every row
@@ -811,20 +840,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         step_done(rows_sm);
       }
-      // ---- context O / l -> A operand: half hf takes heads 2 hf, 2 hf + 1 ---
+      // ---- the last head's context O / l -> A operand (half 1) -------------
       wait_mma(0x6600);
-#pragma unroll 1
-      for (int hh = 0; hh < 2; ++hh) {
-        const int h = 2 * hf + hh;
-        float o[HD];
-        tmem_ld32(lb + T_O + h * HD, o);
-        tmem_wait_ld();
-        const float lsum = xl[(h * 2) * TR + r] + xl[(h * 2 + 1) * TR + r];
-        const float il = lsum > 0.f ? 1.0f / lsum : 0.f;
-#pragma unroll
-        for (int i = 0; i < HD; ++i) o[i] *= il;
-        put_kblock_row(bp + OFF_A + h * KBLK, HALF, r, o);
-      }
+      if (hf == 1) ctx_to_a(H - 1);
       step_done(rows_misc);
       // ---- out_proj: x = valid ? x + ctx Wo^T + bo : 0, then LayerNorm 2 -----
       pf_vec(P(a.off.bo));
