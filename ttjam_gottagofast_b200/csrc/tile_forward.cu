@@ -736,6 +736,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < HD; ++i) t[i] = fmaf(t[i], s_qkv, bv[i]);
           float amax = put_kblock_row(bp + (hf ? OFF_K : OFF_Q), HALF, r, t);
+          // Q and K are in place (and every accumulator value is in registers):
+          // the scores may start while V^T, which only P.V reads, is written
+          // (the softmax's arrival, after it, publishes V^T)
+          step_done(rows_epi);
           // V^T: dim i is row i of k-block r / 32, key r % 32 its element
           const float *bvv = bqkv + 2 * D + h * HD + 16 * hf;
           float bv16[16];
@@ -760,7 +764,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (!(amax <= 65504.f) && in) raise_status(a.status, TT_ERR_DEVICE_RANGE, 0x6400 + h);
         }
-        step_done(rows_epi);
         // ---- softmax of row r, keys split by half: the row max (the halves'
         // maxima meet in xch), then 2^7-scaled P over S and the partial sums
         wait_mma(0x6500 + h);
